@@ -1,0 +1,276 @@
+// capi.cu -- the extern "C" entry points declared in include/eahmmf_b200.h (groups 1 and 2).
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+#include "../../include/eahmmf_b200.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+using namespace eb;
+
+namespace {
+
+bool legacy_type(int t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K; }
+
+// Device scratch of the legacy entry points: grown on demand and kept, like the reference's static
+// buffers (expert_cuda.cu:269-301). The entry points are documented single-threaded.
+struct Scratch {
+    float* p = nullptr;
+    size_t cap = 0;
+    bool ensure(size_t bytes) {
+        if (bytes <= cap) return true;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return false;
+        cap = bytes;
+        return true;
+    }
+};
+Scratch g_x, g_o1, g_o2, g_xf;
+cudaStream_t g_stream = nullptr;
+
+bool legacy_stream() {
+    if (g_stream) return true;
+    return cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking) == cudaSuccess;
+}
+bool use_generic() {
+    static const bool v = getenv("EAHMMF_OLD_KERNEL") != nullptr;  // the reference's switch (expert_cuda.cu:307)
+    return v;
+}
+
+bool fragment_path(const QMat& W, const float* dx, int ldx) {
+    return !use_generic() && gemv_mma_ok(W) && (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && ldx % 4 == 0;
+}
+// Workspace of gemv_all: the activations of MT tokens in fragment form.
+size_t gemv_ws_bytes(int K) { return xf_bytes(MT, K); }
+
+// d_out[t*ldo + r] = W x d_x[t*ldx..] for t < nb, MT tokens per pass. The tensor-core path first puts
+// the pass's activations in fragment form (ws, gemv_ws_bytes(K) bytes); other types and layouts take
+// the per-row kernel.
+cudaError_t gemv_all(const QMat& W, const float* dx, int nb, int ldx, float* dout, int ldo, int accumulate,
+                     void* ws, cudaStream_t st) {
+    const bool frag = ws && fragment_path(W, dx, ldx);
+    for (int t0 = 0; t0 < nb; t0 += MT) {
+        const int m = nb - t0 < MT ? nb - t0 : MT;
+        cudaError_t e;
+        if (frag) {
+            GemvXArgs a{};
+            a.W = W;
+            a.xf = xf_carve(ws, MT, W.K);
+            a.m = m;
+            a.Y = dout + (size_t)t0 * ldo;
+            a.ldy = ldo;
+            a.accumulate = accumulate;
+            e = launch_prep_x(dx + (size_t)t0 * ldx, ldx, m, W.K, a.xf, st);
+            if (e == cudaSuccess) e = launch_gemv_xf(a, st);
+        } else {
+            GemvArgs a{};
+            a.W = W;
+            a.X = dx + (size_t)t0 * ldx;
+            a.ldx = ldx;
+            a.m = m;
+            a.Y = dout + (size_t)t0 * ldo;
+            a.ldy = ldo;
+            a.accumulate = accumulate;
+            e = launch_gemv(a, st);
+        }
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+QMat qmat(const uint8_t* w, int type, int ne0, int ne1, size_t rb) { return QMat{w, type, ne0, ne1, rb}; }
+
+bool shape_ok(int type, int ne0, size_t rb) {
+    return ne0 > 0 && ne0 % block_elems(type) == 0 && rb == (size_t)(ne0 / block_elems(type)) * block_bytes(type);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------
+// 1. reference entry points
+// ---------------------------------------------------------------------------------------------------
+extern "C" bool eahmmf_cuda_matmul(const uint8_t* device_weights, int type, int ne0, int ne1, size_t row_bytes,
+                                   const float* host_x, int nb, int ldx, float* host_out, int ldo) {
+    if (!device_weights || !host_x || !host_out || ne0 <= 0 || ne1 <= 0 || nb <= 0 || ldx < ne0 || ldo < ne1 ||
+        !legacy_type(type) || !shape_ok(type, ne0, row_bytes))
+        return false;
+    if (!legacy_stream() || !g_x.ensure((size_t)nb * ne0 * 4) || !g_o1.ensure((size_t)nb * ne1 * 4) ||
+        !g_xf.ensure(gemv_ws_bytes(ne0)))
+        return false;
+    bool ok = cudaMemcpy2DAsync(g_x.p, (size_t)ne0 * 4, host_x, (size_t)ldx * 4, (size_t)ne0 * 4, nb,
+                                cudaMemcpyHostToDevice, g_stream) == cudaSuccess;
+    if (ok)
+        ok = gemv_all(qmat(device_weights, type, ne0, ne1, row_bytes), g_x.p, nb, ne0, g_o1.p, ne1, 0, g_xf.p,
+                      g_stream) == cudaSuccess;
+    if (ok)
+        ok = cudaMemcpy2DAsync(host_out, (size_t)ldo * 4, g_o1.p, (size_t)ne1 * 4, (size_t)ne1 * 4, nb,
+                               cudaMemcpyDeviceToHost, g_stream) == cudaSuccess;
+    // drain queued work even after an error, before the caller releases the lease or reuses scratch
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) ok = false;
+    return ok;
+}
+
+extern "C" bool eahmmf_cuda_matmul_pair(const uint8_t* gw, int gt, int gne0, int gne1, size_t grb, const uint8_t* uw,
+                                        int ut, int une0, int une1, size_t urb, const float* host_x, int nb, int ldx,
+                                        float* host_g, int ldg, float* host_u, int ldu) {
+    if (!gw || !uw || !host_x || !host_g || !host_u || !legacy_type(gt) || !legacy_type(ut) || gne0 <= 0 ||
+        gne1 <= 0 || une0 != gne0 || une1 != gne1 || nb <= 0 || ldx < gne0 || ldg < gne1 || ldu < une1 ||
+        !shape_ok(gt, gne0, grb) || !shape_ok(ut, une0, urb))
+        return false;
+    if (!legacy_stream() || !g_x.ensure((size_t)nb * gne0 * 4) || !g_o1.ensure((size_t)nb * gne1 * 4) ||
+        !g_o2.ensure((size_t)nb * une1 * 4) || !g_xf.ensure(gemv_ws_bytes(gne0)))
+        return false;
+    bool ok = cudaMemcpy2DAsync(g_x.p, (size_t)gne0 * 4, host_x, (size_t)ldx * 4, (size_t)gne0 * 4, nb,
+                                cudaMemcpyHostToDevice, g_stream) == cudaSuccess;
+    if (ok)
+        ok = gemv_all(qmat(gw, gt, gne0, gne1, grb), g_x.p, nb, gne0, g_o1.p, gne1, 0, g_xf.p, g_stream) == cudaSuccess;
+    if (ok)
+        ok = gemv_all(qmat(uw, ut, une0, une1, urb), g_x.p, nb, une0, g_o2.p, une1, 0, g_xf.p, g_stream) == cudaSuccess;
+    if (ok)
+        ok = cudaMemcpy2DAsync(host_g, (size_t)ldg * 4, g_o1.p, (size_t)gne1 * 4, (size_t)gne1 * 4, nb,
+                               cudaMemcpyDeviceToHost, g_stream) == cudaSuccess;
+    if (ok)
+        ok = cudaMemcpy2DAsync(host_u, (size_t)ldu * 4, g_o2.p, (size_t)une1 * 4, (size_t)une1 * 4, nb,
+                               cudaMemcpyDeviceToHost, g_stream) == cudaSuccess;
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) ok = false;
+    return ok;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// 2. device-resident MoE block
+// ---------------------------------------------------------------------------------------------------
+namespace {
+constexpr int CHUNK = DOWN_TMAX;  // tokens per MoE block pass
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+struct WsLayout {
+    size_t ids, wts, logits, offsets, active, slot_token, slot_w, token_slots, h, xf, hf, y, groups, total;
+};
+WsLayout ws_layout(const EahmmfMoeLayer* L, int T) {
+    const int Tc = T < CHUNK ? T : CHUNK;
+    const size_t K = (size_t)L->n_used, E = (size_t)L->n_expert;
+    WsLayout w;
+    size_t o = 0;
+    w.ids = o;
+    o = a256(o + (size_t)T * K * 4);
+    w.wts = o;
+    o = a256(o + (size_t)T * K * 4);
+    w.logits = o;
+    o = a256(o + (L->d_router ? (size_t)Tc * E * 4 : 0));
+    w.offsets = o;
+    o = a256(o + (E + 1) * 4);
+    w.active = o;
+    o = a256(o + (E + 1) * 4);
+    w.slot_token = o;
+    o = a256(o + (size_t)Tc * K * 4);
+    w.slot_w = o;
+    o = a256(o + (size_t)Tc * K * 4);
+    w.token_slots = o;
+    o = a256(o + (size_t)Tc * K * 4);
+    w.h = o;
+    o = a256(o + (size_t)Tc * K * L->FF * 4);
+    w.xf = o;
+    o = a256(o + xf_bytes(Tc, L->D));
+    w.hf = o;
+    o = a256(o + xf_bytes(Tc * (int)K, L->FF));
+    w.y = o;
+    o = a256(o + (size_t)Tc * K * L->D * 4);
+    w.groups = o;
+    o = a256(o + (size_t)(L->D / 16) * 4);
+    w.total = o;
+    return w;
+}
+bool layer_ok(const EahmmfMoeLayer* L) {
+    return L && L->n_expert > 0 && L->n_expert <= MAX_EXPERTS && L->n_used > 0 && L->n_used <= 32 &&
+           L->n_used <= L->n_expert && L->D > 0 && L->D % 256 == 0 && L->FF > 0 && L->FF % 256 == 0 && L->d_gate &&
+           L->d_up && L->d_down && is_kquant(L->gate_type) && is_kquant(L->up_type) && is_kquant(L->down_type) &&
+           shape_ok(L->gate_type, L->D, L->gate_row_bytes) && shape_ok(L->up_type, L->D, L->up_row_bytes) &&
+           shape_ok(L->down_type, L->FF, L->down_row_bytes);
+}
+}  // namespace
+
+extern "C" size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T) {
+    if (!layer_ok(L) || T < 1) return 0;
+    return ws_layout(L, T).total;
+}
+
+extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits,
+                                     float* d_x, void* d_workspace, size_t workspace_bytes, void* stream,
+                                     int* d_status) {
+    if (!layer_ok(L)) return (L && !(is_kquant(L->gate_type) && is_kquant(L->up_type) && is_kquant(L->down_type)))
+                                  ? ST_BAD_TYPE
+                                  : ST_BAD_ARG;
+    if (T < 1 || !d_xn || !d_x || !d_workspace || (!d_logits && !L->d_router)) return ST_BAD_ARG;
+    if (reinterpret_cast<uintptr_t>(d_xn) & 15 || reinterpret_cast<uintptr_t>(d_workspace) & 255) return ST_BAD_ARG;
+    const WsLayout w = ws_layout(L, T);
+    if (workspace_bytes < w.total) return ST_CAPACITY;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(d_workspace);
+    const int K = L->n_used, E = L->n_expert;
+    for (int t0 = 0; t0 < T; t0 += CHUNK) {
+        const int tc = T - t0 < CHUNK ? T - t0 : CHUNK;
+        MoeArgs a{};
+        a.gate = L->d_gate;
+        a.up = L->d_up;
+        a.down = L->d_down;
+        a.gate_type = L->gate_type;
+        a.up_type = L->up_type;
+        a.down_type = L->down_type;
+        a.gate_rb = L->gate_row_bytes;
+        a.up_rb = L->up_row_bytes;
+        a.down_rb = L->down_row_bytes;
+        a.n_expert = E;
+        a.n_used = K;
+        a.D = L->D;
+        a.FF = L->FF;
+        a.T = tc;
+        a.xn = d_xn + (size_t)t0 * L->D;
+        a.x = d_x + (size_t)t0 * L->D;
+        a.h = reinterpret_cast<float*>(ws + w.h);
+        a.rw.ids = reinterpret_cast<int*>(ws + w.ids) + (size_t)t0 * K;
+        a.rw.wts = reinterpret_cast<float*>(ws + w.wts) + (size_t)t0 * K;
+        a.rw.offsets = reinterpret_cast<int*>(ws + w.offsets);
+        a.rw.active = reinterpret_cast<int*>(ws + w.active);
+        a.rw.slot_token = reinterpret_cast<int*>(ws + w.slot_token);
+        a.rw.slot_w = reinterpret_cast<float*>(ws + w.slot_w);
+        a.rw.token_slots = reinterpret_cast<int*>(ws + w.token_slots);
+        a.rw.group_done = reinterpret_cast<int*>(ws + w.groups);
+        a.xf = xf_carve(ws + w.xf, tc, L->D);
+        a.hf = xf_carve(ws + w.hf, tc * K, L->FF);
+        a.y = reinterpret_cast<float*>(ws + w.y);
+        a.status = d_status;
+        if (d_logits) {
+            a.logits = d_logits + (size_t)t0 * E;
+        } else {
+            float* lg = reinterpret_cast<float*>(ws + w.logits);
+            if (launch_f32_gemv(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, st) != cudaSuccess) return ST_CUDA;
+            a.logits = lg;
+        }
+        if (launch_prep_x(a.xn, L->D, tc, L->D, a.xf, st) != cudaSuccess) return ST_CUDA;
+        if (launch_route_permute(a, st) != cudaSuccess) return ST_CUDA;
+        if (launch_moe_gateup(a, st) != cudaSuccess) return ST_CUDA;
+        if (launch_prep_x(a.h, L->FF, tc * K, L->FF, a.hf, st) != cudaSuccess) return ST_CUDA;
+        if (launch_moe_down(a, st) != cudaSuccess) return ST_CUDA;
+    }
+    return ST_OK;
+}
+
+extern "C" size_t eahmmf_cuda_gemv_workspace_bytes(int ne0) { return ne0 > 0 ? gemv_ws_bytes(ne0) : 0; }
+
+extern "C" int eahmmf_cuda_gemv(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_bytes, const float* d_x,
+                                int nb, int ldx, float* d_out, int ldo, int accumulate, void* d_workspace,
+                                size_t workspace_bytes, void* stream) {
+    if (!type_supported(type)) return ST_BAD_TYPE;
+    if (!d_w || !d_x || !d_out || ne1 <= 0 || nb <= 0 || ldx < ne0 || ldo < ne1 || !shape_ok(type, ne0, row_bytes))
+        return ST_BAD_ARG;
+    if (d_workspace && workspace_bytes < gemv_ws_bytes(ne0)) return ST_CAPACITY;
+    return gemv_all(qmat(d_w, type, ne0, ne1, row_bytes), d_x, nb, ldx, d_out, ldo, accumulate, d_workspace,
+                    reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? ST_OK
+               : ST_CUDA;
+}
+
+extern "C" const char* eahmmf_b200_version(void) { return "eahmmf-b200 0.1.0 (sm_100a)"; }
+extern "C" int eahmmf_b200_sm_count(void) { return sm_count(); }

@@ -1,0 +1,105 @@
+// common.cuh -- shared definitions of the sm_100a expert hot path: ggml type ids, status codes and the
+// TMA-bulk / mbarrier helpers.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eb {
+
+// ggml type ids handled on the path (the reference's table: qwen3moe.cpp:204-218).
+constexpr int T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14;
+
+__host__ __device__ constexpr int block_elems(int t) { return (t == T_Q4_K || t == T_Q5_K || t == T_Q6_K) ? 256 : 32; }
+__host__ __device__ constexpr int block_bytes(int t) {
+    return t == T_Q4_K ? 144 : t == T_Q5_K ? 176 : t == T_Q6_K ? 210 : t == T_Q8_0 ? 34 : t == T_F16 ? 64 : t == T_F32 ? 128 : 0;
+}
+__host__ __device__ constexpr bool is_kquant(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K; }
+__host__ __device__ constexpr bool type_supported(int t) {
+    return t == T_F32 || t == T_F16 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K;
+}
+
+// Status bits written by kernels into a device status word (atomicOr) and returned by the C ABI.
+enum : int {
+    ST_OK = 0,
+    ST_BAD_ARG = 1 << 0,       // host-side argument validation failed
+    ST_BAD_TYPE = 1 << 1,      // unsupported ggml type
+    ST_CUDA = 1 << 2,          // a CUDA runtime call failed
+    ST_WAIT_TIMEOUT = 1 << 3,  // a bounded mbarrier wait gave up (copy never completed)
+    ST_BAD_INDEX = 1 << 4,     // an expert id / token index out of range reached a kernel
+    ST_CAPACITY = 1 << 5,      // a size exceeded the workspace the caller provided
+};
+
+// Activations in fragment form ("xf"), produced once per token row by k_prep_x and read by the
+// tensor-core GEMV tiles (kq.cuh):
+//   frag[(row * nseg + seg) * 8 + p * 4 + t]  MMA B fragment (b0, b1) of lane (g, t) for the row's high
+//                                             (p = 0) or low (p = 1) f16 part, 16-k segment seg
+//   sum[row * nseg + seg]                     sum of the unscaled activations of the segment
+//   tsc[row]                                  2^-e: the fragments hold x * 2^e
+struct XF {
+    const uint2* frag;
+    const float* sum;
+    const float* tsc;
+    int nseg;
+};
+
+// Exact 2^e for -126 <= e <= 127.
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+
+// ---------------------------------------------------------------------------------------------
+// TMA bulk copies and mbarriers (single-CTA clusters).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: gives up after WAIT_LIMIT_NS of wall time (a bulk copy lands in microseconds), so a
+// copy that never completes ends the kernel with ST_WAIT_TIMEOUT instead of hanging the GPU.
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (int i = 0; i < 64; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) return false;
+    }
+}
+// 1-D bulk copy global -> shared, completion counted on bar. dst, src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float f16_to_f32(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
+
+// x / (1 + exp(-x)) * u, the SiLU-gated product of qwen3moe.cpp:1056-1059 (IEEE division).
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
+
+}  // namespace eb

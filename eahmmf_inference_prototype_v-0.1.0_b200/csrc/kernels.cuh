@@ -1,0 +1,95 @@
+// kernels.cuh -- launch-side declarations of the sm_100a kernels (implemented in kernels.cu) and the
+// parameter blocks they take. Host code (capi.cu, engine.cu) only sees these.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace eb {
+
+constexpr int MT = 8;               // tokens handled per pass over a weight tile
+constexpr int STAGES = 3;           // TMA ring depth
+constexpr int DOWN_TMAX = 64;       // tokens per call handled by the row-parallel down/combine kernel
+constexpr int ROUTE_TMAX = 256;     // tokens per call handled by the single-CTA route/permute kernel
+constexpr int MAX_EXPERTS = 512;
+
+// A quantized matrix: rows of row_bytes bytes, ne0 = K elements per row.
+struct QMat {
+    const uint8_t* w;
+    int type;
+    int K;
+    int rows;
+    size_t row_bytes;
+};
+
+// Dense GEMV: Y[t*ldy + r] (=|+=) dot(row r, X[t*ldx ..]) for t < m (m <= MT).
+struct GemvArgs {
+    QMat W;
+    const float* X;
+    int ldx;
+    int m;
+    float* Y;
+    int ldy;
+    int accumulate;
+    int generic;  // force the per-element kernel (the reference's EAHMMF_OLD_KERNEL switch)
+    int* status;
+};
+
+// Routing/permutation workspace of one MoE call (all device pointers, sized for T tokens).
+struct RouteWs {
+    int* ids;          // [T*K] routed expert ids, rank order (bit-exact with the CPU path)
+    float* wts;        // [T*K] renormalised routing weights
+    int* offsets;      // [E+1] exclusive prefix of per-expert slot counts
+    int* active;       // [E+1] active[0] = number of experts with slots; active[1..] their ids ascending
+    int* slot_token;   // [T*K] token of each slot (slots grouped by expert ascending, tokens ascending)
+    float* slot_w;     // [T*K] routing weight of each slot
+    int* token_slots;  // [T*K] slots of token t, ascending (= expert-ascending)
+    int* group_done;   // [D/16] per 16-row group of the output: expert units finished (down kernel)
+};
+
+struct MoeArgs {
+    // experts: per-expert component pointers, gate/up [FF x D], down [D x FF]
+    const uint8_t* const* gate;  // device arrays of n_expert device pointers
+    const uint8_t* const* up;
+    const uint8_t* const* down;
+    int gate_type, up_type, down_type;
+    size_t gate_rb, up_rb, down_rb;
+    int n_expert, n_used, D, FF;
+    int T;
+    const float* xn;      // [T*D] normalised activations (expert input)
+    XF xf;                // xn in fragment form (rows = tokens)
+    const float* logits;  // [T*E] router logits
+    float* x;             // [T*D] residual, += weighted expert outputs
+    float* h;             // [T*K*FF] SiLU(gate)*up per slot
+    XF hf;                // h in fragment form (rows = slots)
+    float* y;             // [T*K*D] expert outputs per slot (down projection, before the combine)
+    RouteWs rw;
+    int* status;
+};
+
+// Dense GEMV on activations already in fragment form: Y[t*ldy + r] (=|+=) row r . x_t, t < m <= 8.
+struct GemvXArgs {
+    QMat W;
+    XF xf;
+    int m;
+    float* Y;
+    int ldy;
+    int accumulate;
+    int* status;
+};
+
+int sm_count();
+bool gemv_mma_ok(const QMat& W);                 // tensor-core path available for this matrix
+size_t xf_bytes(int rows, int K);                // bytes of an XF block of `rows` rows
+XF xf_carve(void* base, int rows, int K);        // XF views over such a block
+cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st);
+cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st);
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st);  // per-row kernel (any type)
+cudaError_t launch_route_permute(const MoeArgs& a, cudaStream_t st);
+cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st);
+cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st);
+cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
+                            cudaStream_t st);
+
+}  // namespace eb

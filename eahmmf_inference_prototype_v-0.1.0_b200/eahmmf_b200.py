@@ -1,0 +1,170 @@
+"""Python host glue over libeahmmf_b200.so (the C ABI in include/eahmmf_b200.h).
+
+ctypes bindings with the reference's argument meaning and error behaviour: the legacy entry points
+return False on bad arguments (the engine then uses its CPU kernel), the device-resident ones return
+EAHMMF_ST_* bits. Device memory and streams come from torch (plumbing only). Importing this module
+never falls back to a CPU implementation: it raises if the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libeahmmf_b200.so")
+
+ST_OK, ST_BAD_ARG, ST_BAD_TYPE, ST_CUDA, ST_WAIT_TIMEOUT, ST_BAD_INDEX, ST_CAPACITY = 0, 1, 2, 4, 8, 16, 32
+
+_lib = None
+
+
+class EahmmfMoeLayer(C.Structure):
+    _fields_ = [("n_expert", C.c_int), ("n_used", C.c_int), ("D", C.c_int), ("FF", C.c_int),
+                ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
+                ("gate_row_bytes", C.c_size_t), ("up_row_bytes", C.c_size_t), ("down_row_bytes", C.c_size_t),
+                ("d_gate", C.c_void_p), ("d_up", C.c_void_p), ("d_down", C.c_void_p), ("d_router", C.c_void_p)]
+
+
+EXPORTS = {
+    "eahmmf_cuda_matmul": (C.c_bool, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int,
+                                      C.c_int, C.c_void_p, C.c_int]),
+    "eahmmf_cuda_matmul_pair": (C.c_bool, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int,
+                                           C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                           C.c_int, C.c_void_p, C.c_int]),
+    "eahmmf_cuda_moe_workspace_bytes": (C.c_size_t, [C.POINTER(EahmmfMoeLayer), C.c_int]),
+    "eahmmf_cuda_moe_layer": (C.c_int, [C.POINTER(EahmmfMoeLayer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+    "eahmmf_cuda_gemv_workspace_bytes": (C.c_size_t, [C.c_int]),
+    "eahmmf_cuda_gemv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "eahmmf_dev_create": (C.c_void_p, [C.c_size_t]),
+    "eahmmf_dev_destroy": (None, [C.c_void_p]),
+    "eahmmf_dev_alloc": (C.c_void_p, [C.c_void_p, C.c_size_t]),
+    "eahmmf_dev_release": (None, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "eahmmf_dev_h2d": (C.c_bool, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    "eahmmf_dev_d2h": (C.c_bool, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    "eahmmf_dev_sync": (C.c_bool, [C.c_void_p]),
+    "eahmmf_dev_total_memory": (C.c_size_t, [C.c_void_p]),
+    "eahmmf_dev_free_memory": (C.c_size_t, [C.c_void_p]),
+    "eahmmf_dev_stream": (C.c_void_p, [C.c_void_p]),
+    "eahmmf_dev_inject_fault": (None, [C.c_void_p, C.c_int, C.c_int]),
+    "eahmmf_b200_version": (C.c_char_p, []),
+    "eahmmf_b200_sm_count": (C.c_int, []),
+}
+
+
+def lib(path: str = LIB_PATH) -> C.CDLL:
+    """Loads libeahmmf_b200.so (built by build.py). Raises when it is missing: there is no fallback."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: run `python {os.path.join(HERE, 'build.py')}` first")
+        L = C.CDLL(path)
+        for name, (res, args) in EXPORTS.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def _ptr(a) -> int:
+    """Device (torch tensor) or host (numpy array) address."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return None
+    return getattr(stream, "cuda_stream", stream)
+
+
+# ---- group 1: the reference's entry points (host activations) -----------------------------------
+def cuda_matmul(d_w, qtype: int, ne0: int, ne1: int, row_bytes: int, x: np.ndarray, out: np.ndarray,
+                nb: int | None = None, ldx: int | None = None, ldo: int | None = None) -> bool:
+    nb = x.shape[0] if nb is None else nb
+    ldx = x.shape[1] if ldx is None else ldx
+    ldo = out.shape[1] if ldo is None else ldo
+    return bool(lib().eahmmf_cuda_matmul(_ptr(d_w), qtype, ne0, ne1, row_bytes, _ptr(x), nb, ldx, _ptr(out), ldo))
+
+
+def cuda_matmul_pair(d_g, gt, d_u, ut, ne0, ne1, grb, urb, x, g_out, u_out) -> bool:
+    return bool(lib().eahmmf_cuda_matmul_pair(_ptr(d_g), gt, ne0, ne1, grb, _ptr(d_u), ut, ne0, ne1, urb, _ptr(x),
+                                              x.shape[0], x.shape[1], _ptr(g_out), g_out.shape[1], _ptr(u_out),
+                                              u_out.shape[1]))
+
+
+# ---- group 2: device-resident ------------------------------------------------------------------
+_gemv_ws = {}
+
+
+def gemv_workspace(ne0: int):
+    """A cached device workspace for gemv() (torch uint8 tensor)."""
+    import torch
+    n = int(lib().eahmmf_cuda_gemv_workspace_bytes(ne0))
+    ws = _gemv_ws.get(torch.cuda.current_device())
+    if ws is None or ws.numel() < n:
+        ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+        _gemv_ws[torch.cuda.current_device()] = ws
+    return ws
+
+
+def gemv(d_w, qtype: int, ne0: int, ne1: int, row_bytes: int, d_x, d_out, accumulate: bool = False,
+         stream=None, ws="auto") -> int:
+    nb, ldx = d_x.shape
+    if isinstance(ws, str):
+        ws = gemv_workspace(ne0)
+    return lib().eahmmf_cuda_gemv(_ptr(d_w), qtype, ne0, ne1, row_bytes, _ptr(d_x), nb, ldx, _ptr(d_out),
+                                  d_out.shape[1], int(accumulate), _ptr(ws),
+                                  0 if ws is None else ws.numel() * ws.element_size(), _stream(stream))
+
+
+class MoeLayer:
+    """One layer's experts on the device, in the form ExpertStore leases publish them: a device array
+    of per-expert component pointers for gate, up and down."""
+
+    def __init__(self, gate_ptrs, up_ptrs, down_ptrs, types, row_bytes, D: int, FF: int, n_used: int,
+                 router=None):
+        import torch
+        self._keep = []
+        E = len(gate_ptrs)
+        tabs = []
+        for ptrs in (gate_ptrs, up_ptrs, down_ptrs):
+            t = torch.tensor(np.array(ptrs, dtype=np.uint64).view(np.int64), device="cuda")
+            self._keep.append(t)
+            tabs.append(t.data_ptr())
+        if router is not None:
+            self._keep.append(router)
+        self.desc = EahmmfMoeLayer(E, n_used, D, FF, types[0], types[1], types[2], row_bytes[0], row_bytes[1],
+                                   row_bytes[2], tabs[0], tabs[1], tabs[2], _ptr(router) if router is not None else None)
+        self.E, self.K, self.D, self.FF = E, n_used, D, FF
+
+    @classmethod
+    def from_expert_set(cls, ex, n_used: int, router=None):
+        """Uploads a synth.ExpertSet: one device buffer per component kind, experts back to back."""
+        import torch
+        bufs = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (ex.gate, ex.up, ex.down)]
+        ptrs = [[b.data_ptr() + e * b.shape[1] for e in range(ex.n_expert)] for b in bufs]
+        layer = cls(*ptrs, ex.types, ex.row_bytes, ex.D, ex.FF, n_used, router=router)
+        layer._keep += bufs
+        return layer
+
+    def workspace_bytes(self, T: int) -> int:
+        return int(lib().eahmmf_cuda_moe_workspace_bytes(C.byref(self.desc), T))
+
+    def __call__(self, T: int, d_xn, d_logits, d_x, d_ws, stream=None, d_status=None) -> int:
+        return lib().eahmmf_cuda_moe_layer(C.byref(self.desc), T, _ptr(d_xn), _ptr(d_logits), _ptr(d_x), _ptr(d_ws),
+                                           d_ws.numel() * d_ws.element_size(), _stream(stream), _ptr(d_status))
+
+    def routing(self, d_ws, T: int):
+        """(ids, weights) of the last call, read from the head of the workspace."""
+        n = T * self.K
+        ids = d_ws[: n * 4].view(dtype=__import__("torch").int32).cpu().numpy().reshape(T, self.K)
+        off = ((n * 4 + 255) // 256) * 256
+        w = d_ws[off: off + n * 4].view(dtype=__import__("torch").float32).cpu().numpy().reshape(T, self.K)
+        return ids, w

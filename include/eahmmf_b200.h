@@ -1,0 +1,128 @@
+/* eahmmf_b200.h -- C ABI of the B200 (sm_100a) expert hot path, libeahmmf_b200.so.
+ *
+ * Three groups of entry points:
+ *
+ *  1. The reference's own CUDA entry points, same names, signatures and conventions, so the unmodified
+ *     engine (qwen3moe.cpp built with -DEAHMMF_CUDA -DEAHMMF_CUDA_COMPUTE) links against this library
+ *     instead of expert_cuda.o. Weights are device pointers (WeightView.dev), activations and outputs
+ *     are HOST pointers, the result is ready on return, `false` means bad arguments, an unsupported
+ *     type or a CUDA error (the caller then falls back to its CPU kernel). Single-threaded caller.
+ *
+ *  2. Device-resident entry points for the whole MoE block: routing, grouping, gate/up/SiLU and
+ *     down/combine run on the GPU with no host round trip. They never allocate: the caller passes a
+ *     workspace of eahmmf_cuda_moe_workspace_bytes(). Return 0 on success or EAHMMF_ST_* bits.
+ *
+ *  3. The device backend used by eahmmf::B200Device (include/eahmmf_b200_device.hpp): allocation,
+ *     pinned-staged asynchronous copies on a side stream, free-memory queries.
+ *
+ * ggml type ids accepted: 0 F32, 1 F16, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K (the expert kernels take the
+ * K-quants 12/13/14). Weight buffers must stay readable up to the next 16-byte boundary after their last
+ * row (bulk copies are 16-byte granular); every ExpertStore footprint and cudaMalloc block is.
+ */
+#ifndef EAHMMF_B200_H
+#define EAHMMF_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status bits (device status word and return values of group 2/3). */
+#define EAHMMF_ST_OK 0
+#define EAHMMF_ST_BAD_ARG 1
+#define EAHMMF_ST_BAD_TYPE 2
+#define EAHMMF_ST_CUDA 4
+#define EAHMMF_ST_WAIT_TIMEOUT 8
+#define EAHMMF_ST_BAD_INDEX 16
+#define EAHMMF_ST_CAPACITY 32
+
+/* ---- 1. reference entry points --------------------------------------------------------------- */
+
+/* out[t*ldo + r] = dot(dequant(row r of device_weights), host_x[t*ldx ..]) for r < ne1, t < nb.
+ * Replaces eahmmf_cuda_matmul, expert_cuda.cu:251-261 (declared by the engine at qwen3moe.cpp:422,
+ * called from gpu_matmul, qwen3moe.cpp:471-474, and matmul_shadow, qwen3moe.cpp:444). Gaps between
+ * rows of host_out (ldo > ne1) are left untouched. */
+bool eahmmf_cuda_matmul(const uint8_t* device_weights, int type, int ne0, int ne1, size_t row_bytes,
+                        const float* host_x, int nb, int ldx, float* host_out, int ldo);
+
+/* Gate and up projections of the same activations: one host->device copy, one synchronisation.
+ * Replaces eahmmf_cuda_matmul_pair, expert_cuda.cu:344-348 (called from gpu_matmul_pair,
+ * qwen3moe.cpp:476-491, in the MoE block at qwen3moe.cpp:1037). */
+bool eahmmf_cuda_matmul_pair(const uint8_t* gw, int gt, int gne0, int gne1, size_t grb, const uint8_t* uw, int ut,
+                             int une0, int une1, size_t urb, const float* host_x, int nb, int ldx, float* host_g,
+                             int ldg, float* host_u, int ldu);
+
+/* ---- 2. device-resident MoE block ------------------------------------------------------------- */
+
+/* One MoE layer's experts: per-expert component pointers, as ExpertStore leases expose them
+ * (WeightView.dev of ExpertViews.gate/up/down, eahmmf.h:54-62, :737-742). gate/up are [FF rows x D],
+ * down is [D rows x FF]. */
+typedef struct EahmmfMoeLayer {
+    int n_expert; /* experts in the layer (<= 512) */
+    int n_used;   /* experts per token, k (<= 32) */
+    int D;        /* hidden size (multiple of 256) */
+    int FF;       /* expert intermediate size (multiple of 256) */
+    int gate_type, up_type, down_type; /* 12 Q4_K, 13 Q5_K or 14 Q6_K */
+    size_t gate_row_bytes, up_row_bytes, down_row_bytes;
+    const uint8_t* const* d_gate; /* device array of n_expert device pointers */
+    const uint8_t* const* d_up;
+    const uint8_t* const* d_down;
+    const float* d_router; /* F32 [n_expert x D] router matrix; NULL when logits are passed in */
+} EahmmfMoeLayer;
+
+/* Bytes of workspace eahmmf_cuda_moe_layer needs for T tokens. The workspace starts with the routing
+ * result of the last call: int32 ids[T*n_used], then float weights[T*n_used] (rank order). */
+size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
+
+/* The MoE block of Engine::forward (qwen3moe.cpp:1008-1069) for T tokens, on `stream` (cudaStream_t,
+ * NULL = default stream), asynchronous:
+ *   logits = d_logits ? d_logits : d_xn x router^T;  softmax numerators exp(l - max);  top-k with the
+ *   reference's comparator;  weights renormalised over the k;  per active expert (ascending id) the
+ *   gate/up projections, SiLU(g)*u, the down projection, and the weighted sum added to d_x.
+ * d_xn: [T x D] expert input (post-norm); d_x: [T x D] residual, updated in place. Tokens are taken in
+ * blocks of 64, as the engine's forward() is fed at most MAXB = 64 tokens (qwen3moe.cpp:39, :933); per-
+ * token results do not depend on the blocking. d_status (optional) receives EAHMMF_ST_* bits raised
+ * inside kernels. */
+int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
+                          void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);
+
+/* Dense quantized GEMV on device buffers: d_out[t*ldo + r] (=, or += when accumulate) dot(row r, d_x[t*ldx..]),
+ * the reference's matmul (qwen3moe.cpp:397-419) with device activations. K-quant rows run on the tensor
+ * cores once the activations are in fragment form, which needs eahmmf_cuda_gemv_workspace_bytes(ne0)
+ * bytes of workspace (256-byte aligned); without a workspace every type takes the per-row kernel. */
+size_t eahmmf_cuda_gemv_workspace_bytes(int ne0);
+int eahmmf_cuda_gemv(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_bytes, const float* d_x, int nb,
+                     int ldx, float* d_out, int ldo, int accumulate, void* d_workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ---- 3. device backend (eahmmf::B200Device) --------------------------------------------------- */
+
+typedef struct EahmmfDev EahmmfDev;
+/* Binds the calling thread's current device; staging_bytes of pinned host memory (two halves) stage
+ * pageable sources so host->device copies run as DMA on a non-blocking side stream. */
+EahmmfDev* eahmmf_dev_create(size_t staging_bytes);
+void eahmmf_dev_destroy(EahmmfDev* d);
+void* eahmmf_dev_alloc(EahmmfDev* d, size_t bytes);        /* NULL on failure (DeviceBackend::alloc) */
+void eahmmf_dev_release(EahmmfDev* d, void* p, size_t bytes);
+bool eahmmf_dev_h2d(EahmmfDev* d, void* dst, const void* src, size_t n); /* enqueued; valid after sync */
+bool eahmmf_dev_d2h(EahmmfDev* d, void* dst, const void* src, size_t n); /* complete on return */
+bool eahmmf_dev_sync(EahmmfDev* d);
+size_t eahmmf_dev_total_memory(EahmmfDev* d);
+size_t eahmmf_dev_free_memory(EahmmfDev* d);
+void* eahmmf_dev_stream(EahmmfDev* d); /* the side stream (cudaStream_t) */
+/* Test hook: the next n calls of the given kind fail before any CUDA call is made
+ * (kind 0 alloc, 1 h2d, 2 d2h). */
+void eahmmf_dev_inject_fault(EahmmfDev* d, int kind, int n);
+
+/* ---- misc ------------------------------------------------------------------------------------ */
+const char* eahmmf_b200_version(void);
+int eahmmf_b200_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

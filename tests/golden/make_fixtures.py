@@ -114,6 +114,7 @@ def main():
     eng.close()
     np.savez_compressed(os.path.join(GOLDEN, "ref_tiny.npz"), prompt=np.array(PROMPT_IDS, np.int32), logits=lg,
                         hello_ids=np.array(hello_ids, np.int32), hello_gen=gen.astype(np.int32),
+                        hello_text=np.frombuffer(text, np.uint8),
                         logits_b4=lg4, gen12=np.array(ids12, np.int32), trace_ids=tr_ids, trace_w=tr_w)
 
     # ---- 3a. config 1 model ---------------------------------------------------------------------
