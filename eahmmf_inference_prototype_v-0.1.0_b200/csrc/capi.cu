@@ -43,8 +43,8 @@ bool use_generic() {
 bool fragment_path(const QMat& W, const float* dx, int ldx) {
     return !use_generic() && gemv_mma_ok(W) && (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && ldx % 4 == 0;
 }
-// Workspace of gemv_all: the activations of MT tokens in fragment form.
-size_t gemv_ws_bytes(int K) { return xf_bytes(MT, K); }
+// Workspace of gemv_all: the activations of one pass in fragment form.
+size_t gemv_ws_bytes(int K) { return xf_bytes(XPASS, K); }
 
 // d_out[t*ldo + r] = W x d_x[t*ldx..] for t < nb, MT tokens per pass. The tensor-core path first puts
 // the pass's activations in fragment form (ws, gemv_ws_bytes(K) bytes); other types and layouts take
@@ -52,13 +52,14 @@ size_t gemv_ws_bytes(int K) { return xf_bytes(MT, K); }
 cudaError_t gemv_all(const QMat& W, const float* dx, int nb, int ldx, float* dout, int ldo, int accumulate,
                      void* ws, cudaStream_t st) {
     const bool frag = ws && fragment_path(W, dx, ldx);
-    for (int t0 = 0; t0 < nb; t0 += MT) {
-        const int m = nb - t0 < MT ? nb - t0 : MT;
+    const int per = frag ? XPASS : MT;
+    for (int t0 = 0; t0 < nb; t0 += per) {
+        const int m = nb - t0 < per ? nb - t0 : per;
         cudaError_t e;
         if (frag) {
             GemvXArgs a{};
             a.W = W;
-            a.xf = xf_carve(ws, MT, W.K);
+            a.xf = xf_carve(ws, XPASS, W.K);
             a.m = m;
             a.Y = dout + (size_t)t0 * ldo;
             a.ldy = ldo;
@@ -191,6 +192,41 @@ bool layer_ok(const EahmmfMoeLayer* L) {
 }
 }  // namespace
 
+// ---- optional per-stage timing of eahmmf_cuda_moe_layer (events on the call's stream) --------------
+namespace {
+constexpr int PROF_STAGES = 6;  // router GEMV, activation prep, route/permute, gate/up, h prep, down/combine
+struct StageTimer {
+    bool on = false;
+    cudaEvent_t ev[PROF_STAGES + 1] = {};
+    int used = 0;
+    bool ensure() {
+        for (auto& e : ev)
+            if (!e && cudaEventCreate(&e) != cudaSuccess) return false;
+        return true;
+    }
+    void mark(int i, cudaStream_t st) {
+        if (on && i <= PROF_STAGES) cudaEventRecord(ev[i], st);
+    }
+} g_prof;
+}  // namespace
+
+extern "C" int eahmmf_cuda_moe_profile(int enable) {
+    if (enable && !g_prof.ensure()) return ST_CUDA;
+    g_prof.on = enable != 0;
+    return ST_OK;
+}
+
+extern "C" int eahmmf_cuda_moe_profile_read(float* us, int cap) {
+    if (!g_prof.on || !us || cap < PROF_STAGES) return ST_BAD_ARG;
+    if (cudaEventSynchronize(g_prof.ev[PROF_STAGES]) != cudaSuccess) return ST_CUDA;
+    for (int i = 0; i < PROF_STAGES; i++) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, g_prof.ev[i], g_prof.ev[i + 1]) != cudaSuccess) return ST_CUDA;
+        us[i] = ms * 1000.f;
+    }
+    return ST_OK;
+}
+
 extern "C" size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T) {
     if (!layer_ok(L) || T < 1) return 0;
     return ws_layout(L, T).total;
@@ -241,6 +277,7 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
         a.hf = xf_carve(ws + w.hf, tc * K, L->FF);
         a.y = reinterpret_cast<float*>(ws + w.y);
         a.status = d_status;
+        g_prof.mark(0, st);
         if (d_logits) {
             a.logits = d_logits + (size_t)t0 * E;
         } else {
@@ -248,11 +285,17 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
             if (launch_f32_gemv(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, st) != cudaSuccess) return ST_CUDA;
             a.logits = lg;
         }
+        g_prof.mark(1, st);
         if (launch_prep_x(a.xn, L->D, tc, L->D, a.xf, st) != cudaSuccess) return ST_CUDA;
+        g_prof.mark(2, st);
         if (launch_route_permute(a, st) != cudaSuccess) return ST_CUDA;
+        g_prof.mark(3, st);
         if (launch_moe_gateup(a, st) != cudaSuccess) return ST_CUDA;
+        g_prof.mark(4, st);
         if (launch_prep_x(a.h, L->FF, tc * K, L->FF, a.hf, st) != cudaSuccess) return ST_CUDA;
+        g_prof.mark(5, st);
         if (launch_moe_down(a, st) != cudaSuccess) return ST_CUDA;
+        g_prof.mark(6, st);
     }
     return ST_OK;
 }

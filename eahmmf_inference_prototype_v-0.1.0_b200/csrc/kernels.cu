@@ -16,6 +16,8 @@
 //                       weighted combine and the residual add: the CTA completing a row group adds each
 //                       token's expert outputs in ascending expert order (qwen3moe.cpp:1025-1069).
 #include <algorithm>
+#include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -130,12 +132,18 @@ __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
 // activations -> fragment form (XF); one CTA per token row
 // ------------------------------------------------------------------------------------------------
 constexpr int PREP_NT = 256;
-// rows: X + row * ldx (row < nrows), K floats each (K % 16 == 0, rows 16-byte aligned).
+__device__ __forceinline__ int digit(float v) { return (int)fminf(127.f, fmaxf(-127.f, rintf(v))); }
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
+}
+// rows: X + row * ldx (row < nrows), K floats each (K % 32 == 0, rows 16-byte aligned). Writes each row
+// as three int8 digits of base 254 of x / s, s = max|x| / 127, in MMA B-fragment order, plus the
+// per-16 sums of x and s.
 __global__ void __launch_bounds__(PREP_NT) k_prep_x(const float* __restrict__ X, int ldx, int K, uint2* __restrict__ frag,
                                                      float* __restrict__ sum, float* __restrict__ tsc) {
     __shared__ float wmax[PREP_NT / 32];
-    __shared__ int sh_e;
-    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, nseg = K >> 4;
+    __shared__ float sh_inv;
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, nblk = K >> 5;
     const float* x = X + (size_t)row * ldx;
     float mx = 0.f;
     for (int i = tid; i < (K >> 2); i += PREP_NT) {
@@ -149,46 +157,51 @@ __global__ void __launch_bounds__(PREP_NT) k_prep_x(const float* __restrict__ X,
     if (tid == 0) {
         float m = 0.f;
         for (int w = 0; w < PREP_NT / 32; w++) m = fmaxf(m, wmax[w]);
-        int e = 0;
-        if (m > 0.f && m < INFINITY) {
-            int p;
-            frexpf(m, &p);  // m < 2^p: scaled max lands in [2^13, 2^14)
-            e = 14 - p;
-            e = e > 100 ? 100 : (e < -100 ? -100 : e);
-        }
-        sh_e = e;
-        tsc[row] = pow2f(-e);
+        if (!(m > 0.f) || m == INFINITY) m = 127.f;  // all-zero (or non-finite) rows: any scale works
+        tsc[row] = m / 127.f;
+        sh_inv = 127.f / m;
     }
     __syncthreads();
-    const float sc = pow2f(sh_e);
-    for (int i = tid; i < nseg * 4; i += PREP_NT) {  // item = (segment, t): 4 consecutive lanes share a segment
+    const float inv = sh_inv;
+    for (int i = tid; i < nblk * 4; i += PREP_NT) {  // item = (32-k block j, t): 4 consecutive lanes share a block
         const int j = i >> 2, t = i & 3;
-        const float4 v = *reinterpret_cast<const float4*>(x + 16 * j + 4 * t);
-        const float xs[4] = {v.x * sc, v.z * sc, v.y * sc, v.w * sc};  // physical order 0, 2, 1, 3
-        uint32_t h16[4], l16[4];
+        const float4 u = *reinterpret_cast<const float4*>(x + 32 * j + 4 * t);
+        const float4 w = *reinterpret_cast<const float4*>(x + 32 * j + 16 + 4 * t);
+        const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+        int dg[3][8];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const __half hh = __float2half_rn(xs[k]);
-            h16[k] = __half_as_ushort(hh);
-            l16[k] = __half_as_ushort(__float2half_rn(xs[k] - __half2float(hh)));
+        for (int k = 0; k < 8; k++) {
+            const float v = xv[k] * inv;
+            const int a0 = digit(v);
+            const float r1 = (v - (float)a0) * DIGIT;
+            const int a1 = digit(r1);
+            const int a2 = digit((r1 - (float)a1) * DIGIT);
+            dg[0][k] = a0;
+            dg[1][k] = a1;
+            dg[2][k] = a2;
         }
-        uint2* o = frag + ((size_t)row * nseg + j) * 8;
-        o[t] = make_uint2(h16[0] | (h16[1] << 16), h16[2] | (h16[3] << 16));
-        o[4 + t] = make_uint2(l16[0] | (l16[1] << 16), l16[2] | (l16[3] << 16));
-        float s = (v.x + v.y) + (v.z + v.w);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if (t == 0) sum[(size_t)row * nseg + j] = s;
+        uint2* o = frag + ((size_t)row * nblk + j) * 12 + t;
+#pragma unroll
+        for (int p = 0; p < 3; p++)
+            o[p * 4] = make_uint2(pack4(dg[p][0], dg[p][1], dg[p][2], dg[p][3]), pack4(dg[p][4], dg[p][5], dg[p][6], dg[p][7]));
+        float s0 = (u.x + u.y) + (u.z + u.w), s1 = (w.x + w.y) + (w.z + w.w);
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+        if (t == 0) {
+            sum[(size_t)row * (K >> 4) + 2 * j] = s0;
+            sum[(size_t)row * (K >> 4) + 2 * j + 1] = s1;
+        }
     }
 }
 
 // ------------------------------------------------------------------------------------------------
 // tile engine: small persistent CTAs (4 warps), one 16-row tile per step, two-slot TMA ring
 // ------------------------------------------------------------------------------------------------
-constexpr int NTS = 128;
-constexpr int NWS = NTS / 32;
-constexpr int RING = 2;
-constexpr int SETS = 2;  // 4-token column sets per pass (8 tokens)
+constexpr int SETS = 2;  // MMA column sets per pass of the dense GEMV (TOK_PER_SET tokens each)
+constexpr int TPASS = SETS * TOK_PER_SET;  // tokens per pass of the dense GEMV
+constexpr int MPASS = TOK_PER_SET;         // tokens per pass of the expert kernels (one column set)
 
 __host__ __device__ inline size_t al128(size_t x) { return (x + 127) & ~(size_t)127; }
 
@@ -226,139 +239,130 @@ __device__ __forceinline__ uint32_t rows_lead(const RowLayout& L, const uint8_t*
     return L.per_row ? 0u : (uint32_t)((reinterpret_cast<uintptr_t>(base) + (size_t)r0 * rb) & 15);
 }
 
-// Scale decode of one 16-row tile: scl [sb][group][16] (rows r and r+8 adjacent), mins [tok][row][sb].
-template <int QT>
-__device__ __forceinline__ void tile_scales(const uint8_t* rows, int stride, int nsb, const XF& xf, const int* tok,
-                                            int m, float* scl, float* mins) {
-    constexpr int G = groups_of(QT);
-    for (int i = threadIdx.x; i < 16 * nsb; i += blockDim.x) {
-        const int r = i / nsb, sb = i - r * nsb;
-        decode_scales<QT>(rows + (size_t)r * stride + (size_t)sb * block_bytes(QT), scl + (size_t)sb * G * 16,
-                          2 * (r & 7) + (r >> 3), [&](int tk) { return xf.sum + (size_t)tok[tk] * xf.nseg; }, sb, m,
-                          mins + (size_t)r * nsb + sb, 16 * nsb);
+// Bulk-copies the fragment rows and per-16 sums of m tokens into shared memory (sfrag: m x K*3 bytes,
+// ssum: m x K/16 floats). rows(i) gives token i's xf row; consecutive rows are merged into one copy.
+// Returns the bytes in flight on bar.
+template <typename Rows>
+__device__ __forceinline__ uint32_t issue_xf(const XF& xf, Rows rows, int m, int K, uint8_t* sfrag, float* ssum,
+                                             uint64_t* bar) {
+    const uint32_t fb = (uint32_t)K * 3, sbytes = (uint32_t)K / 4;
+    uint32_t total = 0;
+    for (int i = 0; i < m;) {
+        int n = 1;
+        while (i + n < m && rows(i + n) == rows(i) + n) n++;
+        const size_t r = (size_t)rows(i);
+        tma_load_1d(sfrag + (size_t)i * fb, reinterpret_cast<const uint8_t*>(xf.frag) + r * fb, n * fb, bar);
+        tma_load_1d(ssum + (size_t)i * (K >> 4), xf.sum + r * (K >> 4), n * sbytes, bar);
+        total += n * (fb + sbytes);
+        i += n;
     }
+    return total;
 }
+__device__ __forceinline__ uint32_t xf_bytes_of(int m, int K) { return (uint32_t)m * ((uint32_t)K * 3 + (uint32_t)K / 4); }
 
-// All MMA tasks (super-block, half) of a staged 16-row tile, part[(task0 + task) * NSET + st][row][tok].
+// All MMA tasks (super-block, half) of a staged 16-row tile:
+//   part[((task0 + task) * NSET + st) * 128 + row * 8 + column] = d * (int32 digit sums)
+//   mpart[(task0 + task) * 64 + row * 4 + token]                = group-minimum term
 template <int QT, int NSET>
-__device__ __forceinline__ void tile_tasks(const uint8_t* rows, int stride, int nsb, const XF& xf, const int* tok, int m,
-                                           const float* scl, float* part, int task0) {
-    constexpr int G = groups_of(QT);
+__device__ __forceinline__ void tile_tasks(const uint8_t* rows, int stride, int nsb, const uint2* sfrag,
+                                           const float* ssum, int m, float* part, float* mpart, int task0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const BPtr<NSET> bp(xf, tok, m);
+    const BPtr<NSET> bp(sfrag, nsb * 8, m);
     for (int k = warp; k < nsb * 2; k += (int)(blockDim.x >> 5)) {
-        const int sb = k >> 1, h = k & 1;
-        float acc[NSET][4];
-#pragma unroll
-        for (int st = 0; st < NSET; st++) acc[st][0] = acc[st][1] = acc[st][2] = acc[st][3] = 0.f;
-        mma_task<QT, NSET>(rows, stride, sb, h, bp, scl, acc);
+        float o[NSET][4], mn[2];
+        mma_task<QT, NSET>(rows, stride, k >> 1, k & 1, bp, ssum, nsb * 16, m, o, mn);
 #pragma unroll
         for (int st = 0; st < NSET; st++) {
-            float* p = part + ((size_t)(task0 + k) * NSET + st) * 64;
-            p[g * 4 + t] = acc[st][0] + acc[st][1];
-            p[(g + 8) * 4 + t] = acc[st][2] + acc[st][3];
+            float* p = part + ((size_t)(task0 + k) * NSET + st) * 128;
+            *reinterpret_cast<float2*>(p + g * 8 + 2 * t) = make_float2(o[st][0], o[st][1]);
+            *reinterpret_cast<float2*>(p + (g + 8) * 8 + 2 * t) = make_float2(o[st][2], o[st][3]);
         }
+        float* q = mpart + (size_t)(task0 + k) * 64;
+        q[g * 4 + t] = mn[0];
+        q[(g + 8) * 4 + t] = mn[1];
     }
 }
 
-// Row r (0..15) of the tile times token tk: MMA partials in super-block order, scaled back by the
-// token's power of two, minus the constant terms.
+// Row r (0..15) of the tile times token tk: the three digit columns summed over the tasks in
+// super-block order and recombined, scaled by the token's s, minus the group-minimum terms.
 template <int NSET>
-__device__ __forceinline__ float tile_value(const float* part, int task0, int r, int nsb, int tk, float tscale,
-                                            const float* mins) {
-    const int st = tk >> 2, c = tk & 3;
-    float s = 0.f, mn = 0.f;
-    for (int sb = 0; sb < nsb; sb++) {
-        const int task = task0 + 2 * sb;
-        s += part[((size_t)task * NSET + st) * 64 + r * 4 + c];
-        s += part[((size_t)(task + 1) * NSET + st) * 64 + r * 4 + c];
-        mn += mins[((size_t)tk * 16 + r) * nsb + sb];
+__device__ __forceinline__ float tile_value(const float* part, const float* mpart, int task0, int r, int nsb, int tk,
+                                            float tscale) {
+    const int st = tk / TOK_PER_SET, c = 3 * (tk % TOK_PER_SET);
+    float a = 0.f, b = 0.f, e = 0.f, mn = 0.f;
+    for (int k = 0; k < 2 * nsb; k++) {
+        const float* p = part + ((size_t)(task0 + k) * NSET + st) * 128 + r * 8 + c;
+        a += p[0];
+        b += p[1];
+        e += p[2];
+        mn += mpart[(size_t)(task0 + k) * 64 + r * 4 + tk];
     }
-    return fmaf(s, tscale, -mn);
+    return fmaf(fmaf(fmaf(e, 1.0f / DIGIT, b), 1.0f / DIGIT, a), tscale, -mn);
 }
 
 // ------------------------------------------------------------------------------------------------
 // dense K-quant GEMV: row groups of 16 strided over the grid
 // ------------------------------------------------------------------------------------------------
+constexpr int NTU = 256;  // threads of the one-unit-per-CTA kernels (8 warps)
 struct GPlan {
-    size_t scl_off, mins_off, part_off, ring_off, slot, total;
+    size_t sfrag_off, ssum_off, part_off, mpart_off, slot_off, total;
 };
-__host__ __device__ inline GPlan gemv_plan(int qt, int K, size_t rb, int nset) {
+// Shared memory of a one-tile unit with m staged tokens and ntask MMA tasks of nset column sets.
+__host__ __device__ inline GPlan unit_plan(int K, int m, int ntask, int nset, size_t slot_bytes_total) {
     GPlan p;
-    const int nsb = K / 256;
-    p.scl_off = 128;
-    p.mins_off = al128(p.scl_off + (size_t)16 * nsb * groups_of(qt) * 4);
-    p.part_off = al128(p.mins_off + (size_t)4 * SETS * 16 * nsb * 4);
-    p.ring_off = al128(p.part_off + (size_t)nsb * 2 * nset * 256);
-    p.slot = slot_bytes(row_layout(rb, true), 16);
-    p.total = p.ring_off + RING * p.slot;
+    p.sfrag_off = 128;
+    p.ssum_off = al128(p.sfrag_off + (size_t)m * K * 3);
+    p.part_off = al128(p.ssum_off + (size_t)m * (K / 16) * 4);
+    p.mpart_off = al128(p.part_off + (size_t)ntask * nset * 512);
+    p.slot_off = al128(p.mpart_off + (size_t)ntask * 256);
+    p.total = p.slot_off + slot_bytes_total;
     return p;
+}
+__host__ __device__ inline GPlan gemv_plan(int qt, int K, size_t rb, int nset, int m) {
+    (void)qt;
+    return unit_plan(K, m, 2 * (K / 256), nset, slot_bytes(row_layout(rb, true), 16));
 }
 
 template <int QT, int NSET>
-__global__ void __launch_bounds__(NTS) k_gemv(GemvXArgs a) {
+__global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int K = a.W.K, nsb = K >> 8, m = a.m, tid = threadIdx.x;
     const size_t rb = a.W.row_bytes;
-    const GPlan pl = gemv_plan(QT, K, rb, NSET);
+    const GPlan pl = gemv_plan(QT, K, rb, NSET, m);
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
-    int* tok = reinterpret_cast<int*>(sm + 64);
-    float* scl = reinterpret_cast<float*>(sm + pl.scl_off);
-    float* mins = reinterpret_cast<float*>(sm + pl.mins_off);
+    uint8_t* sfrag = sm + pl.sfrag_off;
+    float* ssum = reinterpret_cast<float*>(sm + pl.ssum_off);
     float* part = reinterpret_cast<float*>(sm + pl.part_off);
-    uint8_t* ring = sm + pl.ring_off;
+    float* mpart = reinterpret_cast<float*>(sm + pl.mpart_off);
+    uint8_t* slot = sm + pl.slot_off;
     const RowLayout L = layout_of(a.W.w, rb);
-    const int NRG = (a.W.rows + 15) >> 4;
-    const int G = gridDim.x;
-    if ((int)blockIdx.x >= NRG) return;
-    const int nunits = (NRG - 1 - (int)blockIdx.x) / G + 1;
+    const int r0 = 16 * (int)blockIdx.x, r1 = min(a.W.rows, r0 + 16);
     if (tid == 0) {
-        for (int s = 0; s < RING; s++) mbar_init(&bar[s], 1);
+        mbar_init(&bar[0], 1);
         mbar_fence_init();
+        mbar_expect_tx(&bar[0], rows_bytes(L, a.W.w, rb, r0, r1) + xf_bytes_of(m, K));
+        issue_rows(L, a.W.w, rb, r0, r1, slot, &bar[0]);
+        issue_xf(a.xf, [](int i) { return i; }, m, K, sfrag, ssum, &bar[0]);
     }
-    if (tid < 8) tok[tid] = tid;
     __syncthreads();
-    auto rows_of = [&](int i, int& r0, int& r1) {
-        r0 = 16 * ((int)blockIdx.x + i * G);
-        r1 = min(a.W.rows, r0 + 16);
-    };
-    int issued = 0;
-    auto issue = [&]() {
-        int r0, r1;
-        rows_of(issued, r0, r1);
-        uint64_t* b = &bar[issued % RING];
-        mbar_expect_tx(b, rows_bytes(L, a.W.w, rb, r0, r1));
-        issue_rows(L, a.W.w, rb, r0, r1, ring + (size_t)(issued % RING) * pl.slot, b);
-        issued++;
-    };
-    if (tid == 0)
-        while (issued < min(RING, nunits)) issue();
-    for (int i = 0; i < nunits; i++) {
-        int r0, r1;
-        rows_of(i, r0, r1);
-        const bool ok = mbar_wait_bounded(&bar[i % RING], (uint32_t)(i / RING) & 1u);
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) {
-                flag(a.status, ST_WAIT_TIMEOUT);
-                drain_ring(bar, issued, i, RING);
-            }
-            return;
+    if (__syncthreads_or(!mbar_wait_bounded(&bar[0], 0u))) {
+        if (tid == 0) {
+            flag(a.status, ST_WAIT_TIMEOUT);
+            drain_ring(bar, 1, 0, 1);
         }
-        const uint8_t* rows = ring + (size_t)(i % RING) * pl.slot + rows_lead(L, a.W.w, rb, r0);
-        tile_scales<QT>(rows, L.stride, nsb, a.xf, tok, m, scl, mins);
-        __syncthreads();
-        tile_tasks<QT, NSET>(rows, L.stride, nsb, a.xf, tok, m, scl, part, 0);
-        __syncthreads();
-        for (int j = tid; j < (r1 - r0) * m; j += NTS) {
-            const int r = j / m, tk = j - r * m;
-            const float v = tile_value<NSET>(part, 0, r, nsb, tk, __ldg(a.xf.tsc + tk), mins);
-            float* y = a.Y + (size_t)tk * a.ldy + r0 + r;
-            *y = a.accumulate ? *y + v : v;
-        }
-        __syncthreads();
-        if (tid == 0 && issued < nunits) issue();
+        return;
+    }
+    const uint8_t* rows = slot + rows_lead(L, a.W.w, rb, r0);
+    tile_tasks<QT, NSET>(rows, L.stride, nsb, reinterpret_cast<const uint2*>(sfrag), ssum, m, part, mpart, 0);
+    __syncthreads();
+    for (int j = tid; j < (r1 - r0) * m; j += blockDim.x) {
+        const int r = j / m, tk = j - r * m;
+        const float v = tile_value<NSET>(part, mpart, 0, r, nsb, tk, __ldg(a.xf.tsc + tk));
+        float* y = a.Y + (size_t)tk * a.ldy + r0 + r;
+        *y = a.accumulate ? *y + v : v;
     }
 }
+
 // ------------------------------------------------------------------------------------------------
 // routing + permutation (single CTA of 1024 threads)
 // ------------------------------------------------------------------------------------------------
@@ -384,6 +388,7 @@ __global__ void __launch_bounds__(1024) k_route_permute(MoeArgs a) {
     // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022)
     const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
     constexpr int PER = MAX_EXPERTS / 32;
+    const int per = (E + 31) >> 5;  // entries per lane
     for (int t = warp; t < T; t += nwarp) {
         const float* lg = a.logits + (size_t)t * E;
         float l[PER];
@@ -391,7 +396,7 @@ __global__ void __launch_bounds__(1024) k_route_permute(MoeArgs a) {
 #pragma unroll
         for (int i = 0; i < PER; i++) {
             const int e = lane + 32 * i;
-            l[i] = e < E ? lg[e] : -INFINITY;
+            l[i] = (i < per && e < E) ? lg[e] : -INFINITY;
             mx = fmaxf(mx, l[i]);
         }
 #pragma unroll
@@ -399,7 +404,8 @@ __global__ void __launch_bounds__(1024) k_route_permute(MoeArgs a) {
         // r = exp(l - max): the difference in fp32 as on the CPU, the exponential correctly rounded
         float r[PER];
 #pragma unroll
-        for (int i = 0; i < PER; i++) r[i] = (lane + 32 * i) < E ? (float)exp((double)(l[i] - mx)) : -1.0f;
+        for (int i = 0; i < PER; i++)
+            r[i] = (i < per && (lane + 32 * i) < E) ? (float)exp((double)(l[i] - mx)) : -1.0f;
         unsigned used = 0;
         float tot = 0.f;
         int my_e = -1;
@@ -408,6 +414,7 @@ __global__ void __launch_bounds__(1024) k_route_permute(MoeArgs a) {
             Cand best{-2.0f, 0x7fffffff};
 #pragma unroll
             for (int i = 0; i < PER; i++) {
+                if (i >= per) break;
                 const Cand c{r[i], lane + 32 * i};
                 if (!((used >> i) & 1u) && (lane + 32 * i) < E && better(c, best)) best = c;
             }
@@ -492,111 +499,84 @@ __global__ void __launch_bounds__(1024) k_route_permute(MoeArgs a) {
 // gate + up + SiLU*mul: units = (active expert, 16-row group), contiguous unit ranges per CTA
 // ------------------------------------------------------------------------------------------------
 struct UPlan {
-    size_t sclg_off, sclu_off, minsg_off, minsu_off, part_off, ring_off, up_at, slot, total;
+    GPlan u;
+    size_t up_at;
 };
 __host__ __device__ inline UPlan gateup_plan(int qg, int qu, int D, size_t rbg, size_t rbu) {
+    (void)qg;
+    (void)qu;
     UPlan p;
-    const int nsb = D / 256;
-    p.sclg_off = 256;
-    p.sclu_off = al128(p.sclg_off + (size_t)16 * nsb * groups_of(qg) * 4);
-    p.minsg_off = al128(p.sclu_off + (size_t)16 * nsb * groups_of(qu) * 4);
-    p.minsu_off = al128(p.minsg_off + (size_t)4 * SETS * 16 * nsb * 4);
-    p.part_off = al128(p.minsu_off + (size_t)4 * SETS * 16 * nsb * 4);
-    p.ring_off = al128(p.part_off + (size_t)2 * nsb * 2 * SETS * 256);
     p.up_at = slot_bytes(row_layout(rbg, true), 16);
-    p.slot = p.up_at + slot_bytes(row_layout(rbu, true), 16);
-    p.total = p.ring_off + RING * p.slot;
+    p.u = unit_plan(D, MPASS, 4 * (D / 256), 1, p.up_at + slot_bytes(row_layout(rbu, true), 16));
     return p;
 }
 
 template <int QG, int QU, int NSET>
 __device__ __forceinline__ void gateup_tasks(const uint8_t* grows, int gstride, const uint8_t* urows, int ustride,
-                                             int nsb, const XF& xf, const int* tok, int m, const float* sclg,
-                                             const float* sclu, float* part) {
-    tile_tasks<QG, NSET>(grows, gstride, nsb, xf, tok, m, sclg, part, 0);
-    tile_tasks<QU, NSET>(urows, ustride, nsb, xf, tok, m, sclu, part, 2 * nsb);
+                                             int nsb, const uint2* sfrag, const float* ssum, int m, float* part,
+                                             float* mpart) {
+    tile_tasks<QG, NSET>(grows, gstride, nsb, sfrag, ssum, m, part, mpart, 0);
+    tile_tasks<QU, NSET>(urows, ustride, nsb, sfrag, ssum, m, part, mpart, 2 * nsb);
 }
 
 template <int QG, int QU>
-__global__ void __launch_bounds__(NTS) k_moe_gateup(MoeArgs a) {
+__global__ void __launch_bounds__(NTU) k_moe_gateup(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int D = a.D, FF = a.FF, nsb = D >> 8, tid = threadIdx.x;
     const UPlan pl = gateup_plan(QG, QU, D, a.gate_rb, a.up_rb);
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
     int* tok = reinterpret_cast<int*>(sm + 64);
-    float* sclg = reinterpret_cast<float*>(sm + pl.sclg_off);
-    float* sclu = reinterpret_cast<float*>(sm + pl.sclu_off);
-    float* minsg = reinterpret_cast<float*>(sm + pl.minsg_off);
-    float* minsu = reinterpret_cast<float*>(sm + pl.minsu_off);
-    float* part = reinterpret_cast<float*>(sm + pl.part_off);
-    uint8_t* ring = sm + pl.ring_off;
+    uint8_t* sfrag = sm + pl.u.sfrag_off;
+    float* ssum = reinterpret_cast<float*>(sm + pl.u.ssum_off);
+    float* part = reinterpret_cast<float*>(sm + pl.u.part_off);
+    float* mpart = reinterpret_cast<float*>(sm + pl.u.mpart_off);
+    uint8_t* slot = sm + pl.u.slot_off;
 
     const int NRG = FF >> 4;
     const int nact = a.rw.active[0];
-    const long long U = (long long)nact * NRG;
-    const int u0 = (int)(U * blockIdx.x / gridDim.x), u1 = (int)(U * (blockIdx.x + 1) / gridDim.x);
-    if (u0 >= u1) return;
+    const int ai = (int)blockIdx.x / NRG, r0 = 16 * ((int)blockIdx.x - ai * NRG);
+    if (ai >= nact) return;  // the grid covers the largest possible number of active experts
+    const int e = a.rw.active[1 + ai];
+    const int s0 = a.rw.offsets[e], me = a.rw.offsets[e + 1] - s0;
+    const RowLayout Lg = layout_of(a.gate[e], a.gate_rb), Lu = layout_of(a.up[e], a.up_rb);
+    const uint8_t* grows = slot + rows_lead(Lg, a.gate[e], a.gate_rb, r0);
+    const uint8_t* urows = slot + pl.up_at + rows_lead(Lu, a.up[e], a.up_rb, r0);
     if (tid == 0) {
-        for (int s = 0; s < RING; s++) mbar_init(&bar[s], 1);
+        mbar_init(&bar[0], 1);
         mbar_fence_init();
     }
-    __syncthreads();
-    int issued = 0;
-    auto issue = [&]() {
-        const int u = u0 + issued, ai = u / NRG, r0 = 16 * (u - ai * NRG);
-        const int e = a.rw.active[1 + ai];
-        const RowLayout Lg = layout_of(a.gate[e], a.gate_rb), Lu = layout_of(a.up[e], a.up_rb);
-        uint8_t* dst = ring + (size_t)(issued % RING) * pl.slot;
-        uint64_t* b = &bar[issued % RING];
-        mbar_expect_tx(b, rows_bytes(Lg, a.gate[e], a.gate_rb, r0, r0 + 16) + rows_bytes(Lu, a.up[e], a.up_rb, r0, r0 + 16));
-        issue_rows(Lg, a.gate[e], a.gate_rb, r0, r0 + 16, dst, b);
-        issue_rows(Lu, a.up[e], a.up_rb, r0, r0 + 16, dst + pl.up_at, b);
-        issued++;
-    };
-    if (tid == 0)
-        while (issued < min(RING, u1 - u0)) issue();
-    for (int i = 0; i < u1 - u0; i++) {
-        const int u = u0 + i, ai = u / NRG, r0 = 16 * (u - ai * NRG);
-        const int e = a.rw.active[1 + ai];
-        const int s0 = a.rw.offsets[e], me = a.rw.offsets[e + 1] - s0;
-        const RowLayout Lg = layout_of(a.gate[e], a.gate_rb), Lu = layout_of(a.up[e], a.up_rb);
-        const uint8_t* slot = ring + (size_t)(i % RING) * pl.slot;
-        const uint8_t* grows = slot + rows_lead(Lg, a.gate[e], a.gate_rb, r0);
-        const uint8_t* urows = slot + pl.up_at + rows_lead(Lu, a.up[e], a.up_rb, r0);
-        const bool ok = mbar_wait_bounded(&bar[i % RING], (uint32_t)(i / RING) & 1u);
-        if (__syncthreads_or(!ok)) {
+    for (int c0 = 0, pass = 0; c0 < me; c0 += MPASS, pass++) {
+        const int mc = min(MPASS, me - c0);
+        if (tid < mc) tok[tid] = a.rw.slot_token[s0 + c0 + tid];
+        __syncthreads();  // tok visible; the previous pass is done with the staged activations
+        if (tid == 0) {
+            uint32_t bytes = xf_bytes_of(mc, D);
+            if (pass == 0) bytes += rows_bytes(Lg, a.gate[e], a.gate_rb, r0, r0 + 16) + rows_bytes(Lu, a.up[e], a.up_rb, r0, r0 + 16);
+            mbar_expect_tx(&bar[0], bytes);
+            if (pass == 0) {
+                issue_rows(Lg, a.gate[e], a.gate_rb, r0, r0 + 16, slot, &bar[0]);
+                issue_rows(Lu, a.up[e], a.up_rb, r0, r0 + 16, slot + pl.up_at, &bar[0]);
+            }
+            issue_xf(a.xf, [&](int i) { return tok[i]; }, mc, D, sfrag, ssum, &bar[0]);
+        }
+        if (__syncthreads_or(!mbar_wait_bounded(&bar[0], (uint32_t)pass & 1u))) {
             if (tid == 0) {
                 flag(a.status, ST_WAIT_TIMEOUT);
-                drain_ring(bar, issued, i, RING);
+                drain_ring(bar, pass + 1, pass, 1);
             }
             return;
         }
-        for (int c0 = 0; c0 < me; c0 += 4 * SETS) {
-            const int mc = min(4 * SETS, me - c0);
-            if (tid < mc) tok[tid] = a.rw.slot_token[s0 + c0 + tid];
-            __syncthreads();
-            tile_scales<QG>(grows, Lg.stride, nsb, a.xf, tok, mc, sclg, minsg);
-            tile_scales<QU>(urows, Lu.stride, nsb, a.xf, tok, mc, sclu, minsu);
-            __syncthreads();
-            if (mc > 4) gateup_tasks<QG, QU, 2>(grows, Lg.stride, urows, Lu.stride, nsb, a.xf, tok, mc, sclg, sclu, part);
-            else gateup_tasks<QG, QU, 1>(grows, Lg.stride, urows, Lu.stride, nsb, a.xf, tok, mc, sclg, sclu, part);
-            __syncthreads();
-            for (int j = tid; j < 16 * mc; j += NTS) {
-                const int r = j / mc, tk = j - r * mc;
-                const float ts = __ldg(a.xf.tsc + tok[tk]);
-                float g, u;
-                if (mc > 4) {
-                    g = tile_value<2>(part, 0, r, nsb, tk, ts, minsg);
-                    u = tile_value<2>(part, 2 * nsb, r, nsb, tk, ts, minsu);
-                } else {
-                    g = tile_value<1>(part, 0, r, nsb, tk, ts, minsg);
-                    u = tile_value<1>(part, 2 * nsb, r, nsb, tk, ts, minsu);
-                }
-                a.h[(size_t)(s0 + c0 + tk) * FF + r0 + r] = silu_mul(g, u);
-            }
-            __syncthreads();
+        gateup_tasks<QG, QU, 1>(grows, Lg.stride, urows, Lu.stride, nsb, reinterpret_cast<const uint2*>(sfrag), ssum, mc,
+                                part, mpart);
+        __syncthreads();
+        for (int j = tid; j < 16 * mc; j += blockDim.x) {
+            const int r = j / mc, tk = j - r * mc;
+            const float ts = __ldg(a.xf.tsc + tok[tk]);
+            const float g = tile_value<1>(part, mpart, 0, r, nsb, tk, ts);
+            const float u = tile_value<1>(part, mpart, 2 * nsb, r, nsb, tk, ts);
+            a.h[(size_t)(s0 + c0 + tk) * FF + r0 + r] = silu_mul(g, u);
         }
-        if (tid == 0 && issued < u1 - u0) issue();
+        __syncthreads();  // tok and the staged activations are rewritten by the next pass
     }
 }
 
@@ -606,118 +586,81 @@ __global__ void __launch_bounds__(NTS) k_moe_gateup(MoeArgs a) {
 // row group (a per-group counter reaches the number of active experts) adds each token's expert
 // outputs in ascending expert order, weighted, to the residual (qwen3moe.cpp:1024-1069).
 // ------------------------------------------------------------------------------------------------
-struct DPlan {
-    size_t scl_off, mins_off, part_off, ring_off, slot, total;
-};
-__host__ __device__ inline DPlan down_plan(int qd, int FF, size_t rb) {
-    DPlan p;
-    const int nsb = FF / 256;
-    p.scl_off = 256;
-    p.mins_off = al128(p.scl_off + (size_t)16 * nsb * groups_of(qd) * 4);
-    p.part_off = al128(p.mins_off + (size_t)4 * SETS * 16 * nsb * 4);
-    p.ring_off = al128(p.part_off + (size_t)nsb * 2 * SETS * 256);
-    p.slot = slot_bytes(row_layout(rb, true), 16);
-    p.total = p.ring_off + RING * p.slot;
-    return p;
+__host__ __device__ inline GPlan down_plan(int qd, int FF, size_t rb) {
+    (void)qd;
+    return unit_plan(FF, MPASS, 2 * (FF / 256), 1, slot_bytes(row_layout(rb, true), 16));
 }
 
 template <int QD>
-__global__ void __launch_bounds__(NTS) k_moe_down(MoeArgs a) {
+__global__ void __launch_bounds__(NTU) k_moe_down(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ int s_last;
     const int D = a.D, FF = a.FF, nsb = FF >> 8, T = a.T, K = a.n_used, tid = threadIdx.x;
     const size_t rb = a.down_rb;
-    const DPlan pl = down_plan(QD, FF, rb);
+    const GPlan pl = down_plan(QD, FF, rb);
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
-    int* tok = reinterpret_cast<int*>(sm + 64);
-    float* scl = reinterpret_cast<float*>(sm + pl.scl_off);
-    float* mins = reinterpret_cast<float*>(sm + pl.mins_off);
+    uint8_t* sfrag = sm + pl.sfrag_off;
+    float* ssum = reinterpret_cast<float*>(sm + pl.ssum_off);
     float* part = reinterpret_cast<float*>(sm + pl.part_off);
-    uint8_t* ring = sm + pl.ring_off;
+    float* mpart = reinterpret_cast<float*>(sm + pl.mpart_off);
+    uint8_t* slot = sm + pl.slot_off;
 
-    const int NRG = D >> 4;
     const int nact = a.rw.active[0];
-    const int* act = a.rw.active + 1;
-    const int* off = a.rw.offsets;
-    const long long U = (long long)NRG * nact;
-    const int u0 = (int)(U * blockIdx.x / gridDim.x), u1 = (int)(U * (blockIdx.x + 1) / gridDim.x);
-    if (u0 >= u1) return;
+    const int rg = (int)blockIdx.x, ai = (int)blockIdx.y, r0 = 16 * rg;
+    if (ai >= nact) return;  // grid.y covers the largest possible number of active experts
+    const int e = a.rw.active[1 + ai];
+    const int s0 = a.rw.offsets[e], me = a.rw.offsets[e + 1] - s0;
+    const uint8_t* w = a.down[e];
+    const RowLayout L = layout_of(w, rb);
+    const uint8_t* rows = slot + rows_lead(L, w, rb, r0);
     if (tid == 0) {
-        for (int s = 0; s < RING; s++) mbar_init(&bar[s], 1);
+        mbar_init(&bar[0], 1);
         mbar_fence_init();
     }
-    __syncthreads();
-    int issued = 0;
-    auto issue = [&]() {
-        const int u = u0 + issued, rg = u / nact, ai = u - rg * nact;
-        const uint8_t* w = a.down[act[ai]];
-        const RowLayout L = layout_of(w, rb);
-        uint64_t* b = &bar[issued % RING];
-        mbar_expect_tx(b, rows_bytes(L, w, rb, 16 * rg, 16 * rg + 16));
-        issue_rows(L, w, rb, 16 * rg, 16 * rg + 16, ring + (size_t)(issued % RING) * pl.slot, b);
-        issued++;
-    };
-    if (tid == 0)
-        while (issued < min(RING, u1 - u0)) issue();
-    int done_in_group = 0;
-    for (int i = 0; i < u1 - u0; i++) {
-        const int u = u0 + i, rg = u / nact, ai = u - rg * nact, r0 = 16 * rg;
-        const int e = act[ai];
-        const int s0 = off[e], me = off[e + 1] - s0;
-        const uint8_t* w = a.down[e];
-        const RowLayout L = layout_of(w, rb);
-        const uint8_t* rows = ring + (size_t)(i % RING) * pl.slot + rows_lead(L, w, rb, r0);
-        const bool ok = mbar_wait_bounded(&bar[i % RING], (uint32_t)(i / RING) & 1u);
-        if (__syncthreads_or(!ok)) {
+    for (int c0 = 0, pass = 0; c0 < me; c0 += MPASS, pass++) {
+        const int mc = min(MPASS, me - c0);
+        __syncthreads();  // the previous pass is done with the staged activations
+        if (tid == 0) {
+            uint32_t bytes = xf_bytes_of(mc, FF);
+            if (pass == 0) bytes += rows_bytes(L, w, rb, r0, r0 + 16);
+            mbar_expect_tx(&bar[0], bytes);
+            if (pass == 0) issue_rows(L, w, rb, r0, r0 + 16, slot, &bar[0]);
+            issue_xf(a.hf, [&](int i) { return s0 + c0 + i; }, mc, FF, sfrag, ssum, &bar[0]);  // xf rows = slots
+        }
+        if (__syncthreads_or(!mbar_wait_bounded(&bar[0], (uint32_t)pass & 1u))) {
             if (tid == 0) {
                 flag(a.status, ST_WAIT_TIMEOUT);
-                drain_ring(bar, issued, i, RING);
+                drain_ring(bar, pass + 1, pass, 1);
             }
             return;
         }
-        for (int c0 = 0; c0 < me; c0 += 4 * SETS) {
-            const int mc = min(4 * SETS, me - c0);
-            if (tid < mc) tok[tid] = s0 + c0 + tid;  // xf rows of the down input are slots
-            __syncthreads();
-            tile_scales<QD>(rows, L.stride, nsb, a.hf, tok, mc, scl, mins);
-            __syncthreads();
-            if (mc > 4) tile_tasks<QD, 2>(rows, L.stride, nsb, a.hf, tok, mc, scl, part, 0);
-            else tile_tasks<QD, 1>(rows, L.stride, nsb, a.hf, tok, mc, scl, part, 0);
-            __syncthreads();
-            for (int j = tid; j < 16 * mc; j += NTS) {
-                const int r = j / mc, tk = j - r * mc;
-                const float ts = __ldg(a.hf.tsc + tok[tk]);
-                const float v = mc > 4 ? tile_value<2>(part, 0, r, nsb, tk, ts, mins) : tile_value<1>(part, 0, r, nsb, tk, ts, mins);
-                a.y[(size_t)(s0 + c0 + tk) * D + r0 + r] = v;
-            }
-            __syncthreads();
-        }
-        if (tid == 0 && issued < u1 - u0) issue();
-        done_in_group++;
-        const bool group_end = (i + 1 == u1 - u0) || ((u + 1) / nact != rg);
-        if (group_end) {
-            // publish this CTA's expert outputs of the group; the CTA that completes it combines
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) s_last = (atomicAdd(&a.rw.group_done[rg], done_in_group) + done_in_group == nact);
-            __syncthreads();
-            done_in_group = 0;
-            if (s_last) {
-                __threadfence();
-                for (int j = tid; j < T * 16; j += NTS) {
-                    const int t = j >> 4, r = j & 15;
-                    const int* ts = a.rw.token_slots + (size_t)t * K;
-                    float acc = 0.f;
-                    for (int k = 0; k < K; k++) {
-                        const int s = ts[k];
-                        acc = fmaf(a.rw.slot_w[s], __ldcg(a.y + (size_t)s * D + r0 + r), acc);
-                    }
-                    a.x[(size_t)t * D + r0 + r] += acc;
-                }
-                if (tid == 0) a.rw.group_done[rg] = 0;  // ready for the next call
-            }
+        tile_tasks<QD, 1>(rows, L.stride, nsb, reinterpret_cast<const uint2*>(sfrag), ssum, mc, part, mpart, 0);
+        __syncthreads();
+        for (int j = tid; j < 16 * mc; j += blockDim.x) {
+            const int r = j / mc, tk = j - r * mc;
+            const float ts = __ldg(a.hf.tsc + s0 + c0 + tk);
+            const float v = tile_value<1>(part, mpart, 0, r, nsb, tk, ts);
+            a.y[(size_t)(s0 + c0 + tk) * D + r0 + r] = v;
         }
     }
+    // publish this expert's rows of the group; the CTA that completes the group combines it
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&a.rw.group_done[rg], 1) + 1 == nact);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int j = tid; j < T * 16; j += blockDim.x) {
+        const int t = j >> 4, r = j & 15;
+        const int* ts = a.rw.token_slots + (size_t)t * K;
+        float acc = 0.f;
+        for (int k = 0; k < K; k++) {  // ascending slots = ascending experts (qwen3moe.cpp:1025)
+            const int s = ts[k];
+            acc = fmaf(a.rw.slot_w[s], __ldcg(a.y + (size_t)s * D + r0 + r), acc);
+        }
+        a.x[(size_t)t * D + r0 + r] += acc;
+    }
+    if (tid == 0) a.rw.group_done[rg] = 0;  // ready for the next call
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -734,57 +677,56 @@ int sm_count() {
     return n;
 }
 
-// Persistent grid of a kernel: SMs x resident CTAs at this shared-memory size.
-template <typename Kern>
-static int persistent_grid(Kern k, size_t smem) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    int per = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, NTS, smem) != cudaSuccess || per < 1) per = 1;
-    return sm_count() * per;
-}
-
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 constexpr size_t SMEM_CAP = 227 * 1024;
 
 bool gemv_mma_ok(const QMat& W) {
     return is_kquant(W.type) && W.K % 256 == 0 && W.row_bytes == (size_t)(W.K / 256) * block_bytes(W.type) &&
-           gemv_plan(W.type, W.K, W.row_bytes, SETS).total <= SMEM_CAP;
+           gemv_plan(W.type, W.K, W.row_bytes, SETS, TPASS).total <= SMEM_CAP;
 }
 
-size_t xf_bytes(int rows, int K) { return (size_t)rows * K * 4 + (size_t)rows * (K / 16) * 4 + (size_t)rows * 4 + 256; }
+// XF block of `rows` rows: digits (3 bytes per element), per-16 sums, per-row scale.
+size_t xf_bytes(int rows, int K) { return (size_t)rows * K * 3 + (size_t)rows * (K / 16) * 4 + (size_t)rows * 4 + 256; }
 XF xf_carve(void* base, int rows, int K) {
     uint8_t* p = static_cast<uint8_t*>(base);
     XF x;
     x.frag = reinterpret_cast<const uint2*>(p);
-    x.sum = reinterpret_cast<const float*>(p + (size_t)rows * K * 4);
-    x.tsc = reinterpret_cast<const float*>(p + (size_t)rows * K * 4 + (size_t)rows * (K / 16) * 4);
+    x.sum = reinterpret_cast<const float*>(p + (size_t)rows * K * 3);
+    x.tsc = reinterpret_cast<const float*>(p + (size_t)rows * K * 3 + (size_t)rows * (K / 16) * 4);
     x.nseg = K / 16;
     return x;
 }
 
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st) {
-    if (rows < 1 || K % 16 || ldx % 4 || !aligned16(X)) return cudaErrorInvalidValue;
+    if (rows < 1 || K % 32 || ldx % 4 || !aligned16(X)) return cudaErrorInvalidValue;
     k_prep_x<<<rows, PREP_NT, 0, st>>>(X, ldx, K, const_cast<uint2*>(out.frag), const_cast<float*>(out.sum),
                                        const_cast<float*>(out.tsc));
     return cudaGetLastError();
 }
 
+// Raises a kernel's dynamic shared-memory limit once per kernel and size (host-side bookkeeping only).
+template <typename Kern>
+static void smem_attr(Kern k, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, size_t> done;
+    std::lock_guard<std::mutex> g(mu);
+    size_t& cur = done[reinterpret_cast<const void*>(k)];
+    if (cur < smem) {
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cur = smem;
+    }
+}
+
 template <int QT, int NSET>
 static void gemv_go(const GemvXArgs& a, cudaStream_t st) {
-    const GPlan pl = gemv_plan(QT, a.W.K, a.W.row_bytes, NSET);
-    const int nrg = (a.W.rows + 15) / 16;
-    static int grid = 0;
-    static size_t grid_smem = 0;
-    if (grid_smem != pl.total) {
-        grid = persistent_grid(k_gemv<QT, NSET>, pl.total);
-        grid_smem = pl.total;
-    }
-    k_gemv<QT, NSET><<<std::min(grid, nrg), NTS, pl.total, st>>>(a);
+    const GPlan pl = gemv_plan(QT, a.W.K, a.W.row_bytes, NSET, a.m);
+    smem_attr(k_gemv<QT, NSET>, pl.total);
+    k_gemv<QT, NSET><<<(a.W.rows + 15) / 16, NTU, pl.total, st>>>(a);
 }
 
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st) {
-    if (a.m < 1 || a.m > 4 * SETS || !gemv_mma_ok(a.W)) return cudaErrorInvalidValue;
-    const bool two = a.m > 4;
+    if (a.m < 1 || a.m > TPASS || !gemv_mma_ok(a.W)) return cudaErrorInvalidValue;
+    const bool two = a.m > TOK_PER_SET;
     switch (a.W.type) {
         case T_Q4_K: two ? gemv_go<T_Q4_K, 2>(a, st) : gemv_go<T_Q4_K, 1>(a, st); break;
         case T_Q5_K: two ? gemv_go<T_Q5_K, 2>(a, st) : gemv_go<T_Q5_K, 1>(a, st); break;
@@ -802,21 +744,18 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
 cudaError_t launch_route_permute(const MoeArgs& a, cudaStream_t st) {
     if (a.T < 1 || a.T > ROUTE_TMAX || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert)
         return cudaErrorInvalidValue;
-    k_route_permute<<<1, 1024, 0, st>>>(a);
+    const int threads = a.T <= 4 ? 128 : (a.T <= 32 ? 512 : 1024);  // one warp per token, at most 32
+    k_route_permute<<<1, threads, 0, st>>>(a);
     return cudaGetLastError();
 }
 
 template <int QG, int QU>
 static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
     const UPlan pl = gateup_plan(QG, QU, a.D, a.gate_rb, a.up_rb);
-    if (pl.total > SMEM_CAP) return cudaErrorInvalidValue;
-    static int grid = 0;
-    static size_t grid_smem = 0;
-    if (grid_smem != pl.total) {
-        grid = persistent_grid(k_moe_gateup<QG, QU>, pl.total);
-        grid_smem = pl.total;
-    }
-    k_moe_gateup<QG, QU><<<grid, NTS, pl.total, st>>>(a);
+    if (pl.u.total > SMEM_CAP) return cudaErrorInvalidValue;
+    smem_attr(k_moe_gateup<QG, QU>, pl.u.total);
+    const int maxact = std::min(a.n_expert, a.T * a.n_used);
+    k_moe_gateup<QG, QU><<<maxact * (a.FF / 16), NTU, pl.u.total, st>>>(a);
     return cudaGetLastError();
 }
 template <int QG>
@@ -840,15 +779,11 @@ cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st) {
 
 template <int QD>
 static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
-    const DPlan pl = down_plan(QD, a.FF, a.down_rb);
+    const GPlan pl = down_plan(QD, a.FF, a.down_rb);
     if (pl.total > SMEM_CAP) return cudaErrorInvalidValue;
-    static int grid = 0;
-    static size_t grid_smem = 0;
-    if (grid_smem != pl.total) {
-        grid = persistent_grid(k_moe_down<QD>, pl.total);
-        grid_smem = pl.total;
-    }
-    k_moe_down<QD><<<grid, NTS, pl.total, st>>>(a);
+    smem_attr(k_moe_down<QD>, pl.total);
+    const int maxact = std::min(a.n_expert, a.T * a.n_used);
+    k_moe_down<QD><<<dim3(a.D / 16, maxact), NTU, pl.total, st>>>(a);
     return cudaGetLastError();
 }
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {

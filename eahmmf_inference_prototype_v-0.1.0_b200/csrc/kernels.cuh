@@ -8,7 +8,8 @@
 
 namespace eb {
 
-constexpr int MT = 8;               // tokens handled per pass over a weight tile
+constexpr int MT = 8;               // tokens per pass of the per-row kernel
+constexpr int XPASS = 4;            // tokens per pass of the tensor-core GEMV
 constexpr int STAGES = 3;           // TMA ring depth
 constexpr int DOWN_TMAX = 64;       // tokens per call handled by the row-parallel down/combine kernel
 constexpr int ROUTE_TMAX = 256;     // tokens per call handled by the single-CTA route/permute kernel
@@ -68,7 +69,7 @@ struct MoeArgs {
     int* status;
 };
 
-// Dense GEMV on activations already in fragment form: Y[t*ldy + r] (=|+=) row r . x_t, t < m <= 8.
+// Dense GEMV on activations already in fragment form: Y[t*ldy + r] (=|+=) row r . x_t, t < m <= XPASS.
 struct GemvXArgs {
     QMat W;
     XF xf;

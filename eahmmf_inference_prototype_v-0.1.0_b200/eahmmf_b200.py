@@ -36,6 +36,8 @@ EXPORTS = {
     "eahmmf_cuda_moe_workspace_bytes": (C.c_size_t, [C.POINTER(EahmmfMoeLayer), C.c_int]),
     "eahmmf_cuda_moe_layer": (C.c_int, [C.POINTER(EahmmfMoeLayer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+    "eahmmf_cuda_moe_profile": (C.c_int, [C.c_int]),
+    "eahmmf_cuda_moe_profile_read": (C.c_int, [C.c_void_p, C.c_int]),
     "eahmmf_cuda_gemv_workspace_bytes": (C.c_size_t, [C.c_int]),
     "eahmmf_cuda_gemv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int, C.c_int,
                                    C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
@@ -160,6 +162,19 @@ class MoeLayer:
     def __call__(self, T: int, d_xn, d_logits, d_x, d_ws, stream=None, d_status=None) -> int:
         return lib().eahmmf_cuda_moe_layer(C.byref(self.desc), T, _ptr(d_xn), _ptr(d_logits), _ptr(d_x), _ptr(d_ws),
                                            d_ws.numel() * d_ws.element_size(), _stream(stream), _ptr(d_status))
+
+    @staticmethod
+    def profile(enable: bool) -> None:
+        if lib().eahmmf_cuda_moe_profile(int(enable)):
+            raise RuntimeError("eahmmf_cuda_moe_profile failed")
+
+    @staticmethod
+    def profile_read() -> np.ndarray:
+        """Stage durations (us) of the last call: router GEMV, prep, route/permute, gate/up, h prep, down."""
+        us = np.zeros(6, np.float32)
+        if lib().eahmmf_cuda_moe_profile_read(us.ctypes.data, 6):
+            raise RuntimeError("eahmmf_cuda_moe_profile_read failed")
+        return us
 
     def routing(self, d_ws, T: int):
         """(ids, weights) of the last call, read from the head of the workspace."""

@@ -90,6 +90,13 @@ size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
 int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                           void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);
 
+/* Stage timing of eahmmf_cuda_moe_layer: when enabled, each call records CUDA events on its stream
+ * around its six stages (router GEMV, activation prep, route/permute, gate/up, h prep, down/combine);
+ * eahmmf_cuda_moe_profile_read waits for the last call and returns the six stage durations (us) of its
+ * last 64-token block. Off by default; single-threaded use. */
+int eahmmf_cuda_moe_profile(int enable);
+int eahmmf_cuda_moe_profile_read(float* us, int cap);
+
 /* Dense quantized GEMV on device buffers: d_out[t*ldo + r] (=, or += when accumulate) dot(row r, d_x[t*ldx..]),
  * the reference's matmul (qwen3moe.cpp:397-419) with device activations. K-quant rows run on the tensor
  * cores once the activations are in fragment form, which needs eahmmf_cuda_gemv_workspace_bytes(ne0)
