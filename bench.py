@@ -273,6 +273,26 @@ def run_ours(args, rank: int, world: int, local: int):
     return line
 
 
+def profile_case(T: int) -> int:
+    """Three calls of the config-2 MoE layer at T tokens on fixed seeded inputs, nothing timed: the
+    small case ncu captures are taken on (a few hundred MB on the device)."""
+    import torch
+    import eahmmf_b200 as eb
+    import synth
+    ex = synth.expert_set()
+    layer = eb.MoeLayer.from_expert_set(ex, n_used=8)
+    xt = torch.from_numpy(synth.activations(T, ex.D, 5)).cuda()
+    lg = torch.from_numpy(synth.router_logits(T, ex.n_expert, 6)).cuda()
+    ws = torch.zeros(layer.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        st = layer(T, xt, lg, xt.clone(), ws)
+        if st:
+            raise RuntimeError(f"eahmmf_cuda_moe_layer returned {st}")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": T, "ok": True}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -281,7 +301,11 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile-case", type=int, metavar="T", default=0,
+                    help="no timing: run the config-2 layer three times at T tokens (a small case for ncu)")
     args = ap.parse_args()
+    if args.profile_case:
+        return profile_case(args.profile_case)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
