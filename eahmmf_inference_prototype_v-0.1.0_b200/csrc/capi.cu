@@ -2,6 +2,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/eahmmf_b200.h"
 #include "common.cuh"
@@ -44,7 +45,7 @@ bool fragment_path(const QMat& W, const float* dx, int ldx) {
     return !use_generic() && gemv_mma_ok(W) && (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && ldx % 4 == 0;
 }
 // Workspace of gemv_all: the activations of one pass in fragment form.
-size_t gemv_ws_bytes(int K) { return xf_bytes(XPASS, K); }
+constexpr size_t gemv_ws_bytes(int K) { return xf_bytes(XPASS, K); }
 
 // d_out[t*ldo + r] = W x d_x[t*ldx..] for t < nb, MT tokens per pass. The tensor-core path first puts
 // the pass's activations in fragment form (ws, gemv_ws_bytes(K) bytes); other types and layouts take
@@ -310,6 +311,58 @@ extern "C" int eahmmf_cuda_gemv(const uint8_t* d_w, int type, int ne0, int ne1, 
         return ST_BAD_ARG;
     if (d_workspace && workspace_bytes < gemv_ws_bytes(ne0)) return ST_CAPACITY;
     return gemv_all(qmat(d_w, type, ne0, ne1, row_bytes), d_x, nb, ldx, d_out, ldo, accumulate, d_workspace,
+                    reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? ST_OK
+               : ST_CUDA;
+}
+
+// ---- eahmmf_cuda_gemv_static: the same GEMV with its workspace in a fixed device array -------------
+// For callers that may not allocate device memory on this path. The fragment-form activations of one
+// pass live in a file-scope __device__ array sized for ne0 <= EAHMMF_GEMV_STATIC_MAX_NE0; larger
+// rows are refused with EAHMMF_ST_CAPACITY. Every byte a pass reads is written by that pass's prep
+// kernel first, so the array needs no clearing. One array per device: calls that overlap on one
+// device (several streams or threads) race on it.
+namespace {
+constexpr size_t STATIC_WS_BYTES = 224 * 1024;
+static_assert(EAHMMF_GEMV_STATIC_MAX_NE0 % 256 == 0, "row length must be whole super-blocks");
+__device__ __align__(256) uint8_t g_static_ws[STATIC_WS_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[MAX_DEVICES] = {};
+
+// Address of this device's copy of g_static_ws, looked up once per device with that device current.
+void* static_ws(int* err) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
+        *err = ST_CUDA;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> g(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_ws) != cudaSuccess || !p) {
+            *err = ST_CUDA;
+            return nullptr;
+        }
+        g_static_ptr[dev] = p;
+    }
+    return g_static_ptr[dev];
+}
+}  // namespace
+
+extern "C" int eahmmf_cuda_gemv_static(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_bytes,
+                                       const float* d_x, int nb, int ldx, float* d_out, int ldo, int accumulate,
+                                       void* stream) {
+    static_assert(gemv_ws_bytes(EAHMMF_GEMV_STATIC_MAX_NE0) <= STATIC_WS_BYTES, "static workspace too small");
+    if (!type_supported(type)) return ST_BAD_TYPE;
+    if (!d_w || !d_x || !d_out || ne1 <= 0 || nb <= 0 || ldx < ne0 || ldo < ne1 || !shape_ok(type, ne0, row_bytes))
+        return ST_BAD_ARG;
+    if (ne0 > EAHMMF_GEMV_STATIC_MAX_NE0 || gemv_ws_bytes(ne0) > STATIC_WS_BYTES) return ST_CAPACITY;
+    int err = ST_OK;
+    void* ws = static_ws(&err);
+    if (!ws) return err;
+    return gemv_all(qmat(d_w, type, ne0, ne1, row_bytes), d_x, nb, ldx, d_out, ldo, accumulate, ws,
                     reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
                ? ST_OK
                : ST_CUDA;

@@ -685,8 +685,6 @@ bool gemv_mma_ok(const QMat& W) {
            gemv_plan(W.type, W.K, W.row_bytes, SETS, TPASS).total <= SMEM_CAP;
 }
 
-// XF block of `rows` rows: digits (3 bytes per element), per-16 sums, per-row scale.
-size_t xf_bytes(int rows, int K) { return (size_t)rows * K * 3 + (size_t)rows * (K / 16) * 4 + (size_t)rows * 4 + 256; }
 XF xf_carve(void* base, int rows, int K) {
     uint8_t* p = static_cast<uint8_t*>(base);
     XF x;

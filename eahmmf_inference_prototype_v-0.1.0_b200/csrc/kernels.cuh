@@ -82,7 +82,10 @@ struct GemvXArgs {
 
 int sm_count();
 bool gemv_mma_ok(const QMat& W);                 // tensor-core path available for this matrix
-size_t xf_bytes(int rows, int K);                // bytes of an XF block of `rows` rows
+// bytes of an XF block of `rows` rows: digits (3 bytes per element), per-16 sums, per-row scale
+constexpr size_t xf_bytes(int rows, int K) {
+    return (size_t)rows * K * 3 + (size_t)rows * (K / 16) * 4 + (size_t)rows * 4 + 256;
+}
 XF xf_carve(void* base, int rows, int K);        // XF views over such a block
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st);
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st);

@@ -41,6 +41,8 @@ EXPORTS = {
     "eahmmf_cuda_gemv_workspace_bytes": (C.c_size_t, [C.c_int]),
     "eahmmf_cuda_gemv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int, C.c_int,
                                    C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "eahmmf_cuda_gemv_static": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int,
+                                          C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "eahmmf_dev_create": (C.c_void_p, [C.c_size_t]),
     "eahmmf_dev_destroy": (None, [C.c_void_p]),
     "eahmmf_dev_alloc": (C.c_void_p, [C.c_void_p, C.c_size_t]),
@@ -124,6 +126,17 @@ def gemv(d_w, qtype: int, ne0: int, ne1: int, row_bytes: int, d_x, d_out, accumu
     return lib().eahmmf_cuda_gemv(_ptr(d_w), qtype, ne0, ne1, row_bytes, _ptr(d_x), nb, ldx, _ptr(d_out),
                                   d_out.shape[1], int(accumulate), _ptr(ws),
                                   0 if ws is None else ws.numel() * ws.element_size(), _stream(stream))
+
+
+GEMV_STATIC_MAX_NE0 = 16384  # EAHMMF_GEMV_STATIC_MAX_NE0
+
+
+def gemv_static(d_w, qtype: int, ne0: int, ne1: int, row_bytes: int, d_x, d_out, accumulate: bool = False,
+                stream=None) -> int:
+    """eahmmf_cuda_gemv_static: gemv() with the library's fixed device workspace (no allocation)."""
+    nb, ldx = d_x.shape
+    return lib().eahmmf_cuda_gemv_static(_ptr(d_w), qtype, ne0, ne1, row_bytes, _ptr(d_x), nb, ldx, _ptr(d_out),
+                                         d_out.shape[1], int(accumulate), _stream(stream))
 
 
 class MoeLayer:

@@ -106,6 +106,19 @@ int eahmmf_cuda_gemv(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_
                      int ldx, float* d_out, int ldo, int accumulate, void* d_workspace, size_t workspace_bytes,
                      void* stream);
 
+/* eahmmf_cuda_gemv without a caller workspace and without any allocation: no counterpart in the
+ * reference (its expert_cuda.cu grows cudaMalloc'd static buffers on demand). The fragment-form
+ * activations go to a fixed __device__ array of 224 KiB, enough for rows of up to
+ * EAHMMF_GEMV_STATIC_MAX_NE0 elements; a longer ne0 returns EAHMMF_ST_CAPACITY before anything is
+ * launched. Results are identical to eahmmf_cuda_gemv's.
+ *   - The first call on each device, with that device current, looks up the array's address
+ *     (cudaGetSymbolAddress) and keeps it; make that first call before any stream capture begins.
+ *   - There is one array per device: calls that overlap on the same device (several streams or
+ *     host threads) race on it and must be serialised by the caller. */
+#define EAHMMF_GEMV_STATIC_MAX_NE0 16384
+int eahmmf_cuda_gemv_static(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_bytes, const float* d_x,
+                            int nb, int ldx, float* d_out, int ldo, int accumulate, void* stream);
+
 /* ---- 3. device backend (eahmmf::B200Device) --------------------------------------------------- */
 
 typedef struct EahmmfDev EahmmfDev;
