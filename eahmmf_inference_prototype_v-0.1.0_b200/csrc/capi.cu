@@ -145,42 +145,35 @@ extern "C" bool eahmmf_cuda_matmul_pair(const uint8_t* gw, int gt, int gne0, int
 // 2. device-resident MoE block
 // ---------------------------------------------------------------------------------------------------
 namespace {
-constexpr int CHUNK = DOWN_TMAX;  // tokens per MoE block pass
+constexpr int CHUNK = MOE_TMAX;  // tokens per MoE block pass
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 struct WsLayout {
-    size_t ids, wts, logits, offsets, active, slot_token, slot_w, token_slots, h, xf, hf, y, groups, total;
+    size_t ids, wts, logits, offsets, active, slot_token, slot_w, token_slots, ngroups, groups, rg_done, h, xf, y,
+        total;
 };
 WsLayout ws_layout(const EahmmfMoeLayer* L, int T) {
     const int Tc = T < CHUNK ? T : CHUNK;
-    const size_t K = (size_t)L->n_used, E = (size_t)L->n_expert;
+    const size_t K = (size_t)L->n_used, E = (size_t)L->n_expert, S = (size_t)Tc * K;
     WsLayout w;
     size_t o = 0;
-    w.ids = o;
-    o = a256(o + (size_t)T * K * 4);
-    w.wts = o;
-    o = a256(o + (size_t)T * K * 4);
-    w.logits = o;
-    o = a256(o + (L->d_router ? (size_t)Tc * E * 4 : 0));
-    w.offsets = o;
-    o = a256(o + (E + 1) * 4);
-    w.active = o;
-    o = a256(o + (E + 1) * 4);
-    w.slot_token = o;
-    o = a256(o + (size_t)Tc * K * 4);
-    w.slot_w = o;
-    o = a256(o + (size_t)Tc * K * 4);
-    w.token_slots = o;
-    o = a256(o + (size_t)Tc * K * 4);
-    w.h = o;
-    o = a256(o + (size_t)Tc * K * L->FF * 4);
-    w.xf = o;
-    o = a256(o + xf_bytes(Tc, L->D));
-    w.hf = o;
-    o = a256(o + xf_bytes(Tc * (int)K, L->FF));
-    w.y = o;
-    o = a256(o + (size_t)Tc * K * L->D * 4);
-    w.groups = o;
-    o = a256(o + (size_t)(L->D / 16) * 4);
+    auto take = [&](size_t& at, size_t bytes) {
+        at = o;
+        o = a256(o + bytes);
+    };
+    take(w.ids, (size_t)T * K * 4);  // routing of every token of the call (kept for the engine's trace)
+    take(w.wts, (size_t)T * K * 4);
+    take(w.logits, L->d_router ? (size_t)Tc * E * 4 : 0);
+    take(w.offsets, (E + 1) * 4);
+    take(w.active, (E + 1) * 4);
+    take(w.slot_token, S * 4);
+    take(w.slot_w, S * 4);
+    take(w.token_slots, S * 4);
+    take(w.ngroups, 4);
+    take(w.groups, S * sizeof(GroupRec));
+    take(w.rg_done, (size_t)(L->D / 64) * 4);
+    take(w.h, S * L->FF * 4);
+    take(w.xf, xf_bytes(Tc, L->D));
+    take(w.y, S * L->D * 4);
     w.total = o;
     return w;
 }
@@ -189,13 +182,15 @@ bool layer_ok(const EahmmfMoeLayer* L) {
            L->n_used <= L->n_expert && L->D > 0 && L->D % 256 == 0 && L->FF > 0 && L->FF % 256 == 0 && L->d_gate &&
            L->d_up && L->d_down && is_kquant(L->gate_type) && is_kquant(L->up_type) && is_kquant(L->down_type) &&
            shape_ok(L->gate_type, L->D, L->gate_row_bytes) && shape_ok(L->up_type, L->D, L->up_row_bytes) &&
-           shape_ok(L->down_type, L->FF, L->down_row_bytes);
+           shape_ok(L->down_type, L->FF, L->down_row_bytes) &&
+           moe_smem_gateup(L->D, L->gate_row_bytes, L->up_row_bytes) <= 227 * 1024 &&
+           moe_smem_down(L->FF, L->down_row_bytes) <= 227 * 1024;
 }
 }  // namespace
 
 // ---- optional per-stage timing of eahmmf_cuda_moe_layer (events on the call's stream) --------------
 namespace {
-constexpr int PROF_STAGES = 6;  // router GEMV, activation prep, route/permute, gate/up, h prep, down/combine
+constexpr int PROF_STAGES = 4;  // router GEMV, routing + activation prep, gate/up (+ h prep), down/combine
 struct StageTimer {
     bool on = false;
     cudaEvent_t ev[PROF_STAGES + 1] = {};
@@ -273,9 +268,10 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
         a.rw.slot_token = reinterpret_cast<int*>(ws + w.slot_token);
         a.rw.slot_w = reinterpret_cast<float*>(ws + w.slot_w);
         a.rw.token_slots = reinterpret_cast<int*>(ws + w.token_slots);
-        a.rw.group_done = reinterpret_cast<int*>(ws + w.groups);
+        a.rw.ngroups = reinterpret_cast<int*>(ws + w.ngroups);
+        a.rw.groups = reinterpret_cast<GroupRec*>(ws + w.groups);
+        a.rw.rg_done = reinterpret_cast<int*>(ws + w.rg_done);
         a.xf = xf_carve(ws + w.xf, tc, L->D);
-        a.hf = xf_carve(ws + w.hf, tc * K, L->FF);
         a.y = reinterpret_cast<float*>(ws + w.y);
         a.status = d_status;
         g_prof.mark(0, st);
@@ -287,16 +283,12 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
             a.logits = lg;
         }
         g_prof.mark(1, st);
-        if (launch_prep_x(a.xn, L->D, tc, L->D, a.xf, st) != cudaSuccess) return ST_CUDA;
+        if (launch_moe_route(a, st) != cudaSuccess) return ST_CUDA;
         g_prof.mark(2, st);
-        if (launch_route_permute(a, st) != cudaSuccess) return ST_CUDA;
-        g_prof.mark(3, st);
         if (launch_moe_gateup(a, st) != cudaSuccess) return ST_CUDA;
-        g_prof.mark(4, st);
-        if (launch_prep_x(a.h, L->FF, tc * K, L->FF, a.hf, st) != cudaSuccess) return ST_CUDA;
-        g_prof.mark(5, st);
+        g_prof.mark(3, st);
         if (launch_moe_down(a, st) != cudaSuccess) return ST_CUDA;
-        g_prof.mark(6, st);
+        g_prof.mark(4, st);
     }
     return ST_OK;
 }

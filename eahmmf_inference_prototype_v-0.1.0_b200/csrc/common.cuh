@@ -30,18 +30,22 @@ enum : int {
     ST_CAPACITY = 1 << 5,      // a size exceeded the workspace the caller provided
 };
 
-// Activations in fragment form ("xf"), produced once per token row by k_prep_x and read by the
-// tensor-core GEMV tiles (kq.cuh):
-//   frag[(row * nseg + seg) * 8 + p * 4 + t]  MMA B fragment (b0, b1) of lane (g, t) for the row's high
-//                                             (p = 0) or low (p = 1) f16 part, 16-k segment seg
-//   sum[row * nseg + seg]                     sum of the unscaled activations of the segment
-//   tsc[row]                                  2^-e: the fragments hold x * 2^e
+// Activations in fragment form ("XF", layout in kq.cuh), rows of K elements:
+//   frag   rows x K*3 bytes: three int8 digits per element in MMA B-fragment order
+//   sum    rows x (K/16 + 4) floats: the per-16 sums of the row, then the row scale s and three zeros
+//          (the dense GEMV's minimum terms)
+//   gs     rows x (16 + K/8) bytes: the row scale s (float, then 12 zero bytes), then per super-block
+//          32 bytes: the eight 32-element group sums of the row divided by s, as f16 high parts
+//          (16 bytes) and f16 residues (16 bytes) -- the B operand of the expert kernels' minimum-term
+//          MMA; divided by s they are bounded by 32 * 127 and fit f16
 struct XF {
     const uint2* frag;
     const float* sum;
-    const float* tsc;
-    int nseg;
+    const uint8_t* gs;
+    int nseg;  // K / 16
 };
+constexpr int XF_SUM_PAD = 4;  // floats after a row's segment sums (scale + padding to 16 bytes)
+__host__ __device__ constexpr int xf_gs_bytes(int K) { return 16 + K / 8; }
 
 // Exact 2^e for -126 <= e <= 127.
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }

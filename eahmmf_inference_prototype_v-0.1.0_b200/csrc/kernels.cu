@@ -1,20 +1,12 @@
-// kernels.cu -- sm_100a kernels of the MoE expert hot path.
+// kernels.cu -- sm_100a kernels of the dense quantized GEMV (the reference's two C entry points and
+// eahmmf_cuda_gemv); the MoE block's kernels are in moe.cu.
 //
-//   k_prep_x            activations -> fragment form (f16 high/low split, per-16 sums, power-of-two
-//                       scale), once per token row, read by every weight tile afterwards.
-//   k_gemv<QT,N>        dense quantized GEMV (attention/output rows, the C ABI): 16-row tiles streamed
-//                       HBM -> shared memory by 1-D TMA bulk copies (two-slot mbarrier ring per CTA,
-//                       several small CTAs per SM) and decoded in registers straight into tensor-core
-//                       operands (kq.cuh).
+//   k_prep_x            activations -> fragment form (three int8 digits per element, per-16 sums, row
+//                       scale; kq.cuh), once per token row, read by every weight tile afterwards.
+//   k_gemv<QT,N>        dense K-quant GEMV: one 16-row tile per CTA, staged HBM -> shared memory with the
+//                       tokens' XF rows by 1-D TMA bulk copies on an mbarrier, decoded in registers
+//                       straight into int8 tensor-core operands (kq.cuh).
 //   k_gemv_generic      one warp per row for F32/F16/Q8_0 and for buffers TMA cannot address.
-//   k_route_permute     router softmax + top-k + renormalisation (warp per token, the CPU comparator of
-//                       qwen3moe.cpp:1016) fused with the token->expert grouping (histogram, exclusive
-//                       scan, stable scatter), one CTA, no host round trip.
-//   k_moe_gateup<G,U>   gate and up projections of every routed (expert, token) pair with SiLU(g)*u in
-//                       the epilogue; work = (active expert, 16-row group) units split evenly over the grid.
-//   k_moe_down<QD>      down projection per (16-row group, active expert) unit, fused with the router-
-//                       weighted combine and the residual add: the CTA completing a row group adds each
-//                       token's expert outputs in ascending expert order (qwen3moe.cpp:1025-1069).
 #include <algorithm>
 #include <mutex>
 #include <unordered_map>
@@ -129,79 +121,21 @@ __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
 
 
 // ------------------------------------------------------------------------------------------------
-// activations -> fragment form (XF); one CTA per token row
+// activations -> fragment form (XF, kq.cuh); one CTA per token row
 // ------------------------------------------------------------------------------------------------
-constexpr int PREP_NT = 256;
-__device__ __forceinline__ int digit(float v) { return (int)fminf(127.f, fmaxf(-127.f, rintf(v))); }
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
-}
-// rows: X + row * ldx (row < nrows), K floats each (K % 32 == 0, rows 16-byte aligned). Writes each row
-// as three int8 digits of base 254 of x / s, s = max|x| / 127, in MMA B-fragment order, plus the
-// per-16 sums of x and s.
 __global__ void __launch_bounds__(PREP_NT) k_prep_x(const float* __restrict__ X, int ldx, int K, uint2* __restrict__ frag,
-                                                     float* __restrict__ sum, float* __restrict__ tsc) {
-    __shared__ float wmax[PREP_NT / 32];
-    __shared__ float sh_inv;
-    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, nblk = K >> 5;
-    const float* x = X + (size_t)row * ldx;
-    float mx = 0.f;
-    for (int i = tid; i < (K >> 2); i += PREP_NT) {
-        const float4 v = reinterpret_cast<const float4*>(x)[i];
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) wmax[tid >> 5] = mx;
-    __syncthreads();
-    if (tid == 0) {
-        float m = 0.f;
-        for (int w = 0; w < PREP_NT / 32; w++) m = fmaxf(m, wmax[w]);
-        if (!(m > 0.f) || m == INFINITY) m = 127.f;  // all-zero (or non-finite) rows: any scale works
-        tsc[row] = m / 127.f;
-        sh_inv = 127.f / m;
-    }
-    __syncthreads();
-    const float inv = sh_inv;
-    for (int i = tid; i < nblk * 4; i += PREP_NT) {  // item = (32-k block j, t): 4 consecutive lanes share a block
-        const int j = i >> 2, t = i & 3;
-        const float4 u = *reinterpret_cast<const float4*>(x + 32 * j + 4 * t);
-        const float4 w = *reinterpret_cast<const float4*>(x + 32 * j + 16 + 4 * t);
-        const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
-        int dg[3][8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const float v = xv[k] * inv;
-            const int a0 = digit(v);
-            const float r1 = (v - (float)a0) * DIGIT;
-            const int a1 = digit(r1);
-            const int a2 = digit((r1 - (float)a1) * DIGIT);
-            dg[0][k] = a0;
-            dg[1][k] = a1;
-            dg[2][k] = a2;
-        }
-        uint2* o = frag + ((size_t)row * nblk + j) * 12 + t;
-#pragma unroll
-        for (int p = 0; p < 3; p++)
-            o[p * 4] = make_uint2(pack4(dg[p][0], dg[p][1], dg[p][2], dg[p][3]), pack4(dg[p][4], dg[p][5], dg[p][6], dg[p][7]));
-        float s0 = (u.x + u.y) + (u.z + u.w), s1 = (w.x + w.y) + (w.z + w.w);
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-        if (t == 0) {
-            sum[(size_t)row * (K >> 4) + 2 * j] = s0;
-            sum[(size_t)row * (K >> 4) + 2 * j + 1] = s1;
-        }
-    }
+                                                     float* __restrict__ sum, uint8_t* __restrict__ gs) {
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    prep_row(X + (size_t)row * ldx, K, frag + (size_t)row * (K >> 5) * 12, sum + (size_t)row * ((K >> 4) + XF_SUM_PAD),
+             gs + (size_t)row * xf_gs_bytes(K), red);
 }
 
 // ------------------------------------------------------------------------------------------------
-// tile engine: small persistent CTAs (4 warps), one 16-row tile per step, two-slot TMA ring
+// dense GEMV tile engine: one 16-row tile per CTA, staged with its tokens' XF rows by 1-D TMA copies
 // ------------------------------------------------------------------------------------------------
 constexpr int SETS = 2;  // MMA column sets per pass of the dense GEMV (TOK_PER_SET tokens each)
 constexpr int TPASS = SETS * TOK_PER_SET;  // tokens per pass of the dense GEMV
-constexpr int MPASS = TOK_PER_SET;         // tokens per pass of the expert kernels (one column set)
 
 __host__ __device__ inline size_t al128(size_t x) { return (x + 127) & ~(size_t)127; }
 
@@ -239,38 +173,44 @@ __device__ __forceinline__ uint32_t rows_lead(const RowLayout& L, const uint8_t*
     return L.per_row ? 0u : (uint32_t)((reinterpret_cast<uintptr_t>(base) + (size_t)r0 * rb) & 15);
 }
 
-// Bulk-copies the fragment rows and per-16 sums of m tokens into shared memory (sfrag: m x K*3 bytes,
-// ssum: m x K/16 floats). rows(i) gives token i's xf row; consecutive rows are merged into one copy.
-// Returns the bytes in flight on bar.
+// Bulk-copies the fragment rows and the sums (with the scale) of m tokens into shared memory (sfrag:
+// m x K*3 bytes, ssum: m x (K/16 + 4) floats). rows(i) gives token i's xf row; consecutive rows are
+// merged into one copy. Returns the bytes in flight on bar.
 template <typename Rows>
 __device__ __forceinline__ uint32_t issue_xf(const XF& xf, Rows rows, int m, int K, uint8_t* sfrag, float* ssum,
                                              uint64_t* bar) {
-    const uint32_t fb = (uint32_t)K * 3, sbytes = (uint32_t)K / 4;
+    const uint32_t fb = (uint32_t)K * 3, sbytes = (uint32_t)K / 4 + 4 * XF_SUM_PAD;
+    const int ss = (K >> 4) + XF_SUM_PAD;
     uint32_t total = 0;
     for (int i = 0; i < m;) {
         int n = 1;
         while (i + n < m && rows(i + n) == rows(i) + n) n++;
         const size_t r = (size_t)rows(i);
         tma_load_1d(sfrag + (size_t)i * fb, reinterpret_cast<const uint8_t*>(xf.frag) + r * fb, n * fb, bar);
-        tma_load_1d(ssum + (size_t)i * (K >> 4), xf.sum + r * (K >> 4), n * sbytes, bar);
+        tma_load_1d(ssum + (size_t)i * ss, xf.sum + r * ss, n * sbytes, bar);
         total += n * (fb + sbytes);
         i += n;
     }
     return total;
 }
-__device__ __forceinline__ uint32_t xf_bytes_of(int m, int K) { return (uint32_t)m * ((uint32_t)K * 3 + (uint32_t)K / 4); }
+__device__ __forceinline__ uint32_t xf_bytes_of(int m, int K) {
+    return (uint32_t)m * ((uint32_t)K * 3 + (uint32_t)K / 4 + 4 * XF_SUM_PAD);
+}
 
 // All MMA tasks (super-block, half) of a staged 16-row tile:
 //   part[((task0 + task) * NSET + st) * 128 + row * 8 + column] = d * (int32 digit sums)
 //   mpart[(task0 + task) * 64 + row * 4 + token]                = group-minimum term
 template <int QT, int NSET>
-__device__ __forceinline__ void tile_tasks(const uint8_t* rows, int stride, int nsb, const uint2* sfrag,
+__device__ __forceinline__ void tile_tasks(const uint8_t* rows, int stride, int nsb, const uint8_t* sfrag,
                                            const float* ssum, int m, float* part, float* mpart, int task0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const BPtr<NSET> bp(sfrag, nsb * 8, m);
+    const uint8_t* rg = rows + (size_t)g * stride;
     for (int k = warp; k < nsb * 2; k += (int)(blockDim.x >> 5)) {
-        float o[NSET][4], mn[2];
-        mma_task<QT, NSET>(rows, stride, k >> 1, k & 1, bp, ssum, nsb * 16, m, o, mn);
+        const int sb = k >> 1, h = k & 1;
+        float o[NSET][4] = {}, mn[2] = {0.f, 0.f};
+        const RowsAny R{{rg, rg + 8 * (size_t)stride}};
+        kq_task<QT, NSET>(R, sb, h, bp, t < m ? ssum + (size_t)t * (nsb * 16 + XF_SUM_PAD) + sb * 16 : nullptr, o, mn);
 #pragma unroll
         for (int st = 0; st < NSET; st++) {
             float* p = part + ((size_t)(task0 + k) * NSET + st) * 128;
@@ -312,7 +252,7 @@ __host__ __device__ inline GPlan unit_plan(int K, int m, int ntask, int nset, si
     GPlan p;
     p.sfrag_off = 128;
     p.ssum_off = al128(p.sfrag_off + (size_t)m * K * 3);
-    p.part_off = al128(p.ssum_off + (size_t)m * (K / 16) * 4);
+    p.part_off = al128(p.ssum_off + (size_t)m * (K / 16 + XF_SUM_PAD) * 4);
     p.mpart_off = al128(p.part_off + (size_t)ntask * nset * 512);
     p.slot_off = al128(p.mpart_off + (size_t)ntask * 256);
     p.total = p.slot_off + slot_bytes_total;
@@ -353,314 +293,14 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
         return;
     }
     const uint8_t* rows = slot + rows_lead(L, a.W.w, rb, r0);
-    tile_tasks<QT, NSET>(rows, L.stride, nsb, reinterpret_cast<const uint2*>(sfrag), ssum, m, part, mpart, 0);
+    tile_tasks<QT, NSET>(rows, L.stride, nsb, sfrag, ssum, m, part, mpart, 0);
     __syncthreads();
     for (int j = tid; j < (r1 - r0) * m; j += blockDim.x) {
         const int r = j / m, tk = j - r * m;
-        const float v = tile_value<NSET>(part, mpart, 0, r, nsb, tk, __ldg(a.xf.tsc + tk));
+        const float v = tile_value<NSET>(part, mpart, 0, r, nsb, tk, ssum[(size_t)tk * (16 * nsb + XF_SUM_PAD) + 16 * nsb]);
         float* y = a.Y + (size_t)tk * a.ldy + r0 + r;
         *y = a.accumulate ? *y + v : v;
     }
-}
-
-// ------------------------------------------------------------------------------------------------
-// routing + permutation (single CTA of 1024 threads)
-// ------------------------------------------------------------------------------------------------
-struct Cand {
-    float r;
-    int e;
-};
-__device__ __forceinline__ bool better(const Cand& a, const Cand& b) {
-    return a.r > b.r || (a.r == b.r && a.e < b.e);  // the partial_sort comparator, qwen3moe.cpp:1016
-}
-
-__global__ void __launch_bounds__(1024) k_route_permute(MoeArgs a) {
-    __shared__ int cnt[MAX_EXPERTS];
-    __shared__ int off[MAX_EXPERTS + 1];
-    __shared__ unsigned long long mask[MAX_EXPERTS * (ROUTE_TMAX / 64)];
-    const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
-    const int W = (T + 63) >> 6;
-    for (int i = tid; i < E; i += blockDim.x) cnt[i] = 0;
-    for (int i = tid; i < (a.D >> 4); i += blockDim.x) a.rw.group_done[i] = 0;
-    for (int i = tid; i < E * W; i += blockDim.x) mask[i] = 0ull;
-    __syncthreads();
-
-    // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022)
-    const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
-    constexpr int PER = MAX_EXPERTS / 32;
-    const int per = (E + 31) >> 5;  // entries per lane
-    for (int t = warp; t < T; t += nwarp) {
-        const float* lg = a.logits + (size_t)t * E;
-        float l[PER];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-            const int e = lane + 32 * i;
-            l[i] = (i < per && e < E) ? lg[e] : -INFINITY;
-            mx = fmaxf(mx, l[i]);
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        // r = exp(l - max): the difference in fp32 as on the CPU, the exponential correctly rounded
-        float r[PER];
-#pragma unroll
-        for (int i = 0; i < PER; i++)
-            r[i] = (i < per && (lane + 32 * i) < E) ? (float)exp((double)(l[i] - mx)) : -1.0f;
-        unsigned used = 0;
-        float tot = 0.f;
-        int my_e = -1;
-        float my_r = 0.f;
-        for (int k = 0; k < K; k++) {
-            Cand best{-2.0f, 0x7fffffff};
-#pragma unroll
-            for (int i = 0; i < PER; i++) {
-                if (i >= per) break;
-                const Cand c{r[i], lane + 32 * i};
-                if (!((used >> i) & 1u) && (lane + 32 * i) < E && better(c, best)) best = c;
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                Cand other{__shfl_xor_sync(0xffffffffu, best.r, o), __shfl_xor_sync(0xffffffffu, best.e, o)};
-                if (better(other, best)) best = other;
-            }
-            if ((best.e & 31) == lane) used |= 1u << (best.e >> 5);
-            tot += best.r;  // rank-order sum, identical on every lane
-            if (lane == k) {
-                my_e = best.e;
-                my_r = best.r;
-            }
-        }
-        if (lane < K) {
-            const float w = __fdiv_rn(my_r, tot);
-            if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
-                flag(a.status, ST_BAD_INDEX);
-                my_e = 0;
-            }
-            a.rw.ids[(size_t)t * K + lane] = my_e;
-            a.rw.wts[(size_t)t * K + lane] = w;
-            atomicAdd(&cnt[my_e], 1);
-            atomicOr(&mask[my_e * W + (t >> 6)], 1ull << (t & 63));
-        }
-    }
-    __syncthreads();
-    // ---- exclusive scan of the counts and the ascending active-expert list
-    if (warp == 0) {
-        int run = 0, nact = 0;
-        for (int base = 0; base < E; base += 32) {
-            const int e = base + lane;
-            const int c = e < E ? cnt[e] : 0;
-            int inc = c, act = c > 0;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, inc, o), u = __shfl_up_sync(0xffffffffu, act, o);
-                if (lane >= o) {
-                    inc += v;
-                    act += u;
-                }
-            }
-            if (e < E) {
-                off[e] = run + inc - c;
-                a.rw.offsets[e] = run + inc - c;
-                if (c > 0) a.rw.active[1 + nact + act - 1] = e;
-            }
-            run += __shfl_sync(0xffffffffu, inc, 31);
-            nact += __shfl_sync(0xffffffffu, act, 31);
-        }
-        if (lane == 0) {
-            off[E] = run;
-            a.rw.offsets[E] = run;
-            a.rw.active[0] = nact;
-        }
-    }
-    __syncthreads();
-    // ---- stable scatter: slot = offset[e] + number of earlier tokens routed to e
-    for (int t = tid; t < T; t += blockDim.x) {
-        int slots[32];
-        for (int k = 0; k < K; k++) {
-            const int e = a.rw.ids[(size_t)t * K + k];
-            int rank = __popcll(mask[e * W + (t >> 6)] & ((1ull << (t & 63)) - 1ull));
-            for (int w = 0; w < (t >> 6); w++) rank += __popcll(mask[e * W + w]);
-            const int s = off[e] + rank;
-            a.rw.slot_token[s] = t;
-            a.rw.slot_w[s] = a.rw.wts[(size_t)t * K + k];
-            int j = k;  // insertion: token_slots ascending == expert ascending
-            while (j > 0 && slots[j - 1] > s) {
-                slots[j] = slots[j - 1];
-                j--;
-            }
-            slots[j] = s;
-        }
-        for (int k = 0; k < K; k++) a.rw.token_slots[(size_t)t * K + k] = slots[k];
-    }
-}
-
-
-// ------------------------------------------------------------------------------------------------
-// gate + up + SiLU*mul: units = (active expert, 16-row group), contiguous unit ranges per CTA
-// ------------------------------------------------------------------------------------------------
-struct UPlan {
-    GPlan u;
-    size_t up_at;
-};
-__host__ __device__ inline UPlan gateup_plan(int qg, int qu, int D, size_t rbg, size_t rbu) {
-    (void)qg;
-    (void)qu;
-    UPlan p;
-    p.up_at = slot_bytes(row_layout(rbg, true), 16);
-    p.u = unit_plan(D, MPASS, 4 * (D / 256), 1, p.up_at + slot_bytes(row_layout(rbu, true), 16));
-    return p;
-}
-
-template <int QG, int QU, int NSET>
-__device__ __forceinline__ void gateup_tasks(const uint8_t* grows, int gstride, const uint8_t* urows, int ustride,
-                                             int nsb, const uint2* sfrag, const float* ssum, int m, float* part,
-                                             float* mpart) {
-    tile_tasks<QG, NSET>(grows, gstride, nsb, sfrag, ssum, m, part, mpart, 0);
-    tile_tasks<QU, NSET>(urows, ustride, nsb, sfrag, ssum, m, part, mpart, 2 * nsb);
-}
-
-template <int QG, int QU>
-__global__ void __launch_bounds__(NTU) k_moe_gateup(MoeArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    const int D = a.D, FF = a.FF, nsb = D >> 8, tid = threadIdx.x;
-    const UPlan pl = gateup_plan(QG, QU, D, a.gate_rb, a.up_rb);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
-    int* tok = reinterpret_cast<int*>(sm + 64);
-    uint8_t* sfrag = sm + pl.u.sfrag_off;
-    float* ssum = reinterpret_cast<float*>(sm + pl.u.ssum_off);
-    float* part = reinterpret_cast<float*>(sm + pl.u.part_off);
-    float* mpart = reinterpret_cast<float*>(sm + pl.u.mpart_off);
-    uint8_t* slot = sm + pl.u.slot_off;
-
-    const int NRG = FF >> 4;
-    const int nact = a.rw.active[0];
-    const int ai = (int)blockIdx.x / NRG, r0 = 16 * ((int)blockIdx.x - ai * NRG);
-    if (ai >= nact) return;  // the grid covers the largest possible number of active experts
-    const int e = a.rw.active[1 + ai];
-    const int s0 = a.rw.offsets[e], me = a.rw.offsets[e + 1] - s0;
-    const RowLayout Lg = layout_of(a.gate[e], a.gate_rb), Lu = layout_of(a.up[e], a.up_rb);
-    const uint8_t* grows = slot + rows_lead(Lg, a.gate[e], a.gate_rb, r0);
-    const uint8_t* urows = slot + pl.up_at + rows_lead(Lu, a.up[e], a.up_rb, r0);
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_fence_init();
-    }
-    for (int c0 = 0, pass = 0; c0 < me; c0 += MPASS, pass++) {
-        const int mc = min(MPASS, me - c0);
-        if (tid < mc) tok[tid] = a.rw.slot_token[s0 + c0 + tid];
-        __syncthreads();  // tok visible; the previous pass is done with the staged activations
-        if (tid == 0) {
-            uint32_t bytes = xf_bytes_of(mc, D);
-            if (pass == 0) bytes += rows_bytes(Lg, a.gate[e], a.gate_rb, r0, r0 + 16) + rows_bytes(Lu, a.up[e], a.up_rb, r0, r0 + 16);
-            mbar_expect_tx(&bar[0], bytes);
-            if (pass == 0) {
-                issue_rows(Lg, a.gate[e], a.gate_rb, r0, r0 + 16, slot, &bar[0]);
-                issue_rows(Lu, a.up[e], a.up_rb, r0, r0 + 16, slot + pl.up_at, &bar[0]);
-            }
-            issue_xf(a.xf, [&](int i) { return tok[i]; }, mc, D, sfrag, ssum, &bar[0]);
-        }
-        if (__syncthreads_or(!mbar_wait_bounded(&bar[0], (uint32_t)pass & 1u))) {
-            if (tid == 0) {
-                flag(a.status, ST_WAIT_TIMEOUT);
-                drain_ring(bar, pass + 1, pass, 1);
-            }
-            return;
-        }
-        gateup_tasks<QG, QU, 1>(grows, Lg.stride, urows, Lu.stride, nsb, reinterpret_cast<const uint2*>(sfrag), ssum, mc,
-                                part, mpart);
-        __syncthreads();
-        for (int j = tid; j < 16 * mc; j += blockDim.x) {
-            const int r = j / mc, tk = j - r * mc;
-            const float ts = __ldg(a.xf.tsc + tok[tk]);
-            const float g = tile_value<1>(part, mpart, 0, r, nsb, tk, ts);
-            const float u = tile_value<1>(part, mpart, 2 * nsb, r, nsb, tk, ts);
-            a.h[(size_t)(s0 + c0 + tk) * FF + r0 + r] = silu_mul(g, u);
-        }
-        __syncthreads();  // tok and the staged activations are rewritten by the next pass
-    }
-}
-
-// ------------------------------------------------------------------------------------------------
-// down projection: units = (16-row group of D, active expert), contiguous ranges per CTA, so a CTA
-// mostly walks the experts of one row group. Expert outputs go to y[slot][D]; the CTA that completes a
-// row group (a per-group counter reaches the number of active experts) adds each token's expert
-// outputs in ascending expert order, weighted, to the residual (qwen3moe.cpp:1024-1069).
-// ------------------------------------------------------------------------------------------------
-__host__ __device__ inline GPlan down_plan(int qd, int FF, size_t rb) {
-    (void)qd;
-    return unit_plan(FF, MPASS, 2 * (FF / 256), 1, slot_bytes(row_layout(rb, true), 16));
-}
-
-template <int QD>
-__global__ void __launch_bounds__(NTU) k_moe_down(MoeArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    __shared__ int s_last;
-    const int D = a.D, FF = a.FF, nsb = FF >> 8, T = a.T, K = a.n_used, tid = threadIdx.x;
-    const size_t rb = a.down_rb;
-    const GPlan pl = down_plan(QD, FF, rb);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
-    uint8_t* sfrag = sm + pl.sfrag_off;
-    float* ssum = reinterpret_cast<float*>(sm + pl.ssum_off);
-    float* part = reinterpret_cast<float*>(sm + pl.part_off);
-    float* mpart = reinterpret_cast<float*>(sm + pl.mpart_off);
-    uint8_t* slot = sm + pl.slot_off;
-
-    const int nact = a.rw.active[0];
-    const int rg = (int)blockIdx.x, ai = (int)blockIdx.y, r0 = 16 * rg;
-    if (ai >= nact) return;  // grid.y covers the largest possible number of active experts
-    const int e = a.rw.active[1 + ai];
-    const int s0 = a.rw.offsets[e], me = a.rw.offsets[e + 1] - s0;
-    const uint8_t* w = a.down[e];
-    const RowLayout L = layout_of(w, rb);
-    const uint8_t* rows = slot + rows_lead(L, w, rb, r0);
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_fence_init();
-    }
-    for (int c0 = 0, pass = 0; c0 < me; c0 += MPASS, pass++) {
-        const int mc = min(MPASS, me - c0);
-        __syncthreads();  // the previous pass is done with the staged activations
-        if (tid == 0) {
-            uint32_t bytes = xf_bytes_of(mc, FF);
-            if (pass == 0) bytes += rows_bytes(L, w, rb, r0, r0 + 16);
-            mbar_expect_tx(&bar[0], bytes);
-            if (pass == 0) issue_rows(L, w, rb, r0, r0 + 16, slot, &bar[0]);
-            issue_xf(a.hf, [&](int i) { return s0 + c0 + i; }, mc, FF, sfrag, ssum, &bar[0]);  // xf rows = slots
-        }
-        if (__syncthreads_or(!mbar_wait_bounded(&bar[0], (uint32_t)pass & 1u))) {
-            if (tid == 0) {
-                flag(a.status, ST_WAIT_TIMEOUT);
-                drain_ring(bar, pass + 1, pass, 1);
-            }
-            return;
-        }
-        tile_tasks<QD, 1>(rows, L.stride, nsb, reinterpret_cast<const uint2*>(sfrag), ssum, mc, part, mpart, 0);
-        __syncthreads();
-        for (int j = tid; j < 16 * mc; j += blockDim.x) {
-            const int r = j / mc, tk = j - r * mc;
-            const float ts = __ldg(a.hf.tsc + s0 + c0 + tk);
-            const float v = tile_value<1>(part, mpart, 0, r, nsb, tk, ts);
-            a.y[(size_t)(s0 + c0 + tk) * D + r0 + r] = v;
-        }
-    }
-    // publish this expert's rows of the group; the CTA that completes the group combines it
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.rw.group_done[rg], 1) + 1 == nact);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int j = tid; j < T * 16; j += blockDim.x) {
-        const int t = j >> 4, r = j & 15;
-        const int* ts = a.rw.token_slots + (size_t)t * K;
-        float acc = 0.f;
-        for (int k = 0; k < K; k++) {  // ascending slots = ascending experts (qwen3moe.cpp:1025)
-            const int s = ts[k];
-            acc = fmaf(a.rw.slot_w[s], __ldcg(a.y + (size_t)s * D + r0 + r), acc);
-        }
-        a.x[(size_t)t * D + r0 + r] += acc;
-    }
-    if (tid == 0) a.rw.group_done[rg] = 0;  // ready for the next call
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -681,7 +321,7 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 constexpr size_t SMEM_CAP = 227 * 1024;
 
 bool gemv_mma_ok(const QMat& W) {
-    return is_kquant(W.type) && W.K % 256 == 0 && W.row_bytes == (size_t)(W.K / 256) * block_bytes(W.type) &&
+    return is_kquant(W.type) && aligned16(W.w) && W.K % 256 == 0 && W.row_bytes == (size_t)(W.K / 256) * block_bytes(W.type) &&
            gemv_plan(W.type, W.K, W.row_bytes, SETS, TPASS).total <= SMEM_CAP;
 }
 
@@ -690,15 +330,15 @@ XF xf_carve(void* base, int rows, int K) {
     XF x;
     x.frag = reinterpret_cast<const uint2*>(p);
     x.sum = reinterpret_cast<const float*>(p + (size_t)rows * K * 3);
-    x.tsc = reinterpret_cast<const float*>(p + (size_t)rows * K * 3 + (size_t)rows * (K / 16) * 4);
+    x.gs = p + (size_t)rows * K * 3 + (size_t)rows * (K / 16 + XF_SUM_PAD) * 4;
     x.nseg = K / 16;
     return x;
 }
 
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st) {
-    if (rows < 1 || K % 32 || ldx % 4 || !aligned16(X)) return cudaErrorInvalidValue;
+    if (rows < 1 || K % 256 || ldx % 4 || !aligned16(X)) return cudaErrorInvalidValue;
     k_prep_x<<<rows, PREP_NT, 0, st>>>(X, ldx, K, const_cast<uint2*>(out.frag), const_cast<float*>(out.sum),
-                                       const_cast<float*>(out.tsc));
+                                       const_cast<uint8_t*>(out.gs));
     return cudaGetLastError();
 }
 
@@ -737,61 +377,6 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
     if (a.m < 1 || a.m > MT) return cudaErrorInvalidValue;
     k_gemv_generic<<<(a.W.rows * 32 + 255) / 256, 256, 0, st>>>(a);
     return cudaGetLastError();
-}
-
-cudaError_t launch_route_permute(const MoeArgs& a, cudaStream_t st) {
-    if (a.T < 1 || a.T > ROUTE_TMAX || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert)
-        return cudaErrorInvalidValue;
-    const int threads = a.T <= 4 ? 128 : (a.T <= 32 ? 512 : 1024);  // one warp per token, at most 32
-    k_route_permute<<<1, threads, 0, st>>>(a);
-    return cudaGetLastError();
-}
-
-template <int QG, int QU>
-static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
-    const UPlan pl = gateup_plan(QG, QU, a.D, a.gate_rb, a.up_rb);
-    if (pl.u.total > SMEM_CAP) return cudaErrorInvalidValue;
-    smem_attr(k_moe_gateup<QG, QU>, pl.u.total);
-    const int maxact = std::min(a.n_expert, a.T * a.n_used);
-    k_moe_gateup<QG, QU><<<maxact * (a.FF / 16), NTU, pl.u.total, st>>>(a);
-    return cudaGetLastError();
-}
-template <int QG>
-static cudaError_t gateup_g(const MoeArgs& a, cudaStream_t st) {
-    switch (a.up_type) {
-        case T_Q4_K: return gateup_as<QG, T_Q4_K>(a, st);
-        case T_Q5_K: return gateup_as<QG, T_Q5_K>(a, st);
-        case T_Q6_K: return gateup_as<QG, T_Q6_K>(a, st);
-        default: return cudaErrorInvalidValue;
-    }
-}
-cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st) {
-    if (a.D % 256 || a.FF % 16) return cudaErrorInvalidValue;
-    switch (a.gate_type) {
-        case T_Q4_K: return gateup_g<T_Q4_K>(a, st);
-        case T_Q5_K: return gateup_g<T_Q5_K>(a, st);
-        case T_Q6_K: return gateup_g<T_Q6_K>(a, st);
-        default: return cudaErrorInvalidValue;
-    }
-}
-
-template <int QD>
-static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
-    const GPlan pl = down_plan(QD, a.FF, a.down_rb);
-    if (pl.total > SMEM_CAP) return cudaErrorInvalidValue;
-    smem_attr(k_moe_down<QD>, pl.total);
-    const int maxact = std::min(a.n_expert, a.T * a.n_used);
-    k_moe_down<QD><<<dim3(a.D / 16, maxact), NTU, pl.total, st>>>(a);
-    return cudaGetLastError();
-}
-cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {
-    if (a.FF % 256 || a.D % 16 || a.T > DOWN_TMAX) return cudaErrorInvalidValue;
-    switch (a.down_type) {
-        case T_Q4_K: return down_as<T_Q4_K>(a, st);
-        case T_Q5_K: return down_as<T_Q5_K>(a, st);
-        case T_Q6_K: return down_as<T_Q6_K>(a, st);
-        default: return cudaErrorInvalidValue;
-    }
 }
 
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,

@@ -10,9 +10,9 @@ namespace eb {
 
 constexpr int MT = 8;               // tokens per pass of the per-row kernel
 constexpr int XPASS = 4;            // tokens per pass of the tensor-core GEMV
-constexpr int STAGES = 3;           // TMA ring depth
-constexpr int DOWN_TMAX = 64;       // tokens per call handled by the row-parallel down/combine kernel
-constexpr int ROUTE_TMAX = 256;     // tokens per call handled by the single-CTA route/permute kernel
+constexpr int MOE_TMAX = 64;        // tokens per MoE block call (the engine's MAXB, qwen3moe.cpp:39)
+constexpr int MU = 2;               // slots per MoE work group (one MMA column set)
+constexpr int ROUTE_NT = 512;       // threads of the routing / prep kernel
 constexpr int MAX_EXPERTS = 512;
 
 // A quantized matrix: rows of row_bytes bytes, ne0 = K elements per row.
@@ -37,6 +37,17 @@ struct GemvArgs {
     int* status;
 };
 
+// One work group of the MoE block: up to MU consecutive slots of one expert (written by k_moe_route).
+struct __align__(16) GroupRec {
+    const uint8_t* w[3];  // the expert's gate, up and down matrices
+    int e;                // expert
+    int s0;               // first slot
+    int mc;               // slots in the group (1..MU)
+    int tok[MU];          // token of each slot
+    int pad[16 - 6 - 3 - MU];
+};
+static_assert(sizeof(GroupRec) == 64, "GroupRec is one 64-byte record");
+
 // Routing/permutation workspace of one MoE call (all device pointers, sized for T tokens).
 struct RouteWs {
     int* ids;          // [T*K] routed expert ids, rank order (bit-exact with the CPU path)
@@ -46,7 +57,9 @@ struct RouteWs {
     int* slot_token;   // [T*K] token of each slot (slots grouped by expert ascending, tokens ascending)
     float* slot_w;     // [T*K] routing weight of each slot
     int* token_slots;  // [T*K] slots of token t, ascending (= expert-ascending)
-    int* group_done;   // [D/16] per 16-row group of the output: expert units finished (down kernel)
+    int* ngroups;      // [1] number of work groups
+    GroupRec* groups;  // [T*K] work groups, expert ascending
+    int* rg_done;      // [D/64] down units finished per 64-row group of the output
 };
 
 struct MoeArgs {
@@ -63,7 +76,6 @@ struct MoeArgs {
     const float* logits;  // [T*E] router logits
     float* x;             // [T*D] residual, += weighted expert outputs
     float* h;             // [T*K*FF] SiLU(gate)*up per slot
-    XF hf;                // h in fragment form (rows = slots)
     float* y;             // [T*K*D] expert outputs per slot (down projection, before the combine)
     RouteWs rw;
     int* status;
@@ -82,17 +94,22 @@ struct GemvXArgs {
 
 int sm_count();
 bool gemv_mma_ok(const QMat& W);                 // tensor-core path available for this matrix
-// bytes of an XF block of `rows` rows: digits (3 bytes per element), per-16 sums, per-row scale
+// bytes of an XF block of `rows` rows: digits (3 bytes per element), per row the per-16 sums and the
+// scale (K/16 + 4 floats), per row the group sums (16 + K/8 bytes)
 constexpr size_t xf_bytes(int rows, int K) {
-    return (size_t)rows * K * 3 + (size_t)rows * (K / 16) * 4 + (size_t)rows * 4 + 256;
+    return (size_t)rows * K * 3 + (size_t)rows * (K / 16 + XF_SUM_PAD) * 4 + (size_t)rows * xf_gs_bytes(K) + 256;
 }
 XF xf_carve(void* base, int rows, int K);        // XF views over such a block
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st);
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st);
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st);  // per-row kernel (any type)
-cudaError_t launch_route_permute(const MoeArgs& a, cudaStream_t st);
+// MoE block (moe.cu): routing + grouping + activation prep, then gate/up, then down + combine; the
+// last two are launched with programmatic stream serialization.
+cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st);
+size_t moe_smem_gateup(int D, size_t rbg, size_t rbu);
+size_t moe_smem_down(int FF, size_t rbd);
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
                             cudaStream_t st);
 

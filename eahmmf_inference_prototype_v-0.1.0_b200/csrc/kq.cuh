@@ -15,9 +15,10 @@
 // then scaled by the super-block's fp16 d in fp32. Q4_K/Q5_K group minimums are applied through
 // per-16 activation sums. Every task decodes the scales of its own rows from the staged block headers.
 //
-// Fragment ownership (PTX ISA, integer mma, lane = 4*g + t): A rows g and g+8, k 4t..4t+3 (and
-// 16+4t.. for k32) -- exactly the t-th 32-bit word of a row's 16-byte run; B column g, same k;
-// C rows g and g+8, columns 2t and 2t+1.
+// Fragment ownership (PTX ISA, integer mma, lane = 4*g + t): A rows g and g+8, B column g, C rows g
+// and g+8 with columns 2t and 2t+1. The k order inside a 32-k MMA is free as long as A and B agree:
+// here lane t's two A/B registers hold elements 8t..8t+3 and 8t+4..8t+7 of the group, so a lane
+// loads 8 contiguous weight bytes of a row with one 64-bit shared load.
 #pragma once
 #include "common.cuh"
 
@@ -37,7 +38,7 @@ struct IFrag {
 // C = A (16x32 u8) x B (32x8 s8), fresh accumulator
 __device__ __forceinline__ IFrag imma32(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
     IFrag d;
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
         : "=r"(d.c[0]), "=r"(d.c[1]), "=r"(d.c[2]), "=r"(d.c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
@@ -46,7 +47,7 @@ __device__ __forceinline__ IFrag imma32(uint32_t a0, uint32_t a1, uint32_t a2, u
 // C = A (16x16 u8) x B (16x8 s8), fresh accumulator
 __device__ __forceinline__ IFrag imma16(uint32_t a0, uint32_t a1, uint32_t b0) {
     IFrag d;
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
         : "=r"(d.c[0]), "=r"(d.c[1]), "=r"(d.c[2]), "=r"(d.c[3])
         : "r"(a0), "r"(a1), "r"(b0), "r"(0));
@@ -55,7 +56,7 @@ __device__ __forceinline__ IFrag imma16(uint32_t a0, uint32_t a1, uint32_t b0) {
 // C = A (16x16 s8) x B (16x8 s8), fresh accumulator
 __device__ __forceinline__ IFrag imma16s(uint32_t a0, uint32_t a1, uint32_t b0) {
     IFrag d;
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
         : "=r"(d.c[0]), "=r"(d.c[1]), "=r"(d.c[2]), "=r"(d.c[3])
         : "r"(a0), "r"(a1), "r"(b0), "r"(0));
@@ -83,147 +84,254 @@ __device__ __forceinline__ uint32_t lop_sel(uint32_t a, uint32_t b, uint32_t mas
     return r;
 }
 
-// Per-lane B-fragment pointers of up to NSET column sets over a staged copy of the tokens' fragment
-// rows (frag: m rows of nblk * 12 uint2). Set st carries tokens 2st, 2st+1; column g holds digit g % 3
-// of token 2st + g / 3 (columns 6, 7 are zero).
+// ---- activations in fragment form (XF) ----------------------------------------------------------
+// A token row x (K floats) is stored as three int8 digits of base 254 of x / s, s = max|x| / 127, so
+// x = s * (a + b/254 + c/254^2) to within s / (2 * 254^2). Layout of one row (nblk = K/32 blocks of 32
+// elements): 96 bytes per block = 3 digit planes p x 4 lanes t x 8 bytes, where the 8 bytes of (p, t)
+// are digit p of elements 32j + 8t .. 32j + 8t + 7. A 32-k MMA then takes the lane's uint2 directly
+// as its B fragment (b0 = elements 8t..8t+3, b1 = 8t+4..8t+7: the k order the A side uses as well);
+// a 16-k MMA over segment s of the block takes the u32 at byte 16 (s & 1) + 4t. Per-16-element sums
+// of x followed by the scale s (and three zeros) complete the row.
+constexpr int PREP_NT = 256;
+__device__ __forceinline__ int digit(float v) { return (int)fminf(127.f, fmaxf(-127.f, rintf(v))); }
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
+}
+// Group sum S of 32 elements (already divided by the row scale) -> f16 high part and residue at
+// gs + 16 + sb * 32 + 2g and + 16 (see XF).
+__device__ __forceinline__ void put_group_sum(uint8_t* gs, int j, float S) {
+    const __half hi = __float2half_rn(S);
+    const __half lo = __float2half_rn(S - __half2float(hi));
+    __half* p = reinterpret_cast<__half*>(gs + 16 + (j >> 3) * 32) + (j & 7);
+    p[0] = hi;
+    p[8] = lo;
+}
+// One row x (K floats, K % 256 == 0, 16-byte aligned) by the whole block (blockDim.x a multiple of 32,
+// <= 1024): writes frag (K * 3 bytes), sum (K / 16 segment sums, then s, 0, 0, 0) and gs (XF). red: 33
+// floats of shared scratch.
+__device__ __forceinline__ void prep_row(const float* __restrict__ x, int K, uint2* __restrict__ frag,
+                                         float* __restrict__ sum, uint8_t* __restrict__ gs, float* red) {
+    const int tid = threadIdx.x, lane = tid & 31, nthr = blockDim.x, nblk = K >> 5;
+    float mx = 0.f;
+    for (int i = tid; i < (K >> 2); i += nthr) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = 0.f;
+        for (int w = 0; w < (nthr >> 5); w++) m = fmaxf(m, red[w]);
+        if (!(m > 0.f) || m == INFINITY) m = 127.f;  // all-zero (or non-finite) rows: any scale works
+        *reinterpret_cast<float4*>(sum + (K >> 4)) = make_float4(m / 127.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(gs) = make_float4(m / 127.f, 0.f, 0.f, 0.f);
+        red[32] = 127.f / m;
+    }
+    __syncthreads();
+    const float inv = red[32];
+    for (int i = tid; i < nblk * 4; i += nthr) {  // item (block j, lane t): elements 32j + 8t .. + 7
+        const int j = i >> 2, t = i & 3;
+        const float4 u = *reinterpret_cast<const float4*>(x + 32 * j + 8 * t);
+        const float4 w = *reinterpret_cast<const float4*>(x + 32 * j + 8 * t + 4);
+        const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+        int dg[3][8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float v = xv[k] * inv;
+            const int a0 = digit(v);
+            const float r1 = (v - (float)a0) * DIGIT;
+            const int a1 = digit(r1);
+            dg[0][k] = a0;
+            dg[1][k] = a1;
+            dg[2][k] = digit((r1 - (float)a1) * DIGIT);
+        }
+        uint2* o = frag + (size_t)j * 12 + t;
+#pragma unroll
+        for (int p = 0; p < 3; p++)
+            o[p * 4] = make_uint2(pack4(dg[p][0], dg[p][1], dg[p][2], dg[p][3]), pack4(dg[p][4], dg[p][5], dg[p][6], dg[p][7]));
+        // segment sums: lanes t = 0,1 hold segment 2j, t = 2,3 segment 2j + 1 (items i, i^1 are
+        // adjacent lanes of the same warp: nthr is a multiple of 32 and items advance by nthr)
+        float s8 = ((u.x + u.y) + (u.z + u.w)) + ((w.x + w.y) + (w.z + w.w));
+        s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+        if ((t & 1) == 0) sum[2 * j + (t >> 1)] = s8;
+        const float s32 = s8 + __shfl_xor_sync(0xffffffffu, s8, 2);  // lanes i, i^2: the same warp
+        if (t == 0) put_group_sum(gs, j, s32 * inv);
+    }
+}
+
+// Per-lane B-fragment pointers of up to NSET column sets over staged XF rows (m tokens, nblk blocks
+// per row). Set st carries tokens 2st, 2st+1; column g holds digit g % 3 of token 2st + g / 3.
+// Columns 6, 7 and tokens >= m read token 0: MMA columns are independent, and the results of those
+// columns are never used.
 template <int NSET>
 struct BPtr {
-    const uint2* p[NSET];
-    __device__ __forceinline__ BPtr(const uint2* frag, int nblk, int m) {
-        const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const uint8_t* p[NSET];
+    int t;
+    __device__ __forceinline__ BPtr(const uint8_t* frag, int nblk, int m) {
+        const int lane = threadIdx.x & 31, g = lane >> 2;
+        t = lane & 3;
 #pragma unroll
         for (int st = 0; st < NSET; st++) {
-            const int i = TOK_PER_SET * st + g / 3;
-            p[st] = (g < 6 && i < m) ? frag + ((size_t)i * nblk * 3 + g % 3) * 4 + t : nullptr;
+            int i = TOK_PER_SET * st + g / 3, pg = g % 3;
+            if (g >= 6 || i >= m) i = pg = 0;
+            p[st] = frag + ((size_t)i * nblk * 3 + pg) * 32;
         }
     }
     // (b0, b1) of the 32-k block j
-    __device__ __forceinline__ uint2 blk(int st, int j) const { return p[st] ? p[st][j * 12] : make_uint2(0u, 0u); }
+    __device__ __forceinline__ uint2 blk(int st, int j) const {
+        return *reinterpret_cast<const uint2*>(p[st] + 96 * j + 8 * t);
+    }
     // b0 of the 16-k segment s
     __device__ __forceinline__ uint32_t seg(int st, int s) const {
-        return p[st] ? reinterpret_cast<const uint32_t*>(p[st] + (s >> 1) * 12)[s & 1] : 0u;
+        return *reinterpret_cast<const uint32_t*>(p[st] + 96 * (s >> 1) + 16 * (s & 1) + 4 * t);
     }
 };
 __device__ __forceinline__ int sbyte(uint32_t w, int k) { return ((int32_t)(w << (24 - 8 * k))) >> 24; }
+__device__ __forceinline__ int ubyte(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
 
+// ---- row accessors: where the task's two rows (MMA rows g and g+8) live in shared memory ------------
+// off: byte offset inside the row. ld128/ld64 need 16/8-byte alignment of the address they compute.
+struct RowsAny {  // any 2-byte aligned rows (dense GEMV tiles): 32-bit loads go through ld_u32_any
+    const uint8_t* r[2];
+    __device__ __forceinline__ uint4 ld128(int i, int off) const { return *reinterpret_cast<const uint4*>(r[i] + off); }
+    __device__ __forceinline__ uint2 ld64(int i, int off) const { return *reinterpret_cast<const uint2*>(r[i] + off); }
+    __device__ __forceinline__ uint32_t ld32(int i, int off) const { return ld_u32_any(r[i] + off); }
+    __device__ __forceinline__ uint32_t ld16(int i, int off) const { return *reinterpret_cast<const uint16_t*>(r[i] + off); }
+};
+struct RowsQ6 {  // row 0 4-byte aligned, row 1 two bytes past a 4-byte boundary (Q6_K rows of 630 B)
+    const uint8_t* r[2];
+    __device__ __forceinline__ uint4 ld128(int i, int off) const { return *reinterpret_cast<const uint4*>(r[i] + off); }
+    __device__ __forceinline__ uint2 ld64(int i, int off) const { return *reinterpret_cast<const uint2*>(r[i] + off); }
+    __device__ __forceinline__ uint32_t ld32(int i, int off) const {
+        if (i == 0) return *reinterpret_cast<const uint32_t*>(r[0] + off);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(r[1] + off - 2);
+        return __funnelshift_r(w[0], w[1], 16);
+    }
+    __device__ __forceinline__ uint32_t ld16(int i, int off) const { return *reinterpret_cast<const uint16_t*>(r[i] + off); }
+};
 // ---- one task: 16 rows x 128 weights (half h of super-block sb) ------------------------------------
-// base + r*stride: row r of the staged tile. out[set][4] receives d * (int32 sums) for rows g, g+8 and
-// this lane's two digit columns; mn[2] the group-minimum term of rows g, g+8 for token t (Q4_K/Q5_K;
-// sums: staged per-16 activation sums, m tokens x nseg).
-template <int QT, int NSET>
-__device__ __forceinline__ void mma_task(const uint8_t* __restrict__ base, int stride, int sb, int h,
-                                         const BPtr<NSET>& bf, const float* __restrict__ sums, int nseg, int m,
-                                         float (&out)[NSET][4], float (&mn)[2]) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+// R: the task's two rows; offsets are relative to the rows' starts (super-block sb at sb * block bytes).
+// Accumulates into out[set][4] the d-scaled int32 sums of rows g, g+8 for this lane's two digit
+// columns, and into mn[2] the group-minimum term of rows g, g+8 for token t (Q4_K/Q5_K; tsum = token t's
+// per-16 sums at super-block sb, nullptr when the lane has no token).
+template <int QT, int NSET, class R>
+__device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr<NSET>& bf,
+                                        const float* __restrict__ tsum, float (&out)[NSET][4], float (&mn)[2]) {
+    const int t = bf.t;
     constexpr int BB = block_bytes(QT);
-    const uint8_t* r0 = base + (size_t)g * stride + (size_t)sb * BB;
-    const uint8_t* r1 = r0 + (size_t)8 * stride;
+    const int o = sb * BB;
     int acc[NSET][4];
 #pragma unroll
     for (int st = 0; st < NSET; st++) acc[st][0] = acc[st][1] = acc[st][2] = acc[st][3] = 0;
     float d0, d1;
     if constexpr (QT == T_Q4_K || QT == T_Q5_K) {
         constexpr int QS = QT == T_Q4_K ? 16 : 48;
-        const uint4 H0 = *reinterpret_cast<const uint4*>(r0), H1 = *reinterpret_cast<const uint4*>(r1);
-        d0 = f16_to_f32(H0.x & 0xffffu);
-        d1 = f16_to_f32(H1.x & 0xffffu);
+        const uint4 H0 = rows.ld128(0, o), H1 = rows.ld128(1, o);
+        // Q4_K: high nibbles enter the MMA in place (16 x their value), so low-nibble groups take
+        // 16 x their scale and d is divided by 16 (exact)
+        constexpr float DS = QT == T_Q4_K ? 0.0625f : 1.0f;
+        d0 = f16_to_f32(H0.x & 0xffffu) * DS;
+        d1 = f16_to_f32(H1.x & 0xffffu) * DS;
         // 6-bit scales / mins of groups 4h..4h+3, word-parallel restatement of scale_min_k4
         // (qwen3moe.cpp:133-141): bytes 0..3 of the selected word
         const uint32_t s0 = h ? ((H0.w & 0x0f0f0f0fu) | ((H0.y >> 2) & 0x30303030u)) : (H0.y & 0x3f3f3f3fu);
         const uint32_t s1 = h ? ((H1.w & 0x0f0f0f0fu) | ((H1.y >> 2) & 0x30303030u)) : (H1.y & 0x3f3f3f3fu);
-        if (t < m) {  // group minimums for token t: dmin * m_g * sum(x of the group)
+        if (tsum) {  // group minimums for token t: dmin * m_g * sum(x of the group)
             const uint32_t m0 = h ? (((H0.w >> 4) & 0x0f0f0f0fu) | ((H0.z >> 2) & 0x30303030u)) : (H0.z & 0x3f3f3f3fu);
             const uint32_t m1 = h ? (((H1.w >> 4) & 0x0f0f0f0fu) | ((H1.z >> 2) & 0x30303030u)) : (H1.z & 0x3f3f3f3fu);
-            const float4 sa = *reinterpret_cast<const float4*>(sums + (size_t)t * nseg + sb * 16 + 8 * h);
-            const float4 sbv = *reinterpret_cast<const float4*>(sums + (size_t)t * nseg + sb * 16 + 8 * h + 4);
+            const float4 sa = *reinterpret_cast<const float4*>(tsum + 8 * h);
+            const float4 sbv = *reinterpret_cast<const float4*>(tsum + 8 * h + 4);
             const float gs[4] = {sa.x + sa.y, sa.z + sa.w, sbv.x + sbv.y, sbv.z + sbv.w};
             float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                a0 = fmaf((float)((m0 >> (8 * k)) & 63u), gs[k], a0);
-                a1 = fmaf((float)((m1 >> (8 * k)) & 63u), gs[k], a1);
+                a0 = fmaf((float)ubyte(m0, k), gs[k], a0);
+                a1 = fmaf((float)ubyte(m1, k), gs[k], a1);
             }
-            mn[0] = f16_to_f32(H0.x >> 16) * a0;
-            mn[1] = f16_to_f32(H1.x >> 16) * a1;
-        } else {
-            mn[0] = mn[1] = 0.f;
+            mn[0] = fmaf(f16_to_f32(H0.x >> 16), a0, mn[0]);
+            mn[1] = fmaf(f16_to_f32(H1.x >> 16), a1, mn[1]);
         }
-        uint32_t qh0a = 0, qh0b = 0, qh1a = 0, qh1b = 0;
+        uint2 qh0{0u, 0u}, qh1{0u, 0u};
         if constexpr (QT == T_Q5_K) {
-            qh0a = *reinterpret_cast<const uint32_t*>(r0 + 16 + 4 * t);
-            qh0b = *reinterpret_cast<const uint32_t*>(r0 + 32 + 4 * t);
-            qh1a = *reinterpret_cast<const uint32_t*>(r1 + 16 + 4 * t);
-            qh1b = *reinterpret_cast<const uint32_t*>(r1 + 32 + 4 * t);
+            qh0 = rows.ld64(0, o + 16 + 8 * t);
+            qh1 = rows.ld64(1, o + 16 + 8 * t);
+        }
+        // all operands of the task first (weights of both chunks, activations of the four 32-k blocks)
+        uint2 w0[2], w1[2], bl[2][NSET], bh[2][NSET];
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            const int c = 2 * h + cc;
+            // bytes 8t..8t+7 of chunk c: low nibbles = weights 64c + 8t.., high = 64c + 32 + 8t..
+            w0[cc] = rows.ld64(0, o + QS + 32 * c + 8 * t);
+            w1[cc] = rows.ld64(1, o + QS + 32 * c + 8 * t);
+#pragma unroll
+            for (int st = 0; st < NSET; st++) {
+                bl[cc][st] = bf.blk(st, sb * 8 + 2 * c);  // 32-k blocks: low nibbles of chunk c,
+                bh[cc][st] = bf.blk(st, sb * 8 + 2 * c + 1);  // then its high nibbles
+            }
         }
 #pragma unroll
         for (int cc = 0; cc < 2; cc++) {
             const int c = 2 * h + cc;
-            const uint32_t w0a = *reinterpret_cast<const uint32_t*>(r0 + QS + 32 * c + 4 * t);       // row g, l 4t..
-            const uint32_t w0b = *reinterpret_cast<const uint32_t*>(r0 + QS + 32 * c + 16 + 4 * t);  // row g, l 16+4t..
-            const uint32_t w1a = *reinterpret_cast<const uint32_t*>(r1 + QS + 32 * c + 4 * t);
-            const uint32_t w1b = *reinterpret_cast<const uint32_t*>(r1 + QS + 32 * c + 16 + 4 * t);
             uint32_t lo[4], hi[4];
             if constexpr (QT == T_Q4_K) {
-                lo[0] = w0a & 0x0f0f0f0fu;
-                lo[1] = w1a & 0x0f0f0f0fu;
-                lo[2] = w0b & 0x0f0f0f0fu;
-                lo[3] = w1b & 0x0f0f0f0fu;
-                hi[0] = (w0a >> 4) & 0x0f0f0f0fu;
-                hi[1] = (w1a >> 4) & 0x0f0f0f0fu;
-                hi[2] = (w0b >> 4) & 0x0f0f0f0fu;
-                hi[3] = (w1b >> 4) & 0x0f0f0f0fu;
+                lo[0] = w0[cc].x & 0x0f0f0f0fu;
+                lo[1] = w1[cc].x & 0x0f0f0f0fu;
+                lo[2] = w0[cc].y & 0x0f0f0f0fu;
+                lo[3] = w1[cc].y & 0x0f0f0f0fu;
+                hi[0] = w0[cc].x & 0xf0f0f0f0u;
+                hi[1] = w1[cc].x & 0xf0f0f0f0u;
+                hi[2] = w0[cc].y & 0xf0f0f0f0u;
+                hi[3] = w1[cc].y & 0xf0f0f0f0u;
             } else {  // fifth bit from qh: bit 2c for the low nibbles, 2c+1 for the high ones
-                lo[0] = (w0a & 0x0f0f0f0fu) | (((qh0a >> (2 * c)) & 0x01010101u) << 4);
-                lo[1] = (w1a & 0x0f0f0f0fu) | (((qh1a >> (2 * c)) & 0x01010101u) << 4);
-                lo[2] = (w0b & 0x0f0f0f0fu) | (((qh0b >> (2 * c)) & 0x01010101u) << 4);
-                lo[3] = (w1b & 0x0f0f0f0fu) | (((qh1b >> (2 * c)) & 0x01010101u) << 4);
-                hi[0] = ((w0a >> 4) & 0x0f0f0f0fu) | (((qh0a >> (2 * c + 1)) & 0x01010101u) << 4);
-                hi[1] = ((w1a >> 4) & 0x0f0f0f0fu) | (((qh1a >> (2 * c + 1)) & 0x01010101u) << 4);
-                hi[2] = ((w0b >> 4) & 0x0f0f0f0fu) | (((qh0b >> (2 * c + 1)) & 0x01010101u) << 4);
-                hi[3] = ((w1b >> 4) & 0x0f0f0f0fu) | (((qh1b >> (2 * c + 1)) & 0x01010101u) << 4);
+                lo[0] = (w0[cc].x & 0x0f0f0f0fu) | (((qh0.x >> (2 * c)) & 0x01010101u) << 4);
+                lo[1] = (w1[cc].x & 0x0f0f0f0fu) | (((qh1.x >> (2 * c)) & 0x01010101u) << 4);
+                lo[2] = (w0[cc].y & 0x0f0f0f0fu) | (((qh0.y >> (2 * c)) & 0x01010101u) << 4);
+                lo[3] = (w1[cc].y & 0x0f0f0f0fu) | (((qh1.y >> (2 * c)) & 0x01010101u) << 4);
+                hi[0] = ((w0[cc].x >> 4) & 0x0f0f0f0fu) | (((qh0.x >> (2 * c + 1)) & 0x01010101u) << 4);
+                hi[1] = ((w1[cc].x >> 4) & 0x0f0f0f0fu) | (((qh1.x >> (2 * c + 1)) & 0x01010101u) << 4);
+                hi[2] = ((w0[cc].y >> 4) & 0x0f0f0f0fu) | (((qh0.y >> (2 * c + 1)) & 0x01010101u) << 4);
+                hi[3] = ((w1[cc].y >> 4) & 0x0f0f0f0fu) | (((qh1.y >> (2 * c + 1)) & 0x01010101u) << 4);
             }
-            const int sl0 = (s0 >> (16 * cc)) & 63, sh0 = (s0 >> (16 * cc + 8)) & 63;
-            const int sl1 = (s1 >> (16 * cc)) & 63, sh1 = (s1 >> (16 * cc + 8)) & 63;
-            const int jl = sb * 8 + 2 * c;  // 32-k blocks: low nibbles of chunk c, then its high nibbles
+            constexpr int LS = QT == T_Q4_K ? 16 : 1;
+            const int sl0 = LS * ubyte(s0, 2 * cc), sh0 = ubyte(s0, 2 * cc + 1);
+            const int sl1 = LS * ubyte(s1, 2 * cc), sh1 = ubyte(s1, 2 * cc + 1);
 #pragma unroll
             for (int st = 0; st < NSET; st++) {
-                const uint2 bl = bf.blk(st, jl), bh = bf.blk(st, jl + 1);
-                scale_acc(acc[st], imma32(lo[0], lo[1], lo[2], lo[3], bl.x, bl.y), sl0, sl1);
-                scale_acc(acc[st], imma32(hi[0], hi[1], hi[2], hi[3], bh.x, bh.y), sh0, sh1);
+                scale_acc(acc[st], imma32(lo[0], lo[1], lo[2], lo[3], bl[cc][st].x, bl[cc][st].y), sl0, sl1);
+                scale_acc(acc[st], imma32(hi[0], hi[1], hi[2], hi[3], bh[cc][st].x, bh[cc][st].y), sh0, sh1);
             }
         }
     } else {  // Q6_K: half h = 128 weights; ib selects l in [16ib, 16ib+16)
-        d0 = f16_to_f32(*reinterpret_cast<const uint16_t*>(r0 + 208));
-        d1 = f16_to_f32(*reinterpret_cast<const uint16_t*>(r1 + 208));
-        const uint32_t sc0[2] = {ld_u32_any(r0 + 192 + 8 * h), ld_u32_any(r0 + 196 + 8 * h)};
-        const uint32_t sc1[2] = {ld_u32_any(r1 + 192 + 8 * h), ld_u32_any(r1 + 196 + 8 * h)};
-        mn[0] = mn[1] = 0.f;
-        const bool al4 = ((reinterpret_cast<uintptr_t>(r0) | reinterpret_cast<uintptr_t>(r1)) & 3) == 0;
+        d0 = f16_to_f32(rows.ld16(0, o + 208));
+        d1 = f16_to_f32(rows.ld16(1, o + 208));
+        const uint32_t sc0[2] = {rows.ld32(0, o + 192 + 8 * h), rows.ld32(0, o + 196 + 8 * h)};
+        const uint32_t sc1[2] = {rows.ld32(1, o + 192 + 8 * h), rows.ld32(1, o + 196 + 8 * h)};
+        uint32_t qa[2][2], qb[2][2], qh[2][2], bs[2][4][NSET];  // [ib][row]
 #pragma unroll
         for (int ib = 0; ib < 2; ib++) {
-            const int o = 16 * ib + 4 * t;
-            uint32_t qa0, qb0, qh0, qa1, qb1, qh1;
-            if (al4) {
-                qa0 = *reinterpret_cast<const uint32_t*>(r0 + 64 * h + o);
-                qb0 = *reinterpret_cast<const uint32_t*>(r0 + 64 * h + 32 + o);
-                qh0 = *reinterpret_cast<const uint32_t*>(r0 + 128 + 32 * h + o);
-                qa1 = *reinterpret_cast<const uint32_t*>(r1 + 64 * h + o);
-                qb1 = *reinterpret_cast<const uint32_t*>(r1 + 64 * h + 32 + o);
-                qh1 = *reinterpret_cast<const uint32_t*>(r1 + 128 + 32 * h + o);
-            } else {
-                qa0 = ld_u32_any(r0 + 64 * h + o);
-                qb0 = ld_u32_any(r0 + 64 * h + 32 + o);
-                qh0 = ld_u32_any(r0 + 128 + 32 * h + o);
-                qa1 = ld_u32_any(r1 + 64 * h + o);
-                qb1 = ld_u32_any(r1 + 64 * h + 32 + o);
-                qh1 = ld_u32_any(r1 + 128 + 32 * h + o);
+            const int q0 = o + 16 * ib + 4 * t;
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                qa[ib][r] = rows.ld32(r, q0 + 64 * h);
+                qb[ib][r] = rows.ld32(r, q0 + 64 * h + 32);
+                qh[ib][r] = rows.ld32(r, q0 + 128 + 32 * h);
             }
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int st = 0; st < NSET; st++) bs[ib][q][st] = bf.seg(st, sb * 16 + 8 * h + 2 * q + ib);
+        }
+#pragma unroll
+        for (int ib = 0; ib < 2; ib++) {
             // 6-bit values per byte (low nibble from ql, bits 4-5 from qh; qwen3moe.cpp:187-195),
             // then q - 32 as s8: ((q & 63) + 0x60) ^ 0x80 per byte, carry-free
-            const uint32_t v0[4] = {lop_sel(qa0, qh0 << 4, 0x0f0f0f0fu), lop_sel(qb0, qh0 << 2, 0x0f0f0f0fu),
-                                    lop_sel(qa0 >> 4, qh0, 0x0f0f0f0fu), lop_sel(qb0 >> 4, qh0 >> 2, 0x0f0f0f0fu)};
-            const uint32_t v1[4] = {lop_sel(qa1, qh1 << 4, 0x0f0f0f0fu), lop_sel(qb1, qh1 << 2, 0x0f0f0f0fu),
-                                    lop_sel(qa1 >> 4, qh1, 0x0f0f0f0fu), lop_sel(qb1 >> 4, qh1 >> 2, 0x0f0f0f0fu)};
+            const uint32_t v0[4] = {lop_sel(qa[ib][0], qh[ib][0] << 4, 0x0f0f0f0fu), lop_sel(qb[ib][0], qh[ib][0] << 2, 0x0f0f0f0fu),
+                                    lop_sel(qa[ib][0] >> 4, qh[ib][0], 0x0f0f0f0fu), lop_sel(qb[ib][0] >> 4, qh[ib][0] >> 2, 0x0f0f0f0fu)};
+            const uint32_t v1[4] = {lop_sel(qa[ib][1], qh[ib][1] << 4, 0x0f0f0f0fu), lop_sel(qb[ib][1], qh[ib][1] << 2, 0x0f0f0f0fu),
+                                    lop_sel(qa[ib][1] >> 4, qh[ib][1], 0x0f0f0f0fu), lop_sel(qb[ib][1] >> 4, qh[ib][1] >> 2, 0x0f0f0f0fu)};
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 const uint32_t a0 = ((v0[q] & 0x3f3f3f3fu) + 0x60606060u) ^ 0x80808080u;
@@ -231,17 +339,16 @@ __device__ __forceinline__ void mma_task(const uint8_t* __restrict__ base, int s
                 const int gl = 2 * q + ib;  // scale index within the half; segment 8h + gl of the super-block
                 const int sa = sbyte(sc0[gl >> 2], gl & 3), sbb = sbyte(sc1[gl >> 2], gl & 3);
 #pragma unroll
-                for (int st = 0; st < NSET; st++)
-                    scale_acc(acc[st], imma16s(a0, a1, bf.seg(st, sb * 16 + 8 * h + gl)), sa, sbb);
+                for (int st = 0; st < NSET; st++) scale_acc(acc[st], imma16s(a0, a1, bs[ib][q][st]), sa, sbb);
             }
         }
     }
 #pragma unroll
     for (int st = 0; st < NSET; st++) {
-        out[st][0] = d0 * (float)acc[st][0];
-        out[st][1] = d0 * (float)acc[st][1];
-        out[st][2] = d1 * (float)acc[st][2];
-        out[st][3] = d1 * (float)acc[st][3];
+        out[st][0] = fmaf(d0, (float)acc[st][0], out[st][0]);
+        out[st][1] = fmaf(d0, (float)acc[st][1], out[st][1]);
+        out[st][2] = fmaf(d1, (float)acc[st][2], out[st][2]);
+        out[st][3] = fmaf(d1, (float)acc[st][3], out[st][3]);
     }
 }
 

@@ -1,0 +1,873 @@
+// moe.cu -- the MoE block (qwen3moe.cpp:1006-1069) on sm_100a as three launches chained by programmatic
+// dependent launch (each starts while its predecessor finishes and waits in griddepcontrol.wait):
+//
+//   k_moe_route       block 0: router softmax + top-k + renormalisation (warp per token, the CPU
+//                     comparator of qwen3moe.cpp:1016), then the token->expert grouping: per-expert
+//                     token bitmasks (histogram), exclusive scan, stable scatter into expert-major slots,
+//                     and the work list: groups of up to MU consecutive slots of one expert, each with
+//                     its expert's weight pointers and tokens (GroupRec).
+//                     blocks 1..T: the tokens' activations in fragment form (XF).
+//   k_moe_gateup<G,U> persistent, one CTA per SM: units (group, 16 rows of FF) in contiguous ranges per
+//                     CTA. A producer warp streams each unit's gate and up rows HBM -> shared memory
+//                     through a ring of mbarrier-guarded stages, with the group's XF rows when the group
+//                     changes; 16 consumer warps run the int8 tensor-core GEMV (kq.cuh) with register
+//                     accumulators and read nothing from global memory; the last warp to finish a unit
+//                     reduces it and writes SiLU(g)*u. A 1-D bulk copy costs about the same time
+//                     whether it moves 1 KB or 9 KB (one copy per ~0.2 us per SM), so a matrix's 16 rows
+//                     come as two 8-row copies, the second placed 32 bytes off the first's bank
+//                     alignment, instead of sixteen row copies.
+//   k_moe_down<D>     persistent likewise over units (group, 64 rows of D) with 12 consumer warps. The
+//                     consumers put each group's h rows in fragment form in shared memory themselves
+//                     (the first group's while the first weight tiles are in flight). The warp that
+//                     completes a 64-row group's last unit adds each token's expert outputs, weighted, in
+//                     ascending expert order (qwen3moe.cpp:1025-1069) to the residual.
+//
+// Every mbarrier wait is bounded; a timeout flags ST_WAIT_TIMEOUT, stops the producer, drains the copies
+// already in flight (bounded) and ends the CTA.
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "kq.cuh"
+#include "ksb.cuh"
+
+namespace eb {
+
+namespace {
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void set_flag(int* status, int bits) {
+    if (status) atomicOr(status, bits);
+}
+__host__ __device__ constexpr size_t al128(size_t x) { return (x + 127) & ~(size_t)127; }
+__device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Row placement of a staged tile (as in the dense GEMV): rows whose stride is a multiple of 32 words
+// are copied one bulk copy per row into a 16-byte padded stride (bank spread); other strides as one
+// contiguous span from the 16-byte boundary at or below the first row.
+struct Rows {
+    int per_row;
+    int stride;
+};
+__host__ __device__ inline Rows rows_of(size_t rb) {
+    if (rb % 16 == 0 && (rb % 128) % 32 == 0) return {1, (int)rb + 16};
+    return {0, (int)rb};
+}
+__host__ __device__ inline size_t rows_slot(size_t rb, int n) { return al128((size_t)n * rows_of(rb).stride + 64); }
+__device__ __forceinline__ uint32_t rows_copy_bytes(const Rows& L, const uint8_t* base, size_t rb, int r0, int n) {
+    if (L.per_row) return (uint32_t)(n * rb);
+    const uintptr_t s = reinterpret_cast<uintptr_t>(base) + (size_t)r0 * rb, e = s + (size_t)n * rb;
+    return (uint32_t)(((e + 15) & ~(uintptr_t)15) - (s & ~(uintptr_t)15));
+}
+__device__ __forceinline__ uint32_t rows_lead(const Rows& L, const uint8_t* base, size_t rb, int r0) {
+    return L.per_row ? 0u : (uint32_t)((reinterpret_cast<uintptr_t>(base) + (size_t)r0 * rb) & 15);
+}
+__device__ __forceinline__ void rows_issue(const Rows& L, const uint8_t* base, size_t rb, int r0, int n, uint8_t* dst,
+                                           uint64_t* bar) {
+    if (L.per_row) {
+        for (int r = 0; r < n; r++) tma_load_1d(dst + (size_t)r * L.stride, base + (size_t)(r0 + r) * rb, (uint32_t)rb, bar);
+        return;
+    }
+    const uintptr_t s = reinterpret_cast<uintptr_t>(base) + (size_t)r0 * rb;
+    tma_load_1d(dst, reinterpret_cast<const void*>(s & ~(uintptr_t)15), rows_copy_bytes(L, base, rb, r0, n), bar);
+}
+
+// Staging buffer of MU XF rows of K elements: frag rows (K*3 bytes each), then the rows' scale and
+// group sums (XF gs rows, 16 + K/8 bytes each).
+__host__ __device__ constexpr size_t xs_gs_off(int K) { return (size_t)MU * K * 3; }
+__host__ __device__ constexpr size_t xs_bytes(int K) { return al128(xs_gs_off(K) + (size_t)MU * xf_gs_bytes(K)); }
+
+// Bulk copy of the XF rows of a group's tokens (tok0, and tok1 when mc == 2) into a staging buffer.
+static_assert(MU == 2, "xf_issue stages two rows");
+__device__ __forceinline__ void xf_issue(const XF& xf, int tok0, int tok1, int mc, int K, uint8_t* dst, uint64_t* bar) {
+    const uint32_t fb = (uint32_t)K * 3, sb = (uint32_t)xf_gs_bytes(K);
+    const uint8_t* F = reinterpret_cast<const uint8_t*>(xf.frag);
+    const uint8_t* Sg = xf.gs;
+    const uint32_t n0 = (mc == 2 && tok1 == tok0 + 1) ? 2u : 1u;  // adjacent rows: one copy each
+    tma_load_1d(dst, F + (size_t)tok0 * fb, n0 * fb, bar);
+    tma_load_1d(dst + xs_gs_off(K), Sg + (size_t)tok0 * sb, n0 * sb, bar);
+    if (mc == 2 && n0 == 1) {
+        tma_load_1d(dst + fb, F + (size_t)tok1 * fb, fb, bar);
+        tma_load_1d(dst + xs_gs_off(K) + sb, Sg + (size_t)tok1 * sb, sb, bar);
+    }
+}
+
+// After a failed wait: every stage that may still have copies in flight gets one more bounded wait.
+__device__ void drain(uint64_t* full, int issued, int consumed, int S) {
+    for (int i = consumed; i < issued; i++) mbar_wait_bounded(&full[i % S], (uint32_t)(i / S) & 1u);
+}
+
+// ---- shared-memory plan of the persistent kernels ---------------------------------------------------
+//   [0, 128)     mbarriers: full[4], empty[4], done[4], xready[2]
+//   info         per-stage unit descriptors (int4)
+//   cnt          per-stage finished-warp counters
+//   xf           two XF staging buffers (double-buffered by group)
+//   part         per-stage, per-warp partial results [S][NWC][16 rows][MU]
+//   comb         combine scratch of the down kernel (slots and weights of T*K (token, k) pairs)
+//   stages       the ring
+struct Plan {
+    int S;
+    size_t info_off, cnt_off, xf_off, xfb, part_off, comb_off, stage_off, stage_bytes, total;
+};
+constexpr size_t SMEM_CAP = 227 * 1024;
+__host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, size_t comb_bytes) {
+    Plan p;
+    p.info_off = 128;
+    p.cnt_off = p.info_off + 4 * 16;
+    p.xf_off = al128(p.cnt_off + 4 * 4);
+    p.xfb = xs_bytes(K);
+    p.part_off = al128(p.xf_off + 2 * p.xfb);
+    const size_t part_bytes = (size_t)nwc * 16 * MU * 4;
+    p.stage_bytes = al128(stage_bytes);
+    p.S = 4;
+    for (;; p.S--) {
+        p.comb_off = al128(p.part_off + (size_t)p.S * part_bytes);
+        p.stage_off = al128(p.comb_off + comb_bytes);
+        p.total = p.stage_off + (size_t)p.S * p.stage_bytes;
+        if (p.total <= SMEM_CAP || p.S == 2) break;
+    }
+    return p;
+}
+constexpr int NWC_GU = 16;   // consumer warps of the gate/up kernel
+constexpr int NWC_DN = 12;   // consumer warps of the down kernel
+constexpr int DN_ROWS = 64;  // rows of D per down unit
+constexpr size_t COMB_BYTES = (size_t)MOE_TMAX * 32 * 8;
+// Gate/up tiles: 16 rows of a matrix. Rows of a multiple of 16 bytes come as two 8-row copies, the
+// second at split8_off(rb) (32 bytes past a 128-byte boundary, so that rows 0..7 and 8..15 start on
+// different banks); other rows as one contiguous span copy.
+__host__ __device__ inline bool split8(size_t rb) { return rb % 16 == 0; }
+__host__ __device__ inline size_t split8_off(size_t rb) { return al128(8 * rb) + 32; }
+__host__ __device__ inline size_t gu_slot(size_t rb) { return split8(rb) ? al128(split8_off(rb) + 8 * rb) : al128(16 * rb + 64); }
+__host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu) {
+    return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0);
+}
+__host__ __device__ inline Plan down_plan(int FF, size_t rbd) {
+    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), COMB_BYTES);
+}
+
+// info word y: xf buffer (bit 0), slots in the group (bits 4-7), weights usable (bit 8), first unit of
+// the group in this CTA (bit 9)
+__device__ __forceinline__ int info_bits(int xb, int mc, bool ok, bool fresh) {
+    return xb | (mc << 4) | (ok ? 256 : 0) | (fresh ? 512 : 0);
+}
+
+// Per-warp epilogue of a 16-row block (one column set, <= 2 tokens): the lane's digit columns are
+// recombined across lanes, value = (a + b/254 + c/254^2 - min) * s; lanes t = 0, 1 end up with token
+// t's values of MMA rows g and g+8, which hold the block's rows row0 and row1. Stored to part[16][MU].
+__device__ __forceinline__ void warp_values(const float (&acc)[1][4], const float (&mn)[2], float ts, float* part,
+                                            int row0, int row1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const float A0 = __shfl_down_sync(0xffffffffu, acc[0][0], 1), B0 = __shfl_down_sync(0xffffffffu, acc[0][1], 1);
+    const float A1 = __shfl_down_sync(0xffffffffu, acc[0][2], 1), B1 = __shfl_down_sync(0xffffffffu, acc[0][3], 1);
+    constexpr float R = 1.0f / DIGIT;
+    float v0, v1;
+    if (t == 0) {  // token 0: columns 0, 1 (own), 2 (lane t+1's first)
+        v0 = fmaf(fmaf(A0, R, acc[0][1]), R, acc[0][0]);
+        v1 = fmaf(fmaf(A1, R, acc[0][3]), R, acc[0][2]);
+    } else {  // token 1: column 3 (own second), 4, 5 (lane t+1's)
+        v0 = fmaf(fmaf(B0, R, A0), R, acc[0][1]);
+        v1 = fmaf(fmaf(B1, R, A1), R, acc[0][3]);
+    }
+    (void)g;
+    if (t < MU) {
+        part[row0 * MU + t] = (v0 - mn[0]) * ts;
+        part[row1 * MU + t] = (v1 - mn[1]) * ts;
+    }
+}
+
+// One warp puts a row x of K floats (global, written by an earlier grid) in fragment form into
+// shared memory: frag (K*3 bytes) and gs (the scale, then the group sums; XF).
+__device__ void prep_row_warp(const float* __restrict__ x, int K, uint2* __restrict__ frag, uint8_t* __restrict__ gs) {
+    const int lane = threadIdx.x & 31, nblk = K >> 5;
+    float mx = 0.f;
+    for (int i = lane; i < (K >> 2); i += 32) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(x) + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (!(mx > 0.f) || mx == INFINITY) mx = 127.f;
+    if (lane == 0) *reinterpret_cast<float4*>(gs) = make_float4(mx / 127.f, 0.f, 0.f, 0.f);
+    const float inv = 127.f / mx;
+    for (int i = lane; i < nblk * 4; i += 32) {  // nblk * 4 is a multiple of 32 (K % 256 == 0)
+        const int j = i >> 2, t = i & 3;
+        const float4 u = __ldcg(reinterpret_cast<const float4*>(x + 32 * j + 8 * t));
+        const float4 w = __ldcg(reinterpret_cast<const float4*>(x + 32 * j + 8 * t + 4));
+        const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+        int dg[3][8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float v = xv[k] * inv;
+            const int a0 = digit(v);
+            const float r1 = (v - (float)a0) * DIGIT;
+            const int a1 = digit(r1);
+            dg[0][k] = a0;
+            dg[1][k] = a1;
+            dg[2][k] = digit((r1 - (float)a1) * DIGIT);
+        }
+        uint2* o = frag + (size_t)j * 12 + t;
+#pragma unroll
+        for (int p = 0; p < 3; p++)
+            o[p * 4] = make_uint2(pack4(dg[p][0], dg[p][1], dg[p][2], dg[p][3]), pack4(dg[p][4], dg[p][5], dg[p][6], dg[p][7]));
+        float s8 = ((u.x + u.y) + (u.z + u.w)) + ((w.x + w.y) + (w.z + w.w));
+        s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+        s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+        if (t == 0) put_group_sum(gs, j, s8 * inv);
+    }
+}
+
+// The super-blocks sb0, sb0 + step, ... of one warp on a staged 16-row block (rows.r[0], rows.r[1]: the
+// block's rows held by MMA rows g and g+8), accumulated in registers (ksb.cuh).
+template <int QT>
+__device__ __forceinline__ void block_tasks(const RowsAny& rows, int nsb, int sb0, int step, const BPtr<1>& bp,
+                                            const uint8_t* mq, float (&acc)[1][4], float (&mn)[2]) {
+    const int t = threadIdx.x & 3;
+    for (int sb = sb0; sb < nsb; sb += step) {
+        const uint8_t* r0 = rows.r[0] + (size_t)sb * block_bytes(QT);
+        const uint8_t* r1 = rows.r[1] + (size_t)sb * block_bytes(QT);
+        if constexpr (QT == T_Q6_K) {
+            const uint8_t* bq = bp.p[0] + 4 * t + 768 * sb;
+            const bool m0 = (smem_u32(r0) & 2u) != 0, m1 = (smem_u32(r1) & 2u) != 0;  // warp-uniform
+            if (m0) {
+                if (m1) sb_q6<true, true>(r0, r1, bq, t, acc[0]);
+                else sb_q6<true, false>(r0, r1, bq, t, acc[0]);
+            } else {
+                if (m1) sb_q6<false, true>(r0, r1, bq, t, acc[0]);
+                else sb_q6<false, false>(r0, r1, bq, t, acc[0]);
+            }
+        } else {
+            sb_q45<QT>(r0, r1, bp.p[0] + 8 * t + 768 * sb, mq + 32 * sb, t, acc[0], mn);
+        }
+    }
+}
+// The lane's B operand base of the minimum-term MMA (ksb.cuh) in a staging buffer's gs rows: token g/2
+// for g < 4 (token 0 beyond the group's slots or for g >= 4: those columns are never read), f16 high
+// parts for even g, residues for odd g.
+__device__ __forceinline__ const uint8_t* min_operand(const uint8_t* gs_rows, int K, int mc) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    int tok = g >> 1;
+    if (g >= 4 || tok >= mc) tok = 0;
+    return gs_rows + (size_t)tok * xf_gs_bytes(K) + 16 + (g & 1) * 16 + 4 * t;
+}
+// Rows 2g, 2g+1 of a tile staged with a row stride (lead: bytes before row 0)
+__device__ __forceinline__ RowsAny rows_pair(const uint8_t* tile, int stride) {
+    const int g = (threadIdx.x & 31) >> 2;
+    const uint8_t* r0 = tile + (size_t)(2 * g) * stride;
+    return RowsAny{{r0, r0 + stride}};
+}
+// A gate/up tile (16 rows of rb bytes). Split copies: MMA row g takes row p(g) = g/2 + 8 (g & 1), row
+// g+8 takes p(g) + 4, so each half-warp's four rows start on two different bank offsets. Span copies:
+// rows 2g, 2g+1 behind the lead bytes.
+__device__ __forceinline__ RowsAny rows_gu(const uint8_t* slot, size_t rb, uint32_t lead) {
+    const int g = (threadIdx.x & 31) >> 2;
+    if (split8(rb)) {
+        const int p = (g >> 1) + ((g & 1) ? 8 : 0);
+        const uint8_t* hi = slot + split8_off(rb);
+        const uint8_t* r0 = (g & 1) ? hi + (size_t)(g >> 1) * rb : slot + (size_t)(g >> 1) * rb;
+        (void)p;
+        return RowsAny{{r0, r0 + 4 * rb}};
+    }
+    const uint8_t* r0 = slot + lead + (size_t)(2 * g) * rb;
+    return RowsAny{{r0, r0 + rb}};
+}
+// Tile row held by MMA row g (i = 0) or g+8 (i = 1) of a gate/up tile
+__device__ __forceinline__ int gu_row(size_t rb, int g, int i) {
+    if (split8(rb)) return (g >> 1) + ((g & 1) ? 8 : 0) + 4 * i;
+    return 2 * g + i;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+// routing, grouping and activation prep
+// ------------------------------------------------------------------------------------------------
+// Position of the n-th (0-based) set bit of m (n < popcount(m)).
+__device__ __forceinline__ int nth_bit(unsigned long long m, int n) {
+    const int lo = __popc((unsigned)m);
+    if (n < lo) return (int)__fns((unsigned)m, 0, n + 1);
+    return 32 + (int)__fns((unsigned)(m >> 32), 0, n - lo + 1);
+}
+
+__global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
+    pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
+    if (blockIdx.x > 0) {  // activation prep of token blockIdx.x - 1
+        __shared__ float red[33];
+        const int row = blockIdx.x - 1;
+        prep_row(a.xn + (size_t)row * a.D, a.D, const_cast<uint2*>(a.xf.frag) + (size_t)row * (a.D >> 5) * 12,
+                 const_cast<float*>(a.xf.sum) + (size_t)row * ((a.D >> 4) + XF_SUM_PAD),
+                 const_cast<uint8_t*>(a.xf.gs) + (size_t)row * xf_gs_bytes(a.D), red);
+        return;
+    }
+    __shared__ int s_ids[MOE_TMAX * 32];
+    __shared__ float s_w[MOE_TMAX * 32];
+    __shared__ int cnt[MAX_EXPERTS];
+    __shared__ int off[MAX_EXPERTS];
+    __shared__ int goff[MAX_EXPERTS];
+    __shared__ unsigned long long mask[MAX_EXPERTS];
+    const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
+    for (int i = tid; i < E; i += blockDim.x) {
+        cnt[i] = 0;
+        mask[i] = 0ull;
+    }
+    for (int i = tid; i < a.D / DN_ROWS; i += blockDim.x) a.rw.rg_done[i] = 0;
+    __syncthreads();
+
+    // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022).
+    // Each round takes the best remaining (r desc, index asc) entry: a warp max of r (non-negative, so
+    // its bits order as unsigned integers), then the smallest index among the entries holding it.
+    const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
+    constexpr int PER = MAX_EXPERTS / 32;
+    const int per = (E + 31) >> 5;  // entries per lane
+    for (int t = warp; t < T; t += nwarp) {
+        const float* lg = a.logits + (size_t)t * E;
+        float l[PER];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int e = lane + 32 * i;
+            l[i] = (i < per && e < E) ? __ldg(lg + e) : -INFINITY;
+            mx = fmaxf(mx, l[i]);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // r = exp(l - max): the difference in fp32 as on the CPU, the exponential correctly rounded
+        unsigned key[PER];  // bits of r, + 1 (0: no entry or taken)
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            key[i] = (i < per && (lane + 32 * i) < E) ? __float_as_uint((float)exp((double)(l[i] - mx))) + 1u : 0u;
+        float tot = 0.f;
+        int my_e = 0;
+        float my_r = 0.f;
+        for (int k = 0; k < K; k++) {
+            unsigned lb = 0;
+            int li = 0;
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if (key[i] > lb) {  // strict: the lowest index wins ties within the lane
+                    lb = key[i];
+                    li = i;
+                }
+            const unsigned kmax = __reduce_max_sync(0xffffffffu, lb);
+            const unsigned emin = __reduce_min_sync(0xffffffffu, lb == kmax ? (unsigned)(lane + 32 * li) : 0xffffffffu);
+            if ((int)(emin & 31) == lane) {
+#pragma unroll
+                for (int i = 0; i < PER; i++)
+                    if (i == (int)(emin >> 5)) key[i] = 0u;
+            }
+            const float rb = __uint_as_float(kmax - 1u);
+            tot += rb;  // rank-order sum, identical on every lane
+            if (lane == k) {
+                my_e = (int)emin;
+                my_r = rb;
+            }
+        }
+        if (lane < K) {
+            const float w = __fdiv_rn(my_r, tot);
+            if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+                set_flag(a.status, ST_BAD_INDEX);
+                my_e = 0;
+            }
+            s_ids[t * K + lane] = my_e;
+            s_w[t * K + lane] = w;
+            a.rw.ids[(size_t)t * K + lane] = my_e;
+            a.rw.wts[(size_t)t * K + lane] = w;
+            atomicAdd(&cnt[my_e], 1);
+            atomicOr(&mask[my_e], 1ull << t);
+        }
+    }
+    __syncthreads();
+    // ---- exclusive scans: slots per expert, groups per expert (ceil(count / MU)), active experts;
+    // lane i covers experts [i * per, (i + 1) * per)
+    if (warp == 0) {
+        int c_in = 0, g_in = 0, a_in = 0;
+        for (int j = 0; j < per; j++) {
+            const int e = lane * per + j;
+            const int c = e < E ? cnt[e] : 0;
+            c_in += c;
+            g_in += (c + MU - 1) / MU;
+            a_in += c > 0;
+        }
+        int c_x = c_in, g_x = g_in, a_x = a_in;  // inclusive warp scans
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, c_x, o), gv = __shfl_up_sync(0xffffffffu, g_x, o),
+                      av = __shfl_up_sync(0xffffffffu, a_x, o);
+            if (lane >= o) {
+                c_x += v;
+                g_x += gv;
+                a_x += av;
+            }
+        }
+        int c_run = c_x - c_in, g_run = g_x - g_in, a_run = a_x - a_in;
+        for (int j = 0; j < per; j++) {
+            const int e = lane * per + j;
+            if (e >= E) break;
+            const int c = cnt[e];
+            off[e] = c_run;
+            goff[e] = g_run;
+            a.rw.offsets[e] = c_run;
+            if (c > 0) a.rw.active[1 + a_run++] = e;
+            c_run += c;
+            g_run += (c + MU - 1) / MU;
+        }
+        if (lane == 31) {
+            a.rw.offsets[E] = c_x;
+            a.rw.active[0] = a_x;
+            a.rw.ngroups[0] = g_x;
+        }
+    }
+    __syncthreads();
+    // ---- work list: groups of up to MU consecutive slots of one expert, expert ascending
+    for (int e = tid; e < E; e += blockDim.x) {
+        const int c = cnt[e];
+        if (c == 0) continue;
+        const uint8_t* wg = a.gate[e];
+        const uint8_t* wu = a.up[e];
+        const uint8_t* wd = a.down[e];
+        for (int j = 0; j * MU < c; j++) {
+            GroupRec r;
+            r.w[0] = wg;
+            r.w[1] = wu;
+            r.w[2] = wd;
+            r.e = e;
+            r.s0 = off[e] + j * MU;
+            r.mc = min(MU, c - j * MU);
+#pragma unroll
+            for (int k = 0; k < MU; k++) r.tok[k] = k < r.mc ? nth_bit(mask[e], j * MU + k) : 0;
+            a.rw.groups[goff[e] + j] = r;
+        }
+    }
+    // ---- stable scatter, one thread per (token, k): slot = offset[e] + earlier tokens routed to e;
+    // the token's slots in ascending order (= expert order) by rank among its k experts
+    for (int i = tid; i < T * K; i += blockDim.x) {
+        const int t = i / K;
+        const int e = s_ids[i];
+        const int s = off[e] + __popcll(mask[e] & ((1ull << t) - 1ull));
+        a.rw.slot_token[s] = t;
+        a.rw.slot_w[s] = s_w[i];
+        int rank = 0;
+        for (int j = 0; j < K; j++) rank += s_ids[t * K + j] < e;
+        a.rw.token_slots[(size_t)t * K + rank] = s;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// gate + up + SiLU*mul
+// ------------------------------------------------------------------------------------------------
+template <int QG, int QU>
+__global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int D = a.D, FF = a.FF, nsb = D >> 8, NRB = FF >> 4, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const Plan pl = gateup_plan(D, a.gate_rb, a.up_rb);
+    const int S = pl.S;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* empty = full + 4;
+    uint64_t* done = full + 8;  // per stage: every consumer warp has stored its partial results
+    int4* info = reinterpret_cast<int4*>(sm + pl.info_off);
+    __shared__ int abort_flag;
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NWC_GU);
+            mbar_init(&done[s], NWC_GU);
+        }
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();  // routing results and the XF of the tokens come from k_moe_route
+    const int G = a.rw.ngroups[0];
+    const int nunits = G * NRB;
+    const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
+    const size_t rbg = a.gate_rb, rbu = a.up_rb, up_at = gu_slot(rbg);
+    const Rows Lg = rows_of(rbg), Lu = rows_of(rbu);  // span layouts (rows that are not 16-byte multiples)
+
+    if (warp == NWC_GU) {  // ---------------- producer
+        if (lane != 0) return;
+        int cur = -1, xb = 1, i = 0;
+        GroupRec rec{}, nxt{};
+        if (u0 < u1) nxt = a.rw.groups[u0 / NRB];
+        for (int u = u0; u < u1; u++, i++) {
+            const int s = i % S;
+            if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)(i / S - 1) & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                break;
+            }
+            if (*(volatile int*)&abort_flag) break;
+            const int gi = u / NRB, rb = u - gi * NRB, r0 = 16 * rb;
+            const bool fresh = gi != cur;
+            if (fresh) {
+                rec = nxt;
+                cur = gi;
+                xb ^= 1;
+                if ((gi + 1) * NRB < u1) nxt = a.rw.groups[gi + 1];  // the next group's record, ahead of use
+            }
+            const bool ok = al16(rec.w[0]) && al16(rec.w[1]);
+            if (!ok) set_flag(a.status, ST_BAD_ARG);
+            uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
+            const uint32_t lg = (!split8(rbg) && ok) ? rows_lead(Lg, rec.w[0], rbg, r0) : 0u;
+            const uint32_t lu = (!split8(rbu) && ok) ? rows_lead(Lu, rec.w[1], rbu, r0) : 0u;
+            info[s] = make_int4(rb, info_bits(xb, rec.mc, ok, fresh), rec.s0, (int)(lg | (lu << 8)));
+            uint32_t bytes = fresh ? (uint32_t)rec.mc * ((uint32_t)D * 3 + (uint32_t)xf_gs_bytes(D)) : 0u;
+            if (ok) {
+                bytes += split8(rbg) ? (uint32_t)(16 * rbg) : rows_copy_bytes(Lg, rec.w[0], rbg, r0, 16);
+                bytes += split8(rbu) ? (uint32_t)(16 * rbu) : rows_copy_bytes(Lu, rec.w[1], rbu, r0, 16);
+            }
+            mbar_expect_tx(&full[s], bytes);
+            if (fresh) xf_issue(a.xf, rec.tok[0], rec.tok[1], rec.mc, D, sm + pl.xf_off + (size_t)xb * pl.xfb, &full[s]);
+            if (ok) {
+                if (split8(rbg)) {
+                    tma_load_1d(stage, rec.w[0] + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
+                    tma_load_1d(stage + split8_off(rbg), rec.w[0] + (size_t)(r0 + 8) * rbg, (uint32_t)(8 * rbg), &full[s]);
+                } else {
+                    rows_issue(Lg, rec.w[0], rbg, r0, 16, stage, &full[s]);
+                }
+                if (split8(rbu)) {
+                    tma_load_1d(stage + up_at, rec.w[1] + (size_t)r0 * rbu, (uint32_t)(8 * rbu), &full[s]);
+                    tma_load_1d(stage + up_at + split8_off(rbu), rec.w[1] + (size_t)(r0 + 8) * rbu, (uint32_t)(8 * rbu),
+                                &full[s]);
+                } else {
+                    rows_issue(Lu, rec.w[1], rbu, r0, 16, stage + up_at, &full[s]);
+                }
+            }
+        }
+        // wait (bounded) until the consumers have released every issued stage, so that no copy is in
+        // flight when the CTA retires (after a consumer timeout: drain the copies instead)
+        const int issued = i;
+        for (int k = (issued > S ? issued - S : 0); k < issued; k++) {
+            if (!mbar_wait_bounded(&empty[k % S], (uint32_t)(k / S) & 1u)) {
+                drain(full, issued, k, S);
+                break;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers: warp w works on matrix w / 8 (gate, up), super-blocks w % 8 + 8j
+    const int mtx = warp >> 3, wsub = warp & 7, g = lane >> 2, t = lane & 3;
+    const size_t rbm = mtx ? rbu : rbg;
+    const int prow0 = gu_row(rbm, g, 0), prow1 = gu_row(rbm, g, 1);
+    int i = 0;
+    for (int u = u0; u < u1; u++, i++) {
+        const int s = i % S;
+        if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+            set_flag(a.status, ST_WAIT_TIMEOUT);
+            atomicExch(&abort_flag, 1);
+            return;  // the producer drains what it issued
+        }
+        const int4 in = info[s];
+        const int rb = in.x, xb = in.y & 1, mc = (in.y >> 4) & 15, s0 = in.z;
+        const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
+        if (in.y & 256) {
+            const BPtr<1> bp(xs, D >> 5, mc);
+            const uint8_t* mq = min_operand(xs + xs_gs_off(D), D, mc);
+            const uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
+            if (mtx == 0)
+                block_tasks<QG>(rows_gu(stage, rbg, in.w & 255), nsb, wsub, 8, bp, mq, acc, mn);
+            else
+                block_tasks<QU>(rows_gu(stage + up_at, rbu, (in.w >> 8) & 255), nsb, wsub, 8, bp, mq, acc, mn);
+        }
+        const float ts = t < mc ? *reinterpret_cast<const float*>(xs + xs_gs_off(D) + (size_t)t * xf_gs_bytes(D)) : 0.f;
+        float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_GU + warp) * 16 * MU;
+        warp_values(acc, mn, ts, part, prow0, prow1);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&done[s]);
+        if (warp == i % NWC_GU) {  // this unit's reducer (round robin): SiLU*mul of the summed partials
+            if (!mbar_wait_bounded(&done[s], (uint32_t)(i / S) & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                return;
+            }
+            const float* P = reinterpret_cast<const float*>(sm + pl.part_off) + (size_t)s * NWC_GU * 16 * MU;
+            const int r = lane >> 1, tk = lane & 1;
+            if (tk < mc) {
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    gv += P[(w * 16 + r) * MU + tk];
+                    uv += P[((8 + w) * 16 + r) * MU + tk];
+                }
+                a.h[(size_t)(s0 + tk) * FF + 16 * rb + r] = silu_mul(gv, uv);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// down projection + weighted combine + residual add
+// ------------------------------------------------------------------------------------------------
+template <int QD>
+__global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS, T = a.T, K = a.n_used;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t rb = a.down_rb;
+    const Plan pl = down_plan(FF, rb);
+    const int S = pl.S;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* empty = full + 4;
+    uint64_t* done = full + 8;     // per stage: every consumer warp has stored its partial results
+    uint64_t* xready = full + 12;  // per XF buffer: its rows are in fragment form (MU warp arrivals)
+    int4* info = reinterpret_cast<int4*>(sm + pl.info_off);
+    __shared__ int abort_flag;
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NWC_DN);
+            mbar_init(&done[s], NWC_DN);
+        }
+        mbar_init(&xready[0], MU);
+        mbar_init(&xready[1], MU);
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();  // h and the routing come from the previous grids
+    const int G = a.rw.ngroups[0];
+    const int nunits = G * NRG;
+    const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
+    const Rows L = rows_of(rb);
+
+    if (warp == NWC_DN) {  // ---------------- producer
+        if (lane != 0) return;
+        int cur = -1, xb = 1, i = 0;
+        GroupRec rec{}, nxt{};
+        if (u0 < u1) nxt = a.rw.groups[u0 / NRG];
+        for (int u = u0; u < u1; u++, i++) {
+            const int s = i % S;
+            if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)(i / S - 1) & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                break;
+            }
+            if (*(volatile int*)&abort_flag) break;
+            const int gi = u / NRG, rg = u - gi * NRG;
+            const bool fresh = gi != cur;
+            if (fresh) {
+                rec = nxt;
+                cur = gi;
+                xb ^= 1;
+                if ((gi + 1) * NRG < u1) nxt = a.rw.groups[gi + 1];
+            }
+            const uint8_t* w = rec.w[2];
+            const bool ok = al16(w);
+            if (!ok) set_flag(a.status, ST_BAD_ARG);
+            info[s] = make_int4(rg, info_bits(xb, rec.mc, ok, fresh), rec.s0,
+                                ok ? (int)rows_lead(L, w, rb, DN_ROWS * rg) : 0);
+            const uint32_t bytes = ok ? rows_copy_bytes(L, w, rb, DN_ROWS * rg, DN_ROWS) : 0u;
+            mbar_expect_tx(&full[s], bytes);
+            if (ok) rows_issue(L, w, rb, DN_ROWS * rg, DN_ROWS, sm + pl.stage_off + (size_t)s * pl.stage_bytes, &full[s]);
+        }
+        const int issued = i;
+        for (int k = (issued > S ? issued - S : 0); k < issued; k++) {
+            if (!mbar_wait_bounded(&empty[k % S], (uint32_t)(k / S) & 1u)) {
+                drain(full, issued, k, S);
+                break;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers: warp w works on rows 16 (w / 3) .. +15 of the unit, super-blocks w % 3 + 3j
+    const int rbk = warp / 3, wsub = warp - 3 * rbk, t = lane & 3;
+    // h rows of a group -> fragment form in XF buffer xb: warp k < MU preps slot s0 + k (if the group
+    // has it), then arrives on xready[xb]
+    auto prep_group = [&](int xb, int s0, int mc) {
+        if (warp < MU) {
+            uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
+            if (warp < mc)
+                prep_row_warp(a.h + (size_t)(s0 + warp) * FF, FF, reinterpret_cast<uint2*>(xs + (size_t)warp * FF * 3),
+                              xs + xs_gs_off(FF) + (size_t)warp * xf_gs_bytes(FF));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xready[xb]);
+        }
+    };
+    int uses[2] = {0, 0};
+    if (u0 < u1) {  // the first group's h rows, while the first weight tiles are in flight
+        const GroupRec r0 = a.rw.groups[u0 / NRG];
+        prep_group(0, r0.s0, r0.mc);
+    }
+    float* cw = reinterpret_cast<float*>(sm + pl.comb_off);  // combine scratch: weights, then slots
+    int* cs = reinterpret_cast<int*>(sm + pl.comb_off + (size_t)MOE_TMAX * 32 * 4);
+    int i = 0;
+    for (int u = u0; u < u1; u++, i++) {
+        const int s = i % S;
+        if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+            set_flag(a.status, ST_WAIT_TIMEOUT);
+            atomicExch(&abort_flag, 1);
+            return;
+        }
+        const int4 in = info[s];
+        const int rg = in.x, xb = in.y & 1, mc = (in.y >> 4) & 15, s0 = in.z;
+        if (in.y & 512) {  // first unit of a group in this CTA: its h rows must be in fragment form
+            if (u != u0) prep_group(xb, s0, mc);
+            if (!mbar_wait_bounded(&xready[xb], (uint32_t)uses[xb] & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                return;
+            }
+            uses[xb]++;
+        }
+        const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
+        if (in.y & 256) {
+            const BPtr<1> bp(xs, FF >> 5, mc);
+            block_tasks<QD>(rows_pair(sm + pl.stage_off + (size_t)s * pl.stage_bytes + in.w + (size_t)(16 * rbk) * L.stride,
+                                      L.stride),
+                            nsb, wsub, 3, bp, min_operand(xs + xs_gs_off(FF), FF, mc), acc, mn);
+        }
+        const float ts = t < mc ? *reinterpret_cast<const float*>(xs + xs_gs_off(FF) + (size_t)t * xf_gs_bytes(FF)) : 0.f;
+        float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_DN + warp) * 16 * MU;
+        warp_values(acc, mn, ts, part, 2 * ((lane >> 2) & 7), 2 * ((lane >> 2) & 7) + 1);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&done[s]);
+        const bool reducer = warp == i % NWC_DN;
+        if (reducer) {  // this unit's reducer (round robin): y rows of the unit's slots
+            if (!mbar_wait_bounded(&done[s], (uint32_t)(i / S) & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                return;
+            }
+            const float* P = reinterpret_cast<const float*>(sm + pl.part_off) + (size_t)s * NWC_DN * 16 * MU;
+            for (int j = lane; j < DN_ROWS * MU; j += 32) {
+                const int r = j >> 1, tk = j & 1;
+                if (tk < mc) {
+                    const int rk = r >> 4, rr = r & 15;
+                    const float v = (P[((3 * rk) * 16 + rr) * MU + tk] + P[((3 * rk + 1) * 16 + rr) * MU + tk]) +
+                                    P[((3 * rk + 2) * 16 + rr) * MU + tk];
+                    a.y[(size_t)(s0 + tk) * D + DN_ROWS * rg + r] = v;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (reducer) {  // after releasing the stage: count the unit; the last one combines the row group
+            __threadfence();
+            __syncwarp();
+            int done = 0;
+            if (lane == 0) done = atomicAdd(&a.rw.rg_done[rg], 1);
+            done = __shfl_sync(0xffffffffu, done, 0);
+            if (done == G - 1) {  // every group has written these rows: combine in expert order
+                __threadfence();
+                for (int j = lane; j < T * K; j += 32) {
+                    const int sl = __ldcg(a.rw.token_slots + j);
+                    cs[j] = sl;
+                    cw[j] = __ldcg(a.rw.slot_w + sl);
+                }
+                __syncwarp();
+                for (int j = lane; j < T * DN_ROWS; j += 32) {
+                    const int tk = j / DN_ROWS, r = j - tk * DN_ROWS;
+                    float accv = 0.f;
+                    for (int k = 0; k < K; k++)  // ascending slots = ascending experts (qwen3moe.cpp:1025)
+                        accv = fmaf(cw[tk * K + k], __ldcg(a.y + (size_t)cs[tk * K + k] * D + DN_ROWS * rg + r), accv);
+                    a.x[(size_t)tk * D + DN_ROWS * rg + r] += accv;
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// launchers
+// ------------------------------------------------------------------------------------------------
+namespace {
+template <typename Kern>
+void smem_attr(Kern k, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, size_t> done;
+    std::lock_guard<std::mutex> lk(mu);
+    size_t& cur = done[reinterpret_cast<const void*>(k)];
+    if (cur < smem) {
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cur = smem;
+    }
+}
+// Launch with programmatic stream serialization: the kernel may start before its predecessor on the
+// stream has finished and calls griddepcontrol.wait before reading the predecessor's results.
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern k, int grid, int block, size_t smem, cudaStream_t st, const Args&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+int max_groups(const MoeArgs& a) { return std::min(a.T * a.n_used, a.n_expert * ((a.T + MU - 1) / MU)); }
+
+}  // namespace
+
+size_t moe_smem_gateup(int D, size_t rbg, size_t rbu) { return gateup_plan(D, rbg, rbu).total; }
+size_t moe_smem_down(int FF, size_t rbd) { return down_plan(FF, rbd).total; }
+
+cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st) {
+    if (a.T < 1 || a.T > MOE_TMAX || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert ||
+        a.D % 256 || a.D % DN_ROWS)
+        return cudaErrorInvalidValue;
+    k_moe_route<<<1 + a.T, ROUTE_NT, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <int QG, int QU>
+static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
+    const Plan pl = gateup_plan(a.D, a.gate_rb, a.up_rb);
+    if (pl.total > SMEM_CAP || (a.FF >> 4) < pl.S) return cudaErrorInvalidValue;
+    smem_attr(k_moe_gateup<QG, QU>, pl.total);
+    const int units = max_groups(a) * (a.FF >> 4);
+    return launch_pdl(k_moe_gateup<QG, QU>, std::min(sm_count(), units), (NWC_GU + 1) * 32, pl.total, st, a);
+}
+template <int QG>
+static cudaError_t gateup_g(const MoeArgs& a, cudaStream_t st) {
+    switch (a.up_type) {
+        case T_Q4_K: return gateup_as<QG, T_Q4_K>(a, st);
+        case T_Q5_K: return gateup_as<QG, T_Q5_K>(a, st);
+        case T_Q6_K: return gateup_as<QG, T_Q6_K>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st) {
+    if (a.D % 256 || a.FF % 256) return cudaErrorInvalidValue;
+    switch (a.gate_type) {
+        case T_Q4_K: return gateup_g<T_Q4_K>(a, st);
+        case T_Q5_K: return gateup_g<T_Q5_K>(a, st);
+        case T_Q6_K: return gateup_g<T_Q6_K>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int QD>
+static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
+    const Plan pl = down_plan(a.FF, a.down_rb);
+    if (pl.total > SMEM_CAP || a.D / DN_ROWS < pl.S) return cudaErrorInvalidValue;
+    smem_attr(k_moe_down<QD>, pl.total);
+    const int units = max_groups(a) * (a.D / DN_ROWS);
+    return launch_pdl(k_moe_down<QD>, std::min(sm_count(), units), (NWC_DN + 1) * 32, pl.total, st, a);
+}
+cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {
+    if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX) return cudaErrorInvalidValue;
+    switch (a.down_type) {
+        case T_Q4_K: return down_as<T_Q4_K>(a, st);
+        case T_Q5_K: return down_as<T_Q5_K>(a, st);
+        case T_Q6_K: return down_as<T_Q6_K>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace eb

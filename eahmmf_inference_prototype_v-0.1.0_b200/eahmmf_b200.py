@@ -183,9 +183,10 @@ class MoeLayer:
 
     @staticmethod
     def profile_read() -> np.ndarray:
-        """Stage durations (us) of the last call: router GEMV, prep, route/permute, gate/up, h prep, down."""
-        us = np.zeros(6, np.float32)
-        if lib().eahmmf_cuda_moe_profile_read(us.ctypes.data, 6):
+        """Stage durations (us) of the last call: router GEMV, routing + activation prep, gate/up (+ h
+        prep), down + combine."""
+        us = np.zeros(4, np.float32)
+        if lib().eahmmf_cuda_moe_profile_read(us.ctypes.data, 4):
             raise RuntimeError("eahmmf_cuda_moe_profile_read failed")
         return us
 

@@ -91,9 +91,10 @@ int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, con
                           void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);
 
 /* Stage timing of eahmmf_cuda_moe_layer: when enabled, each call records CUDA events on its stream
- * around its six stages (router GEMV, activation prep, route/permute, gate/up, h prep, down/combine);
- * eahmmf_cuda_moe_profile_read waits for the last call and returns the six stage durations (us) of its
- * last 64-token block. Off by default; single-threaded use. */
+ * around its four stages (router GEMV, routing + activation prep, gate/up, down/combine);
+ * eahmmf_cuda_moe_profile_read waits for the last call and returns the four stage durations (us) of its
+ * last 64-token block. The events serialise the stages (each kernel timed on its own). Off by default;
+ * single-threaded use. */
 int eahmmf_cuda_moe_profile(int enable);
 int eahmmf_cuda_moe_profile_read(float* us, int cap);
 
