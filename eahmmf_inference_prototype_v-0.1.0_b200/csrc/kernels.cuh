@@ -59,7 +59,7 @@ struct RouteWs {
     int* token_slots;  // [T*K] slots of token t, ascending (= expert-ascending)
     int* ngroups;      // [1] number of work groups
     GroupRec* groups;  // [T*K] work groups, expert ascending
-    int* rg_done;      // [D/64] down units finished per 64-row group of the output
+    int* tok_done;     // [T * D/64] expert outputs stored per token and 64-row group of the output
 };
 
 struct MoeArgs {

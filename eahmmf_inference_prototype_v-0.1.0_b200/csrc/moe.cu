@@ -18,9 +18,10 @@
 //                     alignment, instead of sixteen row copies.
 //   k_moe_down<D>     persistent likewise over units (group, 64 rows of D) with 12 consumer warps. The
 //                     consumers put each group's h rows in fragment form in shared memory themselves
-//                     (the first group's while the first weight tiles are in flight). The warp that
-//                     completes a 64-row group's last unit adds each token's expert outputs, weighted, in
-//                     ascending expert order (qwen3moe.cpp:1025-1069) to the residual.
+//                     (the first group's while the first weight tiles are in flight). Per token and 64-row
+//                     group of D a counter collects the K expert outputs; the warp that stores the K-th
+//                     adds them, weighted, in ascending expert order (qwen3moe.cpp:1025-1069) to the
+//                     residual, so the combine is spread over all units instead of waiting for the last.
 //
 // Every mbarrier wait is bounded; a timeout flags ST_WAIT_TIMEOUT, stops the producer, drains the copies
 // already in flight (bounded) and ends the CTA.
@@ -137,7 +138,6 @@ __host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, si
 constexpr int NWC_GU = 16;   // consumer warps of the gate/up kernel
 constexpr int NWC_DN = 12;   // consumer warps of the down kernel
 constexpr int DN_ROWS = 64;  // rows of D per down unit
-constexpr size_t COMB_BYTES = (size_t)MOE_TMAX * 32 * 8;
 // Gate/up tiles: 16 rows of a matrix. Rows of a multiple of 16 bytes come as two 8-row copies, the
 // second at split8_off(rb) (32 bytes past a 128-byte boundary, so that rows 0..7 and 8..15 start on
 // different banks); other rows as one contiguous span copy.
@@ -148,7 +148,7 @@ __host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu) {
     return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0);
 }
 __host__ __device__ inline Plan down_plan(int FF, size_t rbd) {
-    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), COMB_BYTES);
+    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0);
 }
 
 // info word y: xf buffer (bit 0), slots in the group (bits 4-7), weights usable (bit 8), first unit of
@@ -294,6 +294,122 @@ __device__ __forceinline__ int nth_bit(unsigned long long m, int n) {
     return 32 + (int)__fns((unsigned)(m >> 32), 0, n - lo + 1);
 }
 
+// Orderable key of a float: a larger float has a larger key; only one NaN pattern maps to 0, which is
+// reserved for "no entry".
+__device__ __forceinline__ uint32_t fkey(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+// Top-k of one token by the reference's ranking (qwen3moe.cpp:1012-1020): r = expf(l - max) computed as
+// the correctly rounded exponential of the fp32 difference, order (r desc, index asc), weights r / sum
+// of the k r in rank order. Lane j < k returns the j-th expert and its weight.
+//
+// exp is monotone, so the top k by r are the top k by d = l - max unless entries of different d round
+// to the same r. Candidates are therefore ranked by (d desc, index asc) without exponentials; if any
+// other entry lies within 2^-20 of the k-th d (it could round to the same r) or the k-th r is below
+// 2^-100 (where rounding groups wider ranges), every entry's r is computed and ranked instead. Otherwise
+// the k candidates take one exponential each (one lane each) and are re-sorted by (r desc, index asc),
+// which only reorders runs of equal r. rk: 64 words of shared scratch of this warp.
+template <int PER>
+__device__ void route_token(const float* __restrict__ lg, int E, int K, int lane, uint32_t* rk, int& out_e,
+                            float& out_w) {
+    float d[PER];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int e = lane + 32 * i;
+        d[i] = e < E ? __ldg(lg + e) : -INFINITY;
+        mx = fmaxf(mx, d[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    uint32_t key[PER];
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        d[i] = d[i] - mx;  // the CPU's fp32 difference
+        key[i] = (lane + 32 * i) < E ? fkey(d[i]) : 0u;
+    }
+    // (d desc, index asc) top k; lane j keeps the j-th (d, e)
+    float cd = 0.f, dk = 0.f;
+    int ce = 0;
+    for (int k = 0; k < K; k++) {
+        uint32_t lb = 0;
+        int li = 0;
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            if (key[i] > lb) {
+                lb = key[i];
+                li = i;
+            }
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, lb);
+        const uint32_t emin = __reduce_min_sync(0xffffffffu, lb == kmax ? (uint32_t)(lane + 32 * li) : 0xffffffffu);
+        float dsel = 0.f;
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            if ((int)(emin & 31) == lane && i == (int)(emin >> 5)) {
+                dsel = d[i];
+                key[i] = 0u;
+            }
+        dsel = __shfl_sync(0xffffffffu, dsel, (int)(emin & 31));
+        if (lane == k) {
+            cd = dsel;
+            ce = (int)emin;
+        }
+        dk = dsel;
+    }
+    const float rK = (float)exp((double)dk);
+    bool near = false;
+#pragma unroll
+    for (int i = 0; i < PER; i++) near |= key[i] != 0u && d[i] >= dk - 9.5367431640625e-07f;  // 2^-20
+    if (!__any_sync(0xffffffffu, near) && rK >= 7.888609052210118e-31f) {  // 2^-100
+        // one exponential per candidate, then rank (r desc, index asc) among the k
+        const float r = lane < K ? (float)exp((double)cd) : -1.0f;
+        int rank = 0;
+        for (int j = 0; j < K; j++) {
+            const float rj = __shfl_sync(0xffffffffu, r, j);
+            const int ej = __shfl_sync(0xffffffffu, ce, j);
+            rank += (rj > r) || (rj == r && ej < ce);
+        }
+        if (lane < K) {
+            rk[2 * rank] = __float_as_uint(r);
+            rk[2 * rank + 1] = (uint32_t)ce;
+        }
+    } else {
+        // every entry's r, then k rounds of (r desc, index asc)
+        uint32_t* rkey = key;  // the logit keys are spent
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            rkey[i] = (lane + 32 * i) < E ? __float_as_uint((float)exp((double)d[i])) + 1u : 0u;
+        for (int k = 0; k < K; k++) {
+            uint32_t lb = 0;
+            int li = 0;
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if (rkey[i] > lb) {
+                    lb = rkey[i];
+                    li = i;
+                }
+            const uint32_t kmax = __reduce_max_sync(0xffffffffu, lb);
+            const uint32_t emin = __reduce_min_sync(0xffffffffu, lb == kmax ? (uint32_t)(lane + 32 * li) : 0xffffffffu);
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if ((int)(emin & 31) == lane && i == (int)(emin >> 5)) rkey[i] = 0u;
+            if (lane == 0) {
+                rk[2 * k] = kmax - 1u;
+                rk[2 * k + 1] = emin;
+            }
+        }
+    }
+    __syncwarp();
+    float tot = 0.f;
+    for (int k = 0; k < K; k++) tot += __uint_as_float(rk[2 * k]);  // rank-order sum, identical on every lane
+    if (lane < K) {
+        out_e = (int)rk[2 * lane + 1];
+        out_w = __fdiv_rn(__uint_as_float(rk[2 * lane]), tot);
+    }
+    __syncwarp();
+}
+
 __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
     if (blockIdx.x > 0) {  // activation prep of token blockIdx.x - 1
@@ -306,6 +422,7 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     }
     __shared__ int s_ids[MOE_TMAX * 32];
     __shared__ float s_w[MOE_TMAX * 32];
+    __shared__ uint32_t s_rk[(ROUTE_NT / 32) * 64];  // per warp: ranked (r, expert) of up to 32 candidates
     __shared__ int cnt[MAX_EXPERTS];
     __shared__ int off[MAX_EXPERTS];
     __shared__ int goff[MAX_EXPERTS];
@@ -315,68 +432,26 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         cnt[i] = 0;
         mask[i] = 0ull;
     }
-    for (int i = tid; i < a.D / DN_ROWS; i += blockDim.x) a.rw.rg_done[i] = 0;
+    for (int i = tid; i < T * (a.D / DN_ROWS); i += blockDim.x) a.rw.tok_done[i] = 0;
     __syncthreads();
 
-    // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022).
-    // Each round takes the best remaining (r desc, index asc) entry: a warp max of r (non-negative, so
-    // its bits order as unsigned integers), then the smallest index among the entries holding it.
+    // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022)
     const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
-    constexpr int PER = MAX_EXPERTS / 32;
-    const int per = (E + 31) >> 5;  // entries per lane
     for (int t = warp; t < T; t += nwarp) {
-        const float* lg = a.logits + (size_t)t * E;
-        float l[PER];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-            const int e = lane + 32 * i;
-            l[i] = (i < per && e < E) ? __ldg(lg + e) : -INFINITY;
-            mx = fmaxf(mx, l[i]);
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        // r = exp(l - max): the difference in fp32 as on the CPU, the exponential correctly rounded
-        unsigned key[PER];  // bits of r, + 1 (0: no entry or taken)
-#pragma unroll
-        for (int i = 0; i < PER; i++)
-            key[i] = (i < per && (lane + 32 * i) < E) ? __float_as_uint((float)exp((double)(l[i] - mx))) + 1u : 0u;
-        float tot = 0.f;
         int my_e = 0;
-        float my_r = 0.f;
-        for (int k = 0; k < K; k++) {
-            unsigned lb = 0;
-            int li = 0;
-#pragma unroll
-            for (int i = 0; i < PER; i++)
-                if (key[i] > lb) {  // strict: the lowest index wins ties within the lane
-                    lb = key[i];
-                    li = i;
-                }
-            const unsigned kmax = __reduce_max_sync(0xffffffffu, lb);
-            const unsigned emin = __reduce_min_sync(0xffffffffu, lb == kmax ? (unsigned)(lane + 32 * li) : 0xffffffffu);
-            if ((int)(emin & 31) == lane) {
-#pragma unroll
-                for (int i = 0; i < PER; i++)
-                    if (i == (int)(emin >> 5)) key[i] = 0u;
-            }
-            const float rb = __uint_as_float(kmax - 1u);
-            tot += rb;  // rank-order sum, identical on every lane
-            if (lane == k) {
-                my_e = (int)emin;
-                my_r = rb;
-            }
-        }
+        float my_w = 0.f;
+        if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, s_rk + warp * 64, my_e, my_w);
+        else if (E <= 256) route_token<8>(a.logits + (size_t)t * E, E, K, lane, s_rk + warp * 64, my_e, my_w);
+        else route_token<16>(a.logits + (size_t)t * E, E, K, lane, s_rk + warp * 64, my_e, my_w);
         if (lane < K) {
-            const float w = __fdiv_rn(my_r, tot);
             if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
                 set_flag(a.status, ST_BAD_INDEX);
                 my_e = 0;
             }
             s_ids[t * K + lane] = my_e;
-            s_w[t * K + lane] = w;
+            s_w[t * K + lane] = my_w;
             a.rw.ids[(size_t)t * K + lane] = my_e;
-            a.rw.wts[(size_t)t * K + lane] = w;
+            a.rw.wts[(size_t)t * K + lane] = my_w;
             atomicAdd(&cnt[my_e], 1);
             atomicOr(&mask[my_e], 1ull << t);
         }
@@ -384,6 +459,7 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     __syncthreads();
     // ---- exclusive scans: slots per expert, groups per expert (ceil(count / MU)), active experts;
     // lane i covers experts [i * per, (i + 1) * per)
+    const int per = (E + 31) >> 5;
     if (warp == 0) {
         int c_in = 0, g_in = 0, a_in = 0;
         for (int j = 0; j < per; j++) {
@@ -610,7 +686,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
 template <int QD>
 __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS, T = a.T, K = a.n_used;
+    const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS, K = a.n_used;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t rb = a.down_rb;
     const Plan pl = down_plan(FF, rb);
@@ -699,8 +775,6 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         const GroupRec r0 = a.rw.groups[u0 / NRG];
         prep_group(0, r0.s0, r0.mc);
     }
-    float* cw = reinterpret_cast<float*>(sm + pl.comb_off);  // combine scratch: weights, then slots
-    int* cs = reinterpret_cast<int*>(sm + pl.comb_off + (size_t)MOE_TMAX * 32 * 4);
     int i = 0;
     for (int u = u0; u < u1; u++, i++) {
         const int s = i % S;
@@ -753,26 +827,36 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        if (reducer) {  // after releasing the stage: count the unit; the last one combines the row group
+        if (reducer) {  // after releasing the stage: count the unit's tokens; the K-th output of a token combines
             __threadfence();
             __syncwarp();
-            int done = 0;
-            if (lane == 0) done = atomicAdd(&a.rw.rg_done[rg], 1);
-            done = __shfl_sync(0xffffffffu, done, 0);
-            if (done == G - 1) {  // every group has written these rows: combine in expert order
-                __threadfence();
-                for (int j = lane; j < T * K; j += 32) {
-                    const int sl = __ldcg(a.rw.token_slots + j);
-                    cs[j] = sl;
-                    cw[j] = __ldcg(a.rw.slot_w + sl);
-                }
-                __syncwarp();
-                for (int j = lane; j < T * DN_ROWS; j += 32) {
-                    const int tk = j / DN_ROWS, r = j - tk * DN_ROWS;
-                    float accv = 0.f;
-                    for (int k = 0; k < K; k++)  // ascending slots = ascending experts (qwen3moe.cpp:1025)
-                        accv = fmaf(cw[tk * K + k], __ldcg(a.y + (size_t)cs[tk * K + k] * D + DN_ROWS * rg + r), accv);
-                    a.x[(size_t)tk * D + DN_ROWS * rg + r] += accv;
+            for (int tk = 0; tk < mc; tk++) {
+                const int tok = __ldcg(a.rw.slot_token + s0 + tk);
+                int done = 0;
+                if (lane == 0) done = atomicAdd(&a.rw.tok_done[tok * NRG + rg], 1);
+                done = __shfl_sync(0xffffffffu, done, 0);
+                if (done == K - 1) {  // all K expert outputs of this token's 64 rows are stored
+                    __threadfence();
+                    int sl = 0;
+                    float wk = 0.f;
+                    if (lane < K) {
+                        sl = __ldcg(a.rw.token_slots + tok * K + lane);
+                        wk = __ldcg(a.rw.slot_w + sl);
+                    }
+                    const size_t col = (size_t)DN_ROWS * rg + 2 * lane;
+                    float2 accv = make_float2(0.f, 0.f);
+                    for (int k = 0; k < K; k++) {  // ascending slots = ascending experts (qwen3moe.cpp:1025)
+                        const int sk = __shfl_sync(0xffffffffu, sl, k);
+                        const float w = __shfl_sync(0xffffffffu, wk, k);
+                        const float2 v = __ldcg(reinterpret_cast<const float2*>(a.y + (size_t)sk * D + col));
+                        accv.x = fmaf(w, v.x, accv.x);
+                        accv.y = fmaf(w, v.y, accv.y);
+                    }
+                    float2* xp = reinterpret_cast<float2*>(a.x + (size_t)tok * D + col);
+                    float2 xv = *xp;
+                    xv.x += accv.x;
+                    xv.y += accv.y;
+                    *xp = xv;
                 }
             }
         }

@@ -83,9 +83,9 @@ size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
  *   logits = d_logits ? d_logits : d_xn x router^T;  softmax numerators exp(l - max);  top-k with the
  *   reference's comparator;  weights renormalised over the k;  per active expert (ascending id) the
  *   gate/up projections, SiLU(g)*u, the down projection, and the weighted sum added to d_x.
- * d_xn: [T x D] expert input (post-norm); d_x: [T x D] residual, updated in place. Tokens are taken in
- * blocks of 64, as the engine's forward() is fed at most MAXB = 64 tokens (qwen3moe.cpp:39, :933); per-
- * token results do not depend on the blocking. d_status (optional) receives EAHMMF_ST_* bits raised
+ * d_xn: [T x D] expert input (post-norm, 16-byte aligned); d_x: [T x D] residual (8-byte aligned), updated
+ * in place. Tokens are taken in blocks of 64, as the engine's forward() is fed at most MAXB = 64 tokens
+ * (qwen3moe.cpp:39, :933); per-token results do not depend on the blocking. d_status (optional) receives EAHMMF_ST_* bits raised
  * inside kernels. */
 int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                           void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);

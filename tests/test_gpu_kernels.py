@@ -176,6 +176,56 @@ def test_moe_routing_ties_and_many_tokens(torch_cuda, orc, experts_c2, layer_c2)
     assert np.all(ids[64:80] == np.arange(8)[None, :])
 
 
+def _adversarial_logits(T, E, K, seed):
+    """Logit rows that stress the routing shortcut: 1-ulp gaps at the k-th place, differences that the
+    exponential rounds to equal numerators, numerators that underflow, and masked (-inf) entries."""
+    rng = synth._rng(seed)
+    lg = synth.router_logits(T, E, seed=seed)
+    q = T // 4
+    for t in range(q):  # 1-ulp (and equal) neighbours of the k-th largest
+        order = np.argsort(-lg[t], kind="stable")
+        kth = lg[t, order[K - 1]]
+        for j, e in enumerate(order[K:K + 4]):
+            lg[t, e] = np.nextafter(kth, np.float32(-np.inf)) if j % 2 == 0 else kth
+    for t in range(q, 2 * q):  # numerators that round to 1.0 (differences below 2^-25) or to its neighbour
+        step = 2.0**-31 if t % 2 == 0 else 1e-9
+        lg[t] = (rng.integers(0, 64, E) * step).astype(np.float32)
+    for t in range(2 * q, 3 * q):  # one dominant entry, the rest underflow or go subnormal
+        lg[t] = rng.uniform(-160.0, -95.0, E).astype(np.float32)
+        lg[t, rng.integers(0, E)] = 0.0
+    for t in range(3 * q, T):  # masked entries
+        lg[t, rng.choice(E, E // 2, replace=False)] = -np.inf
+    return lg
+
+
+def test_moe_routing_adversarial_ties(torch_cuda, orc, layer_c2):
+    """Bit-exact ids and weights where logit order and numerator order disagree (exp rounding ties)."""
+    T = 64
+    lg = _adversarial_logits(T, 128, 8, seed=41)
+    x = synth.activations(T, 2048, seed=6)
+    y, ids, w = run_layer(torch_cuda, layer_c2, x, x, lg)
+    io, wo = orc.route(lg, 8)
+    np.testing.assert_array_equal(ids, io)
+    np.testing.assert_allclose(w, wo, rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("E,K", [(256, 8), (300, 10)])
+def test_moe_routing_wide_expert_counts(torch_cuda, orc, E, K):
+    """Routing of layers with more than 128 experts (wider per-lane candidate lists)."""
+    torch = torch_cuda
+    ex = synth.expert_set(D=256, FF=256, n_expert=E, types=(12, 12, 12), seed=E, d_sigma=0.002)
+    layer = eb.MoeLayer.from_expert_set(ex, n_used=K)
+    T = 32
+    lg = _adversarial_logits(T, E, K, seed=E + 1)
+    x = synth.activations(T, 256, seed=E + 2)
+    y, ids, w = run_layer(torch, layer, x, x, lg)
+    io, wo = orc.route(lg, K)
+    np.testing.assert_array_equal(ids, io)
+    np.testing.assert_allclose(w, wo, rtol=1e-6, atol=0)
+    yo, _, _ = orc.moe_layer(x, x, lg, list(ex.gate), list(ex.up), list(ex.down), ex.types, ex.row_bytes, K)
+    assert rel_l2(y - x, yo - x) < 1e-5
+
+
 def test_moe_layer_is_deterministic(torch_cuda, layer_c2):
     T = 8
     x = synth.activations(T, 2048, seed=9)
