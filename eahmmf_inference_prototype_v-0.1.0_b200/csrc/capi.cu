@@ -148,7 +148,7 @@ namespace {
 constexpr int CHUNK = MOE_TMAX;  // tokens per MoE block pass
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 struct WsLayout {
-    size_t ids, wts, logits, offsets, active, slot_token, slot_w, token_slots, ngroups, groups, tok_done, h, xf, y,
+    size_t ids, wts, logits, offsets, active, slot_token, slot_w, token_slots, ngroups, groups, h, xf, y,
         total;
 };
 WsLayout ws_layout(const EahmmfMoeLayer* L, int T) {
@@ -170,7 +170,6 @@ WsLayout ws_layout(const EahmmfMoeLayer* L, int T) {
     take(w.token_slots, S * 4);
     take(w.ngroups, 4);
     take(w.groups, S * sizeof(GroupRec));
-    take(w.tok_done, (size_t)Tc * (L->D / 64) * 4);
     take(w.h, S * L->FF * 4);
     take(w.xf, xf_bytes(Tc, L->D));
     take(w.y, S * L->D * 4);
@@ -272,7 +271,6 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
         a.rw.token_slots = reinterpret_cast<int*>(ws + w.token_slots);
         a.rw.ngroups = reinterpret_cast<int*>(ws + w.ngroups);
         a.rw.groups = reinterpret_cast<GroupRec*>(ws + w.groups);
-        a.rw.tok_done = reinterpret_cast<int*>(ws + w.tok_done);
         a.xf = xf_carve(ws + w.xf, tc, L->D);
         a.y = reinterpret_cast<float*>(ws + w.y);
         a.status = d_status;

@@ -1,0 +1,447 @@
+// decode.cu -- the non-expert kernels of a qwen3moe forward pass (Engine::forward, qwen3moe.cpp:929-1074)
+// on sm_100a: embedding rows, RMSNorm, QK-norm + NeoX RoPE + KV-cache append, causal GQA attention as
+// split-context partials plus a merge, first-maximum argmax, and the device-side decode state.
+//
+// Every kernel that depends on the position reads it from device memory (`DecodeState.pos`), so one
+// captured CUDA graph serves every decode step: the argmax kernel writes the next token and advances
+// the position for the following replay.
+//
+// These kernels are memory- or latency-bound (a few KB to a few MB per call); the weight GEMVs around
+// them (kernels.cu, moe.cu) carry the bytes.
+#include <float.h>
+#include <math.h>
+
+#include "decode.cuh"
+
+namespace eb {
+
+// ---- dequantisation of single rows (embedding lookup), the reference decoders (qwen3moe.cpp:128-202)
+__device__ __forceinline__ float f16_at(const uint8_t* p) {
+    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, int& mn) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        mn = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+        mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+// Element i of a row of `type` (block-granular random access).
+__device__ float dq_elem(const uint8_t* row, int type, int i) {
+    switch (type) {
+        case T_F32: return reinterpret_cast<const float*>(row)[i];
+        case T_F16: return f16_at(row + 2 * i);
+        case T_Q8_0: {
+            const uint8_t* b = row + (i >> 5) * 34;
+            return f16_at(b) * (float)(int8_t)b[2 + (i & 31)];
+        }
+        case T_Q4_K:
+        case T_Q5_K: {
+            const bool q5 = type == T_Q5_K;
+            const uint8_t* b = row + (i >> 8) * (q5 ? 176 : 144);
+            const int e = i & 255, c = e >> 6, hi = (e >> 5) & 1, l = e & 31;
+            int sc, mn;
+            scale_min_k4(2 * c + hi, b + 4, sc, mn);
+            const uint8_t* qs = b + (q5 ? 48 : 16);
+            int q = hi ? (qs[32 * c + l] >> 4) : (qs[32 * c + l] & 0x0f);
+            if (q5) q += ((b[16 + l] >> (2 * c + hi)) & 1) << 4;
+            const float d = f16_at(b) * (float)sc, o = f16_at(b + 2) * (float)mn;
+            return d * (float)q - o;
+        }
+        case T_Q6_K: {
+            const uint8_t* b = row + (i >> 8) * 210;
+            const int e = i & 255, h = e >> 7, r = e & 127, quad = r >> 5, l = r & 31;
+            const uint8_t* ql = b + 64 * h;
+            const uint8_t* qh = b + 128 + 32 * h;
+            const int8_t* s = reinterpret_cast<const int8_t*>(b + 192) + 8 * h;
+            const uint8_t lo = (quad & 1) ? ql[l + 32] : ql[l];
+            const int q = (int)(((quad & 2) ? (lo >> 4) : (lo & 0x0f)) | (((qh[l] >> (2 * quad)) & 3) << 4)) - 32;
+            return f16_at(b + 208) * (float)s[l / 16 + 2 * quad] * (float)q;
+        }
+        default: return 0.f;
+    }
+}
+
+__global__ void k_embed(const uint8_t* __restrict__ W, int type, size_t row_bytes, int D, int n_rows,
+                        const int* __restrict__ toks, int nb, float* __restrict__ x, int* status) {
+    const int t = blockIdx.x;
+    if (t >= nb) return;
+    const int id = toks[t];
+    if (id < 0 || id >= n_rows) {
+        if (threadIdx.x == 0) atomicOr(status, ST_BAD_INDEX);
+        for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)t * D + i] = 0.f;
+        return;
+    }
+    const uint8_t* row = W + (size_t)id * row_bytes;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)t * D + i] = dq_elem(row, type, i);
+}
+
+// ---- RMSNorm (qwen3moe.cpp:527-532): out = x * (1 / sqrtf(mean(x^2) + eps)) * w, one block per row
+template <int NT>
+__device__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    v = lane < NT / 32 ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+constexpr int NORM_NT = 256;
+__global__ void __launch_bounds__(NORM_NT) k_rmsnorm(const float* __restrict__ x, int ldx, const float* __restrict__ w,
+                                                     float* __restrict__ out, int ldo, int n, float eps) {
+    __shared__ float red[NORM_NT / 32];
+    const float* xr = x + (size_t)blockIdx.x * ldx;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += NORM_NT) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum<NORM_NT>(ss, red);
+    const float sc = 1.0f / sqrtf(ss / (float)n + eps);
+    float* o = out + (size_t)blockIdx.x * ldo;
+    for (int i = threadIdx.x; i < n; i += NORM_NT) o[i] = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+}
+
+// ---- rotary table: cos/sin of (p0 + t) * inv_freq[i] in double, rounded to float (qwen3moe.cpp:937-943)
+__global__ void k_rope_table(const DecodeState* st, const float* __restrict__ inv_freq, int half, int nb,
+                             float2* __restrict__ cs) {
+    const int t = blockIdx.x;
+    const int p = st->pos + t;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const double ang = (double)p * (double)inv_freq[i];
+        cs[(size_t)t * half + i] = make_float2((float)cos(ang), (float)sin(ang));
+    }
+}
+
+// ---- per-head RMSNorm + NeoX rotation of q and k, KV-cache append (qwen3moe.cpp:951-972)
+// qkv: [nb x (QD + 2 KD)] rows as the fused q|k|v projection writes them. One warp per (token, head)
+// over the n_head q heads, n_kv k heads and n_kv v heads; lane l holds elements l, l+32, ... of the head.
+template <int HD>
+__global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv, const float* __restrict__ qn,
+                             const float* __restrict__ kn, float eps, const float2* __restrict__ cs,
+                             const DecodeState* st, int nb, float* __restrict__ q_out, float* __restrict__ kc,
+                             float* __restrict__ vc) {
+    constexpr int PER = HD / 32, HALF = HD / 2;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nh = n_head + 2 * n_kv, QD = n_head * HD, KD = n_kv * HD;
+    if (gw >= nb * nh) return;
+    const int t = gw / nh, h = gw - t * nh;
+    const float* src = qkv + (size_t)t * (QD + 2 * KD) + (size_t)h * HD;
+    const int pos = st->pos + t;
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+    if (h >= n_head + n_kv) {  // v head: copied into the cache unchanged
+        float* dst = vc + (size_t)pos * KD + (size_t)(h - n_head - n_kv) * HD;
+#pragma unroll
+        for (int j = 0; j < PER; j++) dst[lane + 32 * j] = v[j];
+        return;
+    }
+    const float* nw = h < n_head ? qn : kn;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float sc = 1.0f / sqrtf(ss / (float)HD + eps);
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = __fmul_rn(__fmul_rn(v[j], sc), nw[lane + 32 * j]);
+    // element e = lane + 32 j pairs with e + HALF = lane + 32 (j + PER/2)
+#pragma unroll
+    for (int j = 0; j < PER / 2; j++) {
+        const float2 r = cs[(size_t)t * HALF + lane + 32 * j];
+        const float a = v[j], b = v[j + PER / 2];
+        v[j] = a * r.x - b * r.y;
+        v[j + PER / 2] = a * r.y + b * r.x;
+    }
+    float* dst = h < n_head ? q_out + (size_t)t * QD + (size_t)h * HD
+                            : kc + (size_t)pos * KD + (size_t)(h - n_head) * HD;
+#pragma unroll
+    for (int j = 0; j < PER; j++) dst[lane + 32 * j] = v[j];
+}
+
+// ---- causal GQA attention (qwen3moe.cpp:976-1001), split over the context
+// Block (kv head h, split y, token t) runs the GRP q heads sharing kv head h over context chunks
+// y, y + nsplit, ... of ATT_CH positions, with an online softmax, and writes one partial (max, sum,
+// unnormalised output) per q head; k_attn_merge combines the splits. K/V chunks are staged in shared
+// memory with rows padded by 4 floats (conflict-free row-parallel score reads).
+template <int HD>
+__global__ void __launch_bounds__(ATT_NT) k_attn_partial(const float* __restrict__ q, const float* __restrict__ kc,
+                                                          const float* __restrict__ vc, int n_head, int n_kv,
+                                                          float scale, const DecodeState* st, int nsplit,
+                                                          float* __restrict__ part) {
+    constexpr int PER = HD / 32, RS = HD + 4;
+    extern __shared__ __align__(16) float smf[];
+    float* Ks = smf;                  // [ATT_CH][RS]
+    float* Vs = Ks + ATT_CH * RS;     // [ATT_CH][RS]
+    float* Ps = Vs + ATT_CH * RS;     // [ATT_NT/32][ATT_CH] probabilities of the warp's current head
+    float* Qs = Ps + (ATT_NT / 32) * ATT_CH;  // [GRP][HD]
+    const int h = blockIdx.x, y = blockIdx.y, t = blockIdx.z;
+    const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = ATT_NT / 32;
+    const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
+    const int nch = (np + ATT_CH - 1) / ATT_CH;
+    for (int i = threadIdx.x; i < grp * HD; i += ATT_NT) Qs[i] = q[(size_t)t * QD + (size_t)h * grp * HD + i];
+    // each warp owns q heads warp, warp + nwarp, ... (at most ATT_MAXH per warp)
+    float m_run[ATT_MAXH], l_run[ATT_MAXH], o_run[ATT_MAXH][PER];
+#pragma unroll
+    for (int k = 0; k < ATT_MAXH; k++) {
+        m_run[k] = -INFINITY;
+        l_run[k] = 0.f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) o_run[k][j] = 0.f;
+    }
+    for (int c = y; c < nch; c += nsplit) {
+        const int p0 = c * ATT_CH, n = min(ATT_CH, np - p0);
+        __syncthreads();  // previous chunk fully consumed (and Qs written, first time)
+        for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
+            const int r = i / (HD / 4), c4 = i - r * (HD / 4);
+            const size_t g = (size_t)(p0 + r) * KD + (size_t)h * HD + 4 * c4;
+            *reinterpret_cast<float4*>(Ks + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(kc + g);
+            *reinterpret_cast<float4*>(Vs + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(vc + g);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < ATT_MAXH; k++) {
+            const int hq = warp + k * nwarp;
+            if (hq >= grp) break;
+            const float* qh = Qs + hq * HD;
+            // scores: lane handles chunk positions lane, lane + 32
+            float s[ATT_CH / 32];
+            float mc = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < ATT_CH / 32; r++) {
+                const int pr = lane + 32 * r;
+                float acc = 0.f;
+                if (pr < n) {
+                    const float* kr = Ks + pr * RS;
+#pragma unroll 8
+                    for (int d = 0; d < HD; d += 4) {
+                        const float4 kv4 = *reinterpret_cast<const float4*>(kr + d);
+                        const float4 q4 = *reinterpret_cast<const float4*>(qh + d);
+                        acc = fmaf(q4.x, kv4.x, acc);
+                        acc = fmaf(q4.y, kv4.y, acc);
+                        acc = fmaf(q4.z, kv4.z, acc);
+                        acc = fmaf(q4.w, kv4.w, acc);
+                    }
+                    s[r] = acc * scale;
+                    mc = fmaxf(mc, s[r]);
+                } else {
+                    s[r] = -INFINITY;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+            const float m_new = fmaxf(m_run[k], mc);
+            const float alpha = expf(m_run[k] - m_new);  // 0 on the first chunk (m_run = -inf)
+            float ls = 0.f;
+#pragma unroll
+            for (int r = 0; r < ATT_CH / 32; r++) {
+                const float p = (lane + 32 * r) < n ? expf(s[r] - m_new) : 0.f;
+                Ps[warp * ATT_CH + lane + 32 * r] = p;
+                ls += p;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+            l_run[k] = l_run[k] * alpha + ls;
+            m_run[k] = m_new;
+            __syncwarp();
+            float acc[PER];
+#pragma unroll
+            for (int j = 0; j < PER; j++) acc[j] = o_run[k][j] * alpha;
+            for (int r = 0; r < n; r++) {
+                const float p = Ps[warp * ATT_CH + r];
+                const float* vr = Vs + r * RS;
+#pragma unroll
+                for (int j = 0; j < PER; j++) acc[j] = fmaf(p, vr[lane + 32 * j], acc[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < PER; j++) o_run[k][j] = acc[j];
+            __syncwarp();
+        }
+    }
+    // partial record per (token, q head, split): [m, l, o[HD]]
+#pragma unroll
+    for (int k = 0; k < ATT_MAXH; k++) {
+        const int hq = warp + k * nwarp;
+        if (hq >= grp) break;
+        float* pr = part + (((size_t)t * n_head + (size_t)h * grp + hq) * nsplit + y) * (HD + 2);
+        if (lane == 0) {
+            pr[0] = m_run[k];
+            pr[1] = l_run[k];
+        }
+#pragma unroll
+        for (int j = 0; j < PER; j++) pr[2 + lane + 32 * j] = o_run[k][j];
+    }
+}
+
+// out[t, head] = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M); one warp per (token, q head).
+template <int HD>
+__global__ void k_attn_merge(const float* __restrict__ part, int n_head, int nsplit, int nb, float* __restrict__ att) {
+    constexpr int PER = HD / 32;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (gw >= nb * n_head) return;
+    const float* p = part + (size_t)gw * nsplit * (HD + 2);
+    float M = -INFINITY;
+    for (int y = 0; y < nsplit; y++) M = fmaxf(M, p[(size_t)y * (HD + 2)]);
+    float L = 0.f, o[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) o[j] = 0.f;
+    for (int y = 0; y < nsplit; y++) {
+        const float* r = p + (size_t)y * (HD + 2);
+        if (r[0] == -INFINITY) continue;  // split without positions
+        const float e = expf(r[0] - M);
+        L = fmaf(r[1], e, L);
+#pragma unroll
+        for (int j = 0; j < PER; j++) o[j] = fmaf(r[2 + lane + 32 * j], e, o[j]);
+    }
+    const float inv = 1.0f / L;
+    float* dst = att + (size_t)gw * HD;  // gw = t * n_head + head: [nb x QD] rows
+#pragma unroll
+    for (int j = 0; j < PER; j++) dst[lane + 32 * j] = o[j] * inv;
+}
+
+// ---- argmax: first maximum, as std::max_element (qwen3moe.cpp:1103)
+// Blocks reduce strided slices to (value, index); the last block to finish reduces the block results,
+// records the token in the decode state (next input, output history) and advances the position.
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+__global__ void __launch_bounds__(ARGMAX_NT) k_argmax(const float* __restrict__ lg, int n, float2* __restrict__ blk,
+                                                       DecodeState* st, int advance) {
+    __shared__ float sv[ARGMAX_NT / 32];
+    __shared__ int si[ARGMAX_NT / 32];
+    __shared__ bool last;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = blockIdx.x * ARGMAX_NT + threadIdx.x; i < n; i += gridDim.x * ARGMAX_NT) {
+        const float v = lg[i];
+        if (better(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    auto warp_best = [&]() {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+    };
+    auto block_best = [&]() {
+        warp_best();
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        __syncthreads();
+        if (lane == 0) {
+            sv[w] = bv;
+            si[w] = bi;
+        }
+        __syncthreads();
+        bv = lane < ARGMAX_NT / 32 ? sv[lane] : -INFINITY;
+        bi = lane < ARGMAX_NT / 32 ? si[lane] : 0x7fffffff;
+        warp_best();
+    };
+    block_best();
+    if (threadIdx.x == 0) {
+        blk[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+        __threadfence();
+        last = atomicAdd(&st->ticket, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = 0x7fffffff;
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += ARGMAX_NT) {
+        const float2 r = __ldcg(blk + b);
+        const int ri = __float_as_int(r.y);
+        if (better(r.x, ri, bv, bi)) {
+            bv = r.x;
+            bi = ri;
+        }
+    }
+    block_best();
+    if (threadIdx.x == 0) {
+        if (bi == 0x7fffffff) bi = 0;  // every logit NaN: max_element returns the first element
+        st->ticket = 0;
+        st->token = bi;
+        if (st->n_out < st->cap_out) st->out[st->n_out] = bi;
+        st->n_out++;
+        if (advance) st->pos += 1;
+    }
+}
+
+// pos += n (host-enqueued position advance after a prompt chunk, kept on the device)
+__global__ void k_advance(DecodeState* st, int n) { st->pos += n; }
+
+// ---- launchers ---------------------------------------------------------------------------------
+cudaError_t launch_embed(const uint8_t* W, int type, size_t rb, int D, int n_rows, const int* toks, int nb, float* x,
+                         int* status, cudaStream_t s) {
+    k_embed<<<nb, 256, 0, s>>>(W, type, rb, D, n_rows, toks, nb, x, status);
+    return cudaGetLastError();
+}
+cudaError_t launch_rmsnorm(const float* x, int ldx, const float* w, float* out, int ldo, int rows, int n, float eps,
+                           cudaStream_t s) {
+    k_rmsnorm<<<rows, NORM_NT, 0, s>>>(x, ldx, w, out, ldo, n, eps);
+    return cudaGetLastError();
+}
+cudaError_t launch_rope_table(const DecodeState* st, const float* inv_freq, int half, int nb, float2* cs,
+                              cudaStream_t s) {
+    k_rope_table<<<nb, 64, 0, s>>>(st, inv_freq, half, nb, cs);
+    return cudaGetLastError();
+}
+cudaError_t launch_qk_rope_kv(int hd, const float* qkv, int n_head, int n_kv, const float* qn, const float* kn,
+                              float eps, const float2* cs, const DecodeState* st, int nb, float* q_out, float* kc,
+                              float* vc, cudaStream_t s) {
+    const int warps = nb * (n_head + 2 * n_kv), grid = (warps + 7) / 8;
+    if (hd == 128)
+        k_qk_rope_kv<128><<<grid, 256, 0, s>>>(qkv, n_head, n_kv, qn, kn, eps, cs, st, nb, q_out, kc, vc);
+    else if (hd == 64)
+        k_qk_rope_kv<64><<<grid, 256, 0, s>>>(qkv, n_head, n_kv, qn, kn, eps, cs, st, nb, q_out, kc, vc);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+size_t attn_smem(int hd, int grp) {
+    return ((size_t)2 * ATT_CH * (hd + 4) + (size_t)(ATT_NT / 32) * ATT_CH + (size_t)grp * hd) * sizeof(float);
+}
+template <int HD>
+static cudaError_t attn_as(const float* q, const float* kc, const float* vc, int n_head, int n_kv, float scale,
+                           const DecodeState* st, int nb, int nsplit, float* part, float* att, cudaStream_t s) {
+    const size_t smem = attn_smem(HD, n_head / n_kv);
+    static size_t cur = 0;
+    if (smem > cur) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        cur = smem;
+    }
+    k_attn_partial<HD><<<dim3(n_kv, nsplit, nb), ATT_NT, smem, s>>>(q, kc, vc, n_head, n_kv, scale, st, nsplit, part);
+    const int warps = nb * n_head;
+    k_attn_merge<HD><<<(warps + 7) / 8, 256, 0, s>>>(part, n_head, nsplit, nb, att);
+    return cudaGetLastError();
+}
+cudaError_t launch_attention(int hd, const float* q, const float* kc, const float* vc, int n_head, int n_kv,
+                             float scale, const DecodeState* st, int nb, int nsplit, float* part, float* att,
+                             cudaStream_t s) {
+    if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1) return cudaErrorInvalidValue;
+    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, s);
+    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, s);
+    return cudaErrorInvalidValue;
+}
+cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {
+    k_argmax<<<nblk, ARGMAX_NT, 0, s>>>(lg, n, blk, st, advance);
+    return cudaGetLastError();
+}
+cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s) {
+    k_advance<<<1, 1, 0, s>>>(st, n);
+    return cudaGetLastError();
+}
+
+}  // namespace eb

@@ -1,0 +1,48 @@
+// decode.cuh -- launch-side declarations of the forward-pass kernels outside the expert block
+// (decode.cu) and the device-resident decode state they share.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace eb {
+
+constexpr int ATT_CH = 64;       // context positions per attention chunk
+constexpr int ATT_NT = 256;      // threads of an attention block (8 warps)
+constexpr int ATT_MAXH = 2;      // q heads per warp: GQA groups of up to 16 heads per kv head
+constexpr int ARGMAX_NT = 1024;  // threads of an argmax block
+
+// Device-resident state of a generation: the position of the next forward pass, the token it feeds
+// (written by the argmax), and the output history. Kernels read `pos` at run time, so a captured
+// decode step replays unchanged.
+struct DecodeState {
+    int pos;      // position of the first token of the next forward pass
+    int token;    // next input token (argmax of the last logits)
+    int ticket;   // argmax block counter (reset by the last block)
+    int n_out;    // tokens recorded so far
+    int cap_out;  // capacity of out
+    int pad;
+    int* out;     // [cap_out] generated tokens
+};
+
+cudaError_t launch_embed(const uint8_t* W, int type, size_t rb, int D, int n_rows, const int* toks, int nb, float* x,
+                         int* status, cudaStream_t s);
+cudaError_t launch_rmsnorm(const float* x, int ldx, const float* w, float* out, int ldo, int rows, int n, float eps,
+                           cudaStream_t s);
+cudaError_t launch_rope_table(const DecodeState* st, const float* inv_freq, int half, int nb, float2* cs,
+                              cudaStream_t s);
+cudaError_t launch_qk_rope_kv(int hd, const float* qkv, int n_head, int n_kv, const float* qn, const float* kn,
+                              float eps, const float2* cs, const DecodeState* st, int nb, float* q_out, float* kc,
+                              float* vc, cudaStream_t s);
+size_t attn_smem(int hd, int grp);
+// part: nb * n_head * nsplit * (hd + 2) floats
+cudaError_t launch_attention(int hd, const float* q, const float* kc, const float* vc, int n_head, int n_kv,
+                             float scale, const DecodeState* st, int nb, int nsplit, float* part, float* att,
+                             cudaStream_t s);
+// blk: nblk float2 of scratch
+cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s);
+cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s);
+
+}  // namespace eb

@@ -1,0 +1,743 @@
+// engine.cu -- a device-resident qwen3moe forward pass (group 4 of include/eahmmf_b200.h): the whole
+// model of a GGUF file in HBM, Engine::forward / eval / greedy generation (qwen3moe.cpp:929-1084, the
+// harness-level greedy loop with --temp 0 --repeat-penalty 1.0) with every step on the GPU.
+//
+// Per layer and forward pass (nb tokens): RMSNorm -> fused q|k|v GEMV (one K-quant matrix, rows of
+// q, k and v concatenated at load) -> per-head RMSNorm + NeoX RoPE + KV append -> split-context GQA
+// attention -> o-projection GEMV accumulated into the residual -> RMSNorm -> MoE block
+// (eahmmf_cuda_moe_layer: router GEMV, top-k, grouping, gate/up/SiLU, down, combine). After the last
+// layer: RMSNorm of the last row -> output GEMV -> first-maximum argmax, which writes the next token and
+// advances the position on the device. One decode step is captured once as a CUDA graph and replayed
+// per token; nothing returns to the host between tokens.
+//
+// Numerics follow the reference's fp32 formulas (RMSNorm 1/sqrtf(mean + eps), RoPE angles in double
+// rounded to float, softmax attention with 1/sqrt(hd) scaling); summation orders differ (tree and
+// tensor-core reductions), so logits agree to fp32 rounding and greedy tokens agree exactly unless two
+// logits tie within that rounding.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/eahmmf_b200.h"
+#include "common.cuh"
+#include "decode.cuh"
+
+using namespace eb;
+
+namespace {
+
+// ---- GGUF v2/v3 reader (the container layout GGUF::load parses, qwen3moe.cpp:285-347) -------------
+struct GgufValue {
+    uint32_t type = 0;
+    int64_t i = 0;
+    double f = 0;
+    std::string s;
+};
+struct GgufTensor {
+    int nd = 0;
+    int64_t ne[4] = {1, 1, 1, 1};
+    int type = -1;
+    uint64_t off = 0;
+    size_t row_bytes = 0, bytes = 0;
+    uint64_t file_off = 0;
+};
+struct Gguf {
+    const uint8_t* map = nullptr;
+    size_t size = 0;
+    uint64_t data_start = 0;
+    std::map<std::string, GgufValue> kv;
+    std::map<std::string, GgufTensor> tensors;
+    std::string err;
+
+    ~Gguf() {
+        if (map) munmap(const_cast<uint8_t*>(map), size);
+    }
+    struct Rd {
+        const uint8_t *p, *end;
+        bool ok = true;
+        bool need(size_t n) {
+            if (!ok || (size_t)(end - p) < n) ok = false;
+            return ok;
+        }
+        template <typename V>
+        V get() {
+            V v{};
+            if (need(sizeof(V))) {
+                memcpy(&v, p, sizeof(V));
+                p += sizeof(V);
+            }
+            return v;
+        }
+        std::string str() {
+            const uint64_t n = get<uint64_t>();
+            if (!need(n)) return std::string();
+            std::string s(reinterpret_cast<const char*>(p), (size_t)n);
+            p += n;
+            return s;
+        }
+    };
+    static bool scalar(Rd& r, uint32_t t, GgufValue& v) {
+        v.type = t;
+        switch (t) {
+            case 0: v.i = r.get<uint8_t>(); break;
+            case 1: v.i = r.get<int8_t>(); break;
+            case 2: v.i = r.get<uint16_t>(); break;
+            case 3: v.i = r.get<int16_t>(); break;
+            case 4: v.i = r.get<uint32_t>(); break;
+            case 5: v.i = r.get<int32_t>(); break;
+            case 6: v.f = r.get<float>(); v.i = (int64_t)v.f; break;
+            case 7: v.i = r.get<uint8_t>(); break;
+            case 8: v.s = r.str(); break;
+            case 10: v.i = (int64_t)r.get<uint64_t>(); break;
+            case 11: v.i = r.get<int64_t>(); break;
+            case 12: v.f = r.get<double>(); v.i = (int64_t)v.f; break;
+            default: return false;
+        }
+        if (t != 6 && t != 12) v.f = (double)v.i;
+        return r.ok;
+    }
+    bool open(const char* path) {
+        const int fd = ::open(path, O_RDONLY);
+        if (fd < 0) return fail("cannot open file");
+        struct stat st;
+        if (fstat(fd, &st) != 0) {
+            ::close(fd);
+            return fail("cannot stat file");
+        }
+        size = (size_t)st.st_size;
+        void* m = size ? mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+        ::close(fd);
+        if (m == MAP_FAILED) {
+            map = nullptr;
+            return fail("mmap failed");
+        }
+        map = static_cast<const uint8_t*>(m);
+        Rd r{map, map + size};
+        if (size < 4 || memcmp(map, "GGUF", 4) != 0) return fail("not a GGUF file");
+        r.p += 4;
+        const uint32_t ver = r.get<uint32_t>();
+        if (ver < 2 || ver > 3) return fail("unsupported GGUF version");
+        const uint64_t nt = r.get<uint64_t>(), nkv = r.get<uint64_t>();
+        for (uint64_t i = 0; i < nkv && r.ok; i++) {
+            const std::string key = r.str();
+            const uint32_t t = r.get<uint32_t>();
+            GgufValue v;
+            if (t == 9) {  // array: skipped except for its length (tokenizer tables are not needed here)
+                const uint32_t et = r.get<uint32_t>();
+                const uint64_t n = r.get<uint64_t>();
+                if (et == 9) return fail("nested arrays unsupported");
+                for (uint64_t k = 0; k < n && r.ok; k++) {
+                    GgufValue e;
+                    if (!scalar(r, et, e)) return fail("bad array element");
+                }
+                v.type = 9;
+                v.i = (int64_t)n;
+            } else if (!scalar(r, t, v)) {
+                return fail("bad metadata value");
+            }
+            kv[key] = v;
+        }
+        std::vector<std::pair<std::string, GgufTensor>> ts;
+        for (uint64_t i = 0; i < nt && r.ok; i++) {
+            GgufTensor t;
+            const std::string name = r.str();
+            t.nd = (int)r.get<uint32_t>();
+            if (t.nd < 1 || t.nd > 4) return fail("bad tensor dims");
+            for (int d = 0; d < t.nd; d++) t.ne[d] = (int64_t)r.get<uint64_t>();
+            t.type = (int)r.get<uint32_t>();
+            t.off = r.get<uint64_t>();
+            ts.emplace_back(name, t);
+        }
+        if (!r.ok) return fail("truncated header");
+        uint64_t align = 32;
+        auto it = kv.find("general.alignment");
+        if (it != kv.end() && it->second.i > 0) align = (uint64_t)it->second.i;
+        const uint64_t pos = (uint64_t)(r.p - map);
+        data_start = (pos + align - 1) / align * align;
+        for (auto& nt_ : ts) {
+            GgufTensor& t = nt_.second;
+            if (!type_supported(t.type)) return fail("unsupported tensor type");
+            if (t.ne[0] % block_elems(t.type)) return fail("row length not a whole number of blocks");
+            t.row_bytes = (size_t)(t.ne[0] / block_elems(t.type)) * block_bytes(t.type);
+            t.bytes = t.row_bytes * (size_t)(t.ne[1] * t.ne[2] * t.ne[3]);
+            t.file_off = data_start + t.off;
+            if (t.file_off + t.bytes > size) return fail("tensor out of file bounds");
+            tensors[nt_.first] = t;
+        }
+        return true;
+    }
+    bool fail(const char* m) {
+        err = m;
+        return false;
+    }
+    const GgufTensor* tensor(const std::string& n) const {
+        auto it = tensors.find(n);
+        return it == tensors.end() ? nullptr : &it->second;
+    }
+    int64_t geti(const std::string& k, int64_t def, bool* missing = nullptr) const {
+        auto it = kv.find(k);
+        if (it == kv.end()) {
+            if (missing) *missing = true;
+            return def;
+        }
+        return it->second.i;
+    }
+    double getf(const std::string& k, double def) const {
+        auto it = kv.find(k);
+        return it == kv.end() ? def : it->second.f;
+    }
+    std::string gets(const std::string& k) const {
+        auto it = kv.find(k);
+        return it == kv.end() ? std::string() : it->second.s;
+    }
+};
+
+float host_f16(uint16_t h) {
+    const uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 31, m = h & 1023;
+    uint32_t b;
+    if (e == 0) {
+        if (m == 0) {
+            b = s;
+        } else {  // subnormal: renormalise
+            int ee = -1;
+            uint32_t mm = m;
+            do {
+                ee++;
+                mm <<= 1;
+            } while (!(mm & 1024));
+            b = s | ((uint32_t)(127 - 15 - ee) << 23) | ((mm & 1023) << 13);
+        }
+    } else if (e == 31) {
+        b = s | 0x7f800000u | (m << 13);
+    } else {
+        b = s | ((e + 127 - 15) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+
+constexpr int MAXB = 64;  // tokens per forward pass (qwen3moe.cpp:39)
+
+}  // namespace
+
+struct EahmmfEngine {
+    int n_layer = 0, D = 0, n_head = 0, n_kv = 0, hd = 0, QD = 0, KD = 0, n_expert = 0, n_used = 0, FF = 0,
+        n_vocab = 0, n_ctx = 0, n_embd_rows = 0;
+    float eps = 1e-6f, rope_base = 1e6f;
+    cudaStream_t st = nullptr;
+    uint8_t* weights = nullptr;  // the GGUF data section, as in the file
+    struct Layer {
+        float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+        const uint8_t* wq[3];  // q, k, v (or the fused q|k|v matrix in wq[0] when fused)
+        int qkv_type[3];
+        size_t qkv_rb[3];
+        bool fused;
+        const uint8_t* wo;
+        int wo_type;
+        size_t wo_rb;
+        EahmmfMoeLayer moe;
+    };
+    std::vector<Layer> layers;
+    const uint8_t* embd = nullptr;
+    int embd_type = 0;
+    size_t embd_rb = 0;
+    const uint8_t* out_w = nullptr;
+    int out_type = 0;
+    size_t out_rb = 0;
+    std::vector<void*> allocs;  // every cudaMalloc of the engine (freed in the destructor)
+    float *out_norm = nullptr, *inv_freq = nullptr, *kc = nullptr, *vc = nullptr;
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *logits = nullptr;
+    float* attn_part = nullptr;
+    float2 *rope_cs = nullptr, *amax_blk = nullptr;
+    int amax_nblk = 0;
+    void *moe_ws = nullptr, *gemv_ws = nullptr;
+    size_t moe_ws_bytes = 0, gemv_ws_bytes = 0;
+    int* toks = nullptr;       // device token staging [MAXB]
+    int* h_toks = nullptr;     // pinned [MAXB]
+    int* status = nullptr;     // device status word
+    DecodeState* state = nullptr;
+    DecodeState* h_state = nullptr;  // pinned mirror for reads
+    int* out = nullptr;
+    int cap_out = 0;
+    cudaGraphExec_t step_graph = nullptr;
+    bool trace = false;
+    std::vector<int> trace_ids;
+    std::vector<float> trace_w;
+    std::vector<int> h_ids;
+    std::vector<float> h_w;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    std::string err;
+
+    ~EahmmfEngine() {
+        if (st) cudaStreamSynchronize(st);
+        if (step_graph) cudaGraphExecDestroy(step_graph);
+        for (void* p : allocs) cudaFree(p);
+        if (h_toks) cudaFreeHost(h_toks);
+        if (h_state) cudaFreeHost(h_state);
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
+        if (st) cudaStreamDestroy(st);
+    }
+    template <typename T>
+    bool dalloc(T*& p, size_t bytes) {
+        void* v = nullptr;
+        if (cudaMalloc(&v, bytes < 256 ? 256 : bytes) != cudaSuccess) return false;
+        allocs.push_back(v);
+        p = static_cast<T*>(v);
+        return true;
+    }
+    bool fail(const std::string& m) {
+        err = m;
+        return false;
+    }
+
+    // F32 copy of a small F32/F16 tensor (norm weights, router), converted on the host.
+    bool f32_tensor(const Gguf& g, const GgufTensor* t, size_t n, float*& dst) {
+        if (!t || (size_t)(t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3]) != n) return false;
+        std::vector<float> h(n);
+        const uint8_t* src = g.map + t->file_off;
+        if (t->type == T_F32) {
+            memcpy(h.data(), src, n * 4);
+        } else if (t->type == T_F16) {
+            for (size_t i = 0; i < n; i++) h[i] = host_f16((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8)));
+        } else {
+            return false;
+        }
+        return dalloc(dst, n * 4) && cudaMemcpy(dst, h.data(), n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    }
+
+    bool load(const char* path, int ctx) {
+        Gguf g;
+        if (!g.open(path)) return fail("gguf: " + g.err);
+        if (g.gets("general.architecture") != "qwen3moe") return fail("unsupported architecture (need qwen3moe)");
+        const std::string a = "qwen3moe.";
+        bool miss = false;
+        n_layer = (int)g.geti(a + "block_count", 0, &miss);
+        D = (int)g.geti(a + "embedding_length", 0, &miss);
+        n_head = (int)g.geti(a + "attention.head_count", 0, &miss);
+        n_kv = (int)g.geti(a + "attention.head_count_kv", 0, &miss);
+        n_expert = (int)g.geti(a + "expert_count", 0, &miss);
+        n_used = (int)g.geti(a + "expert_used_count", 0, &miss);
+        FF = (int)g.geti(a + "expert_feed_forward_length", 0, &miss);
+        if (miss || n_head <= 0 || n_kv <= 0) return fail("missing hyper-parameters");
+        hd = (int)g.geti(a + "attention.key_length", D / n_head);
+        eps = (float)g.getf(a + "attention.layer_norm_rms_epsilon", 1e-6);
+        rope_base = (float)g.getf(a + "rope.freq_base", 1e6);
+        const int n_ctx_train = (int)g.geti(a + "context_length", 4096);
+        QD = n_head * hd;
+        KD = n_kv * hd;
+        n_ctx = std::min(ctx, n_ctx_train);
+        if (n_ctx < 1) return fail("bad context length");
+        if (hd % 2 || n_head % n_kv) return fail("bad head config");
+        if (hd != 64 && hd != 128) return fail("head size must be 64 or 128");
+        if (n_head / n_kv > ATT_MAXH * (ATT_NT / 32)) return fail("GQA group too large");
+        if (D % 256 || FF % 256) return fail("hidden and expert sizes must be multiples of 256");
+
+        if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
+        // the data section, byte for byte
+        const size_t nbytes = g.size - g.data_start;
+        if (!dalloc(weights, nbytes)) return fail("cannot allocate device memory for the weights");
+        if (!upload(g.map + g.data_start, nbytes)) return fail("weight upload failed");
+        auto dptr = [&](const GgufTensor* t) { return weights + (t->file_off - g.data_start); };
+
+        const GgufTensor* te = g.tensor("token_embd.weight");
+        const GgufTensor* to = g.tensor("output.weight");
+        if (!te) return fail("token_embd.weight missing");
+        if (!to) to = te;  // tied embeddings
+        if (te->ne[0] != D || to->ne[0] != D) return fail("embedding width mismatch");
+        embd = dptr(te);
+        embd_type = te->type;
+        embd_rb = te->row_bytes;
+        n_embd_rows = (int)te->ne[1];
+        out_w = dptr(to);
+        out_type = to->type;
+        out_rb = to->row_bytes;
+        n_vocab = (int)to->ne[1];
+        if (!f32_tensor(g, g.tensor("output_norm.weight"), D, out_norm)) return fail("output_norm.weight");
+        std::vector<float> invf(hd / 2);
+        for (int i = 0; i < hd / 2; i++) invf[i] = (float)pow((double)rope_base, -2.0 * i / hd);
+        if (!dalloc(inv_freq, invf.size() * 4) ||
+            cudaMemcpy(inv_freq, invf.data(), invf.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail("inv_freq");
+
+        layers.resize(n_layer);
+        for (int l = 0; l < n_layer; l++) {
+            Layer& L = layers[l];
+            auto T = [&](const char* s) { return g.tensor("blk." + std::to_string(l) + "." + s); };
+            if (!f32_tensor(g, T("attn_norm.weight"), D, L.attn_norm) ||
+                !f32_tensor(g, T("ffn_norm.weight"), D, L.ffn_norm) ||
+                !f32_tensor(g, T("attn_q_norm.weight"), hd, L.q_norm) ||
+                !f32_tensor(g, T("attn_k_norm.weight"), hd, L.k_norm))
+                return fail("norm weights of layer " + std::to_string(l));
+            const GgufTensor* tq[3] = {T("attn_q.weight"), T("attn_k.weight"), T("attn_v.weight")};
+            const int rows[3] = {QD, KD, KD};
+            for (int c = 0; c < 3; c++)
+                if (!tq[c] || tq[c]->ne[0] != D || tq[c]->ne[1] != rows[c]) return fail("attention projection shape");
+            L.fused = tq[1]->type == tq[0]->type && tq[2]->type == tq[0]->type;
+            if (L.fused) {  // one matrix of QD + 2 KD rows: one activation prep and one GEMV per layer
+                uint8_t* f = nullptr;
+                const size_t rb = tq[0]->row_bytes;
+                if (!dalloc(f, rb * (size_t)(QD + 2 * KD))) return fail("fused qkv allocation");
+                size_t o = 0;
+                for (int c = 0; c < 3; c++) {
+                    if (cudaMemcpy(f + o, dptr(tq[c]), tq[c]->bytes, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                        return fail("fused qkv copy");
+                    o += tq[c]->bytes;
+                }
+                L.wq[0] = f;
+                L.qkv_type[0] = tq[0]->type;
+                L.qkv_rb[0] = rb;
+            } else {
+                for (int c = 0; c < 3; c++) {
+                    L.wq[c] = dptr(tq[c]);
+                    L.qkv_type[c] = tq[c]->type;
+                    L.qkv_rb[c] = tq[c]->row_bytes;
+                }
+            }
+            const GgufTensor* wo = T("attn_output.weight");
+            if (!wo || wo->ne[0] != QD || wo->ne[1] != D) return fail("attn_output shape");
+            L.wo = dptr(wo);
+            L.wo_type = wo->type;
+            L.wo_rb = wo->row_bytes;
+            float* router = nullptr;
+            if (!f32_tensor(g, T("ffn_gate_inp.weight"), (size_t)n_expert * D, router)) return fail("router");
+            const GgufTensor* ex[3] = {T("ffn_gate_exps.weight"), T("ffn_up_exps.weight"), T("ffn_down_exps.weight")};
+            for (int c = 0; c < 3; c++)
+                if (!ex[c]) return fail("expert tensors missing");
+            if (ex[0]->ne[0] != D || ex[0]->ne[1] != FF || ex[0]->ne[2] != n_expert || ex[1]->ne[0] != D ||
+                ex[1]->ne[1] != FF || ex[1]->ne[2] != n_expert || ex[2]->ne[0] != FF || ex[2]->ne[1] != D ||
+                ex[2]->ne[2] != n_expert)
+                return fail("unexpected expert tensor shape");
+            // per-expert component pointers (ExpertViews.gate/up/down, eahmmf.h:737-742)
+            std::vector<const uint8_t*> ptr(3 * (size_t)n_expert);
+            for (int c = 0; c < 3; c++) {
+                const size_t per = ex[c]->row_bytes * (size_t)ex[c]->ne[1];
+                for (int e = 0; e < n_expert; e++) ptr[(size_t)c * n_expert + e] = dptr(ex[c]) + per * e;
+            }
+            const uint8_t** dp = nullptr;
+            if (!dalloc(dp, ptr.size() * sizeof(void*)) ||
+                cudaMemcpy(dp, ptr.data(), ptr.size() * sizeof(void*), cudaMemcpyHostToDevice) != cudaSuccess)
+                return fail("expert tables");
+            EahmmfMoeLayer& M = L.moe;
+            M.n_expert = n_expert;
+            M.n_used = n_used;
+            M.D = D;
+            M.FF = FF;
+            M.gate_type = ex[0]->type;
+            M.up_type = ex[1]->type;
+            M.down_type = ex[2]->type;
+            M.gate_row_bytes = ex[0]->row_bytes;
+            M.up_row_bytes = ex[1]->row_bytes;
+            M.down_row_bytes = ex[2]->row_bytes;
+            M.d_gate = dp;
+            M.d_up = dp + n_expert;
+            M.d_down = dp + 2 * n_expert;
+            M.d_router = router;
+        }
+        moe_ws_bytes = eahmmf_cuda_moe_workspace_bytes(&layers[0].moe, MAXB);
+        if (!moe_ws_bytes) return fail("expert layer not supported by the MoE kernels");
+        gemv_ws_bytes = eahmmf_cuda_gemv_workspace_bytes(std::max(D, QD));
+        const size_t kvn = (size_t)n_layer * n_ctx * KD;
+        amax_nblk = 148;
+        const int nsplit_max = std::max(1, (n_ctx + ATT_CH - 1) / ATT_CH);
+        if (!dalloc(kc, kvn * 4) || !dalloc(vc, kvn * 4) || !dalloc(x, (size_t)MAXB * D * 4) ||
+            !dalloc(xn, (size_t)MAXB * D * 4) || !dalloc(qkv, (size_t)MAXB * (QD + 2 * KD) * 4) ||
+            !dalloc(q, (size_t)MAXB * QD * 4) || !dalloc(att, (size_t)MAXB * QD * 4) ||
+            !dalloc(logits, (size_t)n_vocab * 4) || !dalloc(rope_cs, (size_t)MAXB * (hd / 2) * 8) ||
+            !dalloc(attn_part, (size_t)MAXB * n_head * std::min(nsplit_max, 128) * (hd + 2) * 4) ||
+            !dalloc(amax_blk, (size_t)amax_nblk * 8) || !dalloc(moe_ws, moe_ws_bytes) ||
+            !dalloc(gemv_ws, gemv_ws_bytes) || !dalloc(toks, MAXB * 4) || !dalloc(status, 4) ||
+            !dalloc(state, sizeof(DecodeState)))
+            return fail("cannot allocate activations / KV cache");
+        if (cudaMemset(kc, 0, kvn * 4) != cudaSuccess || cudaMemset(vc, 0, kvn * 4) != cudaSuccess ||
+            cudaMemset(status, 0, 4) != cudaSuccess)
+            return fail("memset");
+        if (cudaHostAlloc((void**)&h_toks, MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc((void**)&h_state, sizeof(DecodeState), cudaHostAllocDefault) != cudaSuccess)
+            return fail("pinned buffers");
+        if (cudaEventCreate(&ev0) != cudaSuccess || cudaEventCreate(&ev1) != cudaSuccess) return fail("events");
+        if (!set_state(0, 0)) return fail("state");
+        return cudaDeviceSynchronize() == cudaSuccess || fail("device error after load");
+    }
+
+    // host -> device through two pinned staging halves (the mapping is pageable)
+    bool upload(const uint8_t* src, size_t n) {
+        const size_t half = 64u << 20;
+        uint8_t* stage[2] = {nullptr, nullptr};
+        cudaEvent_t ev[2] = {nullptr, nullptr};
+        bool ok = true;
+        for (int i = 0; i < 2 && ok; i++)
+            ok = cudaHostAlloc((void**)&stage[i], half, cudaHostAllocDefault) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) == cudaSuccess;
+        bool live[2] = {false, false};
+        for (size_t o = 0, k = 0; ok && o < n; o += half, k ^= 1) {
+            const size_t c = std::min(half, n - o);
+            if (live[k]) ok = cudaEventSynchronize(ev[k]) == cudaSuccess;
+            if (!ok) break;
+            memcpy(stage[k], src + o, c);
+            ok = cudaMemcpyAsync(weights + o, stage[k], c, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+                 cudaEventRecord(ev[k], st) == cudaSuccess;
+            live[k] = true;
+        }
+        if (cudaStreamSynchronize(st) != cudaSuccess) ok = false;
+        for (int i = 0; i < 2; i++) {
+            if (stage[i]) cudaFreeHost(stage[i]);
+            if (ev[i]) cudaEventDestroy(ev[i]);
+        }
+        return ok;
+    }
+
+    bool set_state(int pos, int n_out_cap) {
+        DecodeState s{};
+        s.pos = pos;
+        s.token = 0;
+        s.ticket = 0;
+        s.n_out = 0;
+        s.cap_out = n_out_cap;
+        s.out = out;
+        *h_state = s;
+        return cudaMemcpyAsync(state, h_state, sizeof(DecodeState), cudaMemcpyHostToDevice, st) == cudaSuccess;
+    }
+    bool ensure_out(int n) {
+        if (n <= cap_out) return true;
+        int* p = nullptr;
+        if (!dalloc(p, (size_t)n * 4)) return false;
+        out = p;  // the old buffer stays in `allocs` until the engine is freed; the captured step reads the
+        cap_out = n;  // history pointer from the device state, so it needs no re-capture
+        return true;
+    }
+    int nsplit_for(int nb) const {
+        const int nch = std::max(1, (n_ctx + ATT_CH - 1) / ATT_CH);
+        return std::max(1, std::min({nch, 128, 2 * 148 / std::max(1, n_kv * nb)}));
+    }
+
+    // One forward pass of nb tokens at the device position state->pos (which it does not change).
+    // tok: device pointer to nb token ids. want_logits: logits of the last token into `logits`.
+    int forward(const int* tok, int nb, bool want_logits) {
+        const int nsplit = nsplit_for(nb);
+        const float scale = 1.0f / sqrtf((float)hd);
+        if (launch_rope_table(state, inv_freq, hd / 2, nb, rope_cs, st) != cudaSuccess) return ST_CUDA;
+        if (launch_embed(embd, embd_type, embd_rb, D, n_embd_rows, tok, nb, x, status, st) != cudaSuccess)
+            return ST_CUDA;
+        const int ldq = QD + 2 * KD;
+        for (int l = 0; l < n_layer; l++) {
+            const Layer& L = layers[l];
+            float* lk = kc + (size_t)l * n_ctx * KD;
+            float* lv = vc + (size_t)l * n_ctx * KD;
+            if (launch_rmsnorm(x, D, L.attn_norm, xn, D, nb, D, eps, st) != cudaSuccess) return ST_CUDA;
+            int rc;
+            if (L.fused) {
+                rc = eahmmf_cuda_gemv(L.wq[0], L.qkv_type[0], D, ldq, L.qkv_rb[0], xn, nb, D, qkv, ldq, 0, gemv_ws,
+                                      gemv_ws_bytes, st);
+            } else {
+                const int rows[3] = {QD, KD, KD}, col[3] = {0, QD, QD + KD};
+                rc = ST_OK;
+                for (int c = 0; c < 3 && rc == ST_OK; c++)
+                    rc = eahmmf_cuda_gemv(L.wq[c], L.qkv_type[c], D, rows[c], L.qkv_rb[c], xn, nb, D, qkv + col[c],
+                                          ldq, 0, gemv_ws, gemv_ws_bytes, st);
+            }
+            if (rc != ST_OK) return rc;
+            if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, state, nb, q, lk, lv,
+                                  st) != cudaSuccess)
+                return ST_CUDA;
+            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, att, st) !=
+                cudaSuccess)
+                return ST_CUDA;
+            rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes, st);
+            if (rc != ST_OK) return rc;
+            if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess) return ST_CUDA;
+            rc = eahmmf_cuda_moe_layer(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status);
+            if (rc != ST_OK) return rc;
+            if (trace) {  // routing of this layer (ids, then weights, at the head of the MoE workspace)
+                const size_t nk = (size_t)nb * n_used;
+                h_ids.resize(nk);
+                h_w.resize(nk);
+                const size_t woff = (nk * 4 + 255) & ~(size_t)255;
+                if (cudaMemcpyAsync(h_ids.data(), moe_ws, nk * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                    cudaMemcpyAsync(h_w.data(), static_cast<uint8_t*>(moe_ws) + woff, nk * 4, cudaMemcpyDeviceToHost,
+                                    st) != cudaSuccess ||
+                    cudaStreamSynchronize(st) != cudaSuccess)
+                    return ST_CUDA;
+                trace_ids.insert(trace_ids.end(), h_ids.begin(), h_ids.end());
+                trace_w.insert(trace_w.end(), h_w.begin(), h_w.end());
+            }
+        }
+        if (want_logits) {
+            if (launch_rmsnorm(x + (size_t)(nb - 1) * D, D, out_norm, xn, D, 1, D, eps, st) != cudaSuccess)
+                return ST_CUDA;
+            const int rc = eahmmf_cuda_gemv(out_w, out_type, D, n_vocab, out_rb, xn, 1, D, logits, n_vocab, 0, gemv_ws,
+                                            gemv_ws_bytes, st);
+            if (rc != ST_OK) return rc;
+        }
+        return ST_OK;
+    }
+
+    // Prompt tokens through forward passes of up to n_batch tokens from position p0 (Engine::eval,
+    // qwen3moe.cpp:1078-1084); leaves state->pos = p0 + n and the last token's logits in `logits`.
+    int eval_dev(const int* htoks, int n, int p0, int n_batch) {
+        if (!set_state(p0, cap_out) || cudaMemsetAsync(status, 0, 4, st) != cudaSuccess) return ST_CUDA;
+        for (int i = 0; i < n; i += n_batch) {
+            const int nb = std::min(n_batch, n - i);
+            // the pinned staging is reused per chunk: wait for the previous chunk's copy to be consumed
+            if (cudaStreamSynchronize(st) != cudaSuccess) return ST_CUDA;
+            memcpy(h_toks, htoks + i, (size_t)nb * 4);
+            if (cudaMemcpyAsync(toks, h_toks, (size_t)nb * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+                return ST_CUDA;
+            const int rc = forward(toks, nb, i + nb == n);
+            if (rc != ST_OK) return rc;
+            if (launch_advance(state, nb, st) != cudaSuccess) return ST_CUDA;
+        }
+        return ST_OK;
+    }
+
+    // One decode step: forward of state->token at state->pos, then the argmax records the next token
+    // and advances the position. Captured once, replayed per token.
+    int step(bool use_graph) {
+        if (!use_graph || trace) {
+            const int rc = forward(&state->token, 1, true);
+            if (rc != ST_OK) return rc;
+            return launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, 1, st) == cudaSuccess ? ST_OK : ST_CUDA;
+        }
+        if (!step_graph) {
+            cudaGraph_t gr = nullptr;
+            if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return ST_CUDA;
+            int rc = forward(&state->token, 1, true);
+            if (rc == ST_OK && launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, 1, st) != cudaSuccess)
+                rc = ST_CUDA;
+            const cudaError_t ce = cudaStreamEndCapture(st, &gr);
+            if (rc != ST_OK || ce != cudaSuccess) {
+                if (gr) cudaGraphDestroy(gr);
+                return rc != ST_OK ? rc : ST_CUDA;
+            }
+            const cudaError_t ie = cudaGraphInstantiate(&step_graph, gr, 0);
+            cudaGraphDestroy(gr);
+            if (ie != cudaSuccess) {
+                step_graph = nullptr;
+                return ST_CUDA;
+            }
+        }
+        return cudaGraphLaunch(step_graph, st) == cudaSuccess ? ST_OK : ST_CUDA;
+    }
+
+    int read_status() {
+        int s = 0;
+        if (cudaMemcpyAsync(h_toks, status, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return ST_CUDA;
+        s = h_toks[0];
+        return s;
+    }
+};
+
+// ---------------------------------------------------------------------------------------------------
+// 4. engine entry points
+// ---------------------------------------------------------------------------------------------------
+extern "C" EahmmfEngine* eahmmf_engine_load(const char* gguf_path, int n_ctx, char* err, size_t err_cap) {
+    EahmmfEngine* e = new EahmmfEngine();
+    if (!gguf_path || !e->load(gguf_path, n_ctx)) {
+        if (err && err_cap) snprintf(err, err_cap, "%s", gguf_path ? e->err.c_str() : "null path");
+        delete e;
+        return nullptr;
+    }
+    return e;
+}
+
+extern "C" void eahmmf_engine_free(EahmmfEngine* e) { delete e; }
+
+extern "C" int eahmmf_engine_dims(EahmmfEngine* e, int* dims) {
+    if (!e || !dims) return ST_BAD_ARG;
+    const int v[11] = {e->n_layer, e->D,  e->n_head,  e->n_kv,  e->hd, e->n_expert,
+                       e->n_used,  e->FF, e->n_vocab, e->n_ctx, e->n_embd_rows};
+    memcpy(dims, v, sizeof v);
+    return ST_OK;
+}
+
+extern "C" int eahmmf_engine_eval(EahmmfEngine* e, const int* toks, int n, int p0, int n_batch, float* logits) {
+    if (!e || !toks || n < 1 || n_batch < 1 || n_batch > MAXB || p0 < 0 || p0 + n > e->n_ctx) return ST_BAD_ARG;
+    int rc = e->eval_dev(toks, n, p0, n_batch);
+    if (rc != ST_OK) return rc;
+    if (logits && cudaMemcpyAsync(logits, e->logits, (size_t)e->n_vocab * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+        return ST_CUDA;
+    rc = e->read_status();
+    return rc;
+}
+
+extern "C" int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out,
+                                    float* first_logits) {
+    if (!e || !prompt || !out || n_prompt < 1 || n_gen < 1 || n_batch < 1 || n_batch > MAXB ||
+        n_prompt + n_gen > e->n_ctx)
+        return ST_BAD_ARG;
+    if (!e->ensure_out(n_gen)) return ST_CUDA;
+    int rc = e->eval_dev(prompt, n_prompt, 0, n_batch);
+    if (rc != ST_OK) return rc;
+    // state: pos = n_prompt; cap_out was set by eval_dev's set_state
+    if (first_logits &&
+        cudaMemcpyAsync(first_logits, e->logits, (size_t)e->n_vocab * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+        return ST_CUDA;
+    if (launch_argmax(e->logits, e->n_vocab, e->amax_blk, e->amax_nblk, e->state, 0, e->st) != cudaSuccess) return ST_CUDA;
+    for (int i = 1; i < n_gen; i++) {
+        rc = e->step(true);
+        if (rc != ST_OK) return rc;
+    }
+    if (cudaMemcpyAsync(out, e->out, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) return ST_CUDA;
+    return e->read_status();
+}
+
+extern "C" int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_ms) {
+    if (!e || n_steps < 1) return ST_BAD_ARG;
+    if (cudaMemcpyAsync(e->h_state, e->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, e->st) != cudaSuccess ||
+        cudaStreamSynchronize(e->st) != cudaSuccess)
+        return ST_CUDA;
+    if (e->h_state->pos + n_steps > e->n_ctx) return ST_BAD_ARG;
+    const int have = e->h_state->n_out;
+    if (have + n_steps > e->cap_out) {
+        // grow the history and re-point the state at it (copying what was recorded)
+        int* old = e->out;
+        const int cap_old = e->cap_out;
+        if (!e->ensure_out(have + n_steps)) return ST_CUDA;
+        if (old && cap_old && cudaMemcpyAsync(e->out, old, (size_t)std::min(have, cap_old) * 4,
+                                              cudaMemcpyDeviceToDevice, e->st) != cudaSuccess)
+            return ST_CUDA;
+        DecodeState s = *e->h_state;
+        s.out = e->out;
+        s.cap_out = e->cap_out;
+        *e->h_state = s;
+        if (cudaMemcpyAsync(e->state, e->h_state, sizeof(DecodeState), cudaMemcpyHostToDevice, e->st) != cudaSuccess)
+            return ST_CUDA;
+    }
+    if (cudaEventRecord(e->ev0, e->st) != cudaSuccess) return ST_CUDA;
+    for (int i = 0; i < n_steps; i++) {
+        const int rc = e->step(true);
+        if (rc != ST_OK) return rc;
+    }
+    if (cudaEventRecord(e->ev1, e->st) != cudaSuccess || cudaEventSynchronize(e->ev1) != cudaSuccess) return ST_CUDA;
+    if (device_ms) cudaEventElapsedTime(device_ms, e->ev0, e->ev1);
+    if (out && cudaMemcpyAsync(out, e->out + have, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+        return ST_CUDA;
+    return e->read_status();
+}
+
+extern "C" void eahmmf_engine_trace(EahmmfEngine* e, int enable) {
+    if (!e) return;
+    e->trace = enable != 0;
+    e->trace_ids.clear();
+    e->trace_w.clear();
+}
+
+extern "C" int eahmmf_engine_trace_get(EahmmfEngine* e, int* ids, float* w, int cap) {
+    if (!e) return 0;
+    const int n = (int)std::min<size_t>((size_t)(cap > 0 ? cap : 0), e->trace_ids.size());
+    if (ids) memcpy(ids, e->trace_ids.data(), sizeof(int) * n);
+    if (w) memcpy(w, e->trace_w.data(), sizeof(float) * n);
+    return (int)e->trace_ids.size();
+}

@@ -13,6 +13,7 @@ constexpr int XPASS = 4;            // tokens per pass of the tensor-core GEMV
 constexpr int MOE_TMAX = 64;        // tokens per MoE block call (the engine's MAXB, qwen3moe.cpp:39)
 constexpr int MU = 2;               // slots per MoE work group (one MMA column set)
 constexpr int ROUTE_NT = 512;       // threads of the routing / prep kernel
+constexpr int COMB_NT = 256;        // threads of a combine block
 constexpr int MAX_EXPERTS = 512;
 
 // A quantized matrix: rows of row_bytes bytes, ne0 = K elements per row.
@@ -59,7 +60,6 @@ struct RouteWs {
     int* token_slots;  // [T*K] slots of token t, ascending (= expert-ascending)
     int* ngroups;      // [1] number of work groups
     GroupRec* groups;  // [T*K] work groups, expert ascending
-    int* tok_done;     // [T * D/64] expert outputs stored per token and 64-row group of the output
 };
 
 struct MoeArgs {
@@ -103,8 +103,8 @@ XF xf_carve(void* base, int rows, int K);        // XF views over such a block
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st);
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st);
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st);  // per-row kernel (any type)
-// MoE block (moe.cu): routing + grouping + activation prep, then gate/up, then down + combine; the
-// last two are launched with programmatic stream serialization.
+// MoE block (moe.cu): routing + grouping + activation prep, then gate/up, then down, then the combine;
+// the last three are launched with programmatic stream serialization.
 cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st);

@@ -18,10 +18,10 @@
 //                     alignment, instead of sixteen row copies.
 //   k_moe_down<D>     persistent likewise over units (group, 64 rows of D) with 12 consumer warps. The
 //                     consumers put each group's h rows in fragment form in shared memory themselves
-//                     (the first group's while the first weight tiles are in flight). Per token and 64-row
-//                     group of D a counter collects the K expert outputs; the warp that stores the K-th
-//                     adds them, weighted, in ascending expert order (qwen3moe.cpp:1025-1069) to the
-//                     residual, so the combine is spread over all units instead of waiting for the last.
+//                     (the first group's while the first weight tiles are in flight). Each unit's reducer
+//                     only stores its y rows: no counters or dependent loads in the pipelined loop.
+//   k_moe_combine     adds each token's K expert outputs, weighted, in ascending expert order
+//                     (qwen3moe.cpp:1025-1069) to the residual once the down grid has completed.
 //
 // Every mbarrier wait is bounded; a timeout flags ST_WAIT_TIMEOUT, stops the producer, drains the copies
 // already in flight (bounded) and ends the CTA.
@@ -432,7 +432,6 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         cnt[i] = 0;
         mask[i] = 0ull;
     }
-    for (int i = tid; i < T * (a.D / DN_ROWS); i += blockDim.x) a.rw.tok_done[i] = 0;
     __syncthreads();
 
     // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022)
@@ -686,7 +685,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
 template <int QD>
 __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS, K = a.n_used;
+    const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t rb = a.down_rb;
     const Plan pl = down_plan(FF, rb);
@@ -827,40 +826,38 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        if (reducer) {  // after releasing the stage: count the unit's tokens; the K-th output of a token combines
-            __threadfence();
-            __syncwarp();
-            for (int tk = 0; tk < mc; tk++) {
-                const int tok = __ldcg(a.rw.slot_token + s0 + tk);
-                int done = 0;
-                if (lane == 0) done = atomicAdd(&a.rw.tok_done[tok * NRG + rg], 1);
-                done = __shfl_sync(0xffffffffu, done, 0);
-                if (done == K - 1) {  // all K expert outputs of this token's 64 rows are stored
-                    __threadfence();
-                    int sl = 0;
-                    float wk = 0.f;
-                    if (lane < K) {
-                        sl = __ldcg(a.rw.token_slots + tok * K + lane);
-                        wk = __ldcg(a.rw.slot_w + sl);
-                    }
-                    const size_t col = (size_t)DN_ROWS * rg + 2 * lane;
-                    float2 accv = make_float2(0.f, 0.f);
-                    for (int k = 0; k < K; k++) {  // ascending slots = ascending experts (qwen3moe.cpp:1025)
-                        const int sk = __shfl_sync(0xffffffffu, sl, k);
-                        const float w = __shfl_sync(0xffffffffu, wk, k);
-                        const float2 v = __ldcg(reinterpret_cast<const float2*>(a.y + (size_t)sk * D + col));
-                        accv.x = fmaf(w, v.x, accv.x);
-                        accv.y = fmaf(w, v.y, accv.y);
-                    }
-                    float2* xp = reinterpret_cast<float2*>(a.x + (size_t)tok * D + col);
-                    float2 xv = *xp;
-                    xv.x += accv.x;
-                    xv.y += accv.y;
-                    *xp = xv;
-                }
-            }
-        }
     }
+}
+
+// ------------------------------------------------------------------------------------------------
+// weighted combine + residual add: x[t] += sum_k w_k y[slot_k] over token t's slots in ascending slot
+// (= expert) order (qwen3moe.cpp:1024, :1062-1069). Grid (D / (2 * COMB_NT), T); each thread owns two
+// consecutive elements of one token row.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(COMB_NT) k_moe_combine(MoeArgs a) {
+    __shared__ int s_sl[32];
+    __shared__ float s_w[32];
+    const int t = blockIdx.y, K = a.n_used, D = a.D;
+    pdl_wait();  // y and the routing come from the previous grids
+    if (threadIdx.x < K) {
+        const int sl = a.rw.token_slots[t * K + threadIdx.x];
+        s_sl[threadIdx.x] = sl;
+        s_w[threadIdx.x] = a.rw.slot_w[sl];
+    }
+    __syncthreads();
+    const int c = 2 * (blockIdx.x * COMB_NT + threadIdx.x);
+    if (c >= D) return;
+    float2 acc = make_float2(0.f, 0.f);
+    for (int k = 0; k < K; k++) {
+        const float2 v = *reinterpret_cast<const float2*>(a.y + (size_t)s_sl[k] * D + c);
+        acc.x = fmaf(s_w[k], v.x, acc.x);
+        acc.y = fmaf(s_w[k], v.y, acc.y);
+    }
+    float2* xp = reinterpret_cast<float2*>(a.x + (size_t)t * D + c);
+    float2 xv = *xp;
+    xv.x += acc.x;
+    xv.y += acc.y;
+    *xp = xv;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -881,9 +878,9 @@ void smem_attr(Kern k, size_t smem) {
 // Launch with programmatic stream serialization: the kernel may start before its predecessor on the
 // stream has finished and calls griddepcontrol.wait before reading the predecessor's results.
 template <typename Kern, typename... Args>
-cudaError_t launch_pdl(Kern k, int grid, int block, size_t smem, cudaStream_t st, const Args&... args) {
+cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t st, const Args&... args) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -915,7 +912,7 @@ static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
     if (pl.total > SMEM_CAP || (a.FF >> 4) < pl.S) return cudaErrorInvalidValue;
     smem_attr(k_moe_gateup<QG, QU>, pl.total);
     const int units = max_groups(a) * (a.FF >> 4);
-    return launch_pdl(k_moe_gateup<QG, QU>, std::min(sm_count(), units), (NWC_GU + 1) * 32, pl.total, st, a);
+    return launch_pdl(k_moe_gateup<QG, QU>, dim3(std::min(sm_count(), units)), (NWC_GU + 1) * 32, pl.total, st, a);
 }
 template <int QG>
 static cudaError_t gateup_g(const MoeArgs& a, cudaStream_t st) {
@@ -942,16 +939,20 @@ static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
     if (pl.total > SMEM_CAP || a.D / DN_ROWS < pl.S) return cudaErrorInvalidValue;
     smem_attr(k_moe_down<QD>, pl.total);
     const int units = max_groups(a) * (a.D / DN_ROWS);
-    return launch_pdl(k_moe_down<QD>, std::min(sm_count(), units), (NWC_DN + 1) * 32, pl.total, st, a);
+    return launch_pdl(k_moe_down<QD>, dim3(std::min(sm_count(), units)), (NWC_DN + 1) * 32, pl.total, st, a);
 }
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {
     if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX) return cudaErrorInvalidValue;
+    cudaError_t e;
     switch (a.down_type) {
-        case T_Q4_K: return down_as<T_Q4_K>(a, st);
-        case T_Q5_K: return down_as<T_Q5_K>(a, st);
-        case T_Q6_K: return down_as<T_Q6_K>(a, st);
+        case T_Q4_K: e = down_as<T_Q4_K>(a, st); break;
+        case T_Q5_K: e = down_as<T_Q5_K>(a, st); break;
+        case T_Q6_K: e = down_as<T_Q6_K>(a, st); break;
         default: return cudaErrorInvalidValue;
     }
+    if (e != cudaSuccess) return e;
+    const int bx = (a.D / 2 + COMB_NT - 1) / COMB_NT;
+    return launch_pdl(k_moe_combine, dim3(bx, a.T), COMB_NT, 0, st, a);
 }
 
 }  // namespace eb

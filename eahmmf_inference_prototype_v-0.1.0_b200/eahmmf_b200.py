@@ -54,6 +54,14 @@ EXPORTS = {
     "eahmmf_dev_free_memory": (C.c_size_t, [C.c_void_p]),
     "eahmmf_dev_stream": (C.c_void_p, [C.c_void_p]),
     "eahmmf_dev_inject_fault": (None, [C.c_void_p, C.c_int, C.c_int]),
+    "eahmmf_engine_load": (C.c_void_p, [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]),
+    "eahmmf_engine_free": (None, [C.c_void_p]),
+    "eahmmf_engine_dims": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "eahmmf_engine_eval": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "eahmmf_engine_greedy": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "eahmmf_engine_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "eahmmf_engine_trace": (None, [C.c_void_p, C.c_int]),
+    "eahmmf_engine_trace_get": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
     "eahmmf_b200_version": (C.c_char_p, []),
     "eahmmf_b200_sm_count": (C.c_int, []),
 }
@@ -196,4 +204,64 @@ class MoeLayer:
         ids = d_ws[: n * 4].view(dtype=__import__("torch").int32).cpu().numpy().reshape(T, self.K)
         off = ((n * 4 + 255) // 256) * 256
         w = d_ws[off: off + n * 4].view(dtype=__import__("torch").float32).cpu().numpy().reshape(T, self.K)
+        return ids, w
+
+
+class Engine:
+    """The device-resident qwen3moe engine (eahmmf_engine_*): a GGUF model in HBM, with the reference
+    harness's calls (load, dims, eval, greedy, routing trace). Raises on load failure; calls return the
+    EAHMMF_ST_* status of the C ABI."""
+
+    DIM_NAMES = ("n_layer", "D", "n_head", "n_kv", "hd", "n_expert", "n_used", "FF", "n_vocab", "n_ctx", "n_embd")
+
+    def __init__(self, path: str, n_ctx: int):
+        L = lib()
+        err = C.create_string_buffer(256)
+        h = L.eahmmf_engine_load(path.encode(), n_ctx, err, 256)
+        if not h:
+            raise RuntimeError(f"eahmmf_engine_load: {err.value.decode()}")
+        self._h = h
+        d = np.zeros(11, np.int32)
+        L.eahmmf_engine_dims(h, d.ctypes.data)
+        self.dims = dict(zip(self.DIM_NAMES, (int(v) for v in d)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().eahmmf_engine_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def eval(self, toks, p0: int = 0, n_batch: int = 32, want_logits: bool = True):
+        t = np.ascontiguousarray(toks, np.int32)
+        lg = np.zeros(self.dims["n_vocab"], np.float32) if want_logits else None
+        rc = lib().eahmmf_engine_eval(self._h, t.ctypes.data, len(t), p0, n_batch,
+                                      lg.ctypes.data if lg is not None else None)
+        return rc, lg
+
+    def greedy(self, prompt, n_gen: int, n_batch: int = 32, want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_gen, np.int32)
+        lg = np.zeros(self.dims["n_vocab"], np.float32) if want_logits else None
+        rc = lib().eahmmf_engine_greedy(self._h, p.ctypes.data, len(p), n_gen, n_batch, out.ctypes.data,
+                                        lg.ctypes.data if lg is not None else None)
+        return rc, out, lg
+
+    def decode(self, n_steps: int):
+        """Continue greedy generation by n_steps tokens; returns (rc, tokens, device milliseconds)."""
+        out = np.zeros(n_steps, np.int32)
+        ms = C.c_float(0.0)
+        rc = lib().eahmmf_engine_decode(self._h, n_steps, out.ctypes.data, C.byref(ms))
+        return rc, out, float(ms.value)
+
+    def trace(self, enable: bool) -> None:
+        lib().eahmmf_engine_trace(self._h, 1 if enable else 0)
+
+    def trace_get(self):
+        L = lib()
+        n = L.eahmmf_engine_trace_get(self._h, None, None, 0)
+        ids = np.zeros(n, np.int32)
+        w = np.zeros(n, np.float32)
+        L.eahmmf_engine_trace_get(self._h, ids.ctypes.data, w.ctypes.data, n)
         return ids, w

@@ -139,6 +139,40 @@ void* eahmmf_dev_stream(EahmmfDev* d); /* the side stream (cudaStream_t) */
  * (kind 0 alloc, 1 h2d, 2 d2h). */
 void eahmmf_dev_inject_fault(EahmmfDev* d, int kind, int n);
 
+/* ---- 4. device-resident engine (qwen3moe forward pass) ----------------------------------------- */
+
+/* A whole qwen3moe GGUF model in HBM: Engine::load / forward / eval (qwen3moe.cpp:858-1084) with every
+ * step on the GPU: embedding, RMSNorm, fused q|k|v GEMV, QK-norm + NeoX RoPE, KV cache (fp32, n_ctx
+ * positions), causal GQA attention, o-projection, the MoE block of group 2, output GEMV, argmax. One
+ * decode step is a captured CUDA graph; the next token and position stay on the device. Token ids and
+ * logits cross the host boundary only at the calls below. Single-threaded use per engine. */
+typedef struct EahmmfEngine EahmmfEngine;
+
+/* Loads the GGUF (qwen3moe architecture, head size 64 or 128, D and FF multiples of 256, expert
+ * types Q4_K/Q5_K/Q6_K) into device memory; n_ctx is capped by the model's context_length as in
+ * Engine::load (qwen3moe.cpp:879). NULL on failure, with a message in err (if given). */
+EahmmfEngine* eahmmf_engine_load(const char* gguf_path, int n_ctx, char* err, size_t err_cap);
+void eahmmf_engine_free(EahmmfEngine* e);
+/* dims[0..10] = n_layer, D, n_head, n_kv, hd, n_expert, n_used, FF, n_vocab, n_ctx, embedding rows */
+int eahmmf_engine_dims(EahmmfEngine* e, int* dims);
+/* Engine::eval (qwen3moe.cpp:1078-1084): n tokens from position p0 in forward passes of n_batch
+ * (<= 64) tokens; logits (n_vocab floats, host, optional) of the last token. */
+int eahmmf_engine_eval(EahmmfEngine* e, const int* toks, int n, int p0, int n_batch, float* logits);
+/* Greedy generation (temperature 0, repeat penalty 1.0; std::max_element's first maximum,
+ * qwen3moe.cpp:1103): the prompt from position 0, then n_gen tokens, out[0] being the argmax of the
+ * prompt's logits. first_logits (optional) receives those logits. */
+int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out,
+                         float* first_logits);
+/* Continues generation for n_steps tokens from the engine's current state (after eval or greedy):
+ * each step feeds the last argmax token. device_ms (optional) = device time of the steps (CUDA events
+ * on the engine's stream); out (optional) receives the tokens. */
+int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_ms);
+/* Routing trace (Engine::trace_routing, qwen3moe.cpp:1021): when enabled, every forward pass appends
+ * each layer's top-k ids and weights, layer-major; trace_get copies up to cap entries and returns the
+ * total. Tracing runs decode steps without the graph. */
+void eahmmf_engine_trace(EahmmfEngine* e, int enable);
+int eahmmf_engine_trace_get(EahmmfEngine* e, int* ids, float* w, int cap);
+
 /* ---- misc ------------------------------------------------------------------------------------ */
 const char* eahmmf_b200_version(void);
 int eahmmf_b200_sm_count(void);
