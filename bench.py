@@ -1,31 +1,35 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 expert hot path (one JSON line on stdout, rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|layer]
     torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1: one replica per GPU)
 
-Workload (the configuration the headline metric is quoted on): one Qwen3-30B-A3B-shape
-MoE layer -- hidden 2048, 128 experts top-8, intermediate 768, Q4_K gate/up and Q6_K down, router
-logits ~N(0,1), activations ~N(0,1), all seeded -- run on decode batches of T = 1..8 tokens. One step
-is eight layer calls, T = 1, 2, ..., 8 (36 tokens); routing inputs change every step.
+Workload `decode` (default; BASELINE config 4, the configuration the headline metric is quoted on):
+greedy batch-1 decode of a Qwen3-30B-A3B-shape model -- 48 layers, hidden 2048, 32 q / 4 kv heads of
+128, 128 experts top-8, intermediate 768, vocab 151936; Q4_K attention/gate/up/embedding, Q6_K
+down/output, F32 router/norms; seeded random weights written as a GGUF (synth.config4_30b) and loaded
+through eahmmf_engine_load. A 512-token random-id prompt is prefilled (untimed), then W decode steps
+warm up and K decode steps are timed. One step = one token = one forward pass (48 layers + output GEMV
++ argmax), replayed as the captured CUDA graph.
 
-  value     tokens/s of the layer over all ranks: 36 * ranks / (device time of a step). Each layer
-            call is timed with CUDA events on its stream; the L2 is flushed (256 MiB memset) before
-            every call, outside the timed events.
-  e2e       the same through the C ABI with host buffers: pinned host->device copies of the step's
-            activations and logits, the call, and the device->host copy of the updated residual,
-            all inside the timed events.
-  roofline  the gate/up kernel (the step's largest weight stream): algorithmic bytes (weights of the
-            routed experts + staged activations + outputs) / its duration, timed by CUDA events on the
-            call's stream in a second pass over the same steps (stage events between the kernels would
-            serialise them, so they are kept out of the pass that gives `value`), against the measured
-            HBM copy bandwidth of this pool (MEASURED_PEAKS.json).
-  cpu_baseline  the reference's own CPU code (oracle/_ref, compiled from the reference sources) on a
-            bounded sample of the same workload, rank 0 at N = 1.
+  value     decode tokens/s over all ranks: K * ranks / (device time of the K steps, CUDA events on the
+            engine's stream, max over ranks). Each step streams ~2 GB of weights (far above the 126 MB
+            L2), so no flush is needed between steps.
+  e2e       eahmmf_engine_greedy through the C ABI with host buffers: the 512-token prompt copied in,
+            prefill, K generated tokens copied out; K / wall time of the call.
+  roofline  k_moe_gateup (the Q4_K MoE decode kernel the target names) at T = 1: algorithmic bytes
+            (the 8 routed experts' gate and up matrices + staged activations + h outputs) / its mean
+            duration over every layer of a few eager decode steps (CUDA events around the kernel on
+            its stream), against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the reference engine itself (oracle/_ref, compiled from the reference sources) on the
+            same GGUF, all host threads: decode tokens/s after a short prompt (rank 0 at N = 1).
+
+Workload `layer`: one MoE layer of the same shape on decode batches T = 1..8 (one
+step = eight layer calls, 36 tokens), L2 flushed before every call; value = tokens/s of the layer.
 
 --impl reference times the reference CPU implementation alone on the same workload (all host threads).
-Multi-GPU: the path has no exchange step at this configuration; N ranks run N replicas ("replicas only",
-weak scaling); the step time is the maximum over ranks.
+Multi-GPU: the path has no exchange step at these configurations; N ranks run N replicas ("replicas
+only", weak scaling); the step time is the maximum over ranks.
 """
 from __future__ import annotations
 
@@ -53,7 +57,7 @@ D, FF, E, K = 2048, 768, 128, 8
 TOKENS_PER_STEP = sum(T_LIST)
 LAUNCHES_PER_CALL = 3  # routing + prep, gate/up (+ h prep), down + combine
 GATEUP_STAGE = 2       # index of the gate/up kernel in eahmmf_cuda_moe_profile_read's stages
-CONFIG = {"workload": "config2: Qwen3-30B-A3B-shape MoE layer decode, T=1..8 tokens per step",
+LAYER_CONFIG = {"workload": "config2: Qwen3-30B-A3B-shape MoE layer decode, T=1..8 tokens per step",
           "hidden": D, "experts": E, "top_k": K, "moe_intermediate": FF, "gate_up": "Q4_K", "down": "Q6_K",
           "tokens_per_step": TOKENS_PER_STEP, "l2": "flushed (256 MiB memset) before every layer call, untimed"}
 
@@ -155,7 +159,7 @@ def cpu_reference(ex, steps: int, warmup: int, budget_s: float | None = None):
 
 
 # ---- our arm --------------------------------------------------------------------------------------
-def run_ours(args, rank: int, world: int, local: int):
+def layer_ours(args, rank: int, world: int, local: int):
     import torch
     import eahmmf_b200 as eb
     import synth
@@ -272,7 +276,7 @@ def run_ours(args, rank: int, world: int, local: int):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8/s8 tensor-core MMA, s32 -> fp32 accumulate (fp32 activations)",
-        "data": "synthetic (seeded)", "config": dict(CONFIG, parallelism=f"replicas x{world}"),
+        "data": "synthetic (seeded)", "config": dict(LAYER_CONFIG, parallelism=f"replicas x{world}"),
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -288,6 +292,178 @@ def run_ours(args, rank: int, world: int, local: int):
                                 "sample": f"{n} steps of T=1..8 ({TOKENS_PER_STEP} tokens each) through the "
                                           "reference CPU MoE block (oracle/_ref)"}
     return line
+
+
+# ---- decode workload (config 4) ----------------------------------------------------------------------
+N_PROMPT = 512
+DECODE_CONFIG = {"workload": "config4: Qwen3-30B-A3B-shape greedy batch-1 decode, 48 layers, 512-token prompt",
+                 "model": "qwen3moe 30B-A3B shape (synthetic weights)", "layers": 48, "hidden": 2048,
+                 "heads": "32q/4kv x 128", "experts": 128, "top_k": 8, "moe_intermediate": 768, "vocab": 151936,
+                 "types": "Q4_K attn/gate/up/embd, Q6_K down/output, F32 router/norms", "global_batch": 1,
+                 "prompt": N_PROMPT, "l2": "not flushed: each step streams ~2 GB of weights (> 126 MB L2)"}
+GATEUP_BYTES_T1 = 8 * 2 * 768 * 1152 + 2048 * 3 + 8 * 768 * 4  # routed experts' gate+up, XF digits, h
+
+
+def decode_model(rank: int):
+    """Path of the config-4 GGUF (generated once per machine; rank 0 writes, the others wait)."""
+    import synth
+    cfg = synth.config4_30b()
+    d = os.environ.get("EAHMMF_MODEL_DIR", "/tmp/eahmmf_models")
+    path = os.path.join(d, f"{cfg.name}-L{cfg.n_layer}-{synth.config_digest(cfg)}.gguf")
+    if rank == 0:
+        return synth.cached_gguf(cfg, d, workers=max(1, min(48, (os.cpu_count() or 2) - 1)))
+    t0 = time.time()
+    while not os.path.exists(path):
+        if time.time() - t0 > 1800:
+            raise RuntimeError("timed out waiting for rank 0 to write the model")
+        time.sleep(2)
+    return path
+
+
+def decode_prompt(rank: int, n: int = N_PROMPT):
+    import synth
+    return synth._rng(4, 0x50, rank).integers(0, 151936, n).astype(np.int32)
+
+
+def cpu_decode(path: str, steps: int, warmup: int, budget_s: float | None):
+    """Reference engine decode tokens/s on the host: a short prompt, then single-token forward passes
+    (Engine::forward through eref_engine_eval), `steps` of them or as many as fit in budget_s."""
+    import oracle
+    ref = oracle.Reference(threads=os.cpu_count() or 1)
+    n_prompt = 8
+    eng = ref.engine(path, n_prompt + warmup + max(steps, 4096 if budget_s else steps) + 8)
+    prompt = decode_prompt(0, n_prompt)
+    lg = eng.eval(prompt, 0, 32)
+    pos = n_prompt
+    for _ in range(warmup):
+        lg = eng.eval([int(lg.argmax())], pos, 1)
+        pos += 1
+    t0, done = time.perf_counter(), 0
+    while True:
+        lg = eng.eval([int(lg.argmax())], pos, 1)
+        pos += 1
+        done += 1
+        el = time.perf_counter() - t0
+        if (budget_s is None and done >= steps) or (budget_s is not None and el >= budget_s):
+            break
+        if pos >= eng.dims["n_ctx"] - 1:
+            break
+    eng.close()
+    return done / el, ref.threads, done, n_prompt
+
+
+def decode_ours(args, rank: int, world: int, local: int, path: str):
+    import torch
+    import eahmmf_b200 as eb
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n_ctx = N_PROMPT + args.warmup + args.steps + 16
+    eng = eb.Engine(path, n_ctx)
+    prompt = decode_prompt(rank)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # prefill + first token (untimed), warm-up steps (captures the step graph), then the timed steps
+    rc, first, _ = eng.greedy(prompt, 1, 32)
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
+    rc, warm, _ = eng.decode(args.warmup)
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
+    barrier()
+    with Clocks(local) as clk:
+        rc, toks, ms = eng.decode(args.steps)
+        barrier()
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
+    nodes = eng.graph_nodes()
+
+    # per-operation profile of a few eager steps, and the MoE stages inside them
+    eng.profile(True)
+    eb.MoeLayer.profile(True)
+    eng.decode(4)
+    ops = eng.profile_read()
+    moe_stages = eb.MoeLayer.profile_read()
+    eb.MoeLayer.profile(False)
+    eng.profile(False)
+    barrier()
+
+    # end to end through the C ABI: host prompt in, K host tokens out
+    t0 = time.perf_counter()
+    rc, gen, _ = eng.greedy(prompt, args.steps, 32)
+    e2e_s = time.perf_counter() - t0
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
+    # the captured-graph steps and the greedy call generate the same sequence
+    seq = np.concatenate([first, warm, toks])[:args.steps]
+    consistent = bool(np.array_equal(gen, seq))
+    eng.close()
+
+    t_ms = ms
+    if world > 1:
+        import torch.distributed as dist
+        v = torch.tensor([t_ms, e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        t_ms, e2e_s = float(v[0]), float(v[1])
+    value = args.steps * world / (t_ms * 1e-3)
+    peak, peak_kind = peaks()
+    gu_us = float(moe_stages[GATEUP_STAGE]) if len(moe_stages) else 0.0
+    achieved = GATEUP_BYTES_T1 / (gu_us * 1e-6) / 1e9 if gu_us > 0 else 0.0
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get("k_moe_gateup_decode_T1", {}).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        pass
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8/s8 tensor-core MMA, s32 -> fp32 accumulate (fp32 activations)",
+        "data": "synthetic (seeded random weights, random-id prompt)",
+        "config": dict(DECODE_CONFIG, parallelism=f"replicas x{world}"),
+        "e2e": {"value": args.steps * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
+                "d2h_bytes_per_step": args.steps * 4,
+                "step": "one eahmmf_engine_greedy call: 512-token prompt in, prefill, K tokens out"},
+        "gpu_launches": nodes * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if peak else None, "traffic": traffic, "kernel": "k_moe_gateup (T=1)",
+                     "peak_source": peak_kind,
+                     "timing": "CUDA events around the gate/up kernel on its stream, mean over 4 eager steps x 48 layers"},
+        "clocks": clk.summary(),
+        "decode_ops_us_per_step": ops,
+        "tokens_consistent": consistent,
+        "moe_stages_us_per_layer": {"router": float(moe_stages[0]), "route": float(moe_stages[1]),
+                                    "gateup": float(moe_stages[2]), "down_combine": float(moe_stages[3])}
+        if len(moe_stages) else None,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, n, npr = cpu_decode(path, steps=1, warmup=1, budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                                "sample": f"{n} decode steps of the reference engine (oracle/_ref) on the same GGUF "
+                                          f"after a {npr}-token prompt"}
+    return line
+
+
+def profile_decode(n_layer: int) -> int:
+    """No timing: a config-4-shape model with n_layer layers (generated if absent), an 8-token prompt
+    in one pass and 4 greedy tokens (3 captured-graph steps). The case ncu captures of the decode
+    kernels are taken on: 48 layers for the launch list, 2 layers (1.2 GB) for full captures."""
+    import synth
+    cfg = synth.config4_30b(n_layer=n_layer)
+    path = synth.cached_gguf(cfg, workers=max(1, min(48, (os.cpu_count() or 2) - 1)))
+    import eahmmf_b200 as eb
+    eng = eb.Engine(path, 64)
+    rc, out, _ = eng.greedy(decode_prompt(0, 8), 4, 8)
+    eng.close()
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_greedy returned {rc}")
+    print(json.dumps({"profile_decode": n_layer, "tokens": [int(v) for v in out], "ok": True}))
+    return 0
 
 
 def profile_case(T: int) -> int:
@@ -313,21 +489,46 @@ def profile_case(T: int) -> int:
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (decode: 128, layer: 20)")
+    ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (decode: 8, layer: 3)")
+    ap.add_argument("--workload", choices=("decode", "layer"), default="decode")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile-case", type=int, metavar="T", default=0,
                     help="no timing: run the config-2 layer three times at T tokens (a small case for ncu)")
+    ap.add_argument("--profile-decode", type=int, metavar="LAYERS", default=0,
+                    help="no timing: 8-token prompt + 4 greedy tokens on a config-4-shape model of LAYERS layers")
     args = ap.parse_args()
     if args.profile_case:
         return profile_case(args.profile_case)
+    if args.profile_decode:
+        return profile_decode(args.profile_decode)
+    decode = args.workload == "decode"
+    if args.steps is None:
+        args.steps = 128 if decode else 20
+    if args.warmup is None:
+        args.warmup = 8 if decode else 3
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
 
+    if args.impl == "reference" and decode:
+        if rank != 0:
+            return 0
+        path = decode_model(0)
+        v, cores, n, npr = cpu_decode(path, steps=min(args.steps, 24), warmup=1, budget_s=None)
+        line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": 1,
+                "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "fp32 (reference CPU)", "data": "synthetic (seeded random weights, random-id prompt)",
+                "config": dict(DECODE_CONFIG, parallelism="reference CPU", prompt=npr), "impl": "reference",
+                "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                                 "sample": f"{n} decode steps of the reference engine (oracle/_ref) on the same GGUF "
+                                           f"after a {npr}-token prompt (bounded: the reference takes ~0.2 s/token)"},
+                "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -337,21 +538,22 @@ def main():
         line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
                 "ms_per_step": TOKENS_PER_STEP / v * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "fp32 (reference CPU)", "data": "synthetic (seeded)",
-                "config": dict(CONFIG, parallelism="reference CPU"), "impl": "reference",
+                "config": dict(LAYER_CONFIG, parallelism="reference CPU"), "impl": "reference",
                 "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
                                  "sample": f"{n} steps of T=1..8 through the reference CPU MoE block (oracle/_ref)"},
                 "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
 
+    path = decode_model(rank) if decode else None  # before any CUDA work (spawned writer processes)
     if world > 1:
         import torch
         import torch.distributed as dist
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        line = run_ours(args, rank, world, local)
+        line = decode_ours(args, rank, world, local, path) if decode else layer_ours(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist

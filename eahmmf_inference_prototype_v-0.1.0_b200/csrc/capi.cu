@@ -193,7 +193,8 @@ constexpr int PROF_STAGES = 4;  // router GEMV, routing + activation prep, gate/
 struct StageTimer {
     bool on = false;
     cudaEvent_t ev[PROF_STAGES + 1] = {};
-    int used = 0;
+    double sum[PROF_STAGES] = {};
+    int blocks = 0;
     bool ensure() {
         for (auto& e : ev)
             if (!e && cudaEventCreate(&e) != cudaSuccess) return false;
@@ -202,23 +203,36 @@ struct StageTimer {
     void mark(int i, cudaStream_t st) {
         if (on && i <= PROF_STAGES) cudaEventRecord(ev[i], st);
     }
+    // after a block's last mark: wait for it and add its stage durations
+    bool collect() {
+        if (!on) return true;
+        if (cudaEventSynchronize(ev[PROF_STAGES]) != cudaSuccess) return false;
+        for (int i = 0; i < PROF_STAGES; i++) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, ev[i], ev[i + 1]) != cudaSuccess) return false;
+            sum[i] += ms * 1000.0;
+        }
+        blocks++;
+        return true;
+    }
+    void reset() {
+        for (double& v : sum) v = 0;
+        blocks = 0;
+    }
 } g_prof;
 }  // namespace
 
 extern "C" int eahmmf_cuda_moe_profile(int enable) {
     if (enable && !g_prof.ensure()) return ST_CUDA;
     g_prof.on = enable != 0;
+    g_prof.reset();
     return ST_OK;
 }
 
 extern "C" int eahmmf_cuda_moe_profile_read(float* us, int cap) {
-    if (!g_prof.on || !us || cap < PROF_STAGES) return ST_BAD_ARG;
-    if (cudaEventSynchronize(g_prof.ev[PROF_STAGES]) != cudaSuccess) return ST_CUDA;
-    for (int i = 0; i < PROF_STAGES; i++) {
-        float ms = 0.f;
-        if (cudaEventElapsedTime(&ms, g_prof.ev[i], g_prof.ev[i + 1]) != cudaSuccess) return ST_CUDA;
-        us[i] = ms * 1000.f;
-    }
+    if (!g_prof.on || !us || cap < PROF_STAGES || g_prof.blocks == 0) return ST_BAD_ARG;
+    for (int i = 0; i < PROF_STAGES; i++) us[i] = (float)(g_prof.sum[i] / g_prof.blocks);
+    g_prof.reset();
     return ST_OK;
 }
 
@@ -289,6 +303,7 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
         g_prof.mark(3, st);
         if (launch_moe_down(a, st) != cudaSuccess) return ST_CUDA;
         g_prof.mark(4, st);
+        if (!g_prof.collect()) return ST_CUDA;
     }
     return ST_OK;
 }

@@ -1,6 +1,7 @@
 // decode.cu -- the non-expert kernels of a qwen3moe forward pass (Engine::forward, qwen3moe.cpp:929-1074)
-// on sm_100a: embedding rows, RMSNorm, QK-norm + NeoX RoPE + KV-cache append, causal GQA attention as
-// split-context partials plus a merge, first-maximum argmax, and the device-side decode state.
+// on sm_100a: embedding rows, RMSNorm, QK-norm + NeoX RoPE + KV-cache append, causal GQA attention
+// split over the context (the last block of each head group merges the splits), first-maximum argmax,
+// and the device-side decode state.
 //
 // Every kernel that depends on the position reads it from device memory (`DecodeState.pos`), so one
 // captured CUDA graph serves every decode step: the argmax kernel writes the next token and advances
@@ -166,20 +167,28 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
 
 // ---- causal GQA attention (qwen3moe.cpp:976-1001), split over the context
 // Block (kv head h, split y, token t) runs the GRP q heads sharing kv head h over context chunks
-// y, y + nsplit, ... of ATT_CH positions, with an online softmax, and writes one partial (max, sum,
-// unnormalised output) per q head; k_attn_merge combines the splits. K/V chunks are staged in shared
-// memory with rows padded by 4 floats (conflict-free row-parallel score reads).
+// y, y + nsplit, ... of ATT_CH positions with an online softmax and writes one partial (max, sum,
+// unnormalised output) per q head. K/V chunks are staged in shared memory with cp.async (every thread's
+// 16-byte copies in flight at once), rows padded by 4 floats for conflict-free row-parallel score reads.
+// The last block of a (token, kv head) to finish (a counter per pair, reset by that block) merges the
+// splits: out = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 template <int HD>
-__global__ void __launch_bounds__(ATT_NT) k_attn_partial(const float* __restrict__ q, const float* __restrict__ kc,
-                                                          const float* __restrict__ vc, int n_head, int n_kv,
-                                                          float scale, const DecodeState* st, int nsplit,
-                                                          float* __restrict__ part) {
+__global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ q, const float* __restrict__ kc,
+                                                       const float* __restrict__ vc, int n_head, int n_kv, float scale,
+                                                       const DecodeState* st, int nsplit, float* __restrict__ part,
+                                                       int* __restrict__ counters, float* __restrict__ att) {
     constexpr int PER = HD / 32, RS = HD + 4;
     extern __shared__ __align__(16) float smf[];
-    float* Ks = smf;                  // [ATT_CH][RS]
-    float* Vs = Ks + ATT_CH * RS;     // [ATT_CH][RS]
-    float* Ps = Vs + ATT_CH * RS;     // [ATT_NT/32][ATT_CH] probabilities of the warp's current head
+    float* Ks = smf;                          // [ATT_CH][RS]
+    float* Vs = Ks + ATT_CH * RS;             // [ATT_CH][RS]
+    float* Ps = Vs + ATT_CH * RS;             // [ATT_NT/32][ATT_CH] probabilities of the warp's current head
     float* Qs = Ps + (ATT_NT / 32) * ATT_CH;  // [GRP][HD]
+    __shared__ bool last;
     const int h = blockIdx.x, y = blockIdx.y, t = blockIdx.z;
     const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = ATT_NT / 32;
@@ -201,9 +210,10 @@ __global__ void __launch_bounds__(ATT_NT) k_attn_partial(const float* __restrict
         for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
             const int r = i / (HD / 4), c4 = i - r * (HD / 4);
             const size_t g = (size_t)(p0 + r) * KD + (size_t)h * HD + 4 * c4;
-            *reinterpret_cast<float4*>(Ks + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(kc + g);
-            *reinterpret_cast<float4*>(Vs + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(vc + g);
+            cp_async16(Ks + r * RS + 4 * c4, kc + g);
+            cp_async16(Vs + r * RS + 4 * c4, vc + g);
         }
+        cp_async_wait_all();
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < ATT_MAXH; k++) {
@@ -277,32 +287,38 @@ __global__ void __launch_bounds__(ATT_NT) k_attn_partial(const float* __restrict
 #pragma unroll
         for (int j = 0; j < PER; j++) pr[2 + lane + 32 * j] = o_run[k][j];
     }
-}
-
-// out[t, head] = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M); one warp per (token, q head).
-template <int HD>
-__global__ void k_attn_merge(const float* __restrict__ part, int n_head, int nsplit, int nb, float* __restrict__ att) {
-    constexpr int PER = HD / 32;
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (gw >= nb * n_head) return;
-    const float* p = part + (size_t)gw * nsplit * (HD + 2);
-    float M = -INFINITY;
-    for (int y = 0; y < nsplit; y++) M = fmaxf(M, p[(size_t)y * (HD + 2)]);
-    float L = 0.f, o[PER];
-#pragma unroll
-    for (int j = 0; j < PER; j++) o[j] = 0.f;
-    for (int y = 0; y < nsplit; y++) {
-        const float* r = p + (size_t)y * (HD + 2);
-        if (r[0] == -INFINITY) continue;  // split without positions
-        const float e = expf(r[0] - M);
-        L = fmaf(r[1], e, L);
-#pragma unroll
-        for (int j = 0; j < PER; j++) o[j] = fmaf(r[2 + lane + 32 * j], e, o[j]);
+    // the last split block of (t, h) merges
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int* cnt = counters + (size_t)t * n_kv + h;
+        last = atomicAdd(cnt, 1) == nsplit - 1;
+        if (last) *cnt = 0;  // ready for the next pass (graph replays)
     }
-    const float inv = 1.0f / L;
-    float* dst = att + (size_t)gw * HD;  // gw = t * n_head + head: [nb x QD] rows
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int hq = warp; hq < grp; hq += nwarp) {
+        const float* p = part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2);
+        float M = -INFINITY;
+        for (int yy = 0; yy < nsplit; yy++) M = fmaxf(M, __ldcg(p + (size_t)yy * (HD + 2)));
+        float L = 0.f, o[PER];
 #pragma unroll
-    for (int j = 0; j < PER; j++) dst[lane + 32 * j] = o[j] * inv;
+        for (int j = 0; j < PER; j++) o[j] = 0.f;
+        for (int yy = 0; yy < nsplit; yy++) {
+            const float* r = p + (size_t)yy * (HD + 2);
+            const float m = __ldcg(r);
+            if (m == -INFINITY) continue;  // split without positions
+            const float e = expf(m - M);
+            L = fmaf(__ldcg(r + 1), e, L);
+#pragma unroll
+            for (int j = 0; j < PER; j++) o[j] = fmaf(__ldcg(r + 2 + lane + 32 * j), e, o[j]);
+        }
+        const float inv = 1.0f / L;
+        float* dst = att + (size_t)t * QD + (size_t)(h * grp + hq) * HD;
+#pragma unroll
+        for (int j = 0; j < PER; j++) dst[lane + 32 * j] = o[j] * inv;
+    }
 }
 
 // ---- argmax: first maximum, as std::max_element (qwen3moe.cpp:1103)
@@ -414,25 +430,25 @@ size_t attn_smem(int hd, int grp) {
 }
 template <int HD>
 static cudaError_t attn_as(const float* q, const float* kc, const float* vc, int n_head, int n_kv, float scale,
-                           const DecodeState* st, int nb, int nsplit, float* part, float* att, cudaStream_t s) {
+                           const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
+                           cudaStream_t s) {
     const size_t smem = attn_smem(HD, n_head / n_kv);
     static size_t cur = 0;
     if (smem > cur) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         cur = smem;
     }
-    k_attn_partial<HD><<<dim3(n_kv, nsplit, nb), ATT_NT, smem, s>>>(q, kc, vc, n_head, n_kv, scale, st, nsplit, part);
-    const int warps = nb * n_head;
-    k_attn_merge<HD><<<(warps + 7) / 8, 256, 0, s>>>(part, n_head, nsplit, nb, att);
+    k_attention<HD><<<dim3(n_kv, nsplit, nb), ATT_NT, smem, s>>>(q, kc, vc, n_head, n_kv, scale, st, nsplit, part,
+                                                                  counters, att);
     return cudaGetLastError();
 }
 cudaError_t launch_attention(int hd, const float* q, const float* kc, const float* vc, int n_head, int n_kv,
-                             float scale, const DecodeState* st, int nb, int nsplit, float* part, float* att,
-                             cudaStream_t s) {
+                             float scale, const DecodeState* st, int nb, int nsplit, float* part, int* counters,
+                             float* att, cudaStream_t s) {
     if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1) return cudaErrorInvalidValue;
-    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, s);
-    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, s);
+    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, s);
+    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, s);
     return cudaErrorInvalidValue;
 }
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {

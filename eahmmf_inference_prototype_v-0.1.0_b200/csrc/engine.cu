@@ -258,6 +258,7 @@ struct EahmmfEngine {
     float *out_norm = nullptr, *inv_freq = nullptr, *kc = nullptr, *vc = nullptr;
     float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *logits = nullptr;
     float* attn_part = nullptr;
+    int* attn_cnt = nullptr;  // [MAXB * n_kv] split counters of the attention kernel (self-resetting)
     float2 *rope_cs = nullptr, *amax_blk = nullptr;
     int amax_nblk = 0;
     void *moe_ws = nullptr, *gemv_ws = nullptr;
@@ -270,6 +271,7 @@ struct EahmmfEngine {
     int* out = nullptr;
     int cap_out = 0;
     cudaGraphExec_t step_graph = nullptr;
+    int graph_nodes = 0;
     bool trace = false;
     std::vector<int> trace_ids;
     std::vector<float> trace_w;
@@ -277,9 +279,18 @@ struct EahmmfEngine {
     std::vector<float> h_w;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     std::string err;
+    // per-operation profile of eager decode steps
+    static constexpr int NPROF = EAHMMF_ENGINE_PROFILE_CLASSES;
+    bool prof = false;
+    std::vector<cudaEvent_t> pev;  // pool, reused per step
+    std::vector<int> pcls;         // class of the operation that ends at each recorded event
+    int pn = 0;
+    double psum[NPROF] = {};
+    int psteps = 0;
 
     ~EahmmfEngine() {
         if (st) cudaStreamSynchronize(st);
+        for (cudaEvent_t v : pev) cudaEventDestroy(v);
         if (step_graph) cudaGraphExecDestroy(step_graph);
         for (void* p : allocs) cudaFree(p);
         if (h_toks) cudaFreeHost(h_toks);
@@ -457,9 +468,11 @@ struct EahmmfEngine {
             !dalloc(attn_part, (size_t)MAXB * n_head * std::min(nsplit_max, 128) * (hd + 2) * 4) ||
             !dalloc(amax_blk, (size_t)amax_nblk * 8) || !dalloc(moe_ws, moe_ws_bytes) ||
             !dalloc(gemv_ws, gemv_ws_bytes) || !dalloc(toks, MAXB * 4) || !dalloc(status, 4) ||
+            !dalloc(attn_cnt, (size_t)MAXB * n_kv * 4) ||
             !dalloc(state, sizeof(DecodeState)))
             return fail("cannot allocate activations / KV cache");
         if (cudaMemset(kc, 0, kvn * 4) != cudaSuccess || cudaMemset(vc, 0, kvn * 4) != cudaSuccess ||
+            cudaMemset(attn_cnt, 0, (size_t)MAXB * n_kv * 4) != cudaSuccess ||
             cudaMemset(status, 0, 4) != cudaSuccess)
             return fail("memset");
         if (cudaHostAlloc((void**)&h_toks, MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
@@ -521,20 +534,47 @@ struct EahmmfEngine {
         return std::max(1, std::min({nch, 128, 2 * 148 / std::max(1, n_kv * nb)}));
     }
 
+    // profile: an event after each operation, tagged with the operation's class
+    bool mark(int cls) {
+        if (!prof) return true;
+        if (pn == (int)pev.size()) {
+            cudaEvent_t v;
+            if (cudaEventCreate(&v) != cudaSuccess) return false;
+            pev.push_back(v);
+            pcls.push_back(0);
+        }
+        pcls[pn] = cls;
+        return cudaEventRecord(pev[pn++], st) == cudaSuccess;
+    }
+    bool collect() {
+        if (!prof || pn < 2) return true;
+        if (cudaEventSynchronize(pev[pn - 1]) != cudaSuccess) return false;
+        for (int i = 1; i < pn; i++) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, pev[i - 1], pev[i]) != cudaSuccess) return false;
+            psum[pcls[i]] += ms * 1000.0;
+        }
+        psteps++;
+        pn = 0;
+        return true;
+    }
+
     // One forward pass of nb tokens at the device position state->pos (which it does not change).
     // tok: device pointer to nb token ids. want_logits: logits of the last token into `logits`.
     int forward(const int* tok, int nb, bool want_logits) {
         const int nsplit = nsplit_for(nb);
         const float scale = 1.0f / sqrtf((float)hd);
+        if (!mark(0)) return ST_CUDA;
         if (launch_rope_table(state, inv_freq, hd / 2, nb, rope_cs, st) != cudaSuccess) return ST_CUDA;
         if (launch_embed(embd, embd_type, embd_rb, D, n_embd_rows, tok, nb, x, status, st) != cudaSuccess)
             return ST_CUDA;
+        if (!mark(0)) return ST_CUDA;
         const int ldq = QD + 2 * KD;
         for (int l = 0; l < n_layer; l++) {
             const Layer& L = layers[l];
             float* lk = kc + (size_t)l * n_ctx * KD;
             float* lv = vc + (size_t)l * n_ctx * KD;
-            if (launch_rmsnorm(x, D, L.attn_norm, xn, D, nb, D, eps, st) != cudaSuccess) return ST_CUDA;
+            if (launch_rmsnorm(x, D, L.attn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(1)) return ST_CUDA;
             int rc;
             if (L.fused) {
                 rc = eahmmf_cuda_gemv(L.wq[0], L.qkv_type[0], D, ldq, L.qkv_rb[0], xn, nb, D, qkv, ldq, 0, gemv_ws,
@@ -546,18 +586,19 @@ struct EahmmfEngine {
                     rc = eahmmf_cuda_gemv(L.wq[c], L.qkv_type[c], D, rows[c], L.qkv_rb[c], xn, nb, D, qkv + col[c],
                                           ldq, 0, gemv_ws, gemv_ws_bytes, st);
             }
-            if (rc != ST_OK) return rc;
+            if (rc != ST_OK || !mark(2)) return rc != ST_OK ? rc : ST_CUDA;
             if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, state, nb, q, lk, lv,
-                                  st) != cudaSuccess)
+                                  st) != cudaSuccess || !mark(3))
                 return ST_CUDA;
-            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, att, st) !=
-                cudaSuccess)
+            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, attn_cnt, att, st) !=
+                    cudaSuccess ||
+                !mark(4))
                 return ST_CUDA;
             rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes, st);
-            if (rc != ST_OK) return rc;
-            if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess) return ST_CUDA;
+            if (rc != ST_OK || !mark(5)) return rc != ST_OK ? rc : ST_CUDA;
+            if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(6)) return ST_CUDA;
             rc = eahmmf_cuda_moe_layer(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status);
-            if (rc != ST_OK) return rc;
+            if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
             if (trace) {  // routing of this layer (ids, then weights, at the head of the MoE workspace)
                 const size_t nk = (size_t)nb * n_used;
                 h_ids.resize(nk);
@@ -577,7 +618,7 @@ struct EahmmfEngine {
                 return ST_CUDA;
             const int rc = eahmmf_cuda_gemv(out_w, out_type, D, n_vocab, out_rb, xn, 1, D, logits, n_vocab, 0, gemv_ws,
                                             gemv_ws_bytes, st);
-            if (rc != ST_OK) return rc;
+            if (rc != ST_OK || !mark(8)) return rc != ST_OK ? rc : ST_CUDA;
         }
         return ST_OK;
     }
@@ -603,10 +644,14 @@ struct EahmmfEngine {
     // One decode step: forward of state->token at state->pos, then the argmax records the next token
     // and advances the position. Captured once, replayed per token.
     int step(bool use_graph) {
-        if (!use_graph || trace) {
+        if (!use_graph || trace || prof) {
+            pn = 0;
             const int rc = forward(&state->token, 1, true);
             if (rc != ST_OK) return rc;
-            return launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, 1, st) == cudaSuccess ? ST_OK : ST_CUDA;
+            if (launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, 1, st) != cudaSuccess || !mark(9) ||
+                !collect())
+                return ST_CUDA;
+            return ST_OK;
         }
         if (!step_graph) {
             cudaGraph_t gr = nullptr;
@@ -619,6 +664,8 @@ struct EahmmfEngine {
                 if (gr) cudaGraphDestroy(gr);
                 return rc != ST_OK ? rc : ST_CUDA;
             }
+            size_t nodes = 0;
+            if (cudaGraphGetNodes(gr, nullptr, &nodes) == cudaSuccess) graph_nodes = (int)nodes;
             const cudaError_t ie = cudaGraphInstantiate(&step_graph, gr, 0);
             cudaGraphDestroy(gr);
             if (ie != cudaSuccess) {
@@ -740,4 +787,23 @@ extern "C" int eahmmf_engine_trace_get(EahmmfEngine* e, int* ids, float* w, int 
     if (ids) memcpy(ids, e->trace_ids.data(), sizeof(int) * n);
     if (w) memcpy(w, e->trace_w.data(), sizeof(float) * n);
     return (int)e->trace_ids.size();
+}
+
+extern "C" int eahmmf_engine_graph_nodes(EahmmfEngine* e) { return e && e->step_graph ? e->graph_nodes : 0; }
+
+extern "C" int eahmmf_engine_profile(EahmmfEngine* e, int enable) {
+    if (!e) return ST_BAD_ARG;
+    e->prof = enable != 0;
+    for (double& v : e->psum) v = 0;
+    e->psteps = 0;
+    e->pn = 0;
+    return ST_OK;
+}
+
+extern "C" int eahmmf_engine_profile_read(EahmmfEngine* e, float* us, int cap) {
+    if (!e || !us || cap < EahmmfEngine::NPROF || e->psteps == 0) return 0;
+    for (int i = 0; i < EahmmfEngine::NPROF; i++) us[i] = (float)(e->psum[i] / e->psteps);
+    for (double& v : e->psum) v = 0;
+    e->psteps = 0;
+    return EahmmfEngine::NPROF;
 }

@@ -379,9 +379,55 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// F32 rows (the router, qwen3moe.cpp:1008): one 128-thread block per row, the four warps taking
+// interleaved float4 slices of the row so every thread has all its loads in flight at once; the four
+// partial sums are added in a fixed order (deterministic).
+constexpr int F32_NT = 128;
+__global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W, int K, const float* __restrict__ X,
+                                                     int ldx, int m, float* __restrict__ Y, int ldy) {
+    __shared__ float red[F32_NT / 32][MT];
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)row * K);
+    float acc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; t++) acc[t] = 0.f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < K / 4; i += F32_NT) {
+        const float4 w = __ldg(w4 + i);
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+            if (t < m) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(X + (size_t)t * ldx) + i);
+                acc[t] = fmaf(w.x, x.x, fmaf(w.y, x.y, fmaf(w.z, x.z, fmaf(w.w, x.w, acc[t]))));
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < MT; t++) {
+        float v = acc[t];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[warp][t] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < m) {
+        const int t = threadIdx.x;
+        Y[(size_t)t * ldy + row] = (red[0][t] + red[1][t]) + (red[2][t] + red[3][t]);
+    }
+}
+
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
-                            cudaStream_t st) {  // F32 rows take the per-row kernel, MT tokens per pass
+                            cudaStream_t st) {  // MT tokens per pass
+    const bool vec = K % 4 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(X) & 15) == 0;
     for (int t0 = 0; t0 < m; t0 += MT) {
+        if (vec) {
+            k_gemv_f32<<<rows, F32_NT, 0, st>>>(W, K, X + (size_t)t0 * ldx, ldx, m - t0 < MT ? m - t0 : MT,
+                                                Y + (size_t)t0 * ldy, ldy);
+            const cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+            continue;
+        }
         GemvArgs a{};
         a.W = QMat{reinterpret_cast<const uint8_t*>(W), T_F32, K, rows, (size_t)K * 4};
         a.X = X + (size_t)t0 * ldx;

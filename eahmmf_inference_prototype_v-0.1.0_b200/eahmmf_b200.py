@@ -62,6 +62,9 @@ EXPORTS = {
     "eahmmf_engine_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "eahmmf_engine_trace": (None, [C.c_void_p, C.c_int]),
     "eahmmf_engine_trace_get": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
+    "eahmmf_engine_graph_nodes": (C.c_int, [C.c_void_p]),
+    "eahmmf_engine_profile": (C.c_int, [C.c_void_p, C.c_int]),
+    "eahmmf_engine_profile_read": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "eahmmf_b200_version": (C.c_char_p, []),
     "eahmmf_b200_sm_count": (C.c_int, []),
 }
@@ -257,6 +260,21 @@ class Engine:
 
     def trace(self, enable: bool) -> None:
         lib().eahmmf_engine_trace(self._h, 1 if enable else 0)
+
+    PROFILE_CLASSES = ("embed_rope", "attn_norm", "qkv_gemv", "qk_rope_kv", "attention", "o_gemv", "ffn_norm",
+                       "moe", "output", "argmax")
+
+    def graph_nodes(self) -> int:
+        """Kernel launches in one captured decode step (0 before the first capture)."""
+        return int(lib().eahmmf_engine_graph_nodes(self._h))
+
+    def profile(self, enable: bool) -> None:
+        lib().eahmmf_engine_profile(self._h, 1 if enable else 0)
+
+    def profile_read(self) -> dict:
+        us = np.zeros(len(self.PROFILE_CLASSES), np.float32)
+        n = lib().eahmmf_engine_profile_read(self._h, us.ctypes.data, len(us))
+        return dict(zip(self.PROFILE_CLASSES, map(float, us))) if n else {}
 
     def trace_get(self):
         L = lib()

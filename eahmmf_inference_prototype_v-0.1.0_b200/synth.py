@@ -54,7 +54,7 @@ def quant_blocks(qtype: int, nblocks: int, rng: np.random.Generator, d_sigma: fl
     Q8_0: int8 quants uniform, fp16 d ~ |N(0, d_sigma)|.
     """
     blck, nb = BLOCK[qtype]
-    raw = _random_bytes(rng, nblocks * nb).reshape(nblocks, nb).copy()
+    raw = _random_bytes(rng, nblocks * nb).reshape(nblocks, nb)  # a fresh, writable buffer
     if qtype in (Q4_K, Q5_K):
         raw[:, 0:2] = _f16_bytes(np.abs(rng.normal(0.0, d_sigma, nblocks)))
         raw[:, 2:4] = _f16_bytes(np.abs(rng.normal(0.0, d_sigma, nblocks)))
@@ -266,8 +266,8 @@ def _gguf_kv(key: str, kind: str, val) -> bytes:
     raise ValueError(kind)
 
 
-def write_gguf(path: str, cfg: ModelConfig, progress: Callable[[str], None] | None = None) -> str:
-    """Writes ``cfg`` as a GGUF v3 file at ``path`` (atomically). Returns the path."""
+def _layout(cfg: ModelConfig):
+    """(header bytes, tensor specs, data offsets, total file size) of ``cfg``'s GGUF v3 file."""
     specs = cfg.tensors()
     align = 32
     header = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(specs), len(cfg.metadata())))
@@ -281,18 +281,70 @@ def write_gguf(path: str, cfg: ModelConfig, progress: Callable[[str], None] | No
         header += _gguf_str(s.name) + struct.pack("<I", len(s.shape))
         header += b"".join(struct.pack("<Q", n) for n in s.shape) + struct.pack("<IQ", s.qtype, o)
     header += b"\0" * ((-len(header)) % align)
+    return bytes(header), specs, offsets, len(header) + off
+
+
+def _write_chunks(args):
+    """Pool worker: writes chunks [c0, c1) of tensor ``spec`` (index i of its model) at their offsets."""
+    path, spec, i, c0, c1, base, seed = args
+    fd = os.open(path, os.O_WRONLY)
+    try:
+        blck, nb = BLOCK[spec.qtype]
+        total = spec.nbytes // nb
+        for c in range(c0, c1):
+            b0 = c * CHUNK_BLOCKS
+            n = min(CHUNK_BLOCKS, total - b0)
+            data = quant_blocks(spec.qtype, n, _rng(seed, i, c), spec.scale).reshape(-1)
+            os.pwrite(fd, data.tobytes(), base + b0 * nb)
+    finally:
+        os.close(fd)
+    return c1 - c0
+
+
+def write_gguf(path: str, cfg: ModelConfig, progress: Callable[[str], None] | None = None, workers: int = 0) -> str:
+    """Writes ``cfg`` as a GGUF v3 file at ``path`` (atomically). Returns the path.
+
+    workers > 0 generates the quantized tensors' chunks in that many spawned processes (same bytes:
+    every chunk's generator is keyed by (seed, tensor index, chunk index)). Call it before any CUDA
+    work in the calling process."""
+    header, specs, offsets, size = _layout(cfg)
     tmp = path + ".tmp"
+    if workers <= 0:
+        with open(tmp, "wb") as f:
+            f.write(header)
+            for i, (s, o) in enumerate(zip(specs, offsets)):
+                if progress and i % 12 == 0:
+                    progress(f"{s.name} ({i + 1}/{len(specs)})")
+                n = 0
+                for chunk in tensor_bytes(s, cfg.seed, i):
+                    f.write(chunk.tobytes())
+                    n += chunk.size
+                assert n == s.nbytes, (s.name, n, s.nbytes)
+                f.write(b"\0" * ((-n) % 32))
+        os.replace(tmp, path)
+        return path
+    import multiprocessing as mp
     with open(tmp, "wb") as f:
         f.write(header)
+        f.truncate(size)  # padding and alignment gaps read as zeros
         for i, (s, o) in enumerate(zip(specs, offsets)):
-            if progress and i % 12 == 0:
-                progress(f"{s.name} ({i + 1}/{len(specs)})")
-            n = 0
-            for chunk in tensor_bytes(s, cfg.seed, i):
-                f.write(chunk.tobytes())
-                n += chunk.size
-            assert n == s.nbytes, (s.name, n, s.nbytes)
-            f.write(b"\0" * ((-n) % align))
+            if s.qtype in (F32, F16):
+                f.seek(len(header) + o)
+                for chunk in tensor_bytes(s, cfg.seed, i):
+                    f.write(chunk.tobytes())
+    jobs = []
+    for i, (s, o) in enumerate(zip(specs, offsets)):
+        if s.qtype in (F32, F16):
+            continue
+        nchunk = -(-(s.nbytes // BLOCK[s.qtype][1]) // CHUNK_BLOCKS)
+        for c in range(nchunk):
+            jobs.append((tmp, s, i, c, c + 1, len(header) + o, cfg.seed))
+    done = 0
+    with mp.get_context("spawn").Pool(workers) as pool:
+        for n in pool.imap_unordered(_write_chunks, jobs, chunksize=1):
+            done += n
+            if progress and done % 64 == 0:
+                progress(f"{done}/{len(jobs)} chunks")
     os.replace(tmp, path)
     return path
 
@@ -301,14 +353,14 @@ def config_digest(cfg: ModelConfig) -> str:
     return hashlib.sha256(repr(dataclasses.asdict(cfg)).encode()).hexdigest()[:16]
 
 
-def cached_gguf(cfg: ModelConfig, directory: str | None = None, progress=None) -> str:
+def cached_gguf(cfg: ModelConfig, directory: str | None = None, progress=None, workers: int = 0) -> str:
     """Path of ``cfg``'s GGUF under ``directory`` (default $EAHMMF_MODEL_DIR or /tmp/eahmmf_models),
     generating it when absent."""
     directory = directory or os.environ.get("EAHMMF_MODEL_DIR", "/tmp/eahmmf_models")
     os.makedirs(directory, exist_ok=True)
     path = os.path.join(directory, f"{cfg.name}-L{cfg.n_layer}-{config_digest(cfg)}.gguf")
     if not os.path.exists(path):
-        write_gguf(path, cfg, progress)
+        write_gguf(path, cfg, progress, workers)
     return path
 
 

@@ -1,6 +1,6 @@
 /* eahmmf_b200.h -- C ABI of the B200 (sm_100a) expert hot path, libeahmmf_b200.so.
  *
- * Three groups of entry points:
+ * Four groups of entry points:
  *
  *  1. The reference's own CUDA entry points, same names, signatures and conventions, so the unmodified
  *     engine (qwen3moe.cpp built with -DEAHMMF_CUDA -DEAHMMF_CUDA_COMPUTE) links against this library
@@ -14,6 +14,9 @@
  *
  *  3. The device backend used by eahmmf::B200Device (include/eahmmf_b200_device.hpp): allocation,
  *     pinned-staged asynchronous copies on a side stream, free-memory queries.
+ *
+ *  4. A device-resident engine: a whole qwen3moe GGUF model in HBM, forward / eval / greedy decode
+ *     with the MoE block of group 2 and the attention path on the GPU.
  *
  * ggml type ids accepted: 0 F32, 1 F16, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K (the expert kernels take the
  * K-quants 12/13/14). Weight buffers must stay readable up to the next 16-byte boundary after their last
@@ -83,17 +86,18 @@ size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
  *   logits = d_logits ? d_logits : d_xn x router^T;  softmax numerators exp(l - max);  top-k with the
  *   reference's comparator;  weights renormalised over the k;  per active expert (ascending id) the
  *   gate/up projections, SiLU(g)*u, the down projection, and the weighted sum added to d_x.
- * d_xn: [T x D] expert input (post-norm, 16-byte aligned); d_x: [T x D] residual (8-byte aligned), updated
- * in place. Tokens are taken in blocks of 64, as the engine's forward() is fed at most MAXB = 64 tokens
- * (qwen3moe.cpp:39, :933); per-token results do not depend on the blocking. d_status (optional) receives EAHMMF_ST_* bits raised
- * inside kernels. */
+ * d_xn: [T x D] expert input (post-norm, 16-byte aligned); d_x: [T x D] residual (8-byte aligned),
+ * updated in place. Tokens are taken in blocks of 64, as the engine's forward() is fed at most
+ * MAXB = 64 tokens (qwen3moe.cpp:39, :933); per-token results do not depend on the blocking.
+ * d_status (optional) receives EAHMMF_ST_* bits raised inside kernels. */
 int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                           void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);
 
 /* Stage timing of eahmmf_cuda_moe_layer: when enabled, each call records CUDA events on its stream
- * around its four stages (router GEMV, routing + activation prep, gate/up, down/combine);
- * eahmmf_cuda_moe_profile_read waits for the last call and returns the four stage durations (us) of its
- * last 64-token block. The events serialise the stages (each kernel timed on its own). Off by default;
+ * around its four stages (router GEMV, routing + activation prep, gate/up, down + combine) of every
+ * 64-token block and waits for them; eahmmf_cuda_moe_profile_read returns the mean stage durations (us)
+ * over the blocks since the last read (or enable) and restarts the average. The events serialise the
+ * stages (each kernel timed on its own) and the wait makes each call synchronous. Off by default;
  * single-threaded use. */
 int eahmmf_cuda_moe_profile(int enable);
 int eahmmf_cuda_moe_profile_read(float* us, int cap);
@@ -172,6 +176,16 @@ int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_m
  * total. Tracing runs decode steps without the graph. */
 void eahmmf_engine_trace(EahmmfEngine* e, int enable);
 int eahmmf_engine_trace_get(EahmmfEngine* e, int* ids, float* w, int cap);
+/* Kernel launches in one captured decode step (nodes of its CUDA graph); 0 before the first capture. */
+int eahmmf_engine_graph_nodes(EahmmfEngine* e);
+/* Per-operation timing of decode steps: when enabled, steps run without the graph and record CUDA
+ * events between the operations of the pass; profile_read returns the mean device time per step (us)
+ * of each class, summed over layers: [0] embedding + rotary table, [1] attention RMSNorm, [2] q|k|v
+ * GEMV, [3] QK-norm + RoPE + KV append, [4] attention, [5] o-projection, [6] FFN RMSNorm, [7] MoE block,
+ * [8] output RMSNorm + GEMV, [9] argmax, and restarts the average. Returns the number of classes. */
+#define EAHMMF_ENGINE_PROFILE_CLASSES 10
+int eahmmf_engine_profile(EahmmfEngine* e, int enable);
+int eahmmf_engine_profile_read(EahmmfEngine* e, float* us, int cap);
 
 /* ---- misc ------------------------------------------------------------------------------------ */
 const char* eahmmf_b200_version(void);
