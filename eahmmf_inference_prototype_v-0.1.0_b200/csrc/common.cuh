@@ -47,6 +47,28 @@ struct XF {
 constexpr int XF_SUM_PAD = 4;  // floats after a row's segment sums (scale + padding to 16 bytes)
 __host__ __device__ constexpr int xf_gs_bytes(int K) { return 16 + K / 8; }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl may start while its predecessor on
+// the stream is still running; it must call pdl_wait() before touching anything the predecessor
+// writes (and every kernel of a chain calls it, so completion is transitive). pdl_trigger() lets the
+// successor launch early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, const Args&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 // Exact 2^e for -126 <= e <= 127.
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
 

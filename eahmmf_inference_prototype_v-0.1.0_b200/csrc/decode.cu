@@ -68,6 +68,8 @@ __device__ float dq_elem(const uint8_t* row, int type, int i) {
 __global__ void k_embed(const uint8_t* __restrict__ W, int type, size_t row_bytes, int D, int n_rows,
                         const int* __restrict__ toks, int nb, float* __restrict__ x, int* status) {
     const int t = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
     if (t >= nb) return;
     const int id = toks[t];
     if (id < 0 || id >= n_rows) {
@@ -98,6 +100,8 @@ constexpr int NORM_NT = 256;
 __global__ void __launch_bounds__(NORM_NT) k_rmsnorm(const float* __restrict__ x, int ldx, const float* __restrict__ w,
                                                      float* __restrict__ out, int ldo, int n, float eps) {
     __shared__ float red[NORM_NT / 32];
+    pdl_trigger();
+    pdl_wait();
     const float* xr = x + (size_t)blockIdx.x * ldx;
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += NORM_NT) ss = fmaf(xr[i], xr[i], ss);
@@ -111,6 +115,8 @@ __global__ void __launch_bounds__(NORM_NT) k_rmsnorm(const float* __restrict__ x
 __global__ void k_rope_table(const DecodeState* st, const float* __restrict__ inv_freq, int half, int nb,
                              float2* __restrict__ cs) {
     const int t = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const int p = st->pos + t;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
         const double ang = (double)p * (double)inv_freq[i];
@@ -129,6 +135,8 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
     constexpr int PER = HD / 32, HALF = HD / 2;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nh = n_head + 2 * n_kv, QD = n_head * HD, KD = n_kv * HD;
+    pdl_trigger();
+    pdl_wait();
     if (gw >= nb * nh) return;
     const int t = gw / nh, h = gw - t * nh;
     const float* src = qkv + (size_t)t * (QD + 2 * KD) + (size_t)h * HD;
@@ -192,6 +200,8 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     const int h = blockIdx.x, y = blockIdx.y, t = blockIdx.z;
     const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = ATT_NT / 32;
+    pdl_trigger();
+    pdl_wait();
     const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
     const int nch = (np + ATT_CH - 1) / ATT_CH;
     for (int i = threadIdx.x; i < grp * HD; i += ATT_NT) Qs[i] = q[(size_t)t * QD + (size_t)h * grp * HD + i];
@@ -331,6 +341,8 @@ __global__ void __launch_bounds__(ARGMAX_NT) k_argmax(const float* __restrict__ 
     __shared__ float sv[ARGMAX_NT / 32];
     __shared__ int si[ARGMAX_NT / 32];
     __shared__ bool last;
+    pdl_trigger();
+    pdl_wait();
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int i = blockIdx.x * ARGMAX_NT + threadIdx.x; i < n; i += gridDim.x * ARGMAX_NT) {
@@ -395,35 +407,35 @@ __global__ void __launch_bounds__(ARGMAX_NT) k_argmax(const float* __restrict__ 
 }
 
 // pos += n (host-enqueued position advance after a prompt chunk, kept on the device)
-__global__ void k_advance(DecodeState* st, int n) { st->pos += n; }
+__global__ void k_advance(DecodeState* st, int n) {
+    pdl_wait();
+    st->pos += n;
+}
 
 // ---- launchers ---------------------------------------------------------------------------------
 cudaError_t launch_embed(const uint8_t* W, int type, size_t rb, int D, int n_rows, const int* toks, int nb, float* x,
                          int* status, cudaStream_t s) {
-    k_embed<<<nb, 256, 0, s>>>(W, type, rb, D, n_rows, toks, nb, x, status);
-    return cudaGetLastError();
+    return launch_pdl(k_embed, dim3(nb), dim3(256), 0, s, W, type, rb, D, n_rows, toks, nb, x, status);
 }
 cudaError_t launch_rmsnorm(const float* x, int ldx, const float* w, float* out, int ldo, int rows, int n, float eps,
                            cudaStream_t s) {
-    k_rmsnorm<<<rows, NORM_NT, 0, s>>>(x, ldx, w, out, ldo, n, eps);
-    return cudaGetLastError();
+    return launch_pdl(k_rmsnorm, dim3(rows), dim3(NORM_NT), 0, s, x, ldx, w, out, ldo, n, eps);
 }
 cudaError_t launch_rope_table(const DecodeState* st, const float* inv_freq, int half, int nb, float2* cs,
                               cudaStream_t s) {
-    k_rope_table<<<nb, 64, 0, s>>>(st, inv_freq, half, nb, cs);
-    return cudaGetLastError();
+    return launch_pdl(k_rope_table, dim3(nb), dim3(64), 0, s, st, inv_freq, half, nb, cs);
 }
 cudaError_t launch_qk_rope_kv(int hd, const float* qkv, int n_head, int n_kv, const float* qn, const float* kn,
                               float eps, const float2* cs, const DecodeState* st, int nb, float* q_out, float* kc,
                               float* vc, cudaStream_t s) {
     const int warps = nb * (n_head + 2 * n_kv), grid = (warps + 7) / 8;
     if (hd == 128)
-        k_qk_rope_kv<128><<<grid, 256, 0, s>>>(qkv, n_head, n_kv, qn, kn, eps, cs, st, nb, q_out, kc, vc);
-    else if (hd == 64)
-        k_qk_rope_kv<64><<<grid, 256, 0, s>>>(qkv, n_head, n_kv, qn, kn, eps, cs, st, nb, q_out, kc, vc);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+        return launch_pdl(k_qk_rope_kv<128>, dim3(grid), dim3(256), 0, s, qkv, n_head, n_kv, qn, kn, eps, cs, st, nb,
+                          q_out, kc, vc);
+    if (hd == 64)
+        return launch_pdl(k_qk_rope_kv<64>, dim3(grid), dim3(256), 0, s, qkv, n_head, n_kv, qn, kn, eps, cs, st, nb,
+                          q_out, kc, vc);
+    return cudaErrorInvalidValue;
 }
 size_t attn_smem(int hd, int grp) {
     return ((size_t)2 * ATT_CH * (hd + 4) + (size_t)(ATT_NT / 32) * ATT_CH + (size_t)grp * hd) * sizeof(float);
@@ -439,9 +451,8 @@ static cudaError_t attn_as(const float* q, const float* kc, const float* vc, int
         if (e != cudaSuccess) return e;
         cur = smem;
     }
-    k_attention<HD><<<dim3(n_kv, nsplit, nb), ATT_NT, smem, s>>>(q, kc, vc, n_head, n_kv, scale, st, nsplit, part,
-                                                                  counters, att);
-    return cudaGetLastError();
+    return launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv, scale,
+                      st, nsplit, part, counters, att);
 }
 cudaError_t launch_attention(int hd, const float* q, const float* kc, const float* vc, int n_head, int n_kv,
                              float scale, const DecodeState* st, int nb, int nsplit, float* part, int* counters,
@@ -452,12 +463,10 @@ cudaError_t launch_attention(int hd, const float* q, const float* kc, const floa
     return cudaErrorInvalidValue;
 }
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {
-    k_argmax<<<nblk, ARGMAX_NT, 0, s>>>(lg, n, blk, st, advance);
-    return cudaGetLastError();
+    return launch_pdl(k_argmax, dim3(nblk), dim3(ARGMAX_NT), 0, s, lg, n, blk, st, advance);
 }
 cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s) {
-    k_advance<<<1, 1, 0, s>>>(st, n);
-    return cudaGetLastError();
+    return launch_pdl(k_advance, dim3(1), dim3(1), 0, s, st, n);
 }
 
 }  // namespace eb

@@ -95,6 +95,8 @@ __device__ float weight_at(const uint8_t* row, int type, int k) {
 
 // One warp per row; lanes stride over K; up to MT tokens per launch.
 __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int warp = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= a.W.rows) return;
     const uint8_t* row = a.W.w + (size_t)warp * a.W.row_bytes;
@@ -127,6 +129,8 @@ __global__ void __launch_bounds__(PREP_NT) k_prep_x(const float* __restrict__ X,
                                                      float* __restrict__ sum, uint8_t* __restrict__ gs) {
     __shared__ float red[33];
     const int row = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
     prep_row(X + (size_t)row * ldx, K, frag + (size_t)row * (K >> 5) * 12, sum + (size_t)row * ((K >> 4) + XF_SUM_PAD),
              gs + (size_t)row * xf_gs_bytes(K), red);
 }
@@ -277,13 +281,15 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
     uint8_t* slot = sm + pl.slot_off;
     const RowLayout L = layout_of(a.W.w, rb);
     const int r0 = 16 * (int)blockIdx.x, r1 = min(a.W.rows, r0 + 16);
-    if (tid == 0) {
+    pdl_trigger();
+    if (tid == 0) {  // the weight rows do not depend on earlier grids: their copy starts before the wait
         mbar_init(&bar[0], 1);
         mbar_fence_init();
         mbar_expect_tx(&bar[0], rows_bytes(L, a.W.w, rb, r0, r1) + xf_bytes_of(m, K));
         issue_rows(L, a.W.w, rb, r0, r1, slot, &bar[0]);
-        issue_xf(a.xf, [](int i) { return i; }, m, K, sfrag, ssum, &bar[0]);
     }
+    pdl_wait();  // the activations (XF) and, when accumulating, Y come from earlier grids
+    if (tid == 0) issue_xf(a.xf, [](int i) { return i; }, m, K, sfrag, ssum, &bar[0]);
     __syncthreads();
     if (__syncthreads_or(!mbar_wait_bounded(&bar[0], 0u))) {
         if (tid == 0) {
@@ -337,9 +343,8 @@ XF xf_carve(void* base, int rows, int K) {
 
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st) {
     if (rows < 1 || K % 256 || ldx % 4 || !aligned16(X)) return cudaErrorInvalidValue;
-    k_prep_x<<<rows, PREP_NT, 0, st>>>(X, ldx, K, const_cast<uint2*>(out.frag), const_cast<float*>(out.sum),
-                                       const_cast<uint8_t*>(out.gs));
-    return cudaGetLastError();
+    return launch_pdl(k_prep_x, dim3(rows), dim3(PREP_NT), 0, st, X, ldx, K, const_cast<uint2*>(out.frag),
+                      const_cast<float*>(out.sum), const_cast<uint8_t*>(out.gs));
 }
 
 // Raises a kernel's dynamic shared-memory limit once per kernel and size (host-side bookkeeping only).
@@ -359,7 +364,7 @@ template <int QT, int NSET>
 static void gemv_go(const GemvXArgs& a, cudaStream_t st) {
     const GPlan pl = gemv_plan(QT, a.W.K, a.W.row_bytes, NSET, a.m);
     smem_attr(k_gemv<QT, NSET>, pl.total);
-    k_gemv<QT, NSET><<<(a.W.rows + 15) / 16, NTU, pl.total, st>>>(a);
+    launch_pdl(k_gemv<QT, NSET>, dim3((a.W.rows + 15) / 16), dim3(NTU), pl.total, st, a);
 }
 
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st) {
@@ -375,8 +380,7 @@ cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st) {
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
     if (a.m < 1 || a.m > MT) return cudaErrorInvalidValue;
-    k_gemv_generic<<<(a.W.rows * 32 + 255) / 256, 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_gemv_generic, dim3((a.W.rows * 32 + 255) / 256), dim3(256), 0, st, a);
 }
 
 // F32 rows (the router, qwen3moe.cpp:1008): one 128-thread block per row, the four warps taking
@@ -387,6 +391,8 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
                                                      int ldx, int m, float* __restrict__ Y, int ldy) {
     __shared__ float red[F32_NT / 32][MT];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
     const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)row * K);
     float acc[MT];
 #pragma unroll
@@ -422,9 +428,8 @@ cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int
                      (reinterpret_cast<uintptr_t>(X) & 15) == 0;
     for (int t0 = 0; t0 < m; t0 += MT) {
         if (vec) {
-            k_gemv_f32<<<rows, F32_NT, 0, st>>>(W, K, X + (size_t)t0 * ldx, ldx, m - t0 < MT ? m - t0 : MT,
-                                                Y + (size_t)t0 * ldy, ldy);
-            const cudaError_t e = cudaGetLastError();
+            const cudaError_t e = launch_pdl(k_gemv_f32, dim3(rows), dim3(F32_NT), 0, st, W, K, X + (size_t)t0 * ldx,
+                                             ldx, m - t0 < MT ? m - t0 : MT, Y + (size_t)t0 * ldy, ldy);
             if (e != cudaSuccess) return e;
             continue;
         }

@@ -38,8 +38,6 @@ namespace eb {
 
 namespace {
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -412,6 +410,7 @@ __device__ void route_token(const float* __restrict__ lg, int E, int K, int lane
 
 __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
+    pdl_wait();     // logits and activations come from the previous grids
     if (blockIdx.x > 0) {  // activation prep of token blockIdx.x - 1
         __shared__ float red[33];
         const int row = blockIdx.x - 1;
@@ -875,22 +874,6 @@ void smem_attr(Kern k, size_t smem) {
         cur = smem;
     }
 }
-// Launch with programmatic stream serialization: the kernel may start before its predecessor on the
-// stream has finished and calls griddepcontrol.wait before reading the predecessor's results.
-template <typename Kern, typename... Args>
-cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t st, const Args&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k, args...);
-}
 int max_groups(const MoeArgs& a) { return std::min(a.T * a.n_used, a.n_expert * ((a.T + MU - 1) / MU)); }
 
 }  // namespace
@@ -902,8 +885,7 @@ cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st) {
     if (a.T < 1 || a.T > MOE_TMAX || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert ||
         a.D % 256 || a.D % DN_ROWS)
         return cudaErrorInvalidValue;
-    k_moe_route<<<1 + a.T, ROUTE_NT, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_moe_route, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a);
 }
 
 template <int QG, int QU>
