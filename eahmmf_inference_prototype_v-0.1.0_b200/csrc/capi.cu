@@ -176,6 +176,50 @@ WsLayout ws_layout(const EahmmfMoeLayer* L, int T) {
     w.total = o;
     return w;
 }
+// Tokens per call from which the block runs as grouped tensor-core GEMMs (gemm.cu): every active
+// expert's weights are dequantized once to f16 and each expert's slots are one dense contraction,
+// instead of 64-token passes that each stream the routed experts again.
+constexpr int GROUPED_MIN_T = 256;
+struct GroupedLayout {
+    size_t ids, wts, logits, offsets, active, ngroups, cnt, local, tiles_gu, tiles_dn, slot_token, slot_w,
+        token_slots, wf, rs, xhi, xlo, xscale, h, hhi, hlo, hscale, y, total;
+};
+GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
+    const size_t K = (size_t)L->n_used, E = (size_t)L->n_expert, S = (size_t)T * K, D = L->D, FF = L->FF;
+    GroupedLayout w;
+    size_t o = 0;
+    auto take = [&](size_t& at, size_t bytes) {
+        at = o;
+        o = a256(o + bytes);
+    };
+    take(w.ids, S * 4);  // same head as the 64-token layout: ids, then weights at the next 256 bytes
+    take(w.wts, S * 4);
+    take(w.logits, L->d_router ? (size_t)T * E * 4 : 0);
+    take(w.offsets, (E + 1) * 4);
+    take(w.active, (E + 1) * 4);
+    take(w.ngroups, 4);
+    take(w.cnt, E * 4);
+    take(w.local, S * 4);
+    take(w.tiles_gu, (E + 1) * 4);
+    take(w.tiles_dn, (E + 1) * 4);
+    take(w.slot_token, S * 4);
+    take(w.slot_w, S * 4);
+    take(w.token_slots, S * 4);
+    take(w.wf, E * 3 * FF * D * 2);
+    take(w.rs, E * (2 * FF + D) * 4);
+    take(w.xhi, (size_t)T * D * 2);
+    take(w.xlo, (size_t)T * D * 2);
+    take(w.xscale, (size_t)T * 4);
+    take(w.h, S * FF * 4);
+    take(w.hhi, S * FF * 2);
+    take(w.hlo, S * FF * 2);
+    take(w.hscale, S * 4);
+    take(w.y, S * D * 4);
+    w.total = o;
+    return w;
+}
+bool grouped_ok(const EahmmfMoeLayer* L, int T) { return T >= GROUPED_MIN_T && L->D % 128 == 0 && L->FF % 64 == 0; }
+
 bool layer_ok(const EahmmfMoeLayer* L) {
     return L && L->n_expert > 0 && L->n_expert <= MAX_EXPERTS && L->n_used > 0 && L->n_used <= 32 &&
            L->n_used <= L->n_expert && L->D > 0 && L->D % 256 == 0 && L->FF > 0 && L->FF % 256 == 0 && L->d_gate &&
@@ -238,8 +282,106 @@ extern "C" int eahmmf_cuda_moe_profile_read(float* us, int cap) {
 
 extern "C" size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T) {
     if (!layer_ok(L) || T < 1) return 0;
-    return ws_layout(L, T).total;
+    return grouped_ok(L, T) ? grouped_layout(L, T).total : ws_layout(L, T).total;
 }
+
+namespace {
+// The MoE block for a ragged batch of T >= GROUPED_MIN_T tokens as grouped tensor-core GEMMs.
+int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x, uint8_t* ws,
+                cudaStream_t st, int* d_status) {
+    const GroupedLayout w = grouped_layout(L, T);
+    const int K = L->n_used, E = L->n_expert, S = T * K;
+    MoeArgs a{};
+    a.gate = L->d_gate;
+    a.up = L->d_up;
+    a.down = L->d_down;
+    a.gate_type = L->gate_type;
+    a.up_type = L->up_type;
+    a.down_type = L->down_type;
+    a.gate_rb = L->gate_row_bytes;
+    a.up_rb = L->up_row_bytes;
+    a.down_rb = L->down_row_bytes;
+    a.n_expert = E;
+    a.n_used = K;
+    a.D = L->D;
+    a.FF = L->FF;
+    a.T = T;
+    a.xn = d_xn;
+    a.x = d_x;
+    a.rw.ids = reinterpret_cast<int*>(ws + w.ids);
+    a.rw.wts = reinterpret_cast<float*>(ws + w.wts);
+    a.rw.offsets = reinterpret_cast<int*>(ws + w.offsets);
+    a.rw.active = reinterpret_cast<int*>(ws + w.active);
+    a.rw.ngroups = reinterpret_cast<int*>(ws + w.ngroups);
+    a.rw.slot_token = reinterpret_cast<int*>(ws + w.slot_token);
+    a.rw.slot_w = reinterpret_cast<float*>(ws + w.slot_w);
+    a.rw.token_slots = reinterpret_cast<int*>(ws + w.token_slots);
+    a.y = reinterpret_cast<float*>(ws + w.y);
+    a.status = d_status;
+    int* cnt = reinterpret_cast<int*>(ws + w.cnt);
+    int* local = reinterpret_cast<int*>(ws + w.local);
+    int* tiles_gu = reinterpret_cast<int*>(ws + w.tiles_gu);
+    int* tiles_dn = reinterpret_cast<int*>(ws + w.tiles_dn);
+    GroupedArgs g{};
+    g.w[0] = L->d_gate;
+    g.w[1] = L->d_up;
+    g.w[2] = L->d_down;
+    g.type[0] = L->gate_type;
+    g.type[1] = L->up_type;
+    g.type[2] = L->down_type;
+    g.rb[0] = L->gate_row_bytes;
+    g.rb[1] = L->up_row_bytes;
+    g.rb[2] = L->down_row_bytes;
+    g.E = E;
+    g.D = L->D;
+    g.FF = L->FF;
+    g.offsets = a.rw.offsets;
+    g.slot_token = a.rw.slot_token;
+    g.tiles_gu = tiles_gu;
+    g.tiles_dn = tiles_dn;
+    g.wf = reinterpret_cast<__half*>(ws + w.wf);
+    g.w_expert = (size_t)3 * L->FF * L->D;
+    g.w_off[0] = 0;
+    g.w_off[1] = (size_t)L->FF * L->D;
+    g.w_off[2] = (size_t)2 * L->FF * L->D;
+    g.rs = reinterpret_cast<float*>(ws + w.rs);
+    g.xhi = reinterpret_cast<const __half*>(ws + w.xhi);
+    g.xlo = reinterpret_cast<const __half*>(ws + w.xlo);
+    g.xscale = reinterpret_cast<const float*>(ws + w.xscale);
+    g.h = reinterpret_cast<float*>(ws + w.h);
+    g.hhi = reinterpret_cast<const __half*>(ws + w.hhi);
+    g.hlo = reinterpret_cast<const __half*>(ws + w.hlo);
+    g.hscale = reinterpret_cast<const float*>(ws + w.hscale);
+    g.y = a.y;
+    g.status = d_status;
+    g_prof.mark(0, st);
+    if (d_logits) {
+        a.logits = d_logits;
+    } else {
+        float* lg = reinterpret_cast<float*>(ws + w.logits);
+        if (launch_f32_gemv(L->d_router, L->D, E, d_xn, L->D, T, lg, E, st) != cudaSuccess) return ST_CUDA;
+        a.logits = lg;
+    }
+    g_prof.mark(1, st);
+    if (cudaMemsetAsync(cnt, 0, (size_t)E * 4, st) != cudaSuccess || launch_route_big(a, cnt, local, st) != cudaSuccess ||
+        launch_plan_big(a, cnt, tiles_gu, tiles_dn, st) != cudaSuccess || launch_scatter_big(a, local, st) != cudaSuccess ||
+        launch_grouped_dequant(g, st) != cudaSuccess ||
+        launch_pack_f16(d_xn, T, L->D, const_cast<__half*>(g.xhi), const_cast<__half*>(g.xlo),
+                        const_cast<float*>(g.xscale), st) != cudaSuccess)
+        return ST_CUDA;
+    g_prof.mark(2, st);
+    const int slot_tiles = (S + 127) / 128 + E;  // bound on sum over experts of ceil(m_e / 128)
+    if (launch_grouped_gemm(g, 0, (L->FF / 64) * slot_tiles, st) != cudaSuccess) return ST_CUDA;
+    g_prof.mark(3, st);
+    if (launch_pack_f16(g.h, S, L->FF, const_cast<__half*>(g.hhi), const_cast<__half*>(g.hlo),
+                        const_cast<float*>(g.hscale), st) != cudaSuccess ||
+        launch_grouped_gemm(g, 1, (L->D / 128) * slot_tiles, st) != cudaSuccess || launch_moe_combine(a, st) != cudaSuccess)
+        return ST_CUDA;
+    g_prof.mark(4, st);
+    if (!g_prof.collect()) return ST_CUDA;
+    return ST_OK;
+}
+}  // namespace
 
 extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits,
                                      float* d_x, void* d_workspace, size_t workspace_bytes, void* stream,
@@ -251,10 +393,14 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
     if (reinterpret_cast<uintptr_t>(d_xn) & 15 || reinterpret_cast<uintptr_t>(d_x) & 7 ||
         reinterpret_cast<uintptr_t>(d_workspace) & 255)
         return ST_BAD_ARG;
-    const WsLayout w = ws_layout(L, T);
-    if (workspace_bytes < w.total) return ST_CAPACITY;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     uint8_t* ws = static_cast<uint8_t*>(d_workspace);
+    if (grouped_ok(L, T)) {
+        if (workspace_bytes < grouped_layout(L, T).total) return ST_CAPACITY;
+        return moe_grouped(L, T, d_xn, d_logits, d_x, ws, st, d_status);
+    }
+    const WsLayout w = ws_layout(L, T);
+    if (workspace_bytes < w.total) return ST_CAPACITY;
     const int K = L->n_used, E = L->n_expert;
     for (int t0 = 0; t0 < T; t0 += CHUNK) {
         const int tc = T - t0 < CHUNK ? T - t0 : CHUNK;

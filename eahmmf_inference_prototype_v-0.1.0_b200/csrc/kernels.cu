@@ -383,14 +383,14 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
     return launch_pdl(k_gemv_generic, dim3((a.W.rows * 32 + 255) / 256), dim3(256), 0, st, a);
 }
 
-// F32 rows (the router, qwen3moe.cpp:1008): one 128-thread block per row, the four warps taking
-// interleaved float4 slices of the row so every thread has all its loads in flight at once; the four
-// partial sums are added in a fixed order (deterministic).
 constexpr int F32_NT = 128;
 __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W, int K, const float* __restrict__ X,
-                                                     int ldx, int m, float* __restrict__ Y, int ldy) {
+                                                     int ldx, int m_all, float* __restrict__ Y, int ldy) {
     __shared__ float red[F32_NT / 32][MT];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.y * MT, m = min(MT, m_all - t0);  // this block's tokens
+    X += (size_t)t0 * ldx;
+    Y += (size_t)t0 * ldy;
     pdl_trigger();
     pdl_wait();
     const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)row * K);
@@ -422,17 +422,16 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
     }
 }
 
+// F32 rows (the router, qwen3moe.cpp:1008): one 128-thread block per (row, MT tokens), the four warps
+// taking interleaved float4 slices of the row so every thread has all its loads in flight at once; the
+// four partial sums are added in a fixed order (deterministic).
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
-                            cudaStream_t st) {  // MT tokens per pass
+                            cudaStream_t st) {
     const bool vec = K % 4 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(X) & 15) == 0;
-    for (int t0 = 0; t0 < m; t0 += MT) {
-        if (vec) {
-            const cudaError_t e = launch_pdl(k_gemv_f32, dim3(rows), dim3(F32_NT), 0, st, W, K, X + (size_t)t0 * ldx,
-                                             ldx, m - t0 < MT ? m - t0 : MT, Y + (size_t)t0 * ldy, ldy);
-            if (e != cudaSuccess) return e;
-            continue;
-        }
+    if (vec)
+        return launch_pdl(k_gemv_f32, dim3(rows, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, X, ldx, m, Y, ldy);
+    for (int t0 = 0; t0 < m; t0 += MT) {  // other layouts: the per-row kernel, MT tokens per pass
         GemvArgs a{};
         a.W = QMat{reinterpret_cast<const uint8_t*>(W), T_F32, K, rows, (size_t)K * 4};
         a.X = X + (size_t)t0 * ldx;

@@ -92,6 +92,31 @@ struct GemvXArgs {
     int* status;
 };
 
+// Grouped tensor-core path of the MoE block (gemm.cu) for ragged batches.
+struct GroupedArgs {
+    const uint8_t* const* w[3];  // per-expert component pointer tables: gate, up, down
+    int type[3];
+    size_t rb[3];
+    int E, D, FF;
+    const int* offsets;     // [E+1] slot offsets per expert
+    const int* slot_token;  // [S] token of each slot
+    const int* tiles_gu;    // [E+1] prefix of gate/up tiles per expert (FF/64 row tiles x ceil(m_e/128))
+    const int* tiles_dn;    // [E+1] prefix of down tiles per expert (D/128 row tiles x ceil(m_e/128))
+    __half* wf;             // f16 weights, per expert: gate [FF x D], up [FF x D], down [D x FF]
+    size_t w_expert;        // elements per expert (3 FF D)
+    size_t w_off[3];        // element offsets of gate, up, down within an expert
+    float* rs;              // per expert 2 FF + D row scales (powers of two)
+    const __half* xhi;      // [T x D] tokens, f16 hi/lo of x / xscale
+    const __half* xlo;
+    const float* xscale;    // [T]
+    float* h;               // [S x FF] SiLU(g) * u per slot
+    const __half* hhi;      // [S x FF] f16 hi/lo of h / hscale
+    const __half* hlo;
+    const float* hscale;    // [S]
+    float* y;               // [S x D] down outputs per slot
+    int* status;
+};
+
 int sm_count();
 bool gemv_mma_ok(const QMat& W);                 // tensor-core path available for this matrix
 // bytes of an XF block of `rows` rows: digits (3 bytes per element), per row the per-16 sums and the
@@ -110,6 +135,15 @@ cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st);
 size_t moe_smem_gateup(int D, size_t rbg, size_t rbu);
 size_t moe_smem_down(int FF, size_t rbd);
+cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st);
+cudaError_t launch_pack_f16(const float* x, int n, int K, __half* hi, __half* lo, float* scale, cudaStream_t st);
+cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st);  // 0 gate/up, 1 down
+// routing of a ragged batch of any size (moe.cu): per-token top-k with expert counts (cnt zeroed by the
+// caller), then offsets / tile prefixes / active list, then the slot maps
+cudaError_t launch_route_big(const MoeArgs& a, int* cnt, int* local, cudaStream_t st);
+cudaError_t launch_plan_big(const MoeArgs& a, const int* cnt, int* tiles_gu, int* tiles_dn, cudaStream_t st);
+cudaError_t launch_scatter_big(const MoeArgs& a, const int* local, cudaStream_t st);
+cudaError_t launch_moe_combine(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
                             cudaStream_t st);
 

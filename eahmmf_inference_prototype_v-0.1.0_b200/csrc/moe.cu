@@ -860,6 +860,97 @@ __global__ void __launch_bounds__(COMB_NT) k_moe_combine(MoeArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------
+// ragged batches of any size (the grouped tensor-core path): routing without the 64-token masks.
+// Slot order inside an expert follows the count atomics (not token order); every slot's result depends
+// only on its own token, and the combine visits a token's slots in expert order, so the outputs are
+// the same for any slot order.
+// ------------------------------------------------------------------------------------------------
+constexpr int BIG_NT = 256;
+__global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict__ cnt, int* __restrict__ local) {
+    __shared__ uint32_t s_rk[(BIG_NT / 32) * 64];
+    pdl_trigger();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (BIG_NT / 32) + warp, E = a.n_expert, K = a.n_used;
+    if (t >= a.T) return;  // whole warps
+    int my_e = 0;
+    float my_w = 0.f;
+    const float* lg = a.logits + (size_t)t * E;
+    if (E <= 128) route_token<4>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+    else if (E <= 256) route_token<8>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+    else route_token<16>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+    if (lane < K) {
+        if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+            set_flag(a.status, ST_BAD_INDEX);
+            my_e = 0;
+        }
+        a.rw.ids[(size_t)t * K + lane] = my_e;
+        a.rw.wts[(size_t)t * K + lane] = my_w;
+        local[(size_t)t * K + lane] = atomicAdd(&cnt[my_e], 1);
+    }
+}
+
+// One block: slot offsets, tile prefixes of the two GEMMs, active list.
+__global__ void __launch_bounds__(512) k_plan_big(MoeArgs a, const int* __restrict__ cnt, int* __restrict__ tiles_gu,
+                                                  int* __restrict__ tiles_dn) {
+    __shared__ int ws[3][16];
+    pdl_trigger();
+    pdl_wait();
+    const int E = a.n_expert, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = tid < E ? cnt[tid] : 0;
+    const int nt = (c + 127) / 128;
+    int v[3] = {c, nt, c > 0 ? 1 : 0};
+    int incl[3];
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+        int x = v[q];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        incl[q] = x;
+        if (lane == 31) ws[q][warp] = x;
+    }
+    __syncthreads();
+    int base[3] = {0, 0, 0};
+#pragma unroll
+    for (int q = 0; q < 3; q++)
+        for (int w = 0; w < warp; w++) base[q] += ws[q][w];
+    const int off = base[0] + incl[0] - v[0], toff = base[1] + incl[1] - v[1], aoff = base[2] + incl[2] - v[2];
+    const int RTg = a.FF / 64, RTd = a.D / 128;
+    if (tid < E) {
+        a.rw.offsets[tid] = off;
+        tiles_gu[tid] = RTg * toff;
+        tiles_dn[tid] = RTd * toff;
+        if (c > 0) a.rw.active[1 + aoff] = tid;
+    }
+    if (tid == E - 1) {
+        a.rw.offsets[E] = off + c;
+        tiles_gu[E] = RTg * (toff + nt);
+        tiles_dn[E] = RTd * (toff + nt);
+        a.rw.active[0] = aoff + v[2];
+        a.rw.ngroups[0] = toff + nt;
+    }
+}
+
+// One thread per (token, k): slot = offset[e] + its count index; the token's slots by expert order.
+__global__ void __launch_bounds__(256) k_scatter_big(MoeArgs a, const int* __restrict__ local) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x * 256 + threadIdx.x, K = a.n_used;
+    if (i >= a.T * K) return;
+    const int t = i / K;
+    const int e = a.rw.ids[i];
+    const int slot = a.rw.offsets[e] + local[i];
+    a.rw.slot_token[slot] = t;
+    a.rw.slot_w[slot] = a.rw.wts[i];
+    int rank = 0;
+    for (int j = 0; j < K; j++) rank += a.rw.ids[(size_t)t * K + j] < e;
+    a.rw.token_slots[(size_t)t * K + rank] = slot;
+}
+
+// ------------------------------------------------------------------------------------------------
 // launchers
 // ------------------------------------------------------------------------------------------------
 namespace {
@@ -933,8 +1024,25 @@ cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
+    return launch_moe_combine(a, st);
+}
+
+cudaError_t launch_moe_combine(const MoeArgs& a, cudaStream_t st) {
     const int bx = (a.D / 2 + COMB_NT - 1) / COMB_NT;
-    return launch_pdl(k_moe_combine, dim3(bx, a.T), COMB_NT, 0, st, a);
+    return launch_pdl(k_moe_combine, dim3(bx, a.T), dim3(COMB_NT), 0, st, a);
+}
+
+cudaError_t launch_route_big(const MoeArgs& a, int* cnt, int* local, cudaStream_t st) {
+    if (a.T < 1 || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert) return cudaErrorInvalidValue;
+    const int per = BIG_NT / 32;
+    return launch_pdl(k_route_big, dim3((a.T + per - 1) / per), dim3(BIG_NT), 0, st, a, cnt, local);
+}
+cudaError_t launch_plan_big(const MoeArgs& a, const int* cnt, int* tiles_gu, int* tiles_dn, cudaStream_t st) {
+    if (a.n_expert > 512 || a.FF % 64 || a.D % 128) return cudaErrorInvalidValue;
+    return launch_pdl(k_plan_big, dim3(1), dim3(512), 0, st, a, cnt, tiles_gu, tiles_dn);
+}
+cudaError_t launch_scatter_big(const MoeArgs& a, const int* local, cudaStream_t st) {
+    return launch_pdl(k_scatter_big, dim3((a.T * a.n_used + 255) / 256), dim3(256), 0, st, a, local);
 }
 
 }  // namespace eb

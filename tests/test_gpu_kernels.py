@@ -226,6 +226,38 @@ def test_moe_routing_wide_expert_counts(torch_cuda, orc, E, K):
     assert rel_l2(y - x, yo - x) < 1e-5
 
 
+@pytest.mark.parametrize("T", [256, 333])
+def test_moe_layer_grouped_tensor_core_path(torch_cuda, orc, experts_c2, layer_c2, T):
+    """Ragged batches of >= 256 tokens run as grouped tcgen05 GEMMs over f16-dequantized experts (f16 weight
+    rounding, 2^-12 relative, is the only loss): ids bit-exact, layer output rel-L2 < 5e-4."""
+    ex = experts_c2
+    x = synth.activations(T, 2048, seed=4000 + T)
+    xn = synth.activations(T, 2048, seed=5000 + T)
+    lg = synth.router_logits(T, 128, seed=6000 + T, zipf_bias=1.1)
+    y, ids, w = run_layer(torch_cuda, layer_c2, x, xn, lg)
+    yo, io, wo = orc.moe_layer(x, xn, lg, list(ex.gate), list(ex.up), list(ex.down), ex.types, ex.row_bytes, 8)
+    np.testing.assert_array_equal(ids, io)
+    np.testing.assert_allclose(w, wo, rtol=1e-6, atol=0)
+    assert rel_l2(y - x, yo - x) < 5e-4
+
+
+def test_moe_layer_grouped_mixed_types_and_router(torch_cuda, golden):
+    """The grouped path with Q5_K gate / Q4_K up / Q6_K down and the router matrix, against the oracle."""
+    torch = torch_cuda
+    import oracle
+    mx = synth.expert_set(D=256, FF=256, n_expert=8, types=(13, 12, 14), seed=7, d_sigma=0.002)
+    rw = (synth._rng(19).normal(0, 0.3, (8, 256))).astype(np.float32)
+    layer = eb.MoeLayer.from_expert_set(mx, n_used=2, router=torch.from_numpy(rw).cuda())
+    T = 300
+    x = synth.activations(T, 256, seed=27)
+    xn = synth.activations(T, 256, seed=28)
+    y, ids, w = run_layer(torch, layer, x, xn, None)
+    yo, io, wo = oracle.Oracle().moe_layer(x, xn, None, list(mx.gate), list(mx.up), list(mx.down), mx.types,
+                                           mx.row_bytes, 2, router_w=rw)
+    np.testing.assert_array_equal(ids, io)
+    assert rel_l2(y - x, yo - x) < 5e-4
+
+
 def test_moe_layer_is_deterministic(torch_cuda, layer_c2):
     T = 8
     x = synth.activations(T, 2048, seed=9)
