@@ -449,6 +449,154 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
     return line
 
 
+# ---- ragged workload (config 3) ---------------------------------------------------------------------
+RAGGED_CONFIG = {"workload": "config3: ragged continuous batch through one Qwen3-30B-A3B-shape MoE layer",
+                 "sequences": 64, "tokens_per_sequence": "uniform 1..512", "hidden": D, "experts": E, "top_k": K,
+                 "moe_intermediate": FF, "gate_up": "Q4_K", "down": "Q6_K",
+                 "router_logits": "N(0,1) + log-Zipf(1.1) expert bias",
+                 "l2": "not flushed: each call streams the 391 MB expert set and >1 GB of activations"}
+
+
+def ragged_inputs(step: int, rank: int):
+    import synth
+    counts = synth.ragged_batch(64, 1, 512, seed=3 + 100 * step + rank)
+    T = int(counts.sum())
+    seed = 77 + 1000 * step + 7919 * rank
+    return (T, synth.activations(T, D, seed=seed), synth.activations(T, D, seed=seed + 1),
+            synth.router_logits(T, E, seed=seed + 2, zipf_bias=1.1))
+
+
+def ragged_ours(args, rank: int, world: int, local: int):
+    import torch
+    import eahmmf_b200 as eb
+    import synth
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ex = synth.expert_set()
+    layer = eb.MoeLayer.from_expert_set(ex, n_used=K)
+    nsteps = args.warmup + args.steps
+    inputs = [ragged_inputs(s % 2, rank) for s in range(nsteps)]  # two distinct batches, alternating
+    tmax = max(v[0] for v in inputs)
+    ws = torch.zeros(layer.workspace_bytes(tmax), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    dev_in = [(T, torch.from_numpy(x).to(dev), torch.from_numpy(xn).to(dev), torch.from_numpy(lg).to(dev))
+              for T, x, xn, lg in inputs[:2]]
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    us, toks = [], 0
+    barrier()
+    with Clocks(local) as clk:
+        for s in range(nsteps):
+            T, x, xn, lg = dev_in[s % 2]
+            xo = x.clone()
+            ev0.record(stream)
+            if layer(T, xn, lg, xo, ws, stream=stream, d_status=status):
+                raise RuntimeError("eahmmf_cuda_moe_layer failed")
+            ev1.record(stream)
+            ev1.synchronize()
+            if s >= args.warmup:
+                us.append(ev0.elapsed_time(ev1) * 1e3)
+                toks += T
+        barrier()
+    if int(status.item()):
+        raise RuntimeError(f"kernel status {int(status.item())}")
+    # stage pass: the tensor-core GEMM stages timed on their own (profiler events between the kernels)
+    eb.MoeLayer.profile(True)
+    T, x, xn, lg = dev_in[0]
+    for _ in range(3):
+        layer(T, xn, lg, x.clone(), ws, stream=stream)
+    stages = eb.MoeLayer.profile_read()
+    eb.MoeLayer.profile(False)
+    # end to end: pinned host activations and logits in, the updated residual out
+    T, hx, hxn, hlg = inputs[0]
+    px, pxn, plg = (torch.from_numpy(a).pin_memory() for a in (hx, hxn, hlg))
+    out = torch.empty_like(px).pin_memory()
+    dx, dxn, dlg = (torch.empty(a.shape, dtype=a.dtype, device=dev) for a in (px, pxn, plg))
+    e2e = []
+    for _ in range(3):
+        ev0.record(stream)
+        dx.copy_(px, non_blocking=True)
+        dxn.copy_(pxn, non_blocking=True)
+        dlg.copy_(plg, non_blocking=True)
+        layer(T, dxn, dlg, dx, ws, stream=stream)
+        out.copy_(dx, non_blocking=True)
+        ev1.record(stream)
+        ev1.synchronize()
+        e2e.append(ev0.elapsed_time(ev1) * 1e-3)
+    t_total = float(np.sum(us)) * 1e-6
+    if world > 1:
+        import torch.distributed as dist
+        v = torch.tensor([t_total], dtype=torch.float64, device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        t_total = float(v[0])
+    flops = 2.0 * T * K * 3 * D * FF  # the three projections of every routed slot
+    gemm_us = float(stages[2] + stages[3])
+    achieved = flops / (gemm_us * 1e-6) / 1e12 if gemm_us > 0 else 0.0
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        peak = float(json.load(f).get("bf16_tflops", 1590.0))
+    line = {
+        "metric": "ragged MoE-layer tokens/s (config 3)", "value": toks * world / t_total, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 tcgen05 MMA (weights f16 per-row scaled, activations f16 hi/lo), fp32 accumulate",
+        "data": "synthetic (seeded)", "config": dict(RAGGED_CONFIG, tokens_per_step=toks // args.steps,
+                                                     parallelism=f"replicas x{world}"),
+        "e2e": {"value": T / min(e2e), "unit": "tok/s", "h2d_bytes_per_step": int(T * (2 * D + E) * 4),
+                "d2h_bytes_per_step": int(T * D * 4)},
+        "gpu_launches": 11 * args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "kernel": "k_gemm_tc<gate/up> + k_gemm_tc<down>",
+                     "peak_source": "measured (cuBLAS bf16 burst)",
+                     "timing": "CUDA events around the two GEMM stages (with the h repack between them)"},
+        "stages_us": {"router": float(stages[0]), "route_dequant_pack": float(stages[1]),
+                      "gateup": float(stages[2]), "down_pack_combine": float(stages[3])},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        ref = oracle.Reference(threads=os.cpu_count() or 1)
+        n = 256
+        x, xn, lg = inputs[0][1][:n], inputs[0][2][:n], inputs[0][3][:n]
+        ref.moe_layer(x, xn, lg, list(ex.gate), list(ex.up), list(ex.down), ex.types, ex.row_bytes, K)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 20.0) or reps == 0:
+            ref.moe_layer(x, xn, lg, list(ex.gate), list(ex.up), list(ex.down), ex.types, ex.row_bytes, K)
+            reps += 1
+        v = n * reps / (time.perf_counter() - t0)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": ref.threads, "kind": "reference",
+                                "sample": f"{reps} x {n} tokens of the batch through the reference CPU MoE block "
+                                          "(oracle/_ref, 64-token passes)"}
+    return line
+
+
+def profile_ragged(T: int) -> int:
+    """No timing: three grouped-path calls of the config-2 layer on T ragged tokens (the small case for
+    ncu captures of the tcgen05 GEMMs)."""
+    import torch
+    import eahmmf_b200 as eb
+    import synth
+    ex = synth.expert_set()
+    layer = eb.MoeLayer.from_expert_set(ex, n_used=8)
+    xt = torch.from_numpy(synth.activations(T, ex.D, 5)).cuda()
+    lg = torch.from_numpy(synth.router_logits(T, ex.n_expert, 6, zipf_bias=1.1)).cuda()
+    ws = torch.zeros(layer.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        if layer(T, xt, lg, xt.clone(), ws):
+            raise RuntimeError("eahmmf_cuda_moe_layer failed")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_ragged": T, "ok": True}))
+    return 0
+
+
 def profile_decode(n_layer: int) -> int:
     """No timing: a config-4-shape model with n_layer layers (generated if absent), an 8-token prompt
     in one pass and 4 greedy tokens (3 captured-graph steps). The case ncu captures of the decode
@@ -491,12 +639,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (decode: 128, layer: 20)")
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (decode: 8, layer: 3)")
-    ap.add_argument("--workload", choices=("decode", "layer"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "layer", "ragged"), default="decode")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile-case", type=int, metavar="T", default=0,
                     help="no timing: run the config-2 layer three times at T tokens (a small case for ncu)")
+    ap.add_argument("--profile-ragged", type=int, metavar="T", default=0,
+                    help="no timing: three grouped-path layer calls on T ragged tokens (a small case for ncu)")
     ap.add_argument("--profile-decode", type=int, metavar="LAYERS", default=0,
                     help="no timing: 8-token prompt + 4 greedy tokens on a config-4-shape model of LAYERS layers")
     args = ap.parse_args()
@@ -504,9 +654,11 @@ def main():
         return profile_case(args.profile_case)
     if args.profile_decode:
         return profile_decode(args.profile_decode)
+    if args.profile_ragged:
+        return profile_ragged(args.profile_ragged)
     decode = args.workload == "decode"
     if args.steps is None:
-        args.steps = 128 if decode else 20
+        args.steps = 128 if decode else 5 if args.workload == "ragged" else 20
     if args.warmup is None:
         args.warmup = 8 if decode else 3
     if args.warmup < 3:
@@ -553,7 +705,12 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        line = decode_ours(args, rank, world, local, path) if decode else layer_ours(args, rank, world, local)
+        if decode:
+            line = decode_ours(args, rank, world, local, path)
+        elif args.workload == "ragged":
+            line = ragged_ours(args, rank, world, local)
+        else:
+            line = layer_ours(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
