@@ -597,6 +597,66 @@ def profile_ragged(T: int) -> int:
     return 0
 
 
+# ---- expert-parallel workload (config 5) ---------------------------------------------------------------
+EP_SEQS = 32
+EP_CONFIG = {"workload": "config5: Qwen3-235B-A22B-shape MoE layer, expert-parallel decode step",
+             "hidden": 4096, "experts": 128, "top_k": 8, "moe_intermediate": 1536, "gate_up": "Q4_K", "down": "Q6_K",
+             "sequences": EP_SEQS, "tokens_per_step": EP_SEQS,
+             "l2": "not flushed: the routed experts of a step are ~100 MB per rank and change every step"}
+
+
+def ep_ours(args, rank: int, world: int, local: int):
+    import torch
+    import torch.distributed as dist
+    import ep
+    import synth
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world == 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=0, world_size=1, init_method="tcp://127.0.0.1:" + str(29600 + local),
+                                timeout=timedelta(seconds=120), device_id=dev)
+    ex = synth.expert_set(D=4096, FF=1536, n_expert=128, seed=5, d_sigma=0.002)
+    layer = ep.EpMoeLayer(ex, n_used=8, device=dev)
+    del ex
+    T = EP_SEQS // world + (1 if rank < EP_SEQS % world else 0)
+    nsteps = args.warmup + args.steps
+    xs = [(torch.from_numpy(synth.activations(T, 4096, seed=1000 * s + rank)).to(dev),
+           torch.from_numpy(synth.activations(T, 4096, seed=1000 * s + 500 + rank)).to(dev),
+           torch.from_numpy(synth.router_logits(T, 128, seed=1000 * s + 900 + rank)).to(dev)) for s in range(nsteps)]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    with Clocks(local) as clk:
+        for s in range(nsteps):
+            x, xn, lg = xs[s]
+            xo = x.clone()
+            dist.barrier()
+            ev0.record()
+            layer(xn, lg, xo)
+            ev1.record()
+            ev1.synchronize()
+            if s >= args.warmup:
+                times.append(ev0.elapsed_time(ev1))
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+    t = torch.tensor([float(np.sum(times))], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_ms = float(t[0])
+    value = EP_SEQS * args.steps / (t_ms * 1e-3)
+    line = {"metric": "EP MoE-layer decode tokens/s (config 5, 32 sequences)", "value": value, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "u8/s8 tensor-core MMA, fp32 activations; fp32 rows over NCCL all-to-all",
+            "data": "synthetic (seeded)", "config": dict(EP_CONFIG, parallelism=f"ep{world}"),
+            "clocks": clk.summary(), "gpu_launches": None}
+    if world == 1 and dist.is_initialized():
+        dist.destroy_process_group()
+    return line
+
+
 def profile_decode(n_layer: int) -> int:
     """No timing: a config-4-shape model with n_layer layers (generated if absent), an 8-token prompt
     in one pass and 4 greedy tokens (3 captured-graph steps). The case ncu captures of the decode
@@ -639,7 +699,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (decode: 128, layer: 20)")
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (decode: 8, layer: 3)")
-    ap.add_argument("--workload", choices=("decode", "layer", "ragged"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "layer", "ragged", "ep"), default="decode")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -709,6 +769,8 @@ def main():
             line = decode_ours(args, rank, world, local, path)
         elif args.workload == "ragged":
             line = ragged_ours(args, rank, world, local)
+        elif args.workload == "ep":
+            line = ep_ours(args, rank, world, local)
         else:
             line = layer_ours(args, rank, world, local)
     finally:

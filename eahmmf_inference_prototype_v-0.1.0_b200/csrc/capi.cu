@@ -176,10 +176,11 @@ WsLayout ws_layout(const EahmmfMoeLayer* L, int T) {
     w.total = o;
     return w;
 }
-// Tokens per call from which the block runs as grouped tensor-core GEMMs (gemm.cu): every active
-// expert's weights are dequantized once to f16 and each expert's slots are one dense contraction,
-// instead of 64-token passes that each stream the routed experts again.
+// The block runs as grouped tensor-core GEMMs (gemm.cu) from 256 tokens per call when the slots average
+// at least 16 per expert: every active expert's weights are dequantized once to f16 and each expert's
+// slots are one dense contraction, instead of 64-token passes that each stream the routed experts again.
 constexpr int GROUPED_MIN_T = 256;
+constexpr int GROUPED_MIN_SLOTS_PER_EXPERT = 16;
 struct GroupedLayout {
     size_t ids, wts, logits, offsets, active, ngroups, cnt, local, tiles_gu, tiles_dn, slot_token, slot_w,
         token_slots, wf, rs, xhi, xlo, xscale, h, hhi, hlo, hscale, y, total;
@@ -218,7 +219,10 @@ GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
     w.total = o;
     return w;
 }
-bool grouped_ok(const EahmmfMoeLayer* L, int T) { return T >= GROUPED_MIN_T && L->D % 128 == 0 && L->FF % 64 == 0; }
+bool grouped_ok(const EahmmfMoeLayer* L, int T) {
+    return T >= GROUPED_MIN_T && (long long)T * L->n_used >= (long long)GROUPED_MIN_SLOTS_PER_EXPERT * L->n_expert &&
+           L->D % 128 == 0 && L->FF % 64 == 0;
+}
 
 bool layer_ok(const EahmmfMoeLayer* L) {
     return L && L->n_expert > 0 && L->n_expert <= MAX_EXPERTS && L->n_used > 0 && L->n_used <= 32 &&
@@ -452,6 +456,36 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
         if (!g_prof.collect()) return ST_CUDA;
     }
     return ST_OK;
+}
+
+extern "C" int eahmmf_cuda_route_topk(const float* d_logits, int T, int E, int K, int* d_ids, float* d_w, void* stream,
+                                      int* d_status) {
+    if (!d_logits || !d_ids || !d_w || T < 1 || E < 1 || E > MAX_EXPERTS || K < 1 || K > 32 || K > E) return ST_BAD_ARG;
+    MoeArgs a{};
+    a.logits = d_logits;
+    a.T = T;
+    a.n_expert = E;
+    a.n_used = K;
+    a.rw.ids = d_ids;
+    a.rw.wts = d_w;
+    a.status = d_status;
+    return launch_route_big(a, nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? ST_OK
+                                                                                                      : ST_CUDA;
+}
+
+extern "C" int eahmmf_cuda_moe_combine(int T, int K, int D, const int* d_token_slots, const float* d_slot_w,
+                                       const float* d_y, float* d_x, void* stream) {
+    if (T < 1 || K < 1 || K > 32 || D < 2 || D % 2 || !d_token_slots || !d_slot_w || !d_y || !d_x) return ST_BAD_ARG;
+    if ((reinterpret_cast<uintptr_t>(d_y) | reinterpret_cast<uintptr_t>(d_x)) & 7) return ST_BAD_ARG;
+    MoeArgs a{};
+    a.T = T;
+    a.n_used = K;
+    a.D = D;
+    a.rw.token_slots = const_cast<int*>(d_token_slots);
+    a.rw.slot_w = const_cast<float*>(d_slot_w);
+    a.y = const_cast<float*>(d_y);
+    a.x = d_x;
+    return launch_moe_combine(a, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? ST_OK : ST_CUDA;
 }
 
 extern "C" size_t eahmmf_cuda_gemv_workspace_bytes(int ne0) { return ne0 > 0 ? gemv_ws_bytes(ne0) : 0; }

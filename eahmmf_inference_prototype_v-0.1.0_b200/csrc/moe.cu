@@ -886,7 +886,7 @@ __global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict
         }
         a.rw.ids[(size_t)t * K + lane] = my_e;
         a.rw.wts[(size_t)t * K + lane] = my_w;
-        local[(size_t)t * K + lane] = atomicAdd(&cnt[my_e], 1);
+        if (cnt) local[(size_t)t * K + lane] = atomicAdd(&cnt[my_e], 1);
     }
 }
 
@@ -935,6 +935,7 @@ __global__ void __launch_bounds__(512) k_plan_big(MoeArgs a, const int* __restri
 }
 
 // One thread per (token, k): slot = offset[e] + its count index; the token's slots by expert order.
+// (cnt / local may be null for routing alone.)
 __global__ void __launch_bounds__(256) k_scatter_big(MoeArgs a, const int* __restrict__ local) {
     pdl_trigger();
     pdl_wait();

@@ -54,6 +54,10 @@ EXPORTS = {
     "eahmmf_dev_free_memory": (C.c_size_t, [C.c_void_p]),
     "eahmmf_dev_stream": (C.c_void_p, [C.c_void_p]),
     "eahmmf_dev_inject_fault": (None, [C.c_void_p, C.c_int, C.c_int]),
+    "eahmmf_cuda_route_topk": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p]),
+    "eahmmf_cuda_moe_combine": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_void_p]),
     "eahmmf_engine_load": (C.c_void_p, [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]),
     "eahmmf_engine_free": (None, [C.c_void_p]),
     "eahmmf_engine_dims": (C.c_int, [C.c_void_p, C.c_void_p]),
@@ -283,3 +287,25 @@ class Engine:
         w = np.zeros(n, np.float32)
         L.eahmmf_engine_trace_get(self._h, ids.ctypes.data, w.ctypes.data, n)
         return ids, w
+
+
+def route_topk(d_logits, K: int, stream=None, d_status=None):
+    """Top-k routing of device logits [T x E] (eahmmf_cuda_route_topk): (ids [T x K] int32, weights
+    [T x K] fp32) on the same device, rank order."""
+    import torch
+    T, E = d_logits.shape
+    ids = torch.empty((T, K), dtype=torch.int32, device=d_logits.device)
+    w = torch.empty((T, K), dtype=torch.float32, device=d_logits.device)
+    rc = lib().eahmmf_cuda_route_topk(_ptr(d_logits), T, E, K, _ptr(ids), _ptr(w), _stream(stream),
+                                      _ptr(d_status) if d_status is not None else None)
+    if rc:
+        raise RuntimeError(f"eahmmf_cuda_route_topk returned {rc}")
+    return ids, w
+
+
+def moe_combine(d_token_slots, d_slot_w, d_y, d_x, stream=None) -> int:
+    """d_x[t] += sum_k w[s] y[s] over token t's slots s (ascending expert order), eahmmf_cuda_moe_combine."""
+    T, D = d_x.shape
+    K = d_token_slots.numel() // T
+    return lib().eahmmf_cuda_moe_combine(T, K, D, _ptr(d_token_slots), _ptr(d_slot_w), _ptr(d_y), _ptr(d_x),
+                                         _stream(stream))

@@ -93,6 +93,18 @@ size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
 int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                           void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);
 
+/* The routing step alone (qwen3moe.cpp:1011-1023): per token, softmax numerators, top-k by
+ * (r desc, index asc), weights renormalised over the k, ids bit-exact with the CPU path. d_logits
+ * [T x E], d_ids / d_w [T x K] in rank order. Used by the expert-parallel layer to dispatch tokens. */
+int eahmmf_cuda_route_topk(const float* d_logits, int T, int E, int K, int* d_ids, float* d_w, void* stream,
+                           int* d_status);
+
+/* The weighted combine alone (qwen3moe.cpp:1024, :1062-1069): d_x[t] += sum over k of
+ * d_slot_w[s] * d_y[s] for the K slots s = d_token_slots[t*K + k], which must be listed in ascending
+ * expert order (the reference's summation order). d_y [slots x D]; d_x [T x D]; D even, 8-byte aligned. */
+int eahmmf_cuda_moe_combine(int T, int K, int D, const int* d_token_slots, const float* d_slot_w, const float* d_y,
+                            float* d_x, void* stream);
+
 /* Stage timing of eahmmf_cuda_moe_layer: when enabled, each call records CUDA events on its stream
  * around its four stages (router GEMV, routing + activation prep, gate/up, down + combine) of every
  * 64-token block and waits for them; eahmmf_cuda_moe_profile_read returns the mean stage durations (us)
