@@ -387,9 +387,11 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
 }
 }  // namespace
 
-extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits,
-                                     float* d_x, void* d_workspace, size_t workspace_bytes, void* stream,
-                                     int* d_status) {
+namespace eb {
+// eahmmf_cuda_moe_layer with an optional deferred combine (engine use): when `defer` is set and the call
+// runs as one 64-token pass, the combine is not launched and defer receives what it needs.
+int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
+                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer) {
     if (!layer_ok(L)) return (L && !(is_kquant(L->gate_type) && is_kquant(L->up_type) && is_kquant(L->down_type)))
                                   ? ST_BAD_TYPE
                                   : ST_BAD_ARG;
@@ -451,11 +453,26 @@ extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float
         g_prof.mark(2, st);
         if (launch_moe_gateup(a, st) != cudaSuccess) return ST_CUDA;
         g_prof.mark(3, st);
-        if (launch_moe_down(a, st) != cudaSuccess) return ST_CUDA;
+        const bool deferred = defer && T <= CHUNK;
+        if (launch_moe_down(a, st, !deferred) != cudaSuccess) return ST_CUDA;
+        if (deferred) {
+            defer->token_slots = a.rw.token_slots;
+            defer->slot_w = a.rw.slot_w;
+            defer->y = a.y;
+            defer->K = K;
+        }
         g_prof.mark(4, st);
         if (!g_prof.collect()) return ST_CUDA;
     }
     return ST_OK;
+}
+
+}  // namespace eb
+
+extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits,
+                                     float* d_x, void* d_workspace, size_t workspace_bytes, void* stream,
+                                     int* d_status) {
+    return moe_layer_run(L, T, d_xn, d_logits, d_x, d_workspace, workspace_bytes, stream, d_status, nullptr);
 }
 
 extern "C" int eahmmf_cuda_route_topk(const float* d_logits, int T, int E, int K, int* d_ids, float* d_w, void* stream,

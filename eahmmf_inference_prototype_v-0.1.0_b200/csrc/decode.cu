@@ -13,6 +13,7 @@
 #include <math.h>
 
 #include "decode.cuh"
+#include "kq.cuh"
 
 namespace eb {
 
@@ -109,6 +110,62 @@ __global__ void __launch_bounds__(NORM_NT) k_rmsnorm(const float* __restrict__ x
     const float sc = 1.0f / sqrtf(ss / (float)n + eps);
     float* o = out + (size_t)blockIdx.x * ldo;
     for (int i = threadIdx.x; i < n; i += NORM_NT) o[i] = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+}
+
+// ---- fused: [combine of the previous MoE block] + RMSNorm + activation prep, one CTA per token row
+// x[t] += sum_k w_k y[slot_k] (ascending expert order, as k_moe_combine), then xn = x * (1 / sqrtf(
+// mean(x^2) + eps)) * w (qwen3moe.cpp:527-532), then xn in fragment form (XF) for the next GEMV and,
+// optionally, xn itself. The row stays in shared memory between the steps.
+constexpr int NP_NT = 1024;  // one thread per element pair of a 2048-wide row: every load in flight at once
+__global__ void __launch_bounds__(NP_NT) k_norm_prep(NormPrepArgs a) {
+    extern __shared__ __align__(16) float row[];  // [n]
+    __shared__ float red[33];
+    __shared__ int s_sl[32];
+    __shared__ float s_w[32];
+    pdl_trigger();
+    pdl_wait();
+    const int t = a.t0 + blockIdx.x, n = a.n, tid = threadIdx.x;
+    float* xr = a.x + (size_t)t * a.ldx;
+    if (a.y) {
+        if (tid < a.K) {
+            const int sl = a.token_slots[t * a.K + tid];
+            s_sl[tid] = sl;
+            s_w[tid] = a.slot_w[sl];
+        }
+        __syncthreads();
+        for (int i = 2 * tid; i < n; i += 2 * NP_NT) {
+            float2 acc = make_float2(0.f, 0.f);
+#pragma unroll 8
+            for (int k = 0; k < a.K; k++) {
+                const float2 v = *reinterpret_cast<const float2*>(a.y + (size_t)s_sl[k] * n + i);
+                acc.x = fmaf(s_w[k], v.x, acc.x);
+                acc.y = fmaf(s_w[k], v.y, acc.y);
+            }
+            float2 xv = *reinterpret_cast<const float2*>(xr + i);
+            xv.x += acc.x;
+            xv.y += acc.y;
+            *reinterpret_cast<float2*>(xr + i) = xv;
+            row[i] = xv.x;
+            row[i + 1] = xv.y;
+        }
+    } else {
+        for (int i = tid; i < n; i += NP_NT) row[i] = xr[i];
+    }
+    __syncthreads();
+    float ss = 0.f;
+    for (int i = tid; i < n; i += NP_NT) ss = fmaf(row[i], row[i], ss);
+    ss = block_sum<NP_NT>(ss, red);
+    const float sc = 1.0f / sqrtf(ss / (float)n + a.eps);
+    for (int i = tid; i < n; i += NP_NT) {
+        const float v = __fmul_rn(__fmul_rn(row[i], sc), a.w[i]);
+        row[i] = v;
+        if (a.xn) a.xn[(size_t)blockIdx.x * n + i] = v;
+    }
+    __syncthreads();
+    const int r = blockIdx.x;  // XF row
+    prep_row(row, n, const_cast<uint2*>(a.xf.frag) + (size_t)r * (n >> 5) * 12,
+             const_cast<float*>(a.xf.sum) + (size_t)r * ((n >> 4) + XF_SUM_PAD),
+             const_cast<uint8_t*>(a.xf.gs) + (size_t)r * xf_gs_bytes(n), red);
 }
 
 // ---- rotary table: cos/sin of (p0 + t) * inv_freq[i] in double, rounded to float (qwen3moe.cpp:937-943)
@@ -420,6 +477,19 @@ cudaError_t launch_embed(const uint8_t* W, int type, size_t rb, int D, int n_row
 cudaError_t launch_rmsnorm(const float* x, int ldx, const float* w, float* out, int ldo, int rows, int n, float eps,
                            cudaStream_t s) {
     return launch_pdl(k_rmsnorm, dim3(rows), dim3(NORM_NT), 0, s, x, ldx, w, out, ldo, n, eps);
+}
+cudaError_t launch_norm_prep(const NormPrepArgs& a, int rows, cudaStream_t s) {
+    if (rows < 1 || a.n % 256 || (a.y && (a.K < 1 || a.K > 32))) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)a.n * 4;
+    if (smem > 48 * 1024) {
+        static size_t cur = 0;
+        if (smem > cur) {
+            cudaError_t e = cudaFuncSetAttribute(k_norm_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            cur = smem;
+        }
+    }
+    return launch_pdl(k_norm_prep, dim3(rows), dim3(NP_NT), smem, s, a);
 }
 cudaError_t launch_rope_table(const DecodeState* st, const float* inv_freq, int half, int nb, float2* cs,
                               cudaStream_t s) {

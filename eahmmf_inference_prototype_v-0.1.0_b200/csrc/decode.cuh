@@ -27,6 +27,22 @@ struct DecodeState {
     int* out;     // [cap_out] generated tokens
 };
 
+// Arguments of k_norm_prep: rows t0 .. t0 + rows - 1 of x (row length n, stride ldx); when y is set,
+// first x[t] += sum_k slot_w[s] y[s] over s = token_slots[t*K + k]; then RMSNorm with w, eps; the
+// normalised rows (XF row r = t - t0) go to xf and, when xn is set, to xn[r * n].
+struct NormPrepArgs {
+    float* x;
+    int ldx, n, t0;
+    const float* w;
+    float eps;
+    const float* y;
+    const int* token_slots;
+    const float* slot_w;
+    int K;
+    XF xf;
+    float* xn;
+};
+cudaError_t launch_norm_prep(const NormPrepArgs& a, int rows, cudaStream_t s);
 cudaError_t launch_embed(const uint8_t* W, int type, size_t rb, int D, int n_rows, const int* toks, int nb, float* x,
                          int* status, cudaStream_t s);
 cudaError_t launch_rmsnorm(const float* x, int ldx, const float* w, float* out, int ldo, int rows, int n, float eps,

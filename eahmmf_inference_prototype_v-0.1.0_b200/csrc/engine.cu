@@ -30,7 +30,12 @@
 #include "../../include/eahmmf_b200.h"
 #include "common.cuh"
 #include "decode.cuh"
+#include "kernels.cuh"
 
+namespace eb {
+int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
+                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer);
+}
 using namespace eb;
 
 namespace {
@@ -262,6 +267,7 @@ struct EahmmfEngine {
     float2 *rope_cs = nullptr, *amax_blk = nullptr;
     int amax_nblk = 0;
     void *moe_ws = nullptr, *gemv_ws = nullptr;
+    void* xf_rows = nullptr;  // [MAXB rows of D] normalised activations in fragment form
     size_t moe_ws_bytes = 0, gemv_ws_bytes = 0;
     int* toks = nullptr;       // device token staging [MAXB]
     int* h_toks = nullptr;     // pinned [MAXB]
@@ -468,7 +474,7 @@ struct EahmmfEngine {
             !dalloc(attn_part, (size_t)MAXB * n_head * std::min(nsplit_max, 128) * (hd + 2) * 4) ||
             !dalloc(amax_blk, (size_t)amax_nblk * 8) || !dalloc(moe_ws, moe_ws_bytes) ||
             !dalloc(gemv_ws, gemv_ws_bytes) || !dalloc(toks, MAXB * 4) || !dalloc(status, 4) ||
-            !dalloc(attn_cnt, (size_t)MAXB * n_kv * 4) ||
+            !dalloc(attn_cnt, (size_t)MAXB * n_kv * 4) || !dalloc(xf_rows, xf_bytes(MAXB, D)) ||
             !dalloc(state, sizeof(DecodeState)))
             return fail("cannot allocate activations / KV cache");
         if (cudaMemset(kc, 0, kvn * 4) != cudaSuccess || cudaMemset(vc, 0, kvn * 4) != cudaSuccess ||
@@ -570,21 +576,60 @@ struct EahmmfEngine {
             return ST_CUDA;
         if (!mark(0)) return ST_CUDA;
         const int ldq = QD + 2 * KD;
+        const XF xf_all = xf_carve(xf_rows, MAXB, D);
+        auto xf_row = [&](int t0) {  // XF view starting at row t0 of xf_all
+            XF v = xf_all;
+            v.frag += (size_t)t0 * (D >> 5) * 12;
+            v.sum += (size_t)t0 * ((D >> 4) + XF_SUM_PAD);
+            v.gs += (size_t)t0 * xf_gs_bytes(D);
+            return v;
+        };
+        // GEMV of a matrix with K = D over the rows prepared in xf_all (tensor-core path), or over xn
+        auto gemv_d = [&](const uint8_t* w, int type, int rows, size_t rb, float* out, int ldo) -> int {
+            const QMat W{w, type, D, rows, rb};
+            if (!gemv_mma_ok(W))
+                return eahmmf_cuda_gemv(w, type, D, rows, rb, xn, nb, D, out, ldo, 0, gemv_ws, gemv_ws_bytes, st);
+            for (int t0 = 0; t0 < nb; t0 += XPASS) {
+                GemvXArgs g{};
+                g.W = W;
+                g.xf = xf_row(t0);
+                g.m = std::min(XPASS, nb - t0);
+                g.Y = out + (size_t)t0 * ldo;
+                g.ldy = ldo;
+                g.accumulate = 0;
+                g.status = status;
+                if (launch_gemv_xf(g, st) != cudaSuccess) return ST_CUDA;
+            }
+            return ST_OK;
+        };
+        MoeDeferred pending;  // combine of the previous layer's MoE block, fused into the next norm
         for (int l = 0; l < n_layer; l++) {
             const Layer& L = layers[l];
             float* lk = kc + (size_t)l * n_ctx * KD;
             float* lv = vc + (size_t)l * n_ctx * KD;
-            if (launch_rmsnorm(x, D, L.attn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(1)) return ST_CUDA;
+            NormPrepArgs na{};
+            na.x = x;
+            na.ldx = D;
+            na.n = D;
+            na.t0 = 0;
+            na.w = L.attn_norm;
+            na.eps = eps;
+            na.y = pending.y;
+            na.token_slots = pending.token_slots;
+            na.slot_w = pending.slot_w;
+            na.K = pending.K;
+            na.xf = xf_all;
+            na.xn = xn;
+            if (launch_norm_prep(na, nb, st) != cudaSuccess || !mark(1)) return ST_CUDA;
+            pending = MoeDeferred{};
             int rc;
             if (L.fused) {
-                rc = eahmmf_cuda_gemv(L.wq[0], L.qkv_type[0], D, ldq, L.qkv_rb[0], xn, nb, D, qkv, ldq, 0, gemv_ws,
-                                      gemv_ws_bytes, st);
+                rc = gemv_d(L.wq[0], L.qkv_type[0], ldq, L.qkv_rb[0], qkv, ldq);
             } else {
                 const int rows[3] = {QD, KD, KD}, col[3] = {0, QD, QD + KD};
                 rc = ST_OK;
                 for (int c = 0; c < 3 && rc == ST_OK; c++)
-                    rc = eahmmf_cuda_gemv(L.wq[c], L.qkv_type[c], D, rows[c], L.qkv_rb[c], xn, nb, D, qkv + col[c],
-                                          ldq, 0, gemv_ws, gemv_ws_bytes, st);
+                    rc = gemv_d(L.wq[c], L.qkv_type[c], rows[c], L.qkv_rb[c], qkv + col[c], ldq);
             }
             if (rc != ST_OK || !mark(2)) return rc != ST_OK ? rc : ST_CUDA;
             if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, state, nb, q, lk, lv,
@@ -597,7 +642,7 @@ struct EahmmfEngine {
             rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes, st);
             if (rc != ST_OK || !mark(5)) return rc != ST_OK ? rc : ST_CUDA;
             if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(6)) return ST_CUDA;
-            rc = eahmmf_cuda_moe_layer(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status);
+            rc = moe_layer_run(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending);
             if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
             if (trace) {  // routing of this layer (ids, then weights, at the head of the MoE workspace)
                 const size_t nk = (size_t)nb * n_used;
@@ -613,11 +658,25 @@ struct EahmmfEngine {
                 trace_w.insert(trace_w.end(), h_w.begin(), h_w.end());
             }
         }
-        if (want_logits) {
-            if (launch_rmsnorm(x + (size_t)(nb - 1) * D, D, out_norm, xn, D, 1, D, eps, st) != cudaSuccess)
-                return ST_CUDA;
-            const int rc = eahmmf_cuda_gemv(out_w, out_type, D, n_vocab, out_rb, xn, 1, D, logits, n_vocab, 0, gemv_ws,
-                                            gemv_ws_bytes, st);
+        if (want_logits) {  // last row: the pending combine, the output norm, the output GEMV
+            NormPrepArgs na{};
+            na.x = x;
+            na.ldx = D;
+            na.n = D;
+            na.t0 = nb - 1;
+            na.w = out_norm;
+            na.eps = eps;
+            na.y = pending.y;
+            na.token_slots = pending.token_slots;
+            na.slot_w = pending.slot_w;
+            na.K = pending.K;
+            na.xf = xf_all;
+            na.xn = xn;
+            if (launch_norm_prep(na, 1, st) != cudaSuccess) return ST_CUDA;
+            const int save_nb = nb;
+            nb = 1;  // gemv_d over the single prepared row
+            const int rc = gemv_d(out_w, out_type, n_vocab, out_rb, logits, n_vocab);
+            nb = save_nb;
             if (rc != ST_OK || !mark(8)) return rc != ST_OK ? rc : ST_CUDA;
         }
         return ST_OK;

@@ -117,6 +117,14 @@ struct GroupedArgs {
     int* status;
 };
 
+// The combine inputs of a MoE pass whose combine the caller performs itself.
+struct MoeDeferred {
+    const int* token_slots = nullptr;  // [T*K] slots of each token, ascending expert order
+    const float* slot_w = nullptr;     // routing weight of each slot
+    const float* y = nullptr;          // [slots x D] expert outputs
+    int K = 0;
+};
+
 int sm_count();
 bool gemv_mma_ok(const QMat& W);                 // tensor-core path available for this matrix
 // bytes of an XF block of `rows` rows: digits (3 bytes per element), per row the per-16 sums and the
@@ -132,7 +140,9 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st);  // per-row kernel 
 // the last three are launched with programmatic stream serialization.
 cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st);
-cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st);
+// combine = false leaves y, token_slots and slot_w for the caller to combine (engine: fused into the next
+// RMSNorm)
+cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st, bool combine = true);
 size_t moe_smem_gateup(int D, size_t rbg, size_t rbu);
 size_t moe_smem_down(int FF, size_t rbd);
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st);

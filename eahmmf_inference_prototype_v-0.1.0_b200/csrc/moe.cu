@@ -1015,7 +1015,7 @@ static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
     const int units = max_groups(a) * (a.D / DN_ROWS);
     return launch_pdl(k_moe_down<QD>, dim3(std::min(sm_count(), units)), (NWC_DN + 1) * 32, pl.total, st, a);
 }
-cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {
+cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st, bool combine) {
     if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX) return cudaErrorInvalidValue;
     cudaError_t e;
     switch (a.down_type) {
@@ -1024,7 +1024,7 @@ cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st) {
         case T_Q6_K: e = down_as<T_Q6_K>(a, st); break;
         default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || !combine) return e;
     return launch_moe_combine(a, st);
 }
 
