@@ -183,7 +183,7 @@ constexpr int GROUPED_MIN_T = 256;
 constexpr int GROUPED_MIN_SLOTS_PER_EXPERT = 16;
 struct GroupedLayout {
     size_t ids, wts, logits, offsets, active, ngroups, cnt, local, tiles_gu, tiles_dn, slot_token, slot_w,
-        token_slots, wf, rs, xhi, xlo, xscale, h, hhi, hlo, hscale, y, total;
+        token_slots, wf, rs, bhi, bscale, h, y, total;
 };
 GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
     const size_t K = (size_t)L->n_used, E = (size_t)L->n_expert, S = (size_t)T * K, D = L->D, FF = L->FF;
@@ -208,13 +208,11 @@ GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
     take(w.token_slots, S * 4);
     take(w.wf, E * 3 * FF * D * 2);
     take(w.rs, E * (2 * FF + D) * 4);
-    take(w.xhi, (size_t)T * D * 2);
-    take(w.xlo, (size_t)T * D * 2);
-    take(w.xscale, (size_t)T * 4);
+    const size_t tiles = S / 128 + E + 1;  // bound on sum over experts of ceil(m_e / 128)
+    const size_t kmax = D > FF ? D : FF;
+    take(w.bhi, tiles * 128 * kmax * 2);
+    take(w.bscale, S * 4);
     take(w.h, S * FF * 4);
-    take(w.hhi, S * FF * 2);
-    take(w.hlo, S * FF * 2);
-    take(w.hscale, S * 4);
     take(w.y, S * D * 4);
     w.total = o;
     return w;
@@ -349,13 +347,10 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g.w_off[1] = (size_t)L->FF * L->D;
     g.w_off[2] = (size_t)2 * L->FF * L->D;
     g.rs = reinterpret_cast<float*>(ws + w.rs);
-    g.xhi = reinterpret_cast<const __half*>(ws + w.xhi);
-    g.xlo = reinterpret_cast<const __half*>(ws + w.xlo);
-    g.xscale = reinterpret_cast<const float*>(ws + w.xscale);
+    g.xn = d_xn;
     g.h = reinterpret_cast<float*>(ws + w.h);
-    g.hhi = reinterpret_cast<const __half*>(ws + w.hhi);
-    g.hlo = reinterpret_cast<const __half*>(ws + w.hlo);
-    g.hscale = reinterpret_cast<const float*>(ws + w.hscale);
+    g.bhi = reinterpret_cast<__half*>(ws + w.bhi);
+    g.bscale = reinterpret_cast<float*>(ws + w.bscale);
     g.y = a.y;
     g.status = d_status;
     g_prof.mark(0, st);
@@ -369,16 +364,13 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g_prof.mark(1, st);
     if (cudaMemsetAsync(cnt, 0, (size_t)E * 4, st) != cudaSuccess || launch_route_big(a, cnt, local, st) != cudaSuccess ||
         launch_plan_big(a, cnt, tiles_gu, tiles_dn, st) != cudaSuccess || launch_scatter_big(a, local, st) != cudaSuccess ||
-        launch_grouped_dequant(g, st) != cudaSuccess ||
-        launch_pack_f16(d_xn, T, L->D, const_cast<__half*>(g.xhi), const_cast<__half*>(g.xlo),
-                        const_cast<float*>(g.xscale), st) != cudaSuccess)
+        launch_grouped_dequant(g, st) != cudaSuccess || launch_pack_slots(g, 0, S, st) != cudaSuccess)
         return ST_CUDA;
     g_prof.mark(2, st);
     const int slot_tiles = (S + 127) / 128 + E;  // bound on sum over experts of ceil(m_e / 128)
     if (launch_grouped_gemm(g, 0, (L->FF / 64) * slot_tiles, st) != cudaSuccess) return ST_CUDA;
     g_prof.mark(3, st);
-    if (launch_pack_f16(g.h, S, L->FF, const_cast<__half*>(g.hhi), const_cast<__half*>(g.hlo),
-                        const_cast<float*>(g.hscale), st) != cudaSuccess ||
+    if (launch_pack_slots(g, 1, S, st) != cudaSuccess ||
         launch_grouped_gemm(g, 1, (L->D / 128) * slot_tiles, st) != cudaSuccess || launch_moe_combine(a, st) != cudaSuccess)
         return ST_CUDA;
     g_prof.mark(4, st);

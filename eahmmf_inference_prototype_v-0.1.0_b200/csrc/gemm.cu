@@ -4,17 +4,22 @@
 //   1. k_dequant_f16: every active expert's gate/up/down rows dequantized once (the reference decoders,
 //      qwen3moe.cpp:142-202, exact fp32) and stored as f16 scaled by a per-row power of two, so that
 //      the f16 rounding (2^-12 relative) is the only loss.
-//   2. k_pack_f16: activation rows (tokens for gate/up, slots for down) as a per-row power-of-two
-//      scale and an f16 hi/lo pair, x/s = hi + lo to ~2^-22.
-//   3. k_gemm_tc<GATEUP>: tiles of (expert, 64 gate rows + the same 64 up rows, 128 slots); the K loop
-//      stages W and both activation halves in shared memory (cp.async, two stages) as K-major core
-//      matrices; one thread issues tcgen05.mma (M 128, N 128, K 16, f16 in, fp32 accumulate in tensor
-//      memory) for hi and lo into the same accumulator and commits to an mbarrier; the epilogue reads
-//      the accumulator with tcgen05.ld, pairs gate and up rows through shared memory and writes
-//      h = SiLU(g) * u (qwen3moe.cpp:1056-1059) per slot.
+//   2. k_pack_slots: each slot's activation row (its token's xn for gate/up, its h for down) as a
+//      power-of-two scale and f16 values of x/s (2^-12 relative rounding, like the weights).
+//   Both are written tile-major in the tensor cores' K-major core-matrix order (8 rows x 16 bytes), so
+//   that one 64-element K stage of a 128-row tile is one contiguous 16 KB block: a single bulk copy.
+//   3. k_gemm_tc<GATEUP>: persistent, warp-specialised. Tiles are (expert, 64 gate rows + the same 64 up
+//      rows, 128 slots). A producer lane streams (W, activations) stage blocks into a 6-deep shared-
+//      memory ring (1-D bulk copies, mbarrier complete_tx); one lane issues tcgen05.mma (M 128, N 128,
+//      K 16, f16 in, fp32 accumulate in tensor memory) and commits each stage back to the producer; two
+//      accumulators in tensor memory let
+//      four epilogue warps read tile i (tcgen05.ld) while tile i+1 accumulates. The epilogue pairs
+//      gate and up rows through shared memory and writes h = SiLU(g) * u (qwen3moe.cpp:1056-1059).
 //   4. k_gemm_tc<DOWN>: tiles of (expert, 128 rows of D, 128 slots) over h, writing y per slot; the
 //      weighted combine in expert order is k_moe_combine (moe.cu).
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "kernels.cuh"
 #include "tc.cuh"
@@ -75,6 +80,36 @@ __device__ void dq8(const uint8_t* row, int type, int i, float (&y)[8]) {
         for (int j = 0; j < 8; j++) y[j] = reinterpret_cast<const float*>(row)[i + j];
     }
 }
+// The same for Q4_K / Q5_K rows on an 8-byte boundary: word loads of the header and of the 8 quant bytes.
+__device__ void dq8_k45(const uint8_t* row, bool q5, int i, float (&y)[8]) {
+    const uint8_t* b = row + (i >> 8) * (q5 ? 176 : 144);
+    const int e = i & 255, c = e >> 6, hi = (e >> 5) & 1, l0 = e & 31, j = 2 * c + hi;
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(b);
+    const uint32_t s0 = *reinterpret_cast<const uint32_t*>(b + 4), s1 = *reinterpret_cast<const uint32_t*>(b + 8),
+                   s2 = *reinterpret_cast<const uint32_t*>(b + 12);
+    // 6-bit scale / min j from the 12 header bytes (scale_min_k4, qwen3moe.cpp:133-141)
+    auto byte = [&](int k) -> int { return (int)(((k < 4 ? s0 : k < 8 ? s1 : s2) >> (8 * (k & 3))) & 0xff); };
+    int sc, mn;
+    if (j < 4) {
+        sc = byte(j) & 63;
+        mn = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 0x0f) | ((byte(j - 4) >> 6) << 4);
+        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(dd & 0xffff))) * (float)sc;
+    const float o = __half2float(__ushort_as_half((unsigned short)(dd >> 16))) * (float)mn;
+    const uint2 qw = *reinterpret_cast<const uint2*>(b + (q5 ? 48 : 16) + 32 * c + l0);
+    uint2 hw = make_uint2(0u, 0u);
+    if (q5) hw = *reinterpret_cast<const uint2*>(b + 16 + l0);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t qb = ((k < 4 ? qw.x : qw.y) >> (8 * (k & 3))) & 0xff;
+        int q = hi ? (int)(qb >> 4) : (int)(qb & 0x0f);
+        if (q5) q += (int)((((k < 4 ? hw.x : hw.y) >> (8 * (k & 3))) >> j) & 1) << 4;
+        y[k] = d * (float)q - o;
+    }
+}
 // power-of-two scale that brings max|x| into [2^13, 2^14) (1 for an all-zero row)
 __device__ __forceinline__ float pow2_scale(float m) {
     if (!(m > 0.f) || !isfinite(m)) return 1.f;
@@ -89,7 +124,15 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 }  // namespace
 
-// ---- 1. expert weights -> scaled f16, one warp per row of an active expert
+// Tile-major core-matrix offset (elements) of element (r, k) of a 128-row tile whose K stages are
+// consecutive 128 x 64 blocks: stage k / 64, then core matrix (r / 8, (k % 64) / 8), row r % 8.
+__device__ __forceinline__ size_t tile_off(int r, int k) {
+    return (size_t)(k >> 6) * (128 * 64) + (size_t)(((r >> 3) * 8 + ((k & 63) >> 3)) * 64 + (r & 7) * 8 + (k & 7));
+}
+
+// ---- 1. expert weights -> scaled f16, tile-major; one warp per row of an active expert
+// Per expert: gate/up tiles (FF/64 of them, A rows 0..63 = gate rows 64 rt.., 64..127 = the same up rows,
+// D/64 stages), then down tiles (D/128, FF/64 stages).
 __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
     pdl_trigger();
     pdl_wait();
@@ -104,229 +147,265 @@ __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
     const int K = c == 2 ? g.FF : g.D;
     const uint8_t* src = g.w[c][e] + (size_t)row * g.rb[c];
     const int type = g.type[c];
+    const bool fast = (type == T_Q4_K || type == T_Q5_K) && (reinterpret_cast<uintptr_t>(src) & 7) == 0;
+    auto deq = [&](int i, float (&y)[8]) {
+        if (fast) dq8_k45(src, type == T_Q5_K, i, y);
+        else dq8(src, type, i, y);
+    };
     float m = 0.f;
     for (int i = 8 * lane; i < K; i += 256) {
         float y[8];
-        dq8(src, type, i, y);
+        deq(i, y);
 #pragma unroll
         for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(y[j]));
     }
     const float s = pow2_scale(warp_max(m)), inv = 1.f / s;  // exact: powers of two
-    __half* dst = g.wf + (size_t)e * g.w_expert + g.w_off[c] + (size_t)row * K;
+    __half* base = g.wf + (size_t)e * g.w_expert;
+    int ar;  // row within its 128-row tile
+    if (c < 2) {
+        base += (size_t)(row >> 6) * 128 * K;
+        ar = (c == 0 ? 0 : 64) + (row & 63);
+    } else {
+        base += (size_t)2 * g.FF * g.D + (size_t)(row >> 7) * 128 * K;
+        ar = row & 127;
+    }
     for (int i = 8 * lane; i < K; i += 256) {
         float y[8];
-        dq8(src, type, i, y);
+        deq(i, y);
         __align__(16) __half o[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) o[j] = __float2half_rn(y[j] * inv);
-        *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(o);
+        *reinterpret_cast<uint4*>(base + tile_off(ar, i)) = *reinterpret_cast<const uint4*>(o);
     }
     if (lane == 0) g.rs[(size_t)e * rows_e + r] = s;
 }
 
-// ---- 2. fp32 rows -> scale + f16 hi/lo, one warp per row
-__global__ void __launch_bounds__(256) k_pack_f16(const float* __restrict__ x, int n, int K, __half* __restrict__ hi,
-                                                   __half* __restrict__ lo, float* __restrict__ scale) {
+// ---- 2. slot rows -> scale + f16 hi/lo, tile-major by (expert, slot tile); one warp per slot
+template <int MODE>
+__global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
     pdl_trigger();
     pdl_wait();
-    const int row = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (row >= n) return;
-    const float* xr = x + (size_t)row * K;
+    const int slot = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (slot >= S) return;
+    const int K = MODE == 0 ? g.D : g.FF;
+    int lo_ = 0, hi_ = g.E;  // expert of the slot: largest e with offsets[e] <= slot
+    while (hi_ - lo_ > 1) {
+        const int mid = (lo_ + hi_) >> 1;
+        if (g.offsets[mid] <= slot) lo_ = mid;
+        else hi_ = mid;
+    }
+    const int e = lo_, j = slot - g.offsets[e];
+    const int tile = g.tiles_gu[e] / (g.FF / 64) + (j >> 7), jr = j & 127;
+    const float* xr = MODE == 0 ? g.xn + (size_t)g.slot_token[slot] * K : g.h + (size_t)slot * K;
     float m = 0.f;
     for (int i = 4 * lane; i < K; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
         m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
     const float s = pow2_scale(warp_max(m)), inv = 1.f / s;
-    for (int i = 4 * lane; i < K; i += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(xr + i);
-        const float a[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
-        __align__(8) __half h[4], l[4];
+    __half* bh = g.bhi + (size_t)tile * 128 * K;
+    for (int i = 8 * lane; i < K; i += 256) {
+        const float4 u = *reinterpret_cast<const float4*>(xr + i);
+        const float4 v = *reinterpret_cast<const float4*>(xr + i + 4);
+        const float a[8] = {u.x * inv, u.y * inv, u.z * inv, u.w * inv, v.x * inv, v.y * inv, v.z * inv, v.w * inv};
+        __align__(16) __half h[8];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            h[j] = __float2half_rn(a[j]);
-            l[j] = __float2half_rn(a[j] - __half2float(h[j]));
-        }
-        *reinterpret_cast<uint2*>(hi + (size_t)row * K + i) = *reinterpret_cast<const uint2*>(h);
-        *reinterpret_cast<uint2*>(lo + (size_t)row * K + i) = *reinterpret_cast<const uint2*>(l);
+        for (int q = 0; q < 8; q++) h[q] = __float2half_rn(a[q]);
+        *reinterpret_cast<uint4*>(bh + tile_off(jr, i)) = *reinterpret_cast<const uint4*>(h);
     }
-    if (lane == 0) scale[row] = s;
+    if (lane == 0) g.bscale[slot] = s;
 }
 
 // ---- 3/4. the grouped GEMM
-constexpr int TC_KT = 64;                                 // K elements per stage
-constexpr int TC_TILE_BYTES = 128 * TC_KT * 2;            // one 128-row f16 operand tile of a stage
-constexpr int TC_STAGE_BYTES = 3 * TC_TILE_BYTES;         // W, activations hi, activations lo
-constexpr int TC_SMEM = 2 * TC_STAGE_BYTES + 1024 + 512;  // two stages, slot scales/rows, barriers
+constexpr int TC_KT = 64;                                     // K elements per stage
+constexpr int TC_BLOCK = 128 * TC_KT * 2;                     // one 128-row f16 stage block: 16 KB
+constexpr int TC_STAGES = 6;
+constexpr int TC_STAGE_BYTES = 2 * TC_BLOCK;                  // W, activations
+constexpr int TC_U_BYTES = 128 * 64 * 4;                      // gate/up pairing buffer
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + TC_U_BYTES + 256;
+constexpr int TC_NT = 192;  // warp 0 producer, warp 1 MMA + tensor-memory owner, warps 2..5 epilogue
+
+struct TcTile {
+    int e, rt, m0, mc, btile;
+};
+// tile b of the GEMM (tiles of one expert: row tile fastest, then slot tile)
+template <int MODE>
+__device__ __forceinline__ bool tc_tile(const GroupedArgs& g, int b, TcTile& t) {
+    const int* off = MODE == 0 ? g.tiles_gu : g.tiles_dn;
+    if (b >= off[g.E]) return false;
+    int lo_ = 0, hi_ = g.E;
+    while (hi_ - lo_ > 1) {
+        const int mid = (lo_ + hi_) >> 1;
+        if (off[mid] <= b) lo_ = mid;
+        else hi_ = mid;
+    }
+    const int RT = MODE == 0 ? g.FF / 64 : g.D / 128;
+    const int local = b - off[lo_], st = local / RT;
+    t.e = lo_;
+    t.rt = local - st * RT;
+    t.m0 = g.offsets[lo_] + 128 * st;
+    t.mc = min(128, g.offsets[lo_ + 1] - t.m0);
+    t.btile = g.tiles_gu[lo_] / (g.FF / 64) + st;
+    return true;
+}
 
 template <int MODE>
-__global__ void __launch_bounds__(128) k_gemm_tc(GroupedArgs g) {
+__global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     extern __shared__ __align__(1024) uint8_t smt[];
-    uint8_t* stage0 = smt;
-    float* s_bscale = reinterpret_cast<float*>(smt + 2 * TC_STAGE_BYTES);  // [128]
-    int* s_brow = reinterpret_cast<int*>(smt + 2 * TC_STAGE_BYTES + 512);   // [128]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smt + 2 * TC_STAGE_BYTES + 1024);  // [2]
+    float* U = reinterpret_cast<float*>(smt + TC_STAGES * TC_STAGE_BYTES);  // [128 slots][64 rows]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smt + TC_STAGES * TC_STAGE_BYTES + TC_U_BYTES);
+    uint64_t* full = bars;                    // [TC_STAGES] stage landed
+    uint64_t* empty = bars + TC_STAGES;       // [TC_STAGES] stage consumed by the MMAs
+    uint64_t* acc_full = bars + 2 * TC_STAGES;       // [2] accumulator complete
+    uint64_t* acc_empty = bars + 2 * TC_STAGES + 2;  // [2] accumulator read out (4 epilogue warps)
     __shared__ uint32_t s_tmem;
-    __shared__ int s_info[4];
+    __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    pdl_trigger();
-    pdl_wait();
-    const int* tile_off = MODE == 0 ? g.tiles_gu : g.tiles_dn;
-    if (tid == 0) {  // which (expert, slot tile, row tile)
-        const int b = blockIdx.x, total = tile_off[g.E];
-        int e = -1;
-        if (b < total) {
-            int lo_ = 0, hi_ = g.E;  // largest e with tile_off[e] <= b
-            while (hi_ - lo_ > 1) {
-                const int mid = (lo_ + hi_) >> 1;
-                if (tile_off[mid] <= b) lo_ = mid;
-                else hi_ = mid;
-            }
-            e = lo_;
-        }
-        s_info[0] = e;
-        if (e >= 0) {
-            const int RT = MODE == 0 ? g.FF / 64 : g.D / 128;
-            const int local = b - tile_off[e];
-            s_info[1] = local % RT;                           // row tile
-            s_info[2] = g.offsets[e] + 128 * (local / RT);    // first slot
-            s_info[3] = min(128, g.offsets[e + 1] - s_info[2]);  // slots in the tile
-        }
-    }
-    __syncthreads();
-    const int e = s_info[0];
-    if (e < 0) return;
-    const int rt = s_info[1], m0 = s_info[2], mc = s_info[3];
-    const int K = MODE == 0 ? g.D : g.FF;
-    // activation row of each slot of the tile, and its scale
-    {
-        const int j = tid;
-        int br = 0;
-        float bs = 0.f;
-        if (j < mc) {
-            br = MODE == 0 ? g.slot_token[m0 + j] : m0 + j;
-            bs = (MODE == 0 ? g.xscale : g.hscale)[br];
-        }
-        s_brow[j] = br;
-        s_bscale[j] = bs;
-    }
-    if (warp == 0) tc_alloc(&s_tmem, 128);
+    const int K = MODE == 0 ? g.D : g.FF, nk = K / TC_KT;
+    if (warp == 1) tc_alloc(&s_tmem, 256);
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int i = 0; i < TC_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);
+        }
+        s_abort = 0;
         mbar_fence_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_trigger();
+    pdl_wait();  // routing, packed activations and weights come from the previous grids
     const uint32_t tmem = s_tmem;
-    const __half* We = g.wf + (size_t)e * g.w_expert;
-    const __half* Bh = MODE == 0 ? g.xhi : g.hhi;
-    const __half* Bl = MODE == 0 ? g.xlo : g.hlo;
-    // source row of A row i (the tile's 128 rows)
-    auto a_row = [&](int i) -> const __half* {
-        if (MODE == 0)
-            return We + (i < 64 ? g.w_off[0] : g.w_off[1]) + (size_t)(64 * rt + (i & 63)) * K;
-        return We + g.w_off[2] + (size_t)(128 * rt + i) * K;
+    auto fail = [&]() {
+        if (g.status) atomicOr(g.status, ST_WAIT_TIMEOUT);
+        atomicExch(&s_abort, 1);
     };
-    auto load_stage = [&](int s, int k0) {
-        uint8_t* st = stage0 + s * TC_STAGE_BYTES;
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-            const int i = tid + 128 * q, r = i >> 3, c = i & 7;  // row r, 16-byte chunk c
-            const uint32_t off = (uint32_t)(((r >> 3) * (TC_KT / 8) + c) * 128 + (r & 7) * 16);
-            cp_async16_zfill(st + off, a_row(r) + k0 + 8 * c, 16);
-            const bool ok = r < mc;
-            const size_t boff = (size_t)s_brow[r] * K + k0 + 8 * c;
-            cp_async16_zfill(st + TC_TILE_BYTES + off, Bh + boff, ok ? 16u : 0u);
-            cp_async16_zfill(st + 2 * TC_TILE_BYTES + off, Bl + boff, ok ? 16u : 0u);
+    if (warp == 0) {  // ---------------- producer
+        if (lane == 0) {
+            int it = 0;  // stage fills issued
+            TcTile t;
+            for (int b = blockIdx.x; tc_tile<MODE>(g, b, t) && !*(volatile int*)&s_abort; b += gridDim.x) {
+                const __half* A = g.wf + (size_t)t.e * g.w_expert +
+                                  (MODE == 0 ? (size_t)t.rt * 128 * K : (size_t)2 * g.FF * g.D + (size_t)t.rt * 128 * K);
+                const __half* Bh = g.bhi + (size_t)t.btile * 128 * K;
+                for (int kt = 0; kt < nk; kt++, it++) {
+                    const int s = it % TC_STAGES;
+                    if (it >= TC_STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)(it / TC_STAGES - 1) & 1u)) {
+                        fail();
+                        break;
+                    }
+                    uint8_t* dst = smt + s * TC_STAGE_BYTES;
+                    mbar_expect_tx(&full[s], 2 * TC_BLOCK);
+                    tma_load_1d(dst, A + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
+                    tma_load_1d(dst + TC_BLOCK, Bh + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
+                }
+            }
+            // no copy may still be landing when the CTA exits: wait for the last fill of every stage
+            for (int k = (it > TC_STAGES ? it - TC_STAGES : 0); k < it; k++)
+                if (!mbar_wait_bounded(&full[k % TC_STAGES], (uint32_t)(k / TC_STAGES) & 1u)) break;
         }
-    };
-    constexpr uint32_t idesc = tc_idesc_f16(128, 128);
-    const int nk = K / TC_KT;
-    bool ok = true;
-    for (int kt = 0; kt <= nk && ok; kt++) {
-        if (kt < nk) {
-            const int s = kt & 1;
-            if (kt >= 2) ok = mbar_wait_bounded(&bars[s], (uint32_t)((kt - 2) >> 1) & 1u);
-            load_stage(s, kt * TC_KT);
-            cp_async_commit();
-        }
-        if (kt >= 1) {
-            if (kt < nk) cp_async_wait<1>();
-            else cp_async_wait<0>();
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
+    } else if (warp == 1) {  // ---------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc_f16(128, 128);
+            int it = 0, ti = 0;
+            TcTile t;
+            for (int b = blockIdx.x; tc_tile<MODE>(g, b, t); b += gridDim.x, ti++) {
+                const int a = ti & 1;
+                if (ti >= 2 && !mbar_wait_bounded(&acc_empty[a], (uint32_t)(ti / 2 - 1) & 1u)) {
+                    fail();
+                    break;
+                }
                 tc_fence_after();
-                const int s = (kt - 1) & 1;
-                const uint32_t base = smem_u32(stage0 + s * TC_STAGE_BYTES);
+                const uint32_t acc = tmem + (uint32_t)(128 * a);
+                bool ok = true;
+                for (int kt = 0; kt < nk; kt++, it++) {
+                    const int s = it % TC_STAGES;
+                    if (!mbar_wait_bounded(&full[s], (uint32_t)(it / TC_STAGES) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t base = smem_u32(smt + s * TC_STAGE_BYTES);
 #pragma unroll
-                for (int j = 0; j < TC_KT / 16; j++) {
-                    const uint64_t da = tc_desc(base + 256 * j, 128, (TC_KT / 8) * 128);
-                    const uint64_t dh = tc_desc(base + TC_TILE_BYTES + 256 * j, 128, (TC_KT / 8) * 128);
-                    const uint64_t dl = tc_desc(base + 2 * TC_TILE_BYTES + 256 * j, 128, (TC_KT / 8) * 128);
-                    tc_mma_f16(tmem, da, dh, idesc, (kt > 1 || j > 0) ? 1u : 0u);
-                    tc_mma_f16(tmem, da, dl, idesc, 1u);
+                    for (int j = 0; j < TC_KT / 16; j++) {
+                        const uint64_t da = tc_desc(base + 256 * j, 128, (TC_KT / 8) * 128);
+                        const uint64_t db = tc_desc(base + TC_BLOCK + 256 * j, 128, (TC_KT / 8) * 128);
+                        tc_mma_f16(acc, da, db, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[s]);  // the stage is free once these MMAs completed
                 }
-                tc_commit(&bars[s]);
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                tc_commit(&acc_full[a]);
             }
         }
-        ok = __syncthreads_and(ok);
-    }
-    if (ok) ok = mbar_wait_bounded(&bars[(nk - 1) & 1], (uint32_t)((nk - 1) >> 1) & 1u);
-    ok = __syncthreads_and(ok);
-    if (!ok) {
-        cp_async_wait<0>();
-        if (tid == 0 && g.status) atomicOr(g.status, ST_WAIT_TIMEOUT);
-    } else {
-        tc_fence_after();
-        const int row = 32 * warp + lane;  // accumulator lane = A row
-        const float* rs = g.rs + (size_t)e * (2 * g.FF + g.D);
-        if (MODE == 0) {
-            float* U = reinterpret_cast<float*>(stage0);  // [128 slots][64 rows] up values (stages are idle now)
-            if (warp >= 2) {
-                const float su = rs[g.FF + 64 * rt + row - 64];
-                for (int c0 = 0; c0 < 128; c0 += 16) {
-                    float v[16];
-                    tc_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+    } else {  // ---------------- epilogue: warps 2..5, tensor-memory lane quadrant warp % 4
+        const int q = warp & 3, row = 32 * q + lane;
+        int ti = 0;
+        TcTile t;
+        for (int b = blockIdx.x; tc_tile<MODE>(g, b, t); b += gridDim.x, ti++) {
+            const int a = ti & 1;
+            bool ok = mbar_wait_bounded(&acc_full[a], (uint32_t)(ti / 2) & 1u);
+            if (!ok) fail();
+            tc_fence_after();
+            const uint32_t acc = tmem + (uint32_t)(128 * a) + ((uint32_t)(32 * q) << 16);
+            const float* rs = g.rs + (size_t)t.e * (2 * g.FF + g.D);
+            if (MODE == 0) {
+                if (ok && q >= 2) {  // up rows: scaled values to the pairing buffer
+                    const float su = rs[g.FF + 64 * t.rt + row - 64];
+                    for (int c0 = 0; c0 < 128; c0 += 16) {
+                        float v[16];
+                        tc_ld16(acc + (uint32_t)c0, v);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) U[(c0 + j) * 64 + row - 64] = v[j] * su;
+                        for (int j = 0; j < 16; j++) U[(c0 + j) * 64 + row - 64] = v[j] * su;
+                    }
                 }
-            }
-            __syncthreads();
-            if (warp < 2) {
-                const float sg = rs[64 * rt + row];
-                for (int c0 = 0; c0 < 128; c0 += 16) {
-                    float v[16];
-                    tc_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (ok && q < 2) {
+                    const float sg = rs[64 * t.rt + row];
+                    for (int c0 = 0; c0 < 128; c0 += 16) {
+                        float v[16];
+                        tc_ld16(acc + (uint32_t)c0, v);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int col = c0 + j;
-                        if (col < mc) {
-                            const float bs = s_bscale[col];
-                            const float gv = v[j] * sg * bs, uv = U[col * 64 + row] * bs;
-                            g.h[(size_t)(m0 + col) * g.FF + 64 * rt + row] = silu_mul(gv, uv);
+                        for (int j = 0; j < 16; j++) {
+                            const int col = c0 + j;
+                            if (col < t.mc) {
+                                const float bs = g.bscale[t.m0 + col];
+                                const float gv = v[j] * sg * bs, uv = U[col * 64 + row] * bs;
+                                g.h[(size_t)(t.m0 + col) * g.FF + 64 * t.rt + row] = silu_mul(gv, uv);
+                            }
                         }
                     }
                 }
-            }
-        } else {
-            const float sd = rs[2 * g.FF + 128 * rt + row];
-            for (int c0 = 0; c0 < 128; c0 += 16) {
-                float v[16];
-                tc_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // U is reused by the next tile
+            } else if (ok) {
+                const float sd = rs[2 * g.FF + 128 * t.rt + row];
+                for (int c0 = 0; c0 < 128; c0 += 16) {
+                    float v[16];
+                    tc_ld16(acc + (uint32_t)c0, v);
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int col = c0 + j;
-                    if (col < mc) g.y[(size_t)(m0 + col) * g.D + 128 * rt + row] = v[j] * sd * s_bscale[col];
+                    for (int j = 0; j < 16; j++) {
+                        const int col = c0 + j;
+                        if (col < t.mc) g.y[(size_t)(t.m0 + col) * g.D + 128 * t.rt + row] = v[j] * sd * g.bscale[t.m0 + col];
+                    }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+            if (!ok) break;
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tc_dealloc(tmem, 128);
+    if (warp == 1) tc_dealloc(tmem, 256);
 }
 
 // ---- launchers ----------------------------------------------------------------------------------
@@ -334,27 +413,29 @@ cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st) {
     const long long warps = (long long)g.E * (2 * g.FF + g.D);
     return launch_pdl(k_dequant_f16, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, st, g);
 }
-cudaError_t launch_pack_f16(const float* x, int n, int K, __half* hi, __half* lo, float* scale, cudaStream_t st) {
-    if (n < 1 || K % 128) return cudaErrorInvalidValue;
-    return launch_pdl(k_pack_f16, dim3((n + 7) / 8), dim3(256), 0, st, x, n, K, hi, lo, scale);
+cudaError_t launch_pack_slots(const GroupedArgs& g, int mode, int S, cudaStream_t st) {
+    if (S < 1) return cudaSuccess;
+    if (mode == 0) return launch_pdl(k_pack_slots<0>, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
+    return launch_pdl(k_pack_slots<1>, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
 }
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st) {
     if (g.D % 128 || g.FF % 64 || g.D % TC_KT || g.FF % TC_KT) return cudaErrorInvalidValue;
     if (max_tiles < 1) return cudaSuccess;
+    const int grid = std::min(max_tiles, sm_count());
     if (mode == 0) {
         static bool attr = false;
         if (!attr) {
             cudaFuncSetAttribute(k_gemm_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
             attr = true;
         }
-        return launch_pdl(k_gemm_tc<0>, dim3(max_tiles), dim3(128), TC_SMEM, st, g);
+        return launch_pdl(k_gemm_tc<0>, dim3(grid), dim3(TC_NT), TC_SMEM, st, g);
     }
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(k_gemm_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
         attr = true;
     }
-    return launch_pdl(k_gemm_tc<1>, dim3(max_tiles), dim3(128), TC_SMEM, st, g);
+    return launch_pdl(k_gemm_tc<1>, dim3(grid), dim3(TC_NT), TC_SMEM, st, g);
 }
 
 }  // namespace eb

@@ -106,13 +106,11 @@ struct GroupedArgs {
     size_t w_expert;        // elements per expert (3 FF D)
     size_t w_off[3];        // element offsets of gate, up, down within an expert
     float* rs;              // per expert 2 FF + D row scales (powers of two)
-    const __half* xhi;      // [T x D] tokens, f16 hi/lo of x / xscale
-    const __half* xlo;
-    const float* xscale;    // [T]
+    const float* xn;        // [T x D] expert input rows
     float* h;               // [S x FF] SiLU(g) * u per slot
-    const __half* hhi;      // [S x FF] f16 hi/lo of h / hscale
-    const __half* hlo;
-    const float* hscale;    // [S]
+    __half* bhi;            // activations of the GEMM in progress, f16 of row / bscale, tile-major by
+                            //   (expert, 128-slot tile): tiles x 128 x K
+    float* bscale;          // [S] per-slot scale of the packed rows
     float* y;               // [S x D] down outputs per slot
     int* status;
 };
@@ -146,7 +144,7 @@ cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st, bool combine = tr
 size_t moe_smem_gateup(int D, size_t rbg, size_t rbu);
 size_t moe_smem_down(int FF, size_t rbd);
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st);
-cudaError_t launch_pack_f16(const float* x, int n, int K, __half* hi, __half* lo, float* scale, cudaStream_t st);
+cudaError_t launch_pack_slots(const GroupedArgs& g, int mode, int S, cudaStream_t st);  // 0: xn rows, 1: h rows
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st);  // 0 gate/up, 1 down
 // routing of a ragged batch of any size (moe.cu): per-token top-k with expert counts (cnt zeroed by the
 // caller), then offsets / tile prefixes / active list, then the slot maps

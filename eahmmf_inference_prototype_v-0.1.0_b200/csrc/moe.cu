@@ -38,9 +38,6 @@ namespace eb {
 
 namespace {
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 __device__ __forceinline__ void set_flag(int* status, int bits) {
     if (status) atomicOr(status, bits);
 }
