@@ -369,7 +369,7 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
         torch.cuda.synchronize(dev)
 
     # prefill + first token (untimed), warm-up steps (captures the step graph), then the timed steps
-    rc, first, _ = eng.greedy(prompt, 1, 32)
+    rc, first, _ = eng.greedy(prompt, 1, 64)
     if rc:
         raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
     rc, warm, _ = eng.decode(args.warmup)
@@ -395,7 +395,7 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
 
     # end to end through the C ABI: host prompt in, K host tokens out
     t0 = time.perf_counter()
-    rc, gen, _ = eng.greedy(prompt, args.steps, 32)
+    rc, gen, _ = eng.greedy(prompt, args.steps, 64)
     e2e_s = time.perf_counter() - t0
     if rc:
         raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
@@ -428,7 +428,7 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
         "config": dict(DECODE_CONFIG, parallelism=f"replicas x{world}"),
         "e2e": {"value": args.steps * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
                 "d2h_bytes_per_step": args.steps * 4,
-                "step": "one eahmmf_engine_greedy call: 512-token prompt in, prefill, K tokens out"},
+                "step": "one eahmmf_engine_greedy call: 512-token prompt in, prefill in 64-token passes, K tokens out"},
         "gpu_launches": nodes * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if peak else None, "traffic": traffic, "kernel": "k_moe_gateup (T=1)",
@@ -718,7 +718,7 @@ def main():
         return profile_ragged(args.profile_ragged)
     decode = args.workload == "decode"
     if args.steps is None:
-        args.steps = 128 if decode else 5 if args.workload == "ragged" else 20
+        args.steps = 256 if decode else 5 if args.workload == "ragged" else 20
     if args.warmup is None:
         args.warmup = 8 if decode else 3
     if args.warmup < 3:

@@ -432,16 +432,22 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
         a.xf = xf_carve(ws + w.xf, tc, L->D);
         a.y = reinterpret_cast<float*>(ws + w.y);
         a.status = d_status;
+        // up to FUSED_ROUTE_TMAX tokens: the XF prep rides on the router launch (or a prep launch) and the
+        // gate/up kernel routes by itself; larger blocks go through k_moe_route
+        a.fused_route = tc <= FUSED_ROUTE_TMAX ? 1 : 0;
         g_prof.mark(0, st);
         if (d_logits) {
             a.logits = d_logits + (size_t)t0 * E;
+            if (a.fused_route && launch_prep_x(a.xn, L->D, tc, L->D, a.xf, st) != cudaSuccess) return ST_CUDA;
         } else {
             float* lg = reinterpret_cast<float*>(ws + w.logits);
-            if (launch_f32_gemv(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, st) != cudaSuccess) return ST_CUDA;
+            const cudaError_t e = a.fused_route ? launch_router_prep(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, a.xf, st)
+                                                : launch_f32_gemv(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, st);
+            if (e != cudaSuccess) return ST_CUDA;
             a.logits = lg;
         }
         g_prof.mark(1, st);
-        if (launch_moe_route(a, st) != cudaSuccess) return ST_CUDA;
+        if (!a.fused_route && launch_moe_route(a, st) != cudaSuccess) return ST_CUDA;
         g_prof.mark(2, st);
         if (launch_moe_gateup(a, st) != cudaSuccess) return ST_CUDA;
         g_prof.mark(3, st);

@@ -384,15 +384,25 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
 }
 
 constexpr int F32_NT = 128;
-__global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W, int K, const float* __restrict__ X,
-                                                     int ldx, int m_all, float* __restrict__ Y, int ldy) {
+__global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W, int K, int rows,
+                                                     const float* __restrict__ X, int ldx, int m_all,
+                                                     float* __restrict__ Y, int ldy, XF xf, int prep) {
     __shared__ float red[F32_NT / 32][MT];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
+    if (row >= rows) {  // blocks past the matrix: token (row - rows) in fragment form for the expert kernels
+        __shared__ float pred[33];
+        const int t = row - rows;
+        if (prep && blockIdx.y == 0 && t < m_all)
+            prep_row(X + (size_t)t * ldx, K, const_cast<uint2*>(xf.frag) + (size_t)t * (K >> 5) * 12,
+                     const_cast<float*>(xf.sum) + (size_t)t * ((K >> 4) + XF_SUM_PAD),
+                     const_cast<uint8_t*>(xf.gs) + (size_t)t * xf_gs_bytes(K), pred);
+        return;
+    }
     const int t0 = blockIdx.y * MT, m = min(MT, m_all - t0);  // this block's tokens
     X += (size_t)t0 * ldx;
     Y += (size_t)t0 * ldy;
-    pdl_trigger();
-    pdl_wait();
     const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)row * K);
     float acc[MT];
 #pragma unroll
@@ -425,12 +435,21 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
 // F32 rows (the router, qwen3moe.cpp:1008): one 128-thread block per (row, MT tokens), the four warps
 // taking interleaved float4 slices of the row so every thread has all its loads in flight at once; the
 // four partial sums are added in a fixed order (deterministic).
+cudaError_t launch_router_prep(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
+                               const XF& xf, cudaStream_t st) {
+    if (K % 256 || ldx % 4 || (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(X) & 15))
+        return cudaErrorInvalidValue;
+    return launch_pdl(k_gemv_f32, dim3(rows + m, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, rows, X, ldx, m, Y,
+                      ldy, xf, 1);
+}
+
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
                             cudaStream_t st) {
     const bool vec = K % 4 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(X) & 15) == 0;
     if (vec)
-        return launch_pdl(k_gemv_f32, dim3(rows, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, X, ldx, m, Y, ldy);
+        return launch_pdl(k_gemv_f32, dim3(rows, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, rows, X, ldx, m, Y,
+                          ldy, XF{}, 0);
     for (int t0 = 0; t0 < m; t0 += MT) {  // other layouts: the per-row kernel, MT tokens per pass
         GemvArgs a{};
         a.W = QMat{reinterpret_cast<const uint8_t*>(W), T_F32, K, rows, (size_t)K * 4};

@@ -79,7 +79,10 @@ struct MoeArgs {
     float* y;             // [T*K*D] expert outputs per slot (down projection, before the combine)
     RouteWs rw;
     int* status;
+    int fused_route;  // T <= FUSED_ROUTE_TMAX: k_moe_gateup routes itself (no k_moe_route launch); the
+                      // XF of the tokens must already be in xf
 };
+constexpr int FUSED_ROUTE_TMAX = 8;
 
 // Dense GEMV on activations already in fragment form: Y[t*ldy + r] (=|+=) row r . x_t, t < m <= XPASS.
 struct GemvXArgs {
@@ -154,5 +157,8 @@ cudaError_t launch_scatter_big(const MoeArgs& a, const int* local, cudaStream_t 
 cudaError_t launch_moe_combine(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
                             cudaStream_t st);
+// the router GEMV plus, in m extra blocks, the m token rows of X in fragment form (xf)
+cudaError_t launch_router_prep(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
+                               const XF& xf, cudaStream_t st);
 
 }  // namespace eb

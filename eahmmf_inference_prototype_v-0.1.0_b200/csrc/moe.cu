@@ -109,10 +109,10 @@ __device__ void drain(uint64_t* full, int issued, int consumed, int S) {
 //   stages       the ring
 struct Plan {
     int S;
-    size_t info_off, cnt_off, xf_off, xfb, part_off, comb_off, stage_off, stage_bytes, total;
+    size_t info_off, cnt_off, xf_off, xfb, part_off, comb_off, stage_off, stage_bytes, extra_off, total;
 };
 constexpr size_t SMEM_CAP = 227 * 1024;
-__host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, size_t comb_bytes) {
+__host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, size_t comb_bytes, size_t extra = 0) {
     Plan p;
     p.info_off = 128;
     p.cnt_off = p.info_off + 4 * 16;
@@ -125,7 +125,8 @@ __host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, si
     for (;; p.S--) {
         p.comb_off = al128(p.part_off + (size_t)p.S * part_bytes);
         p.stage_off = al128(p.comb_off + comb_bytes);
-        p.total = p.stage_off + (size_t)p.S * p.stage_bytes;
+        p.extra_off = al128(p.stage_off + (size_t)p.S * p.stage_bytes);
+        p.total = p.extra_off + extra;
         if (p.total <= SMEM_CAP || p.S == 2) break;
     }
     return p;
@@ -139,8 +140,8 @@ constexpr int DN_ROWS = 64;  // rows of D per down unit
 __host__ __device__ inline bool split8(size_t rb) { return rb % 16 == 0; }
 __host__ __device__ inline size_t split8_off(size_t rb) { return al128(8 * rb) + 32; }
 __host__ __device__ inline size_t gu_slot(size_t rb) { return split8(rb) ? al128(split8_off(rb) + 8 * rb) : al128(16 * rb + 64); }
-__host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu) {
-    return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0);
+__host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu, size_t route_bytes = 0) {
+    return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0, route_bytes);
 }
 __host__ __device__ inline Plan down_plan(int FF, size_t rbd) {
     return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0);
@@ -405,50 +406,80 @@ __device__ void route_token(const float* __restrict__ lg, int E, int K, int lane
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
-    pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
-    pdl_wait();     // logits and activations come from the previous grids
-    if (blockIdx.x > 0) {  // activation prep of token blockIdx.x - 1
-        __shared__ float red[33];
-        const int row = blockIdx.x - 1;
-        prep_row(a.xn + (size_t)row * a.D, a.D, const_cast<uint2*>(a.xf.frag) + (size_t)row * (a.D >> 5) * 12,
-                 const_cast<float*>(a.xf.sum) + (size_t)row * ((a.D >> 4) + XF_SUM_PAD),
-                 const_cast<uint8_t*>(a.xf.gs) + (size_t)row * xf_gs_bytes(a.D), red);
-        return;
+// Shared-memory views of one block's routing of T <= MOE_TMAX tokens (E <= MAX_EXPERTS experts).
+struct RouteSm {
+    int *cnt, *off, *goff;        // [E] slots, slot offset, group offset per expert
+    unsigned long long* mask;     // [E] tokens routed to the expert
+    int* s_ids;                   // [T*K] routed experts, rank order
+    float* s_w;                   // [T*K] their weights
+    uint32_t* s_rk;               // [warps * 64] ranking scratch of route_token
+    int* g_info;                  // optional [G][4]: expert, first slot, slots, unused; G <= T*K
+    int* g_tok;                   // optional [G][MU]
+    const uint8_t** g_w;          // optional [G][2]: gate and up matrices of the group's expert
+    int* G;                       // number of groups
+};
+// bytes of a RouteSm for E experts and TK = T*K slots; with_groups adds the shared-memory group list
+__host__ __device__ constexpr size_t route_sm_bytes(int E, int TK, bool with_groups) {
+    return (size_t)E * (8 + 4 + 4 + 4) + (size_t)TK * 8 + (size_t)(ROUTE_NT / 32 + 2) * 64 * 4 + 16 +
+           (with_groups ? (size_t)TK * (16 + 16 + 4 * MU) : 0);
+}
+__device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_groups) {
+    RouteSm r;
+    r.mask = reinterpret_cast<unsigned long long*>(p);  // 8-byte aligned at the start
+    p += (size_t)E * 8;
+    r.cnt = reinterpret_cast<int*>(p);
+    r.off = r.cnt + E;
+    r.goff = r.off + E;
+    r.s_ids = r.goff + E;
+    r.s_w = reinterpret_cast<float*>(r.s_ids + TK);
+    r.s_rk = reinterpret_cast<uint32_t*>(r.s_w + TK);
+    r.G = reinterpret_cast<int*>(r.s_rk + (ROUTE_NT / 32 + 2) * 64);
+    p = reinterpret_cast<uint8_t*>(r.G + 4);  // 16 bytes
+    p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 15) & ~(uintptr_t)15);
+    if (with_groups) {
+        r.g_w = reinterpret_cast<const uint8_t**>(p);
+        r.g_info = reinterpret_cast<int*>(p + (size_t)TK * 16);
+        r.g_tok = r.g_info + 4 * TK;
+    } else {
+        r.g_w = nullptr;
+        r.g_info = nullptr;
+        r.g_tok = nullptr;
     }
-    __shared__ int s_ids[MOE_TMAX * 32];
-    __shared__ float s_w[MOE_TMAX * 32];
-    __shared__ uint32_t s_rk[(ROUTE_NT / 32) * 64];  // per warp: ranked (r, expert) of up to 32 candidates
-    __shared__ int cnt[MAX_EXPERTS];
-    __shared__ int off[MAX_EXPERTS];
-    __shared__ int goff[MAX_EXPERTS];
-    __shared__ unsigned long long mask[MAX_EXPERTS];
+    return r;
+}
+
+// The routing of the T tokens by every thread of the block (qwen3moe.cpp:1009-1029): top-k per token (one
+// warp per token), per-expert counts and token masks, scans, work groups of up to MU slots per expert
+// (expert ascending), slot maps. With `global` the results go to a.rw (routing outputs, groups and slot
+// maps for the later kernels); with r.g_info the group list also stays in shared memory.
+__device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
     for (int i = tid; i < E; i += blockDim.x) {
-        cnt[i] = 0;
-        mask[i] = 0ull;
+        r.cnt[i] = 0;
+        r.mask[i] = 0ull;
     }
     __syncthreads();
-
     // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022)
     const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
     for (int t = warp; t < T; t += nwarp) {
         int my_e = 0;
         float my_w = 0.f;
-        if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, s_rk + warp * 64, my_e, my_w);
-        else if (E <= 256) route_token<8>(a.logits + (size_t)t * E, E, K, lane, s_rk + warp * 64, my_e, my_w);
-        else route_token<16>(a.logits + (size_t)t * E, E, K, lane, s_rk + warp * 64, my_e, my_w);
+        if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, r.s_rk + warp * 64, my_e, my_w);
+        else if (E <= 256) route_token<8>(a.logits + (size_t)t * E, E, K, lane, r.s_rk + warp * 64, my_e, my_w);
+        else route_token<16>(a.logits + (size_t)t * E, E, K, lane, r.s_rk + warp * 64, my_e, my_w);
         if (lane < K) {
             if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
-                set_flag(a.status, ST_BAD_INDEX);
+                if (global) set_flag(a.status, ST_BAD_INDEX);
                 my_e = 0;
             }
-            s_ids[t * K + lane] = my_e;
-            s_w[t * K + lane] = my_w;
-            a.rw.ids[(size_t)t * K + lane] = my_e;
-            a.rw.wts[(size_t)t * K + lane] = my_w;
-            atomicAdd(&cnt[my_e], 1);
-            atomicOr(&mask[my_e], 1ull << t);
+            r.s_ids[t * K + lane] = my_e;
+            r.s_w[t * K + lane] = my_w;
+            if (global) {
+                a.rw.ids[(size_t)t * K + lane] = my_e;
+                a.rw.wts[(size_t)t * K + lane] = my_w;
+            }
+            atomicAdd(&r.cnt[my_e], 1);
+            atomicOr(&r.mask[my_e], 1ull << t);
         }
     }
     __syncthreads();
@@ -459,7 +490,7 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         int c_in = 0, g_in = 0, a_in = 0;
         for (int j = 0; j < per; j++) {
             const int e = lane * per + j;
-            const int c = e < E ? cnt[e] : 0;
+            const int c = e < E ? r.cnt[e] : 0;
             c_in += c;
             g_in += (c + MU - 1) / MU;
             a_in += c > 0;
@@ -479,53 +510,85 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         for (int j = 0; j < per; j++) {
             const int e = lane * per + j;
             if (e >= E) break;
-            const int c = cnt[e];
-            off[e] = c_run;
-            goff[e] = g_run;
-            a.rw.offsets[e] = c_run;
-            if (c > 0) a.rw.active[1 + a_run++] = e;
+            const int c = r.cnt[e];
+            r.off[e] = c_run;
+            r.goff[e] = g_run;
+            if (global) {
+                a.rw.offsets[e] = c_run;
+                if (c > 0) a.rw.active[1 + a_run] = e;
+            }
+            a_run += c > 0;
             c_run += c;
             g_run += (c + MU - 1) / MU;
         }
         if (lane == 31) {
-            a.rw.offsets[E] = c_x;
-            a.rw.active[0] = a_x;
-            a.rw.ngroups[0] = g_x;
+            *r.G = g_x;
+            if (global) {
+                a.rw.offsets[E] = c_x;
+                a.rw.active[0] = a_x;
+                a.rw.ngroups[0] = g_x;
+            }
         }
     }
     __syncthreads();
     // ---- work list: groups of up to MU consecutive slots of one expert, expert ascending
     for (int e = tid; e < E; e += blockDim.x) {
-        const int c = cnt[e];
+        const int c = r.cnt[e];
         if (c == 0) continue;
         const uint8_t* wg = a.gate[e];
         const uint8_t* wu = a.up[e];
-        const uint8_t* wd = a.down[e];
+        const uint8_t* wd = global ? a.down[e] : nullptr;
         for (int j = 0; j * MU < c; j++) {
-            GroupRec r;
-            r.w[0] = wg;
-            r.w[1] = wu;
-            r.w[2] = wd;
-            r.e = e;
-            r.s0 = off[e] + j * MU;
-            r.mc = min(MU, c - j * MU);
+            const int gi = r.goff[e] + j;
+            GroupRec rec;
+            rec.w[0] = wg;
+            rec.w[1] = wu;
+            rec.w[2] = wd;
+            rec.e = e;
+            rec.s0 = r.off[e] + j * MU;
+            rec.mc = min(MU, c - j * MU);
 #pragma unroll
-            for (int k = 0; k < MU; k++) r.tok[k] = k < r.mc ? nth_bit(mask[e], j * MU + k) : 0;
-            a.rw.groups[goff[e] + j] = r;
+            for (int k = 0; k < MU; k++) rec.tok[k] = k < rec.mc ? nth_bit(r.mask[e], j * MU + k) : 0;
+            if (global) a.rw.groups[gi] = rec;
+            if (r.g_info) {
+                r.g_info[4 * gi] = e;
+                r.g_info[4 * gi + 1] = rec.s0;
+                r.g_info[4 * gi + 2] = rec.mc;
+#pragma unroll
+                for (int k = 0; k < MU; k++) r.g_tok[MU * gi + k] = rec.tok[k];
+                r.g_w[2 * gi] = wg;
+                r.g_w[2 * gi + 1] = wu;
+            }
         }
     }
+    if (!global) return;
     // ---- stable scatter, one thread per (token, k): slot = offset[e] + earlier tokens routed to e;
     // the token's slots in ascending order (= expert order) by rank among its k experts
     for (int i = tid; i < T * K; i += blockDim.x) {
         const int t = i / K;
-        const int e = s_ids[i];
-        const int s = off[e] + __popcll(mask[e] & ((1ull << t) - 1ull));
-        a.rw.slot_token[s] = t;
-        a.rw.slot_w[s] = s_w[i];
+        const int e = r.s_ids[i];
+        const int sl = r.off[e] + __popcll(r.mask[e] & ((1ull << t) - 1ull));
+        a.rw.slot_token[sl] = t;
+        a.rw.slot_w[sl] = r.s_w[i];
         int rank = 0;
-        for (int j = 0; j < K; j++) rank += s_ids[t * K + j] < e;
-        a.rw.token_slots[(size_t)t * K + rank] = s;
+        for (int j = 0; j < K; j++) rank += r.s_ids[t * K + j] < e;
+        a.rw.token_slots[(size_t)t * K + rank] = sl;
     }
+}
+
+__global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
+    pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
+    pdl_wait();     // logits and activations come from the previous grids
+    if (blockIdx.x > 0) {  // activation prep of token blockIdx.x - 1
+        __shared__ float red[33];
+        const int row = blockIdx.x - 1;
+        prep_row(a.xn + (size_t)row * a.D, a.D, const_cast<uint2*>(a.xf.frag) + (size_t)row * (a.D >> 5) * 12,
+                 const_cast<float*>(a.xf.sum) + (size_t)row * ((a.D >> 4) + XF_SUM_PAD),
+                 const_cast<uint8_t*>(a.xf.gs) + (size_t)row * xf_gs_bytes(a.D), red);
+        return;
+    }
+    __shared__ __align__(16) uint8_t rsm[route_sm_bytes(MAX_EXPERTS, MOE_TMAX * 32, false) + 16];
+    route_block(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -535,7 +598,8 @@ template <int QG, int QU>
 __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int D = a.D, FF = a.FF, nsb = D >> 8, NRB = FF >> 4, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const Plan pl = gateup_plan(D, a.gate_rb, a.up_rb);
+    const int TK = a.T * a.n_used;
+    const Plan pl = gateup_plan(D, a.gate_rb, a.up_rb, a.fused_route ? route_sm_bytes(a.n_expert, TK, true) : 0);
     const int S = pl.S;
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + 4;
@@ -553,8 +617,28 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
     }
     __syncthreads();
     pdl_trigger();
-    pdl_wait();  // routing results and the XF of the tokens come from k_moe_route
-    const int G = a.rw.ngroups[0];
+    pdl_wait();  // routing results (or the logits) and the XF of the tokens come from the previous grids
+    // small batches: every CTA routes the tokens itself into shared memory (CTA 0 also publishes the
+    // routing, groups and slot maps for the down kernel and the combine)
+    RouteSm rt{};
+    if (a.fused_route) {
+        rt = route_sm_carve(sm + pl.extra_off, a.n_expert, TK, true);
+        route_block(a, rt, blockIdx.x == 0);
+        __syncthreads();
+    }
+    const int G = a.fused_route ? *rt.G : a.rw.ngroups[0];
+    auto group = [&](int gi) {
+        if (!a.fused_route) return a.rw.groups[gi];
+        GroupRec g{};
+        g.w[0] = rt.g_w[2 * gi];
+        g.w[1] = rt.g_w[2 * gi + 1];
+        g.e = rt.g_info[4 * gi];
+        g.s0 = rt.g_info[4 * gi + 1];
+        g.mc = rt.g_info[4 * gi + 2];
+#pragma unroll
+        for (int k = 0; k < MU; k++) g.tok[k] = rt.g_tok[MU * gi + k];
+        return g;
+    };
     const int nunits = G * NRB;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const size_t rbg = a.gate_rb, rbu = a.up_rb, up_at = gu_slot(rbg);
@@ -564,7 +648,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         if (lane != 0) return;
         int cur = -1, xb = 1, i = 0;
         GroupRec rec{}, nxt{};
-        if (u0 < u1) nxt = a.rw.groups[u0 / NRB];
+        if (u0 < u1) nxt = group(u0 / NRB);
         for (int u = u0; u < u1; u++, i++) {
             const int s = i % S;
             if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)(i / S - 1) & 1u)) {
@@ -579,7 +663,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
                 rec = nxt;
                 cur = gi;
                 xb ^= 1;
-                if ((gi + 1) * NRB < u1) nxt = a.rw.groups[gi + 1];  // the next group's record, ahead of use
+                if ((gi + 1) * NRB < u1) nxt = group(gi + 1);  // the next group's record, ahead of use
             }
             const bool ok = al16(rec.w[0]) && al16(rec.w[1]);
             if (!ok) set_flag(a.status, ST_BAD_ARG);
@@ -979,7 +1063,8 @@ cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st) {
 
 template <int QG, int QU>
 static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
-    const Plan pl = gateup_plan(a.D, a.gate_rb, a.up_rb);
+    const Plan pl = gateup_plan(a.D, a.gate_rb, a.up_rb,
+                                a.fused_route ? route_sm_bytes(a.n_expert, a.T * a.n_used, true) : 0);
     if (pl.total > SMEM_CAP || (a.FF >> 4) < pl.S) return cudaErrorInvalidValue;
     smem_attr(k_moe_gateup<QG, QU>, pl.total);
     const int units = max_groups(a) * (a.FF >> 4);
