@@ -383,7 +383,11 @@ namespace eb {
 // eahmmf_cuda_moe_layer with an optional deferred combine (engine use): when `defer` is set and the call
 // runs as one 64-token pass, the combine is not launched and defer receives what it needs.
 int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
-                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer) {
+                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
+                  const float* norm_w, float eps) {
+    // norm_w: d_xn is the un-normalised residual and the RMSNorm is applied inside the router launch
+    // (only for the fused small-batch path: T <= FUSED_ROUTE_TMAX, router matrix present)
+    if (norm_w && (T > FUSED_ROUTE_TMAX || d_logits || !L || !L->d_router)) return ST_BAD_ARG;
     if (!layer_ok(L)) return (L && !(is_kquant(L->gate_type) && is_kquant(L->up_type) && is_kquant(L->down_type)))
                                   ? ST_BAD_TYPE
                                   : ST_BAD_ARG;
@@ -441,8 +445,9 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
             if (a.fused_route && launch_prep_x(a.xn, L->D, tc, L->D, a.xf, st) != cudaSuccess) return ST_CUDA;
         } else {
             float* lg = reinterpret_cast<float*>(ws + w.logits);
-            const cudaError_t e = a.fused_route ? launch_router_prep(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, a.xf, st)
-                                                : launch_f32_gemv(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, st);
+            const cudaError_t e = a.fused_route
+                                      ? launch_router_prep(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, a.xf, norm_w, eps, st)
+                                      : launch_f32_gemv(L->d_router, L->D, E, a.xn, L->D, tc, lg, E, st);
             if (e != cudaSuccess) return ST_CUDA;
             a.logits = lg;
         }
@@ -470,7 +475,8 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
 extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits,
                                      float* d_x, void* d_workspace, size_t workspace_bytes, void* stream,
                                      int* d_status) {
-    return moe_layer_run(L, T, d_xn, d_logits, d_x, d_workspace, workspace_bytes, stream, d_status, nullptr);
+    return moe_layer_run(L, T, d_xn, d_logits, d_x, d_workspace, workspace_bytes, stream, d_status, nullptr, nullptr,
+                         0.f);
 }
 
 extern "C" int eahmmf_cuda_route_topk(const float* d_logits, int T, int E, int K, int* d_ids, float* d_w, void* stream,

@@ -97,19 +97,16 @@ __device__ float block_sum(float v, float* red) {
     return v;
 }
 
-constexpr int NORM_NT = 256;
-__global__ void __launch_bounds__(NORM_NT) k_rmsnorm(const float* __restrict__ x, int ldx, const float* __restrict__ w,
-                                                     float* __restrict__ out, int ldo, int n, float eps) {
-    __shared__ float red[NORM_NT / 32];
+// (128 threads: the sum of squares in row_sumsq128's order, shared with the router launch's fused norm)
+__global__ void __launch_bounds__(128) k_rmsnorm(const float* __restrict__ x, int ldx, const float* __restrict__ w,
+                                                 float* __restrict__ out, int ldo, int n, float eps) {
+    __shared__ float red4[4];
     pdl_trigger();
     pdl_wait();
     const float* xr = x + (size_t)blockIdx.x * ldx;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += NORM_NT) ss = fmaf(xr[i], xr[i], ss);
-    ss = block_sum<NORM_NT>(ss, red);
-    const float sc = 1.0f / sqrtf(ss / (float)n + eps);
+    const float sc = 1.0f / sqrtf(row_sumsq128(xr, n, red4) / (float)n + eps);
     float* o = out + (size_t)blockIdx.x * ldo;
-    for (int i = threadIdx.x; i < n; i += NORM_NT) o[i] = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+    for (int i = threadIdx.x; i < n; i += 128) o[i] = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
 }
 
 // ---- fused: [combine of the previous MoE block] + RMSNorm + activation prep, one CTA per token row
@@ -181,6 +178,29 @@ __global__ void k_rope_table(const DecodeState* st, const float* __restrict__ in
     }
 }
 
+// One head (lane l holds elements l, l+32, ...): per-head RMSNorm with weights nw, then NeoX rotation
+// with the row's cos/sin pairs (qwen3moe.cpp:951-972).
+template <int HD>
+__device__ __forceinline__ void head_norm_rope(float (&v)[HD / 32], const float* __restrict__ nw, float eps,
+                                               const float2* __restrict__ cs_row, int lane) {
+    constexpr int PER = HD / 32;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float sc = 1.0f / sqrtf(ss / (float)HD + eps);
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = __fmul_rn(__fmul_rn(v[j], sc), nw[lane + 32 * j]);
+#pragma unroll
+    for (int j = 0; j < PER / 2; j++) {
+        const float2 r = cs_row[lane + 32 * j];
+        const float a = v[j], b = v[j + PER / 2];
+        v[j] = a * r.x - b * r.y;
+        v[j + PER / 2] = a * r.y + b * r.x;
+    }
+}
+
 // ---- per-head RMSNorm + NeoX rotation of q and k, KV-cache append (qwen3moe.cpp:951-972)
 // qkv: [nb x (QD + 2 KD)] rows as the fused q|k|v projection writes them. One warp per (token, head)
 // over the n_head q heads, n_kv k heads and n_kv v heads; lane l holds elements l, l+32, ... of the head.
@@ -207,23 +227,7 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
         for (int j = 0; j < PER; j++) dst[lane + 32 * j] = v[j];
         return;
     }
-    const float* nw = h < n_head ? qn : kn;
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float sc = 1.0f / sqrtf(ss / (float)HD + eps);
-#pragma unroll
-    for (int j = 0; j < PER; j++) v[j] = __fmul_rn(__fmul_rn(v[j], sc), nw[lane + 32 * j]);
-    // element e = lane + 32 j pairs with e + HALF = lane + 32 (j + PER/2)
-#pragma unroll
-    for (int j = 0; j < PER / 2; j++) {
-        const float2 r = cs[(size_t)t * HALF + lane + 32 * j];
-        const float a = v[j], b = v[j + PER / 2];
-        v[j] = a * r.x - b * r.y;
-        v[j + PER / 2] = a * r.y + b * r.x;
-    }
+    head_norm_rope<HD>(v, h < n_head ? qn : kn, eps, cs + (size_t)t * HALF, lane);  // pairs (e, e + HD/2)
     float* dst = h < n_head ? q_out + (size_t)t * QD + (size_t)h * HD
                             : kc + (size_t)pos * KD + (size_t)(h - n_head) * HD;
 #pragma unroll
@@ -243,10 +247,11 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int HD>
-__global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ q, const float* __restrict__ kc,
-                                                       const float* __restrict__ vc, int n_head, int n_kv, float scale,
+__global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ q, float* __restrict__ kc,
+                                                       float* __restrict__ vc, int n_head, int n_kv, float scale,
                                                        const DecodeState* st, int nsplit, float* __restrict__ part,
-                                                       int* __restrict__ counters, float* __restrict__ att) {
+                                                       int* __restrict__ counters, float* __restrict__ att,
+                                                       RopeFuse rf) {
     constexpr int PER = HD / 32, RS = HD + 4;
     extern __shared__ __align__(16) float smf[];
     float* Ks = smf;                          // [ATT_CH][RS]
@@ -261,7 +266,19 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     pdl_wait();
     const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
     const int nch = (np + ATT_CH - 1) / ATT_CH;
-    for (int i = threadIdx.x; i < grp * HD; i += ATT_NT) Qs[i] = q[(size_t)t * QD + (size_t)h * grp * HD + i];
+    if (rf.qkv) {  // single-token step: the group's q heads normalised and rotated here, from the q|k|v row
+        for (int hq = warp; hq < grp; hq += nwarp) {
+            const float* src = rf.qkv + (size_t)(h * grp + hq) * HD;
+            float v[PER];
+#pragma unroll
+            for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+            head_norm_rope<HD>(v, rf.qn, rf.eps, rf.cs, lane);
+#pragma unroll
+            for (int j = 0; j < PER; j++) Qs[hq * HD + lane + 32 * j] = v[j];
+        }
+    } else {
+        for (int i = threadIdx.x; i < grp * HD; i += ATT_NT) Qs[i] = q[(size_t)t * QD + (size_t)h * grp * HD + i];
+    }
     // each warp owns q heads warp, warp + nwarp, ... (at most ATT_MAXH per warp)
     float m_run[ATT_MAXH], l_run[ATT_MAXH], o_run[ATT_MAXH][PER];
 #pragma unroll
@@ -281,6 +298,24 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
             cp_async16(Vs + r * RS + 4 * c4, vc + g);
         }
         cp_async_wait_all();
+        __syncthreads();  // every thread's copies have landed (the fused row below must not be overwritten)
+        if (rf.qkv && np - 1 >= p0 && np - 1 < p0 + n && warp < 2) {
+            // the step's own position lies in this chunk: its k (normalised, rotated) and v come straight
+            // from the q|k|v row into the staged chunk and into the cache
+            const int r = np - 1 - p0;
+            const float* src = rf.qkv + (size_t)(n_head + (warp == 0 ? 0 : n_kv) + h) * HD;
+            float v[PER];
+#pragma unroll
+            for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+            if (warp == 0) head_norm_rope<HD>(v, rf.kn, rf.eps, rf.cs, lane);
+            float* srow = (warp == 0 ? Ks : Vs) + r * RS;
+            float* grow = (warp == 0 ? kc : vc) + (size_t)(np - 1) * KD + (size_t)h * HD;
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                srow[lane + 32 * j] = v[j];
+                grow[lane + 32 * j] = v[j];
+            }
+        }
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < ATT_MAXH; k++) {
@@ -476,7 +511,8 @@ cudaError_t launch_embed(const uint8_t* W, int type, size_t rb, int D, int n_row
 }
 cudaError_t launch_rmsnorm(const float* x, int ldx, const float* w, float* out, int ldo, int rows, int n, float eps,
                            cudaStream_t s) {
-    return launch_pdl(k_rmsnorm, dim3(rows), dim3(NORM_NT), 0, s, x, ldx, w, out, ldo, n, eps);
+    if (n % 4 || ldx % 4) return cudaErrorInvalidValue;
+    return launch_pdl(k_rmsnorm, dim3(rows), dim3(128), 0, s, x, ldx, w, out, ldo, n, eps);
 }
 cudaError_t launch_norm_prep(const NormPrepArgs& a, int rows, cudaStream_t s) {
     if (rows < 1 || a.n % 256 || (a.y && (a.K < 1 || a.K > 32))) return cudaErrorInvalidValue;
@@ -511,9 +547,9 @@ size_t attn_smem(int hd, int grp) {
     return ((size_t)2 * ATT_CH * (hd + 4) + (size_t)(ATT_NT / 32) * ATT_CH + (size_t)grp * hd) * sizeof(float);
 }
 template <int HD>
-static cudaError_t attn_as(const float* q, const float* kc, const float* vc, int n_head, int n_kv, float scale,
+static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                            const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
-                           cudaStream_t s) {
+                           const RopeFuse& rf, cudaStream_t s) {
     const size_t smem = attn_smem(HD, n_head / n_kv);
     static size_t cur = 0;
     if (smem > cur) {
@@ -522,14 +558,15 @@ static cudaError_t attn_as(const float* q, const float* kc, const float* vc, int
         cur = smem;
     }
     return launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv, scale,
-                      st, nsplit, part, counters, att);
+                      st, nsplit, part, counters, att, rf);
 }
-cudaError_t launch_attention(int hd, const float* q, const float* kc, const float* vc, int n_head, int n_kv,
-                             float scale, const DecodeState* st, int nb, int nsplit, float* part, int* counters,
-                             float* att, cudaStream_t s) {
-    if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1) return cudaErrorInvalidValue;
-    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, s);
-    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, s);
+cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
+                             const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
+                             const RopeFuse& rf, cudaStream_t s) {
+    if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1 || (rf.qkv && nb != 1))
+        return cudaErrorInvalidValue;
+    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, rf, s);
+    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, rf, s);
     return cudaErrorInvalidValue;
 }
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {

@@ -53,11 +53,20 @@ cudaError_t launch_qk_rope_kv(int hd, const float* qkv, int n_head, int n_kv, co
                               float eps, const float2* cs, const DecodeState* st, int nb, float* q_out, float* kc,
                               float* vc, cudaStream_t s);
 size_t attn_smem(int hd, int grp);
+// Single-token steps: when qkv is set the attention kernel does the q/k head norms, the rotation and the
+// KV append itself (k_qk_rope_kv is not launched); q is then unused.
+struct RopeFuse {
+    const float* qkv;  // [QD + 2 KD] q|k|v row of the step's token, or null
+    const float* qn;
+    const float* kn;
+    float eps;
+    const float2* cs;  // the token's HD/2 cos/sin pairs
+};
 // part: nb * n_head * nsplit * (hd + 2) floats; counters: nb * n_kv ints, zero before the first call
 // (each call leaves them zero)
-cudaError_t launch_attention(int hd, const float* q, const float* kc, const float* vc, int n_head, int n_kv,
-                             float scale, const DecodeState* st, int nb, int nsplit, float* part, int* counters,
-                             float* att, cudaStream_t s);
+cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
+                             const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
+                             const RopeFuse& rf, cudaStream_t s);
 // blk: nblk float2 of scratch
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s);
 cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s);

@@ -34,7 +34,8 @@
 
 namespace eb {
 int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
-                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer);
+                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
+                  const float* norm_w, float eps);
 }
 using namespace eb;
 
@@ -535,9 +536,11 @@ struct EahmmfEngine {
         cap_out = n;  // history pointer from the device state, so it needs no re-capture
         return true;
     }
-    int nsplit_for(int nb) const {
+    // Context splits of the attention kernel: independent of the tokens per pass, so that every token's
+    // softmax is merged in the same order however the prompt is split into passes.
+    int nsplit_for(int) const {
         const int nch = std::max(1, (n_ctx + ATT_CH - 1) / ATT_CH);
-        return std::max(1, std::min({nch, 128, 2 * 148 / std::max(1, n_kv * nb)}));
+        return std::max(1, std::min({nch, 128, 2 * 148 / std::max(1, n_kv)}));
     }
 
     // profile: an event after each operation, tagged with the operation's class
@@ -632,17 +635,33 @@ struct EahmmfEngine {
                     rc = gemv_d(L.wq[c], L.qkv_type[c], rows[c], L.qkv_rb[c], qkv + col[c], ldq);
             }
             if (rc != ST_OK || !mark(2)) return rc != ST_OK ? rc : ST_CUDA;
-            if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, state, nb, q, lk, lv,
-                                  st) != cudaSuccess || !mark(3))
+            RopeFuse rf{};
+            if (nb == 1) {  // single-token step: norms, rotation and KV append inside the attention kernel
+                rf.qkv = qkv;
+                rf.qn = L.q_norm;
+                rf.kn = L.k_norm;
+                rf.eps = eps;
+                rf.cs = rope_cs;
+                if (!mark(3)) return ST_CUDA;
+            } else if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, state, nb, q, lk,
+                                         lv, st) != cudaSuccess ||
+                       !mark(3)) {
                 return ST_CUDA;
-            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, attn_cnt, att, st) !=
-                    cudaSuccess ||
+            }
+            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, attn_cnt, att, rf,
+                                 st) != cudaSuccess ||
                 !mark(4))
                 return ST_CUDA;
             rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes, st);
             if (rc != ST_OK || !mark(5)) return rc != ST_OK ? rc : ST_CUDA;
-            if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(6)) return ST_CUDA;
-            rc = moe_layer_run(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending);
+            if (nb <= FUSED_ROUTE_TMAX) {  // the FFN RMSNorm runs inside the router launch
+                if (!mark(6)) return ST_CUDA;
+                rc = moe_layer_run(&L.moe, nb, x, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, L.ffn_norm,
+                                   eps);
+            } else {
+                if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(6)) return ST_CUDA;
+                rc = moe_layer_run(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, nullptr, 0.f);
+            }
             if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
             if (trace) {  // routing of this layer (ids, then weights, at the head of the MoE workspace)
                 const size_t nk = (size_t)nb * n_used;

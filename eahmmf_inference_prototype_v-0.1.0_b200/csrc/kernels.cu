@@ -386,23 +386,41 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
 constexpr int F32_NT = 128;
 __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W, int K, int rows,
                                                      const float* __restrict__ X, int ldx, int m_all,
-                                                     float* __restrict__ Y, int ldy, XF xf, int prep) {
+                                                     float* __restrict__ Y, int ldy, XF xf, int prep,
+                                                     const float* __restrict__ nw, float eps) {
+    extern __shared__ __align__(16) float nrow[];  // [K] (prep blocks with a norm)
     __shared__ float red[F32_NT / 32][MT];
+    __shared__ float red4[4];
+    __shared__ float s_sc[MT];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_trigger();
     pdl_wait();
     if (row >= rows) {  // blocks past the matrix: token (row - rows) in fragment form for the expert kernels
         __shared__ float pred[33];
         const int t = row - rows;
-        if (prep && blockIdx.y == 0 && t < m_all)
-            prep_row(X + (size_t)t * ldx, K, const_cast<uint2*>(xf.frag) + (size_t)t * (K >> 5) * 12,
-                     const_cast<float*>(xf.sum) + (size_t)t * ((K >> 4) + XF_SUM_PAD),
-                     const_cast<uint8_t*>(xf.gs) + (size_t)t * xf_gs_bytes(K), pred);
+        if (!(prep && blockIdx.y == 0 && t < m_all)) return;
+        const float* xr = X + (size_t)t * ldx;
+        if (nw) {  // RMSNorm of the row first (qwen3moe.cpp:527-532)
+            const float sc = 1.0f / sqrtf(row_sumsq128(xr, K, red4) / (float)K + eps);
+            for (int i = threadIdx.x; i < K; i += F32_NT) nrow[i] = __fmul_rn(__fmul_rn(xr[i], sc), nw[i]);
+            __syncthreads();
+            xr = nrow;
+        }
+        prep_row(xr, K, const_cast<uint2*>(xf.frag) + (size_t)t * (K >> 5) * 12,
+                 const_cast<float*>(xf.sum) + (size_t)t * ((K >> 4) + XF_SUM_PAD),
+                 const_cast<uint8_t*>(xf.gs) + (size_t)t * xf_gs_bytes(K), pred);
         return;
     }
     const int t0 = blockIdx.y * MT, m = min(MT, m_all - t0);  // this block's tokens
     X += (size_t)t0 * ldx;
     Y += (size_t)t0 * ldy;
+    if (nw) {
+        for (int t = 0; t < m; t++) {
+            const float sc = 1.0f / sqrtf(row_sumsq128(X + (size_t)t * ldx, K, red4) / (float)K + eps);
+            if (threadIdx.x == 0) s_sc[t] = sc;
+        }
+        __syncthreads();
+    }
     const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)row * K);
     float acc[MT];
 #pragma unroll
@@ -410,10 +428,19 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
 #pragma unroll 4
     for (int i = threadIdx.x; i < K / 4; i += F32_NT) {
         const float4 w = __ldg(w4 + i);
+        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (nw) g = __ldg(reinterpret_cast<const float4*>(nw) + i);
 #pragma unroll
         for (int t = 0; t < MT; t++) {
             if (t < m) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(X + (size_t)t * ldx) + i);
+                float4 x = __ldg(reinterpret_cast<const float4*>(X + (size_t)t * ldx) + i);
+                if (nw) {  // the normalised element, exactly as the prep blocks form it
+                    const float sc = s_sc[t];
+                    x.x = __fmul_rn(__fmul_rn(x.x, sc), g.x);
+                    x.y = __fmul_rn(__fmul_rn(x.y, sc), g.y);
+                    x.z = __fmul_rn(__fmul_rn(x.z, sc), g.z);
+                    x.w = __fmul_rn(__fmul_rn(x.w, sc), g.w);
+                }
                 acc[t] = fmaf(w.x, x.x, fmaf(w.y, x.y, fmaf(w.z, x.z, fmaf(w.w, x.w, acc[t]))));
             }
         }
@@ -436,11 +463,14 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
 // taking interleaved float4 slices of the row so every thread has all its loads in flight at once; the
 // four partial sums are added in a fixed order (deterministic).
 cudaError_t launch_router_prep(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
-                               const XF& xf, cudaStream_t st) {
-    if (K % 256 || ldx % 4 || (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(X) & 15))
+                               const XF& xf, const float* norm_w, float eps, cudaStream_t st) {
+    if (K % 256 || ldx % 4 || (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(X) & 15) ||
+        (norm_w && (reinterpret_cast<uintptr_t>(norm_w) & 15)))
         return cudaErrorInvalidValue;
-    return launch_pdl(k_gemv_f32, dim3(rows + m, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, rows, X, ldx, m, Y,
-                      ldy, xf, 1);
+    const size_t smem = norm_w ? (size_t)K * 4 : 0;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k_gemv_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return launch_pdl(k_gemv_f32, dim3(rows + m, (m + MT - 1) / MT), dim3(F32_NT), smem, st, W, K, rows, X, ldx, m,
+                      Y, ldy, xf, 1, norm_w, eps);
 }
 
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
@@ -449,7 +479,7 @@ cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int
                      (reinterpret_cast<uintptr_t>(X) & 15) == 0;
     if (vec)
         return launch_pdl(k_gemv_f32, dim3(rows, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, rows, X, ldx, m, Y,
-                          ldy, XF{}, 0);
+                          ldy, XF{}, 0, static_cast<const float*>(nullptr), 0.f);
     for (int t0 = 0; t0 < m; t0 += MT) {  // other layouts: the per-row kernel, MT tokens per pass
         GemvArgs a{};
         a.W = QMat{reinterpret_cast<const uint8_t*>(W), T_F32, K, rows, (size_t)K * 4};

@@ -157,8 +157,9 @@ cudaError_t launch_scatter_big(const MoeArgs& a, const int* local, cudaStream_t 
 cudaError_t launch_moe_combine(const MoeArgs& a, cudaStream_t st);
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
                             cudaStream_t st);
-// the router GEMV plus, in m extra blocks, the m token rows of X in fragment form (xf)
+// the router GEMV plus, in m extra blocks, the m token rows of X in fragment form (xf); with norm_w the
+// rows are RMSNorm-ed first (X is then the residual, normalised on the fly)
 cudaError_t launch_router_prep(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
-                               const XF& xf, cudaStream_t st);
+                               const XF& xf, const float* norm_w, float eps, cudaStream_t st);
 
 }  // namespace eb

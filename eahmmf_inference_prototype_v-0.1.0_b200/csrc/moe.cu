@@ -421,7 +421,7 @@ struct RouteSm {
 // bytes of a RouteSm for E experts and TK = T*K slots; with_groups adds the shared-memory group list
 __host__ __device__ constexpr size_t route_sm_bytes(int E, int TK, bool with_groups) {
     return (size_t)E * (8 + 4 + 4 + 4) + (size_t)TK * 8 + (size_t)(ROUTE_NT / 32 + 2) * 64 * 4 + 16 +
-           (with_groups ? (size_t)TK * (16 + 16 + 4 * MU) : 0);
+           (with_groups ? 16 + (size_t)TK * (16 + 16 + 4 * MU) : 0);  // 16: alignment of the group list
 }
 __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_groups) {
     RouteSm r;
