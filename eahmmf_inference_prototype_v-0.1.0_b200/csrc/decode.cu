@@ -1,6 +1,6 @@
 // decode.cu -- the non-expert kernels of a qwen3moe forward pass (Engine::forward, qwen3moe.cpp:929-1074)
 // on sm_100a: embedding rows, RMSNorm, QK-norm + NeoX RoPE + KV-cache append, causal GQA attention
-// split over the context (the last block of each head group merges the splits), first-maximum argmax,
+// split over the context with a merge that also preps the o-projection's activations, first-maximum argmax,
 // and the device-side decode state.
 //
 // Every kernel that depends on the position reads it from device memory (`DecodeState.pos`), so one
@@ -239,8 +239,8 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
 // y, y + nsplit, ... of ATT_CH positions with an online softmax and writes one partial (max, sum,
 // unnormalised output) per q head. K/V chunks are staged in shared memory with cp.async (every thread's
 // 16-byte copies in flight at once), rows padded by 4 floats for conflict-free row-parallel score reads.
-// The last block of a (token, kv head) to finish (a counter per pair, reset by that block) merges the
-// splits: out = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M).
+// k_attn_merge_prep merges the splits of every head of a token row and puts the row in fragment form
+// for the o-projection.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
@@ -250,7 +250,6 @@ template <int HD>
 __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ q, float* __restrict__ kc,
                                                        float* __restrict__ vc, int n_head, int n_kv, float scale,
                                                        const DecodeState* st, int nsplit, float* __restrict__ part,
-                                                       int* __restrict__ counters, float* __restrict__ att,
                                                        RopeFuse rf) {
     constexpr int PER = HD / 32, RS = HD + 4;
     extern __shared__ __align__(16) float smf[];
@@ -258,7 +257,6 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     float* Vs = Ks + ATT_CH * RS;             // [ATT_CH][RS]
     float* Ps = Vs + ATT_CH * RS;             // [ATT_NT/32][ATT_CH] probabilities of the warp's current head
     float* Qs = Ps + (ATT_NT / 32) * ATT_CH;  // [GRP][HD]
-    __shared__ bool last;
     const int h = blockIdx.x, y = blockIdx.y, t = blockIdx.z;
     const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = ATT_NT / 32;
@@ -266,6 +264,16 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     pdl_wait();
     const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
     const int nch = (np + ATT_CH - 1) / ATT_CH;
+    auto stage_chunk = [&](int c) {  // K/V rows of chunk c -> shared memory (cp.async, 16 bytes each)
+        const int p0 = c * ATT_CH, n = min(ATT_CH, np - p0);
+        for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
+            const int r = i / (HD / 4), c4 = i - r * (HD / 4);
+            const size_t g = (size_t)(p0 + r) * KD + (size_t)h * HD + 4 * c4;
+            cp_async16(Ks + r * RS + 4 * c4, kc + g);
+            cp_async16(Vs + r * RS + 4 * c4, vc + g);
+        }
+    };
+    if (y < nch) stage_chunk(y);  // the first chunk's copies fly while the q heads are prepared
     if (rf.qkv) {  // single-token step: the group's q heads normalised and rotated here, from the q|k|v row
         for (int hq = warp; hq < grp; hq += nwarp) {
             const float* src = rf.qkv + (size_t)(h * grp + hq) * HD;
@@ -290,12 +298,9 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     }
     for (int c = y; c < nch; c += nsplit) {
         const int p0 = c * ATT_CH, n = min(ATT_CH, np - p0);
-        __syncthreads();  // previous chunk fully consumed (and Qs written, first time)
-        for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
-            const int r = i / (HD / 4), c4 = i - r * (HD / 4);
-            const size_t g = (size_t)(p0 + r) * KD + (size_t)h * HD + 4 * c4;
-            cp_async16(Ks + r * RS + 4 * c4, kc + g);
-            cp_async16(Vs + r * RS + 4 * c4, vc + g);
+        if (c != y) {
+            __syncthreads();  // previous chunk fully consumed
+            stage_chunk(c);
         }
         cp_async_wait_all();
         __syncthreads();  // every thread's copies have landed (the fused row below must not be overwritten)
@@ -331,15 +336,17 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
                 float acc = 0.f;
                 if (pr < n) {
                     const float* kr = Ks + pr * RS;
+                    float a4[4] = {0.f, 0.f, 0.f, 0.f};  // four chains: the dot is latency-bound otherwise
 #pragma unroll 8
                     for (int d = 0; d < HD; d += 4) {
                         const float4 kv4 = *reinterpret_cast<const float4*>(kr + d);
                         const float4 q4 = *reinterpret_cast<const float4*>(qh + d);
-                        acc = fmaf(q4.x, kv4.x, acc);
-                        acc = fmaf(q4.y, kv4.y, acc);
-                        acc = fmaf(q4.z, kv4.z, acc);
-                        acc = fmaf(q4.w, kv4.w, acc);
+                        a4[0] = fmaf(q4.x, kv4.x, a4[0]);
+                        a4[1] = fmaf(q4.y, kv4.y, a4[1]);
+                        a4[2] = fmaf(q4.z, kv4.z, a4[2]);
+                        a4[3] = fmaf(q4.w, kv4.w, a4[3]);
                     }
+                    acc = (a4[0] + a4[1]) + (a4[2] + a4[3]);
                     s[r] = acc * scale;
                     mc = fmaxf(mc, s[r]);
                 } else {
@@ -362,17 +369,31 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
             l_run[k] = l_run[k] * alpha + ls;
             m_run[k] = m_new;
             __syncwarp();
-            float acc[PER];
+            float acc[2][PER];  // even / odd positions: two chains per element
 #pragma unroll
-            for (int j = 0; j < PER; j++) acc[j] = o_run[k][j] * alpha;
-            for (int r = 0; r < n; r++) {
-                const float p = Ps[warp * ATT_CH + r];
-                const float* vr = Vs + r * RS;
+            for (int j = 0; j < PER; j++) {
+                acc[0][j] = o_run[k][j] * alpha;
+                acc[1][j] = 0.f;
+            }
+            int r = 0;
+#pragma unroll 4
+            for (; r + 1 < n; r += 2) {
+                const float p0 = Ps[warp * ATT_CH + r], p1 = Ps[warp * ATT_CH + r + 1];
+                const float* v0 = Vs + r * RS;
+                const float* v1 = v0 + RS;
 #pragma unroll
-                for (int j = 0; j < PER; j++) acc[j] = fmaf(p, vr[lane + 32 * j], acc[j]);
+                for (int j = 0; j < PER; j++) {
+                    acc[0][j] = fmaf(p0, v0[lane + 32 * j], acc[0][j]);
+                    acc[1][j] = fmaf(p1, v1[lane + 32 * j], acc[1][j]);
+                }
+            }
+            if (r < n) {
+                const float p0 = Ps[warp * ATT_CH + r];
+#pragma unroll
+                for (int j = 0; j < PER; j++) acc[0][j] = fmaf(p0, Vs[r * RS + lane + 32 * j], acc[0][j]);
             }
 #pragma unroll
-            for (int j = 0; j < PER; j++) o_run[k][j] = acc[j];
+            for (int j = 0; j < PER; j++) o_run[k][j] = acc[0][j] + acc[1][j];
             __syncwarp();
         }
     }
@@ -389,38 +410,68 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
 #pragma unroll
         for (int j = 0; j < PER; j++) pr[2 + lane + 32 * j] = o_run[k][j];
     }
-    // the last split block of (t, h) merges
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int* cnt = counters + (size_t)t * n_kv + h;
-        last = atomicAdd(cnt, 1) == nsplit - 1;
-        if (last) *cnt = 0;  // ready for the next pass (graph replays)
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    for (int hq = warp; hq < grp; hq += nwarp) {
-        const float* p = part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2);
-        float M = -INFINITY;
-        for (int yy = 0; yy < nsplit; yy++) M = fmaxf(M, __ldcg(p + (size_t)yy * (HD + 2)));
-        float L = 0.f, o[PER];
+}
+
+// ---- split merge of every head of a token row: out = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M),
+// written to att (fp32) and, in fragment form, to xf for the o-projection. One CTA per token row
+// (32 warps, warp w merges heads w, w + 32, ...; the row stays in shared memory for the prep).
+constexpr int MP_NT = 1024;
+template <int HD>
+__global__ void __launch_bounds__(MP_NT) k_attn_merge_prep(const float* __restrict__ part, int n_head, int nsplit,
+                                                           float* __restrict__ att, XF xf) {
+    constexpr int PER = HD / 32;
+    extern __shared__ __align__(16) float mrow[];  // [n_head * HD]
+    __shared__ float red[33];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, QD = n_head * HD;
+    for (int hq = warp; hq < n_head; hq += MP_NT / 32) {
+        const float* p = part + ((size_t)t * n_head + hq) * nsplit * (HD + 2);
+        float mq[4], lq[4], M = -INFINITY;  // lane y holds split y (nsplit <= 128)
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) {
+            const int yy = lane + 32 * q4;
+            mq[q4] = yy < nsplit ? p[(size_t)yy * (HD + 2)] : -INFINITY;
+            lq[q4] = yy < nsplit ? p[(size_t)yy * (HD + 2) + 1] : 0.f;
+            M = fmaxf(M, mq[q4]);
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float eq[4], L = 0.f;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) {
+            eq[q4] = mq[q4] == -INFINITY ? 0.f : expf(mq[q4] - M);  // splits without positions weigh 0
+            L = fmaf(lq[q4], eq[q4], L);
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        float o[PER];
 #pragma unroll
         for (int j = 0; j < PER; j++) o[j] = 0.f;
-        for (int yy = 0; yy < nsplit; yy++) {
-            const float* r = p + (size_t)yy * (HD + 2);
-            const float m = __ldcg(r);
-            if (m == -INFINITY) continue;  // split without positions
-            const float e = expf(m - M);
-            L = fmaf(__ldcg(r + 1), e, L);
 #pragma unroll
-            for (int j = 0; j < PER; j++) o[j] = fmaf(__ldcg(r + 2 + lane + 32 * j), e, o[j]);
+        for (int q4 = 0; q4 < 4; q4++) {
+            if (32 * q4 >= nsplit) break;
+#pragma unroll 4
+            for (int y32 = 0; y32 < 32 && 32 * q4 + y32 < nsplit; y32++) {
+                const float e = __shfl_sync(0xffffffffu, eq[q4], y32);
+                if (e == 0.f) continue;  // warp-uniform
+                const float* r = p + (size_t)(32 * q4 + y32) * (HD + 2) + 2;
+#pragma unroll
+                for (int j = 0; j < PER; j++) o[j] = fmaf(r[lane + 32 * j], e, o[j]);
+            }
         }
         const float inv = 1.0f / L;
-        float* dst = att + (size_t)t * QD + (size_t)(h * grp + hq) * HD;
 #pragma unroll
-        for (int j = 0; j < PER; j++) dst[lane + 32 * j] = o[j] * inv;
+        for (int j = 0; j < PER; j++) {
+            const float v = o[j] * inv;
+            mrow[hq * HD + lane + 32 * j] = v;
+            att[(size_t)t * QD + hq * HD + lane + 32 * j] = v;
+        }
     }
+    __syncthreads();
+    prep_row(mrow, QD, const_cast<uint2*>(xf.frag) + (size_t)t * (QD >> 5) * 12,
+             const_cast<float*>(xf.sum) + (size_t)t * ((QD >> 4) + XF_SUM_PAD),
+             const_cast<uint8_t*>(xf.gs) + (size_t)t * xf_gs_bytes(QD), red);
 }
 
 // ---- argmax: first maximum, as std::max_element (qwen3moe.cpp:1103)
@@ -548,7 +599,7 @@ size_t attn_smem(int hd, int grp) {
 }
 template <int HD>
 static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
-                           const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
+                           const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
                            const RopeFuse& rf, cudaStream_t s) {
     const size_t smem = attn_smem(HD, n_head / n_kv);
     static size_t cur = 0;
@@ -557,16 +608,26 @@ static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int
         if (e != cudaSuccess) return e;
         cur = smem;
     }
-    return launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv, scale,
-                      st, nsplit, part, counters, att, rf);
+    cudaError_t e = launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv,
+                               scale, st, nsplit, part, rf);
+    if (e != cudaSuccess) return e;
+    const size_t msmem = (size_t)n_head * HD * 4;
+    static size_t mcur = 0;
+    if (msmem > 48 * 1024 && msmem > mcur) {
+        e = cudaFuncSetAttribute(k_attn_merge_prep<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem);
+        if (e != cudaSuccess) return e;
+        mcur = msmem;
+    }
+    return launch_pdl(k_attn_merge_prep<HD>, dim3(nb), dim3(MP_NT), msmem, s, part, n_head, nsplit, att, xf);
 }
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
-                             const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
+                             const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
                              const RopeFuse& rf, cudaStream_t s) {
-    if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1 || (rf.qkv && nb != 1))
+    if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1 || nsplit > 128 ||
+        (rf.qkv && nb != 1) || (n_head * hd) % 256)
         return cudaErrorInvalidValue;
-    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, rf, s);
-    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, counters, att, rf, s);
+    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, s);
+    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, s);
     return cudaErrorInvalidValue;
 }
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {

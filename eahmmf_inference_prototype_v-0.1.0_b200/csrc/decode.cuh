@@ -62,10 +62,11 @@ struct RopeFuse {
     float eps;
     const float2* cs;  // the token's HD/2 cos/sin pairs
 };
-// part: nb * n_head * nsplit * (hd + 2) floats; counters: nb * n_kv ints, zero before the first call
-// (each call leaves them zero)
+// Attention of nb token rows (split partials in part: nb * n_head * nsplit * (hd + 2) floats, nsplit
+// <= 128), then the merge of each row into att (fp32, [nb x n_head hd]) and into xf (fragment form, the
+// o-projection's activations).
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
-                             const DecodeState* st, int nb, int nsplit, float* part, int* counters, float* att,
+                             const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
                              const RopeFuse& rf, cudaStream_t s);
 // blk: nblk float2 of scratch
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s);

@@ -264,11 +264,11 @@ struct EahmmfEngine {
     float *out_norm = nullptr, *inv_freq = nullptr, *kc = nullptr, *vc = nullptr;
     float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *logits = nullptr;
     float* attn_part = nullptr;
-    int* attn_cnt = nullptr;  // [MAXB * n_kv] split counters of the attention kernel (self-resetting)
     float2 *rope_cs = nullptr, *amax_blk = nullptr;
     int amax_nblk = 0;
     void *moe_ws = nullptr, *gemv_ws = nullptr;
     void* xf_rows = nullptr;  // [MAXB rows of D] normalised activations in fragment form
+    void* xf_att = nullptr;   // [MAXB rows of QD] attention outputs in fragment form
     size_t moe_ws_bytes = 0, gemv_ws_bytes = 0;
     int* toks = nullptr;       // device token staging [MAXB]
     int* h_toks = nullptr;     // pinned [MAXB]
@@ -475,11 +475,10 @@ struct EahmmfEngine {
             !dalloc(attn_part, (size_t)MAXB * n_head * std::min(nsplit_max, 128) * (hd + 2) * 4) ||
             !dalloc(amax_blk, (size_t)amax_nblk * 8) || !dalloc(moe_ws, moe_ws_bytes) ||
             !dalloc(gemv_ws, gemv_ws_bytes) || !dalloc(toks, MAXB * 4) || !dalloc(status, 4) ||
-            !dalloc(attn_cnt, (size_t)MAXB * n_kv * 4) || !dalloc(xf_rows, xf_bytes(MAXB, D)) ||
+            !dalloc(xf_rows, xf_bytes(MAXB, D)) || !dalloc(xf_att, xf_bytes(MAXB, QD)) ||
             !dalloc(state, sizeof(DecodeState)))
             return fail("cannot allocate activations / KV cache");
         if (cudaMemset(kc, 0, kvn * 4) != cudaSuccess || cudaMemset(vc, 0, kvn * 4) != cudaSuccess ||
-            cudaMemset(attn_cnt, 0, (size_t)MAXB * n_kv * 4) != cudaSuccess ||
             cudaMemset(status, 0, 4) != cudaSuccess)
             return fail("memset");
         if (cudaHostAlloc((void**)&h_toks, MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
@@ -648,12 +647,35 @@ struct EahmmfEngine {
                        !mark(3)) {
                 return ST_CUDA;
             }
-            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, attn_cnt, att, rf,
-                                 st) != cudaSuccess ||
+            const XF xf_o = xf_carve(xf_att, MAXB, QD);
+            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, att, xf_o, rf, st) !=
+                    cudaSuccess ||
                 !mark(4))
                 return ST_CUDA;
-            rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes, st);
-            if (rc != ST_OK || !mark(5)) return rc != ST_OK ? rc : ST_CUDA;
+            {  // o-projection accumulated into the residual, over the merged rows in fragment form
+                const QMat W{L.wo, L.wo_type, QD, D, L.wo_rb};
+                if (!gemv_mma_ok(W)) {
+                    rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes,
+                                          st);
+                    if (rc != ST_OK) return rc;
+                } else {
+                    for (int t0 = 0; t0 < nb; t0 += XPASS) {
+                        GemvXArgs g{};
+                        g.W = W;
+                        g.xf = xf_o;
+                        g.xf.frag += (size_t)t0 * (QD >> 5) * 12;
+                        g.xf.sum += (size_t)t0 * ((QD >> 4) + XF_SUM_PAD);
+                        g.xf.gs += (size_t)t0 * xf_gs_bytes(QD);
+                        g.m = std::min(XPASS, nb - t0);
+                        g.Y = x + (size_t)t0 * D;
+                        g.ldy = D;
+                        g.accumulate = 1;
+                        g.status = status;
+                        if (launch_gemv_xf(g, st) != cudaSuccess) return ST_CUDA;
+                    }
+                }
+                if (!mark(5)) return ST_CUDA;
+            }
             if (nb <= FUSED_ROUTE_TMAX) {  // the FFN RMSNorm runs inside the router launch
                 if (!mark(6)) return ST_CUDA;
                 rc = moe_layer_run(&L.moe, nb, x, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, L.ffn_norm,

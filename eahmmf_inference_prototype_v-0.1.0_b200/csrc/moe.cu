@@ -16,6 +16,8 @@
 //                     whether it moves 1 KB or 9 KB (one copy per ~0.2 us per SM), so a matrix's 16 rows
 //                     come as two 8-row copies, the second placed 32 bytes off the first's bank
 //                     alignment, instead of sixteen row copies.
+//   (Up to FUSED_ROUTE_TMAX tokens, the gate/up kernel routes the tokens itself from the logits and its
+//   CTA 0 publishes the groups and slot maps for the down kernel and the combine.)
 //   k_moe_down<D>     persistent likewise over units (group, 64 rows of D) with 12 consumer warps. The
 //                     consumers put each group's h rows in fragment form in shared memory themselves
 //                     (the first group's while the first weight tiles are in flight). Each unit's reducer
@@ -143,8 +145,8 @@ __host__ __device__ inline size_t gu_slot(size_t rb) { return split8(rb) ? al128
 __host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu, size_t route_bytes = 0) {
     return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0, route_bytes);
 }
-__host__ __device__ inline Plan down_plan(int FF, size_t rbd) {
-    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0);
+__host__ __device__ inline Plan down_plan(int FF, size_t rbd, size_t route_bytes = 0) {
+    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0, route_bytes);
 }
 
 // info word y: xf buffer (bit 0), slots in the group (bits 4-7), weights usable (bit 8), first unit of
@@ -415,13 +417,13 @@ struct RouteSm {
     uint32_t* s_rk;               // [warps * 64] ranking scratch of route_token
     int* g_info;                  // optional [G][4]: expert, first slot, slots, unused; G <= T*K
     int* g_tok;                   // optional [G][MU]
-    const uint8_t** g_w;          // optional [G][2]: gate and up matrices of the group's expert
+    const uint8_t** g_w;          // optional [G][3]: gate, up and down matrices of the group's expert
     int* G;                       // number of groups
 };
 // bytes of a RouteSm for E experts and TK = T*K slots; with_groups adds the shared-memory group list
 __host__ __device__ constexpr size_t route_sm_bytes(int E, int TK, bool with_groups) {
     return (size_t)E * (8 + 4 + 4 + 4) + (size_t)TK * 8 + (size_t)(ROUTE_NT / 32 + 2) * 64 * 4 + 16 +
-           (with_groups ? 16 + (size_t)TK * (16 + 16 + 4 * MU) : 0);  // 16: alignment of the group list
+           (with_groups ? 16 + (size_t)TK * (24 + 16 + 4 * MU) : 0);  // 16: alignment of the group list
 }
 __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_groups) {
     RouteSm r;
@@ -438,7 +440,7 @@ __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_gr
     p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 15) & ~(uintptr_t)15);
     if (with_groups) {
         r.g_w = reinterpret_cast<const uint8_t**>(p);
-        r.g_info = reinterpret_cast<int*>(p + (size_t)TK * 16);
+        r.g_info = reinterpret_cast<int*>(p + (size_t)TK * 24);
         r.g_tok = r.g_info + 4 * TK;
     } else {
         r.g_w = nullptr;
@@ -537,7 +539,7 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
         if (c == 0) continue;
         const uint8_t* wg = a.gate[e];
         const uint8_t* wu = a.up[e];
-        const uint8_t* wd = global ? a.down[e] : nullptr;
+        const uint8_t* wd = a.down[e];
         for (int j = 0; j * MU < c; j++) {
             const int gi = r.goff[e] + j;
             GroupRec rec;
@@ -556,8 +558,9 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
                 r.g_info[4 * gi + 2] = rec.mc;
 #pragma unroll
                 for (int k = 0; k < MU; k++) r.g_tok[MU * gi + k] = rec.tok[k];
-                r.g_w[2 * gi] = wg;
-                r.g_w[2 * gi + 1] = wu;
+                r.g_w[3 * gi] = wg;
+                r.g_w[3 * gi + 1] = wu;
+                r.g_w[3 * gi + 2] = wd;
             }
         }
     }
@@ -630,8 +633,9 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
     auto group = [&](int gi) {
         if (!a.fused_route) return a.rw.groups[gi];
         GroupRec g{};
-        g.w[0] = rt.g_w[2 * gi];
-        g.w[1] = rt.g_w[2 * gi + 1];
+        g.w[0] = rt.g_w[3 * gi];
+        g.w[1] = rt.g_w[3 * gi + 1];
+        g.w[2] = rt.g_w[3 * gi + 2];
         g.e = rt.g_info[4 * gi];
         g.s0 = rt.g_info[4 * gi + 1];
         g.mc = rt.g_info[4 * gi + 2];
@@ -791,6 +795,7 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     pdl_trigger();
     pdl_wait();  // h and the routing come from the previous grids
     const int G = a.rw.ngroups[0];
+    auto group = [&](int gi) { return a.rw.groups[gi]; };
     const int nunits = G * NRG;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const Rows L = rows_of(rb);
@@ -799,7 +804,7 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         if (lane != 0) return;
         int cur = -1, xb = 1, i = 0;
         GroupRec rec{}, nxt{};
-        if (u0 < u1) nxt = a.rw.groups[u0 / NRG];
+        if (u0 < u1) nxt = group(u0 / NRG);
         for (int u = u0; u < u1; u++, i++) {
             const int s = i % S;
             if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)(i / S - 1) & 1u)) {
@@ -814,7 +819,7 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
                 rec = nxt;
                 cur = gi;
                 xb ^= 1;
-                if ((gi + 1) * NRG < u1) nxt = a.rw.groups[gi + 1];
+                if ((gi + 1) * NRG < u1) nxt = group(gi + 1);
             }
             const uint8_t* w = rec.w[2];
             const bool ok = al16(w);
@@ -851,7 +856,7 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     };
     int uses[2] = {0, 0};
     if (u0 < u1) {  // the first group's h rows, while the first weight tiles are in flight
-        const GroupRec r0 = a.rw.groups[u0 / NRG];
+        const GroupRec r0 = group(u0 / NRG);
         prep_group(0, r0.s0, r0.mc);
     }
     int i = 0;
