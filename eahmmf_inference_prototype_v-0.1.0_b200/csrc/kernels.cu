@@ -384,6 +384,7 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st) {
 }
 
 constexpr int F32_NT = 128;
+constexpr int F32_PF = 8;  // float4 per thread of the weight row loaded before the grid-dependency wait
 __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W, int K, int rows,
                                                      const float* __restrict__ X, int ldx, int m_all,
                                                      float* __restrict__ Y, int ldy, XF xf, int prep,
@@ -393,6 +394,18 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
     __shared__ float red4[4];
     __shared__ float s_sc[MT];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // The row's weights and the norm weights do not depend on earlier grids: the first F32_PF float4 of
+    // each thread are loaded before the wait, so the HBM latency overlaps the previous kernel's tail.
+    const int n4 = K / 4;
+    const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)min(row, rows - 1) * K);
+    const float4* g4 = reinterpret_cast<const float4*>(nw);
+    float4 wpf[F32_PF], gpf[F32_PF];
+#pragma unroll
+    for (int j = 0; j < F32_PF; j++) {
+        const int i = threadIdx.x + j * F32_NT;
+        wpf[j] = row < rows && i < n4 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        gpf[j] = row < rows && nw && i < n4 ? __ldg(g4 + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+    }
     pdl_trigger();
     pdl_wait();
     if (row >= rows) {  // blocks past the matrix: token (row - rows) in fragment form for the expert kernels
@@ -421,15 +434,11 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
         }
         __syncthreads();
     }
-    const float4* w4 = reinterpret_cast<const float4*>(W + (size_t)row * K);
     float acc[MT];
 #pragma unroll
     for (int t = 0; t < MT; t++) acc[t] = 0.f;
-#pragma unroll 4
-    for (int i = threadIdx.x; i < K / 4; i += F32_NT) {
-        const float4 w = __ldg(w4 + i);
-        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
-        if (nw) g = __ldg(reinterpret_cast<const float4*>(nw) + i);
+    // element groups i = tid, tid + F32_NT, ... in order (the first F32_PF from the prefetched registers)
+    auto step = [&](const float4& w, const float4& g, int i) {
 #pragma unroll
         for (int t = 0; t < MT; t++) {
             if (t < m) {
@@ -444,7 +453,13 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
                 acc[t] = fmaf(w.x, x.x, fmaf(w.y, x.y, fmaf(w.z, x.z, fmaf(w.w, x.w, acc[t]))));
             }
         }
-    }
+    };
+#pragma unroll
+    for (int j = 0; j < F32_PF; j++)
+        if (threadIdx.x + j * F32_NT < n4) step(wpf[j], gpf[j], threadIdx.x + j * F32_NT);
+#pragma unroll 1
+    for (int i = threadIdx.x + F32_PF * F32_NT; i < n4; i += F32_NT)
+        step(__ldg(w4 + i), nw ? __ldg(g4 + i) : make_float4(1.f, 1.f, 1.f, 1.f), i);
 #pragma unroll
     for (int t = 0; t < MT; t++) {
         float v = acc[t];

@@ -93,9 +93,31 @@ __device__ __forceinline__ uint32_t lop_sel(uint32_t a, uint32_t b, uint32_t mas
 // a 16-k MMA over segment s of the block takes the u32 at byte 16 (s & 1) + 4t. Per-16-element sums
 // of x followed by the scale s (and three zeros) complete the row.
 constexpr int PREP_NT = 256;
-__device__ __forceinline__ int digit(float v) { return (int)fminf(127.f, fmaxf(-127.f, rintf(v))); }
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
+// Digits by float arithmetic only: adding 1.5 * 2^23 rounds a float of magnitude below 2^22 to an integer
+// (round to nearest even, as rintf) and leaves that integer's two's-complement low byte in the low
+// mantissa bits. __fadd_rn keeps the compiler from folding the add/subtract pair.
+constexpr float RNE_MAGIC = 12582912.0f;
+__device__ __forceinline__ float digit_f(float v) {  // rintf(v) clamped to [-127, 127]
+    return fminf(127.f, fmaxf(-127.f, __fadd_rn(__fadd_rn(v, RNE_MAGIC), -RNE_MAGIC)));
+}
+__device__ __forceinline__ uint32_t digit_byte(float d) { return __float_as_uint(__fadd_rn(d, RNE_MAGIC)) & 0xffu; }
+// The three digit planes of 8 consecutive elements x[k] * inv: plane p packs digit p of elements 0..3 in
+// .x and 4..7 in .y (byte k = element k), a = rint(v), b = rint((v - a) * 254), c = rint((... - b) * 254).
+__device__ __forceinline__ void digits8(const float (&xv)[8], float inv, uint2 (&pl)[3]) {
+    uint32_t w[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float v = __fmul_rn(xv[k], inv);  // explicit roundings: no contraction into FMAs
+        const float a0 = digit_f(v);
+        const float r1 = __fmul_rn(__fsub_rn(v, a0), DIGIT);
+        const float a1 = digit_f(r1);
+        const float a2 = digit_f(__fmul_rn(__fsub_rn(r1, a1), DIGIT));
+        w[0][k >> 2] |= digit_byte(a0) << (8 * (k & 3));
+        w[1][k >> 2] |= digit_byte(a1) << (8 * (k & 3));
+        w[2][k >> 2] |= digit_byte(a2) << (8 * (k & 3));
+    }
+#pragma unroll
+    for (int p = 0; p < 3; p++) pl[p] = make_uint2(w[p][0], w[p][1]);
 }
 // Group sum S of 32 elements (already divided by the row scale) -> f16 high part and residue at
 // gs + 16 + sb * 32 + 2g and + 16 (see XF).
@@ -136,21 +158,11 @@ __device__ __forceinline__ void prep_row(const float* __restrict__ x, int K, uin
         const float4 u = *reinterpret_cast<const float4*>(x + 32 * j + 8 * t);
         const float4 w = *reinterpret_cast<const float4*>(x + 32 * j + 8 * t + 4);
         const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
-        int dg[3][8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const float v = xv[k] * inv;
-            const int a0 = digit(v);
-            const float r1 = (v - (float)a0) * DIGIT;
-            const int a1 = digit(r1);
-            dg[0][k] = a0;
-            dg[1][k] = a1;
-            dg[2][k] = digit((r1 - (float)a1) * DIGIT);
-        }
+        uint2 pl[3];
+        digits8(xv, inv, pl);
         uint2* o = frag + (size_t)j * 12 + t;
 #pragma unroll
-        for (int p = 0; p < 3; p++)
-            o[p * 4] = make_uint2(pack4(dg[p][0], dg[p][1], dg[p][2], dg[p][3]), pack4(dg[p][4], dg[p][5], dg[p][6], dg[p][7]));
+        for (int p = 0; p < 3; p++) o[p * 4] = pl[p];
         // segment sums: lanes t = 0,1 hold segment 2j, t = 2,3 segment 2j + 1 (items i, i^1 are
         // adjacent lanes of the same warp: nthr is a multiple of 32 and items advance by nthr)
         float s8 = ((u.x + u.y) + (u.z + u.w)) + ((w.x + w.y) + (w.z + w.w));

@@ -102,7 +102,7 @@ __device__ void drain(uint64_t* full, int issued, int consumed, int S) {
 }
 
 // ---- shared-memory plan of the persistent kernels ---------------------------------------------------
-//   [0, 128)     mbarriers: full[4], empty[4], done[4], xready[2]
+//   [0, 128)     mbarriers: full[4], empty[4], done[4], the down kernel's consumer barrier
 //   info         per-stage unit descriptors (int4)
 //   cnt          per-stage finished-warp counters
 //   xf           two XF staging buffers (double-buffered by group)
@@ -136,6 +136,7 @@ __host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, si
 constexpr int NWC_GU = 16;   // consumer warps of the gate/up kernel
 constexpr int NWC_DN = 12;   // consumer warps of the down kernel
 constexpr int DN_ROWS = 64;  // rows of D per down unit
+constexpr int DN_PREP_ITEMS = 2;  // 8-element items of a group's h rows per consumer thread: MU * FF <= 6144
 // Gate/up tiles: 16 rows of a matrix. Rows of a multiple of 16 bytes come as two 8-row copies, the
 // second at split8_off(rb) (32 bytes past a 128-byte boundary, so that rows 0..7 and 8..15 start on
 // different banks); other rows as one contiguous span copy.
@@ -147,6 +148,10 @@ __host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu, size_
 }
 __host__ __device__ inline Plan down_plan(int FF, size_t rbd, size_t route_bytes = 0) {
     return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0, route_bytes);
+}
+// the down kernel's shared-memory copy of the group list (small batches, whose gate/up kernel routed)
+__host__ __device__ inline size_t down_cache_bytes(const MoeArgs& a) {
+    return a.fused_route ? (size_t)a.T * a.n_used * sizeof(GroupRec) : 0;
 }
 
 // info word y: xf buffer (bit 0), slots in the group (bits 4-7), weights usable (bit 8), first unit of
@@ -179,45 +184,22 @@ __device__ __forceinline__ void warp_values(const float (&acc)[1][4], const floa
     }
 }
 
-// One warp puts a row x of K floats (global, written by an earlier grid) in fragment form into
-// shared memory: frag (K*3 bytes) and gs (the scale, then the group sums; XF).
-__device__ void prep_row_warp(const float* __restrict__ x, int K, uint2* __restrict__ frag, uint8_t* __restrict__ gs) {
-    const int lane = threadIdx.x & 31, nblk = K >> 5;
-    float mx = 0.f;
-    for (int i = lane; i < (K >> 2); i += 32) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(x) + i);
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
+// Item i of a row in fragment form (block j = i / 4, lane t = i % 4: elements 8i .. 8i + 7, held in u, w):
+// its three digit planes into frag and, from lane t = 0 of each block, the group sum into gs. All 32
+// lanes of the warp take part (shuffles).
+__device__ __forceinline__ void prep_item(const float4& u, const float4& w, int i, float inv, uint2* __restrict__ frag,
+                                          uint8_t* __restrict__ gs) {
+    const int j = i >> 2, t = i & 3;
+    const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+    uint2 pl[3];
+    digits8(xv, inv, pl);
+    uint2* o = frag + (size_t)j * 12 + t;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (!(mx > 0.f) || mx == INFINITY) mx = 127.f;
-    if (lane == 0) *reinterpret_cast<float4*>(gs) = make_float4(mx / 127.f, 0.f, 0.f, 0.f);
-    const float inv = 127.f / mx;
-    for (int i = lane; i < nblk * 4; i += 32) {  // nblk * 4 is a multiple of 32 (K % 256 == 0)
-        const int j = i >> 2, t = i & 3;
-        const float4 u = __ldcg(reinterpret_cast<const float4*>(x + 32 * j + 8 * t));
-        const float4 w = __ldcg(reinterpret_cast<const float4*>(x + 32 * j + 8 * t + 4));
-        const float xv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
-        int dg[3][8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const float v = xv[k] * inv;
-            const int a0 = digit(v);
-            const float r1 = (v - (float)a0) * DIGIT;
-            const int a1 = digit(r1);
-            dg[0][k] = a0;
-            dg[1][k] = a1;
-            dg[2][k] = digit((r1 - (float)a1) * DIGIT);
-        }
-        uint2* o = frag + (size_t)j * 12 + t;
-#pragma unroll
-        for (int p = 0; p < 3; p++)
-            o[p * 4] = make_uint2(pack4(dg[p][0], dg[p][1], dg[p][2], dg[p][3]), pack4(dg[p][4], dg[p][5], dg[p][6], dg[p][7]));
-        float s8 = ((u.x + u.y) + (u.z + u.w)) + ((w.x + w.y) + (w.z + w.w));
-        s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
-        s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
-        if (t == 0) put_group_sum(gs, j, s8 * inv);
-    }
+    for (int p = 0; p < 3; p++) o[p * 4] = pl[p];
+    float s8 = ((u.x + u.y) + (u.z + u.w)) + ((w.x + w.y) + (w.z + w.w));
+    s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+    s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+    if (t == 0) put_group_sum(gs, j, s8 * inv);
 }
 
 // The super-blocks sb0, sb0 + step, ... of one warp on a staged 16-row block (rows.r[0], rows.r[1]: the
@@ -285,13 +267,6 @@ __device__ __forceinline__ int gu_row(size_t rb, int g, int i) {
 // ------------------------------------------------------------------------------------------------
 // routing, grouping and activation prep
 // ------------------------------------------------------------------------------------------------
-// Position of the n-th (0-based) set bit of m (n < popcount(m)).
-__device__ __forceinline__ int nth_bit(unsigned long long m, int n) {
-    const int lo = __popc((unsigned)m);
-    if (n < lo) return (int)__fns((unsigned)m, 0, n + 1);
-    return 32 + (int)__fns((unsigned)(m >> 32), 0, n - lo + 1);
-}
-
 // Orderable key of a float: a larger float has a larger key; only one NaN pattern maps to 0, which is
 // reserved for "no entry".
 __device__ __forceinline__ uint32_t fkey(float f) {
@@ -409,21 +384,37 @@ __device__ void route_token(const float* __restrict__ lg, int E, int K, int lane
 }
 
 // Shared-memory views of one block's routing of T <= MOE_TMAX tokens (E <= MAX_EXPERTS experts).
+constexpr int RT_TEAMS = 4;  // tokens ranked at once by a routing block (128 threads each)
+// 32-bit words of one token group's ranking scratch (spl teams per token; see route_block)
+__host__ __device__ constexpr int rt_group_words(int E, int spl) {
+    return 2 * ((E + 7) & ~7) + (spl > 1 ? spl * ((E + 7) & ~7) : 0) + 72;
+}
+__host__ __device__ constexpr int rt_max(int a, int b) { return a > b ? a : b; }
+// ranking scratch: RT_TEAMS single-team groups or one group of RT_TEAMS teams, or 64 words per warp of
+// route_token (k_moe_route)
+__host__ __device__ constexpr int rt_scr_words(int E) {
+    return rt_max(rt_max(RT_TEAMS * rt_group_words(E, 1), rt_group_words(E, RT_TEAMS)), (ROUTE_NT / 32 + 2) * 64);
+}
+static_assert(RT_TEAMS == 4, "route_block's team split");
+static_assert(ROUTE_NT >= MAX_EXPERTS && ROUTE_NT % 128 == 0, "route_block: one thread per expert");
+static_assert((NWC_GU + 1) * 32 >= MAX_EXPERTS, "route_block in the gate/up kernel: one thread per expert");
 struct RouteSm {
     int *cnt, *off, *goff;        // [E] slots, slot offset, group offset per expert
     unsigned long long* mask;     // [E] tokens routed to the expert
     int* s_ids;                   // [T*K] routed experts, rank order
     float* s_w;                   // [T*K] their weights
-    uint32_t* s_rk;               // [warps * 64] ranking scratch of route_token
+    float* scr;                   // [rt_scr_words(E)] ranking scratch (16-byte aligned)
     int* g_info;                  // optional [G][4]: expert, first slot, slots, unused; G <= T*K
     int* g_tok;                   // optional [G][MU]
     const uint8_t** g_w;          // optional [G][3]: gate, up and down matrices of the group's expert
+    const uint8_t** tab;          // optional [3][E]: the gate, up and down matrix of every expert
     int* G;                       // number of groups
 };
 // bytes of a RouteSm for E experts and TK = T*K slots; with_groups adds the shared-memory group list
+// and the experts' matrix table
 __host__ __device__ constexpr size_t route_sm_bytes(int E, int TK, bool with_groups) {
-    return (size_t)E * (8 + 4 + 4 + 4) + (size_t)TK * 8 + (size_t)(ROUTE_NT / 32 + 2) * 64 * 4 + 16 +
-           (with_groups ? 16 + (size_t)TK * (24 + 16 + 4 * MU) : 0);  // 16: alignment of the group list
+    return (size_t)E * (8 + 4 + 4 + 4) + (size_t)TK * 8 + 16 + (size_t)rt_scr_words(E) * 4 + 16 +
+           (with_groups ? 16 + (size_t)TK * (24 + 16 + 4 * MU) + (size_t)E * 24 : 0);  // 16: alignment
 }
 __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_groups) {
     RouteSm r;
@@ -434,148 +425,309 @@ __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_gr
     r.goff = r.off + E;
     r.s_ids = r.goff + E;
     r.s_w = reinterpret_cast<float*>(r.s_ids + TK);
-    r.s_rk = reinterpret_cast<uint32_t*>(r.s_w + TK);
-    r.G = reinterpret_cast<int*>(r.s_rk + (ROUTE_NT / 32 + 2) * 64);
+    r.scr = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(r.s_w + TK) + 15) & ~(uintptr_t)15);
+    r.G = reinterpret_cast<int*>(r.scr + rt_scr_words(E));
     p = reinterpret_cast<uint8_t*>(r.G + 4);  // 16 bytes
     p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 15) & ~(uintptr_t)15);
     if (with_groups) {
         r.g_w = reinterpret_cast<const uint8_t**>(p);
         r.g_info = reinterpret_cast<int*>(p + (size_t)TK * 24);
         r.g_tok = r.g_info + 4 * TK;
+        r.tab = reinterpret_cast<const uint8_t**>(r.g_tok + MU * TK);  // 8-byte aligned: TK * (40 + 4 MU)
     } else {
         r.g_w = nullptr;
         r.g_info = nullptr;
         r.g_tok = nullptr;
+        r.tab = nullptr;
     }
     return r;
 }
 
-// The routing of the T tokens by every thread of the block (qwen3moe.cpp:1009-1029): top-k per token (one
-// warp per token), per-expert counts and token masks, scans, work groups of up to MU slots per expert
-// (expert ascending), slot maps. With `global` the results go to a.rw (routing outputs, groups and slot
-// maps for the later kernels); with r.g_info the group list also stays in shared memory.
+// The routing of the T tokens by every thread of the block (qwen3moe.cpp:1009-1029): top-k per token,
+// per-expert counts and token masks, scans, work groups of up to MU slots per expert (expert ascending),
+// slot maps. With `global` the results go to a.rw (routing outputs, groups and slot maps for the later
+// kernels); with r.g_info the group list also stays in shared memory. TEAMS: a few tokens, each ranked
+// by a team of 128 threads (latency); otherwise one warp per token (route_token; throughput).
+// Requires blockDim.x >= E (one thread per expert in the scans).
+template <bool TEAMS>
 __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
     for (int i = tid; i < E; i += blockDim.x) {
         r.cnt[i] = 0;
         r.mask[i] = 0ull;
     }
     __syncthreads();
-    // ---- softmax numerators, top-k, renormalisation: one warp per token (qwen3moe.cpp:1012-1022)
-    const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
-    for (int t = warp; t < T; t += nwarp) {
-        int my_e = 0;
-        float my_w = 0.f;
-        if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, r.s_rk + warp * 64, my_e, my_w);
-        else if (E <= 256) route_token<8>(a.logits + (size_t)t * E, E, K, lane, r.s_rk + warp * 64, my_e, my_w);
-        else route_token<16>(a.logits + (size_t)t * E, E, K, lane, r.s_rk + warp * 64, my_e, my_w);
-        if (lane < K) {
-            if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
-                if (global) set_flag(a.status, ST_BAD_INDEX);
-                my_e = 0;
+    // ---- softmax numerators, top-k, renormalisation (qwen3moe.cpp:1012-1022). A team of 128 threads
+    // (4 warps, named barrier 1 + team) ranks one token: every entry's r = (float)exp((double)(l - max))
+    // with the difference in fp32 as on the CPU, then each entry's rank under the comparator (r desc,
+    // index asc) of std::partial_sort by counting the entries ahead of it; ranks < K are the top k, summed
+    // in rank order for the weights r / sum.
+    const int nteam = nwarp >= 16 ? 4 : nwarp >= 8 ? 2 : 1, team = warp >> 2, tt = tid & 127;  // RT_TEAMS = 4
+    if constexpr (!TEAMS) {
+        for (int t = warp; t < T; t += nwarp) {
+            int my_e = 0;
+            float my_w = 0.f;
+            uint32_t* rk = reinterpret_cast<uint32_t*>(r.scr) + warp * 64;
+            if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
+            else if (E <= 256) route_token<8>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
+            else route_token<16>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
+            if (lane < K) {
+                if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+                    if (global) set_flag(a.status, ST_BAD_INDEX);
+                    my_e = 0;
+                }
+                r.s_ids[t * K + lane] = my_e;
+                r.s_w[t * K + lane] = my_w;
+                if (global) {
+                    a.rw.ids[(size_t)t * K + lane] = my_e;
+                    a.rw.wts[(size_t)t * K + lane] = my_w;
+                }
+                atomicAdd(&r.cnt[my_e], 1);
+                atomicOr(&r.mask[my_e], 1ull << t);
             }
-            r.s_ids[t * K + lane] = my_e;
-            r.s_w[t * K + lane] = my_w;
-            if (global) {
-                a.rw.ids[(size_t)t * K + lane] = my_e;
-                a.rw.wts[(size_t)t * K + lane] = my_w;
+        }
+    } else if (team < nteam) {
+        // One token per group of spl teams: spl = nteam for a single token (the decode case), else 1.
+        // Group scratch: [E8] 64-bit keys, [spl][E8] partial ranks (spl > 1), [4] warp maxima, [32] r and
+        // [32] ids by rank, a NaN flag. Key of entry e: (bits of r) << 32 | ~e, so that a larger key ranks
+        // first under (r desc, index asc) (r >= 0: its bits order as the floats do).
+        const int spl = T == 1 ? nteam : 1, ngrp = nteam / spl, grp = team / spl, q = team % spl;
+        const int E8 = (E + 7) & ~7;
+        uint64_t* keys = reinterpret_cast<uint64_t*>(r.scr + (size_t)grp * rt_group_words(E, spl));
+        int* part = reinterpret_cast<int*>(keys + E8);
+        float* wmax = reinterpret_cast<float*>(part + (spl > 1 ? spl * E8 : 0));
+        float* sel_r = wmax + 4;
+        int* sel_e = reinterpret_cast<int*>(sel_r + 32);
+        int* nan_flag = sel_e + 32;
+        auto team_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(1 + team) : "memory"); };
+        auto group_sync = [&]() {
+            if (spl == 1) team_sync();
+            else asm volatile("bar.sync %0, %1;" ::"r"(5 + grp), "r"(128 * spl) : "memory");
+        };
+        const int ept = (E + 127) >> 7;  // entries per thread: e = tt + 128 j
+        for (int t0 = 0; t0 < T; t0 += ngrp) {
+            const int t = t0 + grp;
+            if (t >= T) break;  // whole groups
+            bool nanv[4] = {false, false, false, false};
+            if (q == 0) {  // the group's first team: numerators and keys
+                const float* lg = a.logits + (size_t)t * E;
+                float l[4];
+                float mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int e = tt + 128 * j;
+                    l[j] = j < ept && e < E ? __ldg(lg + e) : -INFINITY;
+                    mx = fmaxf(mx, l[j]);
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (lane == 0) wmax[tt >> 5] = mx;
+                if (tt < 32) sel_e[tt] = -1;
+                if (tt == 0) *nan_flag = 0;
+                team_sync();
+                mx = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int e = tt + 128 * j;
+                    if (j < ept && e < E8) {
+                        uint64_t k = 0;  // padding entries and NaN: below every real key
+                        if (e < E) {
+                            const float rv = (float)exp((double)(l[j] - mx));
+                            if (rv != rv) {
+                                nanv[j] = true;
+                                *nan_flag = 1;
+                            } else {
+                                k = ((uint64_t)__float_as_uint(rv) << 32) | (uint32_t)~(uint32_t)e;
+                            }
+                        }
+                        keys[e] = k;
+                    }
+                }
             }
-            atomicAdd(&r.cnt[my_e], 1);
-            atomicOr(&r.mask[my_e], 1ull << t);
+            group_sync();
+            // ranks: entry e's count of larger keys among this team's share [q E8 / spl, (q+1) E8 / spl)
+            const int f0 = q * (E8 / spl), f1 = f0 + E8 / spl;
+            int rk[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int e = tt + 128 * j;
+                if (j < ept && e < E) {
+                    const uint64_t me = keys[e];
+                    int c0 = 0, c1 = 0;
+#pragma unroll 4
+                    for (int f = f0; f < f1; f += 2) {
+                        const ulonglong2 kk = *reinterpret_cast<const ulonglong2*>(keys + f);
+                        c0 += kk.x > me;
+                        c1 += kk.y > me;
+                    }
+                    rk[j] = c0 + c1;
+                    if (spl > 1) part[q * E8 + e] = rk[j];
+                }
+            }
+            if (spl > 1) group_sync();
+            if (q == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int e = tt + 128 * j;
+                    if (j < ept && e < E && !nanv[j]) {
+                        int rank = rk[j];
+                        for (int qq = 1; qq < spl; qq++) rank += part[qq * E8 + e];
+                        if (rank < K) {
+                            sel_r[rank] = __uint_as_float((uint32_t)(keys[e] >> 32));
+                            sel_e[rank] = e;
+                        }
+                    }
+                }
+                team_sync();
+                if (tt < K) {
+                    float tot = 0.f;
+                    for (int k = 0; k < K; k++) tot += sel_r[k];  // rank-order sum
+                    int my_e = *nan_flag ? -1 : sel_e[tt];
+                    const float my_w = __fdiv_rn(sel_r[tt], tot);
+                    if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+                        if (global) set_flag(a.status, ST_BAD_INDEX);
+                        my_e = 0;
+                    }
+                    r.s_ids[t * K + tt] = my_e;
+                    r.s_w[t * K + tt] = my_w;
+                    if (global) {
+                        a.rw.ids[(size_t)t * K + tt] = my_e;
+                        a.rw.wts[(size_t)t * K + tt] = my_w;
+                    }
+                    atomicAdd(&r.cnt[my_e], 1);
+                    atomicOr(&r.mask[my_e], 1ull << t);
+                }
+            }
+            group_sync();  // the scratch is reused by the group's next token
         }
     }
     __syncthreads();
-    // ---- exclusive scans: slots per expert, groups per expert (ceil(count / MU)), active experts;
-    // lane i covers experts [i * per, (i + 1) * per)
-    const int per = (E + 31) >> 5;
-    if (warp == 0) {
-        int c_in = 0, g_in = 0, a_in = 0;
-        for (int j = 0; j < per; j++) {
-            const int e = lane * per + j;
-            const int c = e < E ? r.cnt[e] : 0;
-            c_in += c;
-            g_in += (c + MU - 1) / MU;
-            a_in += c > 0;
-        }
-        int c_x = c_in, g_x = g_in, a_x = a_in;  // inclusive warp scans
+    // ---- exclusive scans over the experts (thread e: slots, groups of ceil(count / MU), active flag);
+    // E <= blockDim.x
+    {
+        int* wtot = reinterpret_cast<int*>(r.scr);  // [3][32] per-warp totals (the ranking scratch is free)
+        const int e = tid;
+        const int c = e < E ? r.cnt[e] : 0, g = (c + MU - 1) / MU, ac = c > 0;
+        int cx = c, gx = g, ax = ac;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, c_x, o), gv = __shfl_up_sync(0xffffffffu, g_x, o),
-                      av = __shfl_up_sync(0xffffffffu, a_x, o);
+            const int v = __shfl_up_sync(0xffffffffu, cx, o), gv = __shfl_up_sync(0xffffffffu, gx, o),
+                      av = __shfl_up_sync(0xffffffffu, ax, o);
             if (lane >= o) {
-                c_x += v;
-                g_x += gv;
-                a_x += av;
+                cx += v;
+                gx += gv;
+                ax += av;
             }
-        }
-        int c_run = c_x - c_in, g_run = g_x - g_in, a_run = a_x - a_in;
-        for (int j = 0; j < per; j++) {
-            const int e = lane * per + j;
-            if (e >= E) break;
-            const int c = r.cnt[e];
-            r.off[e] = c_run;
-            r.goff[e] = g_run;
-            if (global) {
-                a.rw.offsets[e] = c_run;
-                if (c > 0) a.rw.active[1 + a_run] = e;
-            }
-            a_run += c > 0;
-            c_run += c;
-            g_run += (c + MU - 1) / MU;
         }
         if (lane == 31) {
-            *r.G = g_x;
+            wtot[warp] = cx;
+            wtot[32 + warp] = gx;
+            wtot[64 + warp] = ax;
+        }
+        __syncthreads();
+        int cb = 0, gb = 0, ab = 0;
+        for (int w = 0; w < warp; w++) {
+            cb += wtot[w];
+            gb += wtot[32 + w];
+            ab += wtot[64 + w];
+        }
+        if (e < E) {
+            r.off[e] = cb + cx - c;
+            r.goff[e] = gb + gx - g;
             if (global) {
-                a.rw.offsets[E] = c_x;
-                a.rw.active[0] = a_x;
-                a.rw.ngroups[0] = g_x;
+                a.rw.offsets[e] = cb + cx - c;
+                if (ac) a.rw.active[1 + ab + ax - 1] = e;
+            }
+        }
+        if (e == E - 1) {
+            *r.G = gb + gx;
+            if (global) {
+                a.rw.offsets[E] = cb + cx;
+                a.rw.active[0] = ab + ax;
+                a.rw.ngroups[0] = gb + gx;
             }
         }
     }
     __syncthreads();
-    // ---- work list: groups of up to MU consecutive slots of one expert, expert ascending
+    // ---- work list: groups of up to MU consecutive slots of one expert, expert ascending. Expert threads
+    // write each group's expert, first slot and size (and zero token entries past the size); the
+    // (token, k) threads below fill in the tokens.
     for (int e = tid; e < E; e += blockDim.x) {
         const int c = r.cnt[e];
         if (c == 0) continue;
-        const uint8_t* wg = a.gate[e];
-        const uint8_t* wu = a.up[e];
-        const uint8_t* wd = a.down[e];
+        const uint8_t* wg = r.tab ? r.tab[e] : a.gate[e];
+        const uint8_t* wu = r.tab ? r.tab[E + e] : a.up[e];
+        const uint8_t* wd = r.tab ? r.tab[2 * E + e] : a.down[e];
         for (int j = 0; j * MU < c; j++) {
-            const int gi = r.goff[e] + j;
-            GroupRec rec;
-            rec.w[0] = wg;
-            rec.w[1] = wu;
-            rec.w[2] = wd;
-            rec.e = e;
-            rec.s0 = r.off[e] + j * MU;
-            rec.mc = min(MU, c - j * MU);
-#pragma unroll
-            for (int k = 0; k < MU; k++) rec.tok[k] = k < rec.mc ? nth_bit(r.mask[e], j * MU + k) : 0;
-            if (global) a.rw.groups[gi] = rec;
+            const int gi = r.goff[e] + j, s0 = r.off[e] + j * MU, mc = min(MU, c - j * MU);
+            if (global) {
+                GroupRec& g = a.rw.groups[gi];
+                g.w[0] = wg;
+                g.w[1] = wu;
+                g.w[2] = wd;
+                g.e = e;
+                g.s0 = s0;
+                g.mc = mc;
+                for (int k = mc; k < MU; k++) g.tok[k] = 0;
+            }
             if (r.g_info) {
                 r.g_info[4 * gi] = e;
-                r.g_info[4 * gi + 1] = rec.s0;
-                r.g_info[4 * gi + 2] = rec.mc;
-#pragma unroll
-                for (int k = 0; k < MU; k++) r.g_tok[MU * gi + k] = rec.tok[k];
+                r.g_info[4 * gi + 1] = s0;
+                r.g_info[4 * gi + 2] = mc;
+                for (int k = mc; k < MU; k++) r.g_tok[MU * gi + k] = 0;
                 r.g_w[3 * gi] = wg;
                 r.g_w[3 * gi + 1] = wu;
                 r.g_w[3 * gi + 2] = wd;
             }
         }
     }
-    if (!global) return;
-    // ---- stable scatter, one thread per (token, k): slot = offset[e] + earlier tokens routed to e;
-    // the token's slots in ascending order (= expert order) by rank among its k experts
+    // ---- one thread per (token, k): the slot is offset[e] + the earlier tokens routed to e (stable
+    // scatter); its group and place in the group follow; the token's slots in ascending order (= expert
+    // order) by rank among its k experts
     for (int i = tid; i < T * K; i += blockDim.x) {
         const int t = i / K;
         const int e = r.s_ids[i];
-        const int sl = r.off[e] + __popcll(r.mask[e] & ((1ull << t) - 1ull));
-        a.rw.slot_token[sl] = t;
-        a.rw.slot_w[sl] = r.s_w[i];
-        int rank = 0;
-        for (int j = 0; j < K; j++) rank += r.s_ids[t * K + j] < e;
-        a.rw.token_slots[(size_t)t * K + rank] = sl;
+        const int pos = __popcll(r.mask[e] & ((1ull << t) - 1ull)), sl = r.off[e] + pos;
+        const int gi = r.goff[e] + pos / MU;
+        if (r.g_tok) r.g_tok[MU * gi + pos % MU] = t;
+        if (global) {
+            a.rw.groups[gi].tok[pos % MU] = t;
+            a.rw.slot_token[sl] = t;
+            a.rw.slot_w[sl] = r.s_w[i];
+            int rank = 0;
+            for (int j = 0; j < K; j++) rank += r.s_ids[t * K + j] < e;
+            a.rw.token_slots[(size_t)t * K + rank] = sl;
+        }
+    }
+}
+
+// The down matrices of the experts routed in r (ascending expert order, D * down_rb bytes each) as one
+// byte range, split evenly over the grid: this CTA's share goes to L2 in pieces of at most 32 KB. One
+// warp; a hint only (nothing waits for it). Skipped when a matrix is not a 16-byte multiple.
+__device__ void down_l2_prefetch(const MoeArgs& a, const RouteSm& r) {
+    const int E = a.n_expert, lane = threadIdx.x & 31;
+    const size_t per = (size_t)a.D * a.down_rb;
+    if (per % 16) return;
+    int n_act = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) n_act += __popc(__ballot_sync(0xffffffffu, e0 + lane < E && r.cnt[e0 + lane] > 0));
+    const size_t total = (size_t)n_act * per;
+    const size_t lo = (total * blockIdx.x / gridDim.x) & ~(size_t)15;
+    const size_t hi = blockIdx.x + 1 == gridDim.x ? total : (total * (blockIdx.x + 1) / gridDim.x) & ~(size_t)15;
+    int base = 0;
+    for (int e0 = 0; e0 < E && lo < hi; e0 += 32) {
+        const int e = e0 + lane;
+        const bool act = e < E && r.cnt[e] > 0;
+        const unsigned m = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const size_t k = (size_t)(base + __popc(m & ((1u << lane) - 1u)));
+            const size_t s0 = k * per > lo ? k * per : lo, s1 = (k + 1) * per < hi ? (k + 1) * per : hi;
+            const uint8_t* w = r.tab[2 * E + e];
+            if ((reinterpret_cast<uintptr_t>(w) & 15) == 0)
+                for (size_t o = s0; o < s1; o += 32768)
+                    l2_prefetch_bulk(w + (o - k * per), (uint32_t)(s1 - o < 32768 ? s1 - o : 32768));
+        }
+        base += __popc(m);
     }
 }
 
@@ -591,7 +743,7 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         return;
     }
     __shared__ __align__(16) uint8_t rsm[route_sm_bytes(MAX_EXPERTS, MOE_TMAX * 32, false) + 16];
-    route_block(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
+    route_block<false>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -618,16 +770,22 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         abort_flag = 0;
         mbar_fence_init();
     }
+    RouteSm rt{};
+    if (a.fused_route) {  // the experts' matrix table does not depend on earlier grids
+        rt = route_sm_carve(sm + pl.extra_off, a.n_expert, TK, true);
+        const int E = a.n_expert;
+        for (int i = tid; i < 3 * E; i += blockDim.x) rt.tab[i] = i < E ? a.gate[i] : i < 2 * E ? a.up[i - E] : a.down[i - 2 * E];
+    }
     __syncthreads();
     pdl_trigger();
     pdl_wait();  // routing results (or the logits) and the XF of the tokens come from the previous grids
     // small batches: every CTA routes the tokens itself into shared memory (CTA 0 also publishes the
-    // routing, groups and slot maps for the down kernel and the combine)
-    RouteSm rt{};
+    // routing, groups and slot maps for the down kernel and the combine), then asks L2 for its share of
+    // the routed experts' down matrices, which the down kernel streams next
     if (a.fused_route) {
-        rt = route_sm_carve(sm + pl.extra_off, a.n_expert, TK, true);
-        route_block(a, rt, blockIdx.x == 0);
+        route_block<true>(a, rt, blockIdx.x == 0);
         __syncthreads();
+        if (warp == 0) down_l2_prefetch(a, rt);
     }
     const int G = a.fused_route ? *rt.G : a.rw.ngroups[0];
     auto group = [&](int gi) {
@@ -772,12 +930,12 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t rb = a.down_rb;
-    const Plan pl = down_plan(FF, rb);
+    const Plan pl = down_plan(FF, rb, down_cache_bytes(a));
     const int S = pl.S;
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + 4;
     uint64_t* done = full + 8;     // per stage: every consumer warp has stored its partial results
-    uint64_t* xready = full + 12;  // per XF buffer: its rows are in fragment form (MU warp arrivals)
+    uint64_t* cbar = full + 12;    // the consumer warps' barrier of the h-row prep (one arrival per warp)
     int4* info = reinterpret_cast<int4*>(sm + pl.info_off);
     __shared__ int abort_flag;
     if (tid == 0) {
@@ -786,16 +944,24 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
             mbar_init(&empty[s], NWC_DN);
             mbar_init(&done[s], NWC_DN);
         }
-        mbar_init(&xready[0], MU);
-        mbar_init(&xready[1], MU);
+        mbar_init(cbar, NWC_DN);
         abort_flag = 0;
         mbar_fence_init();
     }
     __syncthreads();
     pdl_trigger();
     pdl_wait();  // h and the routing come from the previous grids
+    // small batches: the whole group list (at most T*K records) is read into shared memory in the same
+    // round trip as its length
+    GroupRec* gcache = a.fused_route ? reinterpret_cast<GroupRec*>(sm + pl.extra_off) : nullptr;
+    if (gcache) {
+        const int4* src = reinterpret_cast<const int4*>(a.rw.groups);
+        int4* dst = reinterpret_cast<int4*>(gcache);
+        for (int i = tid; i < a.T * a.n_used * (int)(sizeof(GroupRec) / 16); i += blockDim.x) dst[i] = __ldcg(src + i);
+    }
     const int G = a.rw.ngroups[0];
-    auto group = [&](int gi) { return a.rw.groups[gi]; };
+    if (gcache) __syncthreads();
+    auto group = [&](int gi) { return gcache ? gcache[gi] : a.rw.groups[gi]; };
     const int nunits = G * NRG;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const Rows L = rows_of(rb);
@@ -842,22 +1008,67 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
 
     // ---------------- consumers: warp w works on rows 16 (w / 3) .. +15 of the unit, super-blocks w % 3 + 3j
     const int rbk = warp / 3, wsub = warp - 3 * rbk, t = lane & 3;
-    // h rows of a group -> fragment form in XF buffer xb: warp k < MU preps slot s0 + k (if the group
-    // has it), then arrives on xready[xb]
-    auto prep_group = [&](int xb, int s0, int mc) {
-        if (warp < MU) {
-            uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
-            if (warp < mc)
-                prep_row_warp(a.h + (size_t)(s0 + warp) * FF, FF, reinterpret_cast<uint2*>(xs + (size_t)warp * FF * 3),
-                              xs + xs_gs_off(FF) + (size_t)warp * xf_gs_bytes(FF));
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&xready[xb]);
+    // h rows of a group -> fragment form in XF buffer xb, by all consumer warps (bounded waits on cbar):
+    // each thread loads up to DN_PREP_ITEMS items of 8 elements (every warp's items belong to one row),
+    // the rows' max |h| are combined across the warps, then each thread writes its items' digits and
+    // sums. False after a timed-out wait (flagged; the caller ends the warp).
+    __shared__ float s_pmax[MU][NWC_DN * DN_PREP_ITEMS];
+    uint32_t cphase = 0;
+    auto consumers_sync = [&]() {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cbar);
+        if (!mbar_wait_bounded(cbar, cphase & 1u)) {
+            set_flag(a.status, ST_WAIT_TIMEOUT);
+            atomicExch(&abort_flag, 1);
+            return false;
         }
+        cphase++;
+        return true;
     };
-    int uses[2] = {0, 0};
+    auto prep_group = [&](int xb, int s0, int mc) {
+        uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
+        const int nit = FF >> 3, tot = mc * nit;  // nit % 32 == 0: warp-uniform rows and bounds
+        float4 u[DN_PREP_ITEMS], w[DN_PREP_ITEMS];
+#pragma unroll
+        for (int k = 0; k < DN_PREP_ITEMS; k++) {
+            const int it = tid + NWC_DN * 32 * k, tk = it < tot ? it / nit : 0, i = it - tk * nit;
+            float m = 0.f;
+            if (it < tot) {
+                const float4* x4 = reinterpret_cast<const float4*>(a.h + (size_t)(s0 + tk) * FF);
+                u[k] = __ldcg(x4 + 2 * i);
+                w[k] = __ldcg(x4 + 2 * i + 1);
+                m = fmaxf(fmaxf(fmaxf(fabsf(u[k].x), fabsf(u[k].y)), fmaxf(fabsf(u[k].z), fabsf(u[k].w))),
+                          fmaxf(fmaxf(fabsf(w[k].x), fabsf(w[k].y)), fmaxf(fabsf(w[k].z), fabsf(w[k].w))));
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane < MU) s_pmax[lane][warp * DN_PREP_ITEMS + k] = (it < tot && lane == tk) ? m : 0.f;
+        }
+        if (!consumers_sync()) return false;
+        float inv[MU];
+#pragma unroll
+        for (int tk = 0; tk < MU; tk++) {
+            float mx = 0.f;
+            for (int j = 0; j < NWC_DN * DN_PREP_ITEMS; j++) mx = fmaxf(mx, s_pmax[tk][j]);
+            if (!(mx > 0.f) || mx == INFINITY) mx = 127.f;
+            inv[tk] = 127.f / mx;
+            if (tid == tk && tk < mc)
+                *reinterpret_cast<float4*>(xs + xs_gs_off(FF) + (size_t)tk * xf_gs_bytes(FF)) = make_float4(mx / 127.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < DN_PREP_ITEMS; k++) {
+            const int it = tid + NWC_DN * 32 * k;
+            if (it < tot) {  // warp-uniform
+                const int tk = it / nit;
+                prep_item(u[k], w[k], it - tk * nit, tk ? inv[1] : inv[0], reinterpret_cast<uint2*>(xs + (size_t)tk * FF * 3),
+                          xs + xs_gs_off(FF) + (size_t)tk * xf_gs_bytes(FF));
+            }
+        }
+        return consumers_sync();  // the group's rows are ready for every consumer warp (and s_pmax is free)
+    };
     if (u0 < u1) {  // the first group's h rows, while the first weight tiles are in flight
         const GroupRec r0 = group(u0 / NRG);
-        prep_group(0, r0.s0, r0.mc);
+        if (!prep_group(0, r0.s0, r0.mc)) return;
     }
     int i = 0;
     for (int u = u0; u < u1; u++, i++) {
@@ -869,15 +1080,7 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         }
         const int4 in = info[s];
         const int rg = in.x, xb = in.y & 1, mc = (in.y >> 4) & 15, s0 = in.z;
-        if (in.y & 512) {  // first unit of a group in this CTA: its h rows must be in fragment form
-            if (u != u0) prep_group(xb, s0, mc);
-            if (!mbar_wait_bounded(&xready[xb], (uint32_t)uses[xb] & 1u)) {
-                set_flag(a.status, ST_WAIT_TIMEOUT);
-                atomicExch(&abort_flag, 1);
-                return;
-            }
-            uses[xb]++;
-        }
+        if ((in.y & 512) && u != u0 && !prep_group(xb, s0, mc)) return;  // a later group's first unit here
         const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
         float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
         if (in.y & 256) {
@@ -1096,14 +1299,15 @@ cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st) {
 
 template <int QD>
 static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
-    const Plan pl = down_plan(a.FF, a.down_rb);
+    const Plan pl = down_plan(a.FF, a.down_rb, down_cache_bytes(a));
     if (pl.total > SMEM_CAP || a.D / DN_ROWS < pl.S) return cudaErrorInvalidValue;
     smem_attr(k_moe_down<QD>, pl.total);
     const int units = max_groups(a) * (a.D / DN_ROWS);
     return launch_pdl(k_moe_down<QD>, dim3(std::min(sm_count(), units)), (NWC_DN + 1) * 32, pl.total, st, a);
 }
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st, bool combine) {
-    if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX) return cudaErrorInvalidValue;
+    if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX || MU * (a.FF / 8) > DN_PREP_ITEMS * NWC_DN * 32)
+        return cudaErrorInvalidValue;
     cudaError_t e;
     switch (a.down_type) {
         case T_Q4_K: e = down_as<T_Q4_K>(a, st); break;
