@@ -591,6 +591,17 @@ struct EahmmfEngine {
             const QMat W{w, type, D, rows, rb};
             if (!gemv_mma_ok(W))
                 return eahmmf_cuda_gemv(w, type, D, rows, rb, xn, nb, D, out, ldo, 0, gemv_ws, gemv_ws_bytes, st);
+            if (nb > XPASS && gemm_xf_ok(W)) {  // prompt passes: every weight tile read once
+                GemvXArgs g{};
+                g.W = W;
+                g.xf = xf_all;
+                g.m = nb;
+                g.Y = out;
+                g.ldy = ldo;
+                g.accumulate = 0;
+                g.status = status;
+                return launch_gemm_xf(g, st) == cudaSuccess ? ST_OK : ST_CUDA;
+            }
             for (int t0 = 0; t0 < nb; t0 += XPASS) {
                 GemvXArgs g{};
                 g.W = W;
@@ -658,6 +669,16 @@ struct EahmmfEngine {
                     rc = eahmmf_cuda_gemv(L.wo, L.wo_type, QD, D, L.wo_rb, att, nb, QD, x, D, 1, gemv_ws, gemv_ws_bytes,
                                           st);
                     if (rc != ST_OK) return rc;
+                } else if (nb > XPASS && gemm_xf_ok(W)) {
+                    GemvXArgs g{};
+                    g.W = W;
+                    g.xf = xf_o;
+                    g.m = nb;
+                    g.Y = x;
+                    g.ldy = D;
+                    g.accumulate = 1;
+                    g.status = status;
+                    if (launch_gemm_xf(g, st) != cudaSuccess) return ST_CUDA;
                 } else {
                     for (int t0 = 0; t0 < nb; t0 += XPASS) {
                         GemvXArgs g{};

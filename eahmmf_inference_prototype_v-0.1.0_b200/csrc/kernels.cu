@@ -310,6 +310,95 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------
+// dense K-quant GEMM over many tokens (prompt passes): the 16-row weight tile is staged once and every
+// warp runs four tokens (two column sets) over all of the tile's tasks, fetching the next task's
+// activation fragments (global memory, L2-resident) while the current one computes. Each token's value
+// is the same sum, in the same order, as k_gemv's (tile_tasks + tile_value), so results do not depend
+// on how the tokens are split into passes.
+// ------------------------------------------------------------------------------------------------
+constexpr int GX_TMAX = 64;                  // tokens per launch
+constexpr int GX_NT = 32 * (GX_TMAX / 4);    // one warp per four tokens
+constexpr int GX_SCR = 2 * 128 + 64;         // floats of per-warp scratch: two sets' partials, minimums
+__host__ __device__ inline size_t gemm_xf_smem(size_t rb, int nwarps) {
+    return 128 + slot_bytes(row_layout(rb, true), 16) + (size_t)nwarps * GX_SCR * 4;
+}
+template <int QT>
+__global__ void __launch_bounds__(GX_NT, 1) k_gemm_xf(GemvXArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int K = a.W.K, nsb = K >> 8, m = a.m, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const size_t rb = a.W.row_bytes;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
+    uint8_t* slot = sm + 128;
+    float* scr = reinterpret_cast<float*>(sm + 128 + slot_bytes(row_layout(rb, true), 16)) + (size_t)warp * GX_SCR;
+    const RowLayout L = layout_of(a.W.w, rb);
+    const int r0 = 16 * (int)blockIdx.x, r1 = min(a.W.rows, r0 + 16);
+    pdl_trigger();
+    if (tid == 0) {  // the weight rows do not depend on earlier grids: their copy starts before the wait
+        mbar_init(&bar[0], 1);
+        mbar_fence_init();
+        mbar_expect_tx(&bar[0], rows_bytes(L, a.W.w, rb, r0, r1));
+        issue_rows(L, a.W.w, rb, r0, r1, slot, &bar[0]);
+    }
+    pdl_wait();  // the activations (XF) and, when accumulating, Y come from earlier grids
+    __syncthreads();
+    if (__syncthreads_or(!mbar_wait_bounded(&bar[0], 0u))) {
+        if (tid == 0) {
+            flag(a.status, ST_WAIT_TIMEOUT);
+            drain_ring(bar, 1, 0, 1);
+        }
+        return;
+    }
+    const int tk0 = 4 * warp;
+    if (tk0 >= m) return;  // whole warps; no block-wide barrier follows
+    const int mw = min(4, m - tk0), ss = (K >> 4) + XF_SUM_PAD;
+    const BPtr<2> bp(reinterpret_cast<const uint8_t*>(a.xf.frag) + (size_t)tk0 * K * 3, K >> 5, mw);
+    const float* tsum = t < mw ? a.xf.sum + (size_t)(tk0 + t) * ss : nullptr;  // lane t's token
+    const uint8_t* rows = slot + rows_lead(L, a.W.w, rb, r0);
+    const uint8_t* rg = rows + (size_t)g * L.stride;
+    const RowsAny R{{rg, rg + 8 * (size_t)L.stride}};
+    float run[2][4] = {}, mnr[2] = {0.f, 0.f};
+    auto step = [&](int k, const KqB<QT, 2>& B) {
+        float o[2][4] = {}, mn[2] = {0.f, 0.f};
+        kq_compute<QT, 2>(R, k >> 1, k & 1, t, B, tsum != nullptr, o, mn);
+#pragma unroll
+        for (int st = 0; st < 2; st++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) run[st][i] += o[st][i];
+        mnr[0] += mn[0];
+        mnr[1] += mn[1];
+    };
+    auto tsum_at = [&](int k) { return tsum ? tsum + (k >> 1) * 16 : nullptr; };
+    KqB<QT, 2> B0, B1;
+    kq_load_b<QT, 2>(bp, 0, 0, tsum_at(0), B0);
+    for (int k = 0; k < 2 * nsb; k += 2) {  // tasks in super-block order, two per pass (B0, B1 alternate)
+        kq_load_b<QT, 2>(bp, (k + 1) >> 1, (k + 1) & 1, tsum_at(k + 1), B1);
+        step(k, B0);
+        if (k + 2 < 2 * nsb) kq_load_b<QT, 2>(bp, (k + 2) >> 1, (k + 2) & 1, tsum_at(k + 2), B0);
+        step(k + 1, B1);
+    }
+    // the warp's partial sums in tile_tasks' layout (one task), then tile_value's recombination
+#pragma unroll
+    for (int st = 0; st < 2; st++) {
+        *reinterpret_cast<float2*>(scr + st * 128 + g * 8 + 2 * t) = make_float2(run[st][0], run[st][1]);
+        *reinterpret_cast<float2*>(scr + st * 128 + (g + 8) * 8 + 2 * t) = make_float2(run[st][2], run[st][3]);
+    }
+    scr[256 + g * 4 + t] = mnr[0];
+    scr[256 + (g + 8) * 4 + t] = mnr[1];
+    __syncwarp();
+    for (int j = lane; j < 64; j += 32) {
+        const int r = j >> 2, tk = j & 3;
+        if (tk < mw && r0 + r < r1) {
+            const float* p = scr + (tk / TOK_PER_SET) * 128 + r * 8 + 3 * (tk % TOK_PER_SET);
+            const float ts = a.xf.sum[(size_t)(tk0 + tk) * ss + (K >> 4)];
+            const float v = fmaf(fmaf(fmaf(p[2], 1.0f / DIGIT, p[1]), 1.0f / DIGIT, p[0]), ts, -scr[256 + r * 4 + tk]);
+            float* y = a.Y + (size_t)(tk0 + tk) * a.ldy + r0 + r;
+            *y = a.accumulate ? *y + v : v;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // launchers
 // ------------------------------------------------------------------------------------------------
 int sm_count() {
@@ -374,6 +463,28 @@ cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st) {
         case T_Q4_K: two ? gemv_go<T_Q4_K, 2>(a, st) : gemv_go<T_Q4_K, 1>(a, st); break;
         case T_Q5_K: two ? gemv_go<T_Q5_K, 2>(a, st) : gemv_go<T_Q5_K, 1>(a, st); break;
         default: two ? gemv_go<T_Q6_K, 2>(a, st) : gemv_go<T_Q6_K, 1>(a, st); break;
+    }
+    return cudaGetLastError();
+}
+
+template <int QT>
+static void gemm_xf_go(const GemvXArgs& a, cudaStream_t st) {
+    const int nw = (a.m + 3) / 4;
+    const size_t smem = gemm_xf_smem(a.W.row_bytes, nw);
+    smem_attr(k_gemm_xf<QT>, gemm_xf_smem(a.W.row_bytes, GX_TMAX / 4));
+    launch_pdl(k_gemm_xf<QT>, dim3((a.W.rows + 15) / 16), dim3(32 * nw), smem, st, a);
+}
+
+bool gemm_xf_ok(const QMat& W) {
+    return gemv_mma_ok(W) && gemm_xf_smem(W.row_bytes, GX_TMAX / 4) <= SMEM_CAP;
+}
+
+cudaError_t launch_gemm_xf(const GemvXArgs& a, cudaStream_t st) {
+    if (a.m < 1 || a.m > GX_TMAX || !gemm_xf_ok(a.W)) return cudaErrorInvalidValue;
+    switch (a.W.type) {
+        case T_Q4_K: gemm_xf_go<T_Q4_K>(a, st); break;
+        case T_Q5_K: gemm_xf_go<T_Q5_K>(a, st); break;
+        default: gemm_xf_go<T_Q6_K>(a, st); break;
     }
     return cudaGetLastError();
 }

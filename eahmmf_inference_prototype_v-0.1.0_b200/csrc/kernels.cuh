@@ -136,6 +136,10 @@ constexpr size_t xf_bytes(int rows, int K) {
 XF xf_carve(void* base, int rows, int K);        // XF views over such a block
 cudaError_t launch_prep_x(const float* X, int ldx, int rows, int K, const XF& out, cudaStream_t st);
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st);
+// Dense K-quant GEMM over 1..64 tokens in fragment form (a.m tokens, one launch): the same per-token
+// arithmetic and summation order as launch_gemv_xf, the weight tiles read once.
+bool gemm_xf_ok(const QMat& W);
+cudaError_t launch_gemm_xf(const GemvXArgs& a, cudaStream_t st);
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st);  // per-row kernel (any type)
 // MoE block (moe.cu): routing + grouping + activation prep, then gate/up, then down, then the combine;
 // the last three are launched with programmatic stream serialization.

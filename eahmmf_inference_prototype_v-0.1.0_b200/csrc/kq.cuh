@@ -224,14 +224,51 @@ struct RowsQ6 {  // row 0 4-byte aligned, row 1 two bytes past a 4-byte boundary
     __device__ __forceinline__ uint32_t ld16(int i, int off) const { return *reinterpret_cast<const uint16_t*>(r[i] + off); }
 };
 // ---- one task: 16 rows x 128 weights (half h of super-block sb) ------------------------------------
+// The task's activation operands (B fragments of every column set, and for Q4_K/Q5_K the lane token's
+// per-16 sums of the half), loaded apart from the arithmetic so that a caller can fetch the next task's
+// while this one computes.
+template <int QT, int NSET>
+struct KqB {
+    uint2 l[2][NSET], h[2][NSET];  // Q4_K/Q5_K: 32-k blocks of the low / high nibbles of chunk cc
+    float4 sa, sb;                 // Q4_K/Q5_K: per-16 sums 8h .. 8h + 7 of the lane's token (if any)
+};
+template <int NSET>
+struct KqB<T_Q6_K, NSET> {
+    uint32_t s[2][4][NSET];  // 16-k segments
+};
+// tsum: the lane token's per-16 sums at super-block sb (nullptr when the lane has no token)
+template <int QT, int NSET, class BP>
+__device__ __forceinline__ void kq_load_b(const BP& bf, int sb, int h, const float* __restrict__ tsum, KqB<QT, NSET>& B) {
+    if constexpr (QT == T_Q4_K || QT == T_Q5_K) {
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            const int c = 2 * h + cc;
+#pragma unroll
+            for (int st = 0; st < NSET; st++) {
+                B.l[cc][st] = bf.blk(st, sb * 8 + 2 * c);      // 32-k blocks: low nibbles of chunk c,
+                B.h[cc][st] = bf.blk(st, sb * 8 + 2 * c + 1);  // then its high nibbles
+            }
+        }
+        if (tsum) {
+            B.sa = *reinterpret_cast<const float4*>(tsum + 8 * h);
+            B.sb = *reinterpret_cast<const float4*>(tsum + 8 * h + 4);
+        }
+    } else {
+#pragma unroll
+        for (int ib = 0; ib < 2; ib++)
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int st = 0; st < NSET; st++) B.s[ib][q][st] = bf.seg(st, sb * 16 + 8 * h + 2 * q + ib);
+    }
+}
 // R: the task's two rows; offsets are relative to the rows' starts (super-block sb at sb * block bytes).
 // Accumulates into out[set][4] the d-scaled int32 sums of rows g, g+8 for this lane's two digit
-// columns, and into mn[2] the group-minimum term of rows g, g+8 for token t (Q4_K/Q5_K; tsum = token t's
-// per-16 sums at super-block sb, nullptr when the lane has no token).
+// columns, and into mn[2] the group-minimum term of rows g, g+8 for token t (Q4_K/Q5_K, when has_sum:
+// B holds the token's sums).
 template <int QT, int NSET, class R>
-__device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr<NSET>& bf,
-                                        const float* __restrict__ tsum, float (&out)[NSET][4], float (&mn)[2]) {
-    const int t = bf.t;
+__device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, const KqB<QT, NSET>& B, bool has_sum,
+                                           float (&out)[NSET][4], float (&mn)[2]) {
     constexpr int BB = block_bytes(QT);
     const int o = sb * BB;
     int acc[NSET][4];
@@ -250,12 +287,10 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
         // (qwen3moe.cpp:133-141): bytes 0..3 of the selected word
         const uint32_t s0 = h ? ((H0.w & 0x0f0f0f0fu) | ((H0.y >> 2) & 0x30303030u)) : (H0.y & 0x3f3f3f3fu);
         const uint32_t s1 = h ? ((H1.w & 0x0f0f0f0fu) | ((H1.y >> 2) & 0x30303030u)) : (H1.y & 0x3f3f3f3fu);
-        if (tsum) {  // group minimums for token t: dmin * m_g * sum(x of the group)
+        if (has_sum) {  // group minimums for token t: dmin * m_g * sum(x of the group)
             const uint32_t m0 = h ? (((H0.w >> 4) & 0x0f0f0f0fu) | ((H0.z >> 2) & 0x30303030u)) : (H0.z & 0x3f3f3f3fu);
             const uint32_t m1 = h ? (((H1.w >> 4) & 0x0f0f0f0fu) | ((H1.z >> 2) & 0x30303030u)) : (H1.z & 0x3f3f3f3fu);
-            const float4 sa = *reinterpret_cast<const float4*>(tsum + 8 * h);
-            const float4 sbv = *reinterpret_cast<const float4*>(tsum + 8 * h + 4);
-            const float gs[4] = {sa.x + sa.y, sa.z + sa.w, sbv.x + sbv.y, sbv.z + sbv.w};
+            const float gs[4] = {B.sa.x + B.sa.y, B.sa.z + B.sa.w, B.sb.x + B.sb.y, B.sb.z + B.sb.w};
             float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -270,19 +305,13 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
             qh0 = rows.ld64(0, o + 16 + 8 * t);
             qh1 = rows.ld64(1, o + 16 + 8 * t);
         }
-        // all operands of the task first (weights of both chunks, activations of the four 32-k blocks)
-        uint2 w0[2], w1[2], bl[2][NSET], bh[2][NSET];
+        uint2 w0[2], w1[2];
 #pragma unroll
         for (int cc = 0; cc < 2; cc++) {
             const int c = 2 * h + cc;
             // bytes 8t..8t+7 of chunk c: low nibbles = weights 64c + 8t.., high = 64c + 32 + 8t..
             w0[cc] = rows.ld64(0, o + QS + 32 * c + 8 * t);
             w1[cc] = rows.ld64(1, o + QS + 32 * c + 8 * t);
-#pragma unroll
-            for (int st = 0; st < NSET; st++) {
-                bl[cc][st] = bf.blk(st, sb * 8 + 2 * c);  // 32-k blocks: low nibbles of chunk c,
-                bh[cc][st] = bf.blk(st, sb * 8 + 2 * c + 1);  // then its high nibbles
-            }
         }
 #pragma unroll
         for (int cc = 0; cc < 2; cc++) {
@@ -312,8 +341,8 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
             const int sl1 = LS * ubyte(s1, 2 * cc), sh1 = ubyte(s1, 2 * cc + 1);
 #pragma unroll
             for (int st = 0; st < NSET; st++) {
-                scale_acc(acc[st], imma32(lo[0], lo[1], lo[2], lo[3], bl[cc][st].x, bl[cc][st].y), sl0, sl1);
-                scale_acc(acc[st], imma32(hi[0], hi[1], hi[2], hi[3], bh[cc][st].x, bh[cc][st].y), sh0, sh1);
+                scale_acc(acc[st], imma32(lo[0], lo[1], lo[2], lo[3], B.l[cc][st].x, B.l[cc][st].y), sl0, sl1);
+                scale_acc(acc[st], imma32(hi[0], hi[1], hi[2], hi[3], B.h[cc][st].x, B.h[cc][st].y), sh0, sh1);
             }
         }
     } else {  // Q6_K: half h = 128 weights; ib selects l in [16ib, 16ib+16)
@@ -321,7 +350,7 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
         d1 = f16_to_f32(rows.ld16(1, o + 208));
         const uint32_t sc0[2] = {rows.ld32(0, o + 192 + 8 * h), rows.ld32(0, o + 196 + 8 * h)};
         const uint32_t sc1[2] = {rows.ld32(1, o + 192 + 8 * h), rows.ld32(1, o + 196 + 8 * h)};
-        uint32_t qa[2][2], qb[2][2], qh[2][2], bs[2][4][NSET];  // [ib][row]
+        uint32_t qa[2][2], qb[2][2], qh[2][2];  // [ib][row]
 #pragma unroll
         for (int ib = 0; ib < 2; ib++) {
             const int q0 = o + 16 * ib + 4 * t;
@@ -331,10 +360,6 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
                 qb[ib][r] = rows.ld32(r, q0 + 64 * h + 32);
                 qh[ib][r] = rows.ld32(r, q0 + 128 + 32 * h);
             }
-#pragma unroll
-            for (int q = 0; q < 4; q++)
-#pragma unroll
-                for (int st = 0; st < NSET; st++) bs[ib][q][st] = bf.seg(st, sb * 16 + 8 * h + 2 * q + ib);
         }
 #pragma unroll
         for (int ib = 0; ib < 2; ib++) {
@@ -351,7 +376,7 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
                 const int gl = 2 * q + ib;  // scale index within the half; segment 8h + gl of the super-block
                 const int sa = sbyte(sc0[gl >> 2], gl & 3), sbb = sbyte(sc1[gl >> 2], gl & 3);
 #pragma unroll
-                for (int st = 0; st < NSET; st++) scale_acc(acc[st], imma16s(a0, a1, bs[ib][q][st]), sa, sbb);
+                for (int st = 0; st < NSET; st++) scale_acc(acc[st], imma16s(a0, a1, B.s[ib][q][st]), sa, sbb);
             }
         }
     }
@@ -362,6 +387,14 @@ __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr
         out[st][2] = fmaf(d1, (float)acc[st][2], out[st][2]);
         out[st][3] = fmaf(d1, (float)acc[st][3], out[st][3]);
     }
+}
+// Both steps of one task (tsum: as kq_load_b).
+template <int QT, int NSET, class R>
+__device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr<NSET>& bf,
+                                        const float* __restrict__ tsum, float (&out)[NSET][4], float (&mn)[2]) {
+    KqB<QT, NSET> B;
+    kq_load_b<QT, NSET>(bf, sb, h, tsum, B);
+    kq_compute<QT, NSET>(rows, sb, h, bf.t, B, tsum != nullptr, out, mn);
 }
 
 }  // namespace eb

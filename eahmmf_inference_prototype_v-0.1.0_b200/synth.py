@@ -234,6 +234,20 @@ def config4_30b(n_layer: int = 48, seed: int = 4) -> ModelConfig:
                        d_sigma=d, f32_sigma=0.02, seed=seed)
 
 
+def config_kquant_small(n_layer: int = 3, seed: int = 6) -> ModelConfig:
+    """A small model with the config-4 structure (every projection K-quant, so the engine takes its
+    tensor-core GEMV/GEMM paths): D 512, 8q/2kv heads of 64, 16 experts top-4, FF 256, vocab 1024;
+    Q4_K q/k/v/embedding/gate, Q5_K attention output and up, Q6_K down and output."""
+    D, QD, FF = 512, 8 * 64, 256
+    d = {"attn_q": _unit_d(Q4_K, D), "attn_k": _unit_d(Q4_K, D), "attn_v": _unit_d(Q4_K, D),
+         "attn_output": _unit_d(Q5_K, QD), "ffn_gate_exps": _unit_d(Q4_K, D), "ffn_up_exps": _unit_d(Q5_K, D),
+         "ffn_down_exps": _unit_d(Q6_K, FF), "output": _unit_d(Q6_K, D), "token_embd": 1.0 / 150.0}
+    return ModelConfig("kquant-small", n_layer=n_layer, D=D, n_head=8, n_kv=2, hd=64, n_expert=16, n_used=4, FF=FF,
+                       n_vocab=1024, ctx_train=512, rope_base=1e6, embd_type=Q4_K,
+                       attn_types=(Q4_K, Q4_K, Q4_K, Q5_K), expert_types=(Q4_K, Q5_K, Q6_K), output_type=Q6_K,
+                       d_sigma=d, f32_sigma=0.02, seed=seed)
+
+
 def config5_235b(n_layer: int = 94, seed: int = 5) -> ModelConfig:
     """Config 5: Qwen3-235B-A22B shape (EP workload), Q4_K attention/gate/up, Q6_K down/output."""
     D, QD, FF = 4096, 64 * 128, 1536

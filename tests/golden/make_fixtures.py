@@ -14,7 +14,10 @@ What it does:
      anything if either check fails.
   3. Records reference outputs as fixtures: ref_tiny.npz (full logits, greedy ids, routing trace),
      config1.npz (BASELINE config 1 model), moe_c2.npz (config-2 MoE layer, T = 1, 3, 8),
-     moe_mixed.npz (Q5_K/Q4_K/Q6_K experts as in the reference's tiny model), matmul.npz (every type).
+     moe_mixed.npz (Q5_K/Q4_K/Q6_K experts as in the reference's tiny model), matmul.npz (every type),
+     kquant_small.npz (a small all-K-quant model: prompt logits and greedy ids).
+
+`--only kquant_small` regenerates just that fixture (and its entry in fixtures.json).
 """
 from __future__ import annotations
 
@@ -64,8 +67,35 @@ def token_bytes(gguf_path):
     return out
 
 
+def kquant_small(R, meta):
+    """A small model with every projection K-quant (synth.config_kquant_small): the reference engine's
+    logits and routing trace of a 40-token prompt (passes of 32) and its 16 greedy tokens after it."""
+    cfg = synth.config_kquant_small()
+    with tempfile.TemporaryDirectory() as td:
+        p = synth.write_gguf(os.path.join(td, "ks.gguf"), cfg)
+        meta["kquant_small_sha256"] = sha256(p)
+        prompt = synth._rng(cfg.seed, 0x9E1).integers(0, cfg.n_vocab, 40).astype(np.int32)
+        e = R.engine(p, 256)
+        e.trace(True)
+        lg = e.eval(prompt, 0, 32)
+        tr_ids, tr_w = e.trace_get()
+        e.close()
+        e = R.engine(p, 256)
+        gen, _ = e.greedy(prompt, 16, 32)
+        e.close()
+    np.savez_compressed(os.path.join(GOLDEN, "kquant_small.npz"), prompt=prompt, logits=lg, gen=gen.astype(np.int32),
+                        trace_ids=tr_ids, trace_w=tr_w)
+
+
 def main():
     R = oracle.Reference(threads=os.cpu_count() or 1)
+    if sys.argv[1:] == ["--only", "kquant_small"]:
+        with open(os.path.join(GOLDEN, "fixtures.json")) as f:
+            meta = json.load(f)
+        kquant_small(R, meta)
+        with open(os.path.join(GOLDEN, "fixtures.json"), "w") as f:
+            json.dump(meta, f, indent=1, sort_keys=True)
+        return
     meta = {"reference": REF}
 
     # ---- 1. reference tiny.gguf -----------------------------------------------------------------
@@ -165,6 +195,9 @@ def main():
             mm[f"x{qt}_{nb}"] = xx
             mm[f"y{qt}_{nb}"] = R.matmul(raw, qt, K, rows, rb, xx)
     np.savez_compressed(os.path.join(GOLDEN, "matmul.npz"), **mm)
+
+    # ---- 3e. small all-K-quant model ----------------------------------------------------------------
+    kquant_small(R, meta)
 
     with open(os.path.join(GOLDEN, "fixtures.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)

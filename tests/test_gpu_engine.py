@@ -2,7 +2,8 @@
 
 Pins: the reference tiny model's golden outputs (ref_tiny.npz: prompt logits, 24-token greedy
 generation of "hello world ab ab", the routing trace of a prompt + 12 decode steps) and the config-1
-synthetic model's golden outputs (config1.npz: 32 greedy tokens, first logits, routing trace), all
+synthetic model's golden outputs (config1.npz: 32 greedy tokens, first logits, routing trace) and a
+small all-K-quant model's (kquant_small.npz: prompt logits and routing trace, 16 greedy tokens), all
 produced by the reference engine (tests/golden/make_fixtures.py). Expected: greedy token ids and
 routed expert ids bit-exact; logits within 1e-4 of the largest |logit| (the reference's own GPU/CPU
 tolerance, qwen3moe.cpp:449-458) with the same argmax; routing weights within 1e-5 relative or 1e-6
@@ -144,6 +145,52 @@ def test_engine_graph_and_eager_steps_agree(config1, golden):
     rc, out, _ = config1.greedy(g["prompt"], 32, 16)
     assert rc == ST_OK
     np.testing.assert_array_equal(out, g["gen"])
+
+
+@pytest.fixture(scope="module")
+def kquant(gpu, tmp_path_factory):
+    cfg = synth.config_kquant_small()
+    path = synth.write_gguf(str(tmp_path_factory.mktemp("ks") / "ks.gguf"), cfg)
+    meta = json.load(open(os.path.join(ROOT, "tests", "golden", "fixtures.json")))
+    h = hashlib.sha256(open(path, "rb").read()).hexdigest()
+    assert h == meta["kquant_small_sha256"], "synthetic K-quant GGUF differs from the one the fixture was made from"
+    e = eb.Engine(path, 256)
+    yield e
+    e.close()
+
+
+def test_engine_kquant_prompt_matches_reference(kquant, golden):
+    """Every projection K-quant: prompt passes of 32 tokens go through the many-token tensor-core GEMM,
+    single tokens through the GEMV; logits, routing trace and greedy ids against the reference engine."""
+    g = golden("kquant_small.npz")
+    kquant.trace(True)
+    try:
+        rc, lg = kquant.eval(g["prompt"], 0, 32)
+        tr_ids, tr_w = kquant.trace_get()
+    finally:
+        kquant.trace(False)
+    assert rc == ST_OK
+    assert rel_max(lg, g["logits"]) < 1e-4
+    assert int(lg.argmax()) == int(g["logits"].argmax())
+    np.testing.assert_array_equal(tr_ids, g["trace_ids"])
+    np.testing.assert_allclose(tr_w, g["trace_w"], rtol=1e-5, atol=1e-6)
+    rc, out, _ = kquant.greedy(g["prompt"], 16, 32)
+    assert rc == ST_OK
+    np.testing.assert_array_equal(out, g["gen"])
+
+
+def test_engine_kquant_logits_independent_of_batching(kquant, golden):
+    """Per-token results are bitwise the same whether a token goes through the many-token GEMM (passes
+    of 5..64 tokens) or the GEMV (passes of 1..4)."""
+    g = golden("kquant_small.npz")
+    ref = None
+    for nb in (40, 4, 1, 13, 64, 5):
+        rc, lg = kquant.eval(g["prompt"], 0, nb)
+        assert rc == ST_OK
+        if ref is None:
+            ref = lg
+        else:
+            np.testing.assert_array_equal(lg, ref, err_msg=f"passes of {nb}")
 
 
 def test_engine_rejects_bad_arguments(tiny):
