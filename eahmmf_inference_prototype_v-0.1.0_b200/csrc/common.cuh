@@ -69,19 +69,22 @@ cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t 
     return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-// Sum of squares of a row of K floats (K % 4 == 0, 16-byte aligned) by a 128-thread block, in one fixed
-// order: every RMSNorm of the FFN input uses it, so the result does not depend on which kernel (or how
-// many tokens per pass) computed it. red4: 4 floats of shared memory.
+// Sum of squares of a row of K floats (K % 4 == 0, 16-byte aligned) by the first 128 threads of a block
+// (blockDim.x >= 128, a multiple of 32; every thread calls it), in one fixed order: every RMSNorm uses
+// it, so the result does not depend on which kernel (or how many tokens per pass) computed it. red4: 4
+// floats of shared memory.
 __device__ __forceinline__ float row_sumsq128(const float* __restrict__ x, int K, float* red4) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < K / 4; i += 128) {
-        const float4 v = reinterpret_cast<const float4*>(x)[i];
-        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    if (threadIdx.x < 128) {  // larger blocks: threads 128.. add nothing, so the order stays the same
+        for (int i = threadIdx.x; i < K / 4; i += 128) {
+            const float4 v = reinterpret_cast<const float4*>(x)[i];
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     __syncthreads();
-    if ((threadIdx.x & 31) == 0) red4[threadIdx.x >> 5] = ss;
+    if ((threadIdx.x & 31) == 0 && threadIdx.x < 128) red4[threadIdx.x >> 5] = ss;
     __syncthreads();
     return (red4[0] + red4[1]) + (red4[2] + red4[3]);
 }

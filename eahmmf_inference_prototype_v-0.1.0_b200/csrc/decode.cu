@@ -83,20 +83,6 @@ __global__ void k_embed(const uint8_t* __restrict__ W, int type, size_t row_byte
 }
 
 // ---- RMSNorm (qwen3moe.cpp:527-532): out = x * (1 / sqrtf(mean(x^2) + eps)) * w, one block per row
-template <int NT>
-__device__ float block_sum(float v, float* red) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) red[w] = v;
-    __syncthreads();
-    v = lane < NT / 32 ? red[lane] : 0.f;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 // (128 threads: the sum of squares in row_sumsq128's order, shared with the router launch's fused norm)
 __global__ void __launch_bounds__(128) k_rmsnorm(const float* __restrict__ x, int ldx, const float* __restrict__ w,
                                                  float* __restrict__ out, int ldo, int n, float eps) {
@@ -121,44 +107,10 @@ __global__ void __launch_bounds__(NP_NT) k_norm_prep(NormPrepArgs a) {
     __shared__ float s_w[32];
     pdl_trigger();
     pdl_wait();
-    const int t = a.t0 + blockIdx.x, n = a.n, tid = threadIdx.x;
+    const int t = a.t0 + blockIdx.x, n = a.n;
     float* xr = a.x + (size_t)t * a.ldx;
-    if (a.y) {
-        if (tid < a.K) {
-            const int sl = a.token_slots[t * a.K + tid];
-            s_sl[tid] = sl;
-            s_w[tid] = a.slot_w[sl];
-        }
-        __syncthreads();
-        for (int i = 2 * tid; i < n; i += 2 * NP_NT) {
-            float2 acc = make_float2(0.f, 0.f);
-#pragma unroll 8
-            for (int k = 0; k < a.K; k++) {
-                const float2 v = *reinterpret_cast<const float2*>(a.y + (size_t)s_sl[k] * n + i);
-                acc.x = fmaf(s_w[k], v.x, acc.x);
-                acc.y = fmaf(s_w[k], v.y, acc.y);
-            }
-            float2 xv = *reinterpret_cast<const float2*>(xr + i);
-            xv.x += acc.x;
-            xv.y += acc.y;
-            *reinterpret_cast<float2*>(xr + i) = xv;
-            row[i] = xv.x;
-            row[i + 1] = xv.y;
-        }
-    } else {
-        for (int i = tid; i < n; i += NP_NT) row[i] = xr[i];
-    }
-    __syncthreads();
-    float ss = 0.f;
-    for (int i = tid; i < n; i += NP_NT) ss = fmaf(row[i], row[i], ss);
-    ss = block_sum<NP_NT>(ss, red);
-    const float sc = 1.0f / sqrtf(ss / (float)n + a.eps);
-    for (int i = tid; i < n; i += NP_NT) {
-        const float v = __fmul_rn(__fmul_rn(row[i], sc), a.w[i]);
-        row[i] = v;
-        if (a.xn) a.xn[(size_t)blockIdx.x * n + i] = v;
-    }
-    __syncthreads();
+    combine_norm_row(xr, a.y, a.y ? a.token_slots + (size_t)t * a.K : nullptr, a.slot_w, a.K, a.w, a.eps, n, row,
+                     xr, a.xn ? a.xn + (size_t)blockIdx.x * n : nullptr, s_sl, s_w, red);
     const int r = blockIdx.x;  // XF row
     prep_row(row, n, const_cast<uint2*>(a.xf.frag) + (size_t)r * (n >> 5) * 12,
              const_cast<float*>(a.xf.sum) + (size_t)r * ((n >> 4) + XF_SUM_PAD),
@@ -245,6 +197,60 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// One warp merges the nsplit partial records [m, l, o[HD]] of one (token, q head) (p: the first record):
+// lane y holds split y's m and l (nsplit <= 128); v[j] = element lane + 32 j of sum_y e_y o_y / sum_y e_y l_y,
+// e_y = expf(m_y - max m) (splits without positions weigh 0), the o sum in split order. The records are
+// read eight splits at a time (independent loads in flight); CG: through L2 only (records written by
+// other blocks of the same grid).
+template <int HD, bool CG>
+__device__ __forceinline__ void merge_head(const float* __restrict__ p, int nsplit, float (&v)[HD / 32]) {
+    constexpr int PER = HD / 32;
+    const int lane = threadIdx.x & 31;
+    auto ld = [](const float* a) { return CG ? __ldcg(a) : *a; };
+    float mq[4], lq[4], M = -INFINITY;
+#pragma unroll
+    for (int q4 = 0; q4 < 4; q4++) {
+        const int yy = lane + 32 * q4;
+        mq[q4] = yy < nsplit ? ld(p + (size_t)yy * (HD + 2)) : -INFINITY;
+        lq[q4] = yy < nsplit ? ld(p + (size_t)yy * (HD + 2) + 1) : 0.f;
+        M = fmaxf(M, mq[q4]);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float eq[4], L = 0.f;
+#pragma unroll
+    for (int q4 = 0; q4 < 4; q4++) {
+        eq[q4] = mq[q4] == -INFINITY ? 0.f : expf(mq[q4] - M);  // splits without positions weigh 0
+        L = fmaf(lq[q4], eq[q4], L);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    float o[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) o[j] = 0.f;
+    for (int y0 = 0; y0 < nsplit; y0 += 8) {
+        const int q4 = y0 >> 5;  // the eight splits share one lane group of eq
+        const float eg = q4 == 0 ? eq[0] : q4 == 1 ? eq[1] : q4 == 2 ? eq[2] : eq[3];
+        float r[8][PER];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+#pragma unroll
+            for (int j = 0; j < PER; j++)
+                r[u][j] = y0 + u < nsplit ? ld(p + (size_t)(y0 + u) * (HD + 2) + 2 + lane + 32 * j) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const float e = __shfl_sync(0xffffffffu, eg, (y0 + u) & 31);
+            if (y0 + u < nsplit && e != 0.f) {  // warp-uniform
+#pragma unroll
+                for (int j = 0; j < PER; j++) o[j] = fmaf(r[u][j], e, o[j]);
+            }
+        }
+    }
+    const float inv = 1.0f / L;
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = o[j] * inv;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ q, float* __restrict__ kc,
@@ -410,6 +416,22 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
 #pragma unroll
         for (int j = 0; j < PER; j++) pr[2 + lane + 32 * j] = o_run[k][j];
     }
+    if (rf.cnt) {  // single-token step: the last split block of (t, kv head h) merges the group's q heads
+        __shared__ bool s_last;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(&rf.cnt[t * n_kv + h], 1) == (int)gridDim.y - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        for (int hq = warp; hq < grp; hq += nwarp) {
+            float v[PER];
+            merge_head<HD, true>(part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2), nsplit, v);
+#pragma unroll
+            for (int j = 0; j < PER; j++) rf.att[(size_t)t * QD + (size_t)(h * grp + hq) * HD + lane + 32 * j] = v[j];
+        }
+        if (threadIdx.x == 0) rf.cnt[t * n_kv + h] = 0;  // counted again by the next launch
+    }
 }
 
 // ---- split merge of every head of a token row: out = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M),
@@ -426,46 +448,12 @@ __global__ void __launch_bounds__(MP_NT) k_attn_merge_prep(const float* __restri
     pdl_wait();
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, QD = n_head * HD;
     for (int hq = warp; hq < n_head; hq += MP_NT / 32) {
-        const float* p = part + ((size_t)t * n_head + hq) * nsplit * (HD + 2);
-        float mq[4], lq[4], M = -INFINITY;  // lane y holds split y (nsplit <= 128)
-#pragma unroll
-        for (int q4 = 0; q4 < 4; q4++) {
-            const int yy = lane + 32 * q4;
-            mq[q4] = yy < nsplit ? p[(size_t)yy * (HD + 2)] : -INFINITY;
-            lq[q4] = yy < nsplit ? p[(size_t)yy * (HD + 2) + 1] : 0.f;
-            M = fmaxf(M, mq[q4]);
-        }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float eq[4], L = 0.f;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; q4++) {
-            eq[q4] = mq[q4] == -INFINITY ? 0.f : expf(mq[q4] - M);  // splits without positions weigh 0
-            L = fmaf(lq[q4], eq[q4], L);
-        }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-        float o[PER];
-#pragma unroll
-        for (int j = 0; j < PER; j++) o[j] = 0.f;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; q4++) {
-            if (32 * q4 >= nsplit) break;
-#pragma unroll 4
-            for (int y32 = 0; y32 < 32 && 32 * q4 + y32 < nsplit; y32++) {
-                const float e = __shfl_sync(0xffffffffu, eq[q4], y32);
-                if (e == 0.f) continue;  // warp-uniform
-                const float* r = p + (size_t)(32 * q4 + y32) * (HD + 2) + 2;
-#pragma unroll
-                for (int j = 0; j < PER; j++) o[j] = fmaf(r[lane + 32 * j], e, o[j]);
-            }
-        }
-        const float inv = 1.0f / L;
+        float v[PER];
+        merge_head<HD, false>(part + ((size_t)t * n_head + hq) * nsplit * (HD + 2), nsplit, v);
 #pragma unroll
         for (int j = 0; j < PER; j++) {
-            const float v = o[j] * inv;
-            mrow[hq * HD + lane + 32 * j] = v;
-            att[(size_t)t * QD + hq * HD + lane + 32 * j] = v;
+            mrow[hq * HD + lane + 32 * j] = v[j];
+            att[(size_t)t * QD + hq * HD + lane + 32 * j] = v[j];
         }
     }
     __syncthreads();
@@ -610,7 +598,7 @@ static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int
     }
     cudaError_t e = launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv,
                                scale, st, nsplit, part, rf);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || rf.cnt) return e;  // merged by the attention launch itself
     const size_t msmem = (size_t)n_head * HD * 4;
     static size_t mcur = 0;
     if (msmem > 48 * 1024 && msmem > mcur) {
@@ -624,7 +612,7 @@ cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n
                              const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
                              const RopeFuse& rf, cudaStream_t s) {
     if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1 || nsplit > 128 ||
-        (rf.qkv && nb != 1) || (n_head * hd) % 256)
+        (rf.qkv && nb != 1) || (rf.cnt && (nb != 1 || !rf.att)) || (n_head * hd) % 256)
         return cudaErrorInvalidValue;
     if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, s);
     if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, s);

@@ -61,10 +61,16 @@ struct RopeFuse {
     const float* kn;
     float eps;
     const float2* cs;  // the token's HD/2 cos/sin pairs
+    // merge fused into the attention launch (single-token steps): the last split block of each kv head
+    // merges its q heads into att; cnt: n_kv zeroed counters (reset by that block). Null: k_attn_merge_prep
+    // merges and puts the rows in fragment form.
+    int* cnt;
+    float* att;
 };
 // Attention of nb token rows (split partials in part: nb * n_head * nsplit * (hd + 2) floats, nsplit
 // <= 128), then the merge of each row into att (fp32, [nb x n_head hd]) and into xf (fragment form, the
-// o-projection's activations).
+// o-projection's activations); with rf.cnt (one row) the attention launch merges into rf.att itself and
+// leaves the fragment form to the o-projection's prologue.
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                              const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
                              const RopeFuse& rf, cudaStream_t s);

@@ -273,6 +273,7 @@ struct EahmmfEngine {
     int* toks = nullptr;       // device token staging [MAXB]
     int* h_toks = nullptr;     // pinned [MAXB]
     int* status = nullptr;     // device status word
+    int* att_cnt = nullptr;    // [n_kv] split counters of the attention launch's fused merge (self-resetting)
     DecodeState* state = nullptr;
     DecodeState* h_state = nullptr;  // pinned mirror for reads
     int* out = nullptr;
@@ -475,11 +476,11 @@ struct EahmmfEngine {
             !dalloc(attn_part, (size_t)MAXB * n_head * std::min(nsplit_max, 128) * (hd + 2) * 4) ||
             !dalloc(amax_blk, (size_t)amax_nblk * 8) || !dalloc(moe_ws, moe_ws_bytes) ||
             !dalloc(gemv_ws, gemv_ws_bytes) || !dalloc(toks, MAXB * 4) || !dalloc(status, 4) ||
-            !dalloc(xf_rows, xf_bytes(MAXB, D)) || !dalloc(xf_att, xf_bytes(MAXB, QD)) ||
+            !dalloc(xf_rows, xf_bytes(MAXB, D)) || !dalloc(xf_att, xf_bytes(MAXB, QD)) || !dalloc(att_cnt, n_kv * 4) ||
             !dalloc(state, sizeof(DecodeState)))
             return fail("cannot allocate activations / KV cache");
         if (cudaMemset(kc, 0, kvn * 4) != cudaSuccess || cudaMemset(vc, 0, kvn * 4) != cudaSuccess ||
-            cudaMemset(status, 0, 4) != cudaSuccess)
+            cudaMemset(status, 0, 4) != cudaSuccess || cudaMemset(att_cnt, 0, n_kv * 4) != cudaSuccess)
             return fail("memset");
         if (cudaHostAlloc((void**)&h_toks, MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
             cudaHostAlloc((void**)&h_state, sizeof(DecodeState), cudaHostAllocDefault) != cudaSuccess)
@@ -567,6 +568,83 @@ struct EahmmfEngine {
         return true;
     }
 
+    // The single-token layer with the norm and merge kernels fused away: the q|k|v GEMV forms its
+    // activations itself (pending MoE combine + attention RMSNorm), the attention launch merges its
+    // splits, the o-projection forms its activations from the merged row and adds the pending combine
+    // to the residual rows it owns; then the router launch (FFN RMSNorm) and the MoE block, whose combine
+    // is left pending for the next layer. Same arithmetic as the multi-token path.
+    bool fused_step_ok(const Layer& L) const {
+        return L.fused && gemv_mma_ok(QMat{L.wq[0], L.qkv_type[0], D, QD + 2 * KD, L.qkv_rb[0]}) &&
+               gemv_mma_ok(QMat{L.wo, L.wo_type, QD, D, L.wo_rb}) && n_used <= 32 && L.moe.d_router;
+    }
+    int layer_step1(const Layer& L, float* lk, float* lv, float scale, int nsplit, MoeDeferred& pending) {
+        const int ldq = QD + 2 * KD;
+        if (!mark(1)) return ST_CUDA;
+        GemvXArgs g{};
+        g.W = QMat{L.wq[0], L.qkv_type[0], D, ldq, L.qkv_rb[0]};
+        g.m = 1;
+        g.Y = qkv;
+        g.ldy = ldq;
+        g.status = status;
+        g.pro = GEMV_PRO_NORM;
+        g.prow = x;
+        g.py = pending.y;
+        g.pslots = pending.token_slots;
+        g.pw = pending.slot_w;
+        g.pK = pending.y ? pending.K : 0;
+        g.pnw = L.attn_norm;
+        g.peps = eps;
+        if (launch_gemv_xf(g, st) != cudaSuccess || !mark(2)) return ST_CUDA;
+        RopeFuse rf{};
+        rf.qkv = qkv;
+        rf.qn = L.q_norm;
+        rf.kn = L.k_norm;
+        rf.eps = eps;
+        rf.cs = rope_cs;
+        rf.cnt = att_cnt;
+        rf.att = att;
+        if (!mark(3) ||
+            launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, 1, nsplit, attn_part, att, XF{}, rf, st) !=
+                cudaSuccess ||
+            !mark(4))
+            return ST_CUDA;
+        GemvXArgs o{};
+        o.W = QMat{L.wo, L.wo_type, QD, D, L.wo_rb};
+        o.m = 1;
+        o.Y = x;
+        o.ldy = D;
+        o.accumulate = 1;
+        o.status = status;
+        o.pro = GEMV_PRO_ROW;
+        o.prow = att;
+        o.ey = pending.y;
+        o.eslots = pending.token_slots;
+        o.ew = pending.slot_w;
+        o.eK = pending.y ? pending.K : 0;
+        if (launch_gemv_xf(o, st) != cudaSuccess || !mark(5)) return ST_CUDA;
+        pending = MoeDeferred{};
+        if (!mark(6)) return ST_CUDA;
+        const int rc = moe_layer_run(&L.moe, 1, x, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, L.ffn_norm, eps);
+        if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
+        return trace_layer(1);
+    }
+    // routing of the layer just run (ids, then weights, at the head of the MoE workspace) into the trace
+    int trace_layer(int nb) {
+        if (!trace) return ST_OK;
+        const size_t nk = (size_t)nb * n_used;
+        h_ids.resize(nk);
+        h_w.resize(nk);
+        const size_t woff = (nk * 4 + 255) & ~(size_t)255;
+        if (cudaMemcpyAsync(h_ids.data(), moe_ws, nk * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(h_w.data(), static_cast<uint8_t*>(moe_ws) + woff, nk * 4, cudaMemcpyDeviceToHost, st) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return ST_CUDA;
+        trace_ids.insert(trace_ids.end(), h_ids.begin(), h_ids.end());
+        trace_w.insert(trace_w.end(), h_w.begin(), h_w.end());
+        return ST_OK;
+    }
+
     // One forward pass of nb tokens at the device position state->pos (which it does not change).
     // tok: device pointer to nb token ids. want_logits: logits of the last token into `logits`.
     int forward(const int* tok, int nb, bool want_logits) {
@@ -620,6 +698,11 @@ struct EahmmfEngine {
             const Layer& L = layers[l];
             float* lk = kc + (size_t)l * n_ctx * KD;
             float* lv = vc + (size_t)l * n_ctx * KD;
+            if (nb == 1 && fused_step_ok(L)) {  // single-token step: 6 launches per layer
+                const int rc = layer_step1(L, lk, lv, scale, nsplit, pending);
+                if (rc != ST_OK) return rc;
+                continue;
+            }
             NormPrepArgs na{};
             na.x = x;
             na.ldx = D;
@@ -706,19 +789,7 @@ struct EahmmfEngine {
                 rc = moe_layer_run(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, nullptr, 0.f);
             }
             if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
-            if (trace) {  // routing of this layer (ids, then weights, at the head of the MoE workspace)
-                const size_t nk = (size_t)nb * n_used;
-                h_ids.resize(nk);
-                h_w.resize(nk);
-                const size_t woff = (nk * 4 + 255) & ~(size_t)255;
-                if (cudaMemcpyAsync(h_ids.data(), moe_ws, nk * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-                    cudaMemcpyAsync(h_w.data(), static_cast<uint8_t*>(moe_ws) + woff, nk * 4, cudaMemcpyDeviceToHost,
-                                    st) != cudaSuccess ||
-                    cudaStreamSynchronize(st) != cudaSuccess)
-                    return ST_CUDA;
-                trace_ids.insert(trace_ids.end(), h_ids.begin(), h_ids.end());
-                trace_w.insert(trace_w.end(), h_w.begin(), h_w.end());
-            }
+            if (trace_layer(nb) != ST_OK) return ST_CUDA;
         }
         if (want_logits) {  // last row: the pending combine, the output norm, the output GEMV
             NormPrepArgs na{};

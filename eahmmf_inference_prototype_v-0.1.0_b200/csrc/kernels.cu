@@ -266,6 +266,9 @@ __host__ __device__ inline GPlan gemv_plan(int qt, int K, size_t rb, int nset, i
     (void)qt;
     return unit_plan(K, m, 2 * (K / 256), nset, slot_bytes(row_layout(rb, true), 16));
 }
+// shared memory of k_gemv's prologue (after the plan's total): the fp32 row [K], the norm weights [K], the
+// XF gs row, the reduction scratch (33 floats) and the pending combine's slots and weights (32 each)
+__host__ __device__ inline size_t gemv_pro_bytes(int K) { return (size_t)K * 8 + al128(xf_gs_bytes(K)) + 128 * 3 + 256; }
 
 template <int QT, int NSET>
 __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
@@ -285,11 +288,40 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
     if (tid == 0) {  // the weight rows do not depend on earlier grids: their copy starts before the wait
         mbar_init(&bar[0], 1);
         mbar_fence_init();
-        mbar_expect_tx(&bar[0], rows_bytes(L, a.W.w, rb, r0, r1) + xf_bytes_of(m, K));
+        mbar_expect_tx(&bar[0], rows_bytes(L, a.W.w, rb, r0, r1) + (a.pro ? 0u : xf_bytes_of(m, K)));
         issue_rows(L, a.W.w, rb, r0, r1, slot, &bar[0]);
     }
-    pdl_wait();  // the activations (XF) and, when accumulating, Y come from earlier grids
-    if (tid == 0) issue_xf(a.xf, [](int i) { return i; }, m, K, sfrag, ssum, &bar[0]);
+    // prologue scratch after the plan: the fp32 row, the norm weights, the XF gs row, reductions, slots
+    float* prow_s = reinterpret_cast<float*>(sm + pl.total);
+    float* nw_s = prow_s + K;
+    uint8_t* gs_s = reinterpret_cast<uint8_t*>(nw_s + K);
+    float* red = reinterpret_cast<float*>(gs_s + al128(xf_gs_bytes(K)));
+    int* sl_s = reinterpret_cast<int*>(red + 64);
+    float* sw_s = reinterpret_cast<float*>(sl_s + 32);
+    if (a.pro == GEMV_PRO_NORM)  // the norm weights do not depend on earlier grids
+        for (int i = tid; i < K / 4; i += NTU)
+            reinterpret_cast<float4*>(nw_s)[i] = __ldg(reinterpret_cast<const float4*>(a.pnw) + i);
+    pdl_wait();  // the activations (XF or their fp32 row) and, when accumulating, Y come from earlier grids
+    if (a.pro == GEMV_PRO_XF) {
+        if (tid == 0) issue_xf(a.xf, [](int i) { return i; }, m, K, sfrag, ssum, &bar[0]);
+    } else {  // the token's row in fragment form, formed here exactly as the norm / merge kernels form it
+        if (a.pro == GEMV_PRO_NORM) {
+            __syncthreads();  // nw_s
+            combine_norm_row(a.prow, a.py, a.pslots, a.pw, a.pK, nw_s, a.peps, K, prow_s, nullptr, nullptr, sl_s, sw_s,
+                             red);
+        } else {  // the row into shared memory first, every thread's loads in flight together
+#pragma unroll 4
+            for (int i = tid; i < K / 4; i += NTU)
+                reinterpret_cast<float4*>(prow_s)[i] = __ldcg(reinterpret_cast<const float4*>(a.prow) + i);
+            __syncthreads();
+        }
+        prep_row(prow_s, K, reinterpret_cast<uint2*>(sfrag), ssum, gs_s, red);
+    }
+    if (a.ey && tid < a.eK) {  // the epilogue's pending combine
+        const int sl = a.eslots[tid];
+        sl_s[tid] = sl;
+        sw_s[tid] = a.ew[sl];
+    }
     __syncthreads();
     if (__syncthreads_or(!mbar_wait_bounded(&bar[0], 0u))) {
         if (tid == 0) {
@@ -305,7 +337,17 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
         const int r = j / m, tk = j - r * m;
         const float v = tile_value<NSET>(part, mpart, 0, r, nsb, tk, ssum[(size_t)tk * (16 * nsb + XF_SUM_PAD) + 16 * nsb]);
         float* y = a.Y + (size_t)tk * a.ldy + r0 + r;
-        *y = a.accumulate ? *y + v : v;
+        if (a.accumulate) {
+            float base = *y;
+            if (a.ey) {  // x + sum_k w_k y_k in the norm kernel's order (combine_norm_row), then + v
+                float acc = 0.f;
+                for (int k = 0; k < a.eK; k++) acc = fmaf(sw_s[k], a.ey[(size_t)sl_s[k] * a.W.rows + r0 + r], acc);
+                base += acc;
+            }
+            *y = base + v;
+        } else {
+            *y = v;
+        }
     }
 }
 
@@ -452,12 +494,17 @@ static void smem_attr(Kern k, size_t smem) {
 template <int QT, int NSET>
 static void gemv_go(const GemvXArgs& a, cudaStream_t st) {
     const GPlan pl = gemv_plan(QT, a.W.K, a.W.row_bytes, NSET, a.m);
-    smem_attr(k_gemv<QT, NSET>, pl.total);
-    launch_pdl(k_gemv<QT, NSET>, dim3((a.W.rows + 15) / 16), dim3(NTU), pl.total, st, a);
+    const size_t smem = pl.total + (a.pro ? gemv_pro_bytes(a.W.K) : 0);
+    smem_attr(k_gemv<QT, NSET>, smem);
+    launch_pdl(k_gemv<QT, NSET>, dim3((a.W.rows + 15) / 16), dim3(NTU), smem, st, a);
 }
 
 cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st) {
     if (a.m < 1 || a.m > TPASS || !gemv_mma_ok(a.W)) return cudaErrorInvalidValue;
+    if ((a.pro && (a.m != 1 || !a.prow || (a.pro == GEMV_PRO_NORM && (!a.pnw || a.pK > 32)) ||
+                   gemv_plan(a.W.type, a.W.K, a.W.row_bytes, 1, 1).total + gemv_pro_bytes(a.W.K) > SMEM_CAP)) ||
+        (a.ey && (a.m != 1 || !a.accumulate || a.eK > 32)))
+        return cudaErrorInvalidValue;
     const bool two = a.m > TOK_PER_SET;
     switch (a.W.type) {
         case T_Q4_K: two ? gemv_go<T_Q4_K, 2>(a, st) : gemv_go<T_Q4_K, 1>(a, st); break;

@@ -93,7 +93,26 @@ struct GemvXArgs {
     int ldy;
     int accumulate;
     int* status;
+    // Prologue (one token, m == 1): instead of copying the token's XF row from xf, every block forms it in
+    // shared memory from a fp32 row: pro = GEMV_PRO_ROW: prow itself; pro = GEMV_PRO_NORM: the RMSNorm
+    // (weight pnw, epsilon peps) of the residual row prow plus its pending MoE combine (py, pslots: pK
+    // slots of the token in ascending expert order, pw: the slots' weights; py null: none).
+    int pro;
+    const float* prow;
+    const float* py;
+    const int* pslots;
+    const float* pw;
+    int pK;
+    const float* pnw;
+    float peps;
+    // Epilogue (accumulate, m == 1): each output row first takes the token's pending MoE combine, as the
+    // norm kernel would have added it: Y = (Y + sum_k w_k ey[slot_k]) + value (ey rows of W.rows floats).
+    const float* ey;
+    const int* eslots;
+    const float* ew;
+    int eK;
 };
+constexpr int GEMV_PRO_XF = 0, GEMV_PRO_ROW = 1, GEMV_PRO_NORM = 2;
 
 // Grouped tensor-core path of the MoE block (gemm.cu) for ragged batches.
 struct GroupedArgs {

@@ -173,6 +173,75 @@ __device__ __forceinline__ void prep_row(const float* __restrict__ x, int K, uin
     }
 }
 
+// The RMSNorm input of one token: its residual row x (n floats, global) plus its pending MoE combine
+// sum_k w_k y[slot_k] (K slots in ascending expert order; K = 0: none), into row[] (shared memory),
+// then normalised in place: row = (row * (1 / sqrtf(mean(row^2) + eps))) * w. Every element is formed
+// the same way whatever the block size (blockDim.x >= 128, a multiple of 32; all threads call it), the
+// sum of squares in row_sumsq128's order. Each thread handles CN_PAIRS element pairs per pass, their
+// loads issued together. xw: the combined residual written back (one block per row only), xn: the
+// normalised row stored, when not null. w may be in shared memory. sl, sw: K words of shared scratch;
+// red: 33 floats.
+constexpr int CN_PAIRS = 4;
+__device__ __forceinline__ void combine_norm_row(const float* __restrict__ x, const float* __restrict__ y,
+                                                 const int* __restrict__ slots, const float* __restrict__ slot_w,
+                                                 int K, const float* w, float eps, int n, float* row, float* xw,
+                                                 float* xn, int* sl, float* sw, float* red) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if (y) {
+        if (tid < K) {
+            const int s = slots[tid];
+            sl[tid] = s;
+            sw[tid] = slot_w[s];
+        }
+        __syncthreads();
+        for (int i0 = 2 * tid; i0 < n; i0 += 2 * nt * CN_PAIRS) {  // pairs i0 + 2 nt p
+            float2 acc[CN_PAIRS], xv[CN_PAIRS];
+#pragma unroll
+            for (int p = 0; p < CN_PAIRS; p++) {
+                const int i = i0 + 2 * nt * p;
+                acc[p] = make_float2(0.f, 0.f);
+                xv[p] = i < n ? *reinterpret_cast<const float2*>(x + i) : make_float2(0.f, 0.f);
+            }
+#pragma unroll 4
+            for (int k = 0; k < K; k++) {
+                const float* yk = y + (size_t)sl[k] * n;
+                float2 v[CN_PAIRS];
+#pragma unroll
+                for (int p = 0; p < CN_PAIRS; p++) {
+                    const int i = i0 + 2 * nt * p;
+                    v[p] = i < n ? *reinterpret_cast<const float2*>(yk + i) : make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int p = 0; p < CN_PAIRS; p++) {
+                    acc[p].x = fmaf(sw[k], v[p].x, acc[p].x);
+                    acc[p].y = fmaf(sw[k], v[p].y, acc[p].y);
+                }
+            }
+#pragma unroll
+            for (int p = 0; p < CN_PAIRS; p++) {
+                const int i = i0 + 2 * nt * p;
+                if (i < n) {
+                    xv[p].x += acc[p].x;
+                    xv[p].y += acc[p].y;
+                    if (xw) *reinterpret_cast<float2*>(xw + i) = xv[p];
+                    row[i] = xv[p].x;
+                    row[i + 1] = xv[p].y;
+                }
+            }
+        }
+    } else {
+        for (int i = tid; i < n; i += nt) row[i] = x[i];
+    }
+    __syncthreads();
+    const float sc = 1.0f / sqrtf(row_sumsq128(row, n, red) / (float)n + eps);
+    for (int i = tid; i < n; i += nt) {
+        const float v = __fmul_rn(__fmul_rn(row[i], sc), w[i]);
+        row[i] = v;
+        if (xn) xn[i] = v;
+    }
+    __syncthreads();
+}
+
 // Per-lane B-fragment pointers of up to NSET column sets over staged XF rows (m tokens, nblk blocks
 // per row). Set st carries tokens 2st, 2st+1; column g holds digit g % 3 of token 2st + g / 3.
 // Columns 6, 7 and tokens >= m read token 0: MMA columns are independent, and the results of those
