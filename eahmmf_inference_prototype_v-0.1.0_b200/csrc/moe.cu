@@ -922,6 +922,202 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
 }
 
 // ------------------------------------------------------------------------------------------------
+// gate + up + SiLU*mul for small batches (T <= FUSED_ROUTE_TMAX, the decode steps): every CTA routes the
+// tokens itself and stages all T tokens' XF rows once (two bulk copies); the 16 consumer warps form
+// FS_GROUPS independent pipelines of 4 warps, group q taking the CTA's units q, q + 4, ... from ring
+// stage q, so up to four units are computed at once. Within a group, warp k takes matrix k / 2 and the
+// super-block subsets ("virtual warps") 4 (k % 2) .. 4 (k % 2) + 3, each subset accumulated and
+// recombined exactly as one consumer warp of k_moe_gateup does it, and the group's first warp sums the
+// eight subsets per matrix in the same order: per-slot results are bitwise those of k_moe_gateup.
+// ------------------------------------------------------------------------------------------------
+constexpr int FS_GROUPS = 4;
+struct FsPlan {
+    size_t info_off, xf_off, xf_gs_off, part_off, stage_off, stage_bytes, extra_off, total;
+};
+__host__ __device__ inline FsPlan gateup_fs_plan(int T, int D, size_t rbg, size_t rbu, size_t route_bytes) {
+    FsPlan p;
+    p.info_off = 128;
+    p.xf_off = 256;
+    p.xf_gs_off = p.xf_off + (size_t)T * D * 3;
+    p.part_off = al128(p.xf_gs_off + (size_t)T * xf_gs_bytes(D));
+    p.stage_bytes = al128(gu_slot(rbg) + gu_slot(rbu));
+    p.stage_off = al128(p.part_off + (size_t)FS_GROUPS * 16 * 16 * MU * 4);
+    p.extra_off = al128(p.stage_off + (size_t)FS_GROUPS * p.stage_bytes);
+    p.total = p.extra_off + route_bytes;
+    return p;
+}
+
+template <int QG, int QU>
+__global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup_fs(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int D = a.D, FF = a.FF, nsb = D >> 8, NRB = FF >> 4, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = a.T, TK = T * a.n_used;
+    const FsPlan pl = gateup_fs_plan(T, D, a.gate_rb, a.up_rb, route_sm_bytes(a.n_expert, TK, true));
+    constexpr int S = FS_GROUPS;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* empty = full + 4;
+    uint64_t* done = full + 8;  // per stage: the group's four warps have stored their partial results
+    uint64_t* xfbar = full + 12;
+    int4* info = reinterpret_cast<int4*>(sm + pl.info_off);
+    __shared__ int abort_flag;
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 4);
+            mbar_init(&done[s], 4);
+        }
+        mbar_init(xfbar, 1);
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    RouteSm rt = route_sm_carve(sm + pl.extra_off, a.n_expert, TK, true);
+    {  // the experts' matrix table does not depend on earlier grids
+        const int E = a.n_expert;
+        for (int i = tid; i < 3 * E; i += blockDim.x) rt.tab[i] = i < E ? a.gate[i] : i < 2 * E ? a.up[i - E] : a.down[i - 2 * E];
+    }
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();  // the logits and the tokens' XF come from the previous grid
+    const uint32_t xfg = (uint32_t)xf_gs_bytes(D);
+    if (tid == 0) {  // all T tokens' XF rows: fragments and group sums, one bulk copy each
+        mbar_expect_tx(xfbar, (uint32_t)T * ((uint32_t)D * 3 + xfg));
+        tma_load_1d(sm + pl.xf_off, a.xf.frag, (uint32_t)T * D * 3, xfbar);
+        tma_load_1d(sm + pl.xf_gs_off, a.xf.gs, (uint32_t)T * xfg, xfbar);
+    }
+    route_block<true>(a, rt, blockIdx.x == 0);
+    __syncthreads();
+    if (warp == 0) down_l2_prefetch(a, rt);
+    const int G = *rt.G;
+    const int nunits = G * NRB;
+    const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
+    const size_t rbg = a.gate_rb, rbu = a.up_rb, up_at = gu_slot(rbg);
+    const Rows Lg = rows_of(rbg), Lu = rows_of(rbu);
+
+    if (warp == NWC_GU) {  // ---------------- producer: weight tiles only
+        if (lane != 0) return;
+        int i = 0;
+        for (int u = u0; u < u1; u++, i++) {
+            const int s = i % S;
+            if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)(i / S - 1) & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                break;
+            }
+            if (*(volatile int*)&abort_flag) break;
+            const int gi = u / NRB, rb = u - gi * NRB, r0 = 16 * rb;
+            const uint8_t* wg = rt.g_w[3 * gi];
+            const uint8_t* wu = rt.g_w[3 * gi + 1];
+            const int mc = rt.g_info[4 * gi + 2];
+            const bool ok = al16(wg) && al16(wu);
+            if (!ok) set_flag(a.status, ST_BAD_ARG);
+            uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
+            const uint32_t lg = (!split8(rbg) && ok) ? rows_lead(Lg, wg, rbg, r0) : 0u;
+            const uint32_t lu = (!split8(rbu) && ok) ? rows_lead(Lu, wu, rbu, r0) : 0u;
+            info[s] = make_int4(rb | (gi << 12), info_bits(0, mc, ok, false), rt.g_info[4 * gi + 1], (int)(lg | (lu << 8)));
+            uint32_t bytes = 0;
+            if (ok) {
+                bytes += split8(rbg) ? (uint32_t)(16 * rbg) : rows_copy_bytes(Lg, wg, rbg, r0, 16);
+                bytes += split8(rbu) ? (uint32_t)(16 * rbu) : rows_copy_bytes(Lu, wu, rbu, r0, 16);
+            }
+            mbar_expect_tx(&full[s], bytes);
+            if (ok) {
+                if (split8(rbg)) {
+                    tma_load_1d(stage, wg + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
+                    tma_load_1d(stage + split8_off(rbg), wg + (size_t)(r0 + 8) * rbg, (uint32_t)(8 * rbg), &full[s]);
+                } else {
+                    rows_issue(Lg, wg, rbg, r0, 16, stage, &full[s]);
+                }
+                if (split8(rbu)) {
+                    tma_load_1d(stage + up_at, wu + (size_t)r0 * rbu, (uint32_t)(8 * rbu), &full[s]);
+                    tma_load_1d(stage + up_at + split8_off(rbu), wu + (size_t)(r0 + 8) * rbu, (uint32_t)(8 * rbu),
+                                &full[s]);
+                } else {
+                    rows_issue(Lu, wu, rbu, r0, 16, stage + up_at, &full[s]);
+                }
+            }
+        }
+        const int issued = i;
+        for (int k = (issued > S ? issued - S : 0); k < issued; k++) {
+            if (!mbar_wait_bounded(&empty[k % S], (uint32_t)(k / S) & 1u)) {
+                drain(full, issued, k, S);
+                break;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers: group q = warp / 4 runs units q, q + 4, ... on stage q
+    const int q = warp >> 2, k4 = warp & 3, mtx = k4 >> 1, vw0 = 4 * (k4 & 1), g = lane >> 2, t = lane & 3;
+    const size_t rbm = mtx ? rbu : rbg;
+    const int prow0 = gu_row(rbm, g, 0), prow1 = gu_row(rbm, g, 1);
+    if (!mbar_wait_bounded(xfbar, 0u)) {  // the tokens' XF rows
+        set_flag(a.status, ST_WAIT_TIMEOUT);
+        atomicExch(&abort_flag, 1);
+        return;
+    }
+    const uint8_t* xfr = sm + pl.xf_off;
+    const uint8_t* xgs = sm + pl.xf_gs_off;
+    float* part = reinterpret_cast<float*>(sm + pl.part_off) + (size_t)q * 16 * 16 * MU;  // [16 subsets][16 rows][MU]
+    int n = 0;  // uses of this group's stage
+    for (int i = q; u0 + i < u1; i += S, n++) {
+        const int s = q;
+        if (!mbar_wait_bounded(&full[s], (uint32_t)n & 1u)) {
+            set_flag(a.status, ST_WAIT_TIMEOUT);
+            atomicExch(&abort_flag, 1);
+            return;  // the producer drains what it issued
+        }
+        const int4 in = info[s];
+        const int rb = in.x & 0xfff, gi = in.x >> 12, mc = (in.y >> 4) & 15, s0 = in.z;
+        const int tok0 = rt.g_tok[MU * gi], tok1 = mc > 1 ? rt.g_tok[MU * gi + 1] : tok0;
+        // the lane's B operands over the staged rows of the group's tokens (as BPtr<1> / min_operand)
+        BPtr<1> bp(xfr, D >> 5, 1);
+        {
+            int ti = g / 3, pg = g % 3;
+            if (g >= 6 || ti >= mc) ti = pg = 0;
+            bp.p[0] = xfr + ((size_t)(ti ? tok1 : tok0) * (D >> 5) * 3 + pg) * 32;
+        }
+        int mt = g >> 1;
+        if (g >= 4 || mt >= mc) mt = 0;
+        const uint8_t* mq = xgs + (size_t)(mt ? tok1 : tok0) * xfg + 16 + (g & 1) * 16 + 4 * t;
+        const float ts = t < mc ? *reinterpret_cast<const float*>(xgs + (size_t)(t ? tok1 : tok0) * xfg) : 0.f;
+        const uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
+#pragma unroll 1
+        for (int v = 0; v < 4; v++) {
+            const int vw = vw0 + v;
+            float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
+            if (in.y & 256) {
+                if (mtx == 0)
+                    block_tasks<QG>(rows_gu(stage, rbg, in.w & 255), nsb, vw, 8, bp, mq, acc, mn);
+                else
+                    block_tasks<QU>(rows_gu(stage + up_at, rbu, (in.w >> 8) & 255), nsb, vw, 8, bp, mq, acc, mn);
+            }
+            warp_values(acc, mn, ts, part + (size_t)(mtx * 8 + vw) * 16 * MU, prow0, prow1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&done[s]);
+        if (k4 == 0) {  // the group's reducer: SiLU*mul of the summed subsets
+            if (!mbar_wait_bounded(&done[s], (uint32_t)n & 1u)) {
+                set_flag(a.status, ST_WAIT_TIMEOUT);
+                atomicExch(&abort_flag, 1);
+                return;
+            }
+            const int r = lane >> 1, tk = lane & 1;
+            if (tk < mc) {
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    gv += part[(w * 16 + r) * MU + tk];
+                    uv += part[((8 + w) * 16 + r) * MU + tk];
+                }
+                a.h[(size_t)(s0 + tk) * FF + 16 * rb + r] = silu_mul(gv, uv);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // down projection + weighted combine + residual add
 // ------------------------------------------------------------------------------------------------
 template <int QD>
@@ -1278,12 +1474,25 @@ static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
     const int units = max_groups(a) * (a.FF >> 4);
     return launch_pdl(k_moe_gateup<QG, QU>, dim3(std::min(sm_count(), units)), (NWC_GU + 1) * 32, pl.total, st, a);
 }
+template <int QG, int QU>
+static cudaError_t gateup_pick(const MoeArgs& a, cudaStream_t st) {
+    if (a.fused_route && a.FF < (1 << 16)) {  // unit info packs the row block in 12 bits
+        const FsPlan pl = gateup_fs_plan(a.T, a.D, a.gate_rb, a.up_rb, route_sm_bytes(a.n_expert, a.T * a.n_used, true));
+        if (pl.total <= SMEM_CAP) {
+            smem_attr(k_moe_gateup_fs<QG, QU>, pl.total);
+            const int units = max_groups(a) * (a.FF >> 4);
+            return launch_pdl(k_moe_gateup_fs<QG, QU>, dim3(std::min(sm_count(), units)), (NWC_GU + 1) * 32, pl.total, st,
+                              a);
+        }
+    }
+    return gateup_as<QG, QU>(a, st);
+}
 template <int QG>
 static cudaError_t gateup_g(const MoeArgs& a, cudaStream_t st) {
     switch (a.up_type) {
-        case T_Q4_K: return gateup_as<QG, T_Q4_K>(a, st);
-        case T_Q5_K: return gateup_as<QG, T_Q5_K>(a, st);
-        case T_Q6_K: return gateup_as<QG, T_Q6_K>(a, st);
+        case T_Q4_K: return gateup_pick<QG, T_Q4_K>(a, st);
+        case T_Q5_K: return gateup_pick<QG, T_Q5_K>(a, st);
+        case T_Q6_K: return gateup_pick<QG, T_Q6_K>(a, st);
         default: return cudaErrorInvalidValue;
     }
 }
