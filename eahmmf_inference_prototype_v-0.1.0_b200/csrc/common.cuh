@@ -147,11 +147,6 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         : "memory");
 }
 
-// Hint: bring [src, src + bytes) into L2 (src 16-byte aligned, bytes a multiple of 16). No completion.
-__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ float f16_to_f32(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 
 // x / (1 + exp(-x)) * u, the SiLU-gated product of qwen3moe.cpp:1056-1059 (IEEE division).

@@ -702,35 +702,6 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     }
 }
 
-// The down matrices of the experts routed in r (ascending expert order, D * down_rb bytes each) as one
-// byte range, split evenly over the grid: this CTA's share goes to L2 in pieces of at most 32 KB. One
-// warp; a hint only (nothing waits for it). Skipped when a matrix is not a 16-byte multiple.
-__device__ void down_l2_prefetch(const MoeArgs& a, const RouteSm& r) {
-    const int E = a.n_expert, lane = threadIdx.x & 31;
-    const size_t per = (size_t)a.D * a.down_rb;
-    if (per % 16) return;
-    int n_act = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) n_act += __popc(__ballot_sync(0xffffffffu, e0 + lane < E && r.cnt[e0 + lane] > 0));
-    const size_t total = (size_t)n_act * per;
-    const size_t lo = (total * blockIdx.x / gridDim.x) & ~(size_t)15;
-    const size_t hi = blockIdx.x + 1 == gridDim.x ? total : (total * (blockIdx.x + 1) / gridDim.x) & ~(size_t)15;
-    int base = 0;
-    for (int e0 = 0; e0 < E && lo < hi; e0 += 32) {
-        const int e = e0 + lane;
-        const bool act = e < E && r.cnt[e] > 0;
-        const unsigned m = __ballot_sync(0xffffffffu, act);
-        if (act) {
-            const size_t k = (size_t)(base + __popc(m & ((1u << lane) - 1u)));
-            const size_t s0 = k * per > lo ? k * per : lo, s1 = (k + 1) * per < hi ? (k + 1) * per : hi;
-            const uint8_t* w = r.tab[2 * E + e];
-            if ((reinterpret_cast<uintptr_t>(w) & 15) == 0)
-                for (size_t o = s0; o < s1; o += 32768)
-                    l2_prefetch_bulk(w + (o - k * per), (uint32_t)(s1 - o < 32768 ? s1 - o : 32768));
-        }
-        base += __popc(m);
-    }
-}
-
 __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
     pdl_wait();     // logits and activations come from the previous grids
@@ -780,12 +751,10 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
     pdl_trigger();
     pdl_wait();  // routing results (or the logits) and the XF of the tokens come from the previous grids
     // small batches: every CTA routes the tokens itself into shared memory (CTA 0 also publishes the
-    // routing, groups and slot maps for the down kernel and the combine), then asks L2 for its share of
-    // the routed experts' down matrices, which the down kernel streams next
+    // routing, groups and slot maps for the down kernel and the combine)
     if (a.fused_route) {
         route_block<true>(a, rt, blockIdx.x == 0);
         __syncthreads();
-        if (warp == 0) down_l2_prefetch(a, rt);
     }
     const int G = a.fused_route ? *rt.G : a.rw.ngroups[0];
     auto group = [&](int gi) {
@@ -986,7 +955,6 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup_fs(MoeArgs 
     }
     route_block<true>(a, rt, blockIdx.x == 0);
     __syncthreads();
-    if (warp == 0) down_l2_prefetch(a, rt);
     const int G = *rt.G;
     const int nunits = G * NRB;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
