@@ -439,6 +439,7 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
         // up to FUSED_ROUTE_TMAX tokens: the XF prep rides on the router launch (or a prep launch) and the
         // gate/up kernel routes by itself; larger blocks go through k_moe_route
         a.fused_route = tc <= FUSED_ROUTE_TMAX ? 1 : 0;
+        a.gsz = a.fused_route ? MU : GW;  // larger chunks: up to GW of an expert's slots per weight pass
         g_prof.mark(0, st);
         if (d_logits) {
             a.logits = d_logits + (size_t)t0 * E;

@@ -12,6 +12,7 @@ constexpr int MT = 8;               // tokens per pass of the per-row kernel
 constexpr int XPASS = 4;            // tokens per pass of the tensor-core GEMV
 constexpr int MOE_TMAX = 64;        // tokens per MoE block call (the engine's MAXB, qwen3moe.cpp:39)
 constexpr int MU = 2;               // slots per MoE work group (one MMA column set)
+constexpr int GW = 8;               // slots per work group of the many-token MoE path (four column sets)
 constexpr int ROUTE_NT = 512;       // threads of the routing / prep kernel
 constexpr int COMB_NT = 256;        // threads of a combine block
 constexpr int MAX_EXPERTS = 512;
@@ -79,6 +80,7 @@ struct MoeArgs {
     float* y;             // [T*K*D] expert outputs per slot (down projection, before the combine)
     RouteWs rw;
     int* status;
+    int gsz;          // slots per work group: MU (small batches, routed in the gate/up kernel) or GW
     int fused_route;  // T <= FUSED_ROUTE_TMAX: k_moe_gateup routes itself (no k_moe_route launch); the
                       // XF of the tokens must already be in xf
 };

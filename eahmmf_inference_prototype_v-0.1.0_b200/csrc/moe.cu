@@ -76,23 +76,24 @@ __device__ __forceinline__ void rows_issue(const Rows& L, const uint8_t* base, s
     tma_load_1d(dst, reinterpret_cast<const void*>(s & ~(uintptr_t)15), rows_copy_bytes(L, base, rb, r0, n), bar);
 }
 
-// Staging buffer of MU XF rows of K elements: frag rows (K*3 bytes each), then the rows' scale and
-// group sums (XF gs rows, 16 + K/8 bytes each).
-__host__ __device__ constexpr size_t xs_gs_off(int K) { return (size_t)MU * K * 3; }
-__host__ __device__ constexpr size_t xs_bytes(int K) { return al128(xs_gs_off(K) + (size_t)MU * xf_gs_bytes(K)); }
+// Staging buffer of G XF rows of K elements (G: slots per work group): frag rows (K*3 bytes each), then
+// the rows' scale and group sums (XF gs rows, 16 + K/8 bytes each).
+__host__ __device__ constexpr size_t xs_gs_off(int K, int G = MU) { return (size_t)G * K * 3; }
+__host__ __device__ constexpr size_t xs_bytes(int K, int G = MU) { return al128(xs_gs_off(K, G) + (size_t)G * xf_gs_bytes(K)); }
 
-// Bulk copy of the XF rows of a group's tokens (tok0, and tok1 when mc == 2) into a staging buffer.
-static_assert(MU == 2, "xf_issue stages two rows");
-__device__ __forceinline__ void xf_issue(const XF& xf, int tok0, int tok1, int mc, int K, uint8_t* dst, uint64_t* bar) {
+// Bulk copy of the XF rows of a group's mc tokens (tok[0..mc)) into a staging buffer of G rows; runs of
+// consecutive token rows go as one copy per array.
+template <int G>
+__device__ __forceinline__ void xf_issue(const XF& xf, const int* tok, int mc, int K, uint8_t* dst, uint64_t* bar) {
     const uint32_t fb = (uint32_t)K * 3, sb = (uint32_t)xf_gs_bytes(K);
     const uint8_t* F = reinterpret_cast<const uint8_t*>(xf.frag);
     const uint8_t* Sg = xf.gs;
-    const uint32_t n0 = (mc == 2 && tok1 == tok0 + 1) ? 2u : 1u;  // adjacent rows: one copy each
-    tma_load_1d(dst, F + (size_t)tok0 * fb, n0 * fb, bar);
-    tma_load_1d(dst + xs_gs_off(K), Sg + (size_t)tok0 * sb, n0 * sb, bar);
-    if (mc == 2 && n0 == 1) {
-        tma_load_1d(dst + fb, F + (size_t)tok1 * fb, fb, bar);
-        tma_load_1d(dst + xs_gs_off(K) + sb, Sg + (size_t)tok1 * sb, sb, bar);
+    for (int k = 0; k < mc;) {
+        int n = 1;
+        while (k + n < mc && tok[k + n] == tok[k] + n) n++;
+        tma_load_1d(dst + (size_t)k * fb, F + (size_t)tok[k] * fb, n * fb, bar);
+        tma_load_1d(dst + xs_gs_off(K, G) + (size_t)k * sb, Sg + (size_t)tok[k] * sb, n * sb, bar);
+        k += n;
     }
 }
 
@@ -106,7 +107,7 @@ __device__ void drain(uint64_t* full, int issued, int consumed, int S) {
 //   info         per-stage unit descriptors (int4)
 //   cnt          per-stage finished-warp counters
 //   xf           two XF staging buffers (double-buffered by group)
-//   part         per-stage, per-warp partial results [S][NWC][16 rows][MU]
+//   part         per-stage, per-warp partial results [S][NWC][16 rows][G]
 //   comb         combine scratch of the down kernel (slots and weights of T*K (token, k) pairs)
 //   stages       the ring
 struct Plan {
@@ -114,14 +115,15 @@ struct Plan {
     size_t info_off, cnt_off, xf_off, xfb, part_off, comb_off, stage_off, stage_bytes, extra_off, total;
 };
 constexpr size_t SMEM_CAP = 227 * 1024;
-__host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, size_t comb_bytes, size_t extra = 0) {
+__host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, size_t comb_bytes, size_t extra = 0,
+                                         int G = MU) {
     Plan p;
     p.info_off = 128;
     p.cnt_off = p.info_off + 4 * 16;
     p.xf_off = al128(p.cnt_off + 4 * 4);
-    p.xfb = xs_bytes(K);
+    p.xfb = xs_bytes(K, G);
     p.part_off = al128(p.xf_off + 2 * p.xfb);
-    const size_t part_bytes = (size_t)nwc * 16 * MU * 4;
+    const size_t part_bytes = (size_t)nwc * 16 * G * 4;
     p.stage_bytes = al128(stage_bytes);
     p.S = 4;
     for (;; p.S--) {
@@ -136,18 +138,19 @@ __host__ __device__ inline Plan make_plan(int nwc, int K, size_t stage_bytes, si
 constexpr int NWC_GU = 16;   // consumer warps of the gate/up kernel
 constexpr int NWC_DN = 12;   // consumer warps of the down kernel
 constexpr int DN_ROWS = 64;  // rows of D per down unit
-constexpr int DN_PREP_ITEMS = 2;  // 8-element items of a group's h rows per consumer thread: MU * FF <= 6144
+// 8-element items of a group's h rows per consumer thread of the down kernel: G * FF <= 8 * 32 * NWC_DN * this
+__host__ __device__ constexpr int dn_prep_items(int G) { return G <= 2 ? 2 : 4; }
 // Gate/up tiles: 16 rows of a matrix. Rows of a multiple of 16 bytes come as two 8-row copies, the
 // second at split8_off(rb) (32 bytes past a 128-byte boundary, so that rows 0..7 and 8..15 start on
 // different banks); other rows as one contiguous span copy.
 __host__ __device__ inline bool split8(size_t rb) { return rb % 16 == 0; }
 __host__ __device__ inline size_t split8_off(size_t rb) { return al128(8 * rb) + 32; }
 __host__ __device__ inline size_t gu_slot(size_t rb) { return split8(rb) ? al128(split8_off(rb) + 8 * rb) : al128(16 * rb + 64); }
-__host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu, size_t route_bytes = 0) {
-    return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0, route_bytes);
+__host__ __device__ inline Plan gateup_plan(int D, size_t rbg, size_t rbu, size_t route_bytes = 0, int G = MU) {
+    return make_plan(NWC_GU, D, gu_slot(rbg) + gu_slot(rbu), 0, route_bytes, G);
 }
-__host__ __device__ inline Plan down_plan(int FF, size_t rbd, size_t route_bytes = 0) {
-    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0, route_bytes);
+__host__ __device__ inline Plan down_plan(int FF, size_t rbd, size_t route_bytes = 0, int G = MU) {
+    return make_plan(NWC_DN, FF, rows_slot(rbd, DN_ROWS), 0, route_bytes, G);
 }
 // the down kernel's shared-memory copy of the group list (small batches, whose gate/up kernel routed)
 __host__ __device__ inline size_t down_cache_bytes(const MoeArgs& a) {
@@ -162,9 +165,10 @@ __device__ __forceinline__ int info_bits(int xb, int mc, bool ok, bool fresh) {
 
 // Per-warp epilogue of a 16-row block (one column set, <= 2 tokens): the lane's digit columns are
 // recombined across lanes, value = (a + b/254 + c/254^2 - min) * s; lanes t = 0, 1 end up with token
-// t's values of MMA rows g and g+8, which hold the block's rows row0 and row1. Stored to part[16][MU].
+// t's values of MMA rows g and g+8, which hold the block's rows row0 and row1. Stored to
+// part[row * G + slot0 + t] (part: [16][G]; the set's tokens are the group's slots slot0, slot0 + 1).
 __device__ __forceinline__ void warp_values(const float (&acc)[1][4], const float (&mn)[2], float ts, float* part,
-                                            int row0, int row1) {
+                                            int row0, int row1, int G = MU, int slot0 = 0) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const float A0 = __shfl_down_sync(0xffffffffu, acc[0][0], 1), B0 = __shfl_down_sync(0xffffffffu, acc[0][1], 1);
     const float A1 = __shfl_down_sync(0xffffffffu, acc[0][2], 1), B1 = __shfl_down_sync(0xffffffffu, acc[0][3], 1);
@@ -178,9 +182,9 @@ __device__ __forceinline__ void warp_values(const float (&acc)[1][4], const floa
         v1 = fmaf(fmaf(B1, R, A1), R, acc[0][3]);
     }
     (void)g;
-    if (t < MU) {
-        part[row0 * MU + t] = (v0 - mn[0]) * ts;
-        part[row1 * MU + t] = (v1 - mn[1]) * ts;
+    if (t < 2) {
+        part[row0 * G + slot0 + t] = (v0 - mn[0]) * ts;
+        part[row1 * G + slot0 + t] = (v1 - mn[1]) * ts;
     }
 }
 
@@ -449,8 +453,9 @@ __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_gr
 // kernels); with r.g_info the group list also stays in shared memory. TEAMS: a few tokens, each ranked
 // by a team of 128 threads (latency); otherwise one warp per token (route_token; throughput).
 // Requires blockDim.x >= E (one thread per expert in the scans).
-template <bool TEAMS>
+template <bool TEAMS, int GS = MU>
 __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
+    static_assert(GS >= MU && GS <= 32, "group size");
     const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
     for (int i = tid; i < E; i += blockDim.x) {
@@ -608,7 +613,7 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     {
         int* wtot = reinterpret_cast<int*>(r.scr);  // [3][32] per-warp totals (the ranking scratch is free)
         const int e = tid;
-        const int c = e < E ? r.cnt[e] : 0, g = (c + MU - 1) / MU, ac = c > 0;
+        const int c = e < E ? r.cnt[e] : 0, g = (c + GS - 1) / GS, ac = c > 0;
         int cx = c, gx = g, ax = ac;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -659,8 +664,8 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
         const uint8_t* wg = r.tab ? r.tab[e] : a.gate[e];
         const uint8_t* wu = r.tab ? r.tab[E + e] : a.up[e];
         const uint8_t* wd = r.tab ? r.tab[2 * E + e] : a.down[e];
-        for (int j = 0; j * MU < c; j++) {
-            const int gi = r.goff[e] + j, s0 = r.off[e] + j * MU, mc = min(MU, c - j * MU);
+        for (int j = 0; j * GS < c; j++) {
+            const int gi = r.goff[e] + j, s0 = r.off[e] + j * GS, mc = min(GS, c - j * GS);
             if (global) {
                 GroupRec& g = a.rw.groups[gi];
                 g.w[0] = wg;
@@ -669,7 +674,8 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
                 g.e = e;
                 g.s0 = s0;
                 g.mc = mc;
-                for (int k = mc; k < MU; k++) g.tok[k] = 0;
+                if (GS == MU)  // wider groups take their tokens from the slot map
+                    for (int k = mc; k < MU; k++) g.tok[k] = 0;
             }
             if (r.g_info) {
                 r.g_info[4 * gi] = e;
@@ -689,10 +695,10 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
         const int t = i / K;
         const int e = r.s_ids[i];
         const int pos = __popcll(r.mask[e] & ((1ull << t) - 1ull)), sl = r.off[e] + pos;
-        const int gi = r.goff[e] + pos / MU;
-        if (r.g_tok) r.g_tok[MU * gi + pos % MU] = t;
+        const int gi = r.goff[e] + pos / GS;
+        if (r.g_tok) r.g_tok[MU * gi + pos % GS] = t;
         if (global) {
-            a.rw.groups[gi].tok[pos % MU] = t;
+            if (GS == MU) a.rw.groups[gi].tok[pos % MU] = t;
             a.rw.slot_token[sl] = t;
             a.rw.slot_w[sl] = r.s_w[i];
             int rank = 0;
@@ -714,18 +720,19 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         return;
     }
     __shared__ __align__(16) uint8_t rsm[route_sm_bytes(MAX_EXPERTS, MOE_TMAX * 32, false) + 16];
-    route_block<false>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
+    route_block<false, GW>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
 }
 
 // ------------------------------------------------------------------------------------------------
 // gate + up + SiLU*mul
 // ------------------------------------------------------------------------------------------------
-template <int QG, int QU>
+template <int QG, int QU, int G>
 __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int D = a.D, FF = a.FF, nsb = D >> 8, NRB = FF >> 4, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int TK = a.T * a.n_used;
-    const Plan pl = gateup_plan(D, a.gate_rb, a.up_rb, a.fused_route ? route_sm_bytes(a.n_expert, TK, true) : 0);
+    const bool fused = G == MU && a.fused_route;  // routing inside (small batches; groups of MU slots)
+    const Plan pl = gateup_plan(D, a.gate_rb, a.up_rb, fused ? route_sm_bytes(a.n_expert, TK, true) : 0, G);
     const int S = pl.S;
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + 4;
@@ -742,7 +749,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         mbar_fence_init();
     }
     RouteSm rt{};
-    if (a.fused_route) {  // the experts' matrix table does not depend on earlier grids
+    if (fused) {  // the experts' matrix table does not depend on earlier grids
         rt = route_sm_carve(sm + pl.extra_off, a.n_expert, TK, true);
         const int E = a.n_expert;
         for (int i = tid; i < 3 * E; i += blockDim.x) rt.tab[i] = i < E ? a.gate[i] : i < 2 * E ? a.up[i - E] : a.down[i - 2 * E];
@@ -752,13 +759,15 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
     pdl_wait();  // routing results (or the logits) and the XF of the tokens come from the previous grids
     // small batches: every CTA routes the tokens itself into shared memory (CTA 0 also publishes the
     // routing, groups and slot maps for the down kernel and the combine)
-    if (a.fused_route) {
-        route_block<true>(a, rt, blockIdx.x == 0);
-        __syncthreads();
+    if constexpr (G == MU) {
+        if (fused) {
+            route_block<true>(a, rt, blockIdx.x == 0);
+            __syncthreads();
+        }
     }
-    const int G = a.fused_route ? *rt.G : a.rw.ngroups[0];
+    const int NG = fused ? *rt.G : a.rw.ngroups[0];
     auto group = [&](int gi) {
-        if (!a.fused_route) return a.rw.groups[gi];
+        if (!fused) return a.rw.groups[gi];
         GroupRec g{};
         g.w[0] = rt.g_w[3 * gi];
         g.w[1] = rt.g_w[3 * gi + 1];
@@ -770,7 +779,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         for (int k = 0; k < MU; k++) g.tok[k] = rt.g_tok[MU * gi + k];
         return g;
     };
-    const int nunits = G * NRB;
+    const int nunits = NG * NRB;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const size_t rbg = a.gate_rb, rbu = a.up_rb, up_at = gu_slot(rbg);
     const Rows Lg = rows_of(rbg), Lu = rows_of(rbu);  // span layouts (rows that are not 16-byte multiples)
@@ -808,7 +817,11 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
                 bytes += split8(rbu) ? (uint32_t)(16 * rbu) : rows_copy_bytes(Lu, rec.w[1], rbu, r0, 16);
             }
             mbar_expect_tx(&full[s], bytes);
-            if (fresh) xf_issue(a.xf, rec.tok[0], rec.tok[1], rec.mc, D, sm + pl.xf_off + (size_t)xb * pl.xfb, &full[s]);
+            if (fresh) {
+                int tok[G];
+                for (int k = 0; k < rec.mc; k++) tok[k] = G == MU ? rec.tok[k < MU ? k : 0] : a.rw.slot_token[rec.s0 + k];
+                xf_issue<G>(a.xf, tok, rec.mc, D, sm + pl.xf_off + (size_t)xb * pl.xfb, &full[s]);
+            }
             if (ok) {
                 if (split8(rbg)) {
                     tma_load_1d(stage, rec.w[0] + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
@@ -852,19 +865,23 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         const int4 in = info[s];
         const int rb = in.x, xb = in.y & 1, mc = (in.y >> 4) & 15, s0 = in.z;
         const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
-        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
-        if (in.y & 256) {
-            const BPtr<1> bp(xs, D >> 5, mc);
-            const uint8_t* mq = min_operand(xs + xs_gs_off(D), D, mc);
-            const uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
-            if (mtx == 0)
-                block_tasks<QG>(rows_gu(stage, rbg, in.w & 255), nsb, wsub, 8, bp, mq, acc, mn);
-            else
-                block_tasks<QU>(rows_gu(stage + up_at, rbu, (in.w >> 8) & 255), nsb, wsub, 8, bp, mq, acc, mn);
+        float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_GU + warp) * 16 * G;
+        const uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
+        for (int st = 0; 2 * st < mc; st++) {  // column sets: slots 2 st, 2 st + 1 of the group
+            const int ms = mc - 2 * st;
+            const uint8_t* xg = xs + xs_gs_off(D, G) + (size_t)(2 * st) * xf_gs_bytes(D);
+            float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
+            if (in.y & 256) {
+                const BPtr<1> bp(xs + (size_t)(2 * st) * D * 3, D >> 5, ms);
+                const uint8_t* mq = min_operand(xg, D, ms);
+                if (mtx == 0)
+                    block_tasks<QG>(rows_gu(stage, rbg, in.w & 255), nsb, wsub, 8, bp, mq, acc, mn);
+                else
+                    block_tasks<QU>(rows_gu(stage + up_at, rbu, (in.w >> 8) & 255), nsb, wsub, 8, bp, mq, acc, mn);
+            }
+            const float ts = t < ms ? *reinterpret_cast<const float*>(xg + (size_t)t * xf_gs_bytes(D)) : 0.f;
+            warp_values(acc, mn, ts, part, prow0, prow1, G, 2 * st);
         }
-        const float ts = t < mc ? *reinterpret_cast<const float*>(xs + xs_gs_off(D) + (size_t)t * xf_gs_bytes(D)) : 0.f;
-        float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_GU + warp) * 16 * MU;
-        warp_values(acc, mn, ts, part, prow0, prow1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&done[s]);
         if (warp == i % NWC_GU) {  // this unit's reducer (round robin): SiLU*mul of the summed partials
@@ -873,16 +890,18 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
                 atomicExch(&abort_flag, 1);
                 return;
             }
-            const float* P = reinterpret_cast<const float*>(sm + pl.part_off) + (size_t)s * NWC_GU * 16 * MU;
-            const int r = lane >> 1, tk = lane & 1;
-            if (tk < mc) {
-                float gv = 0.f, uv = 0.f;
+            const float* P = reinterpret_cast<const float*>(sm + pl.part_off) + (size_t)s * NWC_GU * 16 * G;
+            for (int j = lane; j < 16 * G; j += 32) {
+                const int r = j / G, tk = j - r * G;
+                if (tk < mc) {
+                    float gv = 0.f, uv = 0.f;
 #pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    gv += P[(w * 16 + r) * MU + tk];
-                    uv += P[((8 + w) * 16 + r) * MU + tk];
+                    for (int w = 0; w < 8; w++) {
+                        gv += P[(w * 16 + r) * G + tk];
+                        uv += P[((8 + w) * 16 + r) * G + tk];
+                    }
+                    a.h[(size_t)(s0 + tk) * FF + 16 * rb + r] = silu_mul(gv, uv);
                 }
-                a.h[(size_t)(s0 + tk) * FF + 16 * rb + r] = silu_mul(gv, uv);
             }
         }
         __syncwarp();
@@ -1088,13 +1107,14 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup_fs(MoeArgs 
 // ------------------------------------------------------------------------------------------------
 // down projection + weighted combine + residual add
 // ------------------------------------------------------------------------------------------------
-template <int QD>
+template <int QD, int G>
 __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
+    constexpr int PI = dn_prep_items(G);
     extern __shared__ __align__(128) uint8_t sm[];
     const int D = a.D, FF = a.FF, nsb = FF >> 8, NRG = D / DN_ROWS;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t rb = a.down_rb;
-    const Plan pl = down_plan(FF, rb, down_cache_bytes(a));
+    const Plan pl = down_plan(FF, rb, down_cache_bytes(a), G);
     const int S = pl.S;
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + 4;
@@ -1117,16 +1137,16 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     pdl_wait();  // h and the routing come from the previous grids
     // small batches: the whole group list (at most T*K records) is read into shared memory in the same
     // round trip as its length
-    GroupRec* gcache = a.fused_route ? reinterpret_cast<GroupRec*>(sm + pl.extra_off) : nullptr;
+    GroupRec* gcache = G == MU && a.fused_route ? reinterpret_cast<GroupRec*>(sm + pl.extra_off) : nullptr;
     if (gcache) {
         const int4* src = reinterpret_cast<const int4*>(a.rw.groups);
         int4* dst = reinterpret_cast<int4*>(gcache);
         for (int i = tid; i < a.T * a.n_used * (int)(sizeof(GroupRec) / 16); i += blockDim.x) dst[i] = __ldcg(src + i);
     }
-    const int G = a.rw.ngroups[0];
+    const int NG = a.rw.ngroups[0];
     if (gcache) __syncthreads();
     auto group = [&](int gi) { return gcache ? gcache[gi] : a.rw.groups[gi]; };
-    const int nunits = G * NRG;
+    const int nunits = NG * NRG;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const Rows L = rows_of(rb);
 
@@ -1176,7 +1196,7 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     // each thread loads up to DN_PREP_ITEMS items of 8 elements (every warp's items belong to one row),
     // the rows' max |h| are combined across the warps, then each thread writes its items' digits and
     // sums. False after a timed-out wait (flagged; the caller ends the warp).
-    __shared__ float s_pmax[MU][NWC_DN * DN_PREP_ITEMS];
+    __shared__ float s_pmax[G][NWC_DN * PI];
     uint32_t cphase = 0;
     auto consumers_sync = [&]() {
         __syncwarp();
@@ -1192,9 +1212,9 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
     auto prep_group = [&](int xb, int s0, int mc) {
         uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
         const int nit = FF >> 3, tot = mc * nit;  // nit % 32 == 0: warp-uniform rows and bounds
-        float4 u[DN_PREP_ITEMS], w[DN_PREP_ITEMS];
+        float4 u[PI], w[PI];
 #pragma unroll
-        for (int k = 0; k < DN_PREP_ITEMS; k++) {
+        for (int k = 0; k < PI; k++) {
             const int it = tid + NWC_DN * 32 * k, tk = it < tot ? it / nit : 0, i = it - tk * nit;
             float m = 0.f;
             if (it < tot) {
@@ -1206,26 +1226,24 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
             }
 #pragma unroll
             for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane < MU) s_pmax[lane][warp * DN_PREP_ITEMS + k] = (it < tot && lane == tk) ? m : 0.f;
+            if (lane < G) s_pmax[lane][warp * PI + k] = (it < tot && lane == tk) ? m : 0.f;
         }
         if (!consumers_sync()) return false;
-        float inv[MU];
-#pragma unroll
-        for (int tk = 0; tk < MU; tk++) {
+        auto row_max = [&](int tk) {  // max |h| of row tk over every warp's items
             float mx = 0.f;
-            for (int j = 0; j < NWC_DN * DN_PREP_ITEMS; j++) mx = fmaxf(mx, s_pmax[tk][j]);
-            if (!(mx > 0.f) || mx == INFINITY) mx = 127.f;
-            inv[tk] = 127.f / mx;
-            if (tid == tk && tk < mc)
-                *reinterpret_cast<float4*>(xs + xs_gs_off(FF) + (size_t)tk * xf_gs_bytes(FF)) = make_float4(mx / 127.f, 0.f, 0.f, 0.f);
-        }
+            for (int j = 0; j < NWC_DN * PI; j++) mx = fmaxf(mx, s_pmax[tk][j]);
+            return (!(mx > 0.f) || mx == INFINITY) ? 127.f : mx;
+        };
+        if (tid < mc)
+            *reinterpret_cast<float4*>(xs + xs_gs_off(FF, G) + (size_t)tid * xf_gs_bytes(FF)) =
+                make_float4(row_max(tid) / 127.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int k = 0; k < DN_PREP_ITEMS; k++) {
+        for (int k = 0; k < PI; k++) {
             const int it = tid + NWC_DN * 32 * k;
             if (it < tot) {  // warp-uniform
                 const int tk = it / nit;
-                prep_item(u[k], w[k], it - tk * nit, tk ? inv[1] : inv[0], reinterpret_cast<uint2*>(xs + (size_t)tk * FF * 3),
-                          xs + xs_gs_off(FF) + (size_t)tk * xf_gs_bytes(FF));
+                prep_item(u[k], w[k], it - tk * nit, 127.f / row_max(tk), reinterpret_cast<uint2*>(xs + (size_t)tk * FF * 3),
+                          xs + xs_gs_off(FF, G) + (size_t)tk * xf_gs_bytes(FF));
             }
         }
         return consumers_sync();  // the group's rows are ready for every consumer warp (and s_pmax is free)
@@ -1246,16 +1264,20 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         const int rg = in.x, xb = in.y & 1, mc = (in.y >> 4) & 15, s0 = in.z;
         if ((in.y & 512) && u != u0 && !prep_group(xb, s0, mc)) return;  // a later group's first unit here
         const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
-        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
-        if (in.y & 256) {
-            const BPtr<1> bp(xs, FF >> 5, mc);
-            block_tasks<QD>(rows_pair(sm + pl.stage_off + (size_t)s * pl.stage_bytes + in.w + (size_t)(16 * rbk) * L.stride,
-                                      L.stride),
-                            nsb, wsub, 3, bp, min_operand(xs + xs_gs_off(FF), FF, mc), acc, mn);
+        float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_DN + warp) * 16 * G;
+        for (int st = 0; 2 * st < mc; st++) {  // column sets: slots 2 st, 2 st + 1 of the group
+            const int ms = mc - 2 * st;
+            const uint8_t* xg = xs + xs_gs_off(FF, G) + (size_t)(2 * st) * xf_gs_bytes(FF);
+            float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
+            if (in.y & 256) {
+                const BPtr<1> bp(xs + (size_t)(2 * st) * FF * 3, FF >> 5, ms);
+                block_tasks<QD>(rows_pair(sm + pl.stage_off + (size_t)s * pl.stage_bytes + in.w + (size_t)(16 * rbk) * L.stride,
+                                          L.stride),
+                                nsb, wsub, 3, bp, min_operand(xg, FF, ms), acc, mn);
+            }
+            const float ts = t < ms ? *reinterpret_cast<const float*>(xg + (size_t)t * xf_gs_bytes(FF)) : 0.f;
+            warp_values(acc, mn, ts, part, 2 * ((lane >> 2) & 7), 2 * ((lane >> 2) & 7) + 1, G, 2 * st);
         }
-        const float ts = t < mc ? *reinterpret_cast<const float*>(xs + xs_gs_off(FF) + (size_t)t * xf_gs_bytes(FF)) : 0.f;
-        float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_DN + warp) * 16 * MU;
-        warp_values(acc, mn, ts, part, 2 * ((lane >> 2) & 7), 2 * ((lane >> 2) & 7) + 1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&done[s]);
         const bool reducer = warp == i % NWC_DN;
@@ -1265,13 +1287,13 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
                 atomicExch(&abort_flag, 1);
                 return;
             }
-            const float* P = reinterpret_cast<const float*>(sm + pl.part_off) + (size_t)s * NWC_DN * 16 * MU;
-            for (int j = lane; j < DN_ROWS * MU; j += 32) {
-                const int r = j >> 1, tk = j & 1;
+            const float* P = reinterpret_cast<const float*>(sm + pl.part_off) + (size_t)s * NWC_DN * 16 * G;
+            for (int j = lane; j < DN_ROWS * G; j += 32) {
+                const int r = j / G, tk = j - r * G;
                 if (tk < mc) {
                     const int rk = r >> 4, rr = r & 15;
-                    const float v = (P[((3 * rk) * 16 + rr) * MU + tk] + P[((3 * rk + 1) * 16 + rr) * MU + tk]) +
-                                    P[((3 * rk + 2) * 16 + rr) * MU + tk];
+                    const float v = (P[((3 * rk) * 16 + rr) * G + tk] + P[((3 * rk + 1) * 16 + rr) * G + tk]) +
+                                    P[((3 * rk + 2) * 16 + rr) * G + tk];
                     a.y[(size_t)(s0 + tk) * D + DN_ROWS * rg + r] = v;
                 }
             }
@@ -1419,7 +1441,10 @@ void smem_attr(Kern k, size_t smem) {
         cur = smem;
     }
 }
-int max_groups(const MoeArgs& a) { return std::min(a.T * a.n_used, a.n_expert * ((a.T + MU - 1) / MU)); }
+int max_groups(const MoeArgs& a) {
+    const int g = a.gsz == GW ? GW : MU;
+    return std::min(a.T * a.n_used, a.n_expert * ((a.T + g - 1) / g));
+}
 
 }  // namespace
 
@@ -1433,14 +1458,14 @@ cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st) {
     return launch_pdl(k_moe_route, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a);
 }
 
-template <int QG, int QU>
+template <int QG, int QU, int G>
 static cudaError_t gateup_as(const MoeArgs& a, cudaStream_t st) {
-    const Plan pl = gateup_plan(a.D, a.gate_rb, a.up_rb,
-                                a.fused_route ? route_sm_bytes(a.n_expert, a.T * a.n_used, true) : 0);
+    const bool fused = G == MU && a.fused_route;
+    const Plan pl = gateup_plan(a.D, a.gate_rb, a.up_rb, fused ? route_sm_bytes(a.n_expert, a.T * a.n_used, true) : 0, G);
     if (pl.total > SMEM_CAP || (a.FF >> 4) < pl.S) return cudaErrorInvalidValue;
-    smem_attr(k_moe_gateup<QG, QU>, pl.total);
+    smem_attr(k_moe_gateup<QG, QU, G>, pl.total);
     const int units = max_groups(a) * (a.FF >> 4);
-    return launch_pdl(k_moe_gateup<QG, QU>, dim3(std::min(sm_count(), units)), (NWC_GU + 1) * 32, pl.total, st, a);
+    return launch_pdl(k_moe_gateup<QG, QU, G>, dim3(std::min(sm_count(), units)), (NWC_GU + 1) * 32, pl.total, st, a);
 }
 template <int QG, int QU>
 static cudaError_t gateup_pick(const MoeArgs& a, cudaStream_t st) {
@@ -1453,7 +1478,7 @@ static cudaError_t gateup_pick(const MoeArgs& a, cudaStream_t st) {
                               a);
         }
     }
-    return gateup_as<QG, QU>(a, st);
+    return a.gsz == GW ? gateup_as<QG, QU, GW>(a, st) : gateup_as<QG, QU, MU>(a, st);
 }
 template <int QG>
 static cudaError_t gateup_g(const MoeArgs& a, cudaStream_t st) {
@@ -1474,22 +1499,23 @@ cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st) {
     }
 }
 
-template <int QD>
+template <int QD, int G>
 static cudaError_t down_as(const MoeArgs& a, cudaStream_t st) {
-    const Plan pl = down_plan(a.FF, a.down_rb, down_cache_bytes(a));
-    if (pl.total > SMEM_CAP || a.D / DN_ROWS < pl.S) return cudaErrorInvalidValue;
-    smem_attr(k_moe_down<QD>, pl.total);
+    const Plan pl = down_plan(a.FF, a.down_rb, G == MU ? down_cache_bytes(a) : 0, G);
+    if (pl.total > SMEM_CAP || a.D / DN_ROWS < pl.S || G * (a.FF / 8) > dn_prep_items(G) * NWC_DN * 32)
+        return cudaErrorInvalidValue;
+    smem_attr(k_moe_down<QD, G>, pl.total);
     const int units = max_groups(a) * (a.D / DN_ROWS);
-    return launch_pdl(k_moe_down<QD>, dim3(std::min(sm_count(), units)), (NWC_DN + 1) * 32, pl.total, st, a);
+    return launch_pdl(k_moe_down<QD, G>, dim3(std::min(sm_count(), units)), (NWC_DN + 1) * 32, pl.total, st, a);
 }
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st, bool combine) {
-    if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX || MU * (a.FF / 8) > DN_PREP_ITEMS * NWC_DN * 32)
-        return cudaErrorInvalidValue;
+    if (a.FF % 256 || a.D % DN_ROWS || a.T > MOE_TMAX) return cudaErrorInvalidValue;
     cudaError_t e;
+    const bool w = a.gsz == GW;
     switch (a.down_type) {
-        case T_Q4_K: e = down_as<T_Q4_K>(a, st); break;
-        case T_Q5_K: e = down_as<T_Q5_K>(a, st); break;
-        case T_Q6_K: e = down_as<T_Q6_K>(a, st); break;
+        case T_Q4_K: e = w ? down_as<T_Q4_K, GW>(a, st) : down_as<T_Q4_K, MU>(a, st); break;
+        case T_Q5_K: e = w ? down_as<T_Q5_K, GW>(a, st) : down_as<T_Q5_K, MU>(a, st); break;
+        case T_Q6_K: e = w ? down_as<T_Q6_K, GW>(a, st) : down_as<T_Q6_K, MU>(a, st); break;
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess || !combine) return e;
