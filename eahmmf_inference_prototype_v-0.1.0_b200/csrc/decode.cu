@@ -201,21 +201,35 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // One warp merges the nsplit partial records [m, l, o[HD]] of one (token, q head) (p: the first record):
 // lane y holds split y's m and l (nsplit <= 128); v[j] = element lane + 32 j of sum_y e_y o_y / sum_y e_y l_y,
 // e_y = expf(m_y - max m) (splits without positions weigh 0), the o sum in split order. The records are
-// read eight splits at a time (independent loads in flight); CG: through L2 only (records written by
-// other blocks of the same grid).
-template <int HD, bool CG>
+// read eight splits at a time (independent loads in flight), or with EARLY and up to 16 splits all of
+// them together with the m, l loads (64 more registers); CG: through L2 only (records written by other
+// blocks of the same grid).
+template <int HD, bool CG, bool EARLY>
 __device__ __forceinline__ void merge_head(const float* __restrict__ p, int nsplit, float (&v)[HD / 32]) {
     constexpr int PER = HD / 32;
     const int lane = threadIdx.x & 31;
     auto ld = [](const float* a) { return CG ? __ldcg(a) : *a; };
+    auto load8 = [&](int y0, float (&r)[8][PER]) {  // the o records of splits y0 .. y0 + 7
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+#pragma unroll
+            for (int j = 0; j < PER; j++)
+                r[u][j] = y0 + u < nsplit ? ld(p + (size_t)(y0 + u) * (HD + 2) + 2 + lane + 32 * j) : 0.f;
+    };
     float mq[4], lq[4], M = -INFINITY;
 #pragma unroll
     for (int q4 = 0; q4 < 4; q4++) {
         const int yy = lane + 32 * q4;
         mq[q4] = yy < nsplit ? ld(p + (size_t)yy * (HD + 2)) : -INFINITY;
         lq[q4] = yy < nsplit ? ld(p + (size_t)yy * (HD + 2) + 1) : 0.f;
-        M = fmaxf(M, mq[q4]);
     }
+    float r0[8][PER], r1[8][PER];
+    if (EARLY && nsplit <= 16) {  // up to 16 splits: every record's loads in flight together with m and l
+        load8(0, r0);
+        load8(8, r1);
+    }
+#pragma unroll
+    for (int q4 = 0; q4 < 4; q4++) M = fmaxf(M, mq[q4]);
 #pragma unroll
     for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float eq[4], L = 0.f;
@@ -229,15 +243,9 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ p, int nspl
     float o[PER];
 #pragma unroll
     for (int j = 0; j < PER; j++) o[j] = 0.f;
-    for (int y0 = 0; y0 < nsplit; y0 += 8) {
+    auto accumulate = [&](int y0, const float (&r)[8][PER]) {  // splits y0 .. y0 + 7 in order
         const int q4 = y0 >> 5;  // the eight splits share one lane group of eq
         const float eg = q4 == 0 ? eq[0] : q4 == 1 ? eq[1] : q4 == 2 ? eq[2] : eq[3];
-        float r[8][PER];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-#pragma unroll
-            for (int j = 0; j < PER; j++)
-                r[u][j] = y0 + u < nsplit ? ld(p + (size_t)(y0 + u) * (HD + 2) + 2 + lane + 32 * j) : 0.f;
 #pragma unroll
         for (int u = 0; u < 8; u++) {
             const float e = __shfl_sync(0xffffffffu, eg, (y0 + u) & 31);
@@ -245,6 +253,16 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ p, int nspl
 #pragma unroll
                 for (int j = 0; j < PER; j++) o[j] = fmaf(r[u][j], e, o[j]);
             }
+        }
+    };
+    if (EARLY && nsplit <= 16) {
+        accumulate(0, r0);
+        accumulate(8, r1);
+    } else {
+        for (int y0 = 0; y0 < nsplit; y0 += 8) {
+            float r[8][PER];
+            load8(y0, r);
+            accumulate(y0, r);
         }
     }
     const float inv = 1.0f / L;
@@ -426,7 +444,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
         __threadfence();
         for (int hq = warp; hq < grp; hq += nwarp) {
             float v[PER];
-            merge_head<HD, true>(part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2), nsplit, v);
+            merge_head<HD, true, true>(part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2), nsplit, v);
 #pragma unroll
             for (int j = 0; j < PER; j++) rf.att[(size_t)t * QD + (size_t)(h * grp + hq) * HD + lane + 32 * j] = v[j];
         }
@@ -449,7 +467,7 @@ __global__ void __launch_bounds__(MP_NT) k_attn_merge_prep(const float* __restri
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, QD = n_head * HD;
     for (int hq = warp; hq < n_head; hq += MP_NT / 32) {
         float v[PER];
-        merge_head<HD, false>(part + ((size_t)t * n_head + hq) * nsplit * (HD + 2), nsplit, v);
+        merge_head<HD, false, false>(part + ((size_t)t * n_head + hq) * nsplit * (HD + 2), nsplit, v);
 #pragma unroll
         for (int j = 0; j < PER; j++) {
             mrow[hq * HD + lane + 32 * j] = v[j];

@@ -589,7 +589,7 @@ struct EahmmfEngine {
         g.pro = GEMV_PRO_NORM;
         g.prow = x;
         g.py = pending.y;
-        g.pslots = pending.token_slots;
+        g.pslots = nullptr;  // single-token MoE call: the token's slots are 0..K-1 in expert order
         g.pw = pending.slot_w;
         g.pK = pending.y ? pending.K : 0;
         g.pnw = L.attn_norm;
@@ -618,7 +618,7 @@ struct EahmmfEngine {
         o.pro = GEMV_PRO_ROW;
         o.prow = att;
         o.ey = pending.y;
-        o.eslots = pending.token_slots;
+        o.eslots = nullptr;
         o.ew = pending.slot_w;
         o.eK = pending.y ? pending.K : 0;
         if (launch_gemv_xf(o, st) != cudaSuccess || !mark(5)) return ST_CUDA;

@@ -266,9 +266,12 @@ __host__ __device__ inline GPlan gemv_plan(int qt, int K, size_t rb, int nset, i
     (void)qt;
     return unit_plan(K, m, 2 * (K / 256), nset, slot_bytes(row_layout(rb, true), 16));
 }
-// shared memory of k_gemv's prologue (after the plan's total): the fp32 row [K], the norm weights [K], the
-// XF gs row, the reduction scratch (33 floats) and the pending combine's slots and weights (32 each)
-__host__ __device__ inline size_t gemv_pro_bytes(int K) { return (size_t)K * 8 + al128(xf_gs_bytes(K)) + 128 * 3 + 256; }
+// shared memory of k_gemv's prologue and combine epilogue (after the plan's total): the fp32 row [K], the
+// norm weights [K], the XF gs row, the reduction scratch (33 floats), the pending combine's slots and
+// weights (32 each), its y values of the block's 16 rows [32][16] and the residual rows [16]
+__host__ __device__ inline size_t gemv_pro_bytes(int K) {
+    return (size_t)K * 8 + al128(xf_gs_bytes(K)) + 128 * 3 + 256 + (32 * 16 + 16) * 4;
+}
 
 template <int QT, int NSET>
 __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
@@ -298,6 +301,8 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
     float* red = reinterpret_cast<float*>(gs_s + al128(xf_gs_bytes(K)));
     int* sl_s = reinterpret_cast<int*>(red + 64);
     float* sw_s = reinterpret_cast<float*>(sl_s + 32);
+    float* ey_s = sw_s + 32;  // [32 slots][16 rows] of the epilogue's pending combine
+    float* x_s = ey_s + 32 * 16;
     if (a.pro == GEMV_PRO_NORM)  // the norm weights do not depend on earlier grids
         for (int i = tid; i < K / 4; i += NTU)
             reinterpret_cast<float4*>(nw_s)[i] = __ldg(reinterpret_cast<const float4*>(a.pnw) + i);
@@ -317,10 +322,13 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
         }
         prep_row(prow_s, K, reinterpret_cast<uint2*>(sfrag), ssum, gs_s, red);
     }
-    if (a.ey && tid < a.eK) {  // the epilogue's pending combine
-        const int sl = a.eslots[tid];
-        sl_s[tid] = sl;
-        sw_s[tid] = a.ew[sl];
+    if (a.ey) {  // the epilogue's pending combine and residual rows, loaded with the prologue's loads
+        for (int i = tid; i < a.eK * 16; i += NTU) {
+            const int k = i >> 4, r = i & 15, sl = a.eslots ? a.eslots[k] : k;
+            ey_s[i] = r0 + r < r1 ? a.ey[(size_t)sl * a.W.rows + r0 + r] : 0.f;
+            if (r == 0) sw_s[k] = a.ew[sl];
+        }
+        if (tid < 16) x_s[tid] = r0 + tid < r1 ? a.Y[r0 + tid] : 0.f;
     }
     __syncthreads();
     if (__syncthreads_or(!mbar_wait_bounded(&bar[0], 0u))) {
@@ -341,8 +349,8 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
             float base = *y;
             if (a.ey) {  // x + sum_k w_k y_k in the norm kernel's order (combine_norm_row), then + v
                 float acc = 0.f;
-                for (int k = 0; k < a.eK; k++) acc = fmaf(sw_s[k], a.ey[(size_t)sl_s[k] * a.W.rows + r0 + r], acc);
-                base += acc;
+                for (int k = 0; k < a.eK; k++) acc = fmaf(sw_s[k], ey_s[k * 16 + r], acc);
+                base = x_s[r] + acc;
             }
             *y = base + v;
         } else {
@@ -494,7 +502,7 @@ static void smem_attr(Kern k, size_t smem) {
 template <int QT, int NSET>
 static void gemv_go(const GemvXArgs& a, cudaStream_t st) {
     const GPlan pl = gemv_plan(QT, a.W.K, a.W.row_bytes, NSET, a.m);
-    const size_t smem = pl.total + (a.pro ? gemv_pro_bytes(a.W.K) : 0);
+    const size_t smem = pl.total + (a.pro || a.ey ? gemv_pro_bytes(a.W.K) : 0);
     smem_attr(k_gemv<QT, NSET>, smem);
     launch_pdl(k_gemv<QT, NSET>, dim3((a.W.rows + 15) / 16), dim3(NTU), smem, st, a);
 }
@@ -503,7 +511,8 @@ cudaError_t launch_gemv_xf(const GemvXArgs& a, cudaStream_t st) {
     if (a.m < 1 || a.m > TPASS || !gemv_mma_ok(a.W)) return cudaErrorInvalidValue;
     if ((a.pro && (a.m != 1 || !a.prow || (a.pro == GEMV_PRO_NORM && (!a.pnw || a.pK > 32)) ||
                    gemv_plan(a.W.type, a.W.K, a.W.row_bytes, 1, 1).total + gemv_pro_bytes(a.W.K) > SMEM_CAP)) ||
-        (a.ey && (a.m != 1 || !a.accumulate || a.eK > 32)))
+        (a.ey && (a.m != 1 || !a.accumulate || a.eK > 32 ||
+                  gemv_plan(a.W.type, a.W.K, a.W.row_bytes, 1, 1).total + gemv_pro_bytes(a.W.K) > SMEM_CAP)))
         return cudaErrorInvalidValue;
     const bool two = a.m > TOK_PER_SET;
     switch (a.W.type) {

@@ -109,6 +109,7 @@ struct GemvXArgs {
     float peps;
     // Epilogue (accumulate, m == 1): each output row first takes the token's pending MoE combine, as the
     // norm kernel would have added it: Y = (Y + sum_k w_k ey[slot_k]) + value (ey rows of W.rows floats).
+    // pslots / eslots null: slot k is k (the slot map of a single-token MoE call).
     const float* ey;
     const int* eslots;
     const float* ew;

@@ -174,7 +174,8 @@ __device__ __forceinline__ void prep_row(const float* __restrict__ x, int K, uin
 }
 
 // The RMSNorm input of one token: its residual row x (n floats, global) plus its pending MoE combine
-// sum_k w_k y[slot_k] (K slots in ascending expert order; K = 0: none), into row[] (shared memory),
+// sum_k w_k y[slot_k] (K slots in ascending expert order; K = 0: none; slots null: slot k is k, the map
+// of a single-token MoE call, so no load waits for the map), into row[] (shared memory),
 // then normalised in place: row = (row * (1 / sqrtf(mean(row^2) + eps))) * w. Every element is formed
 // the same way whatever the block size (blockDim.x >= 128, a multiple of 32; all threads call it), the
 // sum of squares in row_sumsq128's order. Each thread handles CN_PAIRS element pairs per pass, their
@@ -187,7 +188,44 @@ __device__ __forceinline__ void combine_norm_row(const float* __restrict__ x, co
                                                  int K, const float* w, float eps, int n, float* row, float* xw,
                                                  float* xn, int* sl, float* sw, float* red) {
     const int tid = threadIdx.x, nt = blockDim.x;
-    if (y) {
+    if (y && !slots) {  // identity slot map: the weights and rows load together, one round trip
+        for (int i0 = 2 * tid; i0 < n; i0 += 2 * nt * CN_PAIRS) {
+            float2 acc[CN_PAIRS], xv[CN_PAIRS];
+#pragma unroll
+            for (int p = 0; p < CN_PAIRS; p++) {
+                const int i = i0 + 2 * nt * p;
+                acc[p] = make_float2(0.f, 0.f);
+                xv[p] = i < n ? *reinterpret_cast<const float2*>(x + i) : make_float2(0.f, 0.f);
+            }
+#pragma unroll 8
+            for (int k = 0; k < K; k++) {
+                const float wk = __ldg(slot_w + k);
+                const float* yk = y + (size_t)k * n;
+                float2 v[CN_PAIRS];
+#pragma unroll
+                for (int p = 0; p < CN_PAIRS; p++) {
+                    const int i = i0 + 2 * nt * p;
+                    v[p] = i < n ? *reinterpret_cast<const float2*>(yk + i) : make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int p = 0; p < CN_PAIRS; p++) {
+                    acc[p].x = fmaf(wk, v[p].x, acc[p].x);
+                    acc[p].y = fmaf(wk, v[p].y, acc[p].y);
+                }
+            }
+#pragma unroll
+            for (int p = 0; p < CN_PAIRS; p++) {
+                const int i = i0 + 2 * nt * p;
+                if (i < n) {
+                    xv[p].x += acc[p].x;
+                    xv[p].y += acc[p].y;
+                    if (xw) *reinterpret_cast<float2*>(xw + i) = xv[p];
+                    row[i] = xv[p].x;
+                    row[i + 1] = xv[p].y;
+                }
+            }
+        }
+    } else if (y) {
         if (tid < K) {
             const int s = slots[tid];
             sl[tid] = s;
