@@ -571,7 +571,7 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
     for (int j = 0; j < F32_PF; j++) {
         const int i = threadIdx.x + j * F32_NT;
         wpf[j] = row < rows && i < n4 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        gpf[j] = row < rows && nw && i < n4 ? __ldg(g4 + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+        gpf[j] = nw && i < n4 ? __ldg(g4 + i) : make_float4(1.f, 1.f, 1.f, 1.f);  // prep blocks too
     }
     pdl_trigger();
     pdl_wait();
@@ -580,9 +580,19 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
         const int t = row - rows;
         if (!(prep && blockIdx.y == 0 && t < m_all)) return;
         const float* xr = X + (size_t)t * ldx;
-        if (nw) {  // RMSNorm of the row first (qwen3moe.cpp:527-532)
+        if (nw) {  // RMSNorm of the row first (qwen3moe.cpp:527-532); the first F32_PF float4 of the norm
+                   // weights per thread were loaded before the wait
             const float sc = 1.0f / sqrtf(row_sumsq128(xr, K, red4) / (float)K + eps);
-            for (int i = threadIdx.x; i < K; i += F32_NT) nrow[i] = __fmul_rn(__fmul_rn(xr[i], sc), nw[i]);
+            const float4* x4 = reinterpret_cast<const float4*>(xr);
+            auto norm4 = [&](int i, const float4& g) {
+                const float4 v = x4[i];
+                reinterpret_cast<float4*>(nrow)[i] = make_float4(__fmul_rn(__fmul_rn(v.x, sc), g.x), __fmul_rn(__fmul_rn(v.y, sc), g.y),
+                                                                 __fmul_rn(__fmul_rn(v.z, sc), g.z), __fmul_rn(__fmul_rn(v.w, sc), g.w));
+            };
+#pragma unroll
+            for (int j = 0; j < F32_PF; j++)
+                if (threadIdx.x + j * F32_NT < n4) norm4(threadIdx.x + j * F32_NT, gpf[j]);
+            for (int i = threadIdx.x + F32_PF * F32_NT; i < n4; i += F32_NT) norm4(i, __ldg(g4 + i));
             __syncthreads();
             xr = nrow;
         }
