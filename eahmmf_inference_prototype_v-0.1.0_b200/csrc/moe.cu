@@ -453,6 +453,22 @@ __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_gr
 // kernels); with r.g_info the group list also stays in shared memory. TEAMS: a few tokens, each ranked
 // by a team of 128 threads (latency); otherwise one warp per token (route_token; throughput).
 // Requires blockDim.x >= E (one thread per expert in the scans).
+// 32 keys, one per lane, sorted descending across the warp (bitonic network); lane i returns the i-th
+// largest.
+__device__ __forceinline__ uint64_t warp_sort_desc(uint64_t key) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, key, j);
+            const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
+            key = (lower == desc) ? (key > o ? key : o) : (key < o ? key : o);
+        }
+    }
+    return key;
+}
+
 template <bool TEAMS, int GS = MU>
 __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     static_assert(GS >= MU && GS <= 32, "group size");
@@ -491,6 +507,57 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
                 atomicAdd(&r.cnt[my_e], 1);
                 atomicOr(&r.mask[my_e], 1ull << t);
             }
+        }
+    } else if (team < nteam && E <= 128 && K <= 8) {
+        // Sorting teams (E <= 128, k <= 8; the Qwen3 shapes): one team of 128 threads per token, one entry
+        // per thread. Key of entry e: (bits of r) << 32 | ~e, so that a larger key ranks first under
+        // (r desc, index asc) (r >= 0: its bits order as the floats do); NaN and absent entries key 0.
+        // Each warp sorts its 32 keys (bitonic, descending), the team's four top-8 lists are sorted once
+        // more by the team's first warp: its lanes 0..k-1 hold the top k in rank order.
+        float* wmax = r.scr + (size_t)team * 80;  // [4] warp maxima, a NaN flag, then 32 candidate keys
+        int* nan_flag = reinterpret_cast<int*>(wmax + 4);
+        uint64_t* cand = reinterpret_cast<uint64_t*>(wmax + 8);
+        const int wt = tt >> 5;  // warp within the team
+        auto team_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(1 + team) : "memory"); };
+        for (int t = team; t < T; t += nteam) {
+            const float l = tt < E ? __ldg(a.logits + (size_t)t * E + tt) : -INFINITY;
+            float mx = l;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) wmax[wt] = mx;
+            if (tt == 0) *nan_flag = 0;
+            team_sync();
+            mx = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+            const float rv = (float)exp((double)(l - mx));
+            const bool isnan_e = tt < E && rv != rv;
+            uint64_t key = tt < E && !isnan_e ? ((uint64_t)__float_as_uint(rv) << 32) | (uint32_t)~(uint32_t)tt : 0ull;
+            key = warp_sort_desc(key);
+            if (lane < 8) cand[wt * 8 + lane] = key;
+            if (__any_sync(0xffffffffu, isnan_e) && lane == 0) *nan_flag = 1;
+            team_sync();
+            if (wt == 0) {
+                key = warp_sort_desc(cand[lane]);
+                const float rk = __uint_as_float((uint32_t)(key >> 32));
+                float tot = 0.f;
+                for (int k = 0; k < K; k++) tot += __shfl_sync(0xffffffffu, rk, k);  // rank-order sum
+                if (lane < K) {
+                    int my_e = *nan_flag || key == 0ull ? -1 : (int)~(uint32_t)key;
+                    const float my_w = __fdiv_rn(rk, tot);
+                    if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+                        if (global) set_flag(a.status, ST_BAD_INDEX);
+                        my_e = 0;
+                    }
+                    r.s_ids[t * K + lane] = my_e;
+                    r.s_w[t * K + lane] = my_w;
+                    if (global) {
+                        a.rw.ids[(size_t)t * K + lane] = my_e;
+                        a.rw.wts[(size_t)t * K + lane] = my_w;
+                    }
+                    atomicAdd(&r.cnt[my_e], 1);
+                    atomicOr(&r.mask[my_e], 1ull << t);
+                }
+            }
+            team_sync();  // the scratch is reused by the team's next token
         }
     } else if (team < nteam) {
         // One token per group of spl teams: spl = nteam for a single token (the decode case), else 1.
