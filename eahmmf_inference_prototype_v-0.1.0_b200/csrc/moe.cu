@@ -469,11 +469,122 @@ __device__ __forceinline__ uint64_t warp_sort_desc(uint64_t key) {
     return key;
 }
 
+// The routing of one token (E <= 128, k <= 8) by the block's first four warps, and its work list: the
+// sorting-team ranking (see route_block), then the first warp sorts its k picks by expert id, so that
+// pick i is slot i, group i (one slot) and the token's i-th slot in expert order. With `global` the
+// routing (rank order), groups, slot maps, offsets and active list go to a.rw as route_block writes them.
+// All threads call it; the results in r (group list) are visible after the caller's __syncthreads.
+__device__ void route_one(const MoeArgs& a, RouteSm r, bool global) {
+    const int E = a.n_expert, K = a.n_used, tid = threadIdx.x, lane = tid & 31, wt = tid >> 5;
+    float* wmax = r.scr;  // [4] warp maxima, a NaN flag, 32 candidate keys, 4 mask words
+    int* nan_flag = reinterpret_cast<int*>(wmax + 4);
+    uint64_t* cand = reinterpret_cast<uint64_t*>(wmax + 8);
+    uint32_t* selm = reinterpret_cast<uint32_t*>(wmax + 8 + 64);
+    if (tid < 128) {
+        auto team_sync = []() { asm volatile("bar.sync 1, 128;" ::: "memory"); };
+        const float l = tid < E ? __ldg(a.logits + tid) : -INFINITY;
+        float mx = l;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) wmax[wt] = mx;
+        if (tid == 0) *nan_flag = 0;
+        if (tid < 4) selm[tid] = 0u;
+        team_sync();
+        mx = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+        const float rv = (float)exp((double)(l - mx));
+        const bool isnan_e = tid < E && rv != rv;
+        uint64_t key = tid < E && !isnan_e ? ((uint64_t)__float_as_uint(rv) << 32) | (uint32_t)~(uint32_t)tid : 0ull;
+        key = warp_sort_desc(key);
+        if (lane < 8) cand[wt * 8 + lane] = key;
+        if (__any_sync(0xffffffffu, isnan_e) && lane == 0) *nan_flag = 1;
+        team_sync();
+        if (wt == 0) {
+            key = warp_sort_desc(cand[lane]);
+            const float rk = __uint_as_float((uint32_t)(key >> 32));
+            float tot = 0.f;
+            for (int k = 0; k < K; k++) tot += __shfl_sync(0xffffffffu, rk, k);  // rank-order sum
+            int my_e = *nan_flag || key == 0ull ? -1 : (int)~(uint32_t)key;
+            const float my_w = __fdiv_rn(rk, tot);
+            if (lane < K) {
+                if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+                    if (global) set_flag(a.status, ST_BAD_INDEX);
+                    my_e = 0;
+                }
+                r.s_ids[lane] = my_e;
+                r.s_w[lane] = my_w;
+                if (global) {
+                    a.rw.ids[lane] = my_e;
+                    a.rw.wts[lane] = my_w;
+                }
+            }
+            // the k picks in ascending expert order (id + 1 in the high word, above the empty lanes' 0; the
+            // weight travels in the low word)
+            uint64_t k2 = lane < K ? ((uint64_t)(uint32_t)(my_e + 1) << 32) | __float_as_uint(my_w) : 0ull;
+            k2 = warp_sort_desc(k2);  // descending: pick i of the ascending order sits in lane K - 1 - i
+            const int i = K - 1 - lane;
+            if (lane < K) {
+                const int e = (int)(k2 >> 32) - 1;
+                const float w = __uint_as_float((uint32_t)k2);
+                const uint8_t* wg = r.tab ? r.tab[e] : a.gate[e];
+                const uint8_t* wu = r.tab ? r.tab[E + e] : a.up[e];
+                const uint8_t* wd = r.tab ? r.tab[2 * E + e] : a.down[e];
+                r.off[e] = i;
+                r.goff[e] = i;
+                atomicOr(&selm[e >> 5], 1u << (e & 31));
+                if (r.g_info) {
+                    r.g_info[4 * i] = e;
+                    r.g_info[4 * i + 1] = i;
+                    r.g_info[4 * i + 2] = 1;
+                    for (int k = 0; k < MU; k++) r.g_tok[MU * i + k] = 0;
+                    r.g_w[3 * i] = wg;
+                    r.g_w[3 * i + 1] = wu;
+                    r.g_w[3 * i + 2] = wd;
+                }
+                if (global) {
+                    GroupRec& g = a.rw.groups[i];
+                    g.w[0] = wg;
+                    g.w[1] = wu;
+                    g.w[2] = wd;
+                    g.e = e;
+                    g.s0 = i;
+                    g.mc = 1;
+                    for (int k = 0; k < MU; k++) g.tok[k] = 0;
+                    a.rw.slot_token[i] = 0;
+                    a.rw.slot_w[i] = w;
+                    a.rw.token_slots[i] = i;
+                    a.rw.active[1 + i] = e;
+                }
+            }
+            if (lane == 0) {
+                *r.G = K;
+                if (global) {
+                    a.rw.ngroups[0] = K;
+                    a.rw.active[0] = K;
+                    a.rw.offsets[E] = K;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (global)  // slot offsets: the picks below each expert id
+        for (int e = tid; e < E; e += blockDim.x) {
+            int c = __popc(selm[e >> 5] & ((1u << (e & 31)) - 1u));
+            for (int w = 0; w < (e >> 5); w++) c += __popc(selm[w]);
+            a.rw.offsets[e] = c;
+        }
+}
+
 template <bool TEAMS, int GS = MU>
 __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     static_assert(GS >= MU && GS <= 32, "group size");
     const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
+    if constexpr (TEAMS) {
+        if (T == 1 && E <= 128 && K <= 8) {  // one token (a decode step): no counts, scans or scatter
+            route_one(a, r, global);
+            return;
+        }
+    }
     for (int i = tid; i < E; i += blockDim.x) {
         r.cnt[i] = 0;
         r.mask[i] = 0ull;
