@@ -50,7 +50,9 @@ __host__ __device__ constexpr int xf_gs_bytes(int K) { return 16 + K / 8; }
 // Programmatic dependent launch. A kernel launched with launch_pdl may start while its predecessor on
 // the stream is still running; it must call pdl_wait() before touching anything the predecessor
 // writes (and every kernel of a chain calls it, so completion is transitive). pdl_trigger() lets the
-// successor launch early.
+// successor launch early; every kernel calls it right after its own pdl_wait(), so at most one kernel
+// waits ahead of the running one (successors launched further ahead would hold SM resources that the
+// running kernel's remaining blocks need).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

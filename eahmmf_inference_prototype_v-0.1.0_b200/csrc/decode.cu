@@ -69,8 +69,8 @@ __device__ float dq_elem(const uint8_t* row, int type, int i) {
 __global__ void k_embed(const uint8_t* __restrict__ W, int type, size_t row_bytes, int D, int n_rows,
                         const int* __restrict__ toks, int nb, float* __restrict__ x, int* status) {
     const int t = blockIdx.x;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     if (t >= nb) return;
     const int id = toks[t];
     if (id < 0 || id >= n_rows) {
@@ -87,8 +87,8 @@ __global__ void k_embed(const uint8_t* __restrict__ W, int type, size_t row_byte
 __global__ void __launch_bounds__(128) k_rmsnorm(const float* __restrict__ x, int ldx, const float* __restrict__ w,
                                                  float* __restrict__ out, int ldo, int n, float eps) {
     __shared__ float red4[4];
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const float* xr = x + (size_t)blockIdx.x * ldx;
     const float sc = 1.0f / sqrtf(row_sumsq128(xr, n, red4) / (float)n + eps);
     float* o = out + (size_t)blockIdx.x * ldo;
@@ -105,8 +105,8 @@ __global__ void __launch_bounds__(NP_NT) k_norm_prep(NormPrepArgs a) {
     __shared__ float red[33];
     __shared__ int s_sl[32];
     __shared__ float s_w[32];
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int t = a.t0 + blockIdx.x, n = a.n;
     float* xr = a.x + (size_t)t * a.ldx;
     combine_norm_row(xr, a.y, a.y ? a.token_slots + (size_t)t * a.K : nullptr, a.slot_w, a.K, a.w, a.eps, n, row,
@@ -121,8 +121,8 @@ __global__ void __launch_bounds__(NP_NT) k_norm_prep(NormPrepArgs a) {
 __global__ void k_rope_table(const DecodeState* st, const float* __restrict__ inv_freq, int half, int nb,
                              float2* __restrict__ cs) {
     const int t = blockIdx.x;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int p = st->pos + t;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
         const double ang = (double)p * (double)inv_freq[i];
@@ -164,8 +164,8 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
     constexpr int PER = HD / 32, HALF = HD / 2;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nh = n_head + 2 * n_kv, QD = n_head * HD, KD = n_kv * HD;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     if (gw >= nb * nh) return;
     const int t = gw / nh, h = gw - t * nh;
     const float* src = qkv + (size_t)t * (QD + 2 * KD) + (size_t)h * HD;
@@ -284,8 +284,8 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     const int h = blockIdx.x, y = blockIdx.y, t = blockIdx.z;
     const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = ATT_NT / 32;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
     const int nch = (np + ATT_CH - 1) / ATT_CH;
     auto stage_chunk = [&](int c) {  // K/V rows of chunk c -> shared memory (cp.async, 16 bytes each)
@@ -462,8 +462,8 @@ __global__ void __launch_bounds__(MP_NT) k_attn_merge_prep(const float* __restri
     constexpr int PER = HD / 32;
     extern __shared__ __align__(16) float mrow[];  // [n_head * HD]
     __shared__ float red[33];
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, QD = n_head * HD;
     for (int hq = warp; hq < n_head; hq += MP_NT / 32) {
         float v[PER];
@@ -490,8 +490,8 @@ __global__ void __launch_bounds__(ARGMAX_NT) k_argmax(const float* __restrict__ 
     __shared__ float sv[ARGMAX_NT / 32];
     __shared__ int si[ARGMAX_NT / 32];
     __shared__ bool last;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int i = blockIdx.x * ARGMAX_NT + threadIdx.x; i < n; i += gridDim.x * ARGMAX_NT) {

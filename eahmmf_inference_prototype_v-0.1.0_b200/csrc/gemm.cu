@@ -134,8 +134,8 @@ __device__ __forceinline__ size_t tile_off(int r, int k) {
 // Per expert: gate/up tiles (FF/64 of them, A rows 0..63 = gate rows 64 rt.., 64..127 = the same up rows,
 // D/64 stages), then down tiles (D/128, FF/64 stages).
 __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int rows_e = 2 * g.FF + g.D;  // gate, up, down rows of one expert
     const long long gw = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -183,8 +183,8 @@ __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
 // ---- 2. slot rows -> scale + f16 hi/lo, tile-major by (expert, slot tile); one warp per slot
 template <int MODE>
 __global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int slot = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (slot >= S) return;
     const int K = MODE == 0 ? g.D : g.FF;
@@ -278,8 +278,8 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    pdl_trigger();
     pdl_wait();  // routing, packed activations and weights come from the previous grids
+    pdl_trigger();
     const uint32_t tmem = s_tmem;
     auto fail = [&]() {
         if (g.status) atomicOr(g.status, ST_WAIT_TIMEOUT);

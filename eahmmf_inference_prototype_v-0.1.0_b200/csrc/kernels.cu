@@ -95,8 +95,8 @@ __device__ float weight_at(const uint8_t* row, int type, int k) {
 
 // One warp per row; lanes stride over K; up to MT tokens per launch.
 __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int warp = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= a.W.rows) return;
     const uint8_t* row = a.W.w + (size_t)warp * a.W.row_bytes;
@@ -129,8 +129,8 @@ __global__ void __launch_bounds__(PREP_NT) k_prep_x(const float* __restrict__ X,
                                                      float* __restrict__ sum, uint8_t* __restrict__ gs) {
     __shared__ float red[33];
     const int row = blockIdx.x;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     prep_row(X + (size_t)row * ldx, K, frag + (size_t)row * (K >> 5) * 12, sum + (size_t)row * ((K >> 4) + XF_SUM_PAD),
              gs + (size_t)row * xf_gs_bytes(K), red);
 }
@@ -287,7 +287,6 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
     uint8_t* slot = sm + pl.slot_off;
     const RowLayout L = layout_of(a.W.w, rb);
     const int r0 = 16 * (int)blockIdx.x, r1 = min(a.W.rows, r0 + 16);
-    pdl_trigger();
     if (tid == 0) {  // the weight rows do not depend on earlier grids: their copy starts before the wait
         mbar_init(&bar[0], 1);
         mbar_fence_init();
@@ -307,6 +306,7 @@ __global__ void __launch_bounds__(NTU) k_gemv(GemvXArgs a) {
         for (int i = tid; i < K / 4; i += NTU)
             reinterpret_cast<float4*>(nw_s)[i] = __ldg(reinterpret_cast<const float4*>(a.pnw) + i);
     pdl_wait();  // the activations (XF or their fp32 row) and, when accumulating, Y come from earlier grids
+    pdl_trigger();
     if (a.pro == GEMV_PRO_XF) {
         if (tid == 0) issue_xf(a.xf, [](int i) { return i; }, m, K, sfrag, ssum, &bar[0]);
     } else {  // the token's row in fragment form, formed here exactly as the norm / merge kernels form it
@@ -383,7 +383,6 @@ __global__ void __launch_bounds__(GX_NT, 1) k_gemm_xf(GemvXArgs a) {
     float* scr = reinterpret_cast<float*>(sm + 128 + slot_bytes(row_layout(rb, true), 16)) + (size_t)warp * GX_SCR;
     const RowLayout L = layout_of(a.W.w, rb);
     const int r0 = 16 * (int)blockIdx.x, r1 = min(a.W.rows, r0 + 16);
-    pdl_trigger();
     if (tid == 0) {  // the weight rows do not depend on earlier grids: their copy starts before the wait
         mbar_init(&bar[0], 1);
         mbar_fence_init();
@@ -391,6 +390,7 @@ __global__ void __launch_bounds__(GX_NT, 1) k_gemm_xf(GemvXArgs a) {
         issue_rows(L, a.W.w, rb, r0, r1, slot, &bar[0]);
     }
     pdl_wait();  // the activations (XF) and, when accumulating, Y come from earlier grids
+    pdl_trigger();
     __syncthreads();
     if (__syncthreads_or(!mbar_wait_bounded(&bar[0], 0u))) {
         if (tid == 0) {
@@ -573,8 +573,8 @@ __global__ void __launch_bounds__(F32_NT) k_gemv_f32(const float* __restrict__ W
         wpf[j] = row < rows && i < n4 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         gpf[j] = nw && i < n4 ? __ldg(g4 + i) : make_float4(1.f, 1.f, 1.f, 1.f);  // prep blocks too
     }
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     if (row >= rows) {  // blocks past the matrix: token (row - rows) in fragment form for the expert kernels
         __shared__ float pred[33];
         const int t = row - rows;

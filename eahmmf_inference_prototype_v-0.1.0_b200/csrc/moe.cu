@@ -887,8 +887,8 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
 }
 
 __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
-    pdl_trigger();  // the gate/up grid may launch now; it waits for this grid's results
     pdl_wait();     // logits and activations come from the previous grids
+    pdl_trigger();
     if (blockIdx.x > 0) {  // activation prep of token blockIdx.x - 1
         __shared__ float red[33];
         const int row = blockIdx.x - 1;
@@ -933,8 +933,8 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         for (int i = tid; i < 3 * E; i += blockDim.x) rt.tab[i] = i < E ? a.gate[i] : i < 2 * E ? a.up[i - E] : a.down[i - 2 * E];
     }
     __syncthreads();
-    pdl_trigger();
     pdl_wait();  // routing results (or the logits) and the XF of the tokens come from the previous grids
+    pdl_trigger();
     // small batches: every CTA routes the tokens itself into shared memory (CTA 0 also publishes the
     // routing, groups and slot maps for the down kernel and the combine)
     if constexpr (G == MU) {
@@ -1142,8 +1142,8 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup_fs(MoeArgs 
         for (int i = tid; i < 3 * E; i += blockDim.x) rt.tab[i] = i < E ? a.gate[i] : i < 2 * E ? a.up[i - E] : a.down[i - 2 * E];
     }
     __syncthreads();
-    pdl_trigger();
     pdl_wait();  // the logits and the tokens' XF come from the previous grid
+    pdl_trigger();
     const uint32_t xfg = (uint32_t)xf_gs_bytes(D);
     if (tid == 0) {  // all T tokens' XF rows: fragments and group sums, one bulk copy each
         mbar_expect_tx(xfbar, (uint32_t)T * ((uint32_t)D * 3 + xfg));
@@ -1311,8 +1311,8 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         mbar_fence_init();
     }
     __syncthreads();
-    pdl_trigger();
     pdl_wait();  // h and the routing come from the previous grids
+    pdl_trigger();
     // small batches: the whole group list (at most T*K records) is read into shared memory in the same
     // round trip as its length
     GroupRec* gcache = G == MU && a.fused_route ? reinterpret_cast<GroupRec*>(sm + pl.extra_off) : nullptr;
@@ -1521,8 +1521,8 @@ __global__ void __launch_bounds__(COMB_NT) k_moe_combine(MoeArgs a) {
 constexpr int BIG_NT = 256;
 __global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict__ cnt, int* __restrict__ local) {
     __shared__ uint32_t s_rk[(BIG_NT / 32) * 64];
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * (BIG_NT / 32) + warp, E = a.n_expert, K = a.n_used;
     if (t >= a.T) return;  // whole warps
@@ -1547,8 +1547,8 @@ __global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict
 __global__ void __launch_bounds__(512) k_plan_big(MoeArgs a, const int* __restrict__ cnt, int* __restrict__ tiles_gu,
                                                   int* __restrict__ tiles_dn) {
     __shared__ int ws[3][16];
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int E = a.n_expert, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int c = tid < E ? cnt[tid] : 0;
     const int nt = (c + 127) / 128;
@@ -1590,8 +1590,8 @@ __global__ void __launch_bounds__(512) k_plan_big(MoeArgs a, const int* __restri
 // One thread per (token, k): slot = offset[e] + its count index; the token's slots by expert order.
 // (cnt / local may be null for routing alone.)
 __global__ void __launch_bounds__(256) k_scatter_big(MoeArgs a, const int* __restrict__ local) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int i = blockIdx.x * 256 + threadIdx.x, K = a.n_used;
     if (i >= a.T * K) return;
     const int t = i / K;
