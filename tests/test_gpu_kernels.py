@@ -41,7 +41,9 @@ def make_matrix(qtype, K, rows, seed):
 
 
 GEMV_CASES = [(12, 2048, 768), (12, 4096, 512), (12, 256, 8), (13, 2048, 300), (13, 256, 256), (14, 768, 2048),
-              (14, 2048, 1001), (14, 256, 256), (14, 1536, 64), (8, 512, 300), (8, 256, 33), (0, 2048, 128)]
+              (14, 2048, 1001), (14, 256, 256), (14, 1536, 64), (8, 512, 300), (8, 256, 33), (0, 2048, 128),
+              # output-projection-sized row counts (thousands of tiles, ragged last tile)
+              (14, 2048, 9600), (12, 512, 9999)]
 
 
 @pytest.mark.parametrize("qtype,K,rows", GEMV_CASES)
