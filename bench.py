@@ -674,6 +674,22 @@ def profile_decode(n_layer: int) -> int:
     return 0
 
 
+def profile_prefill(n_layer: int) -> int:
+    """No timing: a config-4-shape model with n_layer layers, one 512-token prompt through eval in
+    passes of 64 (the prompt half of the e2e step). The case the prefill launch list is taken on."""
+    import synth
+    cfg = synth.config4_30b(n_layer=n_layer)
+    path = synth.cached_gguf(cfg, workers=max(1, min(48, (os.cpu_count() or 2) - 1)))
+    import eahmmf_b200 as eb
+    eng = eb.Engine(path, 1024)
+    rc, lg = eng.eval(decode_prompt(0, 512), 0, 64)
+    eng.close()
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_eval returned {rc}")
+    print(json.dumps({"profile_prefill": n_layer, "argmax": int(np.argmax(lg)), "ok": True}))
+    return 0
+
+
 def profile_case(T: int) -> int:
     """Three calls of the config-2 MoE layer at T tokens on fixed seeded inputs, nothing timed: the
     small case ncu captures are taken on (a few hundred MB on the device)."""
@@ -709,7 +725,11 @@ def main():
                     help="no timing: three grouped-path layer calls on T ragged tokens (a small case for ncu)")
     ap.add_argument("--profile-decode", type=int, metavar="LAYERS", default=0,
                     help="no timing: 8-token prompt + 4 greedy tokens on a config-4-shape model of LAYERS layers")
+    ap.add_argument("--profile-prefill", type=int, metavar="LAYERS", default=0,
+                    help="no timing: one 512-token prompt in passes of 64 on a config-4-shape model of LAYERS layers")
     args = ap.parse_args()
+    if args.profile_prefill:
+        return profile_prefill(args.profile_prefill)
     if args.profile_case:
         return profile_case(args.profile_case)
     if args.profile_decode:

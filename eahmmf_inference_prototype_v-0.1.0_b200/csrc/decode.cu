@@ -189,10 +189,13 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
 // ---- causal GQA attention (qwen3moe.cpp:976-1001), split over the context
 // Block (kv head h, split y, token t) runs the GRP q heads sharing kv head h over context chunks
 // y, y + nsplit, ... of ATT_CH positions with an online softmax and writes one partial (max, sum,
-// unnormalised output) per q head. K/V chunks are staged in shared memory with cp.async (every thread's
-// 16-byte copies in flight at once), rows padded by 4 floats for conflict-free row-parallel score reads.
-// k_attn_merge_prep merges the splits of every head of a token row and puts the row in fragment form
-// for the o-projection.
+// unnormalised output) per q head; splits y >= ceil(np / ATT_CH) hold no positions of the token and write
+// nothing. K/V chunks are staged in shared memory with cp.async (every thread's 16-byte copies in flight
+// at once), rows padded by 4 floats for conflict-free row-parallel score reads. k_attn_merge_prep merges
+// the splits of every head of a token row and puts the row in fragment form for the o-projection. The
+// merges read the min(nsplit, ceil(np / ATT_CH)) records that exist: a split without positions would
+// add exact zeros (weight 0, sum 0) and leave the maximum unchanged, so the merged row is the same as
+// a merge over all nsplit records.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
@@ -288,6 +291,9 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     pdl_trigger();
     const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
     const int nch = (np + ATT_CH - 1) / ATT_CH;
+    // splits y >= nch hold no positions of this token: no record (the merges read the first
+    // min(nsplit, nch) records only); a single-token step still counts the block for its merge
+    if (y >= nch && !rf.cnt) return;
     auto stage_chunk = [&](int c) {  // K/V rows of chunk c -> shared memory (cp.async, 16 bytes each)
         const int p0 = c * ATT_CH, n = min(ATT_CH, np - p0);
         for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
@@ -298,7 +304,8 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
         }
     };
     if (y < nch) stage_chunk(y);  // the first chunk's copies fly while the q heads are prepared
-    if (rf.qkv) {  // single-token step: the group's q heads normalised and rotated here, from the q|k|v row
+    if (y >= nch) {
+    } else if (rf.qkv) {  // single-token step: the group's q heads normalised and rotated here, from the q|k|v row
         for (int hq = warp; hq < grp; hq += nwarp) {
             const float* src = rf.qkv + (size_t)(h * grp + hq) * HD;
             float v[PER];
@@ -425,7 +432,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
 #pragma unroll
     for (int k = 0; k < ATT_MAXH; k++) {
         const int hq = warp + k * nwarp;
-        if (hq >= grp) break;
+        if (hq >= grp || y >= nch) break;
         float* pr = part + (((size_t)t * n_head + (size_t)h * grp + hq) * nsplit + y) * (HD + 2);
         if (lane == 0) {
             pr[0] = m_run[k];
@@ -444,7 +451,8 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
         __threadfence();
         for (int hq = warp; hq < grp; hq += nwarp) {
             float v[PER];
-            merge_head<HD, true, true>(part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2), nsplit, v);
+            merge_head<HD, true, true>(part + ((size_t)t * n_head + (size_t)h * grp + hq) * nsplit * (HD + 2),
+                                       min(nsplit, nch), v);
 #pragma unroll
             for (int j = 0; j < PER; j++) rf.att[(size_t)t * QD + (size_t)(h * grp + hq) * HD + lane + 32 * j] = v[j];
         }
@@ -458,16 +466,17 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
 constexpr int MP_NT = 1024;
 template <int HD>
 __global__ void __launch_bounds__(MP_NT) k_attn_merge_prep(const float* __restrict__ part, int n_head, int nsplit,
-                                                           float* __restrict__ att, XF xf) {
+                                                           const DecodeState* st, float* __restrict__ att, XF xf) {
     constexpr int PER = HD / 32;
     extern __shared__ __align__(16) float mrow[];  // [n_head * HD]
     __shared__ float red[33];
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, QD = n_head * HD;
+    const int nvalid = min(nsplit, (st->pos + t + ATT_CH) / ATT_CH);  // splits holding positions 0 .. pos + t
     for (int hq = warp; hq < n_head; hq += MP_NT / 32) {
         float v[PER];
-        merge_head<HD, false, false>(part + ((size_t)t * n_head + hq) * nsplit * (HD + 2), nsplit, v);
+        merge_head<HD, false, false>(part + ((size_t)t * n_head + hq) * nsplit * (HD + 2), nvalid, v);
 #pragma unroll
         for (int j = 0; j < PER; j++) {
             mrow[hq * HD + lane + 32 * j] = v[j];
@@ -624,7 +633,7 @@ static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int
         if (e != cudaSuccess) return e;
         mcur = msmem;
     }
-    return launch_pdl(k_attn_merge_prep<HD>, dim3(nb), dim3(MP_NT), msmem, s, part, n_head, nsplit, att, xf);
+    return launch_pdl(k_attn_merge_prep<HD>, dim3(nb), dim3(MP_NT), msmem, s, part, n_head, nsplit, st, att, xf);
 }
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                              const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,

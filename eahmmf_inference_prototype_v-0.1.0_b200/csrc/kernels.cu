@@ -665,10 +665,66 @@ cudaError_t launch_router_prep(const float* W, int K, int rows, const float* X, 
                       Y, ldy, xf, 1, norm_w, eps);
 }
 
+// F32 rows over more than MT tokens (the router of a prompt pass): one block per (F32_TR rows, F32_TT
+// tokens), so that every weight and token float4 read from L2 serves F32_TT (F32_TR) products instead
+// of one row's MT tokens. Each (row, token) sum is formed exactly as k_gemv_f32 forms it: thread i owns
+// the float4 groups i, i + F32_NT, ... in order with the same fmaf nesting, then the same warp
+// butterfly and the same fixed-order sum of the four warps' partials, so the logits are bitwise those
+// of the small-batch kernel.
+constexpr int F32_TR = 4, F32_TT = 8;
+__global__ void __launch_bounds__(F32_NT) k_gemv_f32_tile(const float* __restrict__ W, int K, int rows,
+                                                          const float* __restrict__ X, int ldx, int m_all,
+                                                          float* __restrict__ Y, int ldy) {
+    __shared__ float red[F32_NT / 32][F32_TR][F32_TT];
+    const int r0 = blockIdx.x * F32_TR, t0 = blockIdx.y * F32_TT, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nr = min(F32_TR, rows - r0), m = min(F32_TT, m_all - t0), n4 = K / 4;
+    const float4* w4 = reinterpret_cast<const float4*>(W) + (size_t)r0 * n4;
+    const float4* x4 = reinterpret_cast<const float4*>(X + (size_t)t0 * ldx);
+    const int ld4 = ldx / 4;
+    pdl_wait();
+    pdl_trigger();
+    float acc[F32_TR][F32_TT];
+#pragma unroll
+    for (int r = 0; r < F32_TR; r++)
+#pragma unroll
+        for (int t = 0; t < F32_TT; t++) acc[r][t] = 0.f;
+#pragma unroll 2
+    for (int i = threadIdx.x; i < n4; i += F32_NT) {
+        float4 w[F32_TR], x[F32_TT];
+#pragma unroll
+        for (int r = 0; r < F32_TR; r++) w[r] = r < nr ? __ldg(w4 + (size_t)r * n4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int t = 0; t < F32_TT; t++) x[t] = t < m ? __ldg(x4 + (size_t)t * ld4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < F32_TR; r++)
+#pragma unroll
+            for (int t = 0; t < F32_TT; t++)
+                acc[r][t] = fmaf(w[r].x, x[t].x, fmaf(w[r].y, x[t].y, fmaf(w[r].z, x[t].z, fmaf(w[r].w, x[t].w, acc[r][t]))));
+    }
+#pragma unroll
+    for (int r = 0; r < F32_TR; r++)
+#pragma unroll
+        for (int t = 0; t < F32_TT; t++) {
+            float v = acc[r][t];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red[warp][r][t] = v;
+        }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < F32_TR * F32_TT; idx += F32_NT) {
+        const int r = idx / F32_TT, t = idx - r * F32_TT;
+        if (r < nr && t < m)
+            Y[(size_t)(t0 + t) * ldy + r0 + r] = (red[0][r][t] + red[1][r][t]) + (red[2][r][t] + red[3][r][t]);
+    }
+}
+
 cudaError_t launch_f32_gemv(const float* W, int K, int rows, const float* X, int ldx, int m, float* Y, int ldy,
                             cudaStream_t st) {
     const bool vec = K % 4 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+    if (vec && m > MT)
+        return launch_pdl(k_gemv_f32_tile, dim3((rows + F32_TR - 1) / F32_TR, (m + F32_TT - 1) / F32_TT), dim3(F32_NT), 0,
+                          st, W, K, rows, X, ldx, m, Y, ldy);
     if (vec)
         return launch_pdl(k_gemv_f32, dim3(rows, (m + MT - 1) / MT), dim3(F32_NT), 0, st, W, K, rows, X, ldx, m, Y,
                           ldy, XF{}, 0, static_cast<const float*>(nullptr), 0.f);

@@ -163,6 +163,25 @@ def test_moe_layer_mixed_types_router_matrix(torch_cuda, golden):
     assert rel_l2(y - x, g["y"] - x) < 1e-5
 
 
+def test_moe_layer_router_matrix_independent_of_batching(torch_cuda):
+    """The router matrix over 40 tokens in one call (the tiled f32 GEMV of prompt passes, then k_moe_route)
+    against the same tokens in calls of 1 and of 8 (the small-batch router with fused routing): ids and
+    routing weights bitwise equal, so the logits are too; layer outputs within 1e-6."""
+    torch = torch_cuda
+    mx = synth.expert_set(D=512, FF=256, n_expert=16, types=(12, 13, 14), seed=9, d_sigma=0.002)
+    rw = synth._rng(23).normal(0, 0.3, (16, 512)).astype(np.float32)
+    layer = eb.MoeLayer.from_expert_set(mx, n_used=4, router=torch.from_numpy(rw).cuda())
+    x = synth.activations(40, 512, seed=31)
+    xn = synth.activations(40, 512, seed=32)
+    y, ids, w = run_layer(torch, layer, x, xn, None)
+    for step in (1, 8):
+        for t0 in range(0, 40, step):
+            yb, ib, wb = run_layer(torch, layer, x[t0:t0 + step], xn[t0:t0 + step], None)
+            np.testing.assert_array_equal(ib, ids[t0:t0 + step])
+            np.testing.assert_array_equal(wb, w[t0:t0 + step])
+            assert rel_l2(yb - x[t0:t0 + step], y[t0:t0 + step] - x[t0:t0 + step]) < 1e-6
+
+
 def test_moe_routing_ties_and_many_tokens(torch_cuda, orc, experts_c2, layer_c2):
     """Bit-exact expert ids over many tokens, including exact logit ties (lower index wins)."""
     T = 256
