@@ -176,4 +176,141 @@ __device__ __forceinline__ void sb_q6(const uint8_t* __restrict__ r0, const uint
     out[3] = fmaf(d1, (float)acc[3], out[3]);
 }
 
+// ---- several column sets over one decoded super-block (the grouped kernels' larger groups) ----------
+// sb_q45m / sb_q6m: the weights of the super-block are decoded once and every set s runs the MMAs,
+// group-scale sums, d-scaling and minimum term of sb_q45 / sb_q6 on its own operands bq[s] (mq[s]),
+// with the same integer and fp32 operations in the same order: out[s] and mn[s] are bitwise what the
+// single-set function leaves for that set.
+template <int QT, int NS>
+__device__ __forceinline__ void sb_q45m(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
+                                        const uint8_t* const (&bq)[NS], const uint8_t* const (&mq)[NS], int t,
+                                        float (&out)[NS][4], float (&mn)[NS][2]) {
+    constexpr int QS = QT == T_Q4_K ? 16 : 48;
+    const uint4 H0 = *reinterpret_cast<const uint4*>(r0), H1 = *reinterpret_cast<const uint4*>(r1);
+    const uint32_t sA0 = H0.y & 0x3f3f3f3fu, sB0 = (H0.w & 0x0f0f0f0fu) | ((H0.y >> 2) & 0x30303030u);
+    const uint32_t sA1 = H1.y & 0x3f3f3f3fu, sB1 = (H1.w & 0x0f0f0f0fu) | ((H1.y >> 2) & 0x30303030u);
+    constexpr int LSH = QT == T_Q4_K ? 4 : 0;
+    const uint32_t le0[2] = {(sA0 & 0x00ff00ffu) << LSH, (sB0 & 0x00ff00ffu) << LSH};
+    const uint32_t le1[2] = {(sA1 & 0x00ff00ffu) << LSH, (sB1 & 0x00ff00ffu) << LSH};
+    const uint32_t ho0[2] = {(sA0 >> 8) & 0x00ff00ffu, (sB0 >> 8) & 0x00ff00ffu};
+    const uint32_t ho1[2] = {(sA1 >> 8) & 0x00ff00ffu, (sB1 >> 8) & 0x00ff00ffu};
+    uint2 qh0{0u, 0u}, qh1{0u, 0u};
+    if constexpr (QT == T_Q5_K) {
+        qh0 = *reinterpret_cast<const uint2*>(r0 + 16 + 8 * t);
+        qh1 = *reinterpret_cast<const uint2*>(r1 + 16 + 8 * t);
+    }
+    const uint8_t* q0 = r0 + QS + 8 * t;
+    const uint8_t* q1 = r1 + QS + 8 * t;
+    int acc[NS][4];
+#pragma unroll
+    for (int s = 0; s < NS; s++) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint2 w0 = *reinterpret_cast<const uint2*>(q0 + 32 * c), w1 = *reinterpret_cast<const uint2*>(q1 + 32 * c);
+        uint2 bl[NS], bh[NS];
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            bl[s] = *reinterpret_cast<const uint2*>(bq[s] + 96 * (2 * c));
+            bh[s] = *reinterpret_cast<const uint2*>(bq[s] + 96 * (2 * c + 1));
+        }
+        uint32_t lo[4], hi[4];
+        if constexpr (QT == T_Q4_K) {
+            lo[0] = w0.x & 0x0f0f0f0fu;
+            lo[1] = w1.x & 0x0f0f0f0fu;
+            lo[2] = w0.y & 0x0f0f0f0fu;
+            lo[3] = w1.y & 0x0f0f0f0fu;
+            hi[0] = w0.x & 0xf0f0f0f0u;
+            hi[1] = w1.x & 0xf0f0f0f0u;
+            hi[2] = w0.y & 0xf0f0f0f0u;
+            hi[3] = w1.y & 0xf0f0f0f0u;
+        } else {
+            lo[0] = (w0.x & 0x0f0f0f0fu) | (((qh0.x >> (2 * c)) & 0x01010101u) << 4);
+            lo[1] = (w1.x & 0x0f0f0f0fu) | (((qh1.x >> (2 * c)) & 0x01010101u) << 4);
+            lo[2] = (w0.y & 0x0f0f0f0fu) | (((qh0.y >> (2 * c)) & 0x01010101u) << 4);
+            lo[3] = (w1.y & 0x0f0f0f0fu) | (((qh1.y >> (2 * c)) & 0x01010101u) << 4);
+            hi[0] = ((w0.x >> 4) & 0x0f0f0f0fu) | (((qh0.x >> (2 * c + 1)) & 0x01010101u) << 4);
+            hi[1] = ((w1.x >> 4) & 0x0f0f0f0fu) | (((qh1.x >> (2 * c + 1)) & 0x01010101u) << 4);
+            hi[2] = ((w0.y >> 4) & 0x0f0f0f0fu) | (((qh0.y >> (2 * c + 1)) & 0x01010101u) << 4);
+            hi[3] = ((w1.y >> 4) & 0x0f0f0f0fu) | (((qh1.y >> (2 * c + 1)) & 0x01010101u) << 4);
+        }
+        const int f = c & 1, wd = c >> 1;
+        const int sl0 = f ? (int)(le0[wd] >> 16) : (int)(le0[wd] & 0xffffu);
+        const int sl1 = f ? (int)(le1[wd] >> 16) : (int)(le1[wd] & 0xffffu);
+        const int sh0 = f ? (int)(ho0[wd] >> 16) : (int)(ho0[wd] & 0xffffu);
+        const int sh1 = f ? (int)(ho1[wd] >> 16) : (int)(ho1[wd] & 0xffffu);
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            scale_acc(acc[s], imma32(lo[0], lo[1], lo[2], lo[3], bl[s].x, bl[s].y), sl0, sl1);
+            scale_acc(acc[s], imma32(hi[0], hi[1], hi[2], hi[3], bh[s].x, bh[s].y), sh0, sh1);
+        }
+    }
+    constexpr float DS = QT == T_Q4_K ? 0.0625f : 1.0f;
+    const float d0 = f16_to_f32(H0.x & 0xffffu) * DS, d1 = f16_to_f32(H1.x & 0xffffu) * DS;
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        out[s][0] = fmaf(d0, (float)acc[s][0], out[s][0]);
+        out[s][1] = fmaf(d0, (float)acc[s][1], out[s][1]);
+        out[s][2] = fmaf(d1, (float)acc[s][2], out[s][2]);
+        out[s][3] = fmaf(d1, (float)acc[s][3], out[s][3]);
+    }
+    const uint32_t mA0 = H0.z & 0x3f3f3f3fu, mB0 = ((H0.w >> 4) & 0x0f0f0f0fu) | ((H0.z >> 2) & 0x30303030u);
+    const uint32_t mA1 = H1.z & 0x3f3f3f3fu, mB1 = ((H1.w >> 4) & 0x0f0f0f0fu) | ((H1.z >> 2) & 0x30303030u);
+    const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
+    const uint32_t ma0 = u8pair_f16(t < 2 ? mA0 : mB0, sel), ma1 = u8pair_f16(t < 2 ? mA1 : mB1, sel);
+    const float dm0 = f16_to_f32(H0.x >> 16), dm1 = f16_to_f32(H1.x >> 16);
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        float cm[4];
+        hmma8(cm, ma0, ma1, *reinterpret_cast<const uint32_t*>(mq[s]));
+        mn[s][0] = fmaf(dm0, cm[0] + cm[1], mn[s][0]);
+        mn[s][1] = fmaf(dm1, cm[2] + cm[3], mn[s][1]);
+    }
+}
+
+template <bool M0, bool M1, int NS>
+__device__ __forceinline__ void sb_q6m(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
+                                       const uint8_t* const (&bq)[NS], int t, float (&out)[NS][4]) {
+    const uint8_t* p0 = r0 + 4 * t;
+    const uint8_t* p1 = r1 + 4 * t;
+    int acc[NS][4];
+#pragma unroll
+    for (int s = 0; s < NS; s++) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint32_t sc0[2] = {ld32m<M0>(r0 + 192 + 8 * h), ld32m<M0>(r0 + 196 + 8 * h)};
+        const uint32_t sc1[2] = {ld32m<M1>(r1 + 192 + 8 * h), ld32m<M1>(r1 + 196 + 8 * h)};
+#pragma unroll
+        for (int ib = 0; ib < 2; ib++) {
+            const int o = 64 * h + 16 * ib;
+            const uint32_t qa0 = ld32m<M0>(p0 + o), qb0 = ld32m<M0>(p0 + o + 32), qh0 = ld32m<M0>(p0 + 128 + 32 * h + 16 * ib);
+            const uint32_t qa1 = ld32m<M1>(p1 + o), qb1 = ld32m<M1>(p1 + o + 32), qh1 = ld32m<M1>(p1 + 128 + 32 * h + 16 * ib);
+            const uint32_t v0[4] = {lop_sel(qa0, qh0 << 4, 0x0f0f0f0fu), lop_sel(qb0, qh0 << 2, 0x0f0f0f0fu),
+                                    lop_sel(qa0 >> 4, qh0, 0x0f0f0f0fu), lop_sel(qb0 >> 4, qh0 >> 2, 0x0f0f0f0fu)};
+            const uint32_t v1[4] = {lop_sel(qa1, qh1 << 4, 0x0f0f0f0fu), lop_sel(qb1, qh1 << 2, 0x0f0f0f0fu),
+                                    lop_sel(qa1 >> 4, qh1, 0x0f0f0f0fu), lop_sel(qb1 >> 4, qh1 >> 2, 0x0f0f0f0fu)};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t a0 = ((v0[q] & 0x3f3f3f3fu) + 0x60606060u) ^ 0x80808080u;
+                const uint32_t a1 = ((v1[q] & 0x3f3f3f3fu) + 0x60606060u) ^ 0x80808080u;
+                const int gl = 2 * q + ib;
+                const int sa = sbyte(sc0[gl >> 2], gl & 3), sbb = sbyte(sc1[gl >> 2], gl & 3);
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const uint32_t b = *reinterpret_cast<const uint32_t*>(bq[s] + 96 * (4 * h + q) + 16 * ib);
+                    scale_acc(acc[s], imma16s(a0, a1, b), sa, sbb);
+                }
+            }
+        }
+    }
+    const float d0 = f16_to_f32(*reinterpret_cast<const uint16_t*>(r0 + 208));
+    const float d1 = f16_to_f32(*reinterpret_cast<const uint16_t*>(r1 + 208));
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        out[s][0] = fmaf(d0, (float)acc[s][0], out[s][0]);
+        out[s][1] = fmaf(d0, (float)acc[s][1], out[s][1]);
+        out[s][2] = fmaf(d1, (float)acc[s][2], out[s][2]);
+        out[s][3] = fmaf(d1, (float)acc[s][3], out[s][3]);
+    }
+}
+
 }  // namespace eb

@@ -230,6 +230,40 @@ __device__ __forceinline__ void block_tasks(const RowsAny& rows, int nsb, int sb
         }
     }
 }
+// block_tasks over NS column sets at once (sets of a larger group): each super-block's weights are
+// decoded once for all sets; per set the sums are bitwise block_tasks' (ksb.cuh: sb_q45m, sb_q6m).
+// bq[s]: set s's B-fragment base (BPtr<1>::p[0]); mq[s]: its minimum-term operand (Q4_K/Q5_K).
+template <int QT, int NS>
+__device__ __forceinline__ void block_tasks_m(const RowsAny& rows, int nsb, int sb0, int step,
+                                              const uint8_t* const (&bq)[NS], const uint8_t* const (&mq)[NS],
+                                              float (&acc)[NS][4], float (&mn)[NS][2]) {
+    const int t = threadIdx.x & 3;
+    for (int sb = sb0; sb < nsb; sb += step) {
+        const uint8_t* r0 = rows.r[0] + (size_t)sb * block_bytes(QT);
+        const uint8_t* r1 = rows.r[1] + (size_t)sb * block_bytes(QT);
+        const uint8_t* b[NS];
+        if constexpr (QT == T_Q6_K) {
+#pragma unroll
+            for (int k = 0; k < NS; k++) b[k] = bq[k] + 4 * t + 768 * sb;
+            const bool m0 = (smem_u32(r0) & 2u) != 0, m1 = (smem_u32(r1) & 2u) != 0;  // warp-uniform
+            if (m0) {
+                if (m1) sb_q6m<true, true, NS>(r0, r1, b, t, acc);
+                else sb_q6m<true, false, NS>(r0, r1, b, t, acc);
+            } else {
+                if (m1) sb_q6m<false, true, NS>(r0, r1, b, t, acc);
+                else sb_q6m<false, false, NS>(r0, r1, b, t, acc);
+            }
+        } else {
+            const uint8_t* m[NS];
+#pragma unroll
+            for (int k = 0; k < NS; k++) {
+                b[k] = bq[k] + 8 * t + 768 * sb;
+                m[k] = mq[k] + 32 * sb;
+            }
+            sb_q45m<QT, NS>(r0, r1, b, m, t, acc, mn);
+        }
+    }
+}
 // The lane's B operand base of the minimum-term MMA (ksb.cuh) in a staging buffer's gs rows: token g/2
 // for g < 4 (token 0 beyond the group's slots or for g >= 4: those columns are never read), f16 high
 // parts for even g, residues for odd g.
@@ -1045,9 +1079,30 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
         const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
         float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_GU + warp) * 16 * G;
         const uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
-        for (int st = 0; 2 * st < mc; st++) {  // column sets: slots 2 st, 2 st + 1 of the group
+        for (int st = 0; 2 * st < mc;) {  // column sets: slots 2 st, 2 st + 1 of the group
             const int ms = mc - 2 * st;
             const uint8_t* xg = xs + xs_gs_off(D, G) + (size_t)(2 * st) * xf_gs_bytes(D);
+            if (G > MU && ms > 2) {  // sets st, st + 1 over one decode of the weights
+                const uint8_t* xg1 = xg + 2 * (size_t)xf_gs_bytes(D);
+                float acc[2][4] = {}, mn[2][2] = {};
+                if (in.y & 256) {
+                    const uint8_t* bq[2] = {BPtr<1>(xs + (size_t)(2 * st) * D * 3, D >> 5, ms).p[0],
+                                            BPtr<1>(xs + (size_t)(2 * st + 2) * D * 3, D >> 5, ms - 2).p[0]};
+                    const uint8_t* mq[2] = {min_operand(xg, D, ms), min_operand(xg1, D, ms - 2)};
+                    if (mtx == 0)
+                        block_tasks_m<QG, 2>(rows_gu(stage, rbg, in.w & 255), nsb, wsub, 8, bq, mq, acc, mn);
+                    else
+                        block_tasks_m<QU, 2>(rows_gu(stage + up_at, rbu, (in.w >> 8) & 255), nsb, wsub, 8, bq, mq, acc, mn);
+                }
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const float a1[1][4] = {{acc[k][0], acc[k][1], acc[k][2], acc[k][3]}};
+                    const float ts = t < ms - 2 * k ? *reinterpret_cast<const float*>(xg + (size_t)(2 * k + t) * xf_gs_bytes(D)) : 0.f;
+                    warp_values(a1, mn[k], ts, part, prow0, prow1, G, 2 * st + 2 * k);
+                }
+                st += 2;
+                continue;
+            }
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
             if (in.y & 256) {
                 const BPtr<1> bp(xs + (size_t)(2 * st) * D * 3, D >> 5, ms);
@@ -1059,6 +1114,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
             }
             const float ts = t < ms ? *reinterpret_cast<const float*>(xg + (size_t)t * xf_gs_bytes(D)) : 0.f;
             warp_values(acc, mn, ts, part, prow0, prow1, G, 2 * st);
+            st++;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&done[s]);
@@ -1443,18 +1499,37 @@ __global__ void __launch_bounds__((NWC_DN + 1) * 32, 1) k_moe_down(MoeArgs a) {
         if ((in.y & 512) && u != u0 && !prep_group(xb, s0, mc)) return;  // a later group's first unit here
         const uint8_t* xs = sm + pl.xf_off + (size_t)xb * pl.xfb;
         float* part = reinterpret_cast<float*>(sm + pl.part_off) + ((size_t)s * NWC_DN + warp) * 16 * G;
-        for (int st = 0; 2 * st < mc; st++) {  // column sets: slots 2 st, 2 st + 1 of the group
+        for (int st = 0; 2 * st < mc;) {  // column sets: slots 2 st, 2 st + 1 of the group
             const int ms = mc - 2 * st;
             const uint8_t* xg = xs + xs_gs_off(FF, G) + (size_t)(2 * st) * xf_gs_bytes(FF);
+            const RowsAny rows =
+                rows_pair(sm + pl.stage_off + (size_t)s * pl.stage_bytes + in.w + (size_t)(16 * rbk) * L.stride, L.stride);
+            if (G > MU && ms > 2) {  // sets st, st + 1 over one decode of the weights
+                const uint8_t* xg1 = xg + 2 * (size_t)xf_gs_bytes(FF);
+                float acc[2][4] = {}, mn[2][2] = {};
+                if (in.y & 256) {
+                    const uint8_t* bq[2] = {BPtr<1>(xs + (size_t)(2 * st) * FF * 3, FF >> 5, ms).p[0],
+                                            BPtr<1>(xs + (size_t)(2 * st + 2) * FF * 3, FF >> 5, ms - 2).p[0]};
+                    const uint8_t* mq[2] = {min_operand(xg, FF, ms), min_operand(xg1, FF, ms - 2)};
+                    block_tasks_m<QD, 2>(rows, nsb, wsub, 3, bq, mq, acc, mn);
+                }
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const float a1[1][4] = {{acc[k][0], acc[k][1], acc[k][2], acc[k][3]}};
+                    const float ts = t < ms - 2 * k ? *reinterpret_cast<const float*>(xg + (size_t)(2 * k + t) * xf_gs_bytes(FF)) : 0.f;
+                    warp_values(a1, mn[k], ts, part, 2 * ((lane >> 2) & 7), 2 * ((lane >> 2) & 7) + 1, G, 2 * st + 2 * k);
+                }
+                st += 2;
+                continue;
+            }
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
             if (in.y & 256) {
                 const BPtr<1> bp(xs + (size_t)(2 * st) * FF * 3, FF >> 5, ms);
-                block_tasks<QD>(rows_pair(sm + pl.stage_off + (size_t)s * pl.stage_bytes + in.w + (size_t)(16 * rbk) * L.stride,
-                                          L.stride),
-                                nsb, wsub, 3, bp, min_operand(xg, FF, ms), acc, mn);
+                block_tasks<QD>(rows, nsb, wsub, 3, bp, min_operand(xg, FF, ms), acc, mn);
             }
             const float ts = t < ms ? *reinterpret_cast<const float*>(xg + (size_t)t * xf_gs_bytes(FF)) : 0.f;
             warp_values(acc, mn, ts, part, 2 * ((lane >> 2) & 7), 2 * ((lane >> 2) & 7) + 1, G, 2 * st);
+            st++;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&done[s]);
