@@ -460,6 +460,152 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     }
 }
 
+// ---- prompt-pass attention when every split holds one chunk (nch <= nsplit for every token of the pass)
+// Block (kv head h, chunk c, tokens 8z .. 8z + 7) stages chunk c's K/V rows once for its tokens; warp w
+// takes q heads 4 (w % WPT) .. + 3 of one token (WPT = ceil(grp / 4) warps per token, 8 / WPT tokens at
+// a time). Each K float4 a lane loads serves four heads' dot products and each V element four heads'
+// sums, so shared-memory traffic per head is about a quarter of k_attention's. The record of (token,
+// head, split c) is k_attention's for a split with the single chunk c, operation for operation: scores
+// as four fmaf chains over d = i mod 4 then (a0 + a1) + (a2 + a3), times scale; the maximum over the
+// chunk; p = expf(s - m); the sum as lane value p[lane] + p[lane + 32] reduced by the same butterfly;
+// o as two fmaf chains over even and odd positions from +0, then added. The merge therefore sees the
+// same records whichever kernel wrote them.
+constexpr int AC_TG = 8;  // tokens per block
+size_t attn_chunk_smem(int hd, int grp) {
+    return ((size_t)2 * ATT_CH * (hd + 4) + (size_t)AC_TG * grp * (hd + 4) + (size_t)(ATT_NT / 32) * ATT_CH * 4) *
+           sizeof(float);
+}
+template <int HD>
+__global__ void __launch_bounds__(ATT_NT) k_attn_chunk(const float* __restrict__ q, const float* __restrict__ kc,
+                                                        const float* __restrict__ vc, int n_head, int n_kv, float scale,
+                                                        const DecodeState* st, int nb, int nsplit,
+                                                        float* __restrict__ part) {
+    constexpr int PER = HD / 32, RS = HD + 4, QS = HD + 4;
+    extern __shared__ __align__(16) float smf[];
+    const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
+    float* Ks = smf;                          // [ATT_CH][RS]
+    float* Vs = Ks + ATT_CH * RS;             // [ATT_CH][RS]
+    float* Qs = Vs + ATT_CH * RS;             // [AC_TG][grp][QS]
+    float* Ps = Qs + AC_TG * grp * QS;        // [warp][ATT_CH][4]
+    const int h = blockIdx.x, c = blockIdx.y, t0 = blockIdx.z * AC_TG;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_trigger();
+    const int pos = st->pos, p0 = c * ATT_CH, tn = min(AC_TG, nb - t0);
+    // token t has positions 0 .. pos + t: chunk c holds some of them iff pos + t >= p0
+    const int tf = max(t0, p0 - pos);
+    if (tf >= t0 + tn) return;
+    const int n_max = min(ATT_CH, pos + t0 + tn - p0);
+    for (int i = threadIdx.x; i < n_max * (HD / 4); i += ATT_NT) {
+        const int r = i / (HD / 4), c4 = i - r * (HD / 4);
+        const size_t g = (size_t)(p0 + r) * KD + (size_t)h * HD + 4 * c4;
+        cp_async16(Ks + r * RS + 4 * c4, kc + g);
+        cp_async16(Vs + r * RS + 4 * c4, vc + g);
+    }
+    for (int i = threadIdx.x; i < tn * grp * (HD / 4); i += ATT_NT) {
+        const int row = i / (HD / 4), c4 = i - row * (HD / 4), tt = row / grp, hq = row - tt * grp;
+        cp_async16(Qs + row * QS + 4 * c4, q + (size_t)(t0 + tt) * QD + (size_t)(h * grp + hq) * HD + 4 * c4);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int wpt = (grp + 3) / 4, nslot = (ATT_NT / 32) / wpt, slot = warp / wpt, h4 = 4 * (warp - slot * wpt);
+    if (slot >= nslot) return;
+    float* pw = Ps + warp * ATT_CH * 4;
+    for (int t = tf + slot; t < t0 + tn; t += nslot) {
+        const int n = min(ATT_CH, pos + t + 1 - p0);  // positions of token t in this chunk
+        const float* qb = Qs + ((t - t0) * grp + h4) * QS;
+        // scores of positions lane, lane + 32 for the warp's four heads
+        float s[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int pr = lane + 32 * r;
+            float a[4][4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0.f;
+            if (pr < n) {
+                const float* kr = Ks + pr * RS;
+#pragma unroll 4
+                for (int d = 0; d < HD; d += 4) {
+                    const float4 kv4 = *reinterpret_cast<const float4*>(kr + d);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(qb + k * QS + d);
+                        a[k][0] = fmaf(q4.x, kv4.x, a[k][0]);
+                        a[k][1] = fmaf(q4.y, kv4.y, a[k][1]);
+                        a[k][2] = fmaf(q4.z, kv4.z, a[k][2]);
+                        a[k][3] = fmaf(q4.w, kv4.w, a[k][3]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; k++) s[r][k] = pr < n ? ((a[k][0] + a[k][1]) + (a[k][2] + a[k][3])) * scale : -INFINITY;
+        }
+        float m[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float mc = fmaxf(s[0][k], s[1][k]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+            m[k] = mc;
+            float ls = 0.f;
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const float p = (lane + 32 * r) < n ? expf(s[r][k] - mc) : 0.f;
+                pw[(lane + 32 * r) * 4 + k] = p;
+                ls += p;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+            l[k] = ls;
+        }
+        __syncwarp();
+        float acc[2][4][PER];
+#pragma unroll
+        for (int e = 0; e < 2; e++)
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int j = 0; j < PER; j++) acc[e][k][j] = 0.f;
+        int r = 0;
+#pragma unroll 2
+        for (; r + 1 < n; r += 2) {
+            const float4 pe = *reinterpret_cast<const float4*>(pw + r * 4), po = *reinterpret_cast<const float4*>(pw + r * 4 + 4);
+            const float pev[4] = {pe.x, pe.y, pe.z, pe.w}, pov[4] = {po.x, po.y, po.z, po.w};
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const float v0 = Vs[r * RS + lane + 32 * j], v1 = Vs[(r + 1) * RS + lane + 32 * j];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    acc[0][k][j] = fmaf(pev[k], v0, acc[0][k][j]);
+                    acc[1][k][j] = fmaf(pov[k], v1, acc[1][k][j]);
+                }
+            }
+        }
+        if (r < n) {
+            const float4 pe = *reinterpret_cast<const float4*>(pw + r * 4);
+            const float pev[4] = {pe.x, pe.y, pe.z, pe.w};
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const float v0 = Vs[r * RS + lane + 32 * j];
+#pragma unroll
+                for (int k = 0; k < 4; k++) acc[0][k][j] = fmaf(pev[k], v0, acc[0][k][j]);
+            }
+        }
+        __syncwarp();  // pw is rewritten by the warp's next token
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            if (h4 + k >= grp) break;
+            float* pr = part + (((size_t)t * n_head + (size_t)h * grp + h4 + k) * nsplit + c) * (HD + 2);
+            if (lane == 0) {
+                pr[0] = m[k];
+                pr[1] = l[k];
+            }
+#pragma unroll
+            for (int j = 0; j < PER; j++) pr[2 + lane + 32 * j] = acc[0][k][j] + acc[1][k][j];
+        }
+    }
+}
+
 // ---- split merge of every head of a token row: out = sum_y o_y e^(m_y - M) / sum_y l_y e^(m_y - M),
 // written to att (fp32) and, in fragment form, to xf for the o-projection. One CTA per token row
 // (32 warps, warp w merges heads w, w + 32, ...; the row stays in shared memory for the prep).
@@ -615,16 +761,31 @@ size_t attn_smem(int hd, int grp) {
 template <int HD>
 static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                            const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
-                           const RopeFuse& rf, cudaStream_t s) {
-    const size_t smem = attn_smem(HD, n_head / n_kv);
-    static size_t cur = 0;
-    if (smem > cur) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        cur = smem;
+                           const RopeFuse& rf, int pos_host, cudaStream_t s) {
+    cudaError_t e;
+    const int nch_max = pos_host >= 0 ? (pos_host + nb + ATT_CH - 1) / ATT_CH : 0;
+    if (!rf.qkv && !rf.cnt && nb > 1 && pos_host >= 0 && nch_max <= nsplit && n_head / n_kv <= 32) {
+        // prompt pass at a known position, one chunk per split: chunk-shared kernel
+        const size_t smem = attn_chunk_smem(HD, n_head / n_kv);
+        static size_t ccur = 0;
+        if (smem > ccur) {
+            e = cudaFuncSetAttribute(k_attn_chunk<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            ccur = smem;
+        }
+        e = launch_pdl(k_attn_chunk<HD>, dim3(n_kv, nch_max, (nb + AC_TG - 1) / AC_TG), dim3(ATT_NT), smem, s, q,
+                       (const float*)kc, (const float*)vc, n_head, n_kv, scale, st, nb, nsplit, part);
+    } else {
+        const size_t smem = attn_smem(HD, n_head / n_kv);
+        static size_t cur = 0;
+        if (smem > cur) {
+            e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            cur = smem;
+        }
+        e = launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv, scale,
+                       st, nsplit, part, rf);
     }
-    cudaError_t e = launch_pdl(k_attention<HD>, dim3(n_kv, nsplit, nb), dim3(ATT_NT), smem, s, q, kc, vc, n_head, n_kv,
-                               scale, st, nsplit, part, rf);
     if (e != cudaSuccess || rf.cnt) return e;  // merged by the attention launch itself
     const size_t msmem = (size_t)n_head * HD * 4;
     static size_t mcur = 0;
@@ -637,12 +798,12 @@ static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int
 }
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                              const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
-                             const RopeFuse& rf, cudaStream_t s) {
+                             const RopeFuse& rf, int pos_host, cudaStream_t s) {
     if (n_head % n_kv || n_head / n_kv > ATT_MAXH * (ATT_NT / 32) || nsplit < 1 || nsplit > 128 ||
         (rf.qkv && nb != 1) || (rf.cnt && (nb != 1 || !rf.att)) || (n_head * hd) % 256)
         return cudaErrorInvalidValue;
-    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, s);
-    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, s);
+    if (hd == 128) return attn_as<128>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, pos_host, s);
+    if (hd == 64) return attn_as<64>(q, kc, vc, n_head, n_kv, scale, st, nb, nsplit, part, att, xf, rf, pos_host, s);
     return cudaErrorInvalidValue;
 }
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {

@@ -73,7 +73,7 @@ struct RopeFuse {
 // leaves the fragment form to the o-projection's prologue.
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                              const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
-                             const RopeFuse& rf, cudaStream_t s);
+                             const RopeFuse& rf, int pos_host, cudaStream_t s);  // pos_host: state->pos if known, else -1
 // blk: nblk float2 of scratch
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s);
 cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s);

@@ -271,6 +271,7 @@ struct EahmmfEngine {
     void* xf_att = nullptr;   // [MAXB rows of QD] attention outputs in fragment form
     size_t moe_ws_bytes = 0, gemv_ws_bytes = 0;
     int* toks = nullptr;       // device token staging [MAXB]
+    int pos_host = -1;         // state->pos during an eval pass (set by eval_dev), -1 otherwise
     int* h_toks = nullptr;     // pinned [MAXB]
     int* status = nullptr;     // device status word
     int* att_cnt = nullptr;    // [n_kv] split counters of the attention launch's fused merge (self-resetting)
@@ -604,7 +605,7 @@ struct EahmmfEngine {
         rf.cnt = att_cnt;
         rf.att = att;
         if (!mark(3) ||
-            launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, 1, nsplit, attn_part, att, XF{}, rf, st) !=
+            launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, 1, nsplit, attn_part, att, XF{}, rf, -1, st) !=
                 cudaSuccess ||
             !mark(4))
             return ST_CUDA;
@@ -742,7 +743,8 @@ struct EahmmfEngine {
                 return ST_CUDA;
             }
             const XF xf_o = xf_carve(xf_att, MAXB, QD);
-            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, att, xf_o, rf, st) !=
+            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, att, xf_o, rf, pos_host,
+                                 st) !=
                     cudaSuccess ||
                 !mark(4))
                 return ST_CUDA;
@@ -826,7 +828,9 @@ struct EahmmfEngine {
             memcpy(h_toks, htoks + i, (size_t)nb * 4);
             if (cudaMemcpyAsync(toks, h_toks, (size_t)nb * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
                 return ST_CUDA;
+            pos_host = p0 + i;  // the pass's position, known here (the captured decode step reads it on the device)
             const int rc = forward(toks, nb, i + nb == n);
+            pos_host = -1;
             if (rc != ST_OK) return rc;
             if (launch_advance(state, nb, st) != cudaSuccess) return ST_CUDA;
         }
