@@ -273,6 +273,102 @@ __device__ __forceinline__ void merge_head(const float* __restrict__ p, int nspl
     for (int j = 0; j < PER; j++) v[j] = o[j] * inv;
 }
 
+// One split holding a single chunk of n positions (the usual case: the context fits in nsplit chunks),
+// for the grp q heads of a block, with the whole block. Scores: thread (position p, heads 2i, 2i+1), so a
+// K float4 serves two heads; the softmax of head hq: warp hq % 8 with positions lane, lane + 32 per lane;
+// PV: warp (four heads, elements lane + 32 j), so a V element serves four heads. Every record equals the
+// one k_attention's per-warp loop writes for a first (and only) chunk: dots as four fmaf chains over
+// d = i mod 4 then (a0 + a1) + (a2 + a3), times scale; m = the maximum; p = expf(s - m); l = the lane sums
+// p[lane] + p[lane + 32] reduced by the same butterfly (= 0 * 0 + ls); o = even and odd fmaf chains from +0,
+// then added. S: [grp][ATT_CH] scores, P: [ATT_CH][4 ceil(grp / 4)] probabilities. rec0: the record of the
+// group's first head for this split; head hq's is at rec0 + hq * rstride.
+template <int HD>
+__device__ __forceinline__ void attn_one_chunk(const float* __restrict__ Ks, const float* __restrict__ Vs,
+                                               const float* __restrict__ Qs, float* __restrict__ S,
+                                               float* __restrict__ P, int grp, int n, float scale,
+                                               float* __restrict__ rec0, size_t rstride) {
+    constexpr int PER = HD / 32, RS = HD + 4;
+    static_assert(ATT_CH == 64, "positions lane, lane + 32");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int GP2 = (grp + 1) / 2, GQ = (grp + 3) / 4, GP = 4 * GQ;
+    for (int it = tid; it < GP2 * ATT_CH; it += ATT_NT) {
+        const int p = it & (ATT_CH - 1), h0 = 2 * (it / ATT_CH);
+        const float* q0 = Qs + h0 * HD;
+        const float* q1 = h0 + 1 < grp ? q0 + HD : q0;
+        float a[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        if (p < n) {
+            const float* kr = Ks + p * RS;
+#pragma unroll 8
+            for (int d = 0; d < HD; d += 4) {
+                const float4 kv4 = *reinterpret_cast<const float4*>(kr + d);
+                const float4 qa = *reinterpret_cast<const float4*>(q0 + d);
+                const float4 qb = *reinterpret_cast<const float4*>(q1 + d);
+                a[0][0] = fmaf(qa.x, kv4.x, a[0][0]);
+                a[0][1] = fmaf(qa.y, kv4.y, a[0][1]);
+                a[0][2] = fmaf(qa.z, kv4.z, a[0][2]);
+                a[0][3] = fmaf(qa.w, kv4.w, a[0][3]);
+                a[1][0] = fmaf(qb.x, kv4.x, a[1][0]);
+                a[1][1] = fmaf(qb.y, kv4.y, a[1][1]);
+                a[1][2] = fmaf(qb.z, kv4.z, a[1][2]);
+                a[1][3] = fmaf(qb.w, kv4.w, a[1][3]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+            if (h0 + k < grp) S[(h0 + k) * ATT_CH + p] = p < n ? ((a[k][0] + a[k][1]) + (a[k][2] + a[k][3])) * scale : -INFINITY;
+    }
+    __syncthreads();
+    for (int hq = warp; hq < grp; hq += ATT_NT / 32) {
+        const float s0 = S[hq * ATT_CH + lane], s1 = S[hq * ATT_CH + lane + 32];
+        float mc = fmaxf(fmaxf(-INFINITY, s0), s1);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+        const float p0 = lane < n ? expf(s0 - mc) : 0.f, p1 = lane + 32 < n ? expf(s1 - mc) : 0.f;
+        P[lane * GP + hq] = p0;
+        P[(lane + 32) * GP + hq] = p1;
+        float ls = 0.f;
+        ls += p0;
+        ls += p1;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+        if (lane == 0) {
+            rec0[hq * rstride] = mc;
+            rec0[hq * rstride + 1] = ls;
+        }
+    }
+    __syncthreads();
+    for (int it = warp; it < GQ * PER; it += ATT_NT / 32) {
+        const int qd = it % GQ, e = lane + 32 * (it / GQ);
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        int r = 0;
+#pragma unroll 4
+        for (; r + 1 < n; r += 2) {
+            const float4 pe = *reinterpret_cast<const float4*>(P + r * GP + 4 * qd);
+            const float4 po = *reinterpret_cast<const float4*>(P + (r + 1) * GP + 4 * qd);
+            const float v0 = Vs[r * RS + e], v1 = Vs[(r + 1) * RS + e];
+            acc[0][0] = fmaf(pe.x, v0, acc[0][0]);
+            acc[0][1] = fmaf(pe.y, v0, acc[0][1]);
+            acc[0][2] = fmaf(pe.z, v0, acc[0][2]);
+            acc[0][3] = fmaf(pe.w, v0, acc[0][3]);
+            acc[1][0] = fmaf(po.x, v1, acc[1][0]);
+            acc[1][1] = fmaf(po.y, v1, acc[1][1]);
+            acc[1][2] = fmaf(po.z, v1, acc[1][2]);
+            acc[1][3] = fmaf(po.w, v1, acc[1][3]);
+        }
+        if (r < n) {
+            const float4 pe = *reinterpret_cast<const float4*>(P + r * GP + 4 * qd);
+            const float v0 = Vs[r * RS + e];
+            acc[0][0] = fmaf(pe.x, v0, acc[0][0]);
+            acc[0][1] = fmaf(pe.y, v0, acc[0][1]);
+            acc[0][2] = fmaf(pe.z, v0, acc[0][2]);
+            acc[0][3] = fmaf(pe.w, v0, acc[0][3]);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (4 * qd + k < grp) rec0[(4 * qd + k) * rstride + 2 + e] = acc[0][k] + acc[1][k];
+    }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ q, float* __restrict__ kc,
                                                        float* __restrict__ vc, int n_head, int n_kv, float scale,
@@ -353,6 +449,12 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
             }
         }
         __syncthreads();
+        if (nch <= nsplit) {  // this split's only chunk (block-uniform): the block-wide layout writes the records
+            attn_one_chunk<HD>(Ks, Vs, Qs, Qs + grp * HD, Qs + grp * HD + grp * ATT_CH, grp, n, scale,
+                               part + (((size_t)t * n_head + (size_t)h * grp) * nsplit + y) * (HD + 2),
+                               (size_t)nsplit * (HD + 2));
+            break;
+        }
 #pragma unroll
         for (int k = 0; k < ATT_MAXH; k++) {
             const int hq = warp + k * nwarp;
@@ -432,7 +534,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
 #pragma unroll
     for (int k = 0; k < ATT_MAXH; k++) {
         const int hq = warp + k * nwarp;
-        if (hq >= grp || y >= nch) break;
+        if (hq >= grp || y >= nch || nch <= nsplit) break;  // (nch <= nsplit: written by attn_one_chunk)
         float* pr = part + (((size_t)t * n_head + (size_t)h * grp + hq) * nsplit + y) * (HD + 2);
         if (lane == 0) {
             pr[0] = m_run[k];
@@ -755,8 +857,10 @@ cudaError_t launch_qk_rope_kv(int hd, const float* qkv, int n_head, int n_kv, co
                           q_out, kc, vc);
     return cudaErrorInvalidValue;
 }
-size_t attn_smem(int hd, int grp) {
-    return ((size_t)2 * ATT_CH * (hd + 4) + (size_t)(ATT_NT / 32) * ATT_CH + (size_t)grp * hd) * sizeof(float);
+size_t attn_smem(int hd, int grp) {  // K, V, per-warp P, Q, then attn_one_chunk's S and P
+    return ((size_t)2 * ATT_CH * (hd + 4) + (size_t)(ATT_NT / 32) * ATT_CH + (size_t)grp * hd + (size_t)grp * ATT_CH +
+            (size_t)ATT_CH * 4 * ((grp + 3) / 4)) *
+           sizeof(float);
 }
 template <int HD>
 static cudaError_t attn_as(const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
