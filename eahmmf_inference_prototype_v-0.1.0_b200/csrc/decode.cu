@@ -383,13 +383,11 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     const int h = blockIdx.x, y = blockIdx.y, t = blockIdx.z;
     const int grp = n_head / n_kv, QD = n_head * HD, KD = n_kv * HD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = ATT_NT / 32;
-    pdl_wait();
-    pdl_trigger();
-    const int np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
-    const int nch = (np + ATT_CH - 1) / ATT_CH;
-    // splits y >= nch hold no positions of this token: no record (the merges read the first
-    // min(nsplit, nch) records only); a single-token step still counts the block for its merge
-    if (y >= nch && !rf.cnt) return;
+    // A single-token step reads the position and stages its first chunk before the grid-dependency wait:
+    // the position and the cache rows of earlier positions were written by kernels that completed before
+    // the previous grid passed its own wait, and the step's own row is replaced below from the q|k|v row.
+    // A prompt pass's rows come from the previous grid (k_qk_rope_kv): its copies start after the wait.
+    int np = 0, nch = 0;
     auto stage_chunk = [&](int c) {  // K/V rows of chunk c -> shared memory (cp.async, 16 bytes each)
         const int p0 = c * ATT_CH, n = min(ATT_CH, np - p0);
         for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
@@ -399,7 +397,21 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
             cp_async16(Vs + r * RS + 4 * c4, vc + g);
         }
     };
-    if (y < nch) stage_chunk(y);  // the first chunk's copies fly while the q heads are prepared
+    if (rf.qkv) {
+        np = st->pos + t + 1;
+        nch = (np + ATT_CH - 1) / ATT_CH;
+        if (y < nch) stage_chunk(y);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (!rf.qkv) {
+        np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
+        nch = (np + ATT_CH - 1) / ATT_CH;
+    }
+    // splits y >= nch hold no positions of this token: no record (the merges read the first
+    // min(nsplit, nch) records only); a single-token step still counts the block for its merge
+    if (y >= nch && !rf.cnt) return;
+    if (!rf.qkv && y < nch) stage_chunk(y);  // the first chunk's copies fly while the q heads are prepared
     if (y >= nch) {
     } else if (rf.qkv) {  // single-token step: the group's q heads normalised and rotated here, from the q|k|v row
         for (int hq = warp; hq < grp; hq += nwarp) {
