@@ -1,5 +1,5 @@
-// ksb.cuh -- one super-block (16 rows x 256 weights) of the expert GEMV with one MMA column set (two
-// tokens), the inner loop of the MoE kernels (moe.cu).
+// ksb.cuh -- one super-block (16 rows x 256 weights) of the expert GEMV with NS MMA column sets (two
+// tokens each; the weights decoded once), the inner loop of the MoE kernels (moe.cu).
 //
 // Same arithmetic as kq_task (kq.cuh) on both halves of a super-block at once, written for the
 // instruction budget of a kernel that must decode ~40 weight bytes per cycle per SM: all operands are
@@ -9,9 +9,9 @@
 //
 // Operands, per lane (g, t) of the warp:
 //   r0, r1   the super-block in MMA rows g and g+8 (shared memory; Q4_K/Q5_K: 16-byte aligned)
-//   bq       the lane's B fragments of this super-block: Q4_K/Q5_K: XF row base + 8t + sb * 768,
+//   bq[s]    set s's B fragments of this super-block for the lane: Q4_K/Q5_K: XF row base + 8t + sb * 768,
 //            Q6_K: XF row base + 4t + sb * 768 (kq.cuh: 96 bytes per 32-k block)
-//   mq       Q4_K/Q5_K: the lane's B operand of the minimum-term MMA at this super-block: in the XF
+//   mq[s]    Q4_K/Q5_K: set s's B operand for the lane of the minimum-term MMA at this super-block: in the XF
 //            group sums of token g/2 (g < 4; token 0 otherwise), f16 high parts (g even) or residues
 //            (g odd), + 4t
 //   out      d-scaled sums of rows g, g+8 for the lane's two digit columns (accumulated)
@@ -40,89 +40,6 @@ __device__ __forceinline__ uint32_t u8pair_f16(uint32_t w, uint32_t sel) {
     return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-// Q4_K / Q5_K super-block. Int32 bound per row: eight groups of 32 x 15 (x16 for in-place high
-// nibbles, 31 for Q5_K) x 127 x 63 (x16 for Q4_K low-nibble scales) < 5e8.
-template <int QT>
-__device__ __forceinline__ void sb_q45(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
-                                       const uint8_t* __restrict__ bq, const uint8_t* __restrict__ mq, int t,
-                                       float (&out)[4], float (&mn)[2]) {
-    constexpr int QS = QT == T_Q4_K ? 16 : 48;
-    const uint4 H0 = *reinterpret_cast<const uint4*>(r0), H1 = *reinterpret_cast<const uint4*>(r1);
-    // 6-bit scales of groups 0-3 (A) and 4-7 (B), word-parallel restatement of scale_min_k4
-    // (qwen3moe.cpp:133-141)
-    const uint32_t sA0 = H0.y & 0x3f3f3f3fu, sB0 = (H0.w & 0x0f0f0f0fu) | ((H0.y >> 2) & 0x30303030u);
-    const uint32_t sA1 = H1.y & 0x3f3f3f3fu, sB1 = (H1.w & 0x0f0f0f0fu) | ((H1.y >> 2) & 0x30303030u);
-    // low-nibble groups (even) and high-nibble groups (odd) as 16-bit fields; Q4_K low scales x16
-    // (the high nibbles enter the MMA in place, i.e. x16)
-    constexpr int LSH = QT == T_Q4_K ? 4 : 0;
-    const uint32_t le0[2] = {(sA0 & 0x00ff00ffu) << LSH, (sB0 & 0x00ff00ffu) << LSH};
-    const uint32_t le1[2] = {(sA1 & 0x00ff00ffu) << LSH, (sB1 & 0x00ff00ffu) << LSH};
-    const uint32_t ho0[2] = {(sA0 >> 8) & 0x00ff00ffu, (sB0 >> 8) & 0x00ff00ffu};
-    const uint32_t ho1[2] = {(sA1 >> 8) & 0x00ff00ffu, (sB1 >> 8) & 0x00ff00ffu};
-    uint2 qh0{0u, 0u}, qh1{0u, 0u};
-    if constexpr (QT == T_Q5_K) {
-        qh0 = *reinterpret_cast<const uint2*>(r0 + 16 + 8 * t);
-        qh1 = *reinterpret_cast<const uint2*>(r1 + 16 + 8 * t);
-    }
-    const uint8_t* q0 = r0 + QS + 8 * t;
-    const uint8_t* q1 = r1 + QS + 8 * t;
-    uint2 w0[4], w1[4], bl[4], bh[4];
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        w0[c] = *reinterpret_cast<const uint2*>(q0 + 32 * c);
-        w1[c] = *reinterpret_cast<const uint2*>(q1 + 32 * c);
-        bl[c] = *reinterpret_cast<const uint2*>(bq + 96 * (2 * c));
-        bh[c] = *reinterpret_cast<const uint2*>(bq + 96 * (2 * c + 1));
-    }
-    int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        uint32_t lo[4], hi[4];
-        if constexpr (QT == T_Q4_K) {
-            lo[0] = w0[c].x & 0x0f0f0f0fu;
-            lo[1] = w1[c].x & 0x0f0f0f0fu;
-            lo[2] = w0[c].y & 0x0f0f0f0fu;
-            lo[3] = w1[c].y & 0x0f0f0f0fu;
-            hi[0] = w0[c].x & 0xf0f0f0f0u;
-            hi[1] = w1[c].x & 0xf0f0f0f0u;
-            hi[2] = w0[c].y & 0xf0f0f0f0u;
-            hi[3] = w1[c].y & 0xf0f0f0f0u;
-        } else {  // fifth bit from qh: bit 2c for the low nibbles, 2c+1 for the high ones
-            lo[0] = (w0[c].x & 0x0f0f0f0fu) | (((qh0.x >> (2 * c)) & 0x01010101u) << 4);
-            lo[1] = (w1[c].x & 0x0f0f0f0fu) | (((qh1.x >> (2 * c)) & 0x01010101u) << 4);
-            lo[2] = (w0[c].y & 0x0f0f0f0fu) | (((qh0.y >> (2 * c)) & 0x01010101u) << 4);
-            lo[3] = (w1[c].y & 0x0f0f0f0fu) | (((qh1.y >> (2 * c)) & 0x01010101u) << 4);
-            hi[0] = ((w0[c].x >> 4) & 0x0f0f0f0fu) | (((qh0.x >> (2 * c + 1)) & 0x01010101u) << 4);
-            hi[1] = ((w1[c].x >> 4) & 0x0f0f0f0fu) | (((qh1.x >> (2 * c + 1)) & 0x01010101u) << 4);
-            hi[2] = ((w0[c].y >> 4) & 0x0f0f0f0fu) | (((qh0.y >> (2 * c + 1)) & 0x01010101u) << 4);
-            hi[3] = ((w1[c].y >> 4) & 0x0f0f0f0fu) | (((qh1.y >> (2 * c + 1)) & 0x01010101u) << 4);
-        }
-        // chunk c: low group 2c = byte 2 (c & 1) of word c >> 1, high group 2c + 1 = the byte after
-        const int f = c & 1, wd = c >> 1;
-        const int sl0 = f ? (int)(le0[wd] >> 16) : (int)(le0[wd] & 0xffffu);
-        const int sl1 = f ? (int)(le1[wd] >> 16) : (int)(le1[wd] & 0xffffu);
-        const int sh0 = f ? (int)(ho0[wd] >> 16) : (int)(ho0[wd] & 0xffffu);
-        const int sh1 = f ? (int)(ho1[wd] >> 16) : (int)(ho1[wd] & 0xffffu);
-        scale_acc(acc, imma32(lo[0], lo[1], lo[2], lo[3], bl[c].x, bl[c].y), sl0, sl1);
-        scale_acc(acc, imma32(hi[0], hi[1], hi[2], hi[3], bh[c].x, bh[c].y), sh0, sh1);
-    }
-    constexpr float DS = QT == T_Q4_K ? 0.0625f : 1.0f;
-    const float d0 = f16_to_f32(H0.x & 0xffffu) * DS, d1 = f16_to_f32(H1.x & 0xffffu) * DS;
-    out[0] = fmaf(d0, (float)acc[0], out[0]);
-    out[1] = fmaf(d0, (float)acc[1], out[1]);
-    out[2] = fmaf(d1, (float)acc[2], out[2]);
-    out[3] = fmaf(d1, (float)acc[3], out[3]);
-    {  // group minimums: the lane needs the mins of groups 2t, 2t+1 (bytes of the A or B word)
-        const uint32_t mA0 = H0.z & 0x3f3f3f3fu, mB0 = ((H0.w >> 4) & 0x0f0f0f0fu) | ((H0.z >> 2) & 0x30303030u);
-        const uint32_t mA1 = H1.z & 0x3f3f3f3fu, mB1 = ((H1.w >> 4) & 0x0f0f0f0fu) | ((H1.z >> 2) & 0x30303030u);
-        const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
-        float c[4];
-        hmma8(c, u8pair_f16(t < 2 ? mA0 : mB0, sel), u8pair_f16(t < 2 ? mA1 : mB1, sel), *reinterpret_cast<const uint32_t*>(mq));
-        mn[0] = fmaf(f16_to_f32(H0.x >> 16), c[0] + c[1], mn[0]);
-        mn[1] = fmaf(f16_to_f32(H1.x >> 16), c[2] + c[3], mn[1]);
-    }
-}
-
 // 32-bit word at p; M: p is 2 bytes past a 4-byte boundary (Q6_K rows of 630 bytes)
 template <bool M>
 __device__ __forceinline__ uint32_t ld32m(const uint8_t* p) {
@@ -134,53 +51,10 @@ __device__ __forceinline__ uint32_t ld32m(const uint8_t* p) {
     }
 }
 
-// Q6_K super-block (ql 128 | qh 64 | 16 int8 scales | f16 d; qwen3moe.cpp:180-202). M0/M1: row g /
-// g+8 of this super-block starts 2 bytes past a 4-byte boundary. Int32 bound per row: sixteen groups
-// of 16 x 32 x 127 x 128 < 1.4e8.
-template <bool M0, bool M1>
-__device__ __forceinline__ void sb_q6(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
-                                      const uint8_t* __restrict__ bq, int t, float (&out)[4]) {
-    const uint8_t* p0 = r0 + 4 * t;
-    const uint8_t* p1 = r1 + 4 * t;
-    int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint32_t sc0[2] = {ld32m<M0>(r0 + 192 + 8 * h), ld32m<M0>(r0 + 196 + 8 * h)};
-        const uint32_t sc1[2] = {ld32m<M1>(r1 + 192 + 8 * h), ld32m<M1>(r1 + 196 + 8 * h)};
-#pragma unroll
-        for (int ib = 0; ib < 2; ib++) {
-            const int o = 64 * h + 16 * ib;
-            const uint32_t qa0 = ld32m<M0>(p0 + o), qb0 = ld32m<M0>(p0 + o + 32), qh0 = ld32m<M0>(p0 + 128 + 32 * h + 16 * ib);
-            const uint32_t qa1 = ld32m<M1>(p1 + o), qb1 = ld32m<M1>(p1 + o + 32), qh1 = ld32m<M1>(p1 + 128 + 32 * h + 16 * ib);
-            // 6-bit values per byte (low nibble from ql, bits 4-5 from qh), then q - 32 as s8:
-            // ((q & 63) + 0x60) ^ 0x80 per byte, carry-free
-            const uint32_t v0[4] = {lop_sel(qa0, qh0 << 4, 0x0f0f0f0fu), lop_sel(qb0, qh0 << 2, 0x0f0f0f0fu),
-                                    lop_sel(qa0 >> 4, qh0, 0x0f0f0f0fu), lop_sel(qb0 >> 4, qh0 >> 2, 0x0f0f0f0fu)};
-            const uint32_t v1[4] = {lop_sel(qa1, qh1 << 4, 0x0f0f0f0fu), lop_sel(qb1, qh1 << 2, 0x0f0f0f0fu),
-                                    lop_sel(qa1 >> 4, qh1, 0x0f0f0f0fu), lop_sel(qb1 >> 4, qh1 >> 2, 0x0f0f0f0fu)};
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const uint32_t a0 = ((v0[q] & 0x3f3f3f3fu) + 0x60606060u) ^ 0x80808080u;
-                const uint32_t a1 = ((v1[q] & 0x3f3f3f3fu) + 0x60606060u) ^ 0x80808080u;
-                const int gl = 2 * q + ib;  // scale index within the half
-                const uint32_t b = *reinterpret_cast<const uint32_t*>(bq + 96 * (4 * h + q) + 16 * ib);
-                scale_acc(acc, imma16s(a0, a1, b), sbyte(sc0[gl >> 2], gl & 3), sbyte(sc1[gl >> 2], gl & 3));
-            }
-        }
-    }
-    const float d0 = f16_to_f32(*reinterpret_cast<const uint16_t*>(r0 + 208));
-    const float d1 = f16_to_f32(*reinterpret_cast<const uint16_t*>(r1 + 208));
-    out[0] = fmaf(d0, (float)acc[0], out[0]);
-    out[1] = fmaf(d0, (float)acc[1], out[1]);
-    out[2] = fmaf(d1, (float)acc[2], out[2]);
-    out[3] = fmaf(d1, (float)acc[3], out[3]);
-}
-
-// ---- several column sets over one decoded super-block (the grouped kernels' larger groups) ----------
-// sb_q45m / sb_q6m: the weights of the super-block are decoded once and every set s runs the MMAs,
-// group-scale sums, d-scaling and minimum term of sb_q45 / sb_q6 on its own operands bq[s] (mq[s]),
-// with the same integer and fp32 operations in the same order: out[s] and mn[s] are bitwise what the
-// single-set function leaves for that set.
+// ---- NS column sets over one decoded super-block ---------------------------------------------------
+// sb_q45m / sb_q6m: the weights of the super-block are decoded once and every set s runs its MMAs,
+// group-scale sums, d-scaling and minimum term on its own operands bq[s] (mq[s]); each set's integer
+// and fp32 operations do not depend on NS, so out[s] and mn[s] are bitwise what NS = 1 leaves.
 template <int QT, int NS>
 __device__ __forceinline__ void sb_q45m(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
                                         const uint8_t* const (&bq)[NS], const uint8_t* const (&mq)[NS], int t,
@@ -311,6 +185,27 @@ __device__ __forceinline__ void sb_q6m(const uint8_t* __restrict__ r0, const uin
         out[s][2] = fmaf(d1, (float)acc[s][2], out[s][2]);
         out[s][3] = fmaf(d1, (float)acc[s][3], out[s][3]);
     }
+}
+
+// One column set (the decode kernels and groups of up to two slots): out / mn of that set.
+// Q4_K / Q5_K super-block. Int32 bound per row: eight groups of 32 x 15 (x16 for in-place high
+// nibbles, 31 for Q5_K) x 127 x 63 (x16 for Q4_K low-nibble scales) < 5e8.
+template <int QT>
+__device__ __forceinline__ void sb_q45(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
+                                       const uint8_t* __restrict__ bq, const uint8_t* __restrict__ mq, int t,
+                                       float (&out)[4], float (&mn)[2]) {
+    const uint8_t* const b[1] = {bq};
+    const uint8_t* const m[1] = {mq};
+    sb_q45m<QT, 1>(r0, r1, b, m, t, reinterpret_cast<float(&)[1][4]>(out), reinterpret_cast<float(&)[1][2]>(mn));
+}
+// Q6_K super-block (ql 128 | qh 64 | 16 int8 scales | f16 d; qwen3moe.cpp:180-202). M0/M1: row g /
+// g+8 of this super-block starts 2 bytes past a 4-byte boundary. Int32 bound per row: sixteen groups
+// of 16 x 32 x 127 x 128 < 1.4e8.
+template <bool M0, bool M1>
+__device__ __forceinline__ void sb_q6(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
+                                      const uint8_t* __restrict__ bq, int t, float (&out)[4]) {
+    const uint8_t* const b[1] = {bq};
+    sb_q6m<M0, M1, 1>(r0, r1, b, t, reinterpret_cast<float(&)[1][4]>(out));
 }
 
 }  // namespace eb
