@@ -369,13 +369,36 @@ __device__ __forceinline__ void kq_load_b(const BP& bf, int sb, int h, const flo
                 for (int st = 0; st < NSET; st++) B.s[ib][q][st] = bf.seg(st, sb * 16 + 8 * h + 2 * q + ib);
     }
 }
+// Operand sources of kq_compute_src: the B fragments (and, for Q4_K/Q5_K, the lane token's per-16 sums)
+// of one task, either held in registers (KqB, loaded ahead by the caller) or read where they are used.
+template <int QT, int NSET>
+struct KqBRegs {
+    const KqB<QT, NSET>& B;
+    __device__ __forceinline__ uint2 l(int cc, int st) const { return B.l[cc][st]; }
+    __device__ __forceinline__ uint2 h(int cc, int st) const { return B.h[cc][st]; }
+    __device__ __forceinline__ uint32_t s(int ib, int q, int st) const { return B.s[ib][q][st]; }
+    __device__ __forceinline__ float4 sa() const { return B.sa; }
+    __device__ __forceinline__ float4 sb() const { return B.sb; }
+};
+template <int NSET>
+struct KqBLazy {  // the same values as kq_load_b's, loaded at their use
+    const BPtr<NSET>& bf;
+    int sbk, hh;
+    const float* __restrict__ tsum;
+    __device__ __forceinline__ uint2 l(int cc, int st) const { return bf.blk(st, sbk * 8 + 2 * (2 * hh + cc)); }
+    __device__ __forceinline__ uint2 h(int cc, int st) const { return bf.blk(st, sbk * 8 + 2 * (2 * hh + cc) + 1); }
+    __device__ __forceinline__ uint32_t s(int ib, int q, int st) const { return bf.seg(st, sbk * 16 + 8 * hh + 2 * q + ib); }
+    __device__ __forceinline__ float4 sa() const { return *reinterpret_cast<const float4*>(tsum + 8 * hh); }
+    __device__ __forceinline__ float4 sb() const { return *reinterpret_cast<const float4*>(tsum + 8 * hh + 4); }
+};
 // R: the task's two rows; offsets are relative to the rows' starts (super-block sb at sb * block bytes).
 // Accumulates into out[set][4] the d-scaled int32 sums of rows g, g+8 for this lane's two digit
 // columns, and into mn[2] the group-minimum term of rows g, g+8 for token t (Q4_K/Q5_K, when has_sum:
-// B holds the token's sums).
-template <int QT, int NSET, class R>
-__device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, const KqB<QT, NSET>& B, bool has_sum,
-                                           float (&out)[NSET][4], float (&mn)[2]) {
+// B holds the token's sums). Each 32-k chunk's weight words and B fragments are read right before its
+// MMAs.
+template <int QT, int NSET, class R, class BS>
+__device__ __forceinline__ void kq_compute_src(const R& rows, int sb, int h, int t, const BS& B, bool has_sum,
+                                               float (&out)[NSET][4], float (&mn)[2]) {
     constexpr int BB = block_bytes(QT);
     const int o = sb * BB;
     int acc[NSET][4];
@@ -397,7 +420,8 @@ __device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, 
         if (has_sum) {  // group minimums for token t: dmin * m_g * sum(x of the group)
             const uint32_t m0 = h ? (((H0.w >> 4) & 0x0f0f0f0fu) | ((H0.z >> 2) & 0x30303030u)) : (H0.z & 0x3f3f3f3fu);
             const uint32_t m1 = h ? (((H1.w >> 4) & 0x0f0f0f0fu) | ((H1.z >> 2) & 0x30303030u)) : (H1.z & 0x3f3f3f3fu);
-            const float gs[4] = {B.sa.x + B.sa.y, B.sa.z + B.sa.w, B.sb.x + B.sb.y, B.sb.z + B.sb.w};
+            const float4 sa = B.sa(), sbv = B.sb();
+            const float gs[4] = {sa.x + sa.y, sa.z + sa.w, sbv.x + sbv.y, sbv.z + sbv.w};
             float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -412,44 +436,39 @@ __device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, 
             qh0 = rows.ld64(0, o + 16 + 8 * t);
             qh1 = rows.ld64(1, o + 16 + 8 * t);
         }
-        uint2 w0[2], w1[2];
 #pragma unroll
         for (int cc = 0; cc < 2; cc++) {
             const int c = 2 * h + cc;
             // bytes 8t..8t+7 of chunk c: low nibbles = weights 64c + 8t.., high = 64c + 32 + 8t..
-            w0[cc] = rows.ld64(0, o + QS + 32 * c + 8 * t);
-            w1[cc] = rows.ld64(1, o + QS + 32 * c + 8 * t);
-        }
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-            const int c = 2 * h + cc;
+            const uint2 w0 = rows.ld64(0, o + QS + 32 * c + 8 * t), w1 = rows.ld64(1, o + QS + 32 * c + 8 * t);
             uint32_t lo[4], hi[4];
             if constexpr (QT == T_Q4_K) {
-                lo[0] = w0[cc].x & 0x0f0f0f0fu;
-                lo[1] = w1[cc].x & 0x0f0f0f0fu;
-                lo[2] = w0[cc].y & 0x0f0f0f0fu;
-                lo[3] = w1[cc].y & 0x0f0f0f0fu;
-                hi[0] = w0[cc].x & 0xf0f0f0f0u;
-                hi[1] = w1[cc].x & 0xf0f0f0f0u;
-                hi[2] = w0[cc].y & 0xf0f0f0f0u;
-                hi[3] = w1[cc].y & 0xf0f0f0f0u;
+                lo[0] = w0.x & 0x0f0f0f0fu;
+                lo[1] = w1.x & 0x0f0f0f0fu;
+                lo[2] = w0.y & 0x0f0f0f0fu;
+                lo[3] = w1.y & 0x0f0f0f0fu;
+                hi[0] = w0.x & 0xf0f0f0f0u;
+                hi[1] = w1.x & 0xf0f0f0f0u;
+                hi[2] = w0.y & 0xf0f0f0f0u;
+                hi[3] = w1.y & 0xf0f0f0f0u;
             } else {  // fifth bit from qh: bit 2c for the low nibbles, 2c+1 for the high ones
-                lo[0] = (w0[cc].x & 0x0f0f0f0fu) | (((qh0.x >> (2 * c)) & 0x01010101u) << 4);
-                lo[1] = (w1[cc].x & 0x0f0f0f0fu) | (((qh1.x >> (2 * c)) & 0x01010101u) << 4);
-                lo[2] = (w0[cc].y & 0x0f0f0f0fu) | (((qh0.y >> (2 * c)) & 0x01010101u) << 4);
-                lo[3] = (w1[cc].y & 0x0f0f0f0fu) | (((qh1.y >> (2 * c)) & 0x01010101u) << 4);
-                hi[0] = ((w0[cc].x >> 4) & 0x0f0f0f0fu) | (((qh0.x >> (2 * c + 1)) & 0x01010101u) << 4);
-                hi[1] = ((w1[cc].x >> 4) & 0x0f0f0f0fu) | (((qh1.x >> (2 * c + 1)) & 0x01010101u) << 4);
-                hi[2] = ((w0[cc].y >> 4) & 0x0f0f0f0fu) | (((qh0.y >> (2 * c + 1)) & 0x01010101u) << 4);
-                hi[3] = ((w1[cc].y >> 4) & 0x0f0f0f0fu) | (((qh1.y >> (2 * c + 1)) & 0x01010101u) << 4);
+                lo[0] = (w0.x & 0x0f0f0f0fu) | (((qh0.x >> (2 * c)) & 0x01010101u) << 4);
+                lo[1] = (w1.x & 0x0f0f0f0fu) | (((qh1.x >> (2 * c)) & 0x01010101u) << 4);
+                lo[2] = (w0.y & 0x0f0f0f0fu) | (((qh0.y >> (2 * c)) & 0x01010101u) << 4);
+                lo[3] = (w1.y & 0x0f0f0f0fu) | (((qh1.y >> (2 * c)) & 0x01010101u) << 4);
+                hi[0] = ((w0.x >> 4) & 0x0f0f0f0fu) | (((qh0.x >> (2 * c + 1)) & 0x01010101u) << 4);
+                hi[1] = ((w1.x >> 4) & 0x0f0f0f0fu) | (((qh1.x >> (2 * c + 1)) & 0x01010101u) << 4);
+                hi[2] = ((w0.y >> 4) & 0x0f0f0f0fu) | (((qh0.y >> (2 * c + 1)) & 0x01010101u) << 4);
+                hi[3] = ((w1.y >> 4) & 0x0f0f0f0fu) | (((qh1.y >> (2 * c + 1)) & 0x01010101u) << 4);
             }
             constexpr int LS = QT == T_Q4_K ? 16 : 1;
             const int sl0 = LS * ubyte(s0, 2 * cc), sh0 = ubyte(s0, 2 * cc + 1);
             const int sl1 = LS * ubyte(s1, 2 * cc), sh1 = ubyte(s1, 2 * cc + 1);
 #pragma unroll
             for (int st = 0; st < NSET; st++) {
-                scale_acc(acc[st], imma32(lo[0], lo[1], lo[2], lo[3], B.l[cc][st].x, B.l[cc][st].y), sl0, sl1);
-                scale_acc(acc[st], imma32(hi[0], hi[1], hi[2], hi[3], B.h[cc][st].x, B.h[cc][st].y), sh0, sh1);
+                const uint2 bl = B.l(cc, st), bh = B.h(cc, st);
+                scale_acc(acc[st], imma32(lo[0], lo[1], lo[2], lo[3], bl.x, bl.y), sl0, sl1);
+                scale_acc(acc[st], imma32(hi[0], hi[1], hi[2], hi[3], bh.x, bh.y), sh0, sh1);
             }
         }
     } else {  // Q6_K: half h = 128 weights; ib selects l in [16ib, 16ib+16)
@@ -457,25 +476,22 @@ __device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, 
         d1 = f16_to_f32(rows.ld16(1, o + 208));
         const uint32_t sc0[2] = {rows.ld32(0, o + 192 + 8 * h), rows.ld32(0, o + 196 + 8 * h)};
         const uint32_t sc1[2] = {rows.ld32(1, o + 192 + 8 * h), rows.ld32(1, o + 196 + 8 * h)};
-        uint32_t qa[2][2], qb[2][2], qh[2][2];  // [ib][row]
 #pragma unroll
         for (int ib = 0; ib < 2; ib++) {
             const int q0 = o + 16 * ib + 4 * t;
+            uint32_t qa[2], qb[2], qh[2];  // [row]
 #pragma unroll
             for (int r = 0; r < 2; r++) {
-                qa[ib][r] = rows.ld32(r, q0 + 64 * h);
-                qb[ib][r] = rows.ld32(r, q0 + 64 * h + 32);
-                qh[ib][r] = rows.ld32(r, q0 + 128 + 32 * h);
+                qa[r] = rows.ld32(r, q0 + 64 * h);
+                qb[r] = rows.ld32(r, q0 + 64 * h + 32);
+                qh[r] = rows.ld32(r, q0 + 128 + 32 * h);
             }
-        }
-#pragma unroll
-        for (int ib = 0; ib < 2; ib++) {
             // 6-bit values per byte (low nibble from ql, bits 4-5 from qh; qwen3moe.cpp:187-195),
             // then q - 32 as s8: ((q & 63) + 0x60) ^ 0x80 per byte, carry-free
-            const uint32_t v0[4] = {lop_sel(qa[ib][0], qh[ib][0] << 4, 0x0f0f0f0fu), lop_sel(qb[ib][0], qh[ib][0] << 2, 0x0f0f0f0fu),
-                                    lop_sel(qa[ib][0] >> 4, qh[ib][0], 0x0f0f0f0fu), lop_sel(qb[ib][0] >> 4, qh[ib][0] >> 2, 0x0f0f0f0fu)};
-            const uint32_t v1[4] = {lop_sel(qa[ib][1], qh[ib][1] << 4, 0x0f0f0f0fu), lop_sel(qb[ib][1], qh[ib][1] << 2, 0x0f0f0f0fu),
-                                    lop_sel(qa[ib][1] >> 4, qh[ib][1], 0x0f0f0f0fu), lop_sel(qb[ib][1] >> 4, qh[ib][1] >> 2, 0x0f0f0f0fu)};
+            const uint32_t v0[4] = {lop_sel(qa[0], qh[0] << 4, 0x0f0f0f0fu), lop_sel(qb[0], qh[0] << 2, 0x0f0f0f0fu),
+                                    lop_sel(qa[0] >> 4, qh[0], 0x0f0f0f0fu), lop_sel(qb[0] >> 4, qh[0] >> 2, 0x0f0f0f0fu)};
+            const uint32_t v1[4] = {lop_sel(qa[1], qh[1] << 4, 0x0f0f0f0fu), lop_sel(qb[1], qh[1] << 2, 0x0f0f0f0fu),
+                                    lop_sel(qa[1] >> 4, qh[1], 0x0f0f0f0fu), lop_sel(qb[1] >> 4, qh[1] >> 2, 0x0f0f0f0fu)};
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 const uint32_t a0 = ((v0[q] & 0x3f3f3f3fu) + 0x60606060u) ^ 0x80808080u;
@@ -483,7 +499,7 @@ __device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, 
                 const int gl = 2 * q + ib;  // scale index within the half; segment 8h + gl of the super-block
                 const int sa = sbyte(sc0[gl >> 2], gl & 3), sbb = sbyte(sc1[gl >> 2], gl & 3);
 #pragma unroll
-                for (int st = 0; st < NSET; st++) scale_acc(acc[st], imma16s(a0, a1, B.s[ib][q][st]), sa, sbb);
+                for (int st = 0; st < NSET; st++) scale_acc(acc[st], imma16s(a0, a1, B.s(ib, q, st)), sa, sbb);
             }
         }
     }
@@ -495,13 +511,16 @@ __device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, 
         out[st][3] = fmaf(d1, (float)acc[st][3], out[st][3]);
     }
 }
+template <int QT, int NSET, class R>
+__device__ __forceinline__ void kq_compute(const R& rows, int sb, int h, int t, const KqB<QT, NSET>& B, bool has_sum,
+                                           float (&out)[NSET][4], float (&mn)[2]) {
+    kq_compute_src<QT, NSET>(rows, sb, h, t, KqBRegs<QT, NSET>{B}, has_sum, out, mn);
+}
 // Both steps of one task (tsum: as kq_load_b).
 template <int QT, int NSET, class R>
 __device__ __forceinline__ void kq_task(const R& rows, int sb, int h, const BPtr<NSET>& bf,
                                         const float* __restrict__ tsum, float (&out)[NSET][4], float (&mn)[2]) {
-    KqB<QT, NSET> B;
-    kq_load_b<QT, NSET>(bf, sb, h, tsum, B);
-    kq_compute<QT, NSET>(rows, sb, h, bf.t, B, tsum != nullptr, out, mn);
+    kq_compute_src<QT, NSET>(rows, sb, h, bf.t, KqBLazy<NSET>{bf, sb, h, tsum}, tsum != nullptr, out, mn);
 }
 
 }  // namespace eb
