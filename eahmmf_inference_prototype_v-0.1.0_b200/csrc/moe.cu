@@ -1302,7 +1302,7 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup_fs(MoeArgs 
         const uint8_t* mq = xgs + (size_t)(mt ? tok1 : tok0) * xfg + 16 + (g & 1) * 16 + 4 * t;
         const float ts = t < mc ? *reinterpret_cast<const float*>(xgs + (size_t)(t ? tok1 : tok0) * xfg) : 0.f;
         const uint8_t* stage = sm + pl.stage_off + (size_t)s * pl.stage_bytes;
-#pragma unroll 1
+#pragma unroll 2
         for (int v = 0; v < 4; v++) {
             const int vw = vw0 + v;
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, mn[2] = {0.f, 0.f};
