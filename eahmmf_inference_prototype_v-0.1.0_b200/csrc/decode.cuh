@@ -70,10 +70,12 @@ struct RopeFuse {
 // Attention of nb token rows (split partials in part: nb * n_head * nsplit * (hd + 2) floats, nsplit
 // <= 128), then the merge of each row into att (fp32, [nb x n_head hd]) and into xf (fragment form, the
 // o-projection's activations); with rf.cnt (one row) the attention launch merges into rf.att itself and
-// leaves the fragment form to the o-projection's prologue.
+// leaves the fragment form to the o-projection's prologue. pos_host: state->pos when the host knows it
+// (a prompt pass), else -1; a prompt pass at a known position whose chunks fit the splits runs the
+// chunk-shared kernel (k_attn_chunk), with the same records.
 cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n_head, int n_kv, float scale,
                              const DecodeState* st, int nb, int nsplit, float* part, float* att, const XF& xf,
-                             const RopeFuse& rf, int pos_host, cudaStream_t s);  // pos_host: state->pos if known, else -1
+                             const RopeFuse& rf, int pos_host, cudaStream_t s);
 // blk: nblk float2 of scratch
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s);
 cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s);
