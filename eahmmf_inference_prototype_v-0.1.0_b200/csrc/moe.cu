@@ -487,12 +487,14 @@ __device__ inline RouteSm route_sm_carve(uint8_t* p, int E, int TK, bool with_gr
 // kernels); with r.g_info the group list also stays in shared memory. TEAMS: a few tokens, each ranked
 // by a team of 128 threads (latency); otherwise one warp per token (route_token; throughput).
 // Requires blockDim.x >= E (one thread per expert in the scans).
-// 32 keys, one per lane, sorted descending across the warp (bitonic network); lane i returns the i-th
-// largest.
-__device__ __forceinline__ uint64_t warp_sort_desc(uint64_t key) {
+// Levels K0..K1 (powers of two) of the bitonic sorting network over 32 keys, one per lane. After level k
+// every block of k lanes is sorted, descending when (lane & k) == 0, ascending otherwise; after level 32
+// the warp is sorted descending (lane i holds the i-th largest).
+template <int K0, int K1>
+__device__ __forceinline__ uint64_t warp_bitonic(uint64_t key) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
+    for (int k = K0; k <= K1; k <<= 1) {
 #pragma unroll
         for (int j = k >> 1; j > 0; j >>= 1) {
             const uint64_t o = __shfl_xor_sync(0xffffffffu, key, j);
@@ -502,6 +504,13 @@ __device__ __forceinline__ uint64_t warp_sort_desc(uint64_t key) {
     }
     return key;
 }
+// 32 keys sorted descending across the warp; lane i returns the i-th largest.
+__device__ __forceinline__ uint64_t warp_sort_desc(uint64_t key) { return warp_bitonic<2, 32>(key); }
+// Four descending runs of 8 keys (one per warp of a team) in the lane layout the network has after level
+// 8: run w in lanes 8w..8w+7, reversed (ascending) for odd w. Levels 16 and 32 finish the sort: the
+// result is the same sorted sequence a full sort of the 32 keys gives.
+__device__ __forceinline__ int run8_slot(int w, int i) { return 8 * w + ((w & 1) ? 7 - i : i); }
+__device__ __forceinline__ uint64_t warp_merge_runs8(uint64_t key) { return warp_bitonic<16, 32>(key); }
 
 // The routing of one token (E <= 128, k <= 8) by the block's first four warps, and its work list: the
 // sorting-team ranking (see route_block), then the first warp sorts its k picks by expert id, so that
@@ -529,11 +538,11 @@ __device__ void route_one(const MoeArgs& a, RouteSm r, bool global) {
         const bool isnan_e = tid < E && rv != rv;
         uint64_t key = tid < E && !isnan_e ? ((uint64_t)__float_as_uint(rv) << 32) | (uint32_t)~(uint32_t)tid : 0ull;
         key = warp_sort_desc(key);
-        if (lane < 8) cand[wt * 8 + lane] = key;
+        if (lane < 8) cand[run8_slot(wt, lane)] = key;
         if (__any_sync(0xffffffffu, isnan_e) && lane == 0) *nan_flag = 1;
         team_sync();
         if (wt == 0) {
-            key = warp_sort_desc(cand[lane]);
+            key = warp_merge_runs8(cand[lane]);
             const float rk = __uint_as_float((uint32_t)(key >> 32));
             float tot = 0.f;
             for (int k = 0; k < K; k++) tot += __shfl_sync(0xffffffffu, rk, k);  // rank-order sum
@@ -554,7 +563,9 @@ __device__ void route_one(const MoeArgs& a, RouteSm r, bool global) {
             // the k picks in ascending expert order (id + 1 in the high word, above the empty lanes' 0; the
             // weight travels in the low word)
             uint64_t k2 = lane < K ? ((uint64_t)(uint32_t)(my_e + 1) << 32) | __float_as_uint(my_w) : 0ull;
-            k2 = warp_sort_desc(k2);  // descending: pick i of the ascending order sits in lane K - 1 - i
+            // lanes 0..7 hold every key (the others 0): levels 2..8 sort them descending, so pick i of the
+            // ascending order sits in lane K - 1 - i
+            k2 = warp_bitonic<2, 8>(k2);
             const int i = K - 1 - lane;
             if (lane < K) {
                 const int e = (int)(k2 >> 32) - 1;
@@ -657,8 +668,8 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
         // Sorting teams (E <= 128, k <= 8; the Qwen3 shapes): one team of 128 threads per token, one entry
         // per thread. Key of entry e: (bits of r) << 32 | ~e, so that a larger key ranks first under
         // (r desc, index asc) (r >= 0: its bits order as the floats do); NaN and absent entries key 0.
-        // Each warp sorts its 32 keys (bitonic, descending), the team's four top-8 lists are sorted once
-        // more by the team's first warp: its lanes 0..k-1 hold the top k in rank order.
+        // Each warp sorts its 32 keys (bitonic, descending), the team's four top-8 lists are merged by the
+        // team's first warp (the network's last two levels): its lanes 0..k-1 hold the top k in rank order.
         float* wmax = r.scr + (size_t)team * 80;  // [4] warp maxima, a NaN flag, then 32 candidate keys
         int* nan_flag = reinterpret_cast<int*>(wmax + 4);
         uint64_t* cand = reinterpret_cast<uint64_t*>(wmax + 8);
@@ -677,11 +688,11 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
             const bool isnan_e = tt < E && rv != rv;
             uint64_t key = tt < E && !isnan_e ? ((uint64_t)__float_as_uint(rv) << 32) | (uint32_t)~(uint32_t)tt : 0ull;
             key = warp_sort_desc(key);
-            if (lane < 8) cand[wt * 8 + lane] = key;
+            if (lane < 8) cand[run8_slot(wt, lane)] = key;
             if (__any_sync(0xffffffffu, isnan_e) && lane == 0) *nan_flag = 1;
             team_sync();
             if (wt == 0) {
-                key = warp_sort_desc(cand[lane]);
+                key = warp_merge_runs8(cand[lane]);
                 const float rk = __uint_as_float((uint32_t)(key >> 32));
                 float tot = 0.f;
                 for (int k = 0; k < K; k++) tot += __shfl_sync(0xffffffffu, rk, k);  // rank-order sum
