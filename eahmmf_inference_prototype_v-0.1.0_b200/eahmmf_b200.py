@@ -228,17 +228,21 @@ class Engine:
         if not h:
             raise RuntimeError(f"eahmmf_engine_load: {err.value.decode()}")
         self._h = h
+        self._free = L.eahmmf_engine_free  # held here: module globals may be gone when __del__ runs at exit
         d = np.zeros(11, np.int32)
         L.eahmmf_engine_dims(h, d.ctypes.data)
         self.dims = dict(zip(self.DIM_NAMES, (int(v) for v in d)))
 
     def close(self) -> None:
         if getattr(self, "_h", None):
-            lib().eahmmf_engine_free(self._h)
+            self._free(self._h)
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library or the CUDA context may already be gone
+            pass
 
     def eval(self, toks, p0: int = 0, n_batch: int = 32, want_logits: bool = True):
         t = np.ascontiguousarray(toks, np.int32)
