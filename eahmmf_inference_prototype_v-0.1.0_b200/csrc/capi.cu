@@ -290,7 +290,7 @@ extern "C" size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T
 namespace {
 // The MoE block for a ragged batch of T >= GROUPED_MIN_T tokens as grouped tensor-core GEMMs.
 int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x, uint8_t* ws,
-                cudaStream_t st, int* d_status) {
+                cudaStream_t st, int* d_status, const int* given) {
     const GroupedLayout w = grouped_layout(L, T);
     const int K = L->n_used, E = L->n_expert, S = T * K;
     MoeArgs a{};
@@ -320,6 +320,7 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     a.rw.token_slots = reinterpret_cast<int*>(ws + w.token_slots);
     a.y = reinterpret_cast<float*>(ws + w.y);
     a.status = d_status;
+    a.given = given;
     int* cnt = reinterpret_cast<int*>(ws + w.cnt);
     int* local = reinterpret_cast<int*>(ws + w.local);
     int* tiles_gu = reinterpret_cast<int*>(ws + w.tiles_gu);
@@ -354,7 +355,7 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g.y = a.y;
     g.status = d_status;
     g_prof.mark(0, st);
-    if (d_logits) {
+    if (d_logits || given) {
         a.logits = d_logits;
     } else {
         float* lg = reinterpret_cast<float*>(ws + w.logits);
@@ -379,19 +380,21 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
 }
 }  // namespace
 
-namespace eb {
-// eahmmf_cuda_moe_layer with an optional deferred combine (engine use): when `defer` is set and the call
-// runs as one 64-token pass, the combine is not launched and defer receives what it needs.
-int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
-                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
-                  const float* norm_w, float eps) {
+namespace {
+// The MoE block (eahmmf_cuda_moe_layer) with an optional deferred combine (engine use: when `defer` is
+// set and the call runs as one 64-token pass, the combine is not launched and defer receives what it
+// needs), or, with `given`, on assigned experts instead of a routing of logits (eahmmf_cuda_moe_experts).
+int moe_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x, void* d_workspace,
+            size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer, const float* norm_w, float eps,
+            const int* given) {
     // norm_w: d_xn is the un-normalised residual and the RMSNorm is applied inside the router launch
     // (only for the fused small-batch path: T <= FUSED_ROUTE_TMAX, router matrix present)
-    if (norm_w && (T > FUSED_ROUTE_TMAX || d_logits || !L || !L->d_router)) return ST_BAD_ARG;
+    if (norm_w && (T > FUSED_ROUTE_TMAX || d_logits || given || !L || !L->d_router)) return ST_BAD_ARG;
     if (!layer_ok(L)) return (L && !(is_kquant(L->gate_type) && is_kquant(L->up_type) && is_kquant(L->down_type)))
                                   ? ST_BAD_TYPE
                                   : ST_BAD_ARG;
-    if (T < 1 || !d_xn || !d_x || !d_workspace || (!d_logits && !L->d_router)) return ST_BAD_ARG;
+    if (T < 1 || !d_xn || !d_x || !d_workspace || (!d_logits && !given && !L->d_router)) return ST_BAD_ARG;
+    if (given && (L->n_used != 1 || defer)) return ST_BAD_ARG;
     if (reinterpret_cast<uintptr_t>(d_xn) & 15 || reinterpret_cast<uintptr_t>(d_x) & 7 ||
         reinterpret_cast<uintptr_t>(d_workspace) & 255)
         return ST_BAD_ARG;
@@ -399,7 +402,7 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
     uint8_t* ws = static_cast<uint8_t*>(d_workspace);
     if (grouped_ok(L, T)) {
         if (workspace_bytes < grouped_layout(L, T).total) return ST_CAPACITY;
-        return moe_grouped(L, T, d_xn, d_logits, d_x, ws, st, d_status);
+        return moe_grouped(L, T, d_xn, d_logits, d_x, ws, st, d_status, given);
     }
     const WsLayout w = ws_layout(L, T);
     if (workspace_bytes < w.total) return ST_CAPACITY;
@@ -438,10 +441,13 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
         a.status = d_status;
         // up to FUSED_ROUTE_TMAX tokens: the XF prep rides on the router launch (or a prep launch) and the
         // gate/up kernel routes by itself; larger blocks go through k_moe_route
-        a.fused_route = tc <= FUSED_ROUTE_TMAX ? 1 : 0;
+        a.fused_route = tc <= FUSED_ROUTE_TMAX && !given ? 1 : 0;
         a.gsz = a.fused_route ? MU : GW;  // larger chunks: up to GW of an expert's slots per weight pass
+        a.given = given ? given + (size_t)t0 * K : nullptr;
         g_prof.mark(0, st);
-        if (d_logits) {
+        if (given) {
+            a.logits = nullptr;  // k_moe_route takes the assigned experts and preps the tokens' XF
+        } else if (d_logits) {
             a.logits = d_logits + (size_t)t0 * E;
             if (a.fused_route && launch_prep_x(a.xn, L->D, tc, L->D, a.xf, st) != cudaSuccess) return ST_CUDA;
         } else {
@@ -470,8 +476,41 @@ int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float
     }
     return ST_OK;
 }
+}  // namespace
 
+namespace eb {
+int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
+                  void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
+                  const float* norm_w, float eps) {
+    return moe_run(L, T, d_xn, d_logits, d_x, d_workspace, workspace_bytes, stream, d_status, defer, norm_w, eps,
+                   nullptr);
+}
 }  // namespace eb
+
+namespace {
+// The layer as the assigned-expert entry sees it: one expert per row, no router.
+EahmmfMoeLayer experts_view(const EahmmfMoeLayer* L) {
+    EahmmfMoeLayer v = *L;
+    v.n_used = 1;
+    v.d_router = nullptr;
+    return v;
+}
+}  // namespace
+
+extern "C" size_t eahmmf_cuda_moe_experts_workspace_bytes(const EahmmfMoeLayer* L, int R) {
+    if (!L) return 0;
+    const EahmmfMoeLayer v = experts_view(L);
+    return eahmmf_cuda_moe_workspace_bytes(&v, R);
+}
+
+extern "C" int eahmmf_cuda_moe_experts(const EahmmfMoeLayer* L, int R, const float* d_rows, const int* d_eid,
+                                       float* d_y, void* d_workspace, size_t workspace_bytes, void* stream,
+                                       int* d_status) {
+    if (!L || !d_eid) return ST_BAD_ARG;
+    const EahmmfMoeLayer v = experts_view(L);
+    return moe_run(&v, R, d_rows, nullptr, d_y, d_workspace, workspace_bytes, stream, d_status, nullptr, nullptr, 0.f,
+                   d_eid);
+}
 
 extern "C" int eahmmf_cuda_moe_layer(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits,
                                      float* d_x, void* d_workspace, size_t workspace_bytes, void* stream,

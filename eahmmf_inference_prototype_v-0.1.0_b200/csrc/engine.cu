@@ -272,6 +272,7 @@ struct EahmmfEngine {
     size_t moe_ws_bytes = 0, gemv_ws_bytes = 0;
     int* toks = nullptr;       // device token staging [MAXB]
     int pos_host = -1;         // state->pos during an eval pass (set by eval_dev), -1 otherwise
+    int hpos = 0;              // host copy of state->pos after the work enqueued so far
     int* h_toks = nullptr;     // pinned [MAXB]
     int* status = nullptr;     // device status word
     int* att_cnt = nullptr;    // [n_kv] split counters of the attention launch's fused merge (self-resetting)
@@ -527,6 +528,7 @@ struct EahmmfEngine {
         s.cap_out = n_out_cap;
         s.out = out;
         *h_state = s;
+        hpos = pos;
         return cudaMemcpyAsync(state, h_state, sizeof(DecodeState), cudaMemcpyHostToDevice, st) == cudaSuccess;
     }
     bool ensure_out(int n) {
@@ -833,6 +835,7 @@ struct EahmmfEngine {
             pos_host = -1;
             if (rc != ST_OK) return rc;
             if (launch_advance(state, nb, st) != cudaSuccess) return ST_CUDA;
+            hpos += nb;
         }
         return ST_OK;
     }
@@ -840,6 +843,7 @@ struct EahmmfEngine {
     // One decode step: forward of state->token at state->pos, then the argmax records the next token
     // and advances the position. Captured once, replayed per token.
     int step(bool use_graph) {
+        hpos++;  // the step's argmax advances the position
         if (!use_graph || trace || prof) {
             pn = 0;
             const int rc = forward(&state->token, 1, true);
@@ -942,6 +946,7 @@ extern "C" int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, floa
         cudaStreamSynchronize(e->st) != cudaSuccess)
         return ST_CUDA;
     if (e->h_state->pos + n_steps > e->n_ctx) return ST_BAD_ARG;
+    e->hpos = e->h_state->pos;
     const int have = e->h_state->n_out;
     if (have + n_steps > e->cap_out) {
         // grow the history and re-point the state at it (copying what was recorded)
@@ -968,6 +973,24 @@ extern "C" int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, floa
     if (out && cudaMemcpyAsync(out, e->out + have, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
         return ST_CUDA;
     return e->read_status();
+}
+
+extern "C" int eahmmf_engine_step(EahmmfEngine* e, int token, int* next) {
+    if (!e || !next || token >= e->n_embd_rows) return ST_BAD_ARG;
+    if (e->hpos < 0 || e->hpos >= e->n_ctx) return ST_BAD_ARG;  // no room for the token's KV row
+    if (token >= 0) {
+        e->h_toks[0] = token;
+        if (cudaMemcpyAsync(&e->state->token, e->h_toks, 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess)
+            return ST_CUDA;
+    }
+    int rc = e->step(true);
+    if (rc != ST_OK) return rc;
+    if (cudaMemcpyAsync(e->h_toks + 1, &e->state->token, 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(e->h_toks + 2, e->status, 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess ||
+        cudaStreamSynchronize(e->st) != cudaSuccess)
+        return ST_CUDA;
+    *next = e->h_toks[1];
+    return e->h_toks[2];
 }
 
 extern "C" void eahmmf_engine_trace(EahmmfEngine* e, int enable) {

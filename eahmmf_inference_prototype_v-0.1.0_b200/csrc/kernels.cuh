@@ -83,6 +83,9 @@ struct MoeArgs {
     int gsz;          // slots per work group: MU (small batches, routed in the gate/up kernel) or GW
     int fused_route;  // T <= FUSED_ROUTE_TMAX: k_moe_gateup routes itself (no k_moe_route launch); the
                       // XF of the tokens must already be in xf
+    const int* given; // optional [T*K] expert of every (token, k) slot, taken as routed with weight 1
+                      // instead of a top-k of the logits (unused then; entries < 0 are absent slots,
+                      // K must be 1); needs fused_route = 0
 };
 constexpr int FUSED_ROUTE_TMAX = 8;
 

@@ -619,7 +619,8 @@ __device__ void route_one(const MoeArgs& a, RouteSm r, bool global) {
         }
 }
 
-template <bool TEAMS, int GS = MU>
+// GIVEN: the experts of every slot come from a.given (weight 1, entries < 0 absent) instead of a top-k.
+template <bool TEAMS, int GS = MU, bool GIVEN = false>
 __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     static_assert(GS >= MU && GS <= 32, "group size");
     const int T = a.T, E = a.n_expert, K = a.n_used, tid = threadIdx.x;
@@ -646,11 +647,19 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
             int my_e = 0;
             float my_w = 0.f;
             uint32_t* rk = reinterpret_cast<uint32_t*>(r.scr) + warp * 64;
-            if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
+            if constexpr (GIVEN) {  // assigned experts (expert-parallel receiver): weight 1, no ranking
+                if (lane < K) {
+                    my_e = __ldg(a.given + (size_t)t * K + lane);
+                    my_w = 1.0f;
+                }
+            } else if (E <= 128) route_token<4>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
             else if (E <= 256) route_token<8>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
             else route_token<16>(a.logits + (size_t)t * E, E, K, lane, rk, my_e, my_w);
-            if (lane < K) {
-                if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+            if (GIVEN && lane < K && my_e < 0) {  // an absent slot (padding row of the receiver): no slot
+                r.s_ids[t * K + lane] = -1;
+                if (global) a.rw.ids[(size_t)t * K + lane] = -1;
+            } else if (lane < K) {
+                if (my_e < 0 || my_e >= E) {  // NaN logits or a given id out of range
                     if (global) set_flag(a.status, ST_BAD_INDEX);
                     my_e = 0;
                 }
@@ -917,6 +926,7 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     for (int i = tid; i < T * K; i += blockDim.x) {
         const int t = i / K;
         const int e = r.s_ids[i];
+        if (GIVEN && e < 0) continue;  // absent slot
         const int pos = __popcll(r.mask[e] & ((1ull << t) - 1ull)), sl = r.off[e] + pos;
         const int gi = r.goff[e] + pos / GS;
         if (r.g_tok) r.g_tok[MU * gi + pos % GS] = t;
@@ -931,6 +941,7 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     }
 }
 
+template <bool GIVEN>
 __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     pdl_wait();     // logits and activations come from the previous grids
     pdl_trigger();
@@ -943,7 +954,7 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         return;
     }
     __shared__ __align__(16) uint8_t rsm[route_sm_bytes(MAX_EXPERTS, MOE_TMAX * 32, false) + 16];
-    route_block<false, GW>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
+    route_block<false, GW, GIVEN>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1577,6 +1588,7 @@ __global__ void __launch_bounds__(COMB_NT) k_moe_combine(MoeArgs a) {
     __shared__ float s_w[32];
     const int t = blockIdx.y, K = a.n_used, D = a.D;
     pdl_wait();  // y and the routing come from the previous grids
+    if (a.given && __ldg(a.given + t) < 0) return;  // an absent row (given ids have K == 1)
     if (threadIdx.x < K) {
         const int sl = a.rw.token_slots[t * K + threadIdx.x];
         s_sl[threadIdx.x] = sl;
@@ -1605,6 +1617,7 @@ __global__ void __launch_bounds__(COMB_NT) k_moe_combine(MoeArgs a) {
 // the same for any slot order.
 // ------------------------------------------------------------------------------------------------
 constexpr int BIG_NT = 256;
+template <bool GIVEN>
 __global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict__ cnt, int* __restrict__ local) {
     __shared__ uint32_t s_rk[(BIG_NT / 32) * 64];
     pdl_wait();
@@ -1615,11 +1628,20 @@ __global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict
     int my_e = 0;
     float my_w = 0.f;
     const float* lg = a.logits + (size_t)t * E;
-    if (E <= 128) route_token<4>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+    if constexpr (GIVEN) {  // assigned experts (expert-parallel receiver): weight 1, no ranking
+        if (lane < K) {
+            my_e = __ldg(a.given + (size_t)t * K + lane);
+            my_w = 1.0f;
+        }
+    } else if (E <= 128) route_token<4>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
     else if (E <= 256) route_token<8>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
     else route_token<16>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
     if (lane < K) {
-        if (my_e < 0 || my_e >= E) {  // only reachable with NaN logits
+        if (GIVEN && my_e < 0) {  // an absent slot (padding row of the receiver)
+            a.rw.ids[(size_t)t * K + lane] = -1;
+            return;
+        }
+        if (my_e < 0 || my_e >= E) {  // NaN logits or a given id out of range
             set_flag(a.status, ST_BAD_INDEX);
             my_e = 0;
         }
@@ -1682,6 +1704,7 @@ __global__ void __launch_bounds__(256) k_scatter_big(MoeArgs a, const int* __res
     if (i >= a.T * K) return;
     const int t = i / K;
     const int e = a.rw.ids[i];
+    if (e < 0) return;  // absent slot (given ids only)
     const int slot = a.rw.offsets[e] + local[i];
     a.rw.slot_token[slot] = t;
     a.rw.slot_w[slot] = a.rw.wts[i];
@@ -1719,7 +1742,8 @@ cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st) {
     if (a.T < 1 || a.T > MOE_TMAX || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert ||
         a.D % 256 || a.D % DN_ROWS)
         return cudaErrorInvalidValue;
-    return launch_pdl(k_moe_route, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a);
+    return a.given ? launch_pdl(k_moe_route<true>, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a)
+                   : launch_pdl(k_moe_route<false>, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a);
 }
 
 template <int QG, int QU, int G>
@@ -1794,7 +1818,9 @@ cudaError_t launch_moe_combine(const MoeArgs& a, cudaStream_t st) {
 cudaError_t launch_route_big(const MoeArgs& a, int* cnt, int* local, cudaStream_t st) {
     if (a.T < 1 || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert) return cudaErrorInvalidValue;
     const int per = BIG_NT / 32;
-    return launch_pdl(k_route_big, dim3((a.T + per - 1) / per), dim3(BIG_NT), 0, st, a, cnt, local);
+    const dim3 grid((a.T + per - 1) / per);
+    return a.given ? launch_pdl(k_route_big<true>, grid, dim3(BIG_NT), 0, st, a, cnt, local)
+                   : launch_pdl(k_route_big<false>, grid, dim3(BIG_NT), 0, st, a, cnt, local);
 }
 cudaError_t launch_plan_big(const MoeArgs& a, const int* cnt, int* tiles_gu, int* tiles_dn, cudaStream_t st) {
     if (a.n_expert > 512 || a.FF % 64 || a.D % 128) return cudaErrorInvalidValue;

@@ -58,6 +58,15 @@ EXPORTS = {
                                          C.c_void_p]),
     "eahmmf_cuda_moe_combine": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                           C.c_void_p]),
+    "eahmmf_cuda_moe_experts_workspace_bytes": (C.c_size_t, [C.POINTER(EahmmfMoeLayer), C.c_int]),
+    "eahmmf_cuda_moe_experts": (C.c_int, [C.POINTER(EahmmfMoeLayer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+    "eahmmf_cuda_ep_pack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                      C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "eahmmf_cuda_ep_unpack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_void_p]),
+    "eahmmf_cuda_ep_return": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "eahmmf_engine_step": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
     "eahmmf_engine_load": (C.c_void_p, [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]),
     "eahmmf_engine_free": (None, [C.c_void_p]),
     "eahmmf_engine_dims": (C.c_int, [C.c_void_p, C.c_void_p]),
@@ -205,6 +214,15 @@ class MoeLayer:
             raise RuntimeError("eahmmf_cuda_moe_profile_read failed")
         return us
 
+    def experts_workspace_bytes(self, R: int) -> int:
+        return int(lib().eahmmf_cuda_moe_experts_workspace_bytes(C.byref(self.desc), R))
+
+    def apply_experts(self, R: int, d_rows, d_eid, d_y, d_ws, stream=None, d_status=None) -> int:
+        """eahmmf_cuda_moe_experts: d_y[r] += the output of expert d_eid[r] on d_rows[r] (rows with
+        d_eid[r] < 0 are absent)."""
+        return lib().eahmmf_cuda_moe_experts(C.byref(self.desc), R, _ptr(d_rows), _ptr(d_eid), _ptr(d_y), _ptr(d_ws),
+                                             d_ws.numel() * d_ws.element_size(), _stream(stream), _ptr(d_status))
+
     def routing(self, d_ws, T: int):
         """(ids, weights) of the last call, read from the head of the workspace."""
         n = T * self.K
@@ -266,6 +284,13 @@ class Engine:
         rc = lib().eahmmf_engine_decode(self._h, n_steps, out.ctypes.data, C.byref(ms))
         return rc, out, float(ms.value)
 
+    def step(self, token: int = -1):
+        """One host-driven greedy step (eahmmf_engine_step): token in (negative: the engine's last
+        argmax), next token out. Returns (rc, next)."""
+        nxt = C.c_int(0)
+        rc = lib().eahmmf_engine_step(self._h, int(token), C.byref(nxt))
+        return rc, int(nxt.value)
+
     def trace(self, enable: bool) -> None:
         lib().eahmmf_engine_trace(self._h, 1 if enable else 0)
 
@@ -313,3 +338,26 @@ def moe_combine(d_token_slots, d_slot_w, d_y, d_x, stream=None) -> int:
     K = d_token_slots.numel() // T
     return lib().eahmmf_cuda_moe_combine(T, K, D, _ptr(d_token_slots), _ptr(d_slot_w), _ptr(d_y), _ptr(d_x),
                                          _stream(stream))
+
+
+EP_HDR = 4  # EAHMMF_EP_HDR: header floats before each row of a dispatch buffer
+
+
+def ep_pack(d_ids, d_w, d_xn, K: int, E_loc: int, world: int, cap: int, d_send, d_token_pos, d_pos_w, stream=None,
+            d_status=None) -> int:
+    """eahmmf_cuda_ep_pack: this rank's routed slots (d_ids/d_w [T x K]) into the world x cap dispatch
+    blocks."""
+    T, D = d_xn.shape
+    return lib().eahmmf_cuda_ep_pack(_ptr(d_ids), _ptr(d_w), _ptr(d_xn), T, K, D, E_loc, world, cap, _ptr(d_send),
+                                     _ptr(d_token_pos), _ptr(d_pos_w), _stream(stream), _ptr(d_status))
+
+
+def ep_unpack(d_recv, D: int, world: int, cap: int, d_rows, d_eid, d_src, d_y=None, stream=None) -> int:
+    """eahmmf_cuda_ep_unpack: the received blocks' valid rows compacted to the front (expert -1 after)."""
+    return lib().eahmmf_cuda_ep_unpack(_ptr(d_recv), D, world, cap, _ptr(d_rows), _ptr(d_eid), _ptr(d_src), _ptr(d_y),
+                                       _stream(stream))
+
+
+def ep_return(d_y, d_src, D: int, world: int, cap: int, d_ret, stream=None) -> int:
+    """eahmmf_cuda_ep_return: the valid compact rows' outputs back to their received positions."""
+    return lib().eahmmf_cuda_ep_return(_ptr(d_y), _ptr(d_src), D, world, cap, _ptr(d_ret), _stream(stream))

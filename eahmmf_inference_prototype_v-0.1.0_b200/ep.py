@@ -2,25 +2,32 @@
 dispatched to the ranks that own their routed experts and the expert outputs combined back, over
 torch.distributed all-to-all (NCCL over NVLink on GPUs; gloo on CPU for the host-logic tests).
 
-Per call, on every rank (one process per GPU, each holding its own tokens):
+Per call, on every rank (one process per GPU, each holding its own tokens), with no host synchronisation:
 
-  1. routing of the local tokens (eahmmf_cuda_route_topk: the reference's top-k, qwen3moe.cpp:1011-1023);
-  2. count exchange, then dispatch: each routed (token, k) slot sends its fp32 activation row and the
-     owner-local expert id to rank e // (E / P), slots ordered by destination rank;
-  3. the received rows go through the rank's experts (the MoE block with k = 1 and one-hot logits: the
-     assigned expert's gate/up/SiLU/down with weight exactly 1 added to a zero row, i.e. y itself);
-  4. the outputs return by the inverse all-to-all;
-  5. the weighted combine in ascending expert order into the residual (eahmmf_cuda_moe_combine), the
-     reference's summation order (qwen3moe.cpp:1025-1069).
+  1. routing of the local tokens (the reference's top-k, qwen3moe.cpp:1011-1023);
+  2. pack: each routed (token, k) slot's expert-input row and owner-local expert id go to block
+     e // (E / P) of a dispatch buffer of P blocks of `cap` rows (cap = t_max * k, so no block can
+     overflow); each block's first row carries its count;
+  3. dispatch: one all-to-all of whole blocks (equal splits: no split size needs to reach the host);
+  4. unpack: the received valid rows compacted to the front, their assigned experts beside them;
+  5. the rank's experts applied to those rows directly (no second routing: assigned expert, weight 1);
+  6. return: the outputs scattered back to their received positions, one all-to-all back;
+  7. the weighted combine in ascending expert order into the residual, the reference's summation order
+     (qwen3moe.cpp:1025-1069), reading the returned rows in place.
 
 Every slot's output depends only on its own row, so the result equals the single-GPU layer's up to the
-kernel path (GEMV or grouped) that each rank picks for its batch size.
+kernel path (GEMV or grouped) that each rank picks for the rows it receives.
+
+The stages run on a backend object: `CudaEpBackend` (libeahmmf_b200's kernels, the product) by default.
+Callers can pass any object with the same methods (the CPU tests pass one built on their checker).
 """
 from __future__ import annotations
 
-import numpy as np
 import torch
 import torch.distributed as dist
+
+EP_HDR = 4  # header floats before each row of a dispatch buffer (EAHMMF_EP_HDR)
+STAGE_NAMES = ("route_pack", "dispatch_a2a", "experts", "return_a2a", "combine")
 
 
 def shard(ex, rank: int, world: int):
@@ -35,126 +42,140 @@ def shard(ex, rank: int, world: int):
                            down=ex.down[sl])
 
 
-class _CudaExperts:
-    """Applies each received row's assigned local expert with the device MoE block (k = 1)."""
+class CudaEpBackend:
+    """The exchange and expert stages on the GPU (libeahmmf_b200.so): routing (eahmmf_cuda_route_topk),
+    pack / unpack / return (eahmmf_cuda_ep_*), the rank's experts on assigned rows
+    (eahmmf_cuda_moe_experts) and the expert-ordered combine (eahmmf_cuda_moe_combine)."""
 
-    def __init__(self, local, device):
+    def __init__(self, local, n_used: int, device):
         import eahmmf_b200 as eb
         self.eb = eb
         self.layer = eb.MoeLayer.from_expert_set(local, n_used=1)
-        self.E = local.n_expert
+        self.K = n_used
         self.device = device
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.ws = None
-        self.ws_T = 0
 
-    def __call__(self, rows: torch.Tensor, eid: torch.Tensor) -> torch.Tensor:
-        R = rows.shape[0]
-        y = torch.zeros_like(rows)
-        if R == 0:
-            return y
-        if R > self.ws_T:
-            self.ws = torch.empty(self.layer.workspace_bytes(R), dtype=torch.uint8, device=self.device)
-            self.ws_T = R
-        onehot = torch.full((R, self.E), float("-inf"), dtype=torch.float32, device=self.device)
-        onehot[torch.arange(R, device=self.device), eid.long()] = 0.0
-        rc = self.layer(R, rows.contiguous(), onehot, y, self.ws)
+    def alloc(self, shape, dtype):
+        return torch.empty(shape, dtype=dtype, device=self.device)
+
+    def route(self, logits):
+        return self.eb.route_topk(logits.contiguous(), self.K, d_status=self.status)
+
+    def pack(self, ids, w, xn, E_loc, world, cap, send, token_pos, pos_w):
+        rc = self.eb.ep_pack(ids, w, xn.contiguous(), self.K, E_loc, world, cap, send, token_pos, pos_w,
+                             d_status=self.status)
         if rc:
-            raise RuntimeError(f"eahmmf_cuda_moe_layer returned {rc}")
-        return y
+            raise RuntimeError(f"eahmmf_cuda_ep_pack returned {rc}")
 
+    def unpack(self, recv, D, world, cap, rows, eid, src, y):
+        rc = self.eb.ep_unpack(recv, D, world, cap, rows, eid, src, y)
+        if rc:
+            raise RuntimeError(f"eahmmf_cuda_ep_unpack returned {rc}")
 
-class _CpuExperts:
-    """The same through the CPU oracle (host-logic tests on gloo)."""
-
-    def __init__(self, local):
-        import oracle
-        self.orc = oracle.Oracle()
-        self.local = local
-
-    def __call__(self, rows: torch.Tensor, eid: torch.Tensor) -> torch.Tensor:
+    def apply(self, rows, eid, y):
         R = rows.shape[0]
-        if R == 0:
-            return torch.zeros_like(rows)
-        lx = self.local
-        onehot = np.full((R, lx.n_expert), -np.inf, np.float32)
-        onehot[np.arange(R), eid.numpy()] = 0.0
-        y, _, _ = self.orc.moe_layer(np.zeros((R, lx.D), np.float32), rows.numpy(), onehot, list(lx.gate),
-                                     list(lx.up), list(lx.down), lx.types, lx.row_bytes, 1)
-        return torch.from_numpy(y)
+        need = self.layer.experts_workspace_bytes(R)
+        if self.ws is None or self.ws.numel() < need:
+            self.ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        rc = self.layer.apply_experts(R, rows, eid, y, self.ws, d_status=self.status)
+        if rc:
+            raise RuntimeError(f"eahmmf_cuda_moe_experts returned {rc}")
+
+    def ret(self, y, src, D, world, cap, out):
+        rc = self.eb.ep_return(y, src, D, world, cap, out)
+        if rc:
+            raise RuntimeError(f"eahmmf_cuda_ep_return returned {rc}")
+
+    def combine(self, token_pos, pos_w, back, x):
+        rc = self.eb.moe_combine(token_pos, pos_w, back, x)
+        if rc:
+            raise RuntimeError(f"eahmmf_cuda_moe_combine returned {rc}")
+
+    def check(self) -> int:
+        """Kernel status bits raised so far (0 = none); reads the device status word (synchronises)."""
+        return int(self.status.item())
 
 
 class EpMoeLayer:
     """One MoE layer whose experts are split over the ranks of `group` (rank r owns experts
-    [r E/P, (r+1) E/P)). Call with this rank's tokens: (xn [T x D], logits [T x E], x [T x D] updated
-    in place); returns the routing (ids, weights) of the local tokens."""
+    [r E/P, (r+1) E/P)). `local` holds this rank's experts (an ExpertSet of E/P experts); `t_max` bounds
+    the tokens any rank passes per call (the dispatch blocks hold t_max * k rows). Call with this rank's
+    tokens: (xn [T x D], logits [T x E], x [T x D] updated in place); returns the routing (ids, weights)
+    of the local tokens. `stages` (optional, 6 CUDA events) times the stages of STAGE_NAMES."""
 
-    def __init__(self, ex, n_used: int, group=None, device: torch.device | None = None):
+    def __init__(self, local, n_expert: int, n_used: int, t_max: int, group=None, device=None, backend=None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.E = ex.n_expert
-        self.K = n_used
-        self.D = ex.D
-        self.E_loc = self.E // self.world
+        if n_expert % self.world or local.n_expert != n_expert // self.world:
+            raise ValueError(f"{local.n_expert} local experts do not match {n_expert} over {self.world} ranks")
+        self.E, self.K, self.D, self.E_loc = n_expert, n_used, local.D, local.n_expert
         self.device = device if device is not None else torch.device("cpu")
-        local = shard(ex, self.rank, self.world)
-        self.cuda = self.device.type == "cuda"
-        self.experts = _CudaExperts(local, self.device) if self.cuda else _CpuExperts(local)
+        self.be = backend if backend is not None else CudaEpBackend(local, n_used, self.device)
+        self.t_max = t_max
+        self.cap = t_max * n_used
+        W, cap, D = self.world, self.cap, self.D
+        a = self.be.alloc
+        self.send = a((W * cap * (D + EP_HDR),), torch.float32)
+        self.recv = a((W * cap * (D + EP_HDR),), torch.float32) if W > 1 else self.send
+        self.rows = a((W * cap, D), torch.float32)
+        self.eid = a((W * cap,), torch.int32)
+        self.src = a((W * cap,), torch.int32)
+        self.y = a((W * cap, D), torch.float32)
+        self.ret = a((W * cap, D), torch.float32)
+        self.back = a((W * cap, D), torch.float32) if W > 1 else self.ret
+        self.token_pos = a((t_max, n_used), torch.int32)
+        self.pos_w = a((W * cap,), torch.float32)
 
-    def _route(self, logits: torch.Tensor):
-        if self.cuda:
-            import eahmmf_b200 as eb
-            return eb.route_topk(logits.contiguous(), self.K)
-        import oracle
-        ids, w = oracle.Oracle().route(logits.numpy(), self.K)
-        return torch.from_numpy(ids), torch.from_numpy(w)
+    @classmethod
+    def from_full(cls, ex, n_used: int, t_max: int, group=None, device=None, backend=None):
+        """From the whole layer's ExpertSet (each rank keeps its shard)."""
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        return cls(shard(ex, rank, world), ex.n_expert, n_used, t_max, group=group, device=device, backend=backend)
 
-    def _a2a(self, out, inp, out_splits, in_splits):
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+    def _a2a(self, out, inp):
+        dist.all_to_all_single(out, inp, group=self.group)  # equal splits: one block per rank
 
-    def __call__(self, xn: torch.Tensor, logits: torch.Tensor, x: torch.Tensor):
-        T, D, K, dev = xn.shape[0], self.D, self.K, self.device
-        ids, w = self._route(logits) if T else (torch.zeros((0, K), dtype=torch.int32, device=dev),
-                                                torch.zeros((0, K), dtype=torch.float32, device=dev))
-        S = T * K
-        flat = ids.reshape(-1).long()
-        dest = flat // self.E_loc
-        order = torch.argsort(dest * max(S, 1) + torch.arange(S, device=dev))  # by destination, then slot
-        send_counts = torch.bincount(dest, minlength=self.world)
-        recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, None, None)  # one count per rank
-        send_splits, recv_splits = send_counts.tolist(), recv_counts.tolist()
-        R = int(sum(recv_splits))
-        send_x = xn.index_select(0, order // K).contiguous()
-        send_e = (flat[order] - dest[order] * self.E_loc).to(torch.int32)
-        recv_x = torch.empty((R, D), dtype=xn.dtype, device=dev)
-        recv_e = torch.empty((R,), dtype=torch.int32, device=dev)
-        self._a2a(recv_x, send_x, recv_splits, send_splits)
-        self._a2a(recv_e, send_e, recv_splits, send_splits)
-        y_recv = self.experts(recv_x, recv_e)
-        y_back = torch.empty((S, D), dtype=y_recv.dtype, device=dev)
-        self._a2a(y_back, y_recv.contiguous(), send_splits, recv_splits)
-        y = torch.empty_like(y_back)
-        y[order] = y_back  # slot s = t * K + k
+    def __call__(self, xn: torch.Tensor, logits: torch.Tensor, x: torch.Tensor, stages=None):
+        T, D, K, W, cap = xn.shape[0], self.D, self.K, self.world, self.cap
+        if T > self.t_max:
+            raise ValueError(f"{T} tokens exceed t_max = {self.t_max}")
+
+        def mark(i):
+            if stages:
+                stages[i].record()
+
+        mark(0)
         if T:
-            # each token's slots in ascending expert order, the reference's combine order
-            token_slots = (torch.arange(T, device=dev)[:, None] * K + torch.argsort(ids.long(), dim=1)).to(torch.int32)
-            slot_w = w.reshape(-1).contiguous()
-            if self.cuda:
-                import eahmmf_b200 as eb
-                rc = eb.moe_combine(token_slots.contiguous(), slot_w, y, x)
-                if rc:
-                    raise RuntimeError(f"eahmmf_cuda_moe_combine returned {rc}")
-            else:
-                _combine_cpu(token_slots.numpy(), slot_w.numpy(), y.numpy(), x.numpy())
+            ids, w = self.be.route(logits)
+        else:
+            ids = self.be.alloc((0, K), torch.int32)
+            w = self.be.alloc((0, K), torch.float32)
+        token_pos = self.token_pos[:T]
+        self.be.pack(ids, w, xn, self.E_loc, W, cap, self.send, token_pos, self.pos_w)
+        mark(1)
+        if W > 1:
+            self._a2a(self.recv, self.send)
+        mark(2)
+        self.be.unpack(self.recv, D, W, cap, self.rows, self.eid, self.src, self.y)
+        self.be.apply(self.rows, self.eid, self.y)
+        self.be.ret(self.y, self.src, D, W, cap, self.ret)
+        mark(3)
+        if W > 1:
+            self._a2a(self.back, self.ret)
+        mark(4)
+        if T:
+            self.be.combine(token_pos, self.pos_w, self.back, x)
+        mark(5)
         return ids, w
 
 
-def _combine_cpu(token_slots, slot_w, y, x):
-    T, K = token_slots.shape
-    for t in range(T):
-        acc = np.zeros(x.shape[1], np.float32)
-        for k in range(K):
-            s = token_slots[t, k]
-            acc = (acc + np.float32(slot_w[s]) * y[s]).astype(np.float32)
-        x[t] += acc
+def stage_events(n: int = 6):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def stage_ms(ev) -> dict:
+    """Per-stage milliseconds of one profiled call (waits for its last event)."""
+    ev[-1].synchronize()
+    return {name: float(ev[i].elapsed_time(ev[i + 1])) for i, name in enumerate(STAGE_NAMES)}

@@ -105,6 +105,39 @@ int eahmmf_cuda_route_topk(const float* d_logits, int T, int E, int K, int* d_id
 int eahmmf_cuda_moe_combine(int T, int K, int D, const int* d_token_slots, const float* d_slot_w, const float* d_y,
                             float* d_x, void* stream);
 
+/* The expert application alone, on assigned experts (the expert-parallel receiver; no counterpart in the
+ * reference, whose MoE block routes and applies in one process, qwen3moe.cpp:1025-1067): for every row r
+ * with d_eid[r] >= 0, d_y[r] += down(SiLU(gate x) * (up x)) of expert d_eid[r] over x = d_rows[r], the
+ * same per-row arithmetic as eahmmf_cuda_moe_layer's (no routing, weight 1; zero d_y first to get the
+ * expert output itself). Rows with d_eid[r] < 0 are absent: in no product, d_y[r] untouched.
+ * The router matrix and n_used of L are ignored. Workspace: eahmmf_cuda_moe_experts_workspace_bytes(L, R). */
+size_t eahmmf_cuda_moe_experts_workspace_bytes(const EahmmfMoeLayer* L, int R);
+int eahmmf_cuda_moe_experts(const EahmmfMoeLayer* L, int R, const float* d_rows, const int* d_eid, float* d_y,
+                            void* d_workspace, size_t workspace_bytes, void* stream, int* d_status);
+
+/* Expert-parallel exchange buffers (no counterpart in the reference). A dispatch buffer is `world`
+ * blocks of `cap` rows, block d bound for rank d; a row is EAHMMF_EP_HDR floats of header (word 0: the
+ * destination's local expert id as int bits; word 1 of a block's first row: the block's valid-row count)
+ * and the D floats of the token's expert input. The caller exchanges whole blocks (equal splits of
+ * cap * (D + EAHMMF_EP_HDR) floats, e.g. NCCL all-to-all), so no split size has to reach the host.
+ *  - ep_pack: slot s = t*K + k of this rank's routing (d_ids/d_w [T x K], rank order, global expert ids
+ *    < E_loc * world) goes to rank d_ids[s] / E_loc, at the next row of that block in slot order.
+ *    d_token_pos[t*K + j] receives the position (d * cap + row) of token t's j-th slot by ascending
+ *    expert id, d_pos_w[position] its weight: eahmmf_cuda_moe_combine over the returned rows with these
+ *    gives the reference's expert-ascending sum. Needs cap >= T*K (else EAHMMF_ST_CAPACITY).
+ *  - ep_unpack (receiver): the valid rows of the received blocks, compacted in (source, row) order to
+ *    the front of d_rows [world*cap x D], their experts in d_eid (-1 and zero rows after them), and
+ *    d_src = the received position of each compact row (-1 after). d_y (optional) is zeroed.
+ *  - ep_return: d_ret[d_src[j]] = d_y[j] for the valid compact rows, d_ret being the return buffer
+ *    (world blocks of cap D-float rows) that travels back by the inverse exchange. */
+#define EAHMMF_EP_HDR 4
+int eahmmf_cuda_ep_pack(const int* d_ids, const float* d_w, const float* d_xn, int T, int K, int D, int E_loc,
+                        int world, int cap, float* d_send, int* d_token_pos, float* d_pos_w, void* stream,
+                        int* d_status);
+int eahmmf_cuda_ep_unpack(const float* d_recv, int D, int world, int cap, float* d_rows, int* d_eid, int* d_src,
+                          float* d_y, void* stream);
+int eahmmf_cuda_ep_return(const float* d_y, const int* d_src, int D, int world, int cap, float* d_ret, void* stream);
+
 /* Stage timing of eahmmf_cuda_moe_layer: when enabled, each call records CUDA events on its stream
  * around its four stages (router GEMV, routing + activation prep, gate/up, down + combine) of every
  * 64-token block and waits for them; eahmmf_cuda_moe_profile_read returns the mean stage durations (us)
@@ -183,6 +216,12 @@ int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_prompt, int n
  * each step feeds the last argmax token. device_ms (optional) = device time of the steps (CUDA events
  * on the engine's stream); out (optional) receives the tokens. */
 int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_ms);
+/* One greedy decode step driven from the host, as the reference's generate loop feeds one token per
+ * eval call (qwen3moe.cpp:1294-1310; greedy = first maximum, :1103): `token` (>= 0) is copied in as the
+ * step's input (negative: the engine's own last argmax), one forward pass at the engine's position (the
+ * captured graph), and the argmax is copied back to *next; synchronous. Returns the kernels' status bits
+ * (EAHMMF_ST_BAD_ARG when the context is full). */
+int eahmmf_engine_step(EahmmfEngine* e, int token, int* next);
 /* Routing trace (Engine::trace_routing, qwen3moe.cpp:1021): when enabled, every forward pass appends
  * each layer's top-k ids and weights, layer-major; trace_get copies up to cap entries and returns the
  * total. Tracing runs decode steps without the graph. */

@@ -1,7 +1,8 @@
 """Expert-parallel layer (ep.py) on GPUs: one NCCL rank per visible GPU (at most 2; one rank still runs
-the whole dispatch / all-to-all / combine path), against the CPU oracle over each rank's tokens.
+the whole pack / exchange / assigned-expert / return / combine path), against the CPU oracle over each
+rank's tokens.
 
-Routed ids exact; layer output rel-L2 < 1e-5 where every rank's batch takes the 64-token GEMV path,
+Routed ids exact; layer output rel-L2 < 1e-5 where every rank's received rows take the 64-token GEMV path,
 < 5e-4 where it takes the grouped f16 tensor-core path (>= 256 received rows, >= 16 per local expert).
 """
 import os
@@ -35,7 +36,7 @@ def _rank_main(rank, world, port, T_per, out_path):
     try:
         import ep
         ex = synth.expert_set(D=512, FF=256, n_expert=16, types=(12, 12, 14), seed=21, d_sigma=0.004)
-        layer = ep.EpMoeLayer(ex, n_used=4, device=dev)
+        layer = ep.EpMoeLayer.from_full(ex, n_used=4, t_max=max(T_per), device=dev)
         T = T_per[rank]
         x = synth.activations(T, 512, seed=80 + rank)
         xn = synth.activations(T, 512, seed=90 + rank)
@@ -43,6 +44,7 @@ def _rank_main(rank, world, port, T_per, out_path):
         xt = torch.from_numpy(x.copy()).to(dev)
         ids, w = layer(torch.from_numpy(xn).to(dev), torch.from_numpy(lg).to(dev), xt)
         torch.cuda.synchronize()
+        assert layer.be.check() == 0
         np.savez(out_path + f".{rank}.npz", x=x, xn=xn, lg=lg, y=xt.cpu().numpy(), ids=ids.cpu().numpy(),
                  w=w.cpu().numpy())
     finally:
