@@ -1,35 +1,41 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 expert hot path (one JSON line on stdout, rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|layer]
-    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1: one replica per GPU)
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|layer|ragged|ep]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1: one process per GPU)
 
 Workload `decode` (default; BASELINE config 4, the configuration the headline metric is quoted on):
 greedy batch-1 decode of a Qwen3-30B-A3B-shape model -- 48 layers, hidden 2048, 32 q / 4 kv heads of
 128, 128 experts top-8, intermediate 768, vocab 151936; Q4_K attention/gate/up/embedding, Q6_K
 down/output, F32 router/norms; seeded random weights written as a GGUF (synth.config4_30b) and loaded
-through eahmmf_engine_load. A 512-token random-id prompt is prefilled (untimed), then W decode steps
-warm up and K decode steps are timed. One step = one token = one forward pass (48 layers + output GEMV
-+ argmax), replayed as the captured CUDA graph.
+through eahmmf_engine_load. A 512-token random-id prompt is prefilled (timed apart: `prefill`), then W
+decode steps warm up and K decode steps are timed. One step = one token = one forward pass (48 layers +
+output GEMV + argmax), replayed as the captured CUDA graph.
 
   value     decode tokens/s over all ranks: K * ranks / (device time of the K steps, CUDA events on the
             engine's stream, max over ranks). Each step streams ~2 GB of weights (far above the 126 MB
             L2), so no flush is needed between steps.
-  e2e       eahmmf_engine_greedy through the C ABI with host buffers: the 512-token prompt copied in,
-            prefill, K generated tokens copied out; K / wall time of the call.
+  e2e       the same decode driven from the host through the C ABI (eahmmf_engine_step: token in from
+            pinned memory, one forward pass, next token out, synchronised), after an untimed prefill of
+            the same prompt -- the reference arm's decode follows its prefill the same way.
+            e2e_with_prompt: one eahmmf_engine_greedy call with the prompt inside the timed region.
   roofline  k_moe_gateup (the Q4_K MoE decode kernel the target names) at T = 1: algorithmic bytes
             (the 8 routed experts' gate and up matrices + staged activations + h outputs) / its mean
             duration over every layer of a few eager decode steps (CUDA events around the kernel on
             its stream), against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
   cpu_baseline  the reference engine itself (oracle/_ref, compiled from the reference sources) on the
-            same GGUF, all host threads: decode tokens/s after a short prompt (rank 0 at N = 1).
+            same GGUF and prompt, all host threads (rank 0 at N = 1); its greedy tokens are compared with
+            ours over the steps both produce (tokens_match_reference; exit 1 on a mismatch).
+  ep        the config-5 expert-parallel MoE layer (Qwen3-235B-A22B shape, 32 sequences per step) over
+            the job's N ranks (ep.py: NCCL all-to-all of fixed-capacity blocks), with its stage times.
 
 Workload `layer`: one MoE layer of the same shape on decode batches T = 1..8 (one
 step = eight layer calls, 36 tokens), L2 flushed before every call; value = tokens/s of the layer.
+Workload `ragged` (config 3) and `ep` (config 5 alone) as described at their functions.
 
 --impl reference times the reference CPU implementation alone on the same workload (all host threads).
-Multi-GPU: the path has no exchange step at these configurations; N ranks run N replicas ("replicas
-only", weak scaling); the step time is the maximum over ranks.
+Multi-GPU: the decode path has no exchange step, so N ranks run N replicas (weak scaling, step time the
+maximum over ranks); the `ep` object measures the path that does exchange, over the same N ranks.
 """
 from __future__ import annotations
 
@@ -296,6 +302,7 @@ def layer_ours(args, rank: int, world: int, local: int):
 
 # ---- decode workload (config 4) ----------------------------------------------------------------------
 N_PROMPT = 512
+EXTRA_STEPS = 600  # untimed steps after the timed ones: the clock sampler (100 ms period) sees >= 1 s of decode
 DECODE_CONFIG = {"workload": "config4: Qwen3-30B-A3B-shape greedy batch-1 decode, 48 layers, 512-token prompt",
                  "model": "qwen3moe 30B-A3B shape (synthetic weights)", "layers": 48, "hidden": 2048,
                  "heads": "32q/4kv x 128", "experts": 128, "top_k": 8, "moe_intermediate": 768, "vocab": 151936,
@@ -325,31 +332,44 @@ def decode_prompt(rank: int, n: int = N_PROMPT):
     return synth._rng(4, 0x50, rank).integers(0, 151936, n).astype(np.int32)
 
 
-def cpu_decode(path: str, steps: int, warmup: int, budget_s: float | None):
-    """Reference engine decode tokens/s on the host: a short prompt, then single-token forward passes
-    (Engine::forward through eref_engine_eval), `steps` of them or as many as fit in budget_s."""
+def cpu_decode(path: str, prompt, steps: int, warmup: int, budget_s: float | None):
+    """The reference engine on the host (oracle/_ref, all host threads): the prompt through Engine::eval
+    in 64-token passes (timed apart), its argmax, `warmup` untimed single-token forward passes, then
+    `steps` timed ones -- or, with budget_s, as many more as fit in that many seconds. The reference's
+    own generate loop (qwen3moe.cpp:1294-1310) with greedy selection (first maximum, :1103).
+    Returns a dict: tok_s, cores, steps, prefill_s, ids (the first token, then every step's)."""
     import oracle
     ref = oracle.Reference(threads=os.cpu_count() or 1)
-    n_prompt = 8
-    eng = ref.engine(path, n_prompt + warmup + max(steps, 4096 if budget_s else steps) + 8)
-    prompt = decode_prompt(0, n_prompt)
-    lg = eng.eval(prompt, 0, 32)
-    pos = n_prompt
+    n_ctx = len(prompt) + warmup + max(steps, 512 if budget_s else steps) + 8
+    eng = ref.engine(path, n_ctx)
+    t0 = time.perf_counter()
+    lg = eng.eval(prompt, 0, 64)
+    prefill_s = time.perf_counter() - t0
+    ids = [int(np.argmax(lg))]
+    pos = len(prompt)
     for _ in range(warmup):
-        lg = eng.eval([int(lg.argmax())], pos, 1)
+        lg = eng.eval([ids[-1]], pos, 1)
         pos += 1
+        ids.append(int(np.argmax(lg)))
     t0, done = time.perf_counter(), 0
     while True:
-        lg = eng.eval([int(lg.argmax())], pos, 1)
+        lg = eng.eval([ids[-1]], pos, 1)
         pos += 1
         done += 1
+        ids.append(int(np.argmax(lg)))
         el = time.perf_counter() - t0
-        if (budget_s is None and done >= steps) or (budget_s is not None and el >= budget_s):
+        if done >= steps and (budget_s is None or el >= budget_s):
             break
         if pos >= eng.dims["n_ctx"] - 1:
             break
     eng.close()
-    return done / el, ref.threads, done, n_prompt
+    return {"tok_s": done / el, "cores": ref.threads, "steps": done, "prefill_s": prefill_s, "ids": ids}
+
+
+def first_mismatch(a, b):
+    m = min(len(a), len(b))
+    d = np.nonzero(np.asarray(a[:m]) != np.asarray(b[:m]))[0]
+    return (int(d[0]) if len(d) else None), m
 
 
 def decode_ours(args, rank: int, world: int, local: int, path: str):
@@ -358,7 +378,7 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    n_ctx = N_PROMPT + args.warmup + args.steps + 16
+    n_ctx = N_PROMPT + args.warmup + args.steps + EXTRA_STEPS + 16
     eng = eb.Engine(path, n_ctx)
     prompt = decode_prompt(rank)
 
@@ -368,20 +388,29 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # prefill + first token (untimed), warm-up steps (captures the step graph), then the timed steps
+    # prefill + first token (timed apart, wall clock of the call), warm-up steps (the first captures the
+    # step graph), the timed steps (device events on the engine's stream), then untimed steps so that the
+    # clock sampler covers more than a second of the same decode
+    barrier()
+    t0 = time.perf_counter()
     rc, first, _ = eng.greedy(prompt, 1, 64)
+    prefill_s = time.perf_counter() - t0
     if rc:
         raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
-    rc, warm, _ = eng.decode(args.warmup)
-    if rc:
-        raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
-    barrier()
     with Clocks(local) as clk:
+        rc, warm, _ = eng.decode(args.warmup)
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
+        barrier()
         rc, toks, ms = eng.decode(args.steps)
         barrier()
-    if rc:
-        raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
+        rc, _, _ = eng.decode(EXTRA_STEPS)
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_decode failed: {rc}")
     nodes = eng.graph_nodes()
+    seq = [int(v) for v in np.concatenate([first, warm, toks])]
 
     # per-operation profile of a few eager steps, and the MoE stages inside them
     eng.profile(True)
@@ -393,23 +422,43 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
     eng.profile(False)
     barrier()
 
-    # end to end through the C ABI: host prompt in, K host tokens out
+    # end to end through the C ABI, host-driven as the reference's generate loop: the same prompt
+    # prefilled again (untimed), then per step eahmmf_engine_step -- the input token copied in from
+    # pinned host memory, one forward pass, the next token and the status word copied back
+    rc, lg = eng.eval(prompt, 0, 64)
+    if rc:
+        raise RuntimeError(f"eahmmf_engine_eval failed: {rc}")
+    tok = int(np.argmax(lg))
+    e2e_ids = [tok]
+    for _ in range(args.warmup):
+        rc, tok = eng.step(tok)
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_step failed: {rc}")
+        e2e_ids.append(tok)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        rc, tok = eng.step(tok)
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_step failed: {rc}")
+        e2e_ids.append(tok)
+    e2e_s = time.perf_counter() - t0
+    # and one greedy call with the prompt inside the timed region
+    barrier()
     t0 = time.perf_counter()
     rc, gen, _ = eng.greedy(prompt, args.steps, 64)
-    e2e_s = time.perf_counter() - t0
+    e2e_prompt_s = time.perf_counter() - t0
     if rc:
         raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
-    # the captured-graph steps and the greedy call generate the same sequence
-    seq = np.concatenate([first, warm, toks])[:args.steps]
-    consistent = bool(np.array_equal(gen, seq))
+    consistent = bool(e2e_ids == seq and [int(v) for v in gen] == seq[:args.steps])
     eng.close()
 
     t_ms = ms
     if world > 1:
         import torch.distributed as dist
-        v = torch.tensor([t_ms, e2e_s], dtype=torch.float64, device=dev)
+        v = torch.tensor([t_ms, e2e_s, e2e_prompt_s, prefill_s], dtype=torch.float64, device=dev)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
-        t_ms, e2e_s = float(v[0]), float(v[1])
+        t_ms, e2e_s, e2e_prompt_s, prefill_s = (float(u) for u in v)
     value = args.steps * world / (t_ms * 1e-3)
     peak, peak_kind = peaks()
     gu_us = float(moe_stages[GATEUP_STAGE]) if len(moe_stages) else 0.0
@@ -426,26 +475,45 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
         "vs_baseline": None, "dtype": "u8/s8 tensor-core MMA, s32 -> fp32 accumulate (fp32 activations)",
         "data": "synthetic (seeded random weights, random-id prompt)",
         "config": dict(DECODE_CONFIG, parallelism=f"replicas x{world}"),
-        "e2e": {"value": args.steps * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
-                "d2h_bytes_per_step": args.steps * 4,
-                "step": "one eahmmf_engine_greedy call: 512-token prompt in, prefill in 64-token passes, K tokens out"},
+        "e2e": {"value": args.steps * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8,
+                "step": "eahmmf_engine_step through the C ABI: the input token copied in from pinned host memory, one "
+                        "forward pass, the next token and the status word copied back, synchronised; after an untimed "
+                        "prefill of the same 512-token prompt (the reference arm's timed steps follow its prefill the "
+                        "same way)"},
+        "e2e_with_prompt": {"value": args.steps * world / e2e_prompt_s, "unit": "tok/s",
+                            "h2d_bytes_per_step": N_PROMPT * 4 // args.steps, "d2h_bytes_per_step": 4,
+                            "step": "one eahmmf_engine_greedy call: the 512-token prompt in, prefill in 64-token passes, "
+                                    "K tokens out"},
+        "prefill": {"tok_s": N_PROMPT / prefill_s, "ms": prefill_s * 1e3, "passes": "64-token eval passes + argmax"},
         "gpu_launches": nodes * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if peak else None, "traffic": traffic, "kernel": "k_moe_gateup (T=1)",
                      "peak_source": peak_kind,
                      "timing": "CUDA events around the gate/up kernel on its stream, mean over 4 eager steps x 48 layers"},
         "clocks": clk.summary(),
+        "clocks_window": f"warm-up, the {args.steps} timed steps and {EXTRA_STEPS} more steps of the same decode "
+                         "(the timed steps alone are shorter than the 100 ms sampling period)",
         "decode_ops_us_per_step": ops,
         "tokens_consistent": consistent,
         "moe_stages_us_per_layer": {"router": float(moe_stages[0]), "route": float(moe_stages[1]),
                                     "gateup": float(moe_stages[2]), "down_combine": float(moe_stages[3])}
         if len(moe_stages) else None,
+        "tokens_match_reference": None,
     }
+    if not args.no_ep:
+        line["ep"] = ep_measure(rank, world, local, dev, steps=20, warmup=3, cpu=(rank == 0 and world == 1 and
+                                                                                  not args.no_cpu))
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, cores, n, npr = cpu_decode(path, steps=1, warmup=1, budget_s=args.cpu_seconds)
-        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-                                "sample": f"{n} decode steps of the reference engine (oracle/_ref) on the same GGUF "
-                                          f"after a {npr}-token prompt"}
+        c = cpu_decode(path, prompt, steps=args.steps, warmup=args.warmup, budget_s=args.cpu_seconds)
+        bad, m = first_mismatch(c["ids"], seq)
+        line["tokens_match_reference"] = bad is None
+        line["reference_tokens_compared"] = m
+        line["first_mismatch"] = bad
+        line["cpu_baseline"] = {"value": c["tok_s"], "unit": "tok/s", "cores": c["cores"], "kind": "reference",
+                                "sample": f"{c['steps']} decode steps of the reference engine (oracle/_ref) on the same "
+                                          f"GGUF after the same {N_PROMPT}-token prompt (prefill {c['prefill_s']:.1f} s, "
+                                          f"untimed) and {args.warmup} warm-up steps",
+                                "prefill_tok_s": N_PROMPT / c["prefill_s"]}
     return line
 
 
@@ -599,62 +667,122 @@ def profile_ragged(T: int) -> int:
 
 # ---- expert-parallel workload (config 5) ---------------------------------------------------------------
 EP_SEQS = 32
-EP_CONFIG = {"workload": "config5: Qwen3-235B-A22B-shape MoE layer, expert-parallel decode step",
+EP_CONFIG = {"workload": "config5: Qwen3-235B-A22B-shape MoE layer, expert-parallel decode step of 32 sequences",
              "hidden": 4096, "experts": 128, "top_k": 8, "moe_intermediate": 1536, "gate_up": "Q4_K", "down": "Q6_K",
-             "sequences": EP_SEQS, "tokens_per_step": EP_SEQS,
-             "l2": "not flushed: the routed experts of a step are ~100 MB per rank and change every step"}
+             "sequences": EP_SEQS, "tokens_per_step": EP_SEQS, "layers_of_model": 94,
+             "l2": "not flushed: the routed experts of a step are ~1.3 GB over the ranks and alternate between two "
+                   "token sets"}
+EP_EXPERT_BYTES = 2 * 1536 * 2304 + 4096 * 1260  # one 235B-shape expert: Q4_K gate + up, Q6_K down
 
 
-def ep_ours(args, rank: int, world: int, local: int):
+def ep_measure(rank: int, world: int, local: int, dev, steps: int = 20, warmup: int = 3, cpu: bool = False):
+    """The config-5 expert-parallel MoE layer over the ranks of the job (ep.py: pack, one NCCL all-to-all of
+    fixed-capacity blocks each way, assigned-expert application, expert-ordered combine; no host
+    synchronisation). 32 decode tokens per step split over the ranks; each rank generates only its own
+    128/world experts. Step time = CUDA events around the call on each rank, max over ranks. With `cpu`,
+    the reference CPU MoE block (oracle/_ref) on the same 32 tokens (all experts: world 1 only)."""
     import torch
     import torch.distributed as dist
     import ep
     import synth
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world == 1 and not dist.is_initialized():
+    own = not dist.is_initialized()
+    if own:
         from datetime import timedelta
-        dist.init_process_group("nccl", rank=0, world_size=1, init_method="tcp://127.0.0.1:" + str(29600 + local),
+        port = 29600 + (os.getpid() % 1000)
+        dist.init_process_group("nccl", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{port}",
                                 timeout=timedelta(seconds=120), device_id=dev)
-    ex = synth.expert_set(D=4096, FF=1536, n_expert=128, seed=5, d_sigma=0.002)
-    layer = ep.EpMoeLayer(ex, n_used=8, device=dev)
-    del ex
-    T = EP_SEQS // world + (1 if rank < EP_SEQS % world else 0)
-    nsteps = args.warmup + args.steps
-    xs = [(torch.from_numpy(synth.activations(T, 4096, seed=1000 * s + rank)).to(dev),
-           torch.from_numpy(synth.activations(T, 4096, seed=1000 * s + 500 + rank)).to(dev),
-           torch.from_numpy(synth.router_logits(T, 128, seed=1000 * s + 900 + rank)).to(dev)) for s in range(nsteps)]
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    times = []
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    with Clocks(local) as clk:
-        for s in range(nsteps):
-            x, xn, lg = xs[s]
+    try:
+        E, K, D = 128, 8, 4096
+        if E % world:
+            return {"unavailable": f"{E} experts do not split over {world} ranks"}
+        E_loc = E // world
+        ex = synth.expert_set(D=D, FF=1536, n_expert=E, seed=5, d_sigma=0.002,
+                              experts=range(rank * E_loc, (rank + 1) * E_loc))
+        t_max = -(-EP_SEQS // world)
+        T = EP_SEQS // world + (1 if rank < EP_SEQS % world else 0)
+        layer = ep.EpMoeLayer(ex, E, K, t_max, device=dev)
+        sets = []
+        for s in range(2):  # two token sets, alternating
+            seed = 1000 * s + 31 * rank
+            sets.append(tuple(torch.from_numpy(a).to(dev) for a in (
+                synth.activations(T, D, seed=seed), synth.activations(T, D, seed=seed + 500),
+                synth.router_logits(T, E, seed=seed + 900))))
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        times = []
+        for i in range(warmup + steps):
+            x, xn, lg = sets[i % 2]
             xo = x.clone()
             dist.barrier()
+            torch.cuda.synchronize(dev)
             ev0.record()
             layer(xn, lg, xo)
             ev1.record()
             ev1.synchronize()
-            if s >= args.warmup:
+            if i >= warmup:
                 times.append(ev0.elapsed_time(ev1))
+        if layer.be.check():
+            raise RuntimeError(f"EP kernels raised status {layer.be.check()}")
+        # one call with events between the stages
+        stg = ep.stage_events()
+        x, xn, lg = sets[0]
         dist.barrier()
         torch.cuda.synchronize(dev)
-    t = torch.tensor([float(np.sum(times))], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_ms = float(t[0])
-    value = EP_SEQS * args.steps / (t_ms * 1e-3)
-    line = {"metric": "EP MoE-layer decode tokens/s (config 5, 32 sequences)", "value": value, "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "u8/s8 tensor-core MMA, fp32 activations; fp32 rows over NCCL all-to-all",
-            "data": "synthetic (seeded)", "config": dict(EP_CONFIG, parallelism=f"ep{world}"),
-            "clocks": clk.summary(), "gpu_launches": None}
-    if world == 1 and dist.is_initialized():
-        dist.destroy_process_group()
-    return line
+        layer(xn, lg, x.clone(), stages=stg)
+        st_ms = ep.stage_ms(stg)
+        n_uniq = int(torch.unique(layer.eid[layer.eid >= 0]).numel())
+        v = torch.tensor([float(np.sum(times))] + [st_ms[k] for k in ep.STAGE_NAMES], dtype=torch.float64, device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        t_ms = float(v[0])
+        stages = {k: float(v[1 + i]) for i, k in enumerate(ep.STAGE_NAMES)}
+        peak, peak_kind = peaks()
+        exp_bytes = n_uniq * EP_EXPERT_BYTES
+        achieved = exp_bytes / (st_ms["experts"] * 1e-3) / 1e9 if st_ms["experts"] > 0 else 0.0
+        out = {"metric": "EP MoE-layer decode tokens/s (config 5, 32 sequences per step)",
+               "value": EP_SEQS * steps / (t_ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": steps,
+               "warmup": warmup, "ms_per_step": t_ms / steps, "scaling": "strong",
+               "config": dict(EP_CONFIG, parallelism=f"ep{world}", experts_per_rank=E_loc),
+               "stages_ms_max_over_ranks": stages,
+               "roofline_experts_rank0": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                          "frac": achieved / peak if peak else None, "peak_source": peak_kind,
+                                          "bytes": exp_bytes,
+                                          "what": f"{n_uniq} distinct routed experts' weights on rank 0 / its "
+                                                  "assigned-expert stage (unpack + experts + return)"},
+               "dispatch": "fixed-capacity blocks, one equal-split NCCL all-to-all each way, no host sync"}
+        if cpu and world == 1:
+            import oracle
+            ref = oracle.Reference(threads=os.cpu_count() or 1)
+            x, xn, lg = (a.cpu().numpy() for a in sets[0])
+            args_ = (list(ex.gate), list(ex.up), list(ex.down), ex.types, ex.row_bytes, K)
+            ref.moe_layer(x, xn, lg, *args_)
+            t0, reps = time.perf_counter(), 0
+            while reps < 3 or time.perf_counter() - t0 < 5.0:
+                ref.moe_layer(x, xn, lg, *args_)
+                reps += 1
+            layer_s = (time.perf_counter() - t0) / reps
+            out["cpu_baseline"] = {"value": EP_SEQS / layer_s, "unit": "tok/s", "cores": ref.threads,
+                                   "kind": "reference", "layer_ms": layer_s * 1e3,
+                                   "model_step_ms_extrapolated": 94 * layer_s * 1e3,
+                                   "sample": f"{reps} calls of the reference CPU MoE block (oracle/_ref) on the same "
+                                             "32 tokens; x 94 layers gives the reduced-layer extrapolation of a "
+                                             "235B-shape decode step's MoE time"}
+        return out
+    finally:
+        if own:
+            dist.destroy_process_group()
+
+
+def ep_ours(args, rank: int, world: int, local: int):
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    with Clocks(local) as clk:
+        out = ep_measure(rank, world, local, dev, steps=args.steps, warmup=args.warmup,
+                         cpu=(rank == 0 and world == 1 and not args.no_cpu))
+    out.update({"higher_is_better": True, "vs_baseline": None,
+                "dtype": "u8/s8 tensor-core MMA, fp32 activations; fp32 rows over NCCL all-to-all",
+                "data": "synthetic (seeded)", "clocks": clk.summary(), "gpu_launches": None})
+    return out
 
 
 def profile_decode(n_layer: int) -> int:
@@ -718,7 +846,8 @@ def main():
     ap.add_argument("--workload", choices=("decode", "layer", "ragged", "ep"), default="decode")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (and the reference token check)")
+    ap.add_argument("--no-ep", action="store_true", help="decode: skip the config-5 expert-parallel measurement")
     ap.add_argument("--profile-case", type=int, metavar="T", default=0,
                     help="no timing: run the config-2 layer three times at T tokens (a small case for ncu)")
     ap.add_argument("--profile-ragged", type=int, metavar="T", default=0,
@@ -750,14 +879,18 @@ def main():
         if rank != 0:
             return 0
         path = decode_model(0)
-        v, cores, n, npr = cpu_decode(path, steps=min(args.steps, 24), warmup=1, budget_s=None)
-        line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": 1,
-                "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "fp32 (reference CPU)", "data": "synthetic (seeded random weights, random-id prompt)",
-                "config": dict(DECODE_CONFIG, parallelism="reference CPU", prompt=npr), "impl": "reference",
-                "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-                                 "sample": f"{n} decode steps of the reference engine (oracle/_ref) on the same GGUF "
-                                           f"after a {npr}-token prompt (bounded: the reference takes ~0.2 s/token)"},
+        c = cpu_decode(path, decode_prompt(0), steps=args.steps, warmup=args.warmup, budget_s=None)
+        v = c["tok_s"]
+        line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": c["steps"],
+                "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp32 (reference CPU)",
+                "data": "synthetic (seeded random weights, random-id prompt)",
+                "config": dict(DECODE_CONFIG, parallelism="reference CPU"), "impl": "reference",
+                "cpu_baseline": {"value": v, "unit": "tok/s", "cores": c["cores"], "kind": "reference",
+                                 "sample": f"{c['steps']} decode steps of the reference engine (oracle/_ref) on the "
+                                           f"same GGUF after the same {N_PROMPT}-token prompt (prefill "
+                                           f"{c['prefill_s']:.1f} s, untimed) and {args.warmup} warm-up steps"},
+                "prefill": {"tok_s": N_PROMPT / c["prefill_s"], "ms": c["prefill_s"] * 1e3},
                 "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
@@ -799,6 +932,10 @@ def main():
             dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if line.get("tokens_match_reference") is False:
+        print(f"greedy tokens differ from the reference engine's at step {line.get('first_mismatch')}",
+              file=sys.stderr)
+        return 1
     return 0
 
 

@@ -41,6 +41,9 @@ __global__ void __launch_bounds__(PLAN_NT) k_ep_plan(const int* __restrict__ ids
     __shared__ int run[EP_MAX_WORLD];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, S = T * K, row = D + EAHMMF_EP_HDR;
     if (tid < world) run[tid] = 0;
+    // every position entry starts in range, so that an id the loop rejects (status raised) leaves no
+    // position outside the buffers for the gather and the combine
+    for (int s = tid; s < S; s += PLAN_NT) token_pos[s] = 0;
     __syncthreads();
     for (int base = 0; base < S; base += PLAN_NT) {
         const int s = base + tid;

@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
     pdl_wait();
     pdl_trigger();
     const int slot = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (slot >= S) return;
+    if (slot >= S || slot >= g.offsets[g.E]) return;  // S bounds the grid; absent slots (given ids) hold none
     const int K = MODE == 0 ? g.D : g.FF;
     int lo_ = 0, hi_ = g.E;  // expert of the slot: largest e with offsets[e] <= slot
     while (hi_ - lo_ > 1) {

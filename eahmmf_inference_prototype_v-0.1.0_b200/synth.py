@@ -402,18 +402,21 @@ class ExpertSet:
 
 
 def expert_set(D: int = 2048, FF: int = 768, n_expert: int = 128, types=(Q4_K, Q4_K, Q6_K), seed: int = 2,
-               d_sigma: float = 0.01) -> ExpertSet:
-    """Config 2/3 experts: gate/up [FF x D], down [D x FF], d ~|N(0, d_sigma)| per block."""
+               d_sigma: float = 0.01, experts: range | None = None) -> ExpertSet:
+    """Config 2/3 experts: gate/up [FF x D], down [D x FF], d ~|N(0, d_sigma)| per block. `experts`
+    (optional) generates only that range of the set's experts (an expert-parallel rank's shard): each
+    expert's bytes come from its own seed, so a shard equals the same slice of the whole set."""
     tg, tu, td = types
+    ids = range(n_expert) if experts is None else experts
     comps = []
     for c, (qt, rows, k) in enumerate(((tg, FF, D), (tu, FF, D), (td, D, FF))):
         blck, nb = BLOCK[qt]
         nblk = rows * (k // blck)
-        arr = np.empty((n_expert, nblk * nb), np.uint8)
-        for e in range(n_expert):
-            arr[e] = quant_blocks(qt, nblk, _rng(seed, c, e), d_sigma).reshape(-1)
+        arr = np.empty((len(ids), nblk * nb), np.uint8)
+        for i, e in enumerate(ids):
+            arr[i] = quant_blocks(qt, nblk, _rng(seed, c, e), d_sigma).reshape(-1)
         comps.append(arr)
-    return ExpertSet(D, FF, n_expert, tuple(types), *comps)
+    return ExpertSet(D, FF, len(ids), tuple(types), *comps)
 
 
 def activations(T: int, D: int, seed: int) -> np.ndarray:

@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """Regenerates the golden fixtures in tests/golden/ from the reference itself.
 
-Run in the build container, where the reference tree exists (default /root/reference, or $EAHMMF_REF):
+Run in the build container, where the reference tree exists (default: the directory `reference` beside
+the repository, or $EAHMMF_REF):
 
     make -C oracle ref && python tests/golden/make_fixtures.py
 
@@ -33,7 +34,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 GOLDEN = os.path.join(ROOT, "tests", "golden")
-REF = os.environ.get("EAHMMF_REF", "/root/reference")
+REF = os.environ.get("EAHMMF_REF", os.path.normpath(os.path.join(ROOT, "..", "reference")))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 sys.path.insert(0, os.path.join(ROOT, "eahmmf_inference_prototype_v-0.1.0_b200"))
 
@@ -96,7 +97,7 @@ def main():
         with open(os.path.join(GOLDEN, "fixtures.json"), "w") as f:
             json.dump(meta, f, indent=1, sort_keys=True)
         return
-    meta = {"reference": REF}
+    meta = {"reference": os.path.relpath(REF, ROOT)}
 
     # ---- 1. reference tiny.gguf -----------------------------------------------------------------
     with tempfile.TemporaryDirectory() as td:
