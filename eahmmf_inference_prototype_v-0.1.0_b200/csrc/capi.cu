@@ -442,7 +442,9 @@ int moe_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_lo
         // up to FUSED_ROUTE_TMAX tokens: the XF prep rides on the router launch (or a prep launch) and the
         // gate/up kernel routes by itself; larger blocks go through k_moe_route
         a.fused_route = tc <= FUSED_ROUTE_TMAX && !given ? 1 : 0;
-        a.gsz = a.fused_route ? MU : GW;  // larger chunks: up to GW of an expert's slots per weight pass
+        // larger chunks: up to GW of an expert's slots per weight pass, where those kernels' plans fit
+        a.gsz = a.fused_route ? MU
+                              : moe_chunk_group_size(L->D, L->FF, L->gate_row_bytes, L->up_row_bytes, L->down_row_bytes);
         a.given = given ? given + (size_t)t0 * K : nullptr;
         g_prof.mark(0, st);
         if (given) {

@@ -174,6 +174,9 @@ cudaError_t launch_moe_gateup(const MoeArgs& a, cudaStream_t st);
 // RMSNorm)
 cudaError_t launch_moe_down(const MoeArgs& a, cudaStream_t st, bool combine = true);
 size_t moe_smem_gateup(int D, size_t rbg, size_t rbu);
+// Slots per work group of the chunked (non-fused) MoE path: GW where the wide groups' shared-memory plans
+// fit (the Qwen3-30B shapes), MU otherwise (wider layers such as D 4096 / FF 1536).
+int moe_chunk_group_size(int D, int FF, size_t rbg, size_t rbu, size_t rbd);
 size_t moe_smem_down(int FF, size_t rbd);
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st);
 cudaError_t launch_pack_slots(const GroupedArgs& g, int mode, int S, cudaStream_t st);  // 0: xn rows, 1: h rows

@@ -941,7 +941,7 @@ __device__ void route_block(const MoeArgs& a, RouteSm r, bool global) {
     }
 }
 
-template <bool GIVEN>
+template <bool GIVEN, int GS>
 __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
     pdl_wait();     // logits and activations come from the previous grids
     pdl_trigger();
@@ -954,7 +954,7 @@ __global__ void __launch_bounds__(ROUTE_NT) k_moe_route(MoeArgs a) {
         return;
     }
     __shared__ __align__(16) uint8_t rsm[route_sm_bytes(MAX_EXPERTS, MOE_TMAX * 32, false) + 16];
-    route_block<false, GW, GIVEN>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
+    route_block<false, GS, GIVEN>(a, route_sm_carve(rsm, a.n_expert, a.T * a.n_used, false), true);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1736,14 +1736,24 @@ int max_groups(const MoeArgs& a) {
 }  // namespace
 
 size_t moe_smem_gateup(int D, size_t rbg, size_t rbu) { return gateup_plan(D, rbg, rbu).total; }
+int moe_chunk_group_size(int D, int FF, size_t rbg, size_t rbu, size_t rbd) {
+    const bool wide = gateup_plan(D, rbg, rbu, 0, GW).total <= SMEM_CAP && down_plan(FF, rbd, 0, GW).total <= SMEM_CAP &&
+                      GW * (FF / 8) <= dn_prep_items(GW) * NWC_DN * 32 && (FF >> 4) >= gateup_plan(D, rbg, rbu, 0, GW).S &&
+                      D / DN_ROWS >= down_plan(FF, rbd, 0, GW).S;
+    return wide ? GW : MU;
+}
 size_t moe_smem_down(int FF, size_t rbd) { return down_plan(FF, rbd).total; }
 
 cudaError_t launch_moe_route(const MoeArgs& a, cudaStream_t st) {
     if (a.T < 1 || a.T > MOE_TMAX || a.n_expert > MAX_EXPERTS || a.n_used > 32 || a.n_used > a.n_expert ||
         a.D % 256 || a.D % DN_ROWS)
         return cudaErrorInvalidValue;
-    return a.given ? launch_pdl(k_moe_route<true>, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a)
-                   : launch_pdl(k_moe_route<false>, dim3(1 + a.T), dim3(ROUTE_NT), 0, st, a);
+    const dim3 grid(1 + a.T), block(ROUTE_NT);
+    if (a.gsz == GW)
+        return a.given ? launch_pdl(k_moe_route<true, GW>, grid, block, 0, st, a)
+                       : launch_pdl(k_moe_route<false, GW>, grid, block, 0, st, a);
+    return a.given ? launch_pdl(k_moe_route<true, MU>, grid, block, 0, st, a)
+                   : launch_pdl(k_moe_route<false, MU>, grid, block, 0, st, a);
 }
 
 template <int QG, int QU, int G>

@@ -61,3 +61,45 @@ def test_layer_tables_from_leases(report):
         assert float(m.group(4)) < 1e-5
         assert re.search(rf"^layer {l} released pinned 0$", out, re.M)
     assert re.search(r"^done 1$", out, re.M)
+
+
+# ---- the residency tiers on the device backend (oracle/b200_tier_check) ----------------------------
+TIER_BIN = os.path.join(ROOT, "oracle", "_ref", "b200_tier_check")
+
+
+@pytest.fixture(scope="module")
+def tiers():
+    if not os.path.exists(TIER_BIN):
+        pytest.fail(f"{TIER_BIN} missing: `make -C oracle storecheck` in the build container")
+    r = subprocess.run([TIER_BIN, TINY], capture_output=True, timeout=600, env=dict(os.environ, OMP_NUM_THREADS="4"))
+    assert r.returncode == 0, r.stderr.decode()[-2000:]
+    return r.stdout.decode()
+
+
+def test_tier_matrix_on_b200_device_is_bitwise_baseline(tiers):
+    """Every tier / budget case of the reference suite's matrix (tests/test_eahmmf.cpp:184-219 of the
+    reference) with B200Device as the store's backend: logits, greedy ids and routing trace bitwise equal
+    to the SSD-tier run, invariants hold, no pins left."""
+    cases = re.findall(r"^case (\S+) same (\d) invariants (\d) pinned (\d+) acq (\d+) rel (\d+) ssd_ram (\d+) "
+                       r"ram_vram (\d+) vram_ram (\d+) ram_ssd (\d+) vram_ssd (\d+) fallbacks (\d+)", tiers, re.M)
+    assert len(cases) == 9, tiers[-2000:]
+    by = {c[0]: [int(v) for v in c[1:]] for c in cases}
+    for name, v in by.items():
+        assert v[0] == 1 and v[1] == 1 and v[2] == 0 and v[3] == v[4], (name, v)
+    every = by["vram_2_ram_2_every_path"]
+    assert every[5] > 0 and every[6] > 0 and every[7] > 0 and every[8] > 0  # all four pager paths
+    drop = by["vram_2_ram_1_drop_path"]
+    assert drop[9] > 0 and drop[7] == 0  # VRAM victims dropped to SSD when RAM cannot take them
+    assert by["vram_unlimited"][6] > 0  # experts really went to the device
+
+
+def test_residency_walk_and_faults_on_b200_device(tiers):
+    for name in ("walk_ssd", "walk_ram", "walk_vram", "walk_back_ram", "walk_back_ssd", "walk_invariants"):
+        assert re.search(rf"^check {name} 1$", tiers, re.M), (name, tiers[-1500:])
+    faults = re.findall(r"^fault (\S+) same (\d) migration_failures (\d+) alloc_failures (\d+) fallbacks (\d+) "
+                        r"invariants (\d) pinned (\d+)$", tiers, re.M)
+    assert len(faults) == 3
+    for f in faults:
+        assert f[1] == "1" and f[5] == "1" and f[6] == "0", f
+        assert int(f[2]) + int(f[3]) > 0, f  # the injected faults were seen by the store
+    assert re.search(r"^done 1$", tiers, re.M)
