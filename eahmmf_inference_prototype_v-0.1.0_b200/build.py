@@ -15,8 +15,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libeahmmf_b200.so")
-SOURCES = ["kernels.cu", "moe.cu", "capi.cu", "device.cu", "decode.cu", "engine.cu", "gemm.cu", "ep.cu"]
-HEADERS = ["common.cuh", "kq.cuh", "ksb.cuh", "kernels.cuh", "decode.cuh", "tc.cuh"]
+SOURCES = ["kernels.cu", "moe.cu", "capi.cu", "device.cu", "decode.cu", "engine.cu", "gemm.cu", "ep.cu", "sample.cu"]
+HEADERS = ["common.cuh", "kq.cuh", "ksb.cuh", "kernels.cuh", "decode.cuh", "tc.cuh", "sample.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
          "-ftz=false", "-prec-div=true", "-prec-sqrt=true", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]

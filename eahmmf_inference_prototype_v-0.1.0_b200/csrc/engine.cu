@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "kernels.cuh"
+#include "sample.cuh"
 
 namespace eb {
 int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
@@ -281,6 +282,14 @@ struct EahmmfEngine {
     int* out = nullptr;
     int cap_out = 0;
     cudaGraphExec_t step_graph = nullptr;
+    // token selection: the first maximum (greedy), or the reference's sampler with its random stream
+    bool sampling = false;
+    EahmmfSamplerParams sparams{};
+    EahmmfRng* rng = nullptr;
+    float* u_dev = nullptr;   // [n_ctx + 1] uniform draw of each generated index (device)
+    float* u_host = nullptr;  // pinned staging of the same
+    void* samp_ws = nullptr;
+    int hn_out = 0;           // host copy of state->n_out after the work enqueued so far
     int graph_nodes = 0;
     bool trace = false;
     std::vector<int> trace_ids;
@@ -302,6 +311,8 @@ struct EahmmfEngine {
         if (st) cudaStreamSynchronize(st);
         for (cudaEvent_t v : pev) cudaEventDestroy(v);
         if (step_graph) cudaGraphExecDestroy(step_graph);
+        if (u_host) cudaFreeHost(u_host);
+        if (rng) eahmmf_rng_free(rng);
         for (void* p : allocs) cudaFree(p);
         if (h_toks) cudaFreeHost(h_toks);
         if (h_state) cudaFreeHost(h_state);
@@ -485,8 +496,11 @@ struct EahmmfEngine {
             cudaMemset(status, 0, 4) != cudaSuccess || cudaMemset(att_cnt, 0, n_kv * 4) != cudaSuccess)
             return fail("memset");
         if (cudaHostAlloc((void**)&h_toks, MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
-            cudaHostAlloc((void**)&h_state, sizeof(DecodeState), cudaHostAllocDefault) != cudaSuccess)
+            cudaHostAlloc((void**)&h_state, sizeof(DecodeState), cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc((void**)&u_host, (size_t)(n_ctx + 1) * 4, cudaHostAllocDefault) != cudaSuccess)
             return fail("pinned buffers");
+        if (!dalloc(u_dev, (size_t)(n_ctx + 1) * 4) || !dalloc(samp_ws, sample_ws_bytes(n_vocab)))
+            return fail("sampler buffers");
         if (cudaEventCreate(&ev0) != cudaSuccess || cudaEventCreate(&ev1) != cudaSuccess) return fail("events");
         if (!set_state(0, 0)) return fail("state");
         return cudaDeviceSynchronize() == cudaSuccess || fail("device error after load");
@@ -529,6 +543,7 @@ struct EahmmfEngine {
         s.out = out;
         *h_state = s;
         hpos = pos;
+        hn_out = 0;
         return cudaMemcpyAsync(state, h_state, sizeof(DecodeState), cudaMemcpyHostToDevice, st) == cudaSuccess;
     }
     bool ensure_out(int n) {
@@ -840,25 +855,48 @@ struct EahmmfEngine {
         return ST_OK;
     }
 
+    // The uniform draws of the next m generated indices, from the sampler's stream (the reference draws
+    // one per sampled token, qwen3moe.cpp:1125), into u_dev[hn_out ..]; nothing when greedy.
+    bool prepare_draws(int m) {
+        if (!sampling || sparams.temp <= 0.f || m <= 0) return true;
+        if (hn_out + m > n_ctx + 1) return false;
+        for (int i = 0; i < m; i++) u_host[hn_out + i] = eahmmf_rng_uniform(rng);
+        return cudaMemcpyAsync(u_dev + hn_out, u_host + hn_out, (size_t)m * 4, cudaMemcpyHostToDevice, st) ==
+               cudaSuccess;
+    }
+    // Token selection over `logits` into the state (token, history, position + advance).
+    // The caller has prepared the index's draw (prepare_draws) and advanced hn_out.
+    cudaError_t select(int advance) {
+        if (!sampling) return launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, advance, st);
+        SampleArgs a{};
+        a.logits = logits;
+        a.n = n_vocab;
+        a.p = sparams;
+        a.st = state;
+        a.u_arr = u_dev;
+        a.advance = advance;
+        a.cand = static_cast<uint64_t*>(samp_ws);
+        return launch_sample(a, st);
+    }
+
     // One decode step: forward of state->token at state->pos, then the argmax records the next token
     // and advances the position. Captured once, replayed per token.
     int step(bool use_graph) {
         hpos++;  // the step's argmax advances the position
+        if (!prepare_draws(1)) return ST_CUDA;
+        hn_out++;
         if (!use_graph || trace || prof) {
             pn = 0;
             const int rc = forward(&state->token, 1, true);
             if (rc != ST_OK) return rc;
-            if (launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, 1, st) != cudaSuccess || !mark(9) ||
-                !collect())
-                return ST_CUDA;
+            if (select(1) != cudaSuccess || !mark(9) || !collect()) return ST_CUDA;
             return ST_OK;
         }
         if (!step_graph) {
             cudaGraph_t gr = nullptr;
             if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return ST_CUDA;
             int rc = forward(&state->token, 1, true);
-            if (rc == ST_OK && launch_argmax(logits, n_vocab, amax_blk, amax_nblk, state, 1, st) != cudaSuccess)
-                rc = ST_CUDA;
+            if (rc == ST_OK && select(1) != cudaSuccess) rc = ST_CUDA;
             const cudaError_t ce = cudaStreamEndCapture(st, &gr);
             if (rc != ST_OK || ce != cudaSuccess) {
                 if (gr) cudaGraphDestroy(gr);
@@ -919,8 +957,11 @@ extern "C" int eahmmf_engine_eval(EahmmfEngine* e, const int* toks, int n, int p
     return rc;
 }
 
-extern "C" int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out,
-                                    float* first_logits) {
+namespace {
+// The prompt from position 0, then n_gen tokens chosen by the engine's selection (the first maximum, or
+// the configured sampler), out[0] being the prompt's: the reference's generate loop
+// (qwen3moe.cpp:1294-1310) with the whole prompt in one eval.
+int generate(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out, float* first_logits) {
     if (!e || !prompt || !out || n_prompt < 1 || n_gen < 1 || n_batch < 1 || n_batch > MAXB ||
         n_prompt + n_gen > e->n_ctx)
         return ST_BAD_ARG;
@@ -931,13 +972,43 @@ extern "C" int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_pr
     if (first_logits &&
         cudaMemcpyAsync(first_logits, e->logits, (size_t)e->n_vocab * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
         return ST_CUDA;
-    if (launch_argmax(e->logits, e->n_vocab, e->amax_blk, e->amax_nblk, e->state, 0, e->st) != cudaSuccess) return ST_CUDA;
+    if (!e->prepare_draws(1)) return ST_CUDA;
+    e->hn_out++;
+    if (e->select(0) != cudaSuccess) return ST_CUDA;
     for (int i = 1; i < n_gen; i++) {
         rc = e->step(true);
         if (rc != ST_OK) return rc;
     }
     if (cudaMemcpyAsync(out, e->out, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) return ST_CUDA;
     return e->read_status();
+}
+}  // namespace
+
+extern "C" int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out,
+                                    float* first_logits) {
+    if (e && e->sampling) return ST_BAD_ARG;  // a sampler is configured: eahmmf_engine_generate
+    return generate(e, prompt, n_prompt, n_gen, n_batch, out, first_logits);
+}
+
+extern "C" int eahmmf_engine_generate(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch,
+                                      int* out) {
+    return generate(e, prompt, n_prompt, n_gen, n_batch, out, nullptr);
+}
+
+extern "C" int eahmmf_engine_sampler(EahmmfEngine* e, const EahmmfSamplerParams* p, uint64_t seed) {
+    if (!e) return ST_BAD_ARG;
+    if (p && !sample_ok(*p, e->n_vocab)) return ST_BAD_ARG;
+    if (cudaStreamSynchronize(e->st) != cudaSuccess) return ST_CUDA;
+    if (e->step_graph) {  // the captured step holds the previous selection
+        cudaGraphExecDestroy(e->step_graph);
+        e->step_graph = nullptr;
+        e->graph_nodes = 0;
+    }
+    e->sampling = p != nullptr;
+    if (p) e->sparams = *p;
+    if (e->rng) eahmmf_rng_free(e->rng);
+    e->rng = p ? eahmmf_rng_create(seed) : nullptr;
+    return ST_OK;
 }
 
 extern "C" int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_ms) {
@@ -947,6 +1018,7 @@ extern "C" int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, floa
         return ST_CUDA;
     if (e->h_state->pos + n_steps > e->n_ctx) return ST_BAD_ARG;
     e->hpos = e->h_state->pos;
+    e->hn_out = e->h_state->n_out;
     const int have = e->h_state->n_out;
     if (have + n_steps > e->cap_out) {
         // grow the history and re-point the state at it (copying what was recorded)

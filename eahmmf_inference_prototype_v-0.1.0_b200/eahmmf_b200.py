@@ -20,6 +20,20 @@ ST_OK, ST_BAD_ARG, ST_BAD_TYPE, ST_CUDA, ST_WAIT_TIMEOUT, ST_BAD_INDEX, ST_CAPAC
 _lib = None
 
 
+class EahmmfSamplerParams(C.Structure):
+    _fields_ = [("temp", C.c_float), ("top_p", C.c_float), ("min_p", C.c_float), ("rep", C.c_float),
+                ("top_k", C.c_int), ("rep_n", C.c_int)]
+
+
+# the reference CLI's defaults (qwen3moe.cpp:1091-1092)
+SAMPLER_DEFAULTS = dict(temp=0.7, top_p=0.8, min_p=0.0, rep=1.05, top_k=20, rep_n=64)
+
+
+def sampler_params(**kw) -> EahmmfSamplerParams:
+    p = dict(SAMPLER_DEFAULTS, **kw)
+    return EahmmfSamplerParams(p["temp"], p["top_p"], p["min_p"], p["rep"], p["top_k"], p["rep_n"])
+
+
 class EahmmfMoeLayer(C.Structure):
     _fields_ = [("n_expert", C.c_int), ("n_used", C.c_int), ("D", C.c_int), ("FF", C.c_int),
                 ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
@@ -67,6 +81,14 @@ EXPORTS = {
                                         C.c_void_p, C.c_void_p]),
     "eahmmf_cuda_ep_return": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "eahmmf_engine_step": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    "eahmmf_engine_sampler": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64]),
+    "eahmmf_engine_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "eahmmf_cuda_sample_workspace_bytes": (C.c_size_t, [C.c_int]),
+    "eahmmf_cuda_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_float, C.c_void_p,
+                                     C.c_void_p, C.c_size_t, C.c_void_p]),
+    "eahmmf_rng_create": (C.c_void_p, [C.c_uint64]),
+    "eahmmf_rng_uniform": (C.c_float, [C.c_void_p]),
+    "eahmmf_rng_free": (None, [C.c_void_p]),
     "eahmmf_engine_load": (C.c_void_p, [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]),
     "eahmmf_engine_free": (None, [C.c_void_p]),
     "eahmmf_engine_dims": (C.c_int, [C.c_void_p, C.c_void_p]),
@@ -291,6 +313,19 @@ class Engine:
         rc = lib().eahmmf_engine_step(self._h, int(token), C.byref(nxt))
         return rc, int(nxt.value)
 
+    def sampler(self, seed: int = 0, **params) -> int:
+        """Configure the reference's sampler (eahmmf_engine_sampler): no params = greedy selection; else
+        sampler_params(**params) with its random stream seeded by `seed`."""
+        p = C.byref(sampler_params(**params)) if params else None
+        return lib().eahmmf_engine_sampler(self._h, p, C.c_uint64(seed))
+
+    def generate(self, prompt, n_gen: int, n_batch: int = 32):
+        """eahmmf_engine_generate with the configured selection: (rc, tokens)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_gen, np.int32)
+        rc = lib().eahmmf_engine_generate(self._h, p.ctypes.data, len(p), n_gen, n_batch, out.ctypes.data)
+        return rc, out
+
     def trace(self, enable: bool) -> None:
         lib().eahmmf_engine_trace(self._h, 1 if enable else 0)
 
@@ -361,3 +396,34 @@ def ep_unpack(d_recv, D: int, world: int, cap: int, d_rows, d_eid, d_src, d_y=No
 def ep_return(d_y, d_src, D: int, world: int, cap: int, d_ret, stream=None) -> int:
     """eahmmf_cuda_ep_return: the valid compact rows' outputs back to their received positions."""
     return lib().eahmmf_cuda_ep_return(_ptr(d_y), _ptr(d_src), D, world, cap, _ptr(d_ret), _stream(stream))
+
+
+class Rng:
+    """The reference sampler's random stream (eahmmf_rng_*): std::mt19937_64 seeded as the reference does,
+    one canonical float draw per call."""
+
+    def __init__(self, seed: int):
+        self._h = lib().eahmmf_rng_create(C.c_uint64(seed))
+        self._free = lib().eahmmf_rng_free
+
+    def uniform(self) -> float:
+        return float(lib().eahmmf_rng_uniform(self._h))
+
+    def __del__(self):
+        try:
+            if self._h:
+                self._free(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+def sample(d_logits, d_hist, params: EahmmfSamplerParams, u: float, d_token, d_ws=None, stream=None) -> int:
+    """eahmmf_cuda_sample on one device logits row (penalised in place); the token goes to d_token."""
+    import torch
+    n = d_logits.numel()
+    if d_ws is None:
+        d_ws = torch.empty(int(lib().eahmmf_cuda_sample_workspace_bytes(n)), dtype=torch.uint8, device=d_logits.device)
+    nh = 0 if d_hist is None else d_hist.numel()
+    return lib().eahmmf_cuda_sample(_ptr(d_logits), n, _ptr(d_hist) if nh else None, nh, C.byref(params),
+                                    C.c_float(u), _ptr(d_token), _ptr(d_ws), d_ws.numel(), _stream(stream))

@@ -169,6 +169,36 @@ int eahmmf_cuda_gemv(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_
 int eahmmf_cuda_gemv_static(const uint8_t* d_w, int type, int ne0, int ne1, size_t row_bytes, const float* d_x,
                             int nb, int ldx, float* d_out, int ldo, int accumulate, void* stream);
 
+/* ---- token sampler ---------------------------------------------------------------------------- */
+
+/* Parameters of the reference's Sampler (qwen3moe.cpp:1090-1094; CLI defaults temp 0.7, top_p 0.8,
+ * min_p 0, rep 1.05, top_k 20, rep_n 64). */
+typedef struct EahmmfSamplerParams {
+    float temp, top_p, min_p, rep;
+    int top_k, rep_n;
+} EahmmfSamplerParams;
+
+/* Sampler::sample (qwen3moe.cpp:1095-1130) on the device for one logits row of n entries:
+ *   the repetition penalty over the last rep_n entries of d_hist (each occurrence divides a positive
+ *   logit by rep, multiplies another by it; d_logits is modified in place, as the reference's are);
+ *   temp <= 0: the first maximum; else the top_k largest logits in (value desc, index asc) order,
+ *   p_i = exp((l_i - max) / temp) normalised by their sequential sum, the min-p and top-p cuts, and the
+ *   first i whose running sum reaches r = u * (sum of the kept p), u being the caller's draw of the
+ *   reference's std::uniform_real_distribution<float> from its std::mt19937_64 (eahmmf_rng_uniform).
+ * The token goes to *d_token. Takes 1 <= top_k <= 256 when temp > 0 (else EAHMMF_ST_BAD_ARG) and
+ * n <= 262144. Workspace: eahmmf_cuda_sample_workspace_bytes(n) bytes, 16-byte aligned. Asynchronous. */
+size_t eahmmf_cuda_sample_workspace_bytes(int n);
+int eahmmf_cuda_sample(float* d_logits, int n, const int* d_hist, int n_hist, const EahmmfSamplerParams* p, float u,
+                       int* d_token, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* The reference sampler's random stream: std::mt19937_64 seeded as Sampler::rng.seed(seed)
+ * (qwen3moe.cpp:1231), and one draw of std::uniform_real_distribution<float>(0, 1) -- the canonical
+ * value the reference's uniform_real_distribution(0, total) scales by total. */
+typedef struct EahmmfRng EahmmfRng;
+EahmmfRng* eahmmf_rng_create(uint64_t seed);
+float eahmmf_rng_uniform(EahmmfRng* r);
+void eahmmf_rng_free(EahmmfRng* r);
+
 /* ---- 3. device backend (eahmmf::B200Device) --------------------------------------------------- */
 
 typedef struct EahmmfDev EahmmfDev;
@@ -212,6 +242,16 @@ int eahmmf_engine_eval(EahmmfEngine* e, const int* toks, int n, int p0, int n_ba
  * prompt's logits. first_logits (optional) receives those logits. */
 int eahmmf_engine_greedy(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out,
                          float* first_logits);
+/* Token selection of the engine's generation: p NULL = the first maximum (the default; greedy); else the
+ * reference's sampler with these parameters (eahmmf_cuda_sample's contract, on the device inside every
+ * decode step) and its random stream seeded with `seed` (one draw per generated token, continuing across
+ * generations as the reference's Sampler::rng does). Replaces the captured decode step. */
+int eahmmf_engine_sampler(EahmmfEngine* e, const EahmmfSamplerParams* p, uint64_t seed);
+/* The reference's generate loop (qwen3moe.cpp:1294-1310) with the engine's selection: the prompt from
+ * position 0, then n_gen tokens, out[0] chosen from the prompt's logits; the history the repetition
+ * penalty reads is the tokens generated by this call (hist, :1285, :1301). eahmmf_engine_greedy is this
+ * with the first-maximum selection and returns EAHMMF_ST_BAD_ARG while a sampler is configured. */
+int eahmmf_engine_generate(EahmmfEngine* e, const int* prompt, int n_prompt, int n_gen, int n_batch, int* out);
 /* Continues generation for n_steps tokens from the engine's current state (after eval or greedy):
  * each step feeds the last argmax token. device_ms (optional) = device time of the steps (CUDA events
  * on the engine's stream); out (optional) receives the tokens. */

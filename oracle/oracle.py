@@ -133,7 +133,29 @@ class Reference(_MoeLib):
         lib.eref_engine_trace_get.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         lib.eref_engine_greedy.restype = C.c_int
         lib.eref_engine_greedy.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p, C.c_void_p]
+        lib.eref_sample.restype = C.c_int
+        lib.eref_sample.argtypes = [_f32p, C.c_int, C.c_void_p, C.c_int, C.c_float, C.c_float, C.c_float, C.c_float,
+                                    C.c_int, C.c_int, C.c_uint64]
+        lib.eref_uniform.restype = None
+        lib.eref_uniform.argtypes = [C.c_uint64, C.c_int, _f32p]
+        lib.eref_engine_generate.restype = C.c_int
+        lib.eref_engine_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float,
+                                             C.c_float, C.c_float, C.c_int, C.c_int, C.c_uint64, _i32p]
         self.threads = lib.eref_init(threads)
+
+    def sample(self, logits, hist, temp, top_p, min_p, rep, top_k, rep_n, seed):
+        """Sampler::sample (qwen3moe.cpp:1095-1130) with a stream seeded by `seed`: (token, the penalised
+        logits)."""
+        lg = np.array(logits, np.float32, copy=True)
+        h = np.ascontiguousarray(hist, np.int32)
+        tok = self.lib.eref_sample(lg, len(lg), h.ctypes.data if len(h) else None, len(h), temp, top_p, min_p, rep,
+                                   top_k, rep_n, seed)
+        return int(tok), lg
+
+    def uniform(self, seed: int, n: int) -> np.ndarray:
+        out = np.zeros(n, np.float32)
+        self.lib.eref_uniform(seed, n, out)
+        return out
 
     def matmul(self, w, qtype, ne0, ne1, row_bytes, x):
         x = np.ascontiguousarray(x, np.float32)
@@ -179,6 +201,16 @@ class RefEngine:
         ids, w = np.zeros(n, np.int32), np.zeros(n, np.float32)
         self.lib.eref_engine_trace_get(self.h, ids.ctypes.data, w.ctypes.data, n)
         return ids, w
+
+    def generate(self, prompt, n_gen: int, params: dict, seed: int, n_batch: int = 32):
+        """The reference generate loop with its Sampler (params: temp, top_p, min_p, rep, top_k, rep_n)."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_gen, np.int32)
+        p = params
+        if self.lib.eref_engine_generate(self.h, prompt, len(prompt), n_gen, n_batch, p["temp"], p["top_p"],
+                                         p["min_p"], p["rep"], p["top_k"], p["rep_n"], seed, out):
+            raise RuntimeError("eref_engine_generate failed")
+        return out
 
     def greedy(self, prompt, n_gen: int, n_batch: int = 32):
         prompt = np.ascontiguousarray(prompt, np.int32)

@@ -197,3 +197,58 @@ int eref_engine_greedy(void* h, const int* prompt, int n_prompt, int n_gen, int 
 }
 
 }  // extern "C"
+
+// ---- the reference sampler (qwen3moe.cpp:1090-1130) ------------------------------------------------
+namespace {
+Sampler make_sampler(float temp, float top_p, float min_p, float rep, int top_k, int rep_n, uint64_t seed) {
+    Sampler sp;
+    sp.temp = temp;
+    sp.top_p = top_p;
+    sp.min_p = min_p;
+    sp.rep = rep;
+    sp.top_k = top_k;
+    sp.rep_n = rep_n;
+    sp.rng.seed(seed);  // as main() seeds it (qwen3moe.cpp:1231)
+    return sp;
+}
+}  // namespace
+
+extern "C" {
+// Sampler::sample on one row of n logits (modified in place by the repetition penalty, as there), with
+// the window hist[0 .. n_hist) and a fresh stream seeded with `seed`; returns the token.
+int eref_sample(float* lg, int n, const int* hist, int n_hist, float temp, float top_p, float min_p, float rep,
+                int top_k, int rep_n, uint64_t seed) {
+    Sampler sp = make_sampler(temp, top_p, min_p, rep, top_k, rep_n, seed);
+    std::vector<int> h(hist, hist + n_hist);
+    return sp.sample(lg, n, h);
+}
+
+// n draws of std::uniform_real_distribution<float>(0, 1) from std::mt19937_64 seeded with `seed`.
+void eref_uniform(uint64_t seed, int n, float* out) {
+    std::mt19937_64 g;
+    g.seed(seed);
+    for (int i = 0; i < n; i++) out[i] = std::uniform_real_distribution<float>(0.f, 1.f)(g);
+}
+
+// The generate loop (qwen3moe.cpp:1294-1310) without the tokenizer: the prompt through eval, then per
+// step Sampler::sample over the logits with the generated tokens as history, and that token through a
+// one-token eval; n_gen tokens out. The sampler's stream is seeded with `seed`.
+int eref_engine_generate(void* h, const int* prompt, int n_prompt, int n_gen, int n_batch, float temp, float top_p,
+                         float min_p, float rep, int top_k, int rep_n, uint64_t seed, int* out) {
+    Engine* e = (Engine*)h;
+    if (n_prompt < 1 || n_prompt + n_gen > e->n_ctx || n_batch < 1 || n_batch > MAXB) return -1;
+    Sampler sp = make_sampler(temp, top_p, min_p, rep, top_k, rep_n, seed);
+    std::vector<float> lg(e->n_vocab);
+    std::vector<int> pending(prompt, prompt + n_prompt), hist;
+    int n_past = 0;
+    for (int step = 0; step < n_gen; step++) {
+        e->eval(pending, n_past, n_batch, lg.data());
+        n_past += (int)pending.size();
+        const int tok = sp.sample(lg.data(), e->n_vocab, hist);
+        hist.push_back(tok);
+        out[step] = tok;
+        pending = {tok};
+    }
+    return 0;
+}
+}  // extern "C"
