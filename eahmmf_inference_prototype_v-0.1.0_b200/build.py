@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libeahmmf_b200.so")
-SOURCES = ["kernels.cu", "moe.cu", "capi.cu", "device.cu", "decode.cu", "engine.cu", "gemm.cu", "ep.cu", "sample.cu"]
+SOURCES = ["kernels.cu", "moe.cu", "capi.cu", "device.cu", "decode.cu", "engine.cu", "gemm.cu", "ep.cu", "sample.cu", "verify.cu"]
 HEADERS = ["common.cuh", "kq.cuh", "ksb.cuh", "kernels.cuh", "decode.cuh", "tc.cuh", "sample.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

@@ -25,6 +25,7 @@
 #include <cstring>
 #include <map>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/eahmmf_b200.h"
@@ -37,6 +38,9 @@ namespace eb {
 int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                   void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
                   const float* norm_w, float eps);
+cudaError_t launch_hash64(const uint8_t* const* d_ptrs, const size_t* d_sizes, int n, uint64_t* d_out,
+                          cudaStream_t st);
+uint64_t host_hash64(const uint8_t* p, size_t n);
 }
 using namespace eb;
 
@@ -255,6 +259,14 @@ struct EahmmfEngine {
         EahmmfMoeLayer moe;
     };
     std::vector<Layer> layers;
+    // every expert component in HBM with its place in the file (the residency layer's TensorSlice)
+    struct Slice {
+        const uint8_t* dev;
+        uint64_t file_off;
+        size_t bytes;
+    };
+    std::vector<Slice> slices;
+    std::string path;
     const uint8_t* embd = nullptr;
     int embd_type = 0;
     size_t embd_rb = 0;
@@ -352,6 +364,7 @@ struct EahmmfEngine {
         Gguf g;
         if (!g.open(path)) return fail("gguf: " + g.err);
         if (g.gets("general.architecture") != "qwen3moe") return fail("unsupported architecture (need qwen3moe)");
+        this->path = path;
         const std::string a = "qwen3moe.";
         bool miss = false;
         n_layer = (int)g.geti(a + "block_count", 0, &miss);
@@ -454,7 +467,10 @@ struct EahmmfEngine {
             std::vector<const uint8_t*> ptr(3 * (size_t)n_expert);
             for (int c = 0; c < 3; c++) {
                 const size_t per = ex[c]->row_bytes * (size_t)ex[c]->ne[1];
-                for (int e = 0; e < n_expert; e++) ptr[(size_t)c * n_expert + e] = dptr(ex[c]) + per * e;
+                for (int e = 0; e < n_expert; e++) {
+                    ptr[(size_t)c * n_expert + e] = dptr(ex[c]) + per * e;
+                    slices.push_back(Slice{dptr(ex[c]) + per * e, ex[c]->file_off + per * e, per});
+                }
             }
             const uint8_t** dp = nullptr;
             if (!dalloc(dp, ptr.size() * sizeof(void*)) ||
@@ -1063,6 +1079,54 @@ extern "C" int eahmmf_engine_step(EahmmfEngine* e, int token, int* next) {
         return ST_CUDA;
     *next = e->h_toks[1];
     return e->h_toks[2];
+}
+
+extern "C" int eahmmf_engine_verify(EahmmfEngine* e, int* n_checked, int* n_bad) {
+    if (!e || !n_checked || !n_bad) return ST_BAD_ARG;
+    const int n = (int)e->slices.size();
+    *n_checked = n;
+    *n_bad = 0;
+    if (n == 0) return ST_OK;
+    // device side: one hash per slice, all slices in one launch
+    std::vector<const uint8_t*> hp(n);
+    std::vector<size_t> hs(n);
+    for (int i = 0; i < n; i++) {
+        hp[i] = e->slices[i].dev;
+        hs[i] = e->slices[i].bytes;
+    }
+    void* buf = nullptr;
+    const size_t bytes = (size_t)n * (sizeof(void*) + sizeof(size_t) + 8);
+    if (cudaMalloc(&buf, bytes) != cudaSuccess) return ST_CUDA;
+    auto* dp = static_cast<const uint8_t**>(buf);
+    auto* ds = reinterpret_cast<size_t*>(dp + n);
+    auto* dh = reinterpret_cast<uint64_t*>(ds + n);
+    std::vector<uint64_t> got(n);
+    bool ok = cudaMemcpyAsync(dp, hp.data(), (size_t)n * sizeof(void*), cudaMemcpyHostToDevice, e->st) == cudaSuccess &&
+              cudaMemcpyAsync(ds, hs.data(), (size_t)n * sizeof(size_t), cudaMemcpyHostToDevice, e->st) == cudaSuccess &&
+              launch_hash64(dp, ds, n, dh, e->st) == cudaSuccess &&
+              cudaMemcpyAsync(got.data(), dh, (size_t)n * 8, cudaMemcpyDeviceToHost, e->st) == cudaSuccess;
+    // host side meanwhile: the sources, from the file as it is now, over all host threads
+    Gguf g;
+    std::vector<uint64_t> want(n, 0);
+    const bool src_ok = g.open(e->path.c_str());
+    if (src_ok) {
+        const int nt = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
+        std::vector<std::thread> pool;
+        for (int t = 0; t < nt; t++)
+            pool.emplace_back([&, t]() {
+                for (int i = t; i < n; i += nt) {
+                    const EahmmfEngine::Slice& sl = e->slices[i];
+                    if (sl.file_off + sl.bytes <= g.size) want[i] = host_hash64(g.map + sl.file_off, sl.bytes);
+                }
+            });
+        for (auto& th : pool) th.join();
+    }
+    ok = ok && cudaStreamSynchronize(e->st) == cudaSuccess;
+    cudaFree(buf);
+    if (!ok) return ST_CUDA;
+    if (!src_ok) return ST_BAD_ARG;
+    for (int i = 0; i < n; i++) *n_bad += got[i] != want[i];
+    return ST_OK;
 }
 
 extern "C" void eahmmf_engine_trace(EahmmfEngine* e, int enable) {

@@ -86,6 +86,9 @@ EXPORTS = {
     "eahmmf_cuda_sample_workspace_bytes": (C.c_size_t, [C.c_int]),
     "eahmmf_cuda_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_float, C.c_void_p,
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
+    "eahmmf_engine_verify": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "eahmmf_cuda_hash64": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "eahmmf_hash64": (C.c_uint64, [C.c_void_p, C.c_size_t]),
     "eahmmf_rng_create": (C.c_void_p, [C.c_uint64]),
     "eahmmf_rng_uniform": (C.c_float, [C.c_void_p]),
     "eahmmf_rng_free": (None, [C.c_void_p]),
@@ -326,6 +329,13 @@ class Engine:
         rc = lib().eahmmf_engine_generate(self._h, p.ctypes.data, len(p), n_gen, n_batch, out.ctypes.data)
         return rc, out
 
+    def verify(self):
+        """eahmmf_engine_verify: (rc, components checked, components whose device hash64 differs from
+        the file's)."""
+        n, bad = C.c_int(0), C.c_int(0)
+        rc = lib().eahmmf_engine_verify(self._h, C.byref(n), C.byref(bad))
+        return rc, int(n.value), int(bad.value)
+
     def trace(self, enable: bool) -> None:
         lib().eahmmf_engine_trace(self._h, 1 if enable else 0)
 
@@ -427,3 +437,21 @@ def sample(d_logits, d_hist, params: EahmmfSamplerParams, u: float, d_token, d_w
     nh = 0 if d_hist is None else d_hist.numel()
     return lib().eahmmf_cuda_sample(_ptr(d_logits), n, _ptr(d_hist) if nh else None, nh, C.byref(params),
                                     C.c_float(u), _ptr(d_token), _ptr(d_ws), d_ws.numel(), _stream(stream))
+
+
+def hash64(data) -> int:
+    """eahmmf_hash64 of a host byte buffer (numpy uint8)."""
+    a = np.ascontiguousarray(data, np.uint8)
+    return int(lib().eahmmf_hash64(a.ctypes.data if a.size else None, a.size))
+
+
+def cuda_hash64(d_bufs, stream=None) -> list:
+    """eahmmf_cuda_hash64 over device byte ranges: a list of (torch uint8 tensor, offset, size)."""
+    import torch
+    ptrs = torch.tensor([b.data_ptr() + o for b, o, _ in d_bufs], dtype=torch.int64, device="cuda")
+    sizes = torch.tensor([n for _, _, n in d_bufs], dtype=torch.int64, device="cuda")
+    out = torch.zeros(len(d_bufs), dtype=torch.int64, device="cuda")
+    rc = lib().eahmmf_cuda_hash64(_ptr(ptrs), _ptr(sizes), len(d_bufs), _ptr(out), _stream(stream))
+    if rc:
+        raise RuntimeError(f"eahmmf_cuda_hash64 returned {rc}")
+    return [int(v) & 0xFFFFFFFFFFFFFFFF for v in out.cpu().numpy().tolist()]

@@ -262,6 +262,12 @@ int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_m
  * captured graph), and the argmax is copied back to *next; synchronous. Returns the kernels' status bits
  * (EAHMMF_ST_BAD_ARG when the context is full). */
 int eahmmf_engine_step(EahmmfEngine* e, int token, int* next);
+/* The residency layer's --verify contract (Config::verify, eahmmf.h:203-214: every copy checksummed
+ * against its GGUF source with hash64, eahmmf.h:64-76, :940, :1014) for the engine's HBM copy: the hash64
+ * of every expert component (layers x experts x gate/up/down) computed on the device in one launch, the
+ * source's on the host from the GGUF file as it is now; *n_bad counts the components that differ.
+ * Synchronous; allocates a small table for the launch. */
+int eahmmf_engine_verify(EahmmfEngine* e, int* n_checked, int* n_bad);
 /* Routing trace (Engine::trace_routing, qwen3moe.cpp:1021): when enabled, every forward pass appends
  * each layer's top-k ids and weights, layer-major; trace_get copies up to cap entries and returns the
  * total. Tracing runs decode steps without the graph. */
@@ -277,6 +283,11 @@ int eahmmf_engine_graph_nodes(EahmmfEngine* e);
 #define EAHMMF_ENGINE_PROFILE_CLASSES 10
 int eahmmf_engine_profile(EahmmfEngine* e, int enable);
 int eahmmf_engine_profile_read(EahmmfEngine* e, float* us, int cap);
+
+/* hash64 (eahmmf.h:64-76) of n device byte ranges d_ptrs[i] .. + d_sizes[i] (device arrays) into
+ * d_out[i], one warp per range; and the same on the host. */
+int eahmmf_cuda_hash64(const uint8_t* const* d_ptrs, const size_t* d_sizes, int n, uint64_t* d_out, void* stream);
+uint64_t eahmmf_hash64(const uint8_t* p, size_t n);
 
 /* ---- misc ------------------------------------------------------------------------------------ */
 const char* eahmmf_b200_version(void);

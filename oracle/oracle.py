@@ -136,6 +136,8 @@ class Reference(_MoeLib):
         lib.eref_sample.restype = C.c_int
         lib.eref_sample.argtypes = [_f32p, C.c_int, C.c_void_p, C.c_int, C.c_float, C.c_float, C.c_float, C.c_float,
                                     C.c_int, C.c_int, C.c_uint64]
+        lib.eref_hash64.restype = C.c_uint64
+        lib.eref_hash64.argtypes = [C.c_void_p, C.c_size_t]
         lib.eref_uniform.restype = None
         lib.eref_uniform.argtypes = [C.c_uint64, C.c_int, _f32p]
         lib.eref_engine_generate.restype = C.c_int
@@ -151,6 +153,10 @@ class Reference(_MoeLib):
         tok = self.lib.eref_sample(lg, len(lg), h.ctypes.data if len(h) else None, len(h), temp, top_p, min_p, rep,
                                    top_k, rep_n, seed)
         return int(tok), lg
+
+    def hash64(self, data) -> int:
+        a = np.ascontiguousarray(data, np.uint8)
+        return int(self.lib.eref_hash64(a.ctypes.data if a.size else None, a.size))
 
     def uniform(self, seed: int, n: int) -> np.ndarray:
         out = np.zeros(n, np.float32)

@@ -223,6 +223,9 @@ int eref_sample(float* lg, int n, const int* hist, int n_hist, float temp, float
     return sp.sample(lg, n, h);
 }
 
+// The residency layer's checksum (eahmmf.h:64-76) of a host buffer.
+uint64_t eref_hash64(const uint8_t* p, size_t n) { return eahmmf::hash64(p, n); }
+
 // n draws of std::uniform_real_distribution<float>(0, 1) from std::mt19937_64 seeded with `seed`.
 void eref_uniform(uint64_t seed, int n, float* out) {
     std::mt19937_64 g;
