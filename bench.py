@@ -379,7 +379,15 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     n_ctx = N_PROMPT + args.warmup + args.steps + EXTRA_STEPS + 16
+    t0 = time.perf_counter()
     eng = eb.Engine(path, n_ctx)
+    load_s = time.perf_counter() - t0
+    # the staged copy checked against the file: hash64 of every expert component, on the device
+    t0 = time.perf_counter()
+    vrc, n_checked, n_bad = eng.verify()
+    verify_s = time.perf_counter() - t0
+    if vrc or n_bad:
+        raise RuntimeError(f"eahmmf_engine_verify: rc {vrc}, {n_bad} of {n_checked} expert components differ")
     prompt = decode_prompt(rank)
 
     def barrier():
@@ -485,6 +493,9 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
                             "step": "one eahmmf_engine_greedy call: the 512-token prompt in, prefill in 64-token passes, "
                                     "K tokens out"},
         "prefill": {"tok_s": N_PROMPT / prefill_s, "ms": prefill_s * 1e3, "passes": "64-token eval passes + argmax"},
+        "staging": {"load_s": load_s, "verify_s": verify_s, "components_verified": n_checked, "mismatches": n_bad,
+                    "how": "GGUF mmap -> pinned double buffer -> HBM; hash64 of every expert component on the "
+                           "device against the file's on the host"},
         "gpu_launches": nodes * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if peak else None, "traffic": traffic, "kernel": "k_moe_gateup (T=1)",
@@ -503,6 +514,15 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
     if not args.no_ep:
         line["ep"] = ep_measure(rank, world, local, dev, steps=20, warmup=3, cpu=(rank == 0 and world == 1 and
                                                                                   not args.no_cpu))
+    if not args.no_configs:  # BASELINE configs 2 and 3 on the same ranks (short runs; their own CPU legs)
+        sub = argparse.Namespace(steps=5, warmup=3, no_cpu=args.no_cpu, cpu_seconds=5.0)
+        keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config", "e2e", "roofline",
+                "cpu_baseline", "stages_us", "layer_us_per_step", "dtype")
+        c2 = layer_ours(sub, rank, world, local)
+        line["config2_layer"] = {k: c2[k] for k in keep if k in c2}
+        sub.steps = 3
+        c3 = ragged_ours(sub, rank, world, local)
+        line["config3_ragged"] = {k: c3[k] for k in keep if k in c3}
     if rank == 0 and world == 1 and not args.no_cpu:
         c = cpu_decode(path, prompt, steps=args.steps, warmup=args.warmup, budget_s=args.cpu_seconds)
         bad, m = first_mismatch(c["ids"], seq)
@@ -848,6 +868,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (and the reference token check)")
     ap.add_argument("--no-ep", action="store_true", help="decode: skip the config-5 expert-parallel measurement")
+    ap.add_argument("--no-configs", action="store_true", help="decode: skip the short config-2 and config-3 runs")
     ap.add_argument("--profile-case", type=int, metavar="T", default=0,
                     help="no timing: run the config-2 layer three times at T tokens (a small case for ncu)")
     ap.add_argument("--profile-ragged", type=int, metavar="T", default=0,
