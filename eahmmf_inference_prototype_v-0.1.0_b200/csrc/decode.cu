@@ -123,7 +123,7 @@ __global__ void k_rope_table(const DecodeState* st, const float* __restrict__ in
     const int t = blockIdx.x;
     pdl_wait();
     pdl_trigger();
-    const int p = st->pos + t;
+    const int p = tok_pos(st, t);
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
         const double ang = (double)p * (double)inv_freq[i];
         cs[(size_t)t * half + i] = make_float2((float)cos(ang), (float)sin(ang));
@@ -169,19 +169,20 @@ __global__ void k_qk_rope_kv(const float* __restrict__ qkv, int n_head, int n_kv
     if (gw >= nb * nh) return;
     const int t = gw / nh, h = gw - t * nh;
     const float* src = qkv + (size_t)t * (QD + 2 * KD) + (size_t)h * HD;
-    const int pos = st->pos + t;
+    const int pos = tok_pos(st, t);
+    const size_t row = tok_base(st, t) + (size_t)pos;  // the token's cache row
     float v[PER];
 #pragma unroll
     for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
     if (h >= n_head + n_kv) {  // v head: copied into the cache unchanged
-        float* dst = vc + (size_t)pos * KD + (size_t)(h - n_head - n_kv) * HD;
+        float* dst = vc + row * KD + (size_t)(h - n_head - n_kv) * HD;
 #pragma unroll
         for (int j = 0; j < PER; j++) dst[lane + 32 * j] = v[j];
         return;
     }
     head_norm_rope<HD>(v, h < n_head ? qn : kn, eps, cs + (size_t)t * HALF, lane);  // pairs (e, e + HD/2)
     float* dst = h < n_head ? q_out + (size_t)t * QD + (size_t)h * HD
-                            : kc + (size_t)pos * KD + (size_t)(h - n_head) * HD;
+                            : kc + row * KD + (size_t)(h - n_head) * HD;
 #pragma unroll
     for (int j = 0; j < PER; j++) dst[lane + 32 * j] = v[j];
 }
@@ -388,11 +389,12 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     // the previous grid passed its own wait, and the step's own row is replaced below from the q|k|v row.
     // A prompt pass's rows come from the previous grid (k_qk_rope_kv): its copies start after the wait.
     int np = 0, nch = 0;
+    size_t base = 0;  // first cache row of the token's sequence
     auto stage_chunk = [&](int c) {  // K/V rows of chunk c -> shared memory (cp.async, 16 bytes each)
         const int p0 = c * ATT_CH, n = min(ATT_CH, np - p0);
         for (int i = threadIdx.x; i < n * (HD / 4); i += ATT_NT) {
             const int r = i / (HD / 4), c4 = i - r * (HD / 4);
-            const size_t g = (size_t)(p0 + r) * KD + (size_t)h * HD + 4 * c4;
+            const size_t g = (base + (size_t)(p0 + r)) * KD + (size_t)h * HD + 4 * c4;
             cp_async16(Ks + r * RS + 4 * c4, kc + g);
             cp_async16(Vs + r * RS + 4 * c4, vc + g);
         }
@@ -405,8 +407,9 @@ __global__ void __launch_bounds__(ATT_NT) k_attention(const float* __restrict__ 
     pdl_wait();
     pdl_trigger();
     if (!rf.qkv) {
-        np = st->pos + t + 1;  // causal: positions 0 .. p0 + t
+        np = tok_pos(st, t) + 1;  // causal: positions 0 .. the token's own
         nch = (np + ATT_CH - 1) / ATT_CH;
+        base = tok_base(st, t);
     }
     // splits y >= nch hold no positions of this token: no record (the merges read the first
     // min(nsplit, nch) records only); a single-token step still counts the block for its merge
@@ -733,7 +736,7 @@ __global__ void __launch_bounds__(MP_NT) k_attn_merge_prep(const float* __restri
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, QD = n_head * HD;
-    const int nvalid = min(nsplit, (st->pos + t + ATT_CH) / ATT_CH);  // splits holding positions 0 .. pos + t
+    const int nvalid = min(nsplit, (tok_pos(st, t) + ATT_CH) / ATT_CH);  // splits holding positions 0 .. pos
     for (int hq = warp; hq < n_head; hq += MP_NT / 32) {
         float v[PER];
         merge_head<HD, false, false>(part + ((size_t)t * n_head + hq) * nsplit * (HD + 2), nvalid, v);
@@ -821,6 +824,54 @@ __global__ void __launch_bounds__(ARGMAX_NT) k_argmax(const float* __restrict__ 
         if (st->n_out < st->cap_out) st->out[st->n_out] = bi;
         st->n_out++;
         if (advance) st->pos += 1;
+    }
+}
+
+// One block per row: the first maximum of the row (the order `better` defines), for multi-sequence steps.
+__global__ void __launch_bounds__(ARGMAX_NT) k_argmax_rows(const float* __restrict__ lg, int n, int ld,
+                                                            int* __restrict__ out) {
+    __shared__ float sv[ARGMAX_NT / 32];
+    __shared__ int si[ARGMAX_NT / 32];
+    pdl_wait();
+    pdl_trigger();
+    const float* row = lg + (size_t)blockIdx.x * ld;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += ARGMAX_NT) {
+        const float v = row[i];
+        if (better(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[w] = bv;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        bv = lane < ARGMAX_NT / 32 ? sv[lane] : -INFINITY;
+        bi = lane < ARGMAX_NT / 32 ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
     }
 }
 
@@ -925,6 +976,11 @@ cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s) {
     return launch_pdl(k_argmax, dim3(nblk), dim3(ARGMAX_NT), 0, s, lg, n, blk, st, advance);
 }
+cudaError_t launch_argmax_rows(const float* lg, int n, int ld, int rows, int* out, cudaStream_t s) {
+    if (rows < 1) return cudaSuccess;
+    return launch_pdl(k_argmax_rows, dim3(rows), dim3(ARGMAX_NT), 0, s, lg, n, ld, out);
+}
+
 cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s) {
     return launch_pdl(k_advance, dim3(1), dim3(1), 0, s, st, n);
 }

@@ -23,9 +23,17 @@ struct DecodeState {
     int ticket;   // argmax block counter (reset by the last block)
     int n_out;    // tokens recorded so far
     int cap_out;  // capacity of out
-    int pad;
-    int* out;     // [cap_out] generated tokens
+    int slot_rows;     // cache rows per sequence slot (multi-sequence steps)
+    int* out;          // [cap_out] generated tokens
+    const int* tpos;   // multi-sequence step: [nb] position of each token row (null: pos + t)
+    const int* tslot;  // multi-sequence step: [nb] sequence slot of each row, whose cache rows start at
+                       // slot * slot_rows of the layer's cache (null: the cache passed in, row = position)
 };
+// Position of token row t of a forward pass, and the first cache row of its sequence.
+__device__ __forceinline__ int tok_pos(const DecodeState* st, int t) { return st->tpos ? st->tpos[t] : st->pos + t; }
+__device__ __forceinline__ size_t tok_base(const DecodeState* st, int t) {
+    return st->tslot ? (size_t)st->tslot[t] * (size_t)st->slot_rows : 0;
+}
 
 // Arguments of k_norm_prep: rows t0 .. t0 + rows - 1 of x (row length n, stride ldx); when y is set,
 // first x[t] += sum_k slot_w[s] y[s] over s = token_slots[t*K + k]; then RMSNorm with w, eps; the
@@ -79,5 +87,7 @@ cudaError_t launch_attention(int hd, const float* q, float* kc, float* vc, int n
 // blk: nblk float2 of scratch
 cudaError_t launch_argmax(const float* lg, int n, float2* blk, int nblk, DecodeState* st, int advance, cudaStream_t s);
 cudaError_t launch_advance(DecodeState* st, int n, cudaStream_t s);
+// First maximum of each of `rows` logits rows (n entries each, stride ld) into out[row].
+cudaError_t launch_argmax_rows(const float* lg, int n, int ld, int rows, int* out, cudaStream_t s);
 
 }  // namespace eb

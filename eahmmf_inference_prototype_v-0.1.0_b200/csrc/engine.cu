@@ -302,6 +302,16 @@ struct EahmmfEngine {
     float* u_host = nullptr;  // pinned staging of the same
     void* samp_ws = nullptr;
     int hn_out = 0;           // host copy of state->n_out after the work enqueued so far
+    // multi-sequence decode: n_slots sequences, each with n_ctx cache rows per layer; single-sequence
+    // passes (eval, greedy, decode) run on slot `slot_cur`, a multi-sequence step on bstate's rows
+    int n_slots = 1, slot_cur = 0;
+    DecodeState* bstate = nullptr;  // the multi-sequence step's state (tpos / tslot set)
+    DecodeState* fst = nullptr;     // the state of the forward pass in progress
+    int* d_tpos = nullptr;          // [MAXB] positions of a multi-sequence step's rows
+    int* d_tslot = nullptr;         // [MAXB] their slots
+    int* d_btok = nullptr;          // [MAXB] their input tokens, then their argmax
+    int* h_b = nullptr;             // pinned staging [3 * MAXB]
+    float* logits_b = nullptr;      // [MAXB x n_vocab] logits of every row of a multi-sequence step
     int graph_nodes = 0;
     bool trace = false;
     std::vector<int> trace_ids;
@@ -327,6 +337,7 @@ struct EahmmfEngine {
         if (rng) eahmmf_rng_free(rng);
         for (void* p : allocs) cudaFree(p);
         if (h_toks) cudaFreeHost(h_toks);
+        if (h_b) cudaFreeHost(h_b);
         if (h_state) cudaFreeHost(h_state);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
@@ -495,7 +506,7 @@ struct EahmmfEngine {
         moe_ws_bytes = eahmmf_cuda_moe_workspace_bytes(&layers[0].moe, MAXB);
         if (!moe_ws_bytes) return fail("expert layer not supported by the MoE kernels");
         gemv_ws_bytes = eahmmf_cuda_gemv_workspace_bytes(std::max(D, QD));
-        const size_t kvn = (size_t)n_layer * n_ctx * KD;
+        const size_t kvn = (size_t)n_layer * n_slots * n_ctx * KD;
         amax_nblk = 148;
         const int nsplit_max = std::max(1, (n_ctx + ATT_CH - 1) / ATT_CH);
         if (!dalloc(kc, kvn * 4) || !dalloc(vc, kvn * 4) || !dalloc(x, (size_t)MAXB * D * 4) ||
@@ -506,12 +517,22 @@ struct EahmmfEngine {
             !dalloc(amax_blk, (size_t)amax_nblk * 8) || !dalloc(moe_ws, moe_ws_bytes) ||
             !dalloc(gemv_ws, gemv_ws_bytes) || !dalloc(toks, MAXB * 4) || !dalloc(status, 4) ||
             !dalloc(xf_rows, xf_bytes(MAXB, D)) || !dalloc(xf_att, xf_bytes(MAXB, QD)) || !dalloc(att_cnt, n_kv * 4) ||
-            !dalloc(state, sizeof(DecodeState)))
+            !dalloc(state, sizeof(DecodeState)) || !dalloc(bstate, sizeof(DecodeState)) || !dalloc(d_tpos, MAXB * 4) ||
+            !dalloc(d_tslot, MAXB * 4) || !dalloc(d_btok, MAXB * 4) ||
+            !dalloc(logits_b, (size_t)MAXB * n_vocab * 4))
             return fail("cannot allocate activations / KV cache");
+        {
+            DecodeState b{};
+            b.slot_rows = n_ctx;
+            b.tpos = d_tpos;
+            b.tslot = d_tslot;
+            if (cudaMemcpy(bstate, &b, sizeof b, cudaMemcpyHostToDevice) != cudaSuccess) return fail("state");
+        }
         if (cudaMemset(kc, 0, kvn * 4) != cudaSuccess || cudaMemset(vc, 0, kvn * 4) != cudaSuccess ||
             cudaMemset(status, 0, 4) != cudaSuccess || cudaMemset(att_cnt, 0, n_kv * 4) != cudaSuccess)
             return fail("memset");
         if (cudaHostAlloc((void**)&h_toks, MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc((void**)&h_b, 3 * MAXB * 4, cudaHostAllocDefault) != cudaSuccess ||
             cudaHostAlloc((void**)&h_state, sizeof(DecodeState), cudaHostAllocDefault) != cudaSuccess ||
             cudaHostAlloc((void**)&u_host, (size_t)(n_ctx + 1) * 4, cudaHostAllocDefault) != cudaSuccess)
             return fail("pinned buffers");
@@ -638,7 +659,7 @@ struct EahmmfEngine {
         rf.cnt = att_cnt;
         rf.att = att;
         if (!mark(3) ||
-            launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, 1, nsplit, attn_part, att, XF{}, rf, -1, st) !=
+            launch_attention(hd, q, lk, lv, n_head, n_kv, scale, fst, 1, nsplit, attn_part, att, XF{}, rf, -1, st) !=
                 cudaSuccess ||
             !mark(4))
             return ST_CUDA;
@@ -681,11 +702,12 @@ struct EahmmfEngine {
 
     // One forward pass of nb tokens at the device position state->pos (which it does not change).
     // tok: device pointer to nb token ids. want_logits: logits of the last token into `logits`.
-    int forward(const int* tok, int nb, bool want_logits) {
+    int forward(const int* tok, int nb, bool want_logits, bool batch = false) {
+        fst = batch ? bstate : state;
         const int nsplit = nsplit_for(nb);
         const float scale = 1.0f / sqrtf((float)hd);
         if (!mark(0)) return ST_CUDA;
-        if (launch_rope_table(state, inv_freq, hd / 2, nb, rope_cs, st) != cudaSuccess) return ST_CUDA;
+        if (launch_rope_table(fst, inv_freq, hd / 2, nb, rope_cs, st) != cudaSuccess) return ST_CUDA;
         if (launch_embed(embd, embd_type, embd_rb, D, n_embd_rows, tok, nb, x, status, st) != cudaSuccess)
             return ST_CUDA;
         if (!mark(0)) return ST_CUDA;
@@ -730,9 +752,12 @@ struct EahmmfEngine {
         MoeDeferred pending;  // combine of the previous layer's MoE block, fused into the next norm
         for (int l = 0; l < n_layer; l++) {
             const Layer& L = layers[l];
-            float* lk = kc + (size_t)l * n_ctx * KD;
-            float* lv = vc + (size_t)l * n_ctx * KD;
-            if (nb == 1 && fused_step_ok(L)) {  // single-token step: 6 launches per layer
+            // the layer's cache; a single-sequence pass sees its slot's rows, a multi-sequence step all
+            // slots (rows slot * n_ctx + position, from bstate)
+            const size_t lo = ((size_t)l * n_slots + (batch ? 0 : slot_cur)) * n_ctx * KD;
+            float* lk = kc + lo;
+            float* lv = vc + lo;
+            if (nb == 1 && !batch && fused_step_ok(L)) {  // single-token step: 6 launches per layer
                 const int rc = layer_step1(L, lk, lv, scale, nsplit, pending);
                 if (rc != ST_OK) return rc;
                 continue;
@@ -763,20 +788,20 @@ struct EahmmfEngine {
             }
             if (rc != ST_OK || !mark(2)) return rc != ST_OK ? rc : ST_CUDA;
             RopeFuse rf{};
-            if (nb == 1) {  // single-token step: norms, rotation and KV append inside the attention kernel
+            if (nb == 1 && !batch) {  // single-token step: norms, rotation and KV append inside the attention kernel
                 rf.qkv = qkv;
                 rf.qn = L.q_norm;
                 rf.kn = L.k_norm;
                 rf.eps = eps;
                 rf.cs = rope_cs;
                 if (!mark(3)) return ST_CUDA;
-            } else if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, state, nb, q, lk,
+            } else if (launch_qk_rope_kv(hd, qkv, n_head, n_kv, L.q_norm, L.k_norm, eps, rope_cs, fst, nb, q, lk,
                                          lv, st) != cudaSuccess ||
                        !mark(3)) {
                 return ST_CUDA;
             }
             const XF xf_o = xf_carve(xf_att, MAXB, QD);
-            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, state, nb, nsplit, attn_part, att, xf_o, rf, pos_host,
+            if (launch_attention(hd, q, lk, lv, n_head, n_kv, scale, fst, nb, nsplit, attn_part, att, xf_o, rf, pos_host,
                                  st) !=
                     cudaSuccess ||
                 !mark(4))
@@ -840,6 +865,13 @@ struct EahmmfEngine {
             na.K = pending.K;
             na.xf = xf_all;
             na.xn = xn;
+            if (batch) {  // every row is a sequence's next-token logits
+                na.t0 = 0;
+                if (launch_norm_prep(na, nb, st) != cudaSuccess) return ST_CUDA;
+                const int rc = gemv_d(out_w, out_type, n_vocab, out_rb, logits_b, n_vocab);
+                if (rc != ST_OK || !mark(8)) return rc != ST_OK ? rc : ST_CUDA;
+                return ST_OK;
+            }
             if (launch_norm_prep(na, 1, st) != cudaSuccess) return ST_CUDA;
             const int save_nb = nb;
             nb = 1;  // gemv_d over the single prepared row
@@ -869,6 +901,41 @@ struct EahmmfEngine {
             hpos += nb;
         }
         return ST_OK;
+    }
+
+    // KV caches for n sequence slots of n_ctx positions each (zeroed); the previous caches are freed.
+    bool set_slots(int n) {
+        if (n < 1) return false;
+        if (cudaStreamSynchronize(st) != cudaSuccess) return false;
+        const size_t kvn = (size_t)n_layer * n * n_ctx * KD;
+        float *k2 = nullptr, *v2 = nullptr;
+        if (cudaMalloc(&k2, kvn * 4) != cudaSuccess) return false;
+        if (cudaMalloc(&v2, kvn * 4) != cudaSuccess) {
+            cudaFree(k2);
+            return false;
+        }
+        if (cudaMemset(k2, 0, kvn * 4) != cudaSuccess || cudaMemset(v2, 0, kvn * 4) != cudaSuccess) {
+            cudaFree(k2);
+            cudaFree(v2);
+            return false;
+        }
+        for (void*& a : allocs)
+            if (a == kc || a == vc) {
+                cudaFree(a);
+                a = nullptr;
+            }
+        allocs.push_back(k2);
+        allocs.push_back(v2);
+        kc = k2;
+        vc = v2;
+        n_slots = n;
+        slot_cur = 0;
+        if (step_graph) {  // the captured step holds the old cache pointers
+            cudaGraphExecDestroy(step_graph);
+            step_graph = nullptr;
+            graph_nodes = 0;
+        }
+        return true;
     }
 
     // The uniform draws of the next m generated indices, from the sampler's stream (the reference draws
@@ -1079,6 +1146,58 @@ extern "C" int eahmmf_engine_step(EahmmfEngine* e, int token, int* next) {
         return ST_CUDA;
     *next = e->h_toks[1];
     return e->h_toks[2];
+}
+
+extern "C" int eahmmf_engine_set_slots(EahmmfEngine* e, int n_slots) {
+    if (!e || n_slots < 1 || n_slots > 4096) return ST_BAD_ARG;
+    return e->set_slots(n_slots) ? ST_OK : ST_CUDA;
+}
+
+extern "C" int eahmmf_engine_prefill_slot(EahmmfEngine* e, int slot, const int* prompt, int n, int n_batch, int* first) {
+    if (!e || !prompt || !first || slot < 0 || slot >= e->n_slots || n < 1 || n >= e->n_ctx || n_batch < 1 ||
+        n_batch > MAXB)
+        return ST_BAD_ARG;
+    e->slot_cur = slot;
+    int rc = e->eval_dev(prompt, n, 0, n_batch);
+    e->slot_cur = 0;
+    if (rc != ST_OK) return rc;
+    if (launch_argmax_rows(e->logits, e->n_vocab, e->n_vocab, 1, e->d_btok, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(e->h_b, e->d_btok, 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+        return ST_CUDA;
+    rc = e->read_status();
+    *first = e->h_b[0];
+    return rc;
+}
+
+extern "C" int eahmmf_engine_step_slots(EahmmfEngine* e, int n, const int* slots, const int* pos, const int* toks,
+                                        int* next) {
+    if (!e || !slots || !pos || !toks || !next || n < 1 || n > MAXB) return ST_BAD_ARG;
+    for (int i = 0; i < n; i++) {
+        if (slots[i] < 0 || slots[i] >= e->n_slots || pos[i] < 0 || pos[i] >= e->n_ctx || toks[i] < 0 ||
+            toks[i] >= e->n_embd_rows)
+            return ST_BAD_ARG;
+        for (int j = 0; j < i; j++)
+            if (slots[j] == slots[i]) return ST_BAD_ARG;  // one row per sequence per step
+    }
+    int* h = e->h_b;
+    if (cudaStreamSynchronize(e->st) != cudaSuccess) return ST_CUDA;  // the staging is free
+    memcpy(h, toks, (size_t)n * 4);
+    memcpy(h + MAXB, pos, (size_t)n * 4);
+    memcpy(h + 2 * MAXB, slots, (size_t)n * 4);
+    if (cudaMemsetAsync(e->status, 0, 4, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_btok, h, (size_t)n * 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_tpos, h + MAXB, (size_t)n * 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_tslot, h + 2 * MAXB, (size_t)n * 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess)
+        return ST_CUDA;
+    e->pn = 0;
+    int rc = e->forward(e->d_btok, n, true, true);
+    if (rc != ST_OK) return rc;
+    if (launch_argmax_rows(e->logits_b, e->n_vocab, e->n_vocab, n, e->d_btok, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(h, e->d_btok, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+        return ST_CUDA;
+    rc = e->read_status();
+    memcpy(next, h, (size_t)n * 4);
+    return rc;
 }
 
 extern "C" int eahmmf_engine_verify(EahmmfEngine* e, int* n_checked, int* n_bad) {

@@ -87,6 +87,9 @@ EXPORTS = {
     "eahmmf_cuda_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_float, C.c_void_p,
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
     "eahmmf_engine_verify": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "eahmmf_engine_set_slots": (C.c_int, [C.c_void_p, C.c_int]),
+    "eahmmf_engine_prefill_slot": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "eahmmf_engine_step_slots": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "eahmmf_cuda_hash64": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "eahmmf_hash64": (C.c_uint64, [C.c_void_p, C.c_size_t]),
     "eahmmf_rng_create": (C.c_void_p, [C.c_uint64]),
@@ -327,6 +330,27 @@ class Engine:
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(n_gen, np.int32)
         rc = lib().eahmmf_engine_generate(self._h, p.ctypes.data, len(p), n_gen, n_batch, out.ctypes.data)
+        return rc, out
+
+    def set_slots(self, n: int) -> int:
+        """eahmmf_engine_set_slots: KV caches for n sequences."""
+        return lib().eahmmf_engine_set_slots(self._h, n)
+
+    def prefill_slot(self, slot: int, prompt, n_batch: int = 64):
+        """A new sequence in `slot`: (rc, first token)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        first = C.c_int(0)
+        rc = lib().eahmmf_engine_prefill_slot(self._h, slot, p.ctypes.data, len(p), n_batch, C.byref(first))
+        return rc, int(first.value)
+
+    def step_slots(self, slots, pos, toks):
+        """One greedy step of several sequences: (rc, next tokens)."""
+        s_ = np.ascontiguousarray(slots, np.int32)
+        p_ = np.ascontiguousarray(pos, np.int32)
+        t_ = np.ascontiguousarray(toks, np.int32)
+        out = np.zeros(len(s_), np.int32)
+        rc = lib().eahmmf_engine_step_slots(self._h, len(s_), s_.ctypes.data, p_.ctypes.data, t_.ctypes.data,
+                                            out.ctypes.data)
         return rc, out
 
     def verify(self):

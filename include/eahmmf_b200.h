@@ -262,6 +262,19 @@ int eahmmf_engine_decode(EahmmfEngine* e, int n_steps, int* out, float* device_m
  * captured graph), and the argmax is copied back to *next; synchronous. Returns the kernels' status bits
  * (EAHMMF_ST_BAD_ARG when the context is full). */
 int eahmmf_engine_step(EahmmfEngine* e, int token, int* next);
+/* Several sequences at once (no counterpart in the reference, whose Engine holds one sequence,
+ * qwen3moe.cpp:791, :910-913): the engine keeps n_slots sequences, each with its own KV cache of n_ctx
+ * positions, and a step runs one token of each of up to 64 sequences as one forward pass (the dense and
+ * expert projections batched over the rows, attention per row over its own sequence's cache).
+ *  - set_slots: caches for n_slots sequences, zeroed (the single-sequence calls above use slot 0);
+ *  - prefill_slot: a new sequence in `slot`: the prompt from position 0 (passes of n_batch), the first
+ *    maximum of its logits into *first;
+ *  - step_slots: one greedy step: row i feeds toks[i] to sequence slots[i] at position pos[i] (its next
+ *    free position; distinct slots) and receives the first maximum of that row's logits in next[i].
+ * Per-row results are those of the single-sequence calls (the same kernels' per-token arithmetic). */
+int eahmmf_engine_set_slots(EahmmfEngine* e, int n_slots);
+int eahmmf_engine_prefill_slot(EahmmfEngine* e, int slot, const int* prompt, int n, int n_batch, int* first);
+int eahmmf_engine_step_slots(EahmmfEngine* e, int n, const int* slots, const int* pos, const int* toks, int* next);
 /* The residency layer's --verify contract (Config::verify, eahmmf.h:203-214: every copy checksummed
  * against its GGUF source with hash64, eahmmf.h:64-76, :940, :1014) for the engine's HBM copy: the hash64
  * of every expert component (layers x experts x gate/up/down) computed on the device in one launch, the
