@@ -366,6 +366,44 @@ def cpu_decode(path: str, prompt, steps: int, warmup: int, budget_s: float | Non
     return {"tok_s": done / el, "cores": ref.threads, "steps": done, "prefill_s": prefill_s, "ids": ids}
 
 
+BATCH_SEQS, BATCH_PROMPT, BATCH_STEPS = 32, 128, 32
+
+
+def batched_decode(eng, rank: int):
+    """Several sequences decoded together on the same model (eahmmf_engine_set_slots / prefill_slot /
+    step_slots): 32 sequences with their own 128-token random prompts, then 32 greedy steps that each run
+    one token of every sequence as a single forward pass. Tokens/s = sequence-tokens of the timed steps
+    / wall time of those steps through the C ABI (each step copies its rows in and its tokens out).
+    The engine returns to one slot afterwards."""
+    import synth
+    if eng.set_slots(BATCH_SEQS):
+        return {"unavailable": "eahmmf_engine_set_slots failed"}
+    rng = synth._rng(9, 0xB5, rank)
+    toks, pos = [], []
+    for s in range(BATCH_SEQS):
+        p = rng.integers(0, 151936, BATCH_PROMPT).astype(np.int32)
+        rc, first = eng.prefill_slot(s, p, 64)
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_prefill_slot failed: {rc}")
+        toks.append(first)
+        pos.append(BATCH_PROMPT)
+    slots = list(range(BATCH_SEQS))
+    for _ in range(3):  # warm-up steps
+        rc, toks = eng.step_slots(slots, pos, toks)
+        pos = [p + 1 for p in pos]
+    t0 = time.perf_counter()
+    for _ in range(BATCH_STEPS):
+        rc, toks = eng.step_slots(slots, pos, toks)
+        if rc:
+            raise RuntimeError(f"eahmmf_engine_step_slots failed: {rc}")
+        pos = [p + 1 for p in pos]
+    el = time.perf_counter() - t0
+    eng.set_slots(1)
+    return {"sequences": BATCH_SEQS, "prompt": BATCH_PROMPT, "steps": BATCH_STEPS,
+            "tok_s": BATCH_SEQS * BATCH_STEPS / el, "ms_per_step": el / BATCH_STEPS * 1e3,
+            "timing": "wall clock of the timed steps (host-driven, synchronous per step)"}
+
+
 def first_mismatch(a, b):
     m = min(len(a), len(b))
     d = np.nonzero(np.asarray(a[:m]) != np.asarray(b[:m]))[0]
@@ -459,6 +497,7 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
     if rc:
         raise RuntimeError(f"eahmmf_engine_greedy failed: {rc}")
     consistent = bool(e2e_ids == seq and [int(v) for v in gen] == seq[:args.steps])
+    batched = None if args.no_configs else batched_decode(eng, rank)
     eng.close()
 
     t_ms = ms
@@ -510,6 +549,7 @@ def decode_ours(args, rank: int, world: int, local: int, path: str):
                                     "gateup": float(moe_stages[2]), "down_combine": float(moe_stages[3])}
         if len(moe_stages) else None,
         "tokens_match_reference": None,
+        "batched_decode": batched,
     }
     if not args.no_ep:
         line["ep"] = ep_measure(rank, world, local, dev, steps=20, warmup=3, cpu=(rank == 0 and world == 1 and
