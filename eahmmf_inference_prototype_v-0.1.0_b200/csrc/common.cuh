@@ -149,26 +149,6 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         : "memory");
 }
 
-// The same for weight tiles, which a decode step streams once (~2 GB per token, far above the L2): the
-// lines are marked evict-first, so that the streaming does not push out of L2 what is reused across
-// kernels and layers (activations, routing data, norm and router weights, the KV rows, the code).
-#ifndef EB_WEIGHT_EVICT_FIRST
-#define EB_WEIGHT_EVICT_FIRST 1
-#endif
-__device__ __forceinline__ void tma_load_1d_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-#if EB_WEIGHT_EVICT_FIRST
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
-        : "memory");
-#else
-    tma_load_1d(dst, src, bytes, bar);
-#endif
-}
-
 __device__ __forceinline__ float f16_to_f32(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 
 // x / (1 + exp(-x)) * u, the SiLU-gated product of qwen3moe.cpp:1056-1059 (IEEE division).

@@ -164,11 +164,11 @@ __device__ __forceinline__ uint32_t issue_rows(const RowLayout& L, const uint8_t
                                                uint8_t* dst, uint64_t* bar) {
     if (L.per_row) {
         for (int r = r0; r < r1; r++)
-            tma_load_1d_stream(dst + (size_t)(r - r0) * L.stride, base + (size_t)r * rb, (uint32_t)rb, bar);
+            tma_load_1d(dst + (size_t)(r - r0) * L.stride, base + (size_t)r * rb, (uint32_t)rb, bar);
         return (uint32_t)((r1 - r0) * rb);
     }
     const Span sp = row_span(base, rb, r0, r1);
-    tma_load_1d_stream(dst, sp.src, sp.bytes, bar);
+    tma_load_1d(dst, sp.src, sp.bytes, bar);
     return sp.bytes;
 }
 __device__ __forceinline__ uint32_t rows_bytes(const RowLayout& L, const uint8_t* base, size_t rb, int r0, int r1) {

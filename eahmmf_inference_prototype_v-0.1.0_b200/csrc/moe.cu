@@ -70,11 +70,11 @@ __device__ __forceinline__ void rows_issue(const Rows& L, const uint8_t* base, s
                                            uint64_t* bar) {
     if (L.per_row) {
         for (int r = 0; r < n; r++)
-            tma_load_1d_stream(dst + (size_t)r * L.stride, base + (size_t)(r0 + r) * rb, (uint32_t)rb, bar);
+            tma_load_1d(dst + (size_t)r * L.stride, base + (size_t)(r0 + r) * rb, (uint32_t)rb, bar);
         return;
     }
     const uintptr_t s = reinterpret_cast<uintptr_t>(base) + (size_t)r0 * rb;
-    tma_load_1d_stream(dst, reinterpret_cast<const void*>(s & ~(uintptr_t)15), rows_copy_bytes(L, base, rb, r0, n), bar);
+    tma_load_1d(dst, reinterpret_cast<const void*>(s & ~(uintptr_t)15), rows_copy_bytes(L, base, rb, r0, n), bar);
 }
 
 // Staging buffer of G XF rows of K elements (G: slots per work group): frag rows (K*3 bytes each), then
@@ -1059,14 +1059,14 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup(MoeArgs a) 
             }
             if (ok) {
                 if (split8(rbg)) {
-                    tma_load_1d_stream(stage, rec.w[0] + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
-                    tma_load_1d_stream(stage + split8_off(rbg), rec.w[0] + (size_t)(r0 + 8) * rbg, (uint32_t)(8 * rbg), &full[s]);
+                    tma_load_1d(stage, rec.w[0] + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
+                    tma_load_1d(stage + split8_off(rbg), rec.w[0] + (size_t)(r0 + 8) * rbg, (uint32_t)(8 * rbg), &full[s]);
                 } else {
                     rows_issue(Lg, rec.w[0], rbg, r0, 16, stage, &full[s]);
                 }
                 if (split8(rbu)) {
-                    tma_load_1d_stream(stage + up_at, rec.w[1] + (size_t)r0 * rbu, (uint32_t)(8 * rbu), &full[s]);
-                    tma_load_1d_stream(stage + up_at + split8_off(rbu), rec.w[1] + (size_t)(r0 + 8) * rbu, (uint32_t)(8 * rbu),
+                    tma_load_1d(stage + up_at, rec.w[1] + (size_t)r0 * rbu, (uint32_t)(8 * rbu), &full[s]);
+                    tma_load_1d(stage + up_at + split8_off(rbu), rec.w[1] + (size_t)(r0 + 8) * rbu, (uint32_t)(8 * rbu),
                                 &full[s]);
                 } else {
                     rows_issue(Lu, rec.w[1], rbu, r0, 16, stage + up_at, &full[s]);
@@ -1266,14 +1266,14 @@ __global__ void __launch_bounds__((NWC_GU + 1) * 32, 1) k_moe_gateup_fs(MoeArgs 
             mbar_expect_tx(&full[s], bytes);
             if (ok) {
                 if (split8(rbg)) {
-                    tma_load_1d_stream(stage, wg + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
-                    tma_load_1d_stream(stage + split8_off(rbg), wg + (size_t)(r0 + 8) * rbg, (uint32_t)(8 * rbg), &full[s]);
+                    tma_load_1d(stage, wg + (size_t)r0 * rbg, (uint32_t)(8 * rbg), &full[s]);
+                    tma_load_1d(stage + split8_off(rbg), wg + (size_t)(r0 + 8) * rbg, (uint32_t)(8 * rbg), &full[s]);
                 } else {
                     rows_issue(Lg, wg, rbg, r0, 16, stage, &full[s]);
                 }
                 if (split8(rbu)) {
-                    tma_load_1d_stream(stage + up_at, wu + (size_t)r0 * rbu, (uint32_t)(8 * rbu), &full[s]);
-                    tma_load_1d_stream(stage + up_at + split8_off(rbu), wu + (size_t)(r0 + 8) * rbu, (uint32_t)(8 * rbu),
+                    tma_load_1d(stage + up_at, wu + (size_t)r0 * rbu, (uint32_t)(8 * rbu), &full[s]);
+                    tma_load_1d(stage + up_at + split8_off(rbu), wu + (size_t)(r0 + 8) * rbu, (uint32_t)(8 * rbu),
                                 &full[s]);
                 } else {
                     rows_issue(Lu, wu, rbu, r0, 16, stage + up_at, &full[s]);
