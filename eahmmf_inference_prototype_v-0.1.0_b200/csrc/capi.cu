@@ -386,7 +386,7 @@ namespace {
 // needs), or, with `given`, on assigned experts instead of a routing of logits (eahmmf_cuda_moe_experts).
 int moe_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x, void* d_workspace,
             size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer, const float* norm_w, float eps,
-            const int* given) {
+            const int* given, const MoeHook* hook = nullptr) {
     // norm_w: d_xn is the un-normalised residual and the RMSNorm is applied inside the router launch
     // (only for the fused small-batch path: T <= FUSED_ROUTE_TMAX, router matrix present)
     if (norm_w && (T > FUSED_ROUTE_TMAX || d_logits || given || !L || !L->d_router)) return ST_BAD_ARG;
@@ -460,6 +460,10 @@ int moe_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_lo
             if (e != cudaSuccess) return ST_CUDA;
             a.logits = lg;
         }
+        if (hook && hook->fn) {
+            const int rc = hook->fn(hook->ctx, a.logits, tc, E, st);
+            if (rc != ST_OK) return rc;
+        }
         g_prof.mark(1, st);
         if (!a.fused_route && launch_moe_route(a, st) != cudaSuccess) return ST_CUDA;
         g_prof.mark(2, st);
@@ -483,9 +487,9 @@ int moe_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_lo
 namespace eb {
 int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                   void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
-                  const float* norm_w, float eps) {
+                  const float* norm_w, float eps, const MoeHook* hook = nullptr) {
     return moe_run(L, T, d_xn, d_logits, d_x, d_workspace, workspace_bytes, stream, d_status, defer, norm_w, eps,
-                   nullptr);
+                   nullptr, hook);
 }
 }  // namespace eb
 

@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <string>
 #include <thread>
 #include <vector>
@@ -37,7 +38,7 @@
 namespace eb {
 int moe_layer_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_logits, float* d_x,
                   void* d_workspace, size_t workspace_bytes, void* stream, int* d_status, MoeDeferred* defer,
-                  const float* norm_w, float eps);
+                  const float* norm_w, float eps, const MoeHook* hook = nullptr);
 cudaError_t launch_hash64(const uint8_t* const* d_ptrs, const size_t* d_sizes, int n, uint64_t* d_out,
                           cudaStream_t st);
 uint64_t host_hash64(const uint8_t* p, size_t n);
@@ -267,6 +268,33 @@ struct EahmmfEngine {
     };
     std::vector<Slice> slices;
     std::string path;
+    // Oversubscribed mode (expert_budget > 0): the experts stay in the mapped file (pinned for DMA) and a
+    // device cache of `slots` expert footprints holds the resident ones (see ExpertCache).
+    struct ExpertCache {
+        std::unique_ptr<Gguf> file;     // the mapping the host copies come from
+        bool pinned = false;            // the mapping is registered with the driver (DMA copies)
+        size_t comp[3] = {0, 0, 0};     // bytes of one expert's gate, up, down
+        size_t off[3] = {0, 0, 0};      // their offsets inside a slot
+        size_t foot = 0;                // slot bytes
+        int slots = 0;
+        uint8_t* dev = nullptr;         // [slots x foot]
+        std::vector<uint64_t> src[3];   // [layer * E + expert] file offset of each component
+        std::vector<int> slot_of;       // [layer * E + expert] -> slot or -1
+        std::vector<int> owner;         // [slot] -> layer * E + expert or -1
+        std::vector<uint64_t> last_use, pin;  // per slot: LRU tick, epoch of the pass that needs it
+        std::vector<cudaEvent_t> ready; // per slot: its last fill completed
+        std::vector<std::vector<int>> last_set;  // [layer] experts routed at the layer's last pass
+        uint64_t tick = 0, epoch = 0;
+        cudaStream_t side = nullptr;    // fills (host -> device copies)
+        uint64_t* h_tab = nullptr;      // pinned mirror of every layer's 3 x E pointer table
+        int* d_ids = nullptr;           // [MAXB * K] routing of the pass
+        float* d_w = nullptr;
+        int* h_ids = nullptr;           // pinned
+        uint64_t hits = 0, misses = 0, prefetched = 0, prefetch_hits = 0, bytes = 0, evictions = 0;
+        std::vector<uint8_t> from_prefetch;  // [slot] filled by a prefetch and not used since
+    };
+    std::unique_ptr<ExpertCache> cache;
+    int cur_layer = 0;
     const uint8_t* embd = nullptr;
     int embd_type = 0;
     size_t embd_rb = 0;
@@ -331,6 +359,17 @@ struct EahmmfEngine {
 
     ~EahmmfEngine() {
         if (st) cudaStreamSynchronize(st);
+        if (cache) {
+            ExpertCache& C = *cache;
+            if (C.side) cudaStreamSynchronize(C.side);
+            for (cudaEvent_t ev : C.ready)
+                if (ev) cudaEventDestroy(ev);
+            if (C.side) cudaStreamDestroy(C.side);
+            if (C.h_tab) cudaFreeHost(C.h_tab);
+            if (C.h_ids) cudaFreeHost(C.h_ids);
+            if (C.pinned && C.file) cudaHostUnregister(const_cast<uint8_t*>(C.file->map));
+            cache.reset();  // unmaps the file
+        }
         for (cudaEvent_t v : pev) cudaEventDestroy(v);
         if (step_graph) cudaGraphExecDestroy(step_graph);
         if (u_host) cudaFreeHost(u_host);
@@ -371,8 +410,9 @@ struct EahmmfEngine {
         return dalloc(dst, n * 4) && cudaMemcpy(dst, h.data(), n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
     }
 
-    bool load(const char* path, int ctx) {
-        Gguf g;
+    bool load(const char* path, int ctx, size_t expert_budget = 0) {
+        std::unique_ptr<Gguf> gfile(new Gguf());
+        Gguf& g = *gfile;
         if (!g.open(path)) return fail("gguf: " + g.err);
         if (g.gets("general.architecture") != "qwen3moe") return fail("unsupported architecture (need qwen3moe)");
         this->path = path;
@@ -400,11 +440,31 @@ struct EahmmfEngine {
         if (D % 256 || FF % 256) return fail("hidden and expert sizes must be multiples of 256");
 
         if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
-        // the data section, byte for byte
+        // the data section, byte for byte; in oversubscribed mode everything but the expert tensors, each
+        // tensor at a 256-byte aligned place of one allocation
         const size_t nbytes = g.size - g.data_start;
-        if (!dalloc(weights, nbytes)) return fail("cannot allocate device memory for the weights");
-        if (!upload(g.map + g.data_start, nbytes)) return fail("weight upload failed");
-        auto dptr = [&](const GgufTensor* t) { return weights + (t->file_off - g.data_start); };
+        auto is_expert = [](const std::string& n) {
+            return n.size() > 12 && n.compare(n.size() - 12, 12, "_exps.weight") == 0;
+        };
+        std::map<const GgufTensor*, size_t> place;
+        if (!expert_budget) {
+            if (!dalloc(weights, nbytes)) return fail("cannot allocate device memory for the weights");
+            if (!upload(g.map + g.data_start, nbytes)) return fail("weight upload failed");
+        } else {
+            size_t o = 0;
+            for (auto& kv : g.tensors)
+                if (!is_expert(kv.first)) {
+                    place[&kv.second] = o;
+                    o = (o + kv.second.bytes + 255) & ~(size_t)255;
+                }
+            if (!dalloc(weights, o)) return fail("cannot allocate device memory for the weights");
+            for (auto& kv : place)
+                if (!upload(g.map + kv.first->file_off, kv.first->bytes, weights + kv.second))
+                    return fail("weight upload failed");
+        }
+        auto dptr = [&](const GgufTensor* t) {
+            return expert_budget ? weights + place.at(t) : weights + (t->file_off - g.data_start);
+        };
 
         const GgufTensor* te = g.tensor("token_embd.weight");
         const GgufTensor* to = g.tensor("output.weight");
@@ -478,6 +538,15 @@ struct EahmmfEngine {
             std::vector<const uint8_t*> ptr(3 * (size_t)n_expert);
             for (int c = 0; c < 3; c++) {
                 const size_t per = ex[c]->row_bytes * (size_t)ex[c]->ne[1];
+                if (expert_budget) {  // the cache fills the table; the file keeps the bytes
+                    if (l == 0) {
+                        cache.reset(new ExpertCache());
+                    }
+                    if (cache->comp[c] == 0) cache->comp[c] = per;
+                    if (cache->comp[c] != per) return fail("expert sizes differ between layers");
+                    for (int e = 0; e < n_expert; e++) cache->src[c].push_back(ex[c]->file_off + per * e);
+                    continue;
+                }
                 for (int e = 0; e < n_expert; e++) {
                     ptr[(size_t)c * n_expert + e] = dptr(ex[c]) + per * e;
                     slices.push_back(Slice{dptr(ex[c]) + per * e, ex[c]->file_off + per * e, per});
@@ -503,6 +572,7 @@ struct EahmmfEngine {
             M.d_down = dp + 2 * n_expert;
             M.d_router = router;
         }
+        if (expert_budget && !init_cache(std::move(gfile), expert_budget)) return false;
         moe_ws_bytes = eahmmf_cuda_moe_workspace_bytes(&layers[0].moe, MAXB);
         if (!moe_ws_bytes) return fail("expert layer not supported by the MoE kernels");
         gemv_ws_bytes = eahmmf_cuda_gemv_workspace_bytes(std::max(D, QD));
@@ -543,8 +613,138 @@ struct EahmmfEngine {
         return cudaDeviceSynchronize() == cudaSuccess || fail("device error after load");
     }
 
+    // ---- oversubscribed mode ------------------------------------------------------------------------
+    // The cache: slots of one expert footprint each (gate, up, down at 256-byte aligned offsets), at
+    // least one layer's worth; the file mapping registered with the driver so that fills are DMA copies
+    // from it (pageable copies otherwise); every layer's pointer table aimed at slot 0 until its experts
+    // are made resident.
+    bool init_cache(std::unique_ptr<Gguf> file, size_t budget) {
+        ExpertCache& C = *cache;
+        C.file = std::move(file);
+        auto a256 = [](size_t v) { return (v + 255) & ~(size_t)255; };
+        C.off[0] = 0;
+        C.off[1] = a256(C.comp[0]);
+        C.off[2] = a256(C.off[1] + C.comp[1]);
+        C.foot = a256(C.off[2] + C.comp[2]);
+        C.slots = (int)std::min<size_t>(budget / C.foot, (size_t)n_layer * n_expert);
+        if (C.slots < n_expert) return fail("expert budget below one layer's experts");
+        if (!dalloc(C.dev, (size_t)C.slots * C.foot)) return fail("cannot allocate the expert cache");
+        C.pinned = cudaHostRegister(const_cast<uint8_t*>(C.file->map), C.file->size, cudaHostRegisterReadOnly) ==
+                   cudaSuccess;
+        if (!C.pinned) cudaGetLastError();  // fills then stage through the driver (slower, same bytes)
+        const size_t nk = (size_t)n_layer * n_expert;
+        C.slot_of.assign(nk, -1);
+        C.owner.assign(C.slots, -1);
+        C.last_use.assign(C.slots, 0);
+        C.pin.assign(C.slots, 0);
+        C.from_prefetch.assign(C.slots, 0);
+        C.last_set.assign(n_layer, {});
+        C.ready.assign(C.slots, nullptr);
+        for (auto& ev : C.ready)
+            if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return fail("cache events");
+        if (cudaStreamCreateWithFlags(&C.side, cudaStreamNonBlocking) != cudaSuccess) return fail("cache stream");
+        if (cudaHostAlloc((void**)&C.h_tab, nk * 3 * 8, cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc((void**)&C.h_ids, (size_t)MAXB * n_used * 4, cudaHostAllocDefault) != cudaSuccess)
+            return fail("cache pinned buffers");
+        if (!dalloc(C.d_ids, (size_t)MAXB * n_used * 4) || !dalloc(C.d_w, (size_t)MAXB * n_used * 4))
+            return fail("cache routing buffers");
+        for (size_t i = 0; i < nk * 3; i++) C.h_tab[i] = reinterpret_cast<uint64_t>(C.dev);
+        for (int l = 0; l < n_layer; l++)
+            if (cudaMemcpy(const_cast<const uint8_t**>(layers[l].moe.d_gate), C.h_tab + (size_t)l * 3 * n_expert,
+                           (size_t)3 * n_expert * 8, cudaMemcpyHostToDevice) != cudaSuccess)
+                return fail("expert tables");
+        return true;
+    }
+    // A free slot, or the least recently used one whose expert the current pass does not need (evicted).
+    int cache_victim() {
+        ExpertCache& C = *cache;
+        int best = -1;
+        for (int sl = 0; sl < C.slots; sl++) {
+            if (C.pin[sl] == C.epoch) continue;
+            if (C.owner[sl] < 0) return sl;
+            if (best < 0 || C.last_use[sl] < C.last_use[best]) best = sl;
+        }
+        if (best >= 0) {
+            C.slot_of[C.owner[best]] = -1;
+            C.owner[best] = -1;
+            C.evictions++;
+        }
+        return best;
+    }
+    // Copies expert `key` (layer * E + expert) into slot sl on the fill stream.
+    bool cache_fill(int sl, int key) {
+        ExpertCache& C = *cache;
+        uint8_t* d = C.dev + (size_t)sl * C.foot;
+        for (int c = 0; c < 3; c++)
+            if (cudaMemcpyAsync(d + C.off[c], C.file->map + C.src[c][key], C.comp[c], cudaMemcpyHostToDevice, C.side) !=
+                cudaSuccess)
+                return false;
+        if (cudaEventRecord(C.ready[sl], C.side) != cudaSuccess) return false;
+        C.owner[sl] = key;
+        C.slot_of[key] = sl;
+        C.bytes += C.comp[0] + C.comp[1] + C.comp[2];
+        return true;
+    }
+    // The MoE pass hook: the routing of the pass (the same top-k its kernels compute) read back, every
+    // routed expert made resident (hits wait for a fill in flight; misses evict and fill), the layer's
+    // pointer table uploaded, then the experts the next layer routed at its last pass prefetched into
+    // slots this pass does not use, overlapping this layer's expert kernels.
+    int cache_resident(const float* d_logits, int T, cudaStream_t s) {
+        ExpertCache& C = *cache;
+        const int l = cur_layer, E = n_expert, K = n_used;
+        if (eahmmf_cuda_route_topk(d_logits, T, E, K, C.d_ids, C.d_w, s, status) != ST_OK ||
+            cudaMemcpyAsync(C.h_ids, C.d_ids, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess)
+            return ST_CUDA;
+        C.epoch++;
+        std::vector<int> need(C.h_ids, C.h_ids + (size_t)T * K);
+        std::sort(need.begin(), need.end());
+        need.erase(std::unique(need.begin(), need.end()), need.end());
+        uint64_t* tab = C.h_tab + (size_t)l * 3 * E;
+        for (int e : need) {
+            if (e < 0 || e >= E) return ST_BAD_INDEX;
+            const int key = l * E + e;
+            int sl = C.slot_of[key];
+            if (sl >= 0) {
+                C.hits++;
+                if (C.from_prefetch[sl]) C.prefetch_hits++;
+            } else {
+                C.misses++;
+                sl = cache_victim();
+                if (sl < 0) return ST_CAPACITY;
+                if (!cache_fill(sl, key)) return ST_CUDA;
+            }
+            C.from_prefetch[sl] = 0;
+            if (cudaStreamWaitEvent(s, C.ready[sl], 0) != cudaSuccess) return ST_CUDA;
+            C.pin[sl] = C.epoch;
+            C.last_use[sl] = ++C.tick;
+            for (int c = 0; c < 3; c++) tab[(size_t)c * E + e] = reinterpret_cast<uint64_t>(C.dev + (size_t)sl * C.foot + C.off[c]);
+        }
+        if (cudaMemcpyAsync(const_cast<const uint8_t**>(layers[l].moe.d_gate), tab, (size_t)3 * E * 8,
+                            cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return ST_CUDA;
+        C.last_set[l] = need;
+        const int ln = (l + 1) % n_layer;
+        for (int e : C.last_set[ln]) {
+            const int key = ln * E + e;
+            if (C.slot_of[key] >= 0) continue;
+            const int sl = cache_victim();
+            if (sl < 0) break;
+            if (!cache_fill(sl, key)) return ST_CUDA;
+            C.prefetched++;
+            C.from_prefetch[sl] = 1;
+            C.last_use[sl] = ++C.tick;
+        }
+        return ST_OK;
+    }
+    static int cache_hook(void* ctx, const float* d_logits, int T, int E, cudaStream_t s) {
+        (void)E;
+        return static_cast<EahmmfEngine*>(ctx)->cache_resident(d_logits, T, s);
+    }
+
     // host -> device through two pinned staging halves (the mapping is pageable)
-    bool upload(const uint8_t* src, size_t n) {
+    bool upload(const uint8_t* src, size_t n, uint8_t* dst = nullptr) {
+        if (!dst) dst = weights;
         const size_t half = 64u << 20;
         uint8_t* stage[2] = {nullptr, nullptr};
         cudaEvent_t ev[2] = {nullptr, nullptr};
@@ -558,7 +758,7 @@ struct EahmmfEngine {
             if (live[k]) ok = cudaEventSynchronize(ev[k]) == cudaSuccess;
             if (!ok) break;
             memcpy(stage[k], src + o, c);
-            ok = cudaMemcpyAsync(weights + o, stage[k], c, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+            ok = cudaMemcpyAsync(dst + o, stage[k], c, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                  cudaEventRecord(ev[k], st) == cudaSuccess;
             live[k] = true;
         }
@@ -679,7 +879,9 @@ struct EahmmfEngine {
         if (launch_gemv_xf(o, st) != cudaSuccess || !mark(5)) return ST_CUDA;
         pending = MoeDeferred{};
         if (!mark(6)) return ST_CUDA;
-        const int rc = moe_layer_run(&L.moe, 1, x, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, L.ffn_norm, eps);
+        const MoeHook hk{&EahmmfEngine::cache_hook, this};
+        const int rc = moe_layer_run(&L.moe, 1, x, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, L.ffn_norm, eps,
+                                     cache ? &hk : nullptr);
         if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
         return trace_layer(1);
     }
@@ -750,8 +952,10 @@ struct EahmmfEngine {
             return ST_OK;
         };
         MoeDeferred pending;  // combine of the previous layer's MoE block, fused into the next norm
+        const MoeHook hk{&EahmmfEngine::cache_hook, this};  // oversubscribed mode: residency before the experts
         for (int l = 0; l < n_layer; l++) {
             const Layer& L = layers[l];
+            cur_layer = l;
             // the layer's cache; a single-sequence pass sees its slot's rows, a multi-sequence step all
             // slots (rows slot * n_ctx + position, from bstate)
             const size_t lo = ((size_t)l * n_slots + (batch ? 0 : slot_cur)) * n_ctx * KD;
@@ -843,10 +1047,11 @@ struct EahmmfEngine {
             if (nb <= FUSED_ROUTE_TMAX) {  // the FFN RMSNorm runs inside the router launch
                 if (!mark(6)) return ST_CUDA;
                 rc = moe_layer_run(&L.moe, nb, x, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, L.ffn_norm,
-                                   eps);
+                                   eps, cache ? &hk : nullptr);
             } else {
                 if (launch_rmsnorm(x, D, L.ffn_norm, xn, D, nb, D, eps, st) != cudaSuccess || !mark(6)) return ST_CUDA;
-                rc = moe_layer_run(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, nullptr, 0.f);
+                rc = moe_layer_run(&L.moe, nb, xn, nullptr, x, moe_ws, moe_ws_bytes, st, status, &pending, nullptr, 0.f,
+                                   cache ? &hk : nullptr);
             }
             if (rc != ST_OK || !mark(7)) return rc != ST_OK ? rc : ST_CUDA;
             if (trace_layer(nb) != ST_OK) return ST_CUDA;
@@ -968,7 +1173,7 @@ struct EahmmfEngine {
         hpos++;  // the step's argmax advances the position
         if (!prepare_draws(1)) return ST_CUDA;
         hn_out++;
-        if (!use_graph || trace || prof) {
+        if (!use_graph || trace || prof || cache) {  // oversubscribed mode: the host acts inside the step
             pn = 0;
             const int rc = forward(&state->token, 1, true);
             if (rc != ST_OK) return rc;
@@ -1010,6 +1215,30 @@ struct EahmmfEngine {
 // ---------------------------------------------------------------------------------------------------
 // 4. engine entry points
 // ---------------------------------------------------------------------------------------------------
+extern "C" EahmmfEngine* eahmmf_engine_load_budget(const char* gguf_path, int n_ctx, size_t expert_vram_bytes,
+                                                   char* err, size_t err_cap) {
+    EahmmfEngine* e = new EahmmfEngine();
+    if (!gguf_path || !e->load(gguf_path, n_ctx, expert_vram_bytes)) {
+        if (err && err_cap) snprintf(err, err_cap, "%s", gguf_path ? e->err.c_str() : "null path");
+        delete e;
+        return nullptr;
+    }
+    return e;
+}
+
+extern "C" int eahmmf_engine_cache_stats(EahmmfEngine* e, uint64_t* v, int cap) {
+    if (!e || !v || cap < EAHMMF_CACHE_STATS) return ST_BAD_ARG;
+    if (!e->cache) {
+        for (int i = 0; i < EAHMMF_CACHE_STATS; i++) v[i] = 0;
+        return ST_OK;
+    }
+    const auto& C = *e->cache;
+    const uint64_t vals[EAHMMF_CACHE_STATS] = {(uint64_t)C.slots, C.hits, C.misses, C.prefetched, C.prefetch_hits,
+                                               C.evictions, C.bytes, (uint64_t)C.pinned};
+    for (int i = 0; i < EAHMMF_CACHE_STATS; i++) v[i] = vals[i];
+    return ST_OK;
+}
+
 extern "C" EahmmfEngine* eahmmf_engine_load(const char* gguf_path, int n_ctx, char* err, size_t err_cap) {
     EahmmfEngine* e = new EahmmfEngine();
     if (!gguf_path || !e->load(gguf_path, n_ctx)) {
@@ -1202,6 +1431,16 @@ extern "C" int eahmmf_engine_step_slots(EahmmfEngine* e, int n, const int* slots
 
 extern "C" int eahmmf_engine_verify(EahmmfEngine* e, int* n_checked, int* n_bad) {
     if (!e || !n_checked || !n_bad) return ST_BAD_ARG;
+    if (e->cache) {  // oversubscribed mode: the resident copies in the cache's slots
+        if (cudaStreamSynchronize(e->cache->side) != cudaSuccess) return ST_CUDA;
+        const auto& C = *e->cache;
+        e->slices.clear();
+        for (int sl = 0; sl < C.slots; sl++)
+            if (C.owner[sl] >= 0)
+                for (int c = 0; c < 3; c++)
+                    e->slices.push_back(EahmmfEngine::Slice{C.dev + (size_t)sl * C.foot + C.off[c],
+                                                            C.src[c][C.owner[sl]], C.comp[c]});
+    }
     const int n = (int)e->slices.size();
     *n_checked = n;
     *n_bad = 0;

@@ -143,6 +143,13 @@ struct GroupedArgs {
     int* status;
 };
 
+// A caller's step between the router launch of a MoE pass (the logits of its T tokens complete on the
+// stream) and the expert kernels, e.g. to make the routed experts resident first. Nonzero stops the pass.
+struct MoeHook {
+    int (*fn)(void* ctx, const float* d_logits, int T, int E, cudaStream_t st);
+    void* ctx;
+};
+
 // The combine inputs of a MoE pass whose combine the caller performs itself.
 struct MoeDeferred {
     const int* token_slots = nullptr;  // [T*K] slots of each token, ascending expert order

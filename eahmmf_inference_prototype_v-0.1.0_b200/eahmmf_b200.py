@@ -88,6 +88,8 @@ EXPORTS = {
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
     "eahmmf_engine_verify": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "eahmmf_engine_set_slots": (C.c_int, [C.c_void_p, C.c_int]),
+    "eahmmf_engine_load_budget": (C.c_void_p, [C.c_char_p, C.c_int, C.c_size_t, C.c_char_p, C.c_size_t]),
+    "eahmmf_engine_cache_stats": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "eahmmf_engine_prefill_slot": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "eahmmf_engine_step_slots": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "eahmmf_cuda_hash64": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
@@ -267,10 +269,15 @@ class Engine:
 
     DIM_NAMES = ("n_layer", "D", "n_head", "n_kv", "hd", "n_expert", "n_used", "FF", "n_vocab", "n_ctx", "n_embd")
 
-    def __init__(self, path: str, n_ctx: int):
+    CACHE_STATS = ("slots", "hits", "misses", "prefetched", "prefetch_hits", "evictions", "bytes_h2d", "dma")
+
+    def __init__(self, path: str, n_ctx: int, expert_vram_bytes: int = 0):
         L = lib()
         err = C.create_string_buffer(256)
-        h = L.eahmmf_engine_load(path.encode(), n_ctx, err, 256)
+        if expert_vram_bytes:
+            h = L.eahmmf_engine_load_budget(path.encode(), n_ctx, expert_vram_bytes, err, 256)
+        else:
+            h = L.eahmmf_engine_load(path.encode(), n_ctx, err, 256)
         if not h:
             raise RuntimeError(f"eahmmf_engine_load: {err.value.decode()}")
         self._h = h
@@ -331,6 +338,12 @@ class Engine:
         out = np.zeros(n_gen, np.int32)
         rc = lib().eahmmf_engine_generate(self._h, p.ctypes.data, len(p), n_gen, n_batch, out.ctypes.data)
         return rc, out
+
+    def cache_stats(self) -> dict:
+        """eahmmf_engine_cache_stats of an oversubscribed engine."""
+        v = np.zeros(len(self.CACHE_STATS), np.uint64)
+        lib().eahmmf_engine_cache_stats(self._h, v.ctypes.data, len(v))
+        return dict(zip(self.CACHE_STATS, (int(x) for x in v)))
 
     def set_slots(self, n: int) -> int:
         """eahmmf_engine_set_slots: KV caches for n sequences."""

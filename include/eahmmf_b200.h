@@ -232,6 +232,22 @@ typedef struct EahmmfEngine EahmmfEngine;
  * Engine::load (qwen3moe.cpp:879). NULL on failure, with a message in err (if given). */
 EahmmfEngine* eahmmf_engine_load(const char* gguf_path, int n_ctx, char* err, size_t err_cap);
 void eahmmf_engine_free(EahmmfEngine* e);
+/* Expert residency beyond HBM (the reference's reason to exist: eahmmf.h's RAM/VRAM tiers, with the
+ * asynchronous prefetch its README lists as not implemented): the model loads with only the non-expert
+ * tensors in HBM; expert bytes stay in the mapped GGUF (registered with the driver for DMA) and a device
+ * cache of expert_vram_bytes holds whole experts (at least one layer's worth). Each MoE pass reads back
+ * its routing, makes every routed expert resident (a hit waits for a fill in flight; a miss evicts the
+ * least recently used expert the pass does not need), uploads the layer's pointer table and starts, on a
+ * second stream, the fills of the experts the next layer routed at its last pass, which overlap this
+ * layer's expert kernels. Results are those of the fully resident engine (the same kernels over the same
+ * bytes). Decode steps run without the captured graph (the host acts inside each step). */
+EahmmfEngine* eahmmf_engine_load_budget(const char* gguf_path, int n_ctx, size_t expert_vram_bytes, char* err,
+                                        size_t err_cap);
+/* Cache counters: [0] slots (experts), [1] hits, [2] misses, [3] prefetch fills, [4] hits on prefetched
+ * experts, [5] evictions, [6] bytes copied host -> device, [7] 1 when fills are DMA from the registered
+ * mapping. All zero for a fully resident engine. */
+#define EAHMMF_CACHE_STATS 8
+int eahmmf_engine_cache_stats(EahmmfEngine* e, uint64_t* v, int cap);
 /* dims[0..10] = n_layer, D, n_head, n_kv, hd, n_expert, n_used, FF, n_vocab, n_ctx, embedding rows */
 int eahmmf_engine_dims(EahmmfEngine* e, int* dims);
 /* Engine::eval (qwen3moe.cpp:1078-1084): n tokens from position p0 in forward passes of n_batch
