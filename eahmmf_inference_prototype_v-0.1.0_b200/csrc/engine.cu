@@ -487,6 +487,7 @@ struct EahmmfEngine {
             return fail("inv_freq");
 
         layers.resize(n_layer);
+        if (expert_budget) cache.reset(new ExpertCache());
         for (int l = 0; l < n_layer; l++) {
             Layer& L = layers[l];
             auto T = [&](const char* s) { return g.tensor("blk." + std::to_string(l) + "." + s); };
@@ -539,9 +540,6 @@ struct EahmmfEngine {
             for (int c = 0; c < 3; c++) {
                 const size_t per = ex[c]->row_bytes * (size_t)ex[c]->ne[1];
                 if (expert_budget) {  // the cache fills the table; the file keeps the bytes
-                    if (l == 0) {
-                        cache.reset(new ExpertCache());
-                    }
                     if (cache->comp[c] == 0) cache->comp[c] = per;
                     if (cache->comp[c] != per) return fail("expert sizes differ between layers");
                     for (int e = 0; e < n_expert; e++) cache->src[c].push_back(ex[c]->file_off + per * e);
@@ -633,6 +631,8 @@ struct EahmmfEngine {
                    cudaSuccess;
         if (!C.pinned) cudaGetLastError();  // fills then stage through the driver (slower, same bytes)
         const size_t nk = (size_t)n_layer * n_expert;
+        for (int c = 0; c < 3; c++)
+            if (C.src[c].size() != nk) return fail("expert table of the cache incomplete");
         C.slot_of.assign(nk, -1);
         C.owner.assign(C.slots, -1);
         C.last_use.assign(C.slots, 0);
@@ -674,6 +674,9 @@ struct EahmmfEngine {
     // Copies expert `key` (layer * E + expert) into slot sl on the fill stream.
     bool cache_fill(int sl, int key) {
         ExpertCache& C = *cache;
+        if (sl < 0 || sl >= C.slots || key < 0 || (size_t)key >= C.slot_of.size()) return false;
+        for (int c = 0; c < 3; c++)
+            if ((size_t)key >= C.src[c].size() || C.src[c][key] + C.comp[c] > C.file->size) return false;
         uint8_t* d = C.dev + (size_t)sl * C.foot;
         for (int c = 0; c < 3; c++)
             if (cudaMemcpyAsync(d + C.off[c], C.file->map + C.src[c][key], C.comp[c], cudaMemcpyHostToDevice, C.side) !=
