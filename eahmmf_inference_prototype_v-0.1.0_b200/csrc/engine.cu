@@ -272,7 +272,9 @@ struct EahmmfEngine {
     // device cache of `slots` expert footprints holds the resident ones (see ExpertCache).
     struct ExpertCache {
         std::unique_ptr<Gguf> file;     // the mapping the host copies come from
-        bool pinned = false;            // the mapping is registered with the driver (DMA copies)
+        bool pinned = false;            // fills are DMA copies: from the registered mapping or a pinned copy
+        const uint8_t* host = nullptr;  // the bytes fills copy from (file offsets)
+        uint8_t* host_copy = nullptr;   // pinned copy of the file when the mapping cannot be registered
         size_t comp[3] = {0, 0, 0};     // bytes of one expert's gate, up, down
         size_t off[3] = {0, 0, 0};      // their offsets inside a slot
         size_t foot = 0;                // slot bytes
@@ -367,7 +369,8 @@ struct EahmmfEngine {
             if (C.side) cudaStreamDestroy(C.side);
             if (C.h_tab) cudaFreeHost(C.h_tab);
             if (C.h_ids) cudaFreeHost(C.h_ids);
-            if (C.pinned && C.file) cudaHostUnregister(const_cast<uint8_t*>(C.file->map));
+            if (C.host_copy) cudaFreeHost(C.host_copy);
+            else if (C.pinned && C.file) cudaHostUnregister(const_cast<uint8_t*>(C.file->map));
             cache.reset();  // unmaps the file
         }
         for (cudaEvent_t v : pev) cudaEventDestroy(v);
@@ -377,6 +380,10 @@ struct EahmmfEngine {
         for (void* p : allocs) cudaFree(p);
         if (h_toks) cudaFreeHost(h_toks);
         if (h_b) cudaFreeHost(h_b);
+        for (int i = 0; i < 2; i++) {
+            if (up_stage[i]) cudaFreeHost(up_stage[i]);
+            if (up_ev[i]) cudaEventDestroy(up_ev[i]);
+        }
         if (h_state) cudaFreeHost(h_state);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
@@ -458,8 +465,9 @@ struct EahmmfEngine {
                     o = (o + kv.second.bytes + 255) & ~(size_t)255;
                 }
             if (!dalloc(weights, o)) return fail("cannot allocate device memory for the weights");
+            size_t left = place.size();
             for (auto& kv : place)
-                if (!upload(g.map + kv.first->file_off, kv.first->bytes, weights + kv.second))
+                if (!upload(g.map + kv.first->file_off, kv.first->bytes, weights + kv.second, --left > 0))
                     return fail("weight upload failed");
         }
         auto dptr = [&](const GgufTensor* t) {
@@ -627,9 +635,30 @@ struct EahmmfEngine {
         C.slots = (int)std::min<size_t>(budget / C.foot, (size_t)n_layer * n_expert);
         if (C.slots < n_expert) return fail("expert budget below one layer's experts");
         if (!dalloc(C.dev, (size_t)C.slots * C.foot)) return fail("cannot allocate the expert cache");
-        C.pinned = cudaHostRegister(const_cast<uint8_t*>(C.file->map), C.file->size, cudaHostRegisterReadOnly) ==
-                   cudaSuccess;
-        if (!C.pinned) cudaGetLastError();  // fills then stage through the driver (slower, same bytes)
+        // DMA source: the mapping registered read-only, else a pinned copy of the file, else the pageable
+        // mapping (the driver then stages every fill)
+        C.host = C.file->map;
+        if (cudaHostRegister(const_cast<uint8_t*>(C.file->map), C.file->size, cudaHostRegisterReadOnly) == cudaSuccess) {
+            C.pinned = true;
+        } else {
+            cudaGetLastError();
+            if (cudaHostAlloc((void**)&C.host_copy, C.file->size, cudaHostAllocDefault) == cudaSuccess) {
+                const unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+                std::vector<std::thread> pool;
+                const size_t per = (C.file->size + nt - 1) / nt;
+                for (unsigned t = 0; t < nt; t++)
+                    pool.emplace_back([&, t]() {
+                        const size_t b = std::min(C.file->size, (size_t)t * per), n = std::min(C.file->size - b, per);
+                        memcpy(C.host_copy + b, C.file->map + b, n);
+                    });
+                for (auto& th : pool) th.join();
+                C.host = C.host_copy;
+                C.pinned = true;
+            } else {
+                cudaGetLastError();
+                C.host_copy = nullptr;
+            }
+        }
         const size_t nk = (size_t)n_layer * n_expert;
         for (int c = 0; c < 3; c++)
             if (C.src[c].size() != nk) return fail("expert table of the cache incomplete");
@@ -679,7 +708,7 @@ struct EahmmfEngine {
             if ((size_t)key >= C.src[c].size() || C.src[c][key] + C.comp[c] > C.file->size) return false;
         uint8_t* d = C.dev + (size_t)sl * C.foot;
         for (int c = 0; c < 3; c++)
-            if (cudaMemcpyAsync(d + C.off[c], C.file->map + C.src[c][key], C.comp[c], cudaMemcpyHostToDevice, C.side) !=
+            if (cudaMemcpyAsync(d + C.off[c], C.host + C.src[c][key], C.comp[c], cudaMemcpyHostToDevice, C.side) !=
                 cudaSuccess)
                 return false;
         if (cudaEventRecord(C.ready[sl], C.side) != cudaSuccess) return false;
@@ -746,15 +775,19 @@ struct EahmmfEngine {
     }
 
     // host -> device through two pinned staging halves (the mapping is pageable)
-    bool upload(const uint8_t* src, size_t n, uint8_t* dst = nullptr) {
+    // (keep_staging: the pinned halves stay allocated for the next call; the last call passes false)
+    uint8_t* up_stage[2] = {nullptr, nullptr};
+    cudaEvent_t up_ev[2] = {nullptr, nullptr};
+    bool upload(const uint8_t* src, size_t n, uint8_t* dst = nullptr, bool keep_staging = false) {
         if (!dst) dst = weights;
         const size_t half = 64u << 20;
-        uint8_t* stage[2] = {nullptr, nullptr};
-        cudaEvent_t ev[2] = {nullptr, nullptr};
+        uint8_t** stage = up_stage;
+        cudaEvent_t* ev = up_ev;
         bool ok = true;
-        for (int i = 0; i < 2 && ok; i++)
-            ok = cudaHostAlloc((void**)&stage[i], half, cudaHostAllocDefault) == cudaSuccess &&
-                 cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) == cudaSuccess;
+        for (int i = 0; i < 2 && ok; i++) {
+            if (!stage[i]) ok = cudaHostAlloc((void**)&stage[i], half, cudaHostAllocDefault) == cudaSuccess;
+            if (ok && !ev[i]) ok = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) == cudaSuccess;
+        }
         bool live[2] = {false, false};
         for (size_t o = 0, k = 0; ok && o < n; o += half, k ^= 1) {
             const size_t c = std::min(half, n - o);
@@ -766,10 +799,13 @@ struct EahmmfEngine {
             live[k] = true;
         }
         if (cudaStreamSynchronize(st) != cudaSuccess) ok = false;
-        for (int i = 0; i < 2; i++) {
-            if (stage[i]) cudaFreeHost(stage[i]);
-            if (ev[i]) cudaEventDestroy(ev[i]);
-        }
+        if (!keep_staging)
+            for (int i = 0; i < 2; i++) {
+                if (stage[i]) cudaFreeHost(stage[i]);
+                if (ev[i]) cudaEventDestroy(ev[i]);
+                stage[i] = nullptr;
+                ev[i] = nullptr;
+            }
         return ok;
     }
 
