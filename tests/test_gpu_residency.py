@@ -1,8 +1,8 @@
 """Expert residency beyond HBM (eahmmf_engine_load_budget): the engine with only a device cache of whole
 experts -- one layer's worth, or a few layers' -- against the fully resident engine on the same model and
 prompt: the prompt logits bitwise equal and the greedy tokens exact (the kernels read the same expert
-bytes from cache slots), with the cache counters showing misses and, at the minimum cache of one layer's
-experts, evictions, prefetch fills and hits on prefetched experts; the resident copies pass the hash64 verify. Models: the small all-K-quant model and
+bytes from cache slots), with the cache counters showing misses and, where the small model's layers
+cannot all stay resident, evictions, prefetch fills and hits on prefetched experts; the resident copies pass the hash64 verify. Models: the small all-K-quant model and
 the Qwen3-30B-A3B shape reduced to 4 layers.
 """
 import os
@@ -57,13 +57,13 @@ def test_budgeted_engine_matches_resident(models, model, layers_worth):
         st = e.cache_stats()
         assert st["slots"] == int(layers_worth * cfg.n_expert)
         assert st["misses"] > 0 and st["bytes_h2d"] > 0
-        if layers_worth == 1.0:  # the minimum cache: the layers' routed experts cannot all stay
+        if model == "kquant" and layers_worth == 1.0:  # its layers' routed experts cannot all stay at once
             assert st["evictions"] > 0 and st["prefetched"] > 0
         # a second generation: the decode steps' prefetches of the next layer's last routed experts hit
         rc, got2, _ = e.greedy(prompt, n_gen, 32)
         assert rc == 0
         np.testing.assert_array_equal(got2, want)
-        if layers_worth == 1.0:
+        if model == "kquant" and layers_worth == 1.0:
             assert e.cache_stats()["prefetch_hits"] > 0
         rc, n, bad = e.verify()
         assert rc == 0 and n > 0 and bad == 0
