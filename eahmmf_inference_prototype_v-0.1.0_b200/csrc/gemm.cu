@@ -12,9 +12,10 @@
 //      rows, 128 slots). A producer lane streams (W, activations) stage blocks into a 6-deep shared-
 //      memory ring (1-D bulk copies, mbarrier complete_tx); one lane issues tcgen05.mma (M 128, N 128,
 //      K 16, f16 in, fp32 accumulate in tensor memory) and commits each stage back to the producer; two
-//      accumulators in tensor memory let
-//      four epilogue warps read tile i (tcgen05.ld) while tile i+1 accumulates. The epilogue pairs
-//      gate and up rows through shared memory and writes h = SiLU(g) * u (qwen3moe.cpp:1056-1059).
+//      accumulators in tensor memory let four epilogue warps read tile i (tcgen05.ld) while tile i+1
+//      accumulates. The slot tile is the MMA's A operand here, so an accumulator row is one slot holding
+//      its 64 gate and 64 up values: each thread forms h = SiLU(g) * u (qwen3moe.cpp:1056-1059) for its
+//      own slot and the warp writes the rows out as whole lines through a shared-memory transpose.
 //   4. k_gemm_tc<DOWN>: tiles of (expert, 128 rows of D, 128 slots) over h, writing y per slot; the
 //      weighted combine in expert order is k_moe_combine (moe.cu).
 #include <cuda_fp16.h>
@@ -221,7 +222,8 @@ constexpr int TC_KT = 64;                                     // K elements per 
 constexpr int TC_BLOCK = 128 * TC_KT * 2;                     // one 128-row f16 stage block: 16 KB
 constexpr int TC_STAGES = 6;
 constexpr int TC_STAGE_BYTES = 2 * TC_BLOCK;                  // W, activations
-constexpr int TC_U_BYTES = 128 * 64 * 4;                      // gate/up pairing buffer
+constexpr int TC_XP = 36;                                     // row stride (floats) of an epilogue transpose tile
+constexpr int TC_U_BYTES = 4 * 32 * TC_XP * 4;                 // one 32 x 32 transpose tile per epilogue warp
 constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + TC_U_BYTES + 256;
 constexpr int TC_NT = 192;  // warp 0 producer, warp 1 MMA + tensor-memory owner, warps 2..5 epilogue
 
@@ -252,7 +254,7 @@ __device__ __forceinline__ bool tc_tile(const GroupedArgs& g, int b, TcTile& t) 
 template <int MODE>
 __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     extern __shared__ __align__(1024) uint8_t smt[];
-    float* U = reinterpret_cast<float*>(smt + TC_STAGES * TC_STAGE_BYTES);  // [128 slots][64 rows]
+    float* U = reinterpret_cast<float*>(smt + TC_STAGES * TC_STAGE_BYTES);  // [4 warps][32][TC_XP]
     uint64_t* bars = reinterpret_cast<uint64_t*>(smt + TC_STAGES * TC_STAGE_BYTES + TC_U_BYTES);
     uint64_t* full = bars;                    // [TC_STAGES] stage landed
     uint64_t* empty = bars + TC_STAGES;       // [TC_STAGES] stage consumed by the MMAs
@@ -330,11 +332,14 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t base = smem_u32(smt + s * TC_STAGE_BYTES);
+                    // gate/up: A = the slot tile, B = the 128 weight rows (accumulator rows are slots);
+                    // down: A = the weight rows, B = the slot tile (accumulator rows are output rows)
+                    const uint32_t wbase = smem_u32(smt + s * TC_STAGE_BYTES), xbase = wbase + TC_BLOCK;
+                    const uint32_t abase = MODE == 0 ? xbase : wbase, bbase = MODE == 0 ? wbase : xbase;
 #pragma unroll
                     for (int j = 0; j < TC_KT / 16; j++) {
-                        const uint64_t da = tc_desc(base + 256 * j, 128, (TC_KT / 8) * 128);
-                        const uint64_t db = tc_desc(base + TC_BLOCK + 256 * j, 128, (TC_KT / 8) * 128);
+                        const uint64_t da = tc_desc(abase + 256 * j, 128, (TC_KT / 8) * 128);
+                        const uint64_t db = tc_desc(bbase + 256 * j, 128, (TC_KT / 8) * 128);
                         tc_mma_f16(acc, da, db, idesc, (kt > 0 || j > 0) ? 1u : 0u);
                     }
                     tc_commit(&empty[s]);  // the stage is free once these MMAs completed
@@ -347,53 +352,63 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
             }
         }
     } else {  // ---------------- epilogue: warps 2..5, tensor-memory lane quadrant warp % 4
-        const int q = warp & 3, row = 32 * q + lane;
+        const int q = warp & 3;
+        float* xp = U + (warp - 2) * (32 * TC_XP);  // this warp's 32 x 32 transpose tile
         int ti = 0;
         TcTile t;
         for (int b = blockIdx.x; tc_tile<MODE>(g, b, t); b += gridDim.x, ti++) {
             const int a = ti & 1;
             bool ok = mbar_wait_bounded(&acc_full[a], (uint32_t)(ti / 2) & 1u);
-            if (!ok) fail();
+            ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads below are warp-collective
+            if (!ok && lane == 0) fail();
             tc_fence_after();
             const uint32_t acc = tmem + (uint32_t)(128 * a) + ((uint32_t)(32 * q) << 16);
             const float* rs = g.rs + (size_t)t.e * (2 * g.FF + g.D);
             if (MODE == 0) {
-                if (ok && q >= 2) {  // up rows: scaled values to the pairing buffer
-                    const float su = rs[g.FF + 64 * t.rt + row - 64];
-                    for (int c0 = 0; c0 < 128; c0 += 16) {
-                        float v[16];
-                        tc_ld16(acc + (uint32_t)c0, v);
+                // Accumulator row = slot 32 q + lane of the tile; columns 0..63 are its gate rows, 64..127
+                // the same up rows, so each thread pairs its own values. Rows go out through the warp's
+                // transpose tile: 32 rows x 32 columns per pass, written back as whole 128-byte lines.
+                const int sl = 32 * q + lane;
+                const float bs = sl < t.mc ? g.bscale[t.m0 + sl] : 0.f;
+                for (int half = 0; ok && half < 2; half++) {
+                    const float sg = rs[64 * t.rt + 32 * half + lane], su = rs[g.FF + 64 * t.rt + 32 * half + lane];
 #pragma unroll
-                        for (int j = 0; j < 16; j++) U[(c0 + j) * 64 + row - 64] = v[j] * su;
-                    }
-                }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (ok && q < 2) {
-                    const float sg = rs[64 * t.rt + row];
-                    for (int c0 = 0; c0 < 128; c0 += 16) {
-                        float v[16];
-                        tc_ld16(acc + (uint32_t)c0, v);
+                    for (int c0 = 0; c0 < 32; c0 += 16) {
+                        float gv[16], uv[16];
+                        tc_ld16x2(acc + (uint32_t)(32 * half + c0), acc + (uint32_t)(64 + 32 * half + c0), gv, uv);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            const int col = c0 + j;
-                            if (col < t.mc) {
-                                const float bs = g.bscale[t.m0 + col];
-                                const float gv = v[j] * sg * bs, uv = U[col * 64 + row] * bs;
-                                g.h[(size_t)(t.m0 + col) * g.FF + 64 * t.rt + row] = silu_mul(gv, uv);
-                            }
+                            const float gs = __shfl_sync(0xffffffffu, sg, c0 + j), us = __shfl_sync(0xffffffffu, su, c0 + j);
+                            gv[j] = silu_mul(gv[j] * gs * bs, uv[j] * us * bs);
                         }
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4*>(xp + lane * TC_XP + c0 + j) = make_float4(gv[j], gv[j + 1], gv[j + 2], gv[j + 3]);
                     }
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r = 4 * i + (lane >> 3), c = 4 * (lane & 7), sr = 32 * q + r;
+                        if (sr < t.mc)
+                            *reinterpret_cast<float4*>(g.h + (size_t)(t.m0 + sr) * g.FF + 64 * t.rt + 32 * half + c) =
+                                *reinterpret_cast<const float4*>(xp + r * TC_XP + c);
+                    }
+                    __syncwarp();
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");  // U is reused by the next tile
             } else if (ok) {
+                // accumulator row = output row 128 rt + 32 q + lane, column = slot: each column store is
+                // one 128-byte line; the slot scales of 32 columns come from one load and lane shuffles
+                const int row = 32 * q + lane;
                 const float sd = rs[2 * g.FF + 128 * t.rt + row];
-                for (int c0 = 0; c0 < 128; c0 += 16) {
-                    float v[16];
-                    tc_ld16(acc + (uint32_t)c0, v);
+                for (int c0 = 0; c0 < t.mc; c0 += 32) {
+                    const float bsl = c0 + lane < t.mc ? g.bscale[t.m0 + c0 + lane] : 0.f;
+                    float v[16], w[16];
+                    tc_ld16x2(acc + (uint32_t)c0, acc + (uint32_t)(c0 + 16), v, w);
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const int col = c0 + j;
-                        if (col < t.mc) g.y[(size_t)(t.m0 + col) * g.D + 128 * t.rt + row] = v[j] * sd * g.bscale[t.m0 + col];
+                        const float b0 = __shfl_sync(0xffffffffu, bsl, j), b1 = __shfl_sync(0xffffffffu, bsl, 16 + j);
+                        if (c0 + j < t.mc) g.y[(size_t)(t.m0 + c0 + j) * g.D + 128 * t.rt + row] = v[j] * sd * b0;
+                        if (c0 + 16 + j < t.mc) g.y[(size_t)(t.m0 + c0 + 16 + j) * g.D + 128 * t.rt + row] = w[j] * sd * b1;
                     }
                 }
             }
