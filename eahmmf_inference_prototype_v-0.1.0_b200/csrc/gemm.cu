@@ -2,8 +2,8 @@
 // the per-expert projections as dense contractions on the 5th-generation tensor cores (tcgen05).
 //
 //   1. k_dequant_f16: every active expert's gate/up/down rows dequantized once (the reference decoders,
-//      qwen3moe.cpp:142-202, exact fp32) and stored as f16 scaled by a per-row power of two, so that
-//      the f16 rounding (2^-12 relative) is the only loss.
+//      qwen3moe.cpp:142-202, exact fp32) and stored as f16 scaled by a per-row power of two (from a bound
+//      read off the super-block headers), so that the f16 rounding (2^-12 relative) is the only loss.
 //   2. k_pack_slots: each slot's activation row (its token's xn for gate/up, its h for down) as a
 //      power-of-two scale and f16 values of x/s (2^-12 relative rounding, like the weights).
 //   Both are written tile-major in the tensor cores' K-major core-matrix order (8 rows x 16 bytes), so
@@ -131,36 +131,79 @@ __device__ __forceinline__ size_t tile_off(int r, int k) {
     return (size_t)(k >> 6) * (128 * 64) + (size_t)(((r >> 3) * 8 + ((k & 63) >> 3)) * 64 + (r & 7) * 8 + (k & 7));
 }
 
-// ---- 1. expert weights -> scaled f16, tile-major; one warp per row of an active expert
+// SiLU(g) * u with the fast exponential and division (a few ulp): this path's operands already carry
+// the f16 rounding, 2^-12 relative, so the IEEE forms of the single-token kernels buy nothing here.
+__device__ __forceinline__ float silu_mul_fast(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+
+// Upper bound of |y| over super-block sb of a K-quant row, from its header alone: Q4_K / Q5_K
+// y = d sc q - dmin m with q in [0, 15] / [0, 31]; Q6_K y = d sc (q - 32) with q - 32 in [-32, 31].
+__device__ float kq_bound(const uint8_t* row, int type, int sb) {
+    if (type == T_Q6_K) {
+        const uint8_t* b = row + (size_t)sb * 210;
+        int ms = 0;
+#pragma unroll
+        for (int j = 0; j < 16; j++) ms = max(ms, abs((int)reinterpret_cast<const int8_t*>(b + 192)[j]));
+        return fabsf(h16(b + 208)) * (float)ms * 32.f;
+    }
+    const bool q5 = type == T_Q5_K;
+    const uint8_t* b = row + (size_t)sb * (q5 ? 176 : 144);
+    const float d = fabsf(h16(b)), dm = fabsf(h16(b + 2)), qmax = q5 ? 31.f : 15.f;
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        int sc, mn;
+        sm_k4(j, b + 4, sc, mn);
+        m = fmaxf(m, d * (float)sc * qmax + dm * (float)mn);
+    }
+    return m;
+}
+
+// ---- 1. expert weights -> scaled f16, tile-major; one warp per 8-row group of an active expert
 // Per expert: gate/up tiles (FF/64 of them, A rows 0..63 = gate rows 64 rt.., 64..127 = the same up rows,
-// D/64 stages), then down tiles (D/128, FF/64 stages).
+// D/64 stages), then down tiles (D/128, FF/64 stages). Each row's scale is the power of two of an upper
+// bound of its max|y|; the bound only has to keep the f16 values below 2^14, and since the scale is a
+// power of two the f16 rounding of y / s is the same whatever binade it lands in. K-quant rows take the
+// bound from their super-block headers (one decode pass), other types decode twice. Eight rows of one
+// core-matrix row group per warp: every 64-element K chunk of the group is one contiguous 1 KB block
+// of the tile, written by the warp as 32 x 2 full-line 16-byte stores.
 __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
     pdl_wait();
     pdl_trigger();
     const int rows_e = 2 * g.FF + g.D;  // gate, up, down rows of one expert
+    const int groups_e = rows_e / 8;
     const long long gw = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    const int e = (int)(gw / rows_e), r = (int)(gw - (long long)e * rows_e);
+    const int e = (int)(gw / groups_e), r0 = 8 * (int)(gw - (long long)e * groups_e);
     if (e >= g.E) return;
     if (g.offsets[e + 1] == g.offsets[e]) return;  // expert not routed in this call
-    const int c = r < g.FF ? 0 : r < 2 * g.FF ? 1 : 2;
-    const int row = c == 2 ? r - 2 * g.FF : r - c * g.FF;
+    const int c = r0 < g.FF ? 0 : r0 < 2 * g.FF ? 1 : 2;
+    const int row0 = c == 2 ? r0 - 2 * g.FF : r0 - c * g.FF;
     const int K = c == 2 ? g.FF : g.D;
-    const uint8_t* src = g.w[c][e] + (size_t)row * g.rb[c];
+    const size_t rb = g.rb[c];
     const int type = g.type[c];
-    const bool fast = (type == T_Q4_K || type == T_Q5_K) && (reinterpret_cast<uintptr_t>(src) & 7) == 0;
-    auto deq = [&](int i, float (&y)[8]) {
-        if (fast) dq8_k45(src, type == T_Q5_K, i, y);
-        else dq8(src, type, i, y);
-    };
-    float m = 0.f;
-    for (int i = 8 * lane; i < K; i += 256) {
-        float y[8];
-        deq(i, y);
+    const uint8_t* src0 = g.w[c][e] + (size_t)row0 * rb;
+    float m_own = 0.f;  // lane r < 8: the bound of row r of the group
+    for (int r = 0; r < 8; r++) {
+        float m = 0.f;
+        if (is_kquant(type)) {
+            for (int sb = lane; sb < K / 256; sb += 32) m = fmaxf(m, kq_bound(src0 + (size_t)r * rb, type, sb));
+        } else {
+            for (int i = 8 * lane; i < K; i += 256) {
+                float y[8];
+                dq8(src0 + (size_t)r * rb, type, i, y);
 #pragma unroll
-        for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(y[j]));
+                for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(y[j]));
+            }
+        }
+        m = warp_max(m);
+        if (lane == r) m_own = m;
     }
-    const float s = pow2_scale(warp_max(m)), inv = 1.f / s;  // exact: powers of two
+    const float s_own = pow2_scale(m_own);
+    // this lane: row r of the group, elements 16 (lane % 4) .. +15 of every 64-element chunk
+    const int r = lane >> 2, kq = 16 * (lane & 3), row = row0 + r;
+    const float inv = 1.f / __shfl_sync(0xffffffffu, s_own, r);  // exact: powers of two
+    const uint8_t* src = src0 + (size_t)r * rb;
+    const bool fast = (type == T_Q4_K || type == T_Q5_K) && (reinterpret_cast<uintptr_t>(src) & 7) == 0;
     __half* base = g.wf + (size_t)e * g.w_expert;
     int ar;  // row within its 128-row tile
     if (c < 2) {
@@ -170,15 +213,26 @@ __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
         base += (size_t)2 * g.FF * g.D + (size_t)(row >> 7) * 128 * K;
         ar = row & 127;
     }
-    for (int i = 8 * lane; i < K; i += 256) {
-        float y[8];
-        deq(i, y);
-        __align__(16) __half o[8];
+    for (int k0 = 0; k0 < K; k0 += 64) {
+        const int i = k0 + kq;
+        float y[8], z[8];
+        if (fast) {
+            dq8_k45(src, type == T_Q5_K, i, y);
+            dq8_k45(src, type == T_Q5_K, i + 8, z);
+        } else {
+            dq8(src, type, i, y);
+            dq8(src, type, i + 8, z);
+        }
+        __align__(16) __half o[8], p[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) o[j] = __float2half_rn(y[j] * inv);
+        for (int j = 0; j < 8; j++) {
+            o[j] = __float2half_rn(y[j] * inv);
+            p[j] = __float2half_rn(z[j] * inv);
+        }
         *reinterpret_cast<uint4*>(base + tile_off(ar, i)) = *reinterpret_cast<const uint4*>(o);
+        *reinterpret_cast<uint4*>(base + tile_off(ar, i + 8)) = *reinterpret_cast<const uint4*>(p);
     }
-    if (lane == 0) g.rs[(size_t)e * rows_e + r] = s;
+    if (lane < 8) g.rs[(size_t)e * rows_e + r0 + lane] = s_own;
 }
 
 // ---- 2. slot rows -> scale + f16 hi/lo, tile-major by (expert, slot tile); one warp per slot
@@ -379,7 +433,7 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
                             const float gs = __shfl_sync(0xffffffffu, sg, c0 + j), us = __shfl_sync(0xffffffffu, su, c0 + j);
-                            gv[j] = silu_mul(gv[j] * gs * bs, uv[j] * us * bs);
+                            gv[j] = silu_mul_fast(gv[j] * gs * bs, uv[j] * us * bs);
                         }
 #pragma unroll
                         for (int j = 0; j < 16; j += 4)
@@ -400,8 +454,13 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                 // one 128-byte line; the slot scales of 32 columns come from one load and lane shuffles
                 const int row = 32 * q + lane;
                 const float sd = rs[2 * g.FF + 128 * t.rt + row];
-                for (int c0 = 0; c0 < t.mc; c0 += 32) {
-                    const float bsl = c0 + lane < t.mc ? g.bscale[t.m0 + c0 + lane] : 0.f;
+                float bsv[4];  // slot scales of columns 32 i + lane, loaded before any store of the tile
+#pragma unroll
+                for (int i = 0; i < 4; i++) bsv[i] = 32 * i + lane < t.mc ? g.bscale[t.m0 + 32 * i + lane] : 0.f;
+#pragma unroll
+                for (int c0 = 0; c0 < 128; c0 += 32) {
+                    if (c0 >= t.mc) break;
+                    const float bsl = bsv[c0 / 32];
                     float v[16], w[16];
                     tc_ld16x2(acc + (uint32_t)c0, acc + (uint32_t)(c0 + 16), v, w);
 #pragma unroll
@@ -425,7 +484,8 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
 
 // ---- launchers ----------------------------------------------------------------------------------
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st) {
-    const long long warps = (long long)g.E * (2 * g.FF + g.D);
+    if (g.FF % 8 || g.D % 8) return cudaErrorInvalidValue;
+    const long long warps = (long long)g.E * ((2 * g.FF + g.D) / 8);
     return launch_pdl(k_dequant_f16, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, st, g);
 }
 cudaError_t launch_pack_slots(const GroupedArgs& g, int mode, int S, cudaStream_t st) {
