@@ -183,7 +183,7 @@ constexpr int GROUPED_MIN_T = 256;
 constexpr int GROUPED_MIN_SLOTS_PER_EXPERT = 16;
 struct GroupedLayout {
     size_t ids, wts, logits, offsets, active, ngroups, cnt, local, tiles_gu, tiles_dn, slot_token, slot_w,
-        token_slots, wf, rs, bhi, bscale, h, y, total;
+        token_slots, wf, rs, bhi, bscale, tscale, h, y, total;
 };
 GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
     const size_t K = (size_t)L->n_used, E = (size_t)L->n_expert, S = (size_t)T * K, D = L->D, FF = L->FF;
@@ -212,6 +212,7 @@ GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
     const size_t kmax = D > FF ? D : FF;
     take(w.bhi, tiles * 128 * kmax * 2);
     take(w.bscale, S * 4);
+    take(w.tscale, (size_t)T * 4);
     take(w.h, S * FF * 4);
     take(w.y, S * D * 4);
     w.total = o;
@@ -340,6 +341,7 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g.FF = L->FF;
     g.offsets = a.rw.offsets;
     g.slot_token = a.rw.slot_token;
+    g.T = T;
     g.tiles_gu = tiles_gu;
     g.tiles_dn = tiles_dn;
     g.wf = reinterpret_cast<__half*>(ws + w.wf);
@@ -352,6 +354,7 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g.h = reinterpret_cast<float*>(ws + w.h);
     g.bhi = reinterpret_cast<__half*>(ws + w.bhi);
     g.bscale = reinterpret_cast<float*>(ws + w.bscale);
+    g.tscale = reinterpret_cast<float*>(ws + w.tscale);
     g.y = a.y;
     g.status = d_status;
     g_prof.mark(0, st);
@@ -365,13 +368,14 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g_prof.mark(1, st);
     if (cudaMemsetAsync(cnt, 0, (size_t)E * 4, st) != cudaSuccess || launch_route_big(a, cnt, local, st) != cudaSuccess ||
         launch_plan_big(a, cnt, tiles_gu, tiles_dn, st) != cudaSuccess || launch_scatter_big(a, local, st) != cudaSuccess ||
-        launch_grouped_dequant(g, st) != cudaSuccess || launch_pack_slots(g, 0, S, st) != cudaSuccess)
+        launch_grouped_dequant(g, st) != cudaSuccess)
         return ST_CUDA;
-    g_prof.mark(2, st);
     const int slot_tiles = (S + 127) / 128 + E;  // bound on sum over experts of ceil(m_e / 128)
+    if (launch_pack_tokens(g, slot_tiles, st) != cudaSuccess) return ST_CUDA;
+    g_prof.mark(2, st);
     if (launch_grouped_gemm(g, 0, (L->FF / 64) * slot_tiles, st) != cudaSuccess) return ST_CUDA;
     g_prof.mark(3, st);
-    if (launch_pack_slots(g, 1, S, st) != cudaSuccess ||
+    if (launch_pack_slots(g, S, st) != cudaSuccess ||
         launch_grouped_gemm(g, 1, (L->D / 128) * slot_tiles, st) != cudaSuccess || launch_moe_combine(a, st) != cudaSuccess)
         return ST_CUDA;
     g_prof.mark(4, st);

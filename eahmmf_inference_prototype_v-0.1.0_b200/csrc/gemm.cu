@@ -4,8 +4,9 @@
 //   1. k_dequant_f16: every active expert's gate/up/down rows dequantized once (the reference decoders,
 //      qwen3moe.cpp:142-202, exact fp32) and stored as f16 scaled by a per-row power of two (from a bound
 //      read off the super-block headers), so that the f16 rounding (2^-12 relative) is the only loss.
-//   2. k_pack_slots: each slot's activation row (its token's xn for gate/up, its h for down) as a
-//      power-of-two scale and f16 values of x/s (2^-12 relative rounding, like the weights).
+//   2. k_token_scale + k_pack_groups / k_pack_slots: the activation rows of the slots (for gate/up each
+//      token's xn, its scale found once per token; for down each slot's h) as a power-of-two scale and
+//      f16 values of x/s (2^-12 relative rounding, like the weights).
 //   Both are written tile-major in the tensor cores' K-major core-matrix order (8 rows x 16 bytes), so
 //   that one 64-element K stage of a 128-row tile is one contiguous 16 KB block: a single bulk copy.
 //   3. k_gemm_tc<GATEUP>: persistent, warp-specialised. Tiles are (expert, 64 gate rows + the same 64 up
@@ -81,36 +82,6 @@ __device__ void dq8(const uint8_t* row, int type, int i, float (&y)[8]) {
         for (int j = 0; j < 8; j++) y[j] = reinterpret_cast<const float*>(row)[i + j];
     }
 }
-// The same for Q4_K / Q5_K rows on an 8-byte boundary: word loads of the header and of the 8 quant bytes.
-__device__ void dq8_k45(const uint8_t* row, bool q5, int i, float (&y)[8]) {
-    const uint8_t* b = row + (i >> 8) * (q5 ? 176 : 144);
-    const int e = i & 255, c = e >> 6, hi = (e >> 5) & 1, l0 = e & 31, j = 2 * c + hi;
-    const uint32_t dd = *reinterpret_cast<const uint32_t*>(b);
-    const uint32_t s0 = *reinterpret_cast<const uint32_t*>(b + 4), s1 = *reinterpret_cast<const uint32_t*>(b + 8),
-                   s2 = *reinterpret_cast<const uint32_t*>(b + 12);
-    // 6-bit scale / min j from the 12 header bytes (scale_min_k4, qwen3moe.cpp:133-141)
-    auto byte = [&](int k) -> int { return (int)(((k < 4 ? s0 : k < 8 ? s1 : s2) >> (8 * (k & 3))) & 0xff); };
-    int sc, mn;
-    if (j < 4) {
-        sc = byte(j) & 63;
-        mn = byte(j + 4) & 63;
-    } else {
-        sc = (byte(j + 4) & 0x0f) | ((byte(j - 4) >> 6) << 4);
-        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
-    }
-    const float d = __half2float(__ushort_as_half((unsigned short)(dd & 0xffff))) * (float)sc;
-    const float o = __half2float(__ushort_as_half((unsigned short)(dd >> 16))) * (float)mn;
-    const uint2 qw = *reinterpret_cast<const uint2*>(b + (q5 ? 48 : 16) + 32 * c + l0);
-    uint2 hw = make_uint2(0u, 0u);
-    if (q5) hw = *reinterpret_cast<const uint2*>(b + 16 + l0);
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const uint32_t qb = ((k < 4 ? qw.x : qw.y) >> (8 * (k & 3))) & 0xff;
-        int q = hi ? (int)(qb >> 4) : (int)(qb & 0x0f);
-        if (q5) q += (int)((((k < 4 ? hw.x : hw.y) >> (8 * (k & 3))) >> j) & 1) << 4;
-        y[k] = d * (float)q - o;
-    }
-}
 // power-of-two scale that brings max|x| into [2^13, 2^14) (1 for an all-zero row)
 __device__ __forceinline__ float pow2_scale(float m) {
     if (!(m > 0.f) || !isfinite(m)) return 1.f;
@@ -129,6 +100,60 @@ __device__ __forceinline__ float warp_max(float v) {
 // consecutive 128 x 64 blocks: stage k / 64, then core matrix (r / 8, (k % 64) / 8), row r % 8.
 __device__ __forceinline__ size_t tile_off(int r, int k) {
     return (size_t)(k >> 6) * (128 * 64) + (size_t)(((r >> 3) * 8 + ((k & 63) >> 3)) * 64 + (r & 7) * 8 + (k & 7));
+}
+
+// Byte k of w (0..255) as a float, exactly: the bit pattern 0x4B0000bb is 2^23 + bb.
+template <int k>
+__device__ __forceinline__ float byte_f(uint32_t w) {
+    return __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7650u | k)) - 8388608.f;
+}
+// little-endian 32-bit word at a 2-byte-aligned address
+__device__ __forceinline__ uint32_t ld32_a2(const uint8_t* p) {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+    return (uint32_t)q[0] | ((uint32_t)q[1] << 16);
+}
+// Elements 64 c + kq .. +15 (kq a multiple of 16) of the Q4_K / Q5_K super-block at b (16-byte aligned),
+// times the power of two inv, as 8 f16 pairs. Same values as dq8: d q is exact in fp32 (an 11-bit f16
+// times a 6-bit scale times a 5-bit quant), so fma(d inv, q, -o inv) rounds (d q - o) once and scales it
+// exactly. Four quants per word: nibble masks, then byte permutes into 2^23 + q.
+__device__ __forceinline__ void dq16_k45(const uint8_t* b, bool q5, int c, int kq, float inv, __half2 (&o)[8]) {
+    const int hi = kq >> 5, l0 = kq & 31, j = 2 * c + hi;
+    const uint4 hd = *reinterpret_cast<const uint4*>(b);  // d, dmin, 12 scale / min bytes
+    auto byte = [&](int k) -> int { return (int)(((k < 4 ? hd.y : k < 8 ? hd.z : hd.w) >> (8 * (k & 3))) & 0xff); };
+    int sc, mn;
+    if (j < 4) {
+        sc = byte(j) & 63;
+        mn = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 0x0f) | ((byte(j - 4) >> 6) << 4);
+        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))) * (float)sc * inv;
+    const float mo = -(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))) * (float)mn * inv);
+    const uint4 qw = *reinterpret_cast<const uint4*>(b + (q5 ? 48 : 16) + 32 * c + l0);
+    const uint4 hw = q5 ? *reinterpret_cast<const uint4*>(b + 16 + l0) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ha[4] = {hw.x, hw.y, hw.z, hw.w};
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        uint32_t nib = hi ? (qa[w] >> 4) & 0x0f0f0f0fu : qa[w] & 0x0f0f0f0fu;
+        if (q5) nib |= ((ha[w] >> j) & 0x01010101u) << 4;
+        o[2 * w] = __floats2half2_rn(fmaf(d, byte_f<0>(nib), mo), fmaf(d, byte_f<1>(nib), mo));
+        o[2 * w + 1] = __floats2half2_rn(fmaf(d, byte_f<2>(nib), mo), fmaf(d, byte_f<3>(nib), mo));
+    }
+}
+// The same for a Q6_K super-block at b (2-byte aligned): y = d s (q - 32) is exact in fp32.
+__device__ __forceinline__ void dq16_q6k(const uint8_t* b, int c, int kq, float inv, __half2 (&o)[8]) {
+    const int h = c >> 1, quad = 2 * (c & 1) + (kq >> 5), l0 = kq & 31, shift = 2 * quad;
+    const uint8_t* ql = b + 64 * h + kq;  // = 64 h + 32 (quad & 1) + l0
+    const uint8_t* qh = b + 128 + 32 * h + l0;
+    const float ds = h16(b + 208) * (float)reinterpret_cast<const int8_t*>(b)[192 + 8 * h + (l0 >> 4) + 2 * quad] * inv;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        const uint32_t lw = ld32_a2(ql + 4 * w), hw = ld32_a2(qh + 4 * w);
+        const uint32_t v = ((c & 1) ? (lw >> 4) & 0x0f0f0f0fu : lw & 0x0f0f0f0fu) | (((hw >> shift) & 0x03030303u) << 4);
+        o[2 * w] = __floats2half2_rn(ds * (byte_f<0>(v) - 32.f), ds * (byte_f<1>(v) - 32.f));
+        o[2 * w + 1] = __floats2half2_rn(ds * (byte_f<2>(v) - 32.f), ds * (byte_f<3>(v) - 32.f));
+    }
 }
 
 // SiLU(g) * u with the fast exponential and division (a few ulp): this path's operands already carry
@@ -166,12 +191,17 @@ __device__ float kq_bound(const uint8_t* row, int type, int sb) {
 // bound from their super-block headers (one decode pass), other types decode twice. Eight rows of one
 // core-matrix row group per warp: every 64-element K chunk of the group is one contiguous 1 KB block
 // of the tile, written by the warp as 32 x 2 full-line 16-byte stores.
-__global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
+// The group's 8 rows are one contiguous span of 8 x row-bytes; when it is 16-byte aligned the warp first
+// copies it into its shared-memory slot (`stage` bytes per warp) with every 16-byte load in flight at
+// once, and decodes from there.
+constexpr int DQ_WARPS = 4;
+__global__ void __launch_bounds__(32 * DQ_WARPS) k_dequant_f16(GroupedArgs g, int stage) {
+    extern __shared__ __align__(16) uint8_t dq_raw[];
     pdl_wait();
     pdl_trigger();
     const int rows_e = 2 * g.FF + g.D;  // gate, up, down rows of one expert
     const int groups_e = rows_e / 8;
-    const long long gw = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5;
+    const long long gw = ((long long)blockIdx.x * (32 * DQ_WARPS) + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int e = (int)(gw / groups_e), r0 = 8 * (int)(gw - (long long)e * groups_e);
     if (e >= g.E) return;
@@ -182,6 +212,16 @@ __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
     const size_t rb = g.rb[c];
     const int type = g.type[c];
     const uint8_t* src0 = g.w[c][e] + (size_t)row0 * rb;
+    const size_t span = 8 * rb;
+    if (stage && span <= (size_t)stage && span % 16 == 0 && (reinterpret_cast<uintptr_t>(src0) & 15) == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(dq_raw + (size_t)(threadIdx.x >> 5) * stage);
+        const uint4* gsrc = reinterpret_cast<const uint4*>(src0);
+        const int n16 = (int)(span / 16);
+#pragma unroll 8
+        for (int i = lane; i < n16; i += 32) dst[i] = __ldg(gsrc + i);
+        __syncwarp();
+        src0 = reinterpret_cast<const uint8_t*>(dst);
+    }
     float m_own = 0.f;  // lane r < 8: the bound of row r of the group
     for (int r = 0; r < 8; r++) {
         float m = 0.f;
@@ -203,7 +243,9 @@ __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
     const int r = lane >> 2, kq = 16 * (lane & 3), row = row0 + r;
     const float inv = 1.f / __shfl_sync(0xffffffffu, s_own, r);  // exact: powers of two
     const uint8_t* src = src0 + (size_t)r * rb;
-    const bool fast = (type == T_Q4_K || type == T_Q5_K) && (reinterpret_cast<uintptr_t>(src) & 7) == 0;
+    const bool fast45 = (type == T_Q4_K || type == T_Q5_K) && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+    const bool fast6 = type == T_Q6_K && (reinterpret_cast<uintptr_t>(src) & 1) == 0;
+    const int bsz = type == T_Q5_K ? 176 : type == T_Q6_K ? 210 : 144;
     __half* base = g.wf + (size_t)e * g.w_expert;
     int ar;  // row within its 128-row tile
     if (c < 2) {
@@ -215,34 +257,102 @@ __global__ void __launch_bounds__(256) k_dequant_f16(GroupedArgs g) {
     }
     for (int k0 = 0; k0 < K; k0 += 64) {
         const int i = k0 + kq;
-        float y[8], z[8];
-        if (fast) {
-            dq8_k45(src, type == T_Q5_K, i, y);
-            dq8_k45(src, type == T_Q5_K, i + 8, z);
+        __align__(16) __half2 o[8];
+        if (fast45) {
+            dq16_k45(src + (size_t)(i >> 8) * bsz, type == T_Q5_K, (i >> 6) & 3, kq, inv, o);
+        } else if (fast6) {
+            dq16_q6k(src + (size_t)(i >> 8) * bsz, (i >> 6) & 3, kq, inv, o);
         } else {
+            float y[8], z[8];
             dq8(src, type, i, y);
             dq8(src, type, i + 8, z);
-        }
-        __align__(16) __half o[8], p[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            o[j] = __float2half_rn(y[j] * inv);
-            p[j] = __float2half_rn(z[j] * inv);
+            for (int j = 0; j < 4; j++) {
+                o[j] = __floats2half2_rn(y[2 * j] * inv, y[2 * j + 1] * inv);
+                o[4 + j] = __floats2half2_rn(z[2 * j] * inv, z[2 * j + 1] * inv);
+            }
         }
         *reinterpret_cast<uint4*>(base + tile_off(ar, i)) = *reinterpret_cast<const uint4*>(o);
-        *reinterpret_cast<uint4*>(base + tile_off(ar, i + 8)) = *reinterpret_cast<const uint4*>(p);
+        *reinterpret_cast<uint4*>(base + tile_off(ar, i + 8)) = *reinterpret_cast<const uint4*>(o + 4);
     }
     if (lane < 8) g.rs[(size_t)e * rows_e + r0 + lane] = s_own;
 }
 
-// ---- 2. slot rows -> scale + f16 hi/lo, tile-major by (expert, slot tile); one warp per slot
-template <int MODE>
+// ---- 2a. gate/up activations. k_token_scale: one warp per token, the power-of-two scale of its xn row
+// (every slot of the token packs the same row). k_pack_groups: one warp per 8 consecutive slots of one
+// expert's slot tile (a core-matrix row group): each 64-element K chunk of the group is one contiguous
+// 1 KB block of the tile, written as whole lines; rows past the expert's slots are written as zeros.
+__global__ void __launch_bounds__(256) k_token_scale(GroupedArgs g) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= g.T) return;
+    const float* xr = g.xn + (size_t)t * g.D;
+    float m = 0.f;
+    for (int i = 4 * lane; i < g.D; i += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    m = warp_max(m);
+    if (lane == 0) g.tscale[t] = pow2_scale(m);
+}
+
+__global__ void __launch_bounds__(256) k_pack_groups(GroupedArgs g) {
+    pdl_wait();
+    pdl_trigger();
+    const long long gw = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31, RT = g.FF / 64;
+    const int bt = (int)(gw >> 4), grp = (int)(gw & 15);  // slot tile, row group within it
+    if ((long long)bt * RT >= g.tiles_gu[g.E]) return;
+    int lo_ = 0, hi_ = g.E;  // expert of the slot tile: largest e with tiles_gu[e] <= bt RT
+    while (hi_ - lo_ > 1) {
+        const int mid = (lo_ + hi_) >> 1;
+        if (g.tiles_gu[mid] <= bt * RT) lo_ = mid;
+        else hi_ = mid;
+    }
+    const int e = lo_, cnt = g.offsets[e + 1] - g.offsets[e];
+    const int j0 = 128 * (bt - g.tiles_gu[e] / RT) + 8 * grp;
+    if (j0 >= cnt) return;
+    const int r = lane >> 2, kq = 16 * (lane & 3), jr = 8 * grp + r, K = g.D;
+    const bool valid = j0 + r < cnt;
+    const int slot = g.offsets[e] + j0 + r;
+    const int tok = valid ? g.slot_token[slot] : 0;
+    const float sc = valid ? g.tscale[tok] : 1.f, inv = valid ? 1.f / sc : 0.f;
+    const float* xr = g.xn + (size_t)tok * K + kq;
+    __half* bh = g.bhi + (size_t)bt * 128 * K;
+    for (int k0 = 0; k0 < K; k0 += 256) {  // four 64-element chunks: all loads first, then the stores
+        float4 v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                v[u][q] = k0 + 64 * u < K ? *reinterpret_cast<const float4*>(xr + k0 + 64 * u + 4 * q)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (k0 + 64 * u >= K) break;
+            __align__(16) __half2 hv[8];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                hv[2 * q] = __floats2half2_rn(v[u][q].x * inv, v[u][q].y * inv);
+                hv[2 * q + 1] = __floats2half2_rn(v[u][q].z * inv, v[u][q].w * inv);
+            }
+            const int i = k0 + 64 * u + kq;
+            *reinterpret_cast<uint4*>(bh + tile_off(jr, i)) = *reinterpret_cast<const uint4*>(hv);
+            *reinterpret_cast<uint4*>(bh + tile_off(jr, i + 8)) = *reinterpret_cast<const uint4*>(hv + 4);
+        }
+    }
+    if (valid && (lane & 3) == 0) g.bscale[slot] = sc;
+}
+
+// ---- 2b. down activations: each slot's h row -> scale + f16, tile-major by (expert, slot tile); one warp
+// per slot
 __global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
     pdl_wait();
     pdl_trigger();
     const int slot = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (slot >= S || slot >= g.offsets[g.E]) return;  // S bounds the grid; absent slots (given ids) hold none
-    const int K = MODE == 0 ? g.D : g.FF;
+    const int K = g.FF;
     int lo_ = 0, hi_ = g.E;  // expert of the slot: largest e with offsets[e] <= slot
     while (hi_ - lo_ > 1) {
         const int mid = (lo_ + hi_) >> 1;
@@ -251,7 +361,7 @@ __global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
     }
     const int e = lo_, j = slot - g.offsets[e];
     const int tile = g.tiles_gu[e] / (g.FF / 64) + (j >> 7), jr = j & 127;
-    const float* xr = MODE == 0 ? g.xn + (size_t)g.slot_token[slot] * K : g.h + (size_t)slot * K;
+    const float* xr = g.h + (size_t)slot * K;
     float m = 0.f;
     for (int i = 4 * lane; i < K; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
@@ -486,12 +596,30 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st) {
     if (g.FF % 8 || g.D % 8) return cudaErrorInvalidValue;
     const long long warps = (long long)g.E * ((2 * g.FF + g.D) / 8);
-    return launch_pdl(k_dequant_f16, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, st, g);
+    size_t span = 0;
+    for (int c = 0; c < 3; c++) span = std::max(span, 8 * g.rb[c]);
+    int stage = (int)((span + 15) / 16 * 16);
+    if ((size_t)stage * DQ_WARPS > 200 * 1024) stage = 0;  // rows too long to stage: decode from global memory
+    const int smem = stage * DQ_WARPS;
+    static int attr = 0;
+    if (smem > 48 * 1024 && smem > attr) {
+        if (cudaFuncSetAttribute(k_dequant_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return cudaErrorInvalidValue;
+        attr = smem;
+    }
+    return launch_pdl(k_dequant_f16, dim3((unsigned)((warps + DQ_WARPS - 1) / DQ_WARPS)), dim3(32 * DQ_WARPS), smem, st,
+                      g, stage);
 }
-cudaError_t launch_pack_slots(const GroupedArgs& g, int mode, int S, cudaStream_t st) {
+cudaError_t launch_pack_tokens(const GroupedArgs& g, int slot_tiles, cudaStream_t st) {
+    if (g.T < 1 || slot_tiles < 1) return cudaSuccess;
+    if (g.D % 64) return cudaErrorInvalidValue;
+    cudaError_t err = launch_pdl(k_token_scale, dim3((g.T + 7) / 8), dim3(256), 0, st, g);
+    if (err != cudaSuccess) return err;
+    return launch_pdl(k_pack_groups, dim3((unsigned)(((long long)slot_tiles * 16 + 7) / 8)), dim3(256), 0, st, g);
+}
+cudaError_t launch_pack_slots(const GroupedArgs& g, int S, cudaStream_t st) {
     if (S < 1) return cudaSuccess;
-    if (mode == 0) return launch_pdl(k_pack_slots<0>, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
-    return launch_pdl(k_pack_slots<1>, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
+    return launch_pdl(k_pack_slots, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
 }
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st) {
     if (g.D % 128 || g.FF % 64 || g.D % TC_KT || g.FF % TC_KT) return cudaErrorInvalidValue;

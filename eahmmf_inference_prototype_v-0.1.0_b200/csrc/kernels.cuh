@@ -128,6 +128,7 @@ struct GroupedArgs {
     int E, D, FF;
     const int* offsets;     // [E+1] slot offsets per expert
     const int* slot_token;  // [S] token of each slot
+    int T;                  // tokens of the call
     const int* tiles_gu;    // [E+1] prefix of gate/up tiles per expert (FF/64 row tiles x ceil(m_e/128))
     const int* tiles_dn;    // [E+1] prefix of down tiles per expert (D/128 row tiles x ceil(m_e/128))
     __half* wf;             // f16 weights, per expert: gate [FF x D], up [FF x D], down [D x FF]
@@ -139,6 +140,7 @@ struct GroupedArgs {
     __half* bhi;            // activations of the GEMM in progress, f16 of row / bscale, tile-major by
                             //   (expert, 128-slot tile): tiles x 128 x K
     float* bscale;          // [S] per-slot scale of the packed rows
+    float* tscale;          // [T] per-token scale of the xn rows
     float* y;               // [S x D] down outputs per slot
     int* status;
 };
@@ -186,7 +188,8 @@ size_t moe_smem_gateup(int D, size_t rbg, size_t rbu);
 int moe_chunk_group_size(int D, int FF, size_t rbg, size_t rbu, size_t rbd);
 size_t moe_smem_down(int FF, size_t rbd);
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st);
-cudaError_t launch_pack_slots(const GroupedArgs& g, int mode, int S, cudaStream_t st);  // 0: xn rows, 1: h rows
+cudaError_t launch_pack_tokens(const GroupedArgs& g, int slot_tiles, cudaStream_t st);  // xn rows of the slots
+cudaError_t launch_pack_slots(const GroupedArgs& g, int S, cudaStream_t st);  // the slots' h rows
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st);  // 0 gate/up, 1 down
 // routing of a ragged batch of any size (moe.cu): per-token top-k with expert counts (cnt zeroed by the
 // caller), then offsets / tile prefixes / active list, then the slot maps
