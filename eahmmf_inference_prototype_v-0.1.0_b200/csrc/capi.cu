@@ -220,7 +220,7 @@ GroupedLayout grouped_layout(const EahmmfMoeLayer* L, int T) {
 }
 bool grouped_ok(const EahmmfMoeLayer* L, int T) {
     return T >= GROUPED_MIN_T && (long long)T * L->n_used >= (long long)GROUPED_MIN_SLOTS_PER_EXPERT * L->n_expert &&
-           L->D % 128 == 0 && L->FF % 64 == 0;
+           L->D % DN_TILE_ROWS == 0 && L->FF % GU_TILE_ROWS == 0;
 }
 
 bool layer_ok(const EahmmfMoeLayer* L) {
@@ -373,10 +373,10 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     const int slot_tiles = (S + 127) / 128 + E;  // bound on sum over experts of ceil(m_e / 128)
     if (launch_pack_tokens(g, slot_tiles, st) != cudaSuccess) return ST_CUDA;
     g_prof.mark(2, st);
-    if (launch_grouped_gemm(g, 0, (L->FF / 64) * slot_tiles, st) != cudaSuccess) return ST_CUDA;
+    if (launch_grouped_gemm(g, 0, (L->FF / GU_TILE_ROWS) * slot_tiles, st) != cudaSuccess) return ST_CUDA;
     g_prof.mark(3, st);
     if (launch_pack_slots(g, S, st) != cudaSuccess ||
-        launch_grouped_gemm(g, 1, (L->D / 128) * slot_tiles, st) != cudaSuccess || launch_moe_combine(a, st) != cudaSuccess)
+        launch_grouped_gemm(g, 1, (L->D / DN_TILE_ROWS) * slot_tiles, st) != cudaSuccess || launch_moe_combine(a, st) != cudaSuccess)
         return ST_CUDA;
     g_prof.mark(4, st);
     if (!g_prof.collect()) return ST_CUDA;

@@ -9,16 +9,17 @@
 //      f16 values of x/s (2^-12 relative rounding, like the weights).
 //   Both are written tile-major in the tensor cores' K-major core-matrix order (8 rows x 16 bytes), so
 //   that one 64-element K stage of a 128-row tile is one contiguous 16 KB block: a single bulk copy.
-//   3. k_gemm_tc<GATEUP>: persistent, warp-specialised. Tiles are (expert, 64 gate rows + the same 64 up
-//      rows, 128 slots). A producer lane streams (W, activations) stage blocks into a 6-deep shared-
-//      memory ring (1-D bulk copies, mbarrier complete_tx); one lane issues tcgen05.mma (M 128, N 128,
-//      K 16, f16 in, fp32 accumulate in tensor memory) and commits each stage back to the producer; two
-//      accumulators in tensor memory let four epilogue warps read tile i (tcgen05.ld) while tile i+1
-//      accumulates. The slot tile is the MMA's A operand here, so an accumulator row is one slot holding
-//      its 64 gate and 64 up values: each thread forms h = SiLU(g) * u (qwen3moe.cpp:1056-1059) for its
-//      own slot and the warp writes the rows out as whole lines through a shared-memory transpose.
-//   4. k_gemm_tc<DOWN>: tiles of (expert, 128 rows of D, 128 slots) over h, writing y per slot; the
-//      weighted combine in expert order is k_moe_combine (moe.cu).
+//   3. k_gemm_tc<GATEUP>: persistent, warp-specialised. Tiles are (expert, 128 slots, 128 FF rows): the
+//      slot tile is the MMA's A operand (M 128) and two 128-row weight blocks, each 64 gate rows + the
+//      same 64 up rows, are B (N 256). A producer lane streams (slots, weight block, weight block) stage
+//      blocks into a 4-deep shared-memory ring (1-D bulk copies, mbarrier complete_tx); one lane issues
+//      tcgen05.mma (M 128, N 256, K 16, f16 in, fp32 accumulate in tensor memory) and commits each stage
+//      back to the producer; two accumulators (all 512 tensor-memory columns) let four epilogue warps
+//      read tile i (tcgen05.ld) while tile i+1 accumulates. An accumulator row is one slot holding its
+//      gate and up values: each thread forms h = SiLU(g) * u (qwen3moe.cpp:1056-1059) for its own slot
+//      and the warp writes the rows out as whole lines through a shared-memory transpose.
+//   4. k_gemm_tc<DOWN>: tiles of (expert, 128 slots, 256 rows of D) over h, the same way, writing y per
+//      slot; the weighted combine in expert order is k_moe_combine (moe.cu).
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -184,8 +185,8 @@ __device__ float kq_bound(const uint8_t* row, int type, int sb) {
 }
 
 // ---- 1. expert weights -> scaled f16, tile-major; one warp per 8-row group of an active expert
-// Per expert: gate/up tiles (FF/64 of them, A rows 0..63 = gate rows 64 rt.., 64..127 = the same up rows,
-// D/64 stages), then down tiles (D/128, FF/64 stages). Each row's scale is the power of two of an upper
+// Per expert: gate/up blocks (FF/64 of them; rows 0..63 = gate rows 64 blk.., 64..127 = the same up rows;
+// D/64 stages), then down blocks (D/128 of 128 rows, FF/64 stages). Each row's scale is the power of two of an upper
 // bound of its max|y|; the bound only has to keep the f16 values below 2^14, and since the scale is a
 // power of two the f16 rounding of y / s is the same whatever binade it lands in. K-quant rows take the
 // bound from their super-block headers (one decode pass), other types decode twice. Eight rows of one
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(256) k_pack_groups(GroupedArgs g) {
     pdl_wait();
     pdl_trigger();
     const long long gw = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31, RT = g.FF / 64;
+    const int lane = threadIdx.x & 31, RT = g.FF / GU_TILE_ROWS;
     const int bt = (int)(gw >> 4), grp = (int)(gw & 15);  // slot tile, row group within it
     if ((long long)bt * RT >= g.tiles_gu[g.E]) return;
     int lo_ = 0, hi_ = g.E;  // expert of the slot tile: largest e with tiles_gu[e] <= bt RT
@@ -360,7 +361,7 @@ __global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
         else hi_ = mid;
     }
     const int e = lo_, j = slot - g.offsets[e];
-    const int tile = g.tiles_gu[e] / (g.FF / 64) + (j >> 7), jr = j & 127;
+    const int tile = g.tiles_gu[e] / (g.FF / GU_TILE_ROWS) + (j >> 7), jr = j & 127;
     const float* xr = g.h + (size_t)slot * K;
     float m = 0.f;
     for (int i = 4 * lane; i < K; i += 128) {
@@ -382,14 +383,15 @@ __global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
 }
 
 // ---- 3/4. the grouped GEMM
-constexpr int TC_KT = 64;                                     // K elements per stage
-constexpr int TC_BLOCK = 128 * TC_KT * 2;                     // one 128-row f16 stage block: 16 KB
-constexpr int TC_STAGES = 6;
-constexpr int TC_STAGE_BYTES = 2 * TC_BLOCK;                  // W, activations
-constexpr int TC_XP = 36;                                     // row stride (floats) of an epilogue transpose tile
-constexpr int TC_U_BYTES = 4 * 32 * TC_XP * 4;                 // one 32 x 32 transpose tile per epilogue warp
+constexpr int TC_KT = 64;                     // K elements per stage
+constexpr int TC_BLOCK = 128 * TC_KT * 2;     // one 128-row f16 stage block: 16 KB
+constexpr int TC_STAGES = 4;
+constexpr int TC_STAGE_BYTES = 3 * TC_BLOCK;  // the slot tile (A), two 128-row weight blocks (B)
+constexpr int TC_XP = 36;                     // row stride (floats) of an epilogue transpose tile
+constexpr int TC_U_BYTES = 4 * 32 * TC_XP * 4;  // one 32 x 32 transpose tile per epilogue warp
 constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + TC_U_BYTES + 256;
 constexpr int TC_NT = 192;  // warp 0 producer, warp 1 MMA + tensor-memory owner, warps 2..5 epilogue
+constexpr int TC_N = 256;   // accumulator columns of a tile: two weight blocks
 
 struct TcTile {
     int e, rt, m0, mc, btile;
@@ -405,16 +407,21 @@ __device__ __forceinline__ bool tc_tile(const GroupedArgs& g, int b, TcTile& t) 
         if (off[mid] <= b) lo_ = mid;
         else hi_ = mid;
     }
-    const int RT = MODE == 0 ? g.FF / 64 : g.D / 128;
+    const int RT = MODE == 0 ? g.FF / GU_TILE_ROWS : g.D / DN_TILE_ROWS;
     const int local = b - off[lo_], st = local / RT;
     t.e = lo_;
     t.rt = local - st * RT;
     t.m0 = g.offsets[lo_] + 128 * st;
     t.mc = min(128, g.offsets[lo_ + 1] - t.m0);
-    t.btile = g.tiles_gu[lo_] / (g.FF / 64) + st;
+    t.btile = g.tiles_gu[lo_] / (g.FF / GU_TILE_ROWS) + st;
     return true;
 }
 
+// D[128 slots x 256] = A[slot tile] * B[two weight blocks]^T over K. Gate/up: weight blocks 2 rt and 2 rt + 1
+// (each 64 gate rows + the same 64 up rows), so accumulator columns 0..63 / 64..127 pair the gate and up
+// values of FF rows 128 rt + 0..63 and columns 128..255 those of rows + 64..127. Down: blocks 2 rt, 2 rt + 1
+// are D rows 256 rt + 0..255 = the columns. An accumulator row is one slot: each epilogue thread finishes
+// its own slot's row and the warp writes 32 rows x 32 columns at a time through its transpose tile.
 template <int MODE>
 __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     extern __shared__ __align__(1024) uint8_t smt[];
@@ -428,7 +435,7 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = MODE == 0 ? g.D : g.FF, nk = K / TC_KT;
-    if (warp == 1) tc_alloc(&s_tmem, 256);
+    if (warp == 1) tc_alloc(&s_tmem, 2 * TC_N);
     if (tid == 0) {
         for (int i = 0; i < TC_STAGES; i++) {
             mbar_init(&full[i], 1);
@@ -456,9 +463,9 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
             int it = 0;  // stage fills issued
             TcTile t;
             for (int b = blockIdx.x; tc_tile<MODE>(g, b, t) && !*(volatile int*)&s_abort; b += gridDim.x) {
-                const __half* A = g.wf + (size_t)t.e * g.w_expert +
-                                  (MODE == 0 ? (size_t)t.rt * 128 * K : (size_t)2 * g.FF * g.D + (size_t)t.rt * 128 * K);
-                const __half* Bh = g.bhi + (size_t)t.btile * 128 * K;
+                const __half* W = g.wf + (size_t)t.e * g.w_expert + (MODE == 0 ? 0 : (size_t)2 * g.FF * g.D) +
+                                  (size_t)(2 * t.rt) * 128 * K;
+                const __half* X = g.bhi + (size_t)t.btile * 128 * K;
                 for (int kt = 0; kt < nk; kt++, it++) {
                     const int s = it % TC_STAGES;
                     if (it >= TC_STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)(it / TC_STAGES - 1) & 1u)) {
@@ -466,9 +473,10 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                         break;
                     }
                     uint8_t* dst = smt + s * TC_STAGE_BYTES;
-                    mbar_expect_tx(&full[s], 2 * TC_BLOCK);
-                    tma_load_1d(dst, A + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
-                    tma_load_1d(dst + TC_BLOCK, Bh + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
+                    mbar_expect_tx(&full[s], 3 * TC_BLOCK);
+                    tma_load_1d(dst, X + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
+                    tma_load_1d(dst + TC_BLOCK, W + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
+                    tma_load_1d(dst + 2 * TC_BLOCK, W + (size_t)128 * K + (size_t)kt * 128 * TC_KT, TC_BLOCK, &full[s]);
                 }
             }
             // no copy may still be landing when the CTA exits: wait for the last fill of every stage
@@ -477,7 +485,7 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
         }
     } else if (warp == 1) {  // ---------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = tc_idesc_f16(128, 128);
+            constexpr uint32_t idesc = tc_idesc_f16(128, TC_N);
             int it = 0, ti = 0;
             TcTile t;
             for (int b = blockIdx.x; tc_tile<MODE>(g, b, t); b += gridDim.x, ti++) {
@@ -487,7 +495,7 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                     break;
                 }
                 tc_fence_after();
-                const uint32_t acc = tmem + (uint32_t)(128 * a);
+                const uint32_t acc = tmem + (uint32_t)(TC_N * a);
                 bool ok = true;
                 for (int kt = 0; kt < nk; kt++, it++) {
                     const int s = it % TC_STAGES;
@@ -496,12 +504,11 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                         break;
                     }
                     tc_fence_after();
-                    // gate/up: A = the slot tile, B = the 128 weight rows (accumulator rows are slots);
-                    // down: A = the weight rows, B = the slot tile (accumulator rows are output rows)
-                    const uint32_t wbase = smem_u32(smt + s * TC_STAGE_BYTES), xbase = wbase + TC_BLOCK;
-                    const uint32_t abase = MODE == 0 ? xbase : wbase, bbase = MODE == 0 ? wbase : xbase;
+                    const uint32_t abase = smem_u32(smt + s * TC_STAGE_BYTES), bbase = abase + TC_BLOCK;
 #pragma unroll
                     for (int j = 0; j < TC_KT / 16; j++) {
+                        // K-major core matrices: 128 B between the two K chunks of a step, 1 KB between row
+                        // groups (the second weight block's row groups continue the first's)
                         const uint64_t da = tc_desc(abase + 256 * j, 128, (TC_KT / 8) * 128);
                         const uint64_t db = tc_desc(bbase + 256 * j, 128, (TC_KT / 8) * 128);
                         tc_mma_f16(acc, da, db, idesc, (kt > 0 || j > 0) ? 1u : 0u);
@@ -518,6 +525,7 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     } else {  // ---------------- epilogue: warps 2..5, tensor-memory lane quadrant warp % 4
         const int q = warp & 3;
         float* xp = U + (warp - 2) * (32 * TC_XP);  // this warp's 32 x 32 transpose tile
+        const int sl = 32 * q + lane;                 // this thread's slot within the tile
         int ti = 0;
         TcTile t;
         for (int b = blockIdx.x; tc_tile<MODE>(g, b, t); b += gridDim.x, ti++) {
@@ -526,59 +534,54 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
             ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads below are warp-collective
             if (!ok && lane == 0) fail();
             tc_fence_after();
-            const uint32_t acc = tmem + (uint32_t)(128 * a) + ((uint32_t)(32 * q) << 16);
+            const uint32_t acc = tmem + (uint32_t)(TC_N * a) + ((uint32_t)(32 * q) << 16);
             const float* rs = g.rs + (size_t)t.e * (2 * g.FF + g.D);
+            const float bs = sl < t.mc ? g.bscale[t.m0 + sl] : 0.f;
+            // one pass: 32 output columns of this thread's row, scaled, through the transpose tile to
+            // out + row * ld + col0 (rows of the tile's slots only)
+            auto emit = [&](float (&v)[32], float* out, int ld, int col0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(xp + lane * TC_XP + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int r = 4 * i + (lane >> 3), c = 4 * (lane & 7), sr = 32 * q + r;
+                    if (sr < t.mc)
+                        *reinterpret_cast<float4*>(out + (size_t)(t.m0 + sr) * ld + col0 + c) =
+                            *reinterpret_cast<const float4*>(xp + r * TC_XP + c);
+                }
+                __syncwarp();
+            };
             if (MODE == 0) {
-                // Accumulator row = slot 32 q + lane of the tile; columns 0..63 are its gate rows, 64..127
-                // the same up rows, so each thread pairs its own values. Rows go out through the warp's
-                // transpose tile: 32 rows x 32 columns per pass, written back as whole 128-byte lines.
-                const int sl = 32 * q + lane;
-                const float bs = sl < t.mc ? g.bscale[t.m0 + sl] : 0.f;
-                for (int half = 0; ok && half < 2; half++) {
-                    const float sg = rs[64 * t.rt + 32 * half + lane], su = rs[g.FF + 64 * t.rt + 32 * half + lane];
+                for (int qq = 0; ok && qq < 4; qq++) {  // FF rows 128 rt + 32 qq + 0..31
+                    const int fr = 128 * t.rt + 32 * qq, gcol = (qq >> 1) * 128 + (qq & 1) * 32;
+                    const float sg = rs[fr + lane], su = rs[g.FF + fr + lane];
+                    float hv[32];
 #pragma unroll
                     for (int c0 = 0; c0 < 32; c0 += 16) {
                         float gv[16], uv[16];
-                        tc_ld16x2(acc + (uint32_t)(32 * half + c0), acc + (uint32_t)(64 + 32 * half + c0), gv, uv);
+                        tc_ld16x2(acc + (uint32_t)(gcol + c0), acc + (uint32_t)(gcol + 64 + c0), gv, uv);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
                             const float gs = __shfl_sync(0xffffffffu, sg, c0 + j), us = __shfl_sync(0xffffffffu, su, c0 + j);
-                            gv[j] = silu_mul_fast(gv[j] * gs * bs, uv[j] * us * bs);
+                            hv[c0 + j] = silu_mul_fast(gv[j] * gs * bs, uv[j] * us * bs);
                         }
-#pragma unroll
-                        for (int j = 0; j < 16; j += 4)
-                            *reinterpret_cast<float4*>(xp + lane * TC_XP + c0 + j) = make_float4(gv[j], gv[j + 1], gv[j + 2], gv[j + 3]);
                     }
-                    __syncwarp();
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const int r = 4 * i + (lane >> 3), c = 4 * (lane & 7), sr = 32 * q + r;
-                        if (sr < t.mc)
-                            *reinterpret_cast<float4*>(g.h + (size_t)(t.m0 + sr) * g.FF + 64 * t.rt + 32 * half + c) =
-                                *reinterpret_cast<const float4*>(xp + r * TC_XP + c);
-                    }
-                    __syncwarp();
+                    emit(hv, g.h, g.FF, fr);
                 }
-            } else if (ok) {
-                // accumulator row = output row 128 rt + 32 q + lane, column = slot: each column store is
-                // one 128-byte line; the slot scales of 32 columns come from one load and lane shuffles
-                const int row = 32 * q + lane;
-                const float sd = rs[2 * g.FF + 128 * t.rt + row];
-                float bsv[4];  // slot scales of columns 32 i + lane, loaded before any store of the tile
-#pragma unroll
-                for (int i = 0; i < 4; i++) bsv[i] = 32 * i + lane < t.mc ? g.bscale[t.m0 + 32 * i + lane] : 0.f;
-#pragma unroll
-                for (int c0 = 0; c0 < 128; c0 += 32) {
-                    if (c0 >= t.mc) break;
-                    const float bsl = bsv[c0 / 32];
-                    float v[16], w[16];
-                    tc_ld16x2(acc + (uint32_t)c0, acc + (uint32_t)(c0 + 16), v, w);
+            } else {
+                for (int p = 0; ok && p < 8; p++) {  // D rows 256 rt + 32 p + 0..31
+                    const int dr = 256 * t.rt + 32 * p;
+                    const float sd = rs[2 * g.FF + dr + lane];
+                    float yv[32], v[16], w[16];
+                    tc_ld16x2(acc + (uint32_t)(32 * p), acc + (uint32_t)(32 * p + 16), v, w);
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const float b0 = __shfl_sync(0xffffffffu, bsl, j), b1 = __shfl_sync(0xffffffffu, bsl, 16 + j);
-                        if (c0 + j < t.mc) g.y[(size_t)(t.m0 + c0 + j) * g.D + 128 * t.rt + row] = v[j] * sd * b0;
-                        if (c0 + 16 + j < t.mc) g.y[(size_t)(t.m0 + c0 + 16 + j) * g.D + 128 * t.rt + row] = w[j] * sd * b1;
+                        yv[j] = v[j] * __shfl_sync(0xffffffffu, sd, j) * bs;
+                        yv[16 + j] = w[j] * __shfl_sync(0xffffffffu, sd, 16 + j) * bs;
                     }
+                    emit(yv, g.y, g.D, dr);
                 }
             }
             tc_fence_before();
@@ -589,7 +592,7 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tc_dealloc(tmem, 256);
+    if (warp == 1) tc_dealloc(tmem, 2 * TC_N);
 }
 
 // ---- launchers ----------------------------------------------------------------------------------
@@ -622,7 +625,7 @@ cudaError_t launch_pack_slots(const GroupedArgs& g, int S, cudaStream_t st) {
     return launch_pdl(k_pack_slots, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
 }
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st) {
-    if (g.D % 128 || g.FF % 64 || g.D % TC_KT || g.FF % TC_KT) return cudaErrorInvalidValue;
+    if (g.D % DN_TILE_ROWS || g.FF % GU_TILE_ROWS || g.D % TC_KT || g.FF % TC_KT) return cudaErrorInvalidValue;
     if (max_tiles < 1) return cudaSuccess;
     const int grid = std::min(max_tiles, sm_count());
     if (mode == 0) {

@@ -121,6 +121,10 @@ struct GemvXArgs {
 constexpr int GEMV_PRO_XF = 0, GEMV_PRO_ROW = 1, GEMV_PRO_NORM = 2;
 
 // Grouped tensor-core path of the MoE block (gemm.cu) for ragged batches.
+// Output rows of one grouped tensor-core tile (x 128 slots): a gate/up tile holds 128 FF rows (their gate and
+// up rows, 256 accumulator columns), a down tile 256 D rows.
+constexpr int GU_TILE_ROWS = 128, DN_TILE_ROWS = 256;
+
 struct GroupedArgs {
     const uint8_t* const* w[3];  // per-expert component pointer tables: gate, up, down
     int type[3];
@@ -129,8 +133,8 @@ struct GroupedArgs {
     const int* offsets;     // [E+1] slot offsets per expert
     const int* slot_token;  // [S] token of each slot
     int T;                  // tokens of the call
-    const int* tiles_gu;    // [E+1] prefix of gate/up tiles per expert (FF/64 row tiles x ceil(m_e/128))
-    const int* tiles_dn;    // [E+1] prefix of down tiles per expert (D/128 row tiles x ceil(m_e/128))
+    const int* tiles_gu;    // [E+1] prefix of gate/up tiles per expert (FF/GU_TILE_ROWS x ceil(m_e/128))
+    const int* tiles_dn;    // [E+1] prefix of down tiles per expert (D/DN_TILE_ROWS x ceil(m_e/128))
     __half* wf;             // f16 weights, per expert: gate [FF x D], up [FF x D], down [D x FF]
     size_t w_expert;        // elements per expert (3 FF D)
     size_t w_off[3];        // element offsets of gate, up, down within an expert

@@ -1680,7 +1680,7 @@ __global__ void __launch_bounds__(512) k_plan_big(MoeArgs a, const int* __restri
     for (int q = 0; q < 3; q++)
         for (int w = 0; w < warp; w++) base[q] += ws[q][w];
     const int off = base[0] + incl[0] - v[0], toff = base[1] + incl[1] - v[1], aoff = base[2] + incl[2] - v[2];
-    const int RTg = a.FF / 64, RTd = a.D / 128;
+    const int RTg = a.FF / GU_TILE_ROWS, RTd = a.D / DN_TILE_ROWS;
     if (tid < E) {
         a.rw.offsets[tid] = off;
         tiles_gu[tid] = RTg * toff;
