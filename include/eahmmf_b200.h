@@ -78,7 +78,12 @@ typedef struct EahmmfMoeLayer {
 } EahmmfMoeLayer;
 
 /* Bytes of workspace eahmmf_cuda_moe_layer needs for T tokens. The workspace starts with the routing
- * result of the last call: int32 ids[T*n_used], then float weights[T*n_used] (rank order). */
+ * result of the last call: int32 ids[T*n_used], then float weights[T*n_used] (rank order).
+ * From T >= 256 tokens with >= 16 slots per expert on average the call takes the grouped tensor-core
+ * path, whose workspace holds an f16 copy of every expert of the layer: n_expert x 3 x FF x D x 2
+ * bytes (1.21 GB at the Qwen3-30B-A3B shape, 4.83 GB at the 235B-A22B shape) plus
+ * T x n_used x (FF + D) x 4 bytes of per-slot rows and the packed activations. Smaller T need
+ * T x n_used x (FF + D) x 4 bytes and change. */
 size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
 
 /* The MoE block of Engine::forward (qwen3moe.cpp:1008-1069) for T tokens, on `stream` (cudaStream_t,
