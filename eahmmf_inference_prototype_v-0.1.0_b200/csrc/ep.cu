@@ -119,7 +119,76 @@ __device__ __forceinline__ void block_counts(const float* recv, int world, int c
     __syncthreads();
 }
 
-// One block per received row position (src, i): valid rows are compacted in (src, i) order to the front
+// One block: the order of the received rows. Every position's key is (local expert, position) for a valid
+// row and a value above all of them otherwise; a bitonic sort of the keys in shared memory gives the
+// compact order, valid rows first by ascending expert and, within an expert, by (src, i). Rows of one
+// expert then sit together, so the expert kernels, which take their rows in 64-row chunks, read each
+// expert's weights about once instead of once per chunk it appears in.
+constexpr int ORDER_MAX = 4096;  // positions (world * cap) the sort takes; more use the (src, i) order
+constexpr int ORDER_NT = 1024;
+__global__ void __launch_bounds__(ORDER_NT) k_ep_order(const float* __restrict__ recv, int D, int world, int cap,
+                                                       int* __restrict__ eid, int* __restrict__ src_of) {
+    __shared__ int cnt[EP_MAX_WORLD], pre[EP_MAX_WORLD], total;
+    __shared__ uint32_t key[ORDER_MAX];
+    const int R = world * cap, row = D + EAHMMF_EP_HDR, tid = threadIdx.x;
+    block_counts(recv, world, cap, row, cnt, pre, &total);
+    int n2 = 1;
+    while (n2 < R) n2 <<= 1;
+    for (int b = tid; b < n2; b += ORDER_NT) {
+        uint32_t k = 0xffffffffu;  // padding
+        if (b < R) {
+            const int src = b / cap, i = b - src * cap;
+            if (i < cnt[src]) {
+                const int e = __float_as_int(recv[(size_t)b * row]);
+                k = ((uint32_t)min(max(e, 0), 0x7ffe) << 16) | (uint32_t)b;  // out-of-range ids: after the others
+            } else {
+                k = (0x7fffu << 16) | (uint32_t)b;
+            }
+        }
+        key[b] = k;
+    }
+    __syncthreads();
+    for (int size = 2; size <= n2; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < n2; i += ORDER_NT) {
+                const int p = i ^ stride;
+                if (p > i) {
+                    const uint32_t a = key[i], c = key[p];
+                    if ((a > c) == ((i & size) == 0)) {
+                        key[i] = c;
+                        key[p] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    for (int j = tid; j < R; j += ORDER_NT) {
+        const uint32_t k = key[j];
+        const int b = (int)(k & 0xffffu);
+        const bool valid = (k >> 16) != 0x7fffu;
+        eid[j] = valid ? __float_as_int(recv[(size_t)b * row]) : -1;
+        src_of[j] = valid ? b : -1;
+    }
+}
+// One block per compact row j (after k_ep_order): the received row src_of[j], or zeros.
+__global__ void __launch_bounds__(256) k_ep_fill(const float* __restrict__ recv, int D, const int* __restrict__ src_of,
+                                                 float* __restrict__ rows, float* __restrict__ y) {
+    const int j = blockIdx.x, b = src_of[j], row = D + EAHMMF_EP_HDR;
+    float4* dst = reinterpret_cast<float4*>(rows + (size_t)j * D);
+    if (b >= 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(recv + (size_t)b * row + EAHMMF_EP_HDR);
+        for (int c = threadIdx.x; c < D / 4; c += blockDim.x) dst[c] = s4[c];
+    } else {
+        for (int c = threadIdx.x; c < D / 4; c += blockDim.x) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (y) {
+        float4* y4 = reinterpret_cast<float4*>(y + (size_t)j * D);
+        for (int c = threadIdx.x; c < D / 4; c += blockDim.x) y4[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// More positions than the sort takes: one block per received row position (src, i): valid rows are
+// compacted in (src, i) order to the front
 // of rows / eid / src_of; the other positions become zero rows with expert -1 at the back. y (optional)
 // is zeroed for the expert application that adds into it.
 __global__ void __launch_bounds__(256) k_ep_unpack(const float* __restrict__ recv, int D, int world, int cap,
@@ -186,8 +255,13 @@ extern "C" int eahmmf_cuda_ep_unpack(const float* d_recv, int D, int world, int 
     if (!d_recv || !d_rows || !d_eid || !d_src || D < 4 || D % 4 || world < 1 || world > EP_MAX_WORLD || cap < 1 ||
         !al16(d_recv) || !al16(d_rows) || (d_y && !al16(d_y)))
         return ST_BAD_ARG;
-    k_ep_unpack<<<world * cap, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(d_recv, D, world, cap, d_rows, d_eid,
-                                                                               d_src, d_y);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (world * cap <= ORDER_MAX) {
+        k_ep_order<<<1, ORDER_NT, 0, st>>>(d_recv, D, world, cap, d_eid, d_src);
+        k_ep_fill<<<world * cap, 256, 0, st>>>(d_recv, D, d_src, d_rows, d_y);
+    } else {
+        k_ep_unpack<<<world * cap, 256, 0, st>>>(d_recv, D, world, cap, d_rows, d_eid, d_src, d_y);
+    }
     return cudaGetLastError() == cudaSuccess ? ST_OK : ST_CUDA;
 }
 

@@ -130,9 +130,11 @@ int eahmmf_cuda_moe_experts(const EahmmfMoeLayer* L, int R, const float* d_rows,
  *    d_token_pos[t*K + j] receives the position (d * cap + row) of token t's j-th slot by ascending
  *    expert id, d_pos_w[position] its weight: eahmmf_cuda_moe_combine over the returned rows with these
  *    gives the reference's expert-ascending sum. Needs cap >= T*K (else EAHMMF_ST_CAPACITY).
- *  - ep_unpack (receiver): the valid rows of the received blocks, compacted in (source, row) order to
- *    the front of d_rows [world*cap x D], their experts in d_eid (-1 and zero rows after them), and
- *    d_src = the received position of each compact row (-1 after). d_y (optional) is zeroed.
+ *  - ep_unpack (receiver): the valid rows of the received blocks, compacted to the front of d_rows
+ *    [world*cap x D] in ascending local-expert order (within an expert in (source, row) order; in
+ *    (source, row) order alone when world*cap > 4096), their experts in d_eid (-1 and zero rows after
+ *    them), and d_src = the received position of each compact row (-1 after). d_y (optional) is
+ *    zeroed. Rows of one expert together let eahmmf_cuda_moe_experts read its weights once.
  *  - ep_return: d_ret[d_src[j]] = d_y[j] for the valid compact rows, d_ret being the return buffer
  *    (world blocks of cap D-float rows) that travels back by the inverse exchange. */
 #define EAHMMF_EP_HDR 4

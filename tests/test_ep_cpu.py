@@ -67,14 +67,14 @@ class CpuEpBackend:
     def unpack(self, recv, D, world, cap, rows, eid, src, y):
         buf = recv.numpy().reshape(world * cap, D + HDR)
         cnt = [_f2i(buf[q * cap, 1]) for q in range(world)]
-        R, j = sum(cnt), 0
+        R = sum(cnt)
         eid_np, src_np, rows_np = eid.numpy(), src.numpy(), rows.numpy()
-        for q in range(world):
-            for i in range(cnt[q]):
-                rows_np[j] = buf[q * cap + i, HDR:]
-                eid_np[j] = _f2i(buf[q * cap + i, 0])
-                src_np[j] = q * cap + i
-                j += 1
+        # valid rows by ascending local expert, within an expert in (source, row) order
+        valid = sorted(((_f2i(buf[q * cap + i, 0]), q * cap + i) for q in range(world) for i in range(cnt[q])))
+        for j, (e, b) in enumerate(valid):
+            rows_np[j] = buf[b, HDR:]
+            eid_np[j] = e
+            src_np[j] = b
         rows_np[R:] = 0
         eid_np[R:] = -1
         src_np[R:] = -1
