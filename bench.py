@@ -275,7 +275,7 @@ def layer_ours(args, rank: int, world: int, local: int):
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get("k_moe_gateup", {}).get("dram_bytes_per_launch")
+            traffic = json.load(f).get("k_moe_gateup_T8", {}).get("dram_bytes_per_launch")
     except (OSError, ValueError):
         pass
     line = {
@@ -288,6 +288,8 @@ def layer_ours(args, rank: int, world: int, local: int):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if peak else None, "traffic": traffic,
                      "kernel": "k_moe_gateup", "peak_source": peak_kind,
+                     "traffic_case": "dram bytes of one launch at T = 8 (profiles/traffic.json); achieved is the mean "
+                                     "over T = 1..8",
                      "timing": f"CUDA events around the kernel on its stream, {gu_n} launches over the timed steps"},
         "clocks": clk.summary(),
         "layer_us_per_step": {"mean": float(np.mean(step_us)), "min": float(np.min(step_us))},
