@@ -373,11 +373,13 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     const int slot_tiles = (S + 127) / 128 + E;  // bound on sum over experts of ceil(m_e / 128)
     if (launch_pack_tokens(g, slot_tiles, st) != cudaSuccess) return ST_CUDA;
     g_prof.mark(2, st);
-    if (launch_grouped_gemm(g, 0, (L->FF / GU_TILE_ROWS) * slot_tiles, st) != cudaSuccess) return ST_CUDA;
-    g_prof.mark(3, st);
-    if (launch_pack_slots(g, S, st) != cudaSuccess ||
-        launch_grouped_gemm(g, 1, (L->D / DN_TILE_ROWS) * slot_tiles, st) != cudaSuccess || launch_moe_combine(a, st) != cudaSuccess)
+    // stage timer: [2] the two GEMMs with the h repack between them, [3] the combine
+    if (launch_grouped_gemm(g, 0, (L->FF / GU_TILE_ROWS) * slot_tiles, st) != cudaSuccess ||
+        launch_pack_slots(g, S, st) != cudaSuccess ||
+        launch_grouped_gemm(g, 1, (L->D / DN_TILE_ROWS) * slot_tiles, st) != cudaSuccess)
         return ST_CUDA;
+    g_prof.mark(3, st);
+    if (launch_moe_combine(a, st) != cudaSuccess) return ST_CUDA;
     g_prof.mark(4, st);
     if (!g_prof.collect()) return ST_CUDA;
     return ST_OK;

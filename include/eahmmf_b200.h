@@ -147,7 +147,8 @@ int eahmmf_cuda_ep_return(const float* d_y, const int* d_src, int D, int world, 
 
 /* Stage timing of eahmmf_cuda_moe_layer: when enabled, each call records CUDA events on its stream
  * around its four stages (router GEMV, routing + activation prep, gate/up, down + combine) of every
- * 64-token block and waits for them; eahmmf_cuda_moe_profile_read returns the mean stage durations (us)
+ * 64-token block (on the grouped tensor-core path: router GEMV, routing + dequantization + activation
+ * packing, the two GEMMs with the h repack between them, combine) and waits for them; eahmmf_cuda_moe_profile_read returns the mean stage durations (us)
  * over the blocks since the last read (or enable) and restarts the average. The events serialise the
  * stages (each kernel timed on its own) and the wait makes each call synchronous. Off by default;
  * single-threaded use. */
