@@ -435,7 +435,8 @@ def ep_pack(d_ids, d_w, d_xn, K: int, E_loc: int, world: int, cap: int, d_send, 
 
 
 def ep_unpack(d_recv, D: int, world: int, cap: int, d_rows, d_eid, d_src, d_y=None, stream=None) -> int:
-    """eahmmf_cuda_ep_unpack: the received blocks' valid rows compacted to the front (expert -1 after)."""
+    """eahmmf_cuda_ep_unpack: the received blocks' valid rows compacted to the front by ascending local
+    expert, stable in (source, row) order (expert -1 after)."""
     return lib().eahmmf_cuda_ep_unpack(_ptr(d_recv), D, world, cap, _ptr(d_rows), _ptr(d_eid), _ptr(d_src), _ptr(d_y),
                                        _stream(stream))
 

@@ -69,3 +69,45 @@ def test_ep_layer_nccl_matches_oracle(tmp_path, orc, T_per, tol):
         np.testing.assert_allclose(d["w"], wo, rtol=1e-6, atol=0)
         err = np.linalg.norm((d["y"] - d["x"]) - (yo - d["x"])) / np.linalg.norm(yo - d["x"])
         assert err < tol, (r, err)
+
+
+@pytest.mark.parametrize("world,cap,D", [(2, 24, 64), (8, 32, 32), (4, 1100, 16)])
+def test_ep_unpack_orders_rows_by_expert(world, cap, D):
+    """eahmmf_cuda_ep_unpack: the valid received rows, compacted by ascending local expert and, within an
+    expert, in (source, row) order (up to 4096 positions; beyond that in (source, row) order alone), the
+    expert ids and source positions beside them, -1 and zero rows after them; the return puts each
+    compact row back at its source position."""
+    import torch
+    import eahmmf_b200 as eb
+    rng = np.random.default_rng(world * 1000 + cap)
+    E_loc, HDR, R = 7, 4, world * cap
+    recv = np.zeros((R, D + HDR), np.float32)
+    valid, ids = [], {}
+    for q in range(world):
+        n = int(rng.integers(0, cap + 1))
+        recv[q * cap, 1] = np.array([n], np.int32).view(np.float32)[0]
+        for i in range(n):
+            b = q * cap + i
+            e = int(rng.integers(0, E_loc))
+            recv[b, 0] = np.array([e], np.int32).view(np.float32)[0]
+            recv[b, HDR:] = rng.normal(size=D).astype(np.float32)
+            valid.append(b)
+            ids[b] = e
+    want = sorted(valid, key=lambda b: (ids[b], b)) if R <= 4096 else valid
+    dev = torch.device("cuda", 0)
+    d_recv = torch.from_numpy(recv.reshape(-1)).to(dev)
+    rows = torch.full((R, D), 7.0, device=dev)
+    eid = torch.zeros(R, dtype=torch.int32, device=dev)
+    src = torch.zeros(R, dtype=torch.int32, device=dev)
+    y = torch.full((R, D), 3.0, device=dev)
+    assert eb.ep_unpack(d_recv, D, world, cap, rows, eid, src, y) == 0
+    ret = torch.zeros((R, D), device=dev)
+    assert eb.ep_return(rows, src, D, world, cap, ret) == 0
+    torch.cuda.synchronize()
+    n = len(want)
+    np.testing.assert_array_equal(src.cpu().numpy()[:n], np.array(want, np.int32))
+    np.testing.assert_array_equal(eid.cpu().numpy()[:n], np.array([ids[b] for b in want], np.int32))
+    np.testing.assert_array_equal(rows.cpu().numpy()[:n], recv[want, HDR:])
+    assert (src.cpu().numpy()[n:] == -1).all() and (eid.cpu().numpy()[n:] == -1).all()
+    assert not rows.cpu().numpy()[n:].any() and not y.cpu().numpy().any()
+    np.testing.assert_array_equal(ret.cpu().numpy()[valid], recv[valid, HDR:])
