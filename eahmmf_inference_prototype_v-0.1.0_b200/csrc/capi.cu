@@ -406,7 +406,11 @@ int moe_run(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* d_lo
         return ST_BAD_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     uint8_t* ws = static_cast<uint8_t*>(d_workspace);
-    if (grouped_ok(L, T)) {
+    // assigned-expert calls (the expert-parallel receiver) pass their whole fixed-capacity buffer, most
+    // of it padding rows at larger rank counts: they take the grouped path only at four times the slot
+    // density, so that the f16 copy of every local expert is not made for a few real rows
+    if (grouped_ok(L, T) &&
+        (!given || (long long)T * L->n_used >= 4LL * GROUPED_MIN_SLOTS_PER_EXPERT * L->n_expert)) {
         if (workspace_bytes < grouped_layout(L, T).total) return ST_CAPACITY;
         return moe_grouped(L, T, d_xn, d_logits, d_x, ws, st, d_status, given);
     }

@@ -47,7 +47,7 @@ class CudaEpBackend:
     pack / unpack / return (eahmmf_cuda_ep_*), the rank's experts on assigned rows
     (eahmmf_cuda_moe_experts) and the expert-ordered combine (eahmmf_cuda_moe_combine)."""
 
-    def __init__(self, local, n_used: int, device):
+    def __init__(self, local, n_used: int, device, graph: bool = True):
         import eahmmf_b200 as eb
         self.eb = eb
         self.layer = eb.MoeLayer.from_expert_set(local, n_used=1)
@@ -55,21 +55,29 @@ class CudaEpBackend:
         self.device = device
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.ws = None
+        # the receiver's stage (unpack, the rank's experts, return) works on the layer's fixed buffers:
+        # after its first eager run it is captured once into a CUDA graph and replayed (one launch for
+        # its ~20 kernels; no collective inside)
+        self.use_graph = graph
+        self.graph, self.graph_key = None, None
+
+    def _st(self):
+        return torch.cuda.current_stream(self.device)
 
     def alloc(self, shape, dtype):
         return torch.empty(shape, dtype=dtype, device=self.device)
 
     def route(self, logits):
-        return self.eb.route_topk(logits.contiguous(), self.K, d_status=self.status)
+        return self.eb.route_topk(logits.contiguous(), self.K, stream=self._st(), d_status=self.status)
 
     def pack(self, ids, w, xn, E_loc, world, cap, send, token_pos, pos_w):
         rc = self.eb.ep_pack(ids, w, xn.contiguous(), self.K, E_loc, world, cap, send, token_pos, pos_w,
-                             d_status=self.status)
+                             stream=self._st(), d_status=self.status)
         if rc:
             raise RuntimeError(f"eahmmf_cuda_ep_pack returned {rc}")
 
     def unpack(self, recv, D, world, cap, rows, eid, src, y):
-        rc = self.eb.ep_unpack(recv, D, world, cap, rows, eid, src, y)
+        rc = self.eb.ep_unpack(recv, D, world, cap, rows, eid, src, y, stream=self._st())
         if rc:
             raise RuntimeError(f"eahmmf_cuda_ep_unpack returned {rc}")
 
@@ -78,17 +86,37 @@ class CudaEpBackend:
         need = self.layer.experts_workspace_bytes(R)
         if self.ws is None or self.ws.numel() < need:
             self.ws = torch.empty(need, dtype=torch.uint8, device=self.device)
-        rc = self.layer.apply_experts(R, rows, eid, y, self.ws, d_status=self.status)
+        rc = self.layer.apply_experts(R, rows, eid, y, self.ws, stream=self._st(), d_status=self.status)
         if rc:
             raise RuntimeError(f"eahmmf_cuda_moe_experts returned {rc}")
 
     def ret(self, y, src, D, world, cap, out):
-        rc = self.eb.ep_return(y, src, D, world, cap, out)
+        rc = self.eb.ep_return(y, src, D, world, cap, out, stream=self._st())
         if rc:
             raise RuntimeError(f"eahmmf_cuda_ep_return returned {rc}")
 
+    def post(self, recv, D, world, cap, rows, eid, src, y, out):
+        """unpack, apply and ret in one go: replayed from a CUDA graph after the first call."""
+        key = (recv.data_ptr(), D, world, cap, rows.data_ptr(), eid.data_ptr(), src.data_ptr(), y.data_ptr(),
+               out.data_ptr())
+        if self.graph is not None and self.graph_key == key:
+            self.graph.replay()
+            return
+
+        def run():
+            self.unpack(recv, D, world, cap, rows, eid, src, y)
+            self.apply(rows, eid, y)
+            self.ret(y, src, D, world, cap, out)
+
+        run()  # this call's results, and the workspace
+        if self.use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                run()
+            self.graph, self.graph_key = g, key
+
     def combine(self, token_pos, pos_w, back, x):
-        rc = self.eb.moe_combine(token_pos, pos_w, back, x)
+        rc = self.eb.moe_combine(token_pos, pos_w, back, x, stream=self._st())
         if rc:
             raise RuntimeError(f"eahmmf_cuda_moe_combine returned {rc}")
 
@@ -158,9 +186,12 @@ class EpMoeLayer:
         if W > 1:
             self._a2a(self.recv, self.send)
         mark(2)
-        self.be.unpack(self.recv, D, W, cap, self.rows, self.eid, self.src, self.y)
-        self.be.apply(self.rows, self.eid, self.y)
-        self.be.ret(self.y, self.src, D, W, cap, self.ret)
+        if hasattr(self.be, "post"):
+            self.be.post(self.recv, D, W, cap, self.rows, self.eid, self.src, self.y, self.ret)
+        else:
+            self.be.unpack(self.recv, D, W, cap, self.rows, self.eid, self.src, self.y)
+            self.be.apply(self.rows, self.eid, self.y)
+            self.be.ret(self.y, self.src, D, W, cap, self.ret)
         mark(3)
         if W > 1:
             self._a2a(self.back, self.ret)

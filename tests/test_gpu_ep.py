@@ -45,6 +45,13 @@ def _rank_main(rank, world, port, T_per, out_path):
         ids, w = layer(torch.from_numpy(xn).to(dev), torch.from_numpy(lg).to(dev), xt)
         torch.cuda.synchronize()
         assert layer.be.check() == 0
+        # a second call replays the receiver stage's CUDA graph: the same bits
+        xt2 = torch.from_numpy(x.copy()).to(dev)
+        layer(torch.from_numpy(xn).to(dev), torch.from_numpy(lg).to(dev), xt2)
+        torch.cuda.synchronize()
+        assert layer.be.check() == 0
+        assert layer.be.graph is not None
+        assert torch.equal(xt, xt2)
         np.savez(out_path + f".{rank}.npz", x=x, xn=xn, lg=lg, y=xt.cpu().numpy(), ids=ids.cpu().numpy(),
                  w=w.cpu().numpy())
     finally:
