@@ -36,7 +36,6 @@ __device__ __forceinline__ void tc_dealloc(uint32_t tmem, uint32_t cols) {  // w
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // D[tmem] (+)= A * B^T, one thread
 __device__ __forceinline__ void tc_mma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -48,18 +47,6 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t tmem, uint64_t da, uint64_t 
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
-}
-// 32 lanes x 16 columns of 32-bit accumulators: lane l of the warp gets row (lane base + l)
-__device__ __forceinline__ void tc_ld16(uint32_t addr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(addr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
 }
 // two 32-lane x 16-column loads in flight together, one wait. The wait names the 32 destination registers
 // as read-write operands, so no use of them can be scheduled before the loads have landed.
@@ -88,16 +75,6 @@ __device__ __forceinline__ void tc_ld16x2(uint32_t addr0, uint32_t addr1, float 
         a[j] = __uint_as_float(r[j]);
         b[j] = __uint_as_float(s[j]);
     }
-}
-// 16-byte global -> shared copy; src_bytes = 0 fills the 16 bytes with zeros (nothing is read)
-__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 }  // namespace eb
