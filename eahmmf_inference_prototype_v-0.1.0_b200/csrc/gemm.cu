@@ -530,13 +530,20 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
         TcTile t;
         for (int b = blockIdx.x; tc_tile<MODE>(g, b, t); b += gridDim.x, ti++) {
             const int a = ti & 1;
+            // the tile's row scales (this lane's one per 32-column pass) and its slot's scale, loaded
+            // before the accumulator wait so that no pass waits on them
+            const float* rs = g.rs + (size_t)t.e * (2 * g.FF + g.D);
+            const float bs = sl < t.mc ? g.bscale[t.m0 + sl] : 0.f;
+            float rsc[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                rsc[k] = MODE == 0 ? rs[(k & 1) * g.FF + 128 * t.rt + 32 * (k >> 1) + lane]  // gate / up, pass k / 2
+                                   : rs[2 * g.FF + 256 * t.rt + 32 * k + lane];              // down, pass k
             bool ok = mbar_wait_bounded(&acc_full[a], (uint32_t)(ti / 2) & 1u);
             ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads below are warp-collective
             if (!ok && lane == 0) fail();
             tc_fence_after();
             const uint32_t acc = tmem + (uint32_t)(TC_N * a) + ((uint32_t)(32 * q) << 16);
-            const float* rs = g.rs + (size_t)t.e * (2 * g.FF + g.D);
-            const float bs = sl < t.mc ? g.bscale[t.m0 + sl] : 0.f;
             // one pass: 32 output columns of this thread's row, scaled, through the transpose tile to
             // out + row * ld + col0 (rows of the tile's slots only)
             auto emit = [&](float (&v)[32], float* out, int ld, int col0) {
@@ -553,10 +560,11 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                 }
                 __syncwarp();
             };
-            if (MODE == 0) {
-                for (int qq = 0; ok && qq < 4; qq++) {  // FF rows 128 rt + 32 qq + 0..31
+            if (MODE == 0 && ok) {
+#pragma unroll
+                for (int qq = 0; qq < 4; qq++) {  // FF rows 128 rt + 32 qq + 0..31
                     const int fr = 128 * t.rt + 32 * qq, gcol = (qq >> 1) * 128 + (qq & 1) * 32;
-                    const float sg = rs[fr + lane], su = rs[g.FF + fr + lane];
+                    const float sg = rsc[2 * qq], su = rsc[2 * qq + 1];
                     float hv[32];
 #pragma unroll
                     for (int c0 = 0; c0 < 32; c0 += 16) {
@@ -570,10 +578,11 @@ __global__ void __launch_bounds__(TC_NT, 1) k_gemm_tc(GroupedArgs g) {
                     }
                     emit(hv, g.h, g.FF, fr);
                 }
-            } else {
-                for (int p = 0; ok && p < 8; p++) {  // D rows 256 rt + 32 p + 0..31
+            } else if (ok) {
+#pragma unroll
+                for (int p = 0; p < 8; p++) {  // D rows 256 rt + 32 p + 0..31
                     const int dr = 256 * t.rt + 32 * p;
-                    const float sd = rs[2 * g.FF + dr + lane];
+                    const float sd = rsc[p];
                     float yv[32], v[16], w[16];
                     tc_ld16x2(acc + (uint32_t)(32 * p), acc + (uint32_t)(32 * p + 16), v, w);
 #pragma unroll
