@@ -375,7 +375,7 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g_prof.mark(2, st);
     // stage timer: [2] the two GEMMs with the h repack between them, [3] the combine
     if (launch_grouped_gemm(g, 0, (L->FF / GU_TILE_ROWS) * slot_tiles, st) != cudaSuccess ||
-        launch_pack_slots(g, S, st) != cudaSuccess ||
+        launch_pack_slots(g, slot_tiles, st) != cudaSuccess ||
         launch_grouped_gemm(g, 1, (L->D / DN_TILE_ROWS) * slot_tiles, st) != cudaSuccess)
         return ST_CUDA;
     g_prof.mark(3, st);

@@ -346,40 +346,65 @@ __global__ void __launch_bounds__(256) k_pack_groups(GroupedArgs g) {
     if (valid && (lane & 3) == 0) g.bscale[slot] = sc;
 }
 
-// ---- 2b. down activations: each slot's h row -> scale + f16, tile-major by (expert, slot tile); one warp
-// per slot
-__global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g, int S) {
+// ---- 2b. down activations: each slot's h row -> power-of-two scale + f16, tile-major by (expert, slot
+// tile). One warp per 8 consecutive slots of one expert's slot tile (a core-matrix row group), four lanes
+// per slot: the row's max in a first pass over it, then every 64-element K chunk of the group written as
+// one contiguous 1 KB block of whole lines (rows past the expert's slots as zeros).
+__global__ void __launch_bounds__(256) k_pack_slots(GroupedArgs g) {
     pdl_wait();
     pdl_trigger();
-    const int slot = (blockIdx.x * 256 + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (slot >= S || slot >= g.offsets[g.E]) return;  // S bounds the grid; absent slots (given ids) hold none
-    const int K = g.FF;
-    int lo_ = 0, hi_ = g.E;  // expert of the slot: largest e with offsets[e] <= slot
+    const long long gw = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31, RT = g.FF / GU_TILE_ROWS;
+    const int bt = (int)(gw >> 4), grp = (int)(gw & 15);  // slot tile, row group within it
+    if ((long long)bt * RT >= g.tiles_gu[g.E]) return;
+    int lo_ = 0, hi_ = g.E;  // expert of the slot tile: largest e with tiles_gu[e] <= bt RT
     while (hi_ - lo_ > 1) {
         const int mid = (lo_ + hi_) >> 1;
-        if (g.offsets[mid] <= slot) lo_ = mid;
+        if (g.tiles_gu[mid] <= bt * RT) lo_ = mid;
         else hi_ = mid;
     }
-    const int e = lo_, j = slot - g.offsets[e];
-    const int tile = g.tiles_gu[e] / (g.FF / GU_TILE_ROWS) + (j >> 7), jr = j & 127;
-    const float* xr = g.h + (size_t)slot * K;
+    const int e = lo_, cnt = g.offsets[e + 1] - g.offsets[e];
+    const int j0 = 128 * (bt - g.tiles_gu[e] / RT) + 8 * grp;
+    if (j0 >= cnt) return;
+    const int r = lane >> 2, kq = 16 * (lane & 3), jr = 8 * grp + r, K = g.FF;
+    const bool valid = j0 + r < cnt;
+    const int slot = g.offsets[e] + j0 + r;
+    const float* xr = g.h + (size_t)(valid ? slot : g.offsets[e] + j0) * K + kq;
     float m = 0.f;
-    for (int i = 4 * lane; i < K; i += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(xr + i);
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-    const float s = pow2_scale(warp_max(m)), inv = 1.f / s;
-    __half* bh = g.bhi + (size_t)tile * 128 * K;
-    for (int i = 8 * lane; i < K; i += 256) {
-        const float4 u = *reinterpret_cast<const float4*>(xr + i);
-        const float4 v = *reinterpret_cast<const float4*>(xr + i + 4);
-        const float a[8] = {u.x * inv, u.y * inv, u.z * inv, u.w * inv, v.x * inv, v.y * inv, v.z * inv, v.w * inv};
-        __align__(16) __half h[8];
+    for (int k0 = 0; k0 < K; k0 += 64) {
 #pragma unroll
-        for (int q = 0; q < 8; q++) h[q] = __float2half_rn(a[q]);
-        *reinterpret_cast<uint4*>(bh + tile_off(jr, i)) = *reinterpret_cast<const uint4*>(h);
+        for (int q = 0; q < 4; q++) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + k0 + 4 * q);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
     }
-    if (lane == 0) g.bscale[slot] = s;
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));  // the row's four lanes
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const float sc = valid ? pow2_scale(m) : 1.f, inv = valid ? 1.f / sc : 0.f;
+    __half* bh = g.bhi + (size_t)bt * 128 * K;
+    for (int k0 = 0; k0 < K; k0 += 256) {  // four 64-element chunks: all loads first, then the stores
+        float4 v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                v[u][q] = k0 + 64 * u < K ? *reinterpret_cast<const float4*>(xr + k0 + 64 * u + 4 * q)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (k0 + 64 * u >= K) break;
+            __align__(16) __half2 hv[8];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                hv[2 * q] = __floats2half2_rn(v[u][q].x * inv, v[u][q].y * inv);
+                hv[2 * q + 1] = __floats2half2_rn(v[u][q].z * inv, v[u][q].w * inv);
+            }
+            const int i = k0 + 64 * u + kq;
+            *reinterpret_cast<uint4*>(bh + tile_off(jr, i)) = *reinterpret_cast<const uint4*>(hv);
+            *reinterpret_cast<uint4*>(bh + tile_off(jr, i + 8)) = *reinterpret_cast<const uint4*>(hv + 4);
+        }
+    }
+    if (valid && (lane & 3) == 0) g.bscale[slot] = sc;
 }
 
 // ---- 3/4. the grouped GEMM
@@ -629,9 +654,10 @@ cudaError_t launch_pack_tokens(const GroupedArgs& g, int slot_tiles, cudaStream_
     if (err != cudaSuccess) return err;
     return launch_pdl(k_pack_groups, dim3((unsigned)(((long long)slot_tiles * 16 + 7) / 8)), dim3(256), 0, st, g);
 }
-cudaError_t launch_pack_slots(const GroupedArgs& g, int S, cudaStream_t st) {
-    if (S < 1) return cudaSuccess;
-    return launch_pdl(k_pack_slots, dim3((S + 7) / 8), dim3(256), 0, st, g, S);
+cudaError_t launch_pack_slots(const GroupedArgs& g, int slot_tiles, cudaStream_t st) {
+    if (slot_tiles < 1) return cudaSuccess;
+    if (g.FF % 64) return cudaErrorInvalidValue;
+    return launch_pdl(k_pack_slots, dim3((unsigned)(((long long)slot_tiles * 16 + 7) / 8)), dim3(256), 0, st, g);
 }
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st) {
     if (g.D % DN_TILE_ROWS || g.FF % GU_TILE_ROWS || g.D % TC_KT || g.FF % TC_KT) return cudaErrorInvalidValue;

@@ -193,7 +193,7 @@ int moe_chunk_group_size(int D, int FF, size_t rbg, size_t rbu, size_t rbd);
 size_t moe_smem_down(int FF, size_t rbd);
 cudaError_t launch_grouped_dequant(const GroupedArgs& g, cudaStream_t st);
 cudaError_t launch_pack_tokens(const GroupedArgs& g, int slot_tiles, cudaStream_t st);  // xn rows of the slots
-cudaError_t launch_pack_slots(const GroupedArgs& g, int S, cudaStream_t st);  // the slots' h rows
+cudaError_t launch_pack_slots(const GroupedArgs& g, int slot_tiles, cudaStream_t st);  // the slots' h rows
 cudaError_t launch_grouped_gemm(const GroupedArgs& g, int mode, int max_tiles, cudaStream_t st);  // 0 gate/up, 1 down
 // routing of a ragged batch of any size (moe.cu): per-token top-k with expert counts (cnt zeroed by the
 // caller), then offsets / tile prefixes / active list, then the slot maps
