@@ -356,6 +356,7 @@ int moe_grouped(const EahmmfMoeLayer* L, int T, const float* d_xn, const float* 
     g.bscale = reinterpret_cast<float*>(ws + w.bscale);
     g.tscale = reinterpret_cast<float*>(ws + w.tscale);
     g.y = a.y;
+    g.xh = reinterpret_cast<__half*>(ws + w.y);  // T D f16 <= S D fp32; consumed before y is written
     g.status = d_status;
     g_prof.mark(0, st);
     if (d_logits || given) {

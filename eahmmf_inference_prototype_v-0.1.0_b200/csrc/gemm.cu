@@ -5,8 +5,8 @@
 //      qwen3moe.cpp:142-202, exact fp32) and stored as f16 scaled by a per-row power of two (from a bound
 //      read off the super-block headers), so that the f16 rounding (2^-12 relative) is the only loss.
 //   2. k_token_scale + k_pack_groups / k_pack_slots: the activation rows of the slots (for gate/up each
-//      token's xn, its scale found once per token; for down each slot's h) as a power-of-two scale and
-//      f16 values of x/s (2^-12 relative rounding, like the weights).
+//      token's xn, scaled and rounded to f16 once per token and copied per slot; for down each slot's h)
+//      as a power-of-two scale and f16 values of x/s (2^-12 relative rounding, like the weights).
 //   Both are written tile-major in the tensor cores' K-major core-matrix order (8 rows x 16 bytes), so
 //   that one 64-element K stage of a 128-row tile is one contiguous 16 KB block: a single bulk copy.
 //   3. k_gemm_tc<GATEUP>: persistent, warp-specialised. Tiles are (expert, 128 slots, 128 FF rows): the
@@ -280,9 +280,11 @@ __global__ void __launch_bounds__(32 * DQ_WARPS) k_dequant_f16(GroupedArgs g, in
 }
 
 // ---- 2a. gate/up activations. k_token_scale: one warp per token, the power-of-two scale of its xn row
-// (every slot of the token packs the same row). k_pack_groups: one warp per 8 consecutive slots of one
-// expert's slot tile (a core-matrix row group): each 64-element K chunk of the group is one contiguous
-// 1 KB block of the tile, written as whole lines; rows past the expert's slots are written as zeros.
+// and the row as f16 of x / s (g.xh, half the bytes of the fp32 row, so that the rows stay in L2 while
+// every slot of the token copies them). k_pack_groups: one warp per 8 consecutive slots of one expert's
+// slot tile (a core-matrix row group): each 64-element K chunk of the group is one contiguous 1 KB block
+// of the tile, copied from the tokens' f16 rows and written as whole lines (evict-first, so the stream
+// of tile lines does not push the f16 rows out of L2); rows past the expert's slots are written as zeros.
 __global__ void __launch_bounds__(256) k_token_scale(GroupedArgs g) {
     pdl_wait();
     pdl_trigger();
@@ -295,7 +297,16 @@ __global__ void __launch_bounds__(256) k_token_scale(GroupedArgs g) {
         m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
     m = warp_max(m);
-    if (lane == 0) g.tscale[t] = pow2_scale(m);
+    const float sc = pow2_scale(m), inv = 1.f / sc;
+    __half* xo = g.xh + (size_t)t * g.D;
+    for (int i = 4 * lane; i < g.D; i += 128) {  // the row again (L1 / L2), as f16 of x / s
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        __align__(8) __half2 hv[2];
+        hv[0] = __floats2half2_rn(v.x * inv, v.y * inv);
+        hv[1] = __floats2half2_rn(v.z * inv, v.w * inv);
+        *reinterpret_cast<uint2*>(xo + i) = *reinterpret_cast<const uint2*>(hv);
+    }
+    if (lane == 0) g.tscale[t] = sc;
 }
 
 __global__ void __launch_bounds__(256) k_pack_groups(GroupedArgs g) {
@@ -318,32 +329,27 @@ __global__ void __launch_bounds__(256) k_pack_groups(GroupedArgs g) {
     const bool valid = j0 + r < cnt;
     const int slot = g.offsets[e] + j0 + r;
     const int tok = valid ? g.slot_token[slot] : 0;
-    const float sc = valid ? g.tscale[tok] : 1.f, inv = valid ? 1.f / sc : 0.f;
-    const float* xr = g.xn + (size_t)tok * K + kq;
+    // this lane's 16 elements of every 64-element chunk: two 16-byte words of the token's f16 row
+    const uint4* xr = reinterpret_cast<const uint4*>(g.xh + (size_t)tok * K + kq);
     __half* bh = g.bhi + (size_t)bt * 128 * K;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
     for (int k0 = 0; k0 < K; k0 += 256) {  // four 64-element chunks: all loads first, then the stores
-        float4 v[4][4];
+        uint4 v[4][2];
 #pragma unroll
-        for (int u = 0; u < 4; u++)
-#pragma unroll
-            for (int q = 0; q < 4; q++)
-                v[u][q] = k0 + 64 * u < K ? *reinterpret_cast<const float4*>(xr + k0 + 64 * u + 4 * q)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < 4; u++) {
+            const bool in = valid && k0 + 64 * u < K;
+            v[u][0] = in ? __ldg(xr + (k0 + 64 * u) / 8) : zero;
+            v[u][1] = in ? __ldg(xr + (k0 + 64 * u) / 8 + 1) : zero;
+        }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             if (k0 + 64 * u >= K) break;
-            __align__(16) __half2 hv[8];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                hv[2 * q] = __floats2half2_rn(v[u][q].x * inv, v[u][q].y * inv);
-                hv[2 * q + 1] = __floats2half2_rn(v[u][q].z * inv, v[u][q].w * inv);
-            }
             const int i = k0 + 64 * u + kq;
-            *reinterpret_cast<uint4*>(bh + tile_off(jr, i)) = *reinterpret_cast<const uint4*>(hv);
-            *reinterpret_cast<uint4*>(bh + tile_off(jr, i + 8)) = *reinterpret_cast<const uint4*>(hv + 4);
+            __stcs(reinterpret_cast<uint4*>(bh + tile_off(jr, i)), v[u][0]);
+            __stcs(reinterpret_cast<uint4*>(bh + tile_off(jr, i + 8)), v[u][1]);
         }
     }
-    if (valid && (lane & 3) == 0) g.bscale[slot] = sc;
+    if (valid && (lane & 3) == 0) g.bscale[slot] = g.tscale[tok];
 }
 
 // ---- 2b. down activations: each slot's h row -> power-of-two scale + f16, tile-major by (expert, slot

@@ -145,6 +145,8 @@ struct GroupedArgs {
                             //   (expert, 128-slot tile): tiles x 128 x K
     float* bscale;          // [S] per-slot scale of the packed rows
     float* tscale;          // [T] per-token scale of the xn rows
+    __half* xh;             // [T x D] f16 of each xn row / tscale (held in the y space, which is dead until
+                            //   the down GEMM writes y)
     float* y;               // [S x D] down outputs per slot
     int* status;
 };
