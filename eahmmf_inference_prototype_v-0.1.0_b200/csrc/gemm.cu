@@ -113,47 +113,79 @@ __device__ __forceinline__ uint32_t ld32_a2(const uint8_t* p) {
     const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
     return (uint32_t)q[0] | ((uint32_t)q[1] << 16);
 }
-// Elements 64 c + kq .. +15 (kq a multiple of 16) of the Q4_K / Q5_K super-block at b (16-byte aligned),
-// times the power of two inv, as 8 f16 pairs. Same values as dq8: d q is exact in fp32 (an 11-bit f16
-// times a 6-bit scale times a 5-bit quant), so fma(d inv, q, -o inv) rounds (d q - o) once and scales it
-// exactly. Four quants per word: nibble masks, then byte permutes into 2^23 + q.
-__device__ __forceinline__ void dq16_k45(const uint8_t* b, bool q5, int c, int kq, float inv, __half2 (&o)[8]) {
-    const int hi = kq >> 5, l0 = kq & 31, j = 2 * c + hi;
+// One lane's share of a Q4_K / Q5_K super-block at b (16-byte aligned): elements 64 c + kq .. +15 of
+// each of its four 64-element chunks c (kq a multiple of 16), times the power of two inv, as f16 pairs
+// stored to dst + c * 8192 and dst + c * 8192 + 64 (the chunk's two core-matrix columns of this row in
+// the tile). Same values as dq8: d q is exact in fp32 (an 11-bit f16 times a 6-bit scale times a 5-bit
+// quant), so fma(d inv, q, -o inv) rounds (d q - o) once and scales it exactly. The header and the Q5_K
+// high bits are read once per super-block; four quants per word: nibble masks, then byte permutes into
+// 2^23 + q.
+__device__ __forceinline__ void dq_sb_k45(const uint8_t* b, bool q5, int kq, float inv, __half* dst) {
+    const int hi = kq >> 5, l0 = kq & 31;
     const uint4 hd = *reinterpret_cast<const uint4*>(b);  // d, dmin, 12 scale / min bytes
-    auto byte = [&](int k) -> int { return (int)(((k < 4 ? hd.y : k < 8 ? hd.z : hd.w) >> (8 * (k & 3))) & 0xff); };
-    int sc, mn;
-    if (j < 4) {
-        sc = byte(j) & 63;
-        mn = byte(j + 4) & 63;
-    } else {
-        sc = (byte(j + 4) & 0x0f) | ((byte(j - 4) >> 6) << 4);
-        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
-    }
-    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))) * (float)sc * inv;
-    const float mo = -(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))) * (float)mn * inv);
-    const uint4 qw = *reinterpret_cast<const uint4*>(b + (q5 ? 48 : 16) + 32 * c + l0);
+    const float dh = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff)));
+    const float mh = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
     const uint4 hw = q5 ? *reinterpret_cast<const uint4*>(b + 16 + l0) : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ha[4] = {hw.x, hw.y, hw.z, hw.w};
+    const uint32_t ha[4] = {hw.x, hw.y, hw.z, hw.w};
 #pragma unroll
-    for (int w = 0; w < 4; w++) {
-        uint32_t nib = hi ? (qa[w] >> 4) & 0x0f0f0f0fu : qa[w] & 0x0f0f0f0fu;
-        if (q5) nib |= ((ha[w] >> j) & 0x01010101u) << 4;
-        o[2 * w] = __floats2half2_rn(fmaf(d, byte_f<0>(nib), mo), fmaf(d, byte_f<1>(nib), mo));
-        o[2 * w + 1] = __floats2half2_rn(fmaf(d, byte_f<2>(nib), mo), fmaf(d, byte_f<3>(nib), mo));
+    for (int c = 0; c < 4; c++) {
+        // scale / min of sub-block j = 2 c + hi: bytes j and j + 4 of the 12 (c < 2), or the low / high
+        // nibbles of byte j + 4 with the top two bits of bytes j - 4 / j (c >= 2)
+        const int j = 2 * c + hi, sh = 16 * (c & 1) + 8 * hi;
+        int sc, mn;
+        if (c < 2) {
+            sc = (int)((hd.y >> sh) & 63);
+            mn = (int)((hd.z >> sh) & 63);
+        } else {
+            const uint32_t bw = (hd.w >> sh) & 0xff, by = (hd.y >> sh) & 0xff, bz = (hd.z >> sh) & 0xff;
+            sc = (int)((bw & 0x0f) | ((by >> 6) << 4));
+            mn = (int)((bw >> 4) | ((bz >> 6) << 4));
+        }
+        const float d = dh * (float)sc * inv, mo = -(mh * (float)mn * inv);
+        const uint4 qw = *reinterpret_cast<const uint4*>(b + (q5 ? 48 : 16) + 32 * c + l0);
+        const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w};
+        __align__(16) __half2 o[8];
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            uint32_t nib = (qa[w] >> (4 * hi)) & 0x0f0f0f0fu;
+            if (q5) nib |= ((ha[w] >> j) & 0x01010101u) << 4;
+            o[2 * w] = __floats2half2_rn(fmaf(d, byte_f<0>(nib), mo), fmaf(d, byte_f<1>(nib), mo));
+            o[2 * w + 1] = __floats2half2_rn(fmaf(d, byte_f<2>(nib), mo), fmaf(d, byte_f<3>(nib), mo));
+        }
+        *reinterpret_cast<uint4*>(dst + c * 8192) = *reinterpret_cast<const uint4*>(o);
+        *reinterpret_cast<uint4*>(dst + c * 8192 + 64) = *reinterpret_cast<const uint4*>(o + 4);
     }
 }
-// The same for a Q6_K super-block at b (2-byte aligned): y = d s (q - 32) is exact in fp32.
-__device__ __forceinline__ void dq16_q6k(const uint8_t* b, int c, int kq, float inv, __half2 (&o)[8]) {
-    const int h = c >> 1, quad = 2 * (c & 1) + (kq >> 5), l0 = kq & 31, shift = 2 * quad;
-    const uint8_t* ql = b + 64 * h + kq;  // = 64 h + 32 (quad & 1) + l0
-    const uint8_t* qh = b + 128 + 32 * h + l0;
-    const float ds = h16(b + 208) * (float)reinterpret_cast<const int8_t*>(b)[192 + 8 * h + (l0 >> 4) + 2 * quad] * inv;
+// The same for a Q6_K super-block at b (2-byte aligned): y = d s (q - 32) is exact in fp32. Chunks 2 h
+// and 2 h + 1 take the low and high nibbles of the same 16 low-bit bytes and the same 16 high-bit bytes
+// (at different shifts), so each half h reads them once.
+__device__ __forceinline__ void dq_sb_q6k(const uint8_t* b, int kq, float inv, __half* dst) {
+    const int hi = kq >> 5, l0 = kq & 31;
+    const float dd = h16(b + 208);
+    const int8_t* scl = reinterpret_cast<const int8_t*>(b + 192);
 #pragma unroll
-    for (int w = 0; w < 4; w++) {
-        const uint32_t lw = ld32_a2(ql + 4 * w), hw = ld32_a2(qh + 4 * w);
-        const uint32_t v = ((c & 1) ? (lw >> 4) & 0x0f0f0f0fu : lw & 0x0f0f0f0fu) | (((hw >> shift) & 0x03030303u) << 4);
-        o[2 * w] = __floats2half2_rn(ds * (byte_f<0>(v) - 32.f), ds * (byte_f<1>(v) - 32.f));
-        o[2 * w + 1] = __floats2half2_rn(ds * (byte_f<2>(v) - 32.f), ds * (byte_f<3>(v) - 32.f));
+    for (int h = 0; h < 2; h++) {
+        uint32_t lw[4], hw[4];
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            lw[w] = ld32_a2(b + 64 * h + kq + 4 * w);  // = 64 h + 32 (quad & 1) + l0
+            hw[w] = ld32_a2(b + 128 + 32 * h + l0 + 4 * w);
+        }
+#pragma unroll
+        for (int cl = 0; cl < 2; cl++) {
+            const int c = 2 * h + cl, quad = 2 * cl + hi, shift = 2 * quad;
+            const float ds = dd * (float)scl[8 * h + (l0 >> 4) + 2 * quad] * inv;
+            __align__(16) __half2 o[8];
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                const uint32_t v = (cl ? (lw[w] >> 4) & 0x0f0f0f0fu : lw[w] & 0x0f0f0f0fu) |
+                                   (((hw[w] >> shift) & 0x03030303u) << 4);
+                o[2 * w] = __floats2half2_rn(ds * (byte_f<0>(v) - 32.f), ds * (byte_f<1>(v) - 32.f));
+                o[2 * w + 1] = __floats2half2_rn(ds * (byte_f<2>(v) - 32.f), ds * (byte_f<3>(v) - 32.f));
+            }
+            *reinterpret_cast<uint4*>(dst + c * 8192) = *reinterpret_cast<const uint4*>(o);
+            *reinterpret_cast<uint4*>(dst + c * 8192 + 64) = *reinterpret_cast<const uint4*>(o + 4);
+        }
     }
 }
 
@@ -256,14 +288,18 @@ __global__ void __launch_bounds__(32 * DQ_WARPS) k_dequant_f16(GroupedArgs g, in
         base += (size_t)2 * g.FF * g.D + (size_t)(row >> 7) * 128 * K;
         ar = row & 127;
     }
-    for (int k0 = 0; k0 < K; k0 += 64) {
-        const int i = k0 + kq;
-        __align__(16) __half2 o[8];
-        if (fast45) {
-            dq16_k45(src + (size_t)(i >> 8) * bsz, type == T_Q5_K, (i >> 6) & 3, kq, inv, o);
-        } else if (fast6) {
-            dq16_q6k(src + (size_t)(i >> 8) * bsz, (i >> 6) & 3, kq, inv, o);
-        } else {
+    if (fast45 || fast6) {
+        // super-block sb of the row: chunks 4 sb .. 4 sb + 3, each a 128 x 64 block (8192 elements) of
+        // the tile; this lane's two 8-element words of a chunk are at tile_off(ar, 64 c + kq) and + 8
+        __half* dst = base + tile_off(ar, kq);
+        for (int sb = 0; sb < K / 256; sb++, dst += 4 * 8192) {
+            if (fast45) dq_sb_k45(src + (size_t)sb * bsz, type == T_Q5_K, kq, inv, dst);
+            else dq_sb_q6k(src + (size_t)sb * bsz, kq, inv, dst);
+        }
+    } else {
+        for (int k0 = 0; k0 < K; k0 += 64) {
+            const int i = k0 + kq;
+            __align__(16) __half2 o[8];
             float y[8], z[8];
             dq8(src, type, i, y);
             dq8(src, type, i + 8, z);
@@ -272,9 +308,9 @@ __global__ void __launch_bounds__(32 * DQ_WARPS) k_dequant_f16(GroupedArgs g, in
                 o[j] = __floats2half2_rn(y[2 * j] * inv, y[2 * j + 1] * inv);
                 o[4 + j] = __floats2half2_rn(z[2 * j] * inv, z[2 * j + 1] * inv);
             }
+            *reinterpret_cast<uint4*>(base + tile_off(ar, i)) = *reinterpret_cast<const uint4*>(o);
+            *reinterpret_cast<uint4*>(base + tile_off(ar, i + 8)) = *reinterpret_cast<const uint4*>(o + 4);
         }
-        *reinterpret_cast<uint4*>(base + tile_off(ar, i)) = *reinterpret_cast<const uint4*>(o);
-        *reinterpret_cast<uint4*>(base + tile_off(ar, i + 8)) = *reinterpret_cast<const uint4*>(o + 4);
     }
     if (lane < 8) g.rs[(size_t)e * rows_e + r0 + lane] = s_own;
 }
