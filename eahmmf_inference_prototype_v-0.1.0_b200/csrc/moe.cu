@@ -1617,39 +1617,57 @@ __global__ void __launch_bounds__(COMB_NT) k_moe_combine(MoeArgs a) {
 // only on its own token, and the combine visits a token's slots in expert order, so the outputs are
 // the same for any slot order.
 // ------------------------------------------------------------------------------------------------
-constexpr int BIG_NT = 256;
+constexpr int BIG_NT = 128;
+// One warp per token. The slot counts are gathered per block first (shared-memory atomics), then one
+// global atomic per (block, expert) reserves the block's range of the expert's slots: under skewed
+// routing a few popular experts take a large share of every token's k slots, and one global atomic per
+// slot on their counters serialises.
 template <bool GIVEN>
 __global__ void __launch_bounds__(BIG_NT) k_route_big(MoeArgs a, int* __restrict__ cnt, int* __restrict__ local) {
     __shared__ uint32_t s_rk[(BIG_NT / 32) * 64];
+    __shared__ int s_cnt[MAX_EXPERTS];  // this block's slots per expert, then the block's first slot index
     pdl_wait();
     pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * (BIG_NT / 32) + warp, E = a.n_expert, K = a.n_used;
-    if (t >= a.T) return;  // whole warps
-    int my_e = 0;
-    float my_w = 0.f;
-    const float* lg = a.logits + (size_t)t * E;
-    if constexpr (GIVEN) {  // assigned experts (expert-parallel receiver): weight 1, no ranking
-        if (lane < K) {
-            my_e = __ldg(a.given + (size_t)t * K + lane);
-            my_w = 1.0f;
-        }
-    } else if (E <= 128) route_token<4>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
-    else if (E <= 256) route_token<8>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
-    else route_token<16>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
-    if (lane < K) {
-        if (GIVEN && my_e < 0) {  // an absent slot (padding row of the receiver)
-            a.rw.ids[(size_t)t * K + lane] = -1;
-            return;
-        }
-        if (my_e < 0 || my_e >= E) {  // NaN logits or a given id out of range
-            set_flag(a.status, ST_BAD_INDEX);
-            my_e = 0;
-        }
-        a.rw.ids[(size_t)t * K + lane] = my_e;
-        a.rw.wts[(size_t)t * K + lane] = my_w;
-        if (cnt) local[(size_t)t * K + lane] = atomicAdd(&cnt[my_e], 1);
+    if (cnt) {
+        for (int i = threadIdx.x; i < E; i += BIG_NT) s_cnt[i] = 0;
+        __syncthreads();
     }
+    int my_e = 0, pos = -1;  // pos: this slot's place among the block's slots of my_e (-1: not counted)
+    float my_w = 0.f;
+    if (t < a.T) {  // whole warps
+        const float* lg = a.logits + (size_t)t * E;
+        if constexpr (GIVEN) {  // assigned experts (expert-parallel receiver): weight 1, no ranking
+            if (lane < K) {
+                my_e = __ldg(a.given + (size_t)t * K + lane);
+                my_w = 1.0f;
+            }
+        } else if (E <= 128) route_token<4>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+        else if (E <= 256) route_token<8>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+        else route_token<16>(lg, E, K, lane, s_rk + warp * 64, my_e, my_w);
+        if (lane < K) {
+            if (GIVEN && my_e < 0) {  // an absent slot (padding row of the receiver)
+                a.rw.ids[(size_t)t * K + lane] = -1;
+            } else {
+                if (my_e < 0 || my_e >= E) {  // NaN logits or a given id out of range
+                    set_flag(a.status, ST_BAD_INDEX);
+                    my_e = 0;
+                }
+                a.rw.ids[(size_t)t * K + lane] = my_e;
+                a.rw.wts[(size_t)t * K + lane] = my_w;
+                if (cnt) pos = atomicAdd(&s_cnt[my_e], 1);
+            }
+        }
+    }
+    if (!cnt) return;  // routing alone (the same for the whole block)
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += BIG_NT) {
+        const int n = s_cnt[i];
+        if (n) s_cnt[i] = atomicAdd(&cnt[i], n);
+    }
+    __syncthreads();
+    if (pos >= 0) local[(size_t)t * K + lane] = s_cnt[my_e] + pos;
 }
 
 // One block: slot offsets, tile prefixes of the two GEMMs, active list.
