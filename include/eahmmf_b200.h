@@ -77,13 +77,15 @@ typedef struct EahmmfMoeLayer {
     const float* d_router; /* F32 [n_expert x D] router matrix; NULL when logits are passed in */
 } EahmmfMoeLayer;
 
-/* Bytes of workspace eahmmf_cuda_moe_layer needs for T tokens. The workspace starts with the routing
- * result of the last call: int32 ids[T*n_used], then float weights[T*n_used] (rank order).
- * From T >= 256 tokens with >= 16 slots per expert on average the call takes the grouped tensor-core
- * path, whose workspace holds an f16 copy of every expert of the layer: n_expert x 3 x FF x D x 2
- * bytes (1.21 GB at the Qwen3-30B-A3B shape, 4.83 GB at the 235B-A22B shape) plus
- * T x n_used x (FF + D) x 4 bytes of per-slot rows and the packed activations. Smaller T need
- * T x n_used x (FF + D) x 4 bytes and change. */
+/* Bytes of workspace eahmmf_cuda_moe_layer needs for T tokens (S = T x n_used slots). The workspace
+ * starts with the routing result of the last call: int32 ids[S], then float weights[S] (rank order).
+ * Below 256 tokens (or below 16 slots per expert on average) the call runs in passes of at most 64
+ * tokens: about 8 S + min(T, 64) x n_used x (FF + D) x 4 bytes (6.3 MB at the Qwen3-30B-A3B shape).
+ * From 256 tokens with >= 16 slots per expert it takes the grouped tensor-core path, whose workspace
+ * holds an f16 copy of every expert of the layer, n_expert x 3 x FF x D x 2 bytes (1.21 GB at the
+ * 30B shape, 4.83 GB at the 235B-A22B shape), plus S x (FF + D + 7) x 4 bytes of per-slot rows and
+ * indices and (S / 128 + n_expert + 1) x 128 x max(D, FF) x 2 bytes of packed activations (3.27 GB in
+ * all for 16,193 tokens at the 30B shape). */
 size_t eahmmf_cuda_moe_workspace_bytes(const EahmmfMoeLayer* L, int T);
 
 /* The MoE block of Engine::forward (qwen3moe.cpp:1008-1069) for T tokens, on `stream` (cudaStream_t,

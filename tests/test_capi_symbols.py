@@ -88,3 +88,31 @@ def test_moe_layer_validates_before_launch():
     # misaligned activations / workspace
     assert L.eahmmf_cuda_moe_layer(C.byref(desc), 8, xn + 4, lg, x, ws, 1 << 30, None, None) == eb.ST_BAD_ARG
     assert L.eahmmf_cuda_moe_layer(C.byref(desc), 8, xn, lg, x, ws + 64, 1 << 30, None, None) == eb.ST_BAD_ARG
+
+
+@pytest.mark.parametrize("shape", [(128, 8, 2048, 768, 1152, 630), (128, 8, 4096, 1536, 2304, 1260),
+                                   (16, 2, 512, 256, 288, 210)])
+@pytest.mark.parametrize("router", [False, True])
+def test_moe_workspace_bytes_follow_the_documented_formula(shape, router):
+    """eahmmf_cuda_moe_workspace_bytes against the sizes the header states: 64-token passes below 256
+    tokens (or below 16 slots per expert), the grouped tensor-core path's f16 expert copy and per-slot
+    rows from there. The function's value may exceed the formula only by alignment padding and the
+    per-expert arrays."""
+    E, K, D, FF, rg, rd = shape
+    L = eb.lib()
+    desc = eb.EahmmfMoeLayer(E, K, D, FF, 12, 12, 14, rg, rg, rd, 0x1000, 0x2000, 0x3000, 0x5000 if router else None)
+    prev = 0
+    for T in (1, 8, 64, 65, 255, 256, 2048, 16193):
+        ws = L.eahmmf_cuda_moe_workspace_bytes(C.byref(desc), T)
+        S = T * K
+        if T >= 256 and S >= 16 * E:
+            f = (E * 3 * FF * D * 2 + E * (2 * FF + D) * 4 + S * (FF + D + 7) * 4
+                 + (S // 128 + E + 1) * 128 * max(D, FF) * 2 + (T * E * 4 if router else 0) + T * 4)
+            assert f <= ws <= f + 64 * 1024, (T, ws, f)
+        else:
+            # ids and weights of every token; per pass: slot maps, h and y rows, the XF digits, logits
+            tc = min(T, 64)
+            f = 8 * S + tc * K * (FF + D + 3) * 4 + tc * D * 3 + (tc * E * 4 if router else 0)
+            assert f <= ws <= 1.03 * f + 64 * 1024, (T, ws, f)
+        assert ws >= prev  # a workspace sized for T tokens serves every smaller call
+        prev = ws
