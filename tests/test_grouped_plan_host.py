@@ -1,5 +1,5 @@
-"""The grouped tensor-core path's work plan (moe.cu: k_plan_big; gemm.cu: tc_tile, k_pack_groups,
-k_pack_slots; capi.cu: the launch bounds), modelled on the CPU.
+"""The grouped tensor-core path's work plan (moe.cu: k_route_big's slot counts, k_plan_big; gemm.cu:
+tc_tile, k_pack_groups, k_pack_slots; capi.cu: the launch bounds), modelled on the CPU.
 
 k_plan_big turns the per-expert slot counts into slot offsets and the two GEMMs' tile prefixes (row
 tiles fastest, then 128-slot tiles); every GEMM CTA finds its tile by binary search over a prefix, and
@@ -120,3 +120,41 @@ def test_tiles_cover_every_slot_once_and_packed_rows_sit_where_the_gemm_reads(na
         t = tc_tile(1, b, offsets, tiles_gu, tiles_dn, E, D, FF)
         for sl in range(t["mc"]):
             assert where[t["m0"] + sl] == (t["btile"], sl)
+
+
+def test_block_gathered_slot_counts_give_every_slot_a_place():
+    """k_route_big: each block of 4 tokens counts its slots per expert with shared-memory atomics, then
+    reserves its range of each expert's slots with one global atomic; a slot's place is the block's base
+    plus its place in the block. Whatever order the atomics land in, k_scatter_big's slots
+    offsets[e] + local are a permutation of 0..S-1 and each expert's slots hold exactly its tokens."""
+    rng = np.random.default_rng(11)
+    E, K, T, TPB = 64, 8, 203, 4  # T not a multiple of the block's 4 tokens
+    bias = -1.1 * np.log(np.arange(1, E + 1))
+    ids = np.argsort(-(rng.normal(size=(T, E)) + bias), axis=1)[:, :K]
+    for trial in range(5):
+        cnt = np.zeros(E, np.int64)  # the global counters
+        local = np.full((T, K), -1, np.int64)
+        blocks = list(range((T + TPB - 1) // TPB))
+        rng.shuffle(blocks)  # blocks reach their global atomics in any order
+        for blk in blocks:
+            toks = range(blk * TPB, min(T, (blk + 1) * TPB))
+            s_cnt = np.zeros(E, np.int64)
+            pos = {}
+            order = [(t, k) for t in toks for k in range(K)]
+            rng.shuffle(order)  # shared-memory atomics in any order
+            for t, k in order:
+                pos[t, k] = s_cnt[ids[t, k]]
+                s_cnt[ids[t, k]] += 1
+            base = np.zeros(E, np.int64)
+            for e in rng.permutation(E):  # one global atomic per expert with slots in the block
+                if s_cnt[e]:
+                    base[e] = cnt[e]
+                    cnt[e] += s_cnt[e]
+            for (t, k), p in pos.items():
+                local[t, k] = base[ids[t, k]] + p
+        offsets = np.concatenate([[0], np.cumsum(cnt)])
+        slot = offsets[ids] + local
+        assert sorted(slot.ravel().tolist()) == list(range(T * K))
+        for e in range(E):
+            mine = slot[ids == e]
+            assert mine.min(initial=offsets[e]) >= offsets[e] and mine.max(initial=offsets[e + 1] - 1) < offsets[e + 1]
