@@ -156,9 +156,9 @@ __device__ __forceinline__ void dq_sb_k45(const uint8_t* b, bool q5, int kq, flo
         *reinterpret_cast<uint4*>(dst + c * 8192 + 64) = *reinterpret_cast<const uint4*>(o + 4);
     }
 }
-// The same for a Q6_K super-block at b (2-byte aligned): y = d s (q - 32) is exact in fp32. Chunks 2 h
-// and 2 h + 1 take the low and high nibbles of the same 16 low-bit bytes and the same 16 high-bit bytes
-// (at different shifts), so each half h reads them once.
+// The same for a Q6_K super-block at b (2-byte aligned): y = (d s inv) (q - 32), the reference's products
+// in its order (d s, then times q - 32) scaled exactly. Chunks 2 h and 2 h + 1 take the low and high
+// nibbles of the same 16 low-bit bytes and the 16 high-bit bytes at other shifts: each half reads them once.
 __device__ __forceinline__ void dq_sb_q6k(const uint8_t* b, int kq, float inv, __half* dst) {
     const int hi = kq >> 5, l0 = kq & 31;
     const float dd = h16(b + 208);
